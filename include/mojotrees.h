@@ -1,0 +1,172 @@
+/* mojotrees C ABI, served by the B200-native training library
+ * (libmojotrees_b200.so).
+ *
+ * This header declares the same entry points, with the same signatures,
+ * status codes and ownership rules, as the reference's C ABI v3
+ * (ajhendel/mojoboost capi/mojotrees.h), so a caller built against that
+ * header links against this library unchanged.  Each declaration cites the
+ * reference line it replaces.  Entry points prefixed `mojotrees_b200_` are
+ * extensions with no counterpart in the reference header.
+ *
+ * Rules callers may rely on (reference capi/mojotrees.h:8-35):
+ *   - Only C scalars, C strings and opaque handles cross the boundary.
+ *   - Hyperparameters are a LightGBM-style "key=value key=value" string.
+ *   - Fallible calls return MOJOTREES_OK (0) or a negative code; the reason
+ *     is written into the caller's error object, cleared on entry.
+ *   - The library copies what it needs and never retains caller pointers.
+ *   - Every returned handle is freed exactly once; free functions accept NULL.
+ *   - A NULL required pointer is MOJOTREES_ERROR_INVALID_ARGUMENT, not a crash.
+ *
+ * Device policy of this library: training runs on a CUDA device (sm_100a).
+ * "device=gpu" (the default here) never falls back to the CPU; a request the
+ * device path does not cover returns MOJOTREES_ERROR_UNSUPPORTED naming what
+ * is uncovered.  "device=cpu" is MOJOTREES_ERROR_UNSUPPORTED as well: this
+ * library is the accelerated path only.  Prediction runs on the host.
+ */
+#ifndef MOJOTREES_H
+#define MOJOTREES_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* reference capi/mojotrees.h:84 */
+#define MOJOTREES_ABI_VERSION 3
+
+/* reference capi/mojotrees.h:87-91 */
+#define MOJOTREES_OK 0
+#define MOJOTREES_ERROR_INVALID_ARGUMENT (-1)
+#define MOJOTREES_ERROR_TRAINING (-2)
+#define MOJOTREES_ERROR_IO (-3)
+#define MOJOTREES_ERROR_UNSUPPORTED (-4)
+
+/* reference capi/mojotrees.h:101-103 */
+#define MOJOTREES_DEVICE_CPU 0
+#define MOJOTREES_DEVICE_GPU 1
+#define MOJOTREES_DEVICE_AUTO 2
+
+/* reference capi/mojotrees.h:108-109 */
+#define MOJOTREES_PREDICT_RESPONSE 0
+#define MOJOTREES_PREDICT_RAW 1
+
+/* reference capi/mojotrees.h:115-116 */
+#define MOJOTREES_IMPORTANCE_SPLIT 0
+#define MOJOTREES_IMPORTANCE_GAIN 1
+
+/* reference capi/mojotrees.h:119-122 */
+typedef struct MojoTreesModel MojoTreesModel;
+typedef struct MojoTreesError MojoTreesError;
+
+/* reference capi/mojotrees.h:127 */
+int32_t mojotrees_abi_version(void);
+/* reference capi/mojotrees.h:130-131 */
+void mojotrees_library_version(int32_t *major, int32_t *minor, int32_t *patch);
+/* reference capi/mojotrees.h:142.  1 when a CUDA device is visible. */
+int32_t mojotrees_gpu_available(void);
+
+/* reference capi/mojotrees.h:147-161 */
+MojoTreesError *mojotrees_error_create(void);
+void mojotrees_error_free(MojoTreesError *error);
+const char *mojotrees_error_message(const MojoTreesError *error);
+
+/* reference capi/mojotrees.h:181-185.  data is column-major
+ * (data[f * n_rows + r]), NaN is missing.  weights must be NULL on the
+ * device path (weighted fits return MOJOTREES_ERROR_UNSUPPORTED). */
+int32_t mojotrees_train_dense(const double *data, int64_t n_rows, int64_t n_features, const double *labels,
+                              const double *weights, const char *parameters, MojoTreesModel **out_model,
+                              MojoTreesError *error);
+
+/* reference capi/mojotrees.h:197-200 */
+int32_t mojotrees_predict(const MojoTreesModel *model, const double *data, int64_t n_rows, int64_t n_features,
+                          double *out_values, int64_t out_len, MojoTreesError *error);
+/* reference capi/mojotrees.h:205-208 */
+int32_t mojotrees_predict_raw(const MojoTreesModel *model, const double *data, int64_t n_rows,
+                              int64_t n_features, double *out_values, int64_t out_len, MojoTreesError *error);
+/* reference capi/mojotrees.h:227-233.  device must be CPU or AUTO (host). */
+int32_t mojotrees_predict_ex(const MojoTreesModel *model, const double *data, int64_t n_rows, int64_t n_features,
+                             int64_t start_iteration, int64_t num_iteration, int32_t flags, int32_t device,
+                             double *out_values, int64_t out_len, MojoTreesError *error);
+
+/* reference capi/mojotrees.h:238-246.  The file is this library's own text
+ * format ("mojotrees-b200 v1"), not the reference's format v4. */
+int32_t mojotrees_save_model(const MojoTreesModel *model, const char *path, MojoTreesError *error);
+int32_t mojotrees_load_model(const char *path, MojoTreesModel **out_model, MojoTreesError *error);
+
+/* reference capi/mojotrees.h:251-274 */
+int32_t mojotrees_model_num_features(const MojoTreesModel *model, int64_t *out_value, MojoTreesError *error);
+int32_t mojotrees_model_num_classes(const MojoTreesModel *model, int64_t *out_value, MojoTreesError *error);
+int32_t mojotrees_model_num_trees(const MojoTreesModel *model, int64_t *out_value, MojoTreesError *error);
+int32_t mojotrees_model_num_iterations(const MojoTreesModel *model, int64_t *out_value, MojoTreesError *error);
+
+/* reference capi/mojotrees.h:287-288 */
+int32_t mojotrees_model_dump_json(const MojoTreesModel *model, char **out_text, MojoTreesError *error);
+/* reference capi/mojotrees.h:307-310 */
+int32_t mojotrees_feature_importance(const MojoTreesModel *model, int32_t importance_type, double *out_values,
+                                     int64_t out_len, MojoTreesError *error);
+/* reference capi/mojotrees.h:323 */
+int32_t mojotrees_parameter_keys(char **out_text, MojoTreesError *error);
+
+/* reference capi/mojotrees.h:331-336 */
+void mojotrees_string_free(char *text);
+void mojotrees_model_free(MojoTreesModel *model);
+
+/* ------------------------------------------------------------ extensions */
+
+/* Train on pre-binned data: bins is feature-major uint8 (bins[f * n_rows + r])
+ * with values < n_bins.  missing_bin (NULL = none) gives per feature the bin
+ * that holds missing values or -1; n_categories (NULL = all numeric) gives
+ * per feature -1 for numeric or the number of category bins (bins 1..n,
+ * bin 0 = unseen).  For inputs too large for a float64 matrix, such as
+ * 200M x 128.  Replaces the reference's binned Dataset route
+ * (bindings/dataset_bindings.mojo). */
+int32_t mojotrees_b200_train_binned_u8(const uint8_t *bins, int64_t n_rows, int64_t n_features, int32_t n_bins,
+                                       const int32_t *missing_bin, const int32_t *n_categories,
+                                       const double *labels, const double *weights, const char *parameters,
+                                       MojoTreesModel **out_model, MojoTreesError *error);
+
+/* Host binning exactly as mojotrees_train_dense bins its input: writes
+ * feature-major bins (n_rows * n_features bytes), the per-feature missing bin
+ * and category count.  Parameters: max_bin, min_data_in_bin,
+ * bin_construct_sample_cnt, data_random_seed, use_missing, categorical_feature. */
+int32_t mojotrees_b200_bin_dense(const double *data, int64_t n_rows, int64_t n_features, const char *parameters,
+                                 uint8_t *out_bins, int32_t *out_missing_bin, int32_t *out_n_categories,
+                                 int32_t *out_n_bins, MojoTreesError *error);
+
+/* Raw-score prediction on pre-binned feature-major data (any model). */
+int32_t mojotrees_b200_predict_binned_u8(const MojoTreesModel *model, const uint8_t *bins, int64_t n_rows,
+                                         int64_t n_features, double *out_values, int64_t out_len,
+                                         MojoTreesError *error);
+
+/* Node table of one tree: per node feature, threshold_bin, left, right,
+ * default_left, missing_bin, is_categorical (7 int32 per node, node-major),
+ * value, gain (2 doubles per node) and count (int64), plus 4 uint64 words of
+ * categorical set per node.  Any out pointer may be NULL.  *out_n_nodes
+ * receives the node count; capacities are in nodes. */
+int32_t mojotrees_b200_tree_nodes(const MojoTreesModel *model, int64_t tree, int32_t *out_ints, double *out_doubles,
+                                  int64_t *out_counts, uint64_t *out_cat_bits, int64_t capacity,
+                                  int64_t *out_n_nodes, MojoTreesError *error);
+
+/* Initial scores (num_classes doubles). */
+int32_t mojotrees_b200_base_scores(const MojoTreesModel *model, double *out_values, int64_t out_len,
+                                   MojoTreesError *error);
+
+/* Training-set raw scores after the last round, when the fit was run with
+ * keep_training_scores=true: n_rows * num_classes doubles, row-major. */
+int32_t mojotrees_b200_training_scores(const MojoTreesModel *model, double *out_values, int64_t out_len,
+                                       MojoTreesError *error);
+
+/* Training statistics: fills up to out_len doubles in this order:
+ * fit_seconds, upload_seconds, hist_ms, partition_ms, scan_ms, grad_ms,
+ * hist_rows, hist_bytes, hist_launches, kernel_launches, rounds.  The phase
+ * times are measured with CUDA events only when the fit ran with
+ * profile_phases=true.  Returns the number of values written via *out_n. */
+int32_t mojotrees_b200_train_stats(const MojoTreesModel *model, double *out_values, int64_t out_len,
+                                   int64_t *out_n, MojoTreesError *error);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* MOJOTREES_H */

@@ -1,0 +1,13 @@
+"""B200-native GBDT training path of mojotrees (ajhendel/mojoboost).
+
+Training runs in libmojotrees_b200.so (hand-written sm_100a CUDA behind the
+reference's C ABI, include/mojotrees.h).  Python reaches it through ctypes;
+there is no Python or CPU training fallback.
+"""
+from ._capi import (  # noqa: F401
+    Model, MojoTreesError, UnsupportedError, abi_version, bin_dense, gpu_available, lib,
+    train_binned, train_dense,
+)
+
+__all__ = ["Model", "MojoTreesError", "UnsupportedError", "abi_version", "bin_dense",
+           "gpu_available", "lib", "train_binned", "train_dense"]

@@ -1,0 +1,254 @@
+// Host binning; see binning.h for the reference line map.
+#include "binning.h"
+
+#include <algorithm>
+#include <cmath>
+#include <stdexcept>
+
+#include "mt_math.h"
+
+namespace mtb {
+
+static const double kMaxEdge = 1e300;
+
+static double avoid_inf(double x) {
+  if (std::isnan(x)) return 0.0;
+  if (x >= kMaxEdge) return kMaxEdge;
+  if (x <= -kMaxEdge) return -kMaxEdge;
+  return x;
+}
+
+// binning.mojo:1745-1786: sequential selection sampling with splitmix64 draws.
+static std::vector<int64_t> sample_rows(int64_t n_rows, int64_t cnt, int seed) {
+  std::vector<int64_t> out;
+  if (n_rows < 1 || cnt <= 0 || cnt >= n_rows) return out;
+  out.reserve((size_t)cnt);
+  uint64_t base = (uint64_t)(int64_t)seed * MT_GOLDEN;
+  int64_t need = cnt;
+  for (int64_t r = 0; r < n_rows && need > 0; ++r) {
+    int64_t left = n_rows - r;
+    if (need >= left) {
+      out.push_back(r);
+      --need;
+      continue;
+    }
+    if (mt_uniform(base + (uint64_t)r) * (double)left < (double)need) {
+      out.push_back(r);
+      --need;
+    }
+  }
+  return out;
+}
+
+static void emit_edges(const std::vector<double>& below, const std::vector<double>& above,
+                       std::vector<double>& out) {
+  out.clear();
+  size_t n = std::min(below.size(), above.size());
+  for (size_t j = 0; j < n; ++j) {
+    double lo = below[j], hi = above[j];
+    if (hi <= lo) continue;
+    double edge = avoid_inf((lo + hi) / 2.0);
+    if (!out.empty() && edge <= out.back()) continue;
+    out.push_back(edge);
+  }
+}
+
+// Kept categorical codes: the max_bins-1 most frequent, ties by ascending code
+// (a stable sort of -count over ascending codes), stored ascending.
+static std::vector<int64_t> kept_codes(const double* col, int64_t n_rows, int max_bins) {
+  std::vector<int64_t> present;
+  present.reserve((size_t)n_rows);
+  for (int64_t r = 0; r < n_rows; ++r) {
+    double v = col[r];
+    if (!(v >= 0.0)) continue;
+    if (v >= 2147483648.0) throw std::runtime_error("categorical code out of range (>= 2^31)");
+    present.push_back((int64_t)v);
+  }
+  std::sort(present.begin(), present.end());
+  std::vector<int64_t> codes, counts;
+  for (size_t i = 0; i < present.size();) {
+    size_t j = i;
+    while (j + 1 < present.size() && present[j + 1] == present[i]) ++j;
+    codes.push_back(present[i]);
+    counts.push_back((int64_t)(j - i + 1));
+    i = j + 1;
+  }
+  size_t keep = (size_t)(max_bins - 1);
+  if (codes.size() <= keep) return codes;
+  std::vector<size_t> order(codes.size());
+  for (size_t i = 0; i < order.size(); ++i) order[i] = i;
+  std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) { return counts[a] > counts[b]; });
+  std::vector<int64_t> kept;
+  for (size_t i = 0; i < keep; ++i) kept.push_back(codes[order[i]]);
+  std::sort(kept.begin(), kept.end());
+  return kept;
+}
+
+int BinMapper::bin_value(int f, double v) const {
+  if (!is_cat.empty() && is_cat[f]) {
+    if (!(v >= 0.0) || v >= 2147483648.0) return 0;
+    int64_t code = (int64_t)v;
+    auto b = cat_codes.begin() + cat_offsets[f];
+    auto e = cat_codes.begin() + cat_offsets[f + 1];
+    auto it = std::lower_bound(b, e, code);
+    if (it != e && *it == code) return (int)(it - b) + 1;
+    return 0;
+  }
+  double value = v;
+  if (std::isnan(value)) {
+    if (missing_bin[f] >= 0) return missing_bin[f];
+    value = 0.0;
+  }
+  int64_t lo = edge_offsets[f], hi = edge_offsets[f + 1];
+  int64_t left = lo, right = hi;
+  while (left < right) {
+    int64_t mid = (left + right) / 2;
+    if (value <= edges[mid]) right = mid;
+    else left = mid + 1;
+  }
+  return (int)(left - lo);
+}
+
+BinMapper fit_bins(const double* x, int64_t n_rows, int n_features, const BinningParams& p) {
+  if (p.max_bins < 2 || p.max_bins > 256) throw std::runtime_error("max_bins must be in [2, 256]");
+  if (n_rows < 1) throw std::runtime_error("n_rows must be positive");
+  if (p.min_data_in_bin < 1) throw std::runtime_error("min_data_in_bin must be positive");
+  BinMapper m;
+  m.n_features = n_features;
+  m.n_bins = p.max_bins;
+  m.missing_bin.assign((size_t)n_features, -1);
+  m.is_cat.assign((size_t)n_features, 0);
+  for (int f : p.categorical_features) {
+    if (f < 0 || f >= n_features) throw std::runtime_error("categorical feature index out of range");
+    if (m.is_cat[f]) throw std::runtime_error("categorical feature listed twice");
+    m.is_cat[f] = 1;
+  }
+  m.cat_offsets.push_back(0);
+  for (int f = 0; f < n_features; ++f) {
+    if (m.is_cat[f]) {
+      auto kept = kept_codes(x + (int64_t)f * n_rows, n_rows, p.max_bins);
+      m.cat_codes.insert(m.cat_codes.end(), kept.begin(), kept.end());
+    }
+    m.cat_offsets.push_back((int64_t)m.cat_codes.size());
+  }
+  std::vector<int64_t> sample = sample_rows(n_rows, p.bin_construct_sample_cnt, p.data_random_seed);
+  bool sampled = !sample.empty();
+  int64_t n_sample = sampled ? (int64_t)sample.size() : n_rows;
+  m.edge_offsets.push_back(0);
+  std::vector<double> col, below, above, out, levels;
+  std::vector<int64_t> level_counts;
+  for (int f = 0; f < n_features; ++f) {
+    if (m.is_cat[f]) {
+      m.edge_offsets.push_back((int64_t)m.edges.size());
+      continue;
+    }
+    const double* base = x + (int64_t)f * n_rows;
+    col.clear();
+    if (sampled) {
+      for (int64_t i = 0; i < n_sample; ++i) {
+        double v = base[sample[i]];
+        if (!std::isnan(v)) col.push_back(v);
+      }
+    } else {
+      for (int64_t r = 0; r < n_rows; ++r)
+        if (!std::isnan(base[r])) col.push_back(base[r]);
+    }
+    int64_t n_valid = (int64_t)col.size();
+    bool reserve = p.use_missing && n_valid < n_sample;
+    int n_ordinary = reserve ? p.max_bins - 1 : p.max_bins;
+    below.clear();
+    above.clear();
+    // Sort once; -0.0 and 0.0 compare equal and are one level.
+    std::sort(col.begin(), col.end());
+    levels.clear();
+    level_counts.clear();
+    bool distinct_fits = n_valid >= 1;
+    for (int64_t i = 0; i < n_valid && distinct_fits; ++i) {
+      double v = col[i] == 0.0 ? 0.0 : col[i];
+      if (!levels.empty() && levels.back() == v) {
+        level_counts.back() += 1;
+        continue;
+      }
+      if ((int)levels.size() >= n_ordinary) {
+        distinct_fits = false;
+        break;
+      }
+      levels.push_back(v);
+      level_counts.push_back(1);
+    }
+    if (distinct_fits) {
+      // binning.mojo:3850-3868
+      if (p.min_data_in_bin <= 1) {
+        for (size_t j = 0; j + 1 < levels.size(); ++j) {
+          below.push_back(levels[j]);
+          above.push_back(levels[j + 1]);
+        }
+      } else {
+        int64_t acc = 0;
+        for (size_t j = 0; j + 1 < levels.size(); ++j) {
+          acc += level_counts[j];
+          if (acc >= p.min_data_in_bin) {
+            below.push_back(levels[j]);
+            above.push_back(levels[j + 1]);
+            acc = 0;
+          }
+        }
+      }
+    } else {
+      // binning.mojo:3876-3957
+      int64_t n_ord = n_ordinary;
+      if (p.min_data_in_bin > 1) {
+        int64_t cap = n_valid / p.min_data_in_bin;
+        if (cap < 1) cap = 1;
+        if (cap < n_ord) n_ord = cap;
+      }
+      for (int64_t b = 1; b < n_ord; ++b) {
+        int64_t idx = b * n_valid / n_ord;
+        if (idx <= 0 || idx >= n_valid) continue;
+        double w = col[idx - 1];
+        below.push_back(w);
+        auto it = std::upper_bound(col.begin() + idx, col.end(), w);
+        above.push_back(it != col.end() ? *it : w);
+      }
+    }
+    emit_edges(below, above, out);
+    m.edges.insert(m.edges.end(), out.begin(), out.end());
+    m.edge_offsets.push_back((int64_t)m.edges.size());
+    m.missing_bin[f] = reserve ? (int)out.size() + 1 : -1;
+  }
+  return m;
+}
+
+void transform(const BinMapper& m, const double* x, int64_t n_rows, uint8_t* out) {
+#pragma omp parallel for schedule(static)
+  for (int f = 0; f < m.n_features; ++f) {
+    const double* col = x + (int64_t)f * n_rows;
+    uint8_t* dst = out + (int64_t)f * n_rows;
+    for (int64_t r = 0; r < n_rows; ++r) dst[r] = (uint8_t)m.bin_value(f, col[r]);
+  }
+}
+
+void bin_equal_width(const double* x, int64_t n_rows, int n_features, int n_bins, uint8_t* out) {
+  for (int f = 0; f < n_features; ++f) {
+    const double* col = x + (int64_t)f * n_rows;
+    double lo = col[0], hi = col[0];
+    for (int64_t r = 1; r < n_rows; ++r) {
+      if (col[r] < lo) lo = col[r];
+      if (col[r] > hi) hi = col[r];
+    }
+    double width = (hi - lo) / (double)n_bins;
+    for (int64_t r = 0; r < n_rows; ++r) {
+      double v = col[r];
+      int64_t b;
+      if (width <= 0.0 || std::isnan(v)) b = 0;
+      else {
+        b = (int64_t)((v - lo) / width);
+        if (b >= n_bins) b = n_bins - 1;
+        if (b < 0) b = 0;
+      }
+      out[(int64_t)f * n_rows + r] = (uint8_t)b;
+    }
+  }
+}
+
+}  // namespace mtb

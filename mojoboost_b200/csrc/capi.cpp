@@ -1,0 +1,767 @@
+// The extern "C" surface of libmojotrees_b200.so (declared in include/mojotrees.h).
+//
+// Mirrors the reference C ABI v3 (capi/mojotrees.h, implemented there by
+// capi/mojotrees_capi.mojo:386 onward): LightGBM-style parameter strings,
+// per-call error objects cleared on entry, status codes 0/-1/-2/-3/-4, no
+// retained caller pointers, and no silent CPU fallback for a GPU request.
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <algorithm>
+#include <cctype>
+#include <fstream>
+#include <map>
+#include <memory>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/mojotrees.h"
+#include "binning.h"
+#include "model.h"
+#include "trainer.h"
+
+struct MojoTreesError {
+  std::string message;
+};
+
+struct MojoTreesModel {
+  mtb::Model m;
+};
+
+namespace {
+
+using mtb::TrainConfig;
+
+struct InvalidArgument : std::runtime_error {
+  explicit InvalidArgument(const std::string& m) : std::runtime_error(m) {}
+};
+
+void set_error(MojoTreesError* e, const std::string& msg) {
+  if (e) e->message = msg;
+}
+
+void clear_error(MojoTreesError* e) {
+  if (e) e->message.clear();
+}
+
+std::string lower(std::string s) {
+  for (auto& c : s) c = (char)std::tolower((unsigned char)c);
+  return s;
+}
+
+// primary name -> aliases (LightGBM's names)
+const std::vector<std::pair<std::string, std::vector<std::string>>>& param_table() {
+  static const std::vector<std::pair<std::string, std::vector<std::string>>> t = {
+      {"objective", {"objective_type", "app", "application", "loss"}},
+      {"num_class", {"num_classes"}},
+      {"num_iterations",
+       {"num_iteration", "n_iter", "num_tree", "num_trees", "num_round", "num_rounds", "nrounds", "num_boost_round",
+        "n_estimators", "max_iter"}},
+      {"learning_rate", {"shrinkage_rate", "eta"}},
+      {"num_leaves", {"num_leaf", "max_leaves", "max_leaf", "max_leaf_nodes"}},
+      {"min_data_in_leaf", {"min_data_per_leaf", "min_data", "min_child_samples", "min_samples_leaf"}},
+      {"lambda_l2", {"reg_lambda", "lambda", "l2_regularization"}},
+      {"lambda_l1", {"reg_alpha", "l1_regularization"}},
+      {"min_sum_hessian_in_leaf", {"min_sum_hessian_per_leaf", "min_sum_hessian", "min_hessian", "min_child_weight"}},
+      {"max_bin", {"max_bins"}},
+      {"min_data_in_bin", {}},
+      {"bin_construct_sample_cnt", {"subsample_for_bin"}},
+      {"data_random_seed", {"data_seed"}},
+      {"use_missing", {}},
+      {"categorical_feature", {"cat_feature", "categorical_column", "cat_column", "categorical_features"}},
+      {"device_type", {"device"}},
+      {"gpu_device_id", {"device_id"}},
+      {"use_quantized_grad", {}},
+      {"num_grad_quant_bins", {}},
+      {"stochastic_rounding", {}},
+      {"quant_seed", {}},
+      {"max_cat_to_onehot", {}},
+      {"max_cat_threshold", {}},
+      {"cat_smooth", {}},
+      {"cat_l2", {}},
+      {"min_data_per_group", {}},
+      {"feature_fraction", {"sub_feature", "colsample_bytree"}},
+      {"feature_fraction_seed", {}},
+      {"bagging_fraction", {"sub_row", "subsample", "bagging"}},
+      {"bagging_freq", {"subsample_freq"}},
+      {"bagging_seed", {"bagging_fraction_seed"}},
+      {"max_depth", {}},
+      {"boosting", {"boosting_type", "boost"}},
+      {"data_sample_strategy", {}},
+      {"verbosity", {"verbose"}},
+      {"seed", {"random_seed", "random_state"}},
+      {"num_threads", {"num_thread", "nthread", "nthreads", "n_jobs"}},
+      {"keep_training_scores", {}},
+      {"profile_phases", {}},
+  };
+  return t;
+}
+
+std::map<std::string, std::string> parse_kv(const char* s) {
+  std::map<std::string, std::string> out;
+  if (!s) return out;
+  std::istringstream is(s);
+  std::string tok;
+  std::map<std::string, std::string> alias;
+  for (auto& e : param_table()) {
+    alias[e.first] = e.first;
+    for (auto& a : e.second) alias[a] = e.first;
+  }
+  while (is >> tok) {
+    size_t eq = tok.find('=');
+    if (eq == std::string::npos || eq == 0) throw InvalidArgument("malformed parameter '" + tok + "', expected key=value");
+    std::string key = lower(tok.substr(0, eq)), val = tok.substr(eq + 1);
+    auto it = alias.find(key);
+    if (it == alias.end()) throw InvalidArgument("unknown parameter '" + key + "'");
+    if (out.count(it->second)) throw InvalidArgument("parameter '" + it->second + "' given twice");
+    out[it->second] = val;
+  }
+  return out;
+}
+
+long long to_int(const std::string& k, const std::string& v) {
+  char* end = nullptr;
+  long long x = strtoll(v.c_str(), &end, 10);
+  if (v.empty() || *end) throw InvalidArgument("parameter '" + k + "' expects an integer, got '" + v + "'");
+  return x;
+}
+
+double to_double(const std::string& k, const std::string& v) {
+  char* end = nullptr;
+  double x = strtod(v.c_str(), &end);
+  if (v.empty() || *end) throw InvalidArgument("parameter '" + k + "' expects a number, got '" + v + "'");
+  return x;
+}
+
+bool to_bool(const std::string& k, const std::string& v) {
+  std::string l = lower(v);
+  if (l == "true" || l == "1" || l == "yes" || l == "+") return true;
+  if (l == "false" || l == "0" || l == "no" || l == "-") return false;
+  throw InvalidArgument("parameter '" + k + "' expects a boolean, got '" + v + "'");
+}
+
+// Parses a parameter string into a training configuration.  Requests the
+// device path does not cover throw mtb::Unsupported naming them.
+TrainConfig parse_config(const char* params, bool need_training) {
+  TrainConfig c;
+  auto kv = parse_kv(params);
+  for (auto& p : kv) {
+    const std::string& k = p.first;
+    const std::string& v = p.second;
+    if (k == "objective") {
+      std::string o = lower(v);
+      if (o == "regression" || o == "regression_l2" || o == "l2" || o == "mse" || o == "mean_squared_error" ||
+          o == "rmse" || o == "root_mean_squared_error" || o == "l2_root")
+        c.objective = mtb::OBJECTIVE_L2;
+      else if (o == "binary")
+        c.objective = mtb::OBJECTIVE_BINARY;
+      else if (o == "multiclass" || o == "softmax")
+        c.objective = mtb::OBJECTIVE_MULTICLASS;
+      else
+        throw mtb::Unsupported("objective '" + v + "' is not covered by the device path (regression, binary, multiclass are)");
+    } else if (k == "num_class") c.num_class = (int)to_int(k, v);
+    else if (k == "num_iterations") c.num_iterations = (int)to_int(k, v);
+    else if (k == "learning_rate") c.learning_rate = to_double(k, v);
+    else if (k == "num_leaves") c.num_leaves = (int)to_int(k, v);
+    else if (k == "min_data_in_leaf") c.min_data_in_leaf = (int)to_int(k, v);
+    else if (k == "lambda_l2") c.lambda_l2 = to_double(k, v);
+    else if (k == "lambda_l1") c.lambda_l1 = to_double(k, v);
+    else if (k == "min_sum_hessian_in_leaf") c.min_sum_hessian_in_leaf = to_double(k, v);
+    else if (k == "max_bin") c.binning.max_bins = (int)to_int(k, v);
+    else if (k == "min_data_in_bin") c.binning.min_data_in_bin = (int)to_int(k, v);
+    else if (k == "bin_construct_sample_cnt") c.binning.bin_construct_sample_cnt = to_int(k, v);
+    else if (k == "data_random_seed") c.binning.data_random_seed = (int)to_int(k, v);
+    else if (k == "use_missing") c.binning.use_missing = to_bool(k, v);
+    else if (k == "categorical_feature") {
+      std::string s = v;
+      std::replace(s.begin(), s.end(), ',', ' ');
+      std::istringstream is(s);
+      std::string t;
+      while (is >> t) c.binning.categorical_features.push_back((int)to_int(k, t));
+    } else if (k == "device_type") {
+      std::string d = lower(v);
+      if (d == "cpu") throw mtb::Unsupported("device=cpu: this library implements the GPU training path only");
+      if (!(d == "gpu" || d == "cuda" || d == "auto"))
+        throw InvalidArgument("device must be cpu, gpu or auto, got '" + v + "'");
+    } else if (k == "gpu_device_id") c.gpu_device_id = (int)to_int(k, v);
+    else if (k == "use_quantized_grad") c.use_quantized_grad = to_bool(k, v);
+    else if (k == "num_grad_quant_bins") c.num_grad_quant_bins = (int)to_int(k, v);
+    else if (k == "stochastic_rounding") {
+      if (!to_bool(k, v)) throw mtb::Unsupported("stochastic_rounding=false: the device quantizer rounds stochastically");
+    } else if (k == "quant_seed") c.quant_seed = (int)to_int(k, v);
+    else if (k == "max_cat_to_onehot") c.max_cat_to_onehot = (int)to_int(k, v);
+    else if (k == "max_cat_threshold") c.max_cat_threshold = (int)to_int(k, v);
+    else if (k == "cat_smooth") c.cat_smooth = to_double(k, v);
+    else if (k == "cat_l2") c.cat_l2 = to_double(k, v);
+    else if (k == "min_data_per_group") c.min_data_per_group = (int)to_int(k, v);
+    else if (k == "feature_fraction") c.feature_fraction = to_double(k, v);
+    else if (k == "feature_fraction_seed") c.feature_fraction_seed = (int)to_int(k, v);
+    else if (k == "bagging_fraction") {
+      if (to_double(k, v) < 1.0 && kv.count("bagging_freq") && to_int("bagging_freq", kv["bagging_freq"]) > 0)
+        throw mtb::Unsupported("bagging (bagging_fraction < 1 with bagging_freq > 0) is not covered by the device path");
+    } else if (k == "bagging_freq" || k == "bagging_seed") {
+      to_int(k, v);
+    } else if (k == "max_depth") {
+      if (to_int(k, v) > 0) throw mtb::Unsupported("max_depth is not covered by the device path");
+    } else if (k == "boosting") {
+      std::string b = lower(v);
+      if (!(b == "gbdt" || b == "gbrt")) throw mtb::Unsupported("boosting '" + v + "' is not covered by the device path");
+    } else if (k == "data_sample_strategy") {
+      if (lower(v) != "bagging") throw mtb::Unsupported("data_sample_strategy '" + v + "' (GOSS) is not covered by the device path");
+    } else if (k == "keep_training_scores") c.keep_training_scores = to_bool(k, v);
+    else if (k == "profile_phases") c.profile_phases = to_bool(k, v);
+    else if (k == "verbosity" || k == "seed" || k == "num_threads") {
+      to_int(k, v);
+    }
+  }
+  if (need_training) {
+    if (c.num_iterations < 0) throw InvalidArgument("num_iterations must be non-negative");
+    if (!(c.learning_rate > 0.0)) throw InvalidArgument("learning_rate must be positive");
+    if (c.num_leaves < 2) throw InvalidArgument("num_leaves must be at least 2");
+    if (c.min_data_in_leaf < 0) throw InvalidArgument("min_data_in_leaf must be non-negative");
+    if (c.lambda_l2 < 0.0 || c.lambda_l1 < 0.0) throw InvalidArgument("lambda_l1 and lambda_l2 must be non-negative");
+    if (c.objective == mtb::OBJECTIVE_MULTICLASS && c.num_class < 2)
+      throw InvalidArgument("multiclass needs num_class >= 2");
+    if (c.objective != mtb::OBJECTIVE_MULTICLASS) c.num_class = 1;
+  }
+  return c;
+}
+
+template <typename F>
+int32_t guarded(MojoTreesError* err, F&& fn, int32_t fail_code = MOJOTREES_ERROR_TRAINING) {
+  clear_error(err);
+  try {
+    return fn();
+  } catch (const InvalidArgument& e) {
+    set_error(err, e.what());
+    return MOJOTREES_ERROR_INVALID_ARGUMENT;
+  } catch (const mtb::Unsupported& e) {
+    set_error(err, e.what());
+    return MOJOTREES_ERROR_UNSUPPORTED;
+  } catch (const std::bad_alloc&) {
+    set_error(err, "out of host memory");
+    return fail_code;
+  } catch (const std::exception& e) {
+    set_error(err, e.what());
+    return fail_code;
+  }
+}
+
+// Tree walk on bins (tree.mojo:483-503).
+inline double tree_value(const std::vector<mtb::HostNode>& t, const uint8_t* row_bins, int64_t stride) {
+  int node = 0;
+  while (t[node].feature >= 0) {
+    const mtb::HostNode& nd = t[node];
+    int b = row_bins[(int64_t)nd.feature * stride];
+    bool left;
+    if (nd.is_cat) left = b > 0 && b < 256 && ((nd.bits[b >> 6] >> (b & 63)) & 1ull);
+    else if (b == nd.mbin) left = nd.dleft != 0;
+    else left = b <= nd.thr;
+    node = left ? nd.left : nd.right;
+  }
+  return t[node].value;
+}
+
+// Raw scores of feature-major bins over iterations [it0, it1)
+// (boosting.mojo:1722-1727, 3747-3757; the sum is a fused multiply-add).
+void raw_scores(const mtb::Model& m, const uint8_t* bins, int64_t n, int64_t it0, int64_t it1, double* out) {
+  const int K = m.num_class;
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < n; ++r) {
+    for (int k = 0; k < K; ++k) {
+      double s = it0 == 0 ? m.base_scores[k] : 0.0;
+      for (int64_t i = it0; i < it1; ++i) s = fma(m.learning_rate, tree_value(m.trees[i * K + k], bins + r, n), s);
+      out[r * K + k] = s;
+    }
+  }
+}
+
+void response(const mtb::Model& m, int64_t n, double* v) {
+  if (m.objective == mtb::OBJECTIVE_BINARY) {
+    for (int64_t r = 0; r < n; ++r) {
+      double x = v[r];
+      if (x >= 0.0) v[r] = 1.0 / (1.0 + exp(-x));
+      else {
+        double e = exp(x);
+        v[r] = e / (1.0 + e);
+      }
+    }
+  } else if (m.objective == mtb::OBJECTIVE_MULTICLASS) {
+    const int K = m.num_class;
+    for (int64_t r = 0; r < n; ++r) {
+      double* p = v + r * K;
+      double mx = p[0];
+      for (int k = 1; k < K; ++k)
+        if (p[k] > mx) mx = p[k];
+      double tot = 0.0;
+      for (int k = 0; k < K; ++k) {
+        p[k] = exp(p[k] - mx);
+        tot += p[k];
+      }
+      for (int k = 0; k < K; ++k) p[k] /= tot;
+    }
+  }
+}
+
+int32_t predict_impl(const MojoTreesModel* model, const double* data, int64_t n_rows, int64_t n_features,
+                     int64_t start_iteration, int64_t num_iteration, int32_t flags, int32_t device, double* out,
+                     int64_t out_len, MojoTreesError* err) {
+  return guarded(
+      err,
+      [&]() -> int32_t {
+        if (!model || !data || !out) throw InvalidArgument("null pointer argument");
+        if (flags != MOJOTREES_PREDICT_RESPONSE && flags != MOJOTREES_PREDICT_RAW)
+          throw InvalidArgument("unknown predict flags");
+        if (device == MOJOTREES_DEVICE_GPU)
+          throw mtb::Unsupported("prediction runs on the host in this library; pass MOJOTREES_DEVICE_CPU or AUTO");
+        if (device != MOJOTREES_DEVICE_CPU && device != MOJOTREES_DEVICE_AUTO) throw InvalidArgument("unknown device");
+        const mtb::Model& m = model->m;
+        if (n_rows < 0) throw InvalidArgument("n_rows must be non-negative");
+        if (n_features != m.n_features) throw InvalidArgument("n_features does not match the model");
+        if (out_len < n_rows * m.num_class) throw InvalidArgument("output buffer too small");
+        if (!m.has_mapper)
+          throw mtb::Unsupported("model was trained on pre-binned data; use mojotrees_b200_predict_binned_u8");
+        int64_t iters = (int64_t)m.trees.size() / m.num_class;
+        int64_t it0 = std::max<int64_t>(0, std::min(start_iteration, iters));
+        int64_t it1 = num_iteration <= 0 ? iters : std::min(iters, it0 + num_iteration);
+        std::vector<uint8_t> bins((size_t)n_rows * n_features);
+        mtb::transform(m.mapper, data, n_rows, bins.data());
+        std::vector<double> tmp((size_t)n_rows * m.num_class);
+        raw_scores(m, bins.data(), n_rows, it0, it1, tmp.data());
+        if (flags == MOJOTREES_PREDICT_RESPONSE) response(m, n_rows, tmp.data());
+        memcpy(out, tmp.data(), sizeof(double) * tmp.size());
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+char* dup_string(const std::string& s) {
+  char* p = (char*)malloc(s.size() + 1);
+  if (!p) throw std::bad_alloc();
+  memcpy(p, s.c_str(), s.size() + 1);
+  return p;
+}
+
+int32_t train_binned(const uint8_t* bins, int64_t n_rows, int64_t n_features, int32_t n_bins,
+                     const std::vector<int>& missing, const std::vector<int>& ncats, const double* labels,
+                     const TrainConfig& cfg, MojoTreesModel** out_model, const mtb::BinMapper* mapper) {
+  for (int64_t r = 0; r < n_rows; ++r)
+    if (!std::isfinite(labels[r])) throw InvalidArgument("labels must be finite");
+  mtb::BinnedInput in{bins, n_rows, (int)n_features, n_bins, missing.data(), ncats.data(), labels};
+  std::unique_ptr<MojoTreesModel> h(new MojoTreesModel());
+  mtb::train_gpu(in, cfg, h->m);
+  if (mapper) {
+    h->m.has_mapper = true;
+    h->m.mapper = *mapper;
+  }
+  *out_model = h.release();
+  return MOJOTREES_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t mojotrees_abi_version(void) { return MOJOTREES_ABI_VERSION; }
+
+void mojotrees_library_version(int32_t* major, int32_t* minor, int32_t* patch) {
+  if (major) *major = 0;
+  if (minor) *minor = 1;
+  if (patch) *patch = 0;
+}
+
+int32_t mojotrees_gpu_available(void) { return mtb::cuda_device_count() > 0 ? 1 : 0; }
+
+MojoTreesError* mojotrees_error_create(void) { return new (std::nothrow) MojoTreesError(); }
+
+void mojotrees_error_free(MojoTreesError* error) { delete error; }
+
+const char* mojotrees_error_message(const MojoTreesError* error) { return error ? error->message.c_str() : nullptr; }
+
+int32_t mojotrees_train_dense(const double* data, int64_t n_rows, int64_t n_features, const double* labels,
+                              const double* weights, const char* parameters, MojoTreesModel** out_model,
+                              MojoTreesError* error) {
+  return guarded(error, [&]() -> int32_t {
+    if (!data || !labels || !out_model) throw InvalidArgument("null pointer argument");
+    if (n_rows < 1 || n_features < 1) throw InvalidArgument("n_rows and n_features must be positive");
+    TrainConfig cfg = parse_config(parameters, true);
+    if (weights) throw mtb::Unsupported("sample weights are not covered by the device path");
+    mtb::BinMapper mapper = mtb::fit_bins(data, n_rows, (int)n_features, cfg.binning);
+    std::vector<uint8_t> bins((size_t)n_rows * n_features);
+    mtb::transform(mapper, data, n_rows, bins.data());
+    std::vector<int> ncats(n_features, -1);
+    for (int f = 0; f < n_features; ++f)
+      if (mapper.is_cat[f]) ncats[f] = mapper.n_categories(f);
+    return train_binned(bins.data(), n_rows, n_features, mapper.n_bins, mapper.missing_bin, ncats, labels, cfg,
+                        out_model, &mapper);
+  });
+}
+
+int32_t mojotrees_b200_train_binned_u8(const uint8_t* bins, int64_t n_rows, int64_t n_features, int32_t n_bins,
+                                       const int32_t* missing_bin, const int32_t* n_categories, const double* labels,
+                                       const double* weights, const char* parameters, MojoTreesModel** out_model,
+                                       MojoTreesError* error) {
+  return guarded(error, [&]() -> int32_t {
+    if (!bins || !labels || !out_model) throw InvalidArgument("null pointer argument");
+    if (n_rows < 1 || n_features < 1) throw InvalidArgument("n_rows and n_features must be positive");
+    if (n_bins < 2 || n_bins > 256) throw InvalidArgument("n_bins must be in [2, 256]");
+    TrainConfig cfg = parse_config(parameters, true);
+    if (weights) throw mtb::Unsupported("sample weights are not covered by the device path");
+    std::vector<int> missing(n_features, -1), ncats(n_features, -1);
+    for (int64_t f = 0; f < n_features; ++f) {
+      if (missing_bin) missing[f] = missing_bin[f];
+      if (n_categories) ncats[f] = n_categories[f];
+      if (missing[f] >= n_bins) throw InvalidArgument("missing_bin out of range");
+    }
+    return train_binned(bins, n_rows, n_features, n_bins, missing, ncats, labels, cfg, out_model, nullptr);
+  });
+}
+
+int32_t mojotrees_b200_bin_dense(const double* data, int64_t n_rows, int64_t n_features, const char* parameters,
+                                 uint8_t* out_bins, int32_t* out_missing_bin, int32_t* out_n_categories,
+                                 int32_t* out_n_bins, MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!data || !out_bins) throw InvalidArgument("null pointer argument");
+        if (n_rows < 1 || n_features < 1) throw InvalidArgument("n_rows and n_features must be positive");
+        TrainConfig cfg = parse_config(parameters, false);
+        mtb::BinMapper m = mtb::fit_bins(data, n_rows, (int)n_features, cfg.binning);
+        mtb::transform(m, data, n_rows, out_bins);
+        for (int64_t f = 0; f < n_features; ++f) {
+          if (out_missing_bin) out_missing_bin[f] = m.missing_bin[f];
+          if (out_n_categories) out_n_categories[f] = m.is_cat[f] ? m.n_categories((int)f) : -1;
+        }
+        if (out_n_bins) *out_n_bins = m.n_bins;
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+int32_t mojotrees_predict(const MojoTreesModel* model, const double* data, int64_t n_rows, int64_t n_features,
+                          double* out_values, int64_t out_len, MojoTreesError* error) {
+  return predict_impl(model, data, n_rows, n_features, 0, 0, MOJOTREES_PREDICT_RESPONSE, MOJOTREES_DEVICE_CPU,
+                      out_values, out_len, error);
+}
+
+int32_t mojotrees_predict_raw(const MojoTreesModel* model, const double* data, int64_t n_rows, int64_t n_features,
+                              double* out_values, int64_t out_len, MojoTreesError* error) {
+  return predict_impl(model, data, n_rows, n_features, 0, 0, MOJOTREES_PREDICT_RAW, MOJOTREES_DEVICE_CPU, out_values,
+                      out_len, error);
+}
+
+int32_t mojotrees_predict_ex(const MojoTreesModel* model, const double* data, int64_t n_rows, int64_t n_features,
+                             int64_t start_iteration, int64_t num_iteration, int32_t flags, int32_t device,
+                             double* out_values, int64_t out_len, MojoTreesError* error) {
+  return predict_impl(model, data, n_rows, n_features, start_iteration, num_iteration, flags, device, out_values,
+                      out_len, error);
+}
+
+int32_t mojotrees_b200_predict_binned_u8(const MojoTreesModel* model, const uint8_t* bins, int64_t n_rows,
+                                         int64_t n_features, double* out_values, int64_t out_len,
+                                         MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!model || !bins || !out_values) throw InvalidArgument("null pointer argument");
+        const mtb::Model& m = model->m;
+        if (n_features != m.n_features) throw InvalidArgument("n_features does not match the model");
+        if (out_len < n_rows * m.num_class) throw InvalidArgument("output buffer too small");
+        raw_scores(m, bins, n_rows, 0, (int64_t)m.trees.size() / m.num_class, out_values);
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+static const char kMagic[] = "mojotrees-b200 v1";
+
+int32_t mojotrees_save_model(const MojoTreesModel* model, const char* path, MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!model || !path) throw InvalidArgument("null pointer argument");
+        const mtb::Model& m = model->m;
+        std::ofstream os(path);
+        if (!os) throw std::runtime_error(std::string("cannot open '") + path + "' for writing");
+        os << kMagic << "\n";
+        os.precision(17);
+        os << m.objective << " " << m.num_class << " " << m.n_features << " " << std::hexfloat << m.learning_rate
+           << std::defaultfloat << " " << m.trees.size() << " " << (m.has_mapper ? 1 : 0) << "\n";
+        for (double b : m.base_scores) os << std::hexfloat << b << " ";
+        os << std::defaultfloat << "\n";
+        if (m.has_mapper) {
+          const mtb::BinMapper& mp = m.mapper;
+          os << mp.n_bins << " " << mp.edges.size() << " " << mp.cat_codes.size() << "\n";
+          for (double e : mp.edges) os << std::hexfloat << e << " ";
+          os << std::defaultfloat << "\n";
+          for (auto o : mp.edge_offsets) os << o << " ";
+          os << "\n";
+          for (int v : mp.missing_bin) os << v << " ";
+          os << "\n";
+          for (auto v : mp.is_cat) os << (int)v << " ";
+          os << "\n";
+          for (auto v : mp.cat_codes) os << v << " ";
+          os << "\n";
+          for (auto v : mp.cat_offsets) os << v << " ";
+          os << "\n";
+        }
+        for (auto& t : m.trees) {
+          os << t.size() << "\n";
+          for (auto& nd : t) {
+            os << nd.feature << " " << nd.thr << " " << nd.left << " " << nd.right << " " << nd.dleft << " "
+               << nd.mbin << " " << nd.is_cat << " " << nd.bits[0] << " " << nd.bits[1] << " " << nd.bits[2] << " "
+               << nd.bits[3] << " " << std::hexfloat << nd.value << " " << nd.gain << std::defaultfloat << " "
+               << nd.count << "\n";
+          }
+        }
+        if (!os) throw std::runtime_error("write failed");
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_IO);
+}
+
+static double read_double(std::istream& is) {
+  std::string s;
+  is >> s;
+  return strtod(s.c_str(), nullptr);
+}
+
+int32_t mojotrees_load_model(const char* path, MojoTreesModel** out_model, MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!path || !out_model) throw InvalidArgument("null pointer argument");
+        std::ifstream is(path);
+        if (!is) throw std::runtime_error(std::string("cannot open '") + path + "'");
+        std::string magic;
+        std::getline(is, magic);
+        if (magic != kMagic) throw std::runtime_error("not a mojotrees-b200 v1 model file");
+        std::unique_ptr<MojoTreesModel> h(new MojoTreesModel());
+        mtb::Model& m = h->m;
+        size_t n_trees;
+        int has_mapper;
+        is >> m.objective >> m.num_class >> m.n_features;
+        m.learning_rate = read_double(is);
+        is >> n_trees >> has_mapper;
+        m.base_scores.resize(m.num_class);
+        for (auto& b : m.base_scores) b = read_double(is);
+        if (has_mapper) {
+          mtb::BinMapper& mp = m.mapper;
+          size_t ne, nc;
+          is >> mp.n_bins >> ne >> nc;
+          mp.n_features = m.n_features;
+          mp.edges.resize(ne);
+          for (auto& e : mp.edges) e = read_double(is);
+          mp.edge_offsets.resize(m.n_features + 1);
+          for (auto& o : mp.edge_offsets) is >> o;
+          mp.missing_bin.resize(m.n_features);
+          for (auto& v : mp.missing_bin) is >> v;
+          mp.is_cat.resize(m.n_features);
+          for (auto& v : mp.is_cat) {
+            int x;
+            is >> x;
+            v = (uint8_t)x;
+          }
+          mp.cat_codes.resize(nc);
+          for (auto& v : mp.cat_codes) is >> v;
+          mp.cat_offsets.resize(m.n_features + 1);
+          for (auto& v : mp.cat_offsets) is >> v;
+          m.has_mapper = true;
+        }
+        m.trees.resize(n_trees);
+        for (auto& t : m.trees) {
+          size_t nn;
+          is >> nn;
+          t.resize(nn);
+          for (auto& nd : t) {
+            is >> nd.feature >> nd.thr >> nd.left >> nd.right >> nd.dleft >> nd.mbin >> nd.is_cat >> nd.bits[0] >>
+                nd.bits[1] >> nd.bits[2] >> nd.bits[3];
+            nd.value = read_double(is);
+            nd.gain = read_double(is);
+            is >> nd.count;
+            nd.pad = 0;
+          }
+        }
+        if (!is) throw std::runtime_error("truncated or malformed model file");
+        *out_model = h.release();
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_IO);
+}
+
+#define MTB_ACCESSOR(name, expr)                                                                          \
+  int32_t name(const MojoTreesModel* model, int64_t* out_value, MojoTreesError* error) {                  \
+    return guarded(                                                                                       \
+        error,                                                                                            \
+        [&]() -> int32_t {                                                                                \
+          if (!model || !out_value) throw InvalidArgument("null pointer argument");                       \
+          const mtb::Model& m = model->m;                                                                 \
+          *out_value = (expr);                                                                            \
+          return MOJOTREES_OK;                                                                            \
+        },                                                                                                \
+        MOJOTREES_ERROR_INVALID_ARGUMENT);                                                                \
+  }
+
+MTB_ACCESSOR(mojotrees_model_num_features, m.n_features)
+MTB_ACCESSOR(mojotrees_model_num_classes, m.num_class)
+MTB_ACCESSOR(mojotrees_model_num_trees, (int64_t)m.trees.size())
+MTB_ACCESSOR(mojotrees_model_num_iterations, (int64_t)m.trees.size() / m.num_class)
+
+int32_t mojotrees_model_dump_json(const MojoTreesModel* model, char** out_text, MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!model || !out_text) throw InvalidArgument("null pointer argument");
+        const mtb::Model& m = model->m;
+        std::ostringstream os;
+        os.precision(17);
+        os << "{\"schema\":\"mojotrees-b200\",\"objective\":" << m.objective << ",\"num_class\":" << m.num_class
+           << ",\"num_features\":" << m.n_features << ",\"learning_rate\":" << m.learning_rate << ",\"base_scores\":[";
+        for (size_t i = 0; i < m.base_scores.size(); ++i) os << (i ? "," : "") << m.base_scores[i];
+        os << "],\"feature_names\":[";
+        for (int f = 0; f < m.n_features; ++f) os << (f ? "," : "") << "\"Column_" << f << "\"";
+        os << "],\"trees\":[";
+        for (size_t t = 0; t < m.trees.size(); ++t) {
+          os << (t ? "," : "") << "{\"nodes\":[";
+          for (size_t i = 0; i < m.trees[t].size(); ++i) {
+            const auto& nd = m.trees[t][i];
+            os << (i ? "," : "") << "{\"feature\":" << nd.feature << ",\"threshold_bin\":" << nd.thr
+               << ",\"left\":" << nd.left << ",\"right\":" << nd.right << ",\"default_left\":" << nd.dleft
+               << ",\"missing_bin\":" << nd.mbin << ",\"categorical\":" << nd.is_cat << ",\"value\":" << nd.value
+               << ",\"gain\":" << nd.gain << ",\"count\":" << nd.count << "}";
+          }
+          os << "]}";
+        }
+        os << "]}";
+        *out_text = dup_string(os.str());
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+int32_t mojotrees_feature_importance(const MojoTreesModel* model, int32_t importance_type, double* out_values,
+                                     int64_t out_len, MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!model || !out_values) throw InvalidArgument("null pointer argument");
+        if (importance_type != MOJOTREES_IMPORTANCE_SPLIT && importance_type != MOJOTREES_IMPORTANCE_GAIN)
+          throw InvalidArgument("unknown importance type");
+        const mtb::Model& m = model->m;
+        if (out_len < m.n_features) throw InvalidArgument("output buffer too small");
+        std::vector<double> imp(m.n_features, 0.0);
+        for (auto& t : m.trees)
+          for (auto& nd : t)
+            if (nd.feature >= 0) imp[nd.feature] += importance_type == MOJOTREES_IMPORTANCE_SPLIT ? 1.0 : nd.gain;
+        memcpy(out_values, imp.data(), sizeof(double) * imp.size());
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+int32_t mojotrees_parameter_keys(char** out_text, MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!out_text) throw InvalidArgument("null pointer argument");
+        std::string s;
+        for (auto& e : param_table()) s += (s.empty() ? "" : ",") + e.first;
+        *out_text = dup_string(s);
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+void mojotrees_string_free(char* text) { free(text); }
+
+void mojotrees_model_free(MojoTreesModel* model) { delete model; }
+
+int32_t mojotrees_b200_tree_nodes(const MojoTreesModel* model, int64_t tree, int32_t* out_ints, double* out_doubles,
+                                  int64_t* out_counts, uint64_t* out_cat_bits, int64_t capacity, int64_t* out_n_nodes,
+                                  MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!model || !out_n_nodes) throw InvalidArgument("null pointer argument");
+        const mtb::Model& m = model->m;
+        if (tree < 0 || tree >= (int64_t)m.trees.size()) throw InvalidArgument("tree index out of range");
+        const auto& t = m.trees[tree];
+        *out_n_nodes = (int64_t)t.size();
+        if (capacity < (int64_t)t.size()) throw InvalidArgument("capacity too small for the tree");
+        for (size_t i = 0; i < t.size(); ++i) {
+          const auto& nd = t[i];
+          if (out_ints) {
+            int32_t* p = out_ints + 7 * i;
+            p[0] = nd.feature;
+            p[1] = nd.thr;
+            p[2] = nd.left;
+            p[3] = nd.right;
+            p[4] = nd.dleft;
+            p[5] = nd.mbin;
+            p[6] = nd.is_cat;
+          }
+          if (out_doubles) {
+            out_doubles[2 * i] = nd.value;
+            out_doubles[2 * i + 1] = nd.gain;
+          }
+          if (out_counts) out_counts[i] = nd.count;
+          if (out_cat_bits)
+            for (int w = 0; w < 4; ++w) out_cat_bits[4 * i + w] = nd.bits[w];
+        }
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+int32_t mojotrees_b200_base_scores(const MojoTreesModel* model, double* out_values, int64_t out_len,
+                                   MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!model || !out_values) throw InvalidArgument("null pointer argument");
+        const mtb::Model& m = model->m;
+        if (out_len < (int64_t)m.base_scores.size()) throw InvalidArgument("output buffer too small");
+        memcpy(out_values, m.base_scores.data(), sizeof(double) * m.base_scores.size());
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+int32_t mojotrees_b200_training_scores(const MojoTreesModel* model, double* out_values, int64_t out_len,
+                                       MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!model || !out_values) throw InvalidArgument("null pointer argument");
+        const mtb::Model& m = model->m;
+        if (m.train_scores.empty()) throw InvalidArgument("the fit did not keep training scores (keep_training_scores=true)");
+        if (out_len < (int64_t)m.train_scores.size()) throw InvalidArgument("output buffer too small");
+        memcpy(out_values, m.train_scores.data(), sizeof(double) * m.train_scores.size());
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+int32_t mojotrees_b200_train_stats(const MojoTreesModel* model, double* out_values, int64_t out_len, int64_t* out_n,
+                                   MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!model || !out_values) throw InvalidArgument("null pointer argument");
+        const mtb::TrainStats& s = model->m.stats;
+        const double v[] = {s.fit_seconds, s.upload_seconds, s.hist_ms,   s.partition_ms,
+                            s.scan_ms,     s.grad_ms,        s.hist_rows, s.hist_bytes,
+                            (double)s.hist_launches, (double)s.kernel_launches, (double)s.rounds};
+        int64_t n = std::min<int64_t>(out_len, (int64_t)(sizeof v / sizeof v[0]));
+        for (int64_t i = 0; i < n; ++i) out_values[i] = v[i];
+        if (out_n) *out_n = n;
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+}  // extern "C"

@@ -1,0 +1,161 @@
+// Device-side state and kernels of the B200 GBDT training path.
+//
+// One tree is grown entirely from device-resident state.  The host launches a
+// fixed sequence of kernels per split (pick -> partition -> histogram ->
+// subtract+scan -> finish) whose grids do not depend on any device value, so
+// no host synchronisation is needed inside a tree and the sequence can be
+// replayed as a CUDA graph.  Every kernel reads what it needs (the leaf range,
+// the split being applied, which histogram slot to fill) from `TreeState`.
+//
+// HBM layout (see the trainer for sizes):
+//   bins_rm   uint8 [N][Fp]  row-major, Fp = F rounded up to 16 (histograms)
+//   bins_cm   uint8 [F][N]   feature-major (partition reads one column)
+//   rows[2]   int32 [N]      ping-pong row-id buffers; a leaf is a contiguous
+//                            range [begin, begin+count) of one of them
+//   pairs[2]  quantized (g,h) per row, kept in the same order as rows:
+//             QUANT mode int16 (int8 g | uint8 h << 8), FIXED mode int2
+//   hist      int64 [slots][F][3][B]  integer (g, h, count) cells per leaf
+//
+// Reference map: the per-leaf histogram is gpu_active_rows.mojo:3903
+// (_range_hist_atomic_kernel); the stable partition :1054-1707; sibling
+// subtraction gpu_leaf_batching.mojo:1364 / histogram.mojo:3747; the split
+// scan split.mojo:601-1360 (restated in integer prefix sums, exact); leaf pick
+// growth_policy.mojo:659-677; tree grower tree.mojo:3767-4256.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "mt_math.h"
+
+namespace mtb {
+
+constexpr int kMaxLeaves = 4096;
+constexpr int kMaxNodes = 2 * kMaxLeaves - 1;
+
+enum HistMode : int { MODE_FIXED = 1, MODE_QUANT = 2 };
+
+struct SplitRec {
+  double gain;
+  int found;
+  int feature;
+  int bin;
+  int default_left;
+  int is_cat;
+  int pad;
+  long long n_left;
+  unsigned long long bits[4];
+};
+
+struct LeafRec {
+  int node;
+  int buf;        // which ping-pong row buffer holds this leaf's rows
+  int hist_slot;  // histogram slot of this leaf
+  int depth;
+  long long begin;  // local range [begin, begin + count) in rows[buf]
+  long long count;  // local rows (this device)
+  SplitRec split;   // best split; split.found == 0 when none
+};
+
+struct Plan {
+  int active;        // 1 when this iteration applies a split
+  int parent_slot;   // frontier slot of the leaf being split
+  int built_hist;    // histogram slot of the child built from rows
+  int sib_hist;      // histogram slot of the child derived by subtraction (= parent's)
+  int built_is_left; // decided from global counts, identical on every device
+  int feature;
+  int threshold;
+  int default_left;
+  int missing_bin;
+  int is_cat;
+  unsigned long long bits[4];
+  int src_buf;
+  int dst_buf;
+  int depth;
+  int pad;
+  long long begin;   // parent local range
+  long long count;
+  unsigned long long cursor_left;   // local rows placed left so far (final = local n_left)
+  unsigned long long cursor_right;  // local rows placed right so far
+  int n_children;    // 1 for the root, 2 after a split
+  int child_slot[2]; // frontier slots of the children (left, right)
+  int child_hist[2];
+  int child_node[2];
+};
+
+struct ChildTotals {
+  long long g, h, c;
+};
+
+struct FeatBest {
+  double gain;
+  int bin;
+  int flags;  // bit0 found, bit1 default_left, bit2 categorical
+  long long n_left;  // global rows going left under this candidate
+  unsigned long long bits[4];
+};
+
+struct NodeRec {
+  int feature;   // -1 for a leaf
+  int thr;       // threshold bin, -1 for categorical and leaves
+  int left;
+  int right;
+  int dleft;     // missing values go left
+  int mbin;      // missing bin of the split feature, -1 when none
+  int is_cat;
+  int pad;
+  unsigned long long bits[4];  // categorical set (bins going left)
+  double value;
+  double gain;
+  long long count;  // global rows reaching the node
+};
+
+struct TreeHeader {
+  int n_leaves;
+  int n_nodes;
+  int done;
+  int error;
+};
+
+struct TreeState {
+  TreeHeader hdr;
+  Plan plan;
+  ChildTotals totals[2];
+  LeafRec leaves[kMaxLeaves];
+  NodeRec nodes[kMaxNodes];
+};
+
+// Per-fit constants every kernel reads.
+struct FitConst {
+  long long n_rows;        // rows held by this device
+  long long row_offset;    // global id of this device's first row
+  int n_features;          // F
+  int f_pad;               // Fp (row stride of bins_rm)
+  int n_bins;              // B (histogram width)
+  int mode;                // MODE_FIXED / MODE_QUANT
+  int const_hess;          // hessian constant this fit (L2 unweighted)
+  int num_leaves;
+  int min_data_in_leaf;
+  double lambda_l2;
+  double lambda_l1;
+  double min_child_hess;
+  int max_cat_to_onehot;
+  int max_cat_threshold;
+  double cat_smooth;
+  double cat_l2;
+  int min_data_per_group;
+  int quant_bins;
+};
+
+// Per-round scales (written on device by the scale kernel).
+struct RoundScales {
+  double g_total;   // FIXED: pairwise sum |g|;   QUANT: max |g|
+  double h_total;
+  float gsf, hsf;   // FIXED: pow2 scales as Float32
+  double g_inv, h_inv;  // FIXED: 1 / scale (exact)
+  double g_units, h_units;  // QUANT: units per gradient / hessian
+  double g_lim, h_lim;
+  int hq_const;     // FIXED const-hessian per-row hessian units
+  int pad;
+};
+
+}  // namespace mtb

@@ -1,0 +1,85 @@
+// Host-side model and training configuration shared by the trainer and the
+// C ABI.  A trained model is immutable.
+#pragma once
+#include <stdint.h>
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "binning.h"
+
+namespace mtb {
+
+// One node of a trained tree (layout shared with the device NodeRec).
+struct HostNode {
+  int feature;
+  int thr;
+  int left;
+  int right;
+  int dleft;
+  int mbin;
+  int is_cat;
+  int pad;
+  unsigned long long bits[4];
+  double value;
+  double gain;
+  long long count;
+};
+
+enum ObjectiveKind { OBJECTIVE_L2 = 0, OBJECTIVE_BINARY = 1, OBJECTIVE_MULTICLASS = 2 };
+
+struct TrainConfig {
+  int objective = OBJECTIVE_L2;
+  int num_class = 1;
+  int num_iterations = 100;
+  double learning_rate = 0.1;
+  int num_leaves = 31;
+  int min_data_in_leaf = 20;
+  double lambda_l2 = 1.0;
+  double lambda_l1 = 0.0;
+  double min_sum_hessian_in_leaf = 1e-3;
+  double feature_fraction = 1.0;
+  int feature_fraction_seed = 2;
+  int max_cat_to_onehot = 4;
+  int max_cat_threshold = 32;
+  double cat_smooth = 10.0;
+  double cat_l2 = 10.0;
+  int min_data_per_group = 100;
+  bool use_quantized_grad = false;
+  int num_grad_quant_bins = 4;
+  int quant_seed = 11;
+  int gpu_device_id = -1;      // -1: current device
+  bool keep_training_scores = false;
+  bool profile_phases = false;
+  BinningParams binning;
+};
+
+struct TrainStats {
+  double fit_seconds = 0.0;         // wall time of the device loop
+  double upload_seconds = 0.0;      // host->device copies and layout build
+  double hist_ms = 0.0;             // summed histogram-kernel time (profile_phases)
+  double partition_ms = 0.0;
+  double scan_ms = 0.0;
+  double grad_ms = 0.0;
+  double hist_rows = 0.0;           // rows read by histogram builds (built children + roots)
+  double hist_bytes = 0.0;          // algorithmic bytes: hist_rows * (F + pair bytes)
+  int hist_launches = 0;
+  int kernel_launches = 0;          // kernels this library launched
+  int rounds = 0;
+};
+
+struct Model {
+  int objective = OBJECTIVE_L2;
+  int num_class = 1;        // values per row (1 for single-output objectives)
+  int n_features = 0;
+  double learning_rate = 0.1;
+  std::vector<double> base_scores;
+  std::vector<std::vector<HostNode>> trees;  // multiclass: tree i*K + k is class k
+  bool has_mapper = false;
+  BinMapper mapper;
+  std::vector<double> train_scores;  // when keep_training_scores
+  TrainStats stats;
+};
+
+}  // namespace mtb

@@ -1,0 +1,502 @@
+// Host orchestration of the B200 GBDT training path.
+//
+// Per fit: bins uploaded once (feature-major) and transposed on the device to
+// the row-major copy the histogram kernel streams.  Per round: derivatives,
+// the scale reduction and the quantizer run as three short kernels; then one
+// tree is grown as a fixed launch sequence (see gbdt_device.cuh) with no host
+// synchronisation until the round ends, where the tree's node table is read
+// back and the early-stop rule of boosting.mojo:2898-2907 is applied.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "gbdt_device.cuh"
+#include "gbdt_kernels.cuh"
+#include "trainer.h"
+
+namespace mtb {
+
+#define MTB_CUDA(call)                                                                       \
+  do {                                                                                       \
+    cudaError_t e_ = (call);                                                                 \
+    if (e_ != cudaSuccess)                                                                   \
+      throw std::runtime_error(std::string("CUDA error: ") + cudaGetErrorString(e_) + " at " \
+                               + #call);                                                     \
+  } while (0)
+
+int cuda_device_count() {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+namespace {
+
+template <typename T>
+struct DevBuf {
+  T* p = nullptr;
+  size_t n = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  void alloc(size_t count) {
+    free();
+    n = count;
+    if (count) MTB_CUDA(cudaMalloc(&p, sizeof(T) * count));
+  }
+  void free() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+  }
+  ~DevBuf() { free(); }
+};
+
+struct EventTimer {
+  bool on;
+  cudaStream_t s;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev;
+  double* acc;
+  std::vector<double*> accs;
+  EventTimer(bool enabled, cudaStream_t st) : on(enabled), s(st), acc(nullptr) {}
+  void begin(double* target) {
+    if (!on) return;
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    cudaEventRecord(a, s);
+    ev.push_back({a, b});
+    accs.push_back(target);
+  }
+  void end() {
+    if (!on) return;
+    cudaEventRecord(ev.back().second, s);
+  }
+  void collect() {
+    for (size_t i = 0; i < ev.size(); ++i) {
+      float ms = 0.f;
+      cudaEventSynchronize(ev[i].second);
+      cudaEventElapsedTime(&ms, ev[i].first, ev[i].second);
+      *accs[i] += ms;
+      cudaEventDestroy(ev[i].first);
+      cudaEventDestroy(ev[i].second);
+    }
+    ev.clear();
+    accs.clear();
+  }
+};
+
+struct HistLaunch {
+  int vpr = 1;
+  int groups = 1;
+  int threads = 512;
+  int row_ctas = 1;
+  size_t smem = 0;
+};
+
+template <int VPR, int MODE, bool CH>
+void launch_hist_t(const HistLaunch& hl, cudaStream_t st, const TreeState* ts, const uint8_t* bins_rm, int Fp, int F,
+                   int B, const int* r0, const int* r1, const void* p0, const void* p1, long long* hist,
+                   long long slot_cells, long long rpf) {
+  auto k = k_hist<VPR, MODE, CH>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    configured = true;
+  }
+  dim3 grid(hl.groups, hl.row_ctas);
+  k<<<grid, hl.threads, hl.smem, st>>>(ts, bins_rm, Fp, F, B, r0, r1, p0, p1, hist, slot_cells, rpf);
+}
+
+template <int MODE, bool CH>
+void launch_hist_v(const HistLaunch& hl, cudaStream_t st, const TreeState* ts, const uint8_t* bins_rm, int Fp, int F,
+                   int B, const int* r0, const int* r1, const void* p0, const void* p1, long long* hist,
+                   long long slot_cells, long long rpf) {
+#define MTB_V(V) \
+  case V:        \
+    launch_hist_t<V, MODE, CH>(hl, st, ts, bins_rm, Fp, F, B, r0, r1, p0, p1, hist, slot_cells, rpf); break;
+  switch (hl.vpr) {
+    MTB_V(1) MTB_V(2) MTB_V(3) MTB_V(4) MTB_V(5) MTB_V(6) MTB_V(7) MTB_V(8)
+    default: throw std::runtime_error("bad histogram vector count");
+  }
+#undef MTB_V
+}
+
+}  // namespace
+
+void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
+  const long long N = in.n_rows;
+  const int F = in.n_features;
+  const int B = in.n_bins;
+  if (N < 1 || F < 1) throw std::runtime_error("empty training matrix");
+  if (N >= (1ll << 31)) throw Unsupported("more than 2^31-1 rows on one device");
+  if (B < 2 || B > 256) throw std::runtime_error("n_bins must be in [2, 256]");
+  if (cfg.num_leaves < 2 || cfg.num_leaves > kMaxLeaves)
+    throw Unsupported("num_leaves must be in [2, " + std::to_string(kMaxLeaves) + "] on the device path");
+  if (cfg.feature_fraction <= 0.0 || cfg.feature_fraction > 1.0)
+    throw std::runtime_error("feature_fraction must be in (0, 1]");
+  const int K = cfg.objective == OBJECTIVE_MULTICLASS ? cfg.num_class : 1;
+  if (cfg.objective == OBJECTIVE_MULTICLASS && (K < 2 || K > 64))
+    throw Unsupported("num_class must be in [2, 64] on the device path");
+  const int mode = cfg.use_quantized_grad ? MODE_QUANT : MODE_FIXED;
+  if (mode == MODE_QUANT && (cfg.num_grad_quant_bins < 2 || cfg.num_grad_quant_bins > 254 ||
+                             cfg.num_grad_quant_bins % 2 != 0))
+    throw Unsupported("num_grad_quant_bins must be even and in [2, 254] on the device path");
+  const bool const_h = cfg.objective == OBJECTIVE_L2;
+  for (int f = 0; f < F; ++f)
+    if (in.n_cats[f] >= B) throw std::runtime_error("categorical feature has more categories than bins");
+
+  int dev = cfg.gpu_device_id;
+  if (cuda_device_count() < 1) throw Unsupported("no CUDA device is available");
+  if (dev >= 0) MTB_CUDA(cudaSetDevice(dev));
+  MTB_CUDA(cudaGetDevice(&dev));
+  cudaDeviceProp prop;
+  MTB_CUDA(cudaGetDeviceProperties(&prop, dev));
+  const int n_sm = prop.multiProcessorCount;
+
+  cudaStream_t st;
+  MTB_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  struct StreamGuard {
+    cudaStream_t s;
+    ~StreamGuard() { cudaStreamDestroy(s); }
+  } sg{st};
+
+  TrainStats stats;
+  auto t0 = std::chrono::steady_clock::now();
+  const int Fp = (F + 15) / 16 * 16;
+  DevBuf<uint8_t> d_bins_cm, d_bins_rm;
+  d_bins_cm.alloc((size_t)F * N);
+  d_bins_rm.alloc((size_t)Fp * N);
+  MTB_CUDA(cudaMemcpyAsync(d_bins_cm.p, in.bins_fm, (size_t)F * N, cudaMemcpyHostToDevice, st));
+  {
+    dim3 grid((unsigned)((N + 255) / 256), Fp / 16);
+    k_transpose_bins<<<grid, 256, 0, st>>>(d_bins_cm.p, d_bins_rm.p, N, F, Fp);
+    stats.kernel_launches++;
+  }
+  DevBuf<double> d_y, d_raw, d_prob;
+  d_y.alloc(N);
+  MTB_CUDA(cudaMemcpyAsync(d_y.p, in.labels, sizeof(double) * N, cudaMemcpyHostToDevice, st));
+  d_raw.alloc((size_t)N * K);
+  if (K > 1) d_prob.alloc((size_t)N * K);
+
+  // Initial scores (boosting.mojo:521-577; multiclass :4207-4225).
+  std::vector<double> base(K);
+  if (K == 1) {
+    double mean = 0.0, tw = 0.0;
+    for (long long r = 0; r < N; ++r) {
+      mean += 1.0 * in.labels[r];
+      tw += 1.0;
+    }
+    mean /= tw;
+    if (cfg.objective == OBJECTIVE_BINARY) {
+      for (long long r = 0; r < N; ++r)
+        if (!(in.labels[r] == 0.0 || in.labels[r] == 1.0))
+          throw std::runtime_error("binary labels must be 0 or 1");
+      double p = mean < 1e-15 ? 1e-15 : (mean > 1.0 - 1e-15 ? 1.0 - 1e-15 : mean);
+      base[0] = std::log(p / (1.0 - p));
+    } else {
+      base[0] = mean;
+    }
+  } else {
+    std::vector<double> cw(K, 0.0);
+    double tw = 0.0;
+    for (long long r = 0; r < N; ++r) {
+      double y = in.labels[r];
+      int k = (int)y;
+      if (!(y >= 0.0) || (double)k != y || k >= K) throw std::runtime_error("class labels must be in 0..num_class-1");
+      cw[k] += 1.0;
+      tw += 1.0;
+    }
+    for (int k = 0; k < K; ++k) {
+      double q = cw[k] / tw;
+      q = q < 1e-15 ? 1e-15 : (q > 1.0 - 1e-15 ? 1.0 - 1e-15 : q);
+      base[k] = std::log(q);
+    }
+  }
+  {
+    std::vector<double> init((size_t)N * K);
+    for (long long r = 0; r < N; ++r)
+      for (int k = 0; k < K; ++k) init[(size_t)r * K + k] = base[k];
+    MTB_CUDA(cudaMemcpyAsync(d_raw.p, init.data(), sizeof(double) * init.size(), cudaMemcpyHostToDevice, st));
+    MTB_CUDA(cudaStreamSynchronize(st));
+  }
+
+  DevBuf<int> d_missing, d_ncats, d_feats;
+  d_missing.alloc(F);
+  d_ncats.alloc(F);
+  d_feats.alloc(F);
+  MTB_CUDA(cudaMemcpyAsync(d_missing.p, in.missing_bin, sizeof(int) * F, cudaMemcpyHostToDevice, st));
+  MTB_CUDA(cudaMemcpyAsync(d_ncats.p, in.n_cats, sizeof(int) * F, cudaMemcpyHostToDevice, st));
+
+  const size_t pair_bytes = mode == MODE_QUANT ? 2 : 8;
+  DevBuf<int> d_rows0, d_rows1;
+  DevBuf<unsigned char> d_pairs0, d_pairs1;
+  d_rows0.alloc(N);
+  d_rows1.alloc(N);
+  d_pairs0.alloc((size_t)N * pair_bytes);
+  d_pairs1.alloc((size_t)N * pair_bytes);
+  DevBuf<float> d_g, d_h;
+  d_g.alloc(N);
+  d_h.alloc(N);
+  const long long n_part = (N + 1023) / 1024;
+  DevBuf<double> d_pg, d_ph, d_tg, d_th;
+  d_pg.alloc(n_part);
+  d_ph.alloc(n_part);
+  d_tg.alloc(n_part / 1000 + 16);
+  d_th.alloc(n_part / 1000 + 16);
+  DevBuf<RoundScales> d_sc;
+  d_sc.alloc(1);
+  DevBuf<TreeState> d_ts;
+  d_ts.alloc(1);
+  const long long slot_cells = (long long)F * 3 * B;
+  DevBuf<long long> d_hist;
+  d_hist.alloc((size_t)slot_cells * cfg.num_leaves);
+  DevBuf<FeatBest> d_fb;
+  d_fb.alloc((size_t)2 * F);
+  DevBuf<long long> d_begins;
+  DevBuf<int> d_order;
+  d_begins.alloc(kMaxLeaves);
+  d_order.alloc(kMaxLeaves);
+  MTB_CUDA(cudaStreamSynchronize(st));
+  stats.upload_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+
+  // Histogram launch geometry: as many features per CTA as one SM's shared
+  // memory holds, row chunks sized to fill every SM.
+  HistLaunch hl;
+  {
+    size_t cell_bytes = (mode == MODE_QUANT || const_h) ? 8 : 12;
+    size_t budget = 200 * 1024;
+    int fg_max = (int)(budget / ((size_t)B * cell_bytes)) / 16 * 16;
+    fg_max = std::max(16, std::min(128, fg_max));
+    int vmax = fg_max / 16;
+    int vecs = Fp / 16;
+    hl.groups = (vecs + vmax - 1) / vmax;
+    hl.vpr = (vecs + hl.groups - 1) / hl.groups;
+    hl.smem = (size_t)hl.vpr * 16 * B * cell_bytes;
+    int per_sm = std::max(1, (int)((228 * 1024) / (hl.smem + 1024)));
+    hl.threads = per_sm >= 2 ? 512 : 1024;
+    per_sm = std::min(per_sm, 2048 / hl.threads);
+    hl.row_ctas = std::max(1, (n_sm * per_sm + hl.groups - 1) / hl.groups);
+  }
+  long long rows_per_flush = 1ll << 40;
+  if (mode == MODE_QUANT) {
+    long long gl = cfg.num_grad_quant_bins / 2, hlim = const_h ? 1 : cfg.num_grad_quant_bins;
+    rows_per_flush = std::min<long long>((1ll << 20) - 1, std::min(((1ll << 21) - 1) / gl, ((1ll << 22) - 1) / hlim));
+  }
+  const int part_grid = n_sm * 4;
+  const int part_threads = 256;
+
+  model.objective = cfg.objective;
+  model.num_class = K;
+  model.n_features = F;
+  model.learning_rate = cfg.learning_rate;
+  model.base_scores = base;
+  model.trees.clear();
+
+  const int M = 2 * cfg.num_leaves - 1;
+  std::vector<HostNode> nodes_host((size_t)M);
+  TreeHeader hdr;
+  EventTimer timer(cfg.profile_phases, st);
+
+  ScanParams sp;
+  sp.B = B;
+  sp.mode = mode;
+  sp.const_hess = const_h ? 1 : 0;
+  sp.min_data_in_leaf = cfg.min_data_in_leaf;
+  sp.lambda_l2 = cfg.lambda_l2;
+  sp.lambda_l1 = cfg.lambda_l1;
+  sp.min_child_hess = cfg.min_sum_hessian_in_leaf;
+  sp.max_cat_to_onehot = cfg.max_cat_to_onehot;
+  sp.max_cat_threshold = cfg.max_cat_threshold;
+  sp.cat_smooth = cfg.cat_smooth;
+  sp.cat_l2 = cfg.cat_l2;
+  sp.min_data_per_group = cfg.min_data_per_group;
+
+  auto t_fit = std::chrono::steady_clock::now();
+  int launches = 0;
+  auto hist = [&](const int* r0, const int* r1, const void* p0, const void* p1) {
+    timer.begin(&stats.hist_ms);
+    if (mode == MODE_QUANT)
+      launch_hist_v<MODE_QUANT, false>(hl, st, d_ts.p, d_bins_rm.p, Fp, F, B, r0, r1, p0, p1, d_hist.p, slot_cells,
+                                       rows_per_flush);
+    else if (const_h)
+      launch_hist_v<MODE_FIXED, true>(hl, st, d_ts.p, d_bins_rm.p, Fp, F, B, r0, r1, p0, p1, d_hist.p, slot_cells,
+                                      rows_per_flush);
+    else
+      launch_hist_v<MODE_FIXED, false>(hl, st, d_ts.p, d_bins_rm.p, Fp, F, B, r0, r1, p0, p1, d_hist.p, slot_cells,
+                                       rows_per_flush);
+    timer.end();
+    stats.hist_launches++;
+    launches++;
+  };
+
+  const long long grid1024 = (N + 1023) / 1024;
+  const unsigned grid256 = (unsigned)((N + 255) / 256);
+  int n_trees_total = 0;
+  for (int it = 0; it < cfg.num_iterations; ++it) {
+    if (K > 1) {
+      k_softmax<<<grid256, 256, 0, st>>>(d_raw.p, d_prob.p, N, K);
+      launches++;
+    }
+    bool progress = false;
+    size_t first_tree = model.trees.size();
+    for (int k = 0; k < K; ++k) {
+      // ---- derivatives, scales, quantized pairs
+      timer.begin(&stats.grad_ms);
+      MTB_CUDA(cudaMemsetAsync(d_sc.p, 0, sizeof(RoundScales), st));
+      if (K == 1)
+        k_grad<<<(unsigned)grid1024, 1024, 0, st>>>(d_raw.p, d_y.p, d_g.p, d_h.p, N, cfg.objective, mode, d_pg.p,
+                                                    d_ph.p, d_sc.p);
+      else
+        k_grad_softmax<<<(unsigned)grid1024, 1024, 0, st>>>(d_prob.p, d_y.p, d_g.p, d_h.p, N, K, k, mode, d_pg.p,
+                                                            d_ph.p, d_sc.p);
+      launches++;
+      const double* tot_g = d_pg.p;
+      const double* tot_h = d_ph.p;
+      if (mode == MODE_FIXED) {
+        // pairwise levels: 1024 partials -> 1, outputs packed one after another
+        long long n = n_part, off = 0;
+        const double* ig = d_pg.p;
+        const double* ih = d_ph.p;
+        while (n > 1) {
+          long long nb = (n + 1023) / 1024;
+          double* og = d_tg.p + off;
+          double* oh = d_th.p + off;
+          k_pairwise_level<<<(unsigned)nb, 1024, 0, st>>>(ig, ih, n, og, oh);
+          launches++;
+          ig = og;
+          ih = oh;
+          off += nb;
+          n = nb;
+        }
+        tot_g = ig;
+        tot_h = ih;
+      }
+      k_scales<<<1, 32, 0, st>>>(d_sc.p, tot_g, tot_h, mode, const_h ? 1 : 0, cfg.num_grad_quant_bins);
+      uint64_t gs = mt_quant_stream(cfg.quant_seed, it, k, 0);
+      uint64_t hs = mt_quant_stream(cfg.quant_seed, it, k, 1);
+      if (mode == MODE_QUANT)
+        k_quantize<MODE_QUANT><<<grid256, 256, 0, st>>>(d_g.p, d_h.p, N, 0, d_sc.p, const_h, gs, hs, d_rows0.p,
+                                                         d_pairs0.p);
+      else
+        k_quantize<MODE_FIXED><<<grid256, 256, 0, st>>>(d_g.p, d_h.p, N, 0, d_sc.p, const_h, gs, hs, d_rows0.p,
+                                                         d_pairs0.p);
+      launches += 2;
+      timer.end();
+
+      // ---- active features of this tree (sampling.mojo:424-463)
+      std::vector<int> feats;
+      {
+        int tree_index = K > 1 ? it * K + k : it;
+        if (cfg.feature_fraction >= 1.0) {
+          for (int f = 0; f < F; ++f) feats.push_back(f);
+        } else {
+          const uint64_t mask = 0x7FFFFFFFFFFFFFFFull;
+          uint64_t h = mt_splitmix64((uint64_t)(int64_t)cfg.feature_fraction_seed & mask);
+          h = mt_splitmix64(h ^ ((uint64_t)(int64_t)tree_index & mask));
+          uint64_t stream = mt_splitmix64(h ^ 0ull);
+          int count = (int)((double)F * cfg.feature_fraction + 0.5);
+          int floor_count = F >= 2 ? 2 : F;
+          count = std::max(count, floor_count);
+          count = std::min(count, F);
+          if (count >= F) {
+            for (int f = 0; f < F; ++f) feats.push_back(f);
+          } else {
+            int chosen = 0;
+            for (int i = 0; i < F && chosen < count; ++i) {
+              double prob = (double)(count - chosen) / (double)(F - i);
+              if (mt_uniform(stream + (uint64_t)i) < prob) {
+                feats.push_back(i);
+                ++chosen;
+              }
+            }
+          }
+        }
+      }
+      const int n_active = (int)feats.size();
+      MTB_CUDA(cudaMemcpyAsync(d_feats.p, feats.data(), sizeof(int) * n_active, cudaMemcpyHostToDevice, st));
+      sp.n_active = n_active;
+      const dim3 scan_grid(2, (unsigned)((n_active + kScanWarps - 1) / kScanWarps));
+
+      // ---- grow the tree
+      MTB_CUDA(cudaMemsetAsync(d_hist.p, 0, sizeof(long long) * slot_cells, st));
+      k_tree_init<<<1, 32, 0, st>>>(d_ts.p, N);
+      launches++;
+      hist(d_rows0.p, d_rows1.p, d_pairs0.p, d_pairs1.p);
+      timer.begin(&stats.scan_ms);
+      k_scan<<<scan_grid, kScanWarps * 32, 0, st>>>(d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p,
+                                                    d_ncats.p, d_sc.p, sp, d_fb.p, 1);
+      k_finish<<<1, 256, 0, st>>>(d_ts.p, d_fb.p, d_feats.p, d_sc.p, sp, 1);
+      timer.end();
+      launches += 2;
+      for (int s = 1; s < cfg.num_leaves; ++s) {
+        k_pick<<<1, 256, 0, st>>>(d_ts.p, d_missing.p);
+        timer.begin(&stats.partition_ms);
+        if (mode == MODE_QUANT)
+          k_partition<uint16_t, 8><<<part_grid, part_threads, 0, st>>>(
+              d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<uint16_t*>(d_pairs0.p),
+              reinterpret_cast<uint16_t*>(d_pairs1.p), d_hist.p, slot_cells);
+        else
+          k_partition<int2, 8><<<part_grid, part_threads, 0, st>>>(
+              d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<int2*>(d_pairs0.p),
+              reinterpret_cast<int2*>(d_pairs1.p), d_hist.p, slot_cells);
+        timer.end();
+        hist(d_rows0.p, d_rows1.p, d_pairs0.p, d_pairs1.p);
+        timer.begin(&stats.scan_ms);
+        k_scan<<<scan_grid, kScanWarps * 32, 0, st>>>(d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p,
+                                                      d_ncats.p, d_sc.p, sp, d_fb.p, 0);
+        k_finish<<<1, 256, 0, st>>>(d_ts.p, d_fb.p, d_feats.p, d_sc.p, sp, 0);
+        timer.end();
+        launches += 4;
+      }
+      k_leaf_table<<<1, 1024, 0, st>>>(d_ts.p, d_begins.p, d_order.p);
+      k_update_raw<<<grid256, 256, 0, st>>>(d_ts.p, d_begins.p, d_order.p, d_rows0.p, d_rows1.p, d_raw.p, N, K, k,
+                                            cfg.learning_rate);
+      launches += 2;
+      MTB_CUDA(cudaGetLastError());
+      MTB_CUDA(cudaMemcpyAsync(&hdr, &d_ts.p->hdr, sizeof(TreeHeader), cudaMemcpyDeviceToHost, st));
+      MTB_CUDA(cudaMemcpyAsync(nodes_host.data(), d_ts.p->nodes, sizeof(HostNode) * M, cudaMemcpyDeviceToHost, st));
+      MTB_CUDA(cudaStreamSynchronize(st));
+      timer.collect();
+      if (hdr.error) throw std::runtime_error("device trainer reported an internal error");
+      std::vector<HostNode> tree(nodes_host.begin(), nodes_host.begin() + hdr.n_nodes);
+      bool trivial = hdr.n_leaves == 1 && std::fabs(tree[0].value) < 1e-12;
+      if (!trivial) progress = true;
+      model.trees.push_back(std::move(tree));
+      ++n_trees_total;
+    }
+    stats.rounds++;
+    if (!progress) {
+      // boosting.mojo:2898-2907 / :4153-4162: a round that grew nothing ends the fit
+      model.trees.resize(first_tree);
+      break;
+    }
+  }
+  MTB_CUDA(cudaStreamSynchronize(st));
+  stats.fit_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t_fit).count();
+  stats.kernel_launches += launches;
+  // rows read by histogram builds: every root plus the smaller child of every split
+  for (size_t t = 0; t < model.trees.size(); ++t) {
+    const auto& tr = model.trees[t];
+    stats.hist_rows += (double)tr[0].count;
+    for (const auto& nd : tr)
+      if (nd.feature >= 0) stats.hist_rows += (double)std::min(tr[nd.left].count, tr[nd.right].count);
+  }
+  stats.hist_bytes = stats.hist_rows * (double)(F + (mode == MODE_QUANT ? 2 : 8));
+  if (cfg.keep_training_scores) {
+    model.train_scores.resize((size_t)N * K);
+    MTB_CUDA(cudaMemcpy(model.train_scores.data(), d_raw.p, sizeof(double) * N * K, cudaMemcpyDeviceToHost));
+  }
+  model.stats = stats;
+}
+
+}  // namespace mtb
