@@ -165,6 +165,29 @@ int32_t mojotrees_b200_training_scores(const MojoTreesModel *model, double *out_
 int32_t mojotrees_b200_train_stats(const MojoTreesModel *model, double *out_values, int64_t out_len,
                                    int64_t *out_n, MojoTreesError *error);
 
+/* Device time of each boosting round of the fit, in milliseconds, measured
+ * with CUDA events on the trainer's stream (one round = the K trees of a
+ * multiclass iteration).  *out_n receives the number of rounds. */
+int32_t mojotrees_b200_round_times(const MojoTreesModel *model, double *out_values, int64_t out_len,
+                                   int64_t *out_n, MojoTreesError *error);
+
+/* Data-parallel training (one process per GPU, rows sharded): a fresh
+ * 128-byte NCCL unique id, created on one rank and broadcast by the caller. */
+int32_t mojotrees_b200_nccl_unique_id(uint8_t *out_id, MojoTreesError *error);
+
+/* Data-parallel fit over row shards.  Every rank calls this collectively with
+ * the same parameters and nccl_id; rank r passes its rows
+ * [row_offset, row_offset + n_rows) of n_rows_global, shards other than the
+ * last holding a multiple of 1024 rows.  Histograms are summed across GPUs
+ * with NCCL (exact int32), so every rank grows the same trees, identical to
+ * a single-GPU fit on all rows.  Replaces the reference's CPU data-parallel
+ * strategy (bindings/distributed_bindings.mojo, distributed.mojo:1286-1520). */
+int32_t mojotrees_b200_train_binned_u8_dp(const uint8_t *bins, int64_t n_rows, int64_t n_features, int32_t n_bins,
+                                          const int32_t *missing_bin, const int32_t *n_categories,
+                                          const double *labels, const double *weights, const char *parameters,
+                                          const uint8_t *nccl_id, int32_t rank, int32_t world, int64_t row_offset,
+                                          int64_t n_rows_global, MojoTreesModel **out_model, MojoTreesError *error);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

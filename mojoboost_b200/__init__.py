@@ -6,8 +6,8 @@ there is no Python or CPU training fallback.
 """
 from ._capi import (  # noqa: F401
     Model, MojoTreesError, UnsupportedError, abi_version, bin_dense, gpu_available, lib,
-    train_binned, train_dense,
+    nccl_unique_id, train_binned, train_binned_dp, train_dense,
 )
 
 __all__ = ["Model", "MojoTreesError", "UnsupportedError", "abi_version", "bin_dense",
-           "gpu_available", "lib", "train_binned", "train_dense"]
+           "gpu_available", "lib", "nccl_unique_id", "train_binned", "train_binned_dp", "train_dense"]

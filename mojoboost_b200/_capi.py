@@ -55,6 +55,10 @@ SIGNATURES = {
     "mojotrees_b200_base_scores": (_I32, [_P, _P, _I64, _P]),
     "mojotrees_b200_training_scores": (_I32, [_P, _P, _I64, _P]),
     "mojotrees_b200_train_stats": (_I32, [_P, _P, _I64, _P, _P]),
+    "mojotrees_b200_round_times": (_I32, [_P, _P, _I64, _P, _P]),
+    "mojotrees_b200_nccl_unique_id": (_I32, [_P, _P]),
+    "mojotrees_b200_train_binned_u8_dp": (_I32, [_P, _I64, _I64, _I32, _P, _P, _P, _P, ctypes.c_char_p, _P, _I32,
+                                                 _I32, _I64, _I64, _P, _P]),
 }
 
 _lib = None
@@ -215,6 +219,14 @@ class Model:
         e.check(lib().mojotrees_b200_train_stats(self.h, _ptr(out), out.size, ctypes.byref(n), e.h))
         return dict(zip(STAT_NAMES, out[: n.value].tolist()))
 
+    def round_times_ms(self):
+        n = ctypes.c_int64(0)
+        e = _Err()
+        e.check(lib().mojotrees_b200_round_times(self.h, None, 0, ctypes.byref(n), e.h))
+        out = np.zeros(n.value, np.float64)
+        e.check(lib().mojotrees_b200_round_times(self.h, _ptr(out), out.size, ctypes.byref(n), e.h))
+        return out
+
     def feature_importance(self, importance_type="split"):
         out = np.zeros(self.num_features, np.float64)
         e = _Err()
@@ -268,6 +280,31 @@ def train_binned(bins_fm, n_bins, y, params=None, missing_bin=None, n_categories
     h = ctypes.c_void_p()
     e.check(lib().mojotrees_b200_train_binned_u8(_ptr(bins_fm), n, f, n_bins, _ptr(mb), _ptr(nc), _ptr(y), None,
                                                  params_string(params), ctypes.byref(h), e.h))
+    return Model(h.value)
+
+
+def nccl_unique_id():
+    """128 bytes identifying a new NCCL communicator (create on one rank)."""
+    out = np.zeros(128, np.uint8)
+    e = _Err()
+    e.check(lib().mojotrees_b200_nccl_unique_id(_ptr(out), e.h))
+    return out
+
+
+def train_binned_dp(bins_fm, n_bins, y, nccl_id, rank, world, row_offset, n_rows_global, params=None,
+                    missing_bin=None, n_categories=None):
+    """Data-parallel fit: this rank's feature-major bins [n_features, n_local]."""
+    bins_fm = np.ascontiguousarray(bins_fm, dtype=np.uint8)
+    f, n = bins_fm.shape
+    y = np.ascontiguousarray(y, dtype=np.float64)
+    mb = None if missing_bin is None else np.ascontiguousarray(missing_bin, dtype=np.int32)
+    nc = None if n_categories is None else np.ascontiguousarray(n_categories, dtype=np.int32)
+    nid = np.ascontiguousarray(nccl_id, dtype=np.uint8)
+    e = _Err()
+    h = ctypes.c_void_p()
+    e.check(lib().mojotrees_b200_train_binned_u8_dp(_ptr(bins_fm), n, f, n_bins, _ptr(mb), _ptr(nc), _ptr(y), None,
+                                                    params_string(params), _ptr(nid), rank, world, row_offset,
+                                                    n_rows_global, ctypes.byref(h), e.h))
     return Model(h.value)
 
 

@@ -19,8 +19,11 @@
 #include <string>
 #include <vector>
 
+#include <cuda_runtime.h>
+
 #include "../../include/mojotrees.h"
 #include "binning.h"
+#include "collective.h"
 #include "model.h"
 #include "trainer.h"
 
@@ -348,10 +351,14 @@ char* dup_string(const std::string& s) {
 
 int32_t train_binned(const uint8_t* bins, int64_t n_rows, int64_t n_features, int32_t n_bins,
                      const std::vector<int>& missing, const std::vector<int>& ncats, const double* labels,
-                     const TrainConfig& cfg, MojoTreesModel** out_model, const mtb::BinMapper* mapper) {
+                     const TrainConfig& cfg, MojoTreesModel** out_model, const mtb::BinMapper* mapper,
+                     mtb::Collective* coll = nullptr, int64_t row_offset = 0, int64_t n_rows_global = 0) {
   for (int64_t r = 0; r < n_rows; ++r)
     if (!std::isfinite(labels[r])) throw InvalidArgument("labels must be finite");
   mtb::BinnedInput in{bins, n_rows, (int)n_features, n_bins, missing.data(), ncats.data(), labels};
+  in.coll = coll;
+  in.row_offset = row_offset;
+  in.n_rows_global = coll ? n_rows_global : n_rows;
   std::unique_ptr<MojoTreesModel> h(new MojoTreesModel());
   mtb::train_gpu(in, cfg, h->m);
   if (mapper) {
@@ -419,6 +426,64 @@ int32_t mojotrees_b200_train_binned_u8(const uint8_t* bins, int64_t n_rows, int6
     }
     return train_binned(bins, n_rows, n_features, n_bins, missing, ncats, labels, cfg, out_model, nullptr);
   });
+}
+
+int32_t mojotrees_b200_nccl_unique_id(uint8_t* out_id, MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!out_id) throw InvalidArgument("null pointer argument");
+        std::string why;
+        if (!mtb::Collective::load(&why)) throw mtb::Unsupported(why);
+        mtb::Collective::unique_id(out_id);
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_UNSUPPORTED);
+}
+
+int32_t mojotrees_b200_train_binned_u8_dp(const uint8_t* bins, int64_t n_rows, int64_t n_features, int32_t n_bins,
+                                          const int32_t* missing_bin, const int32_t* n_categories,
+                                          const double* labels, const double* weights, const char* parameters,
+                                          const uint8_t* nccl_id, int32_t rank, int32_t world, int64_t row_offset,
+                                          int64_t n_rows_global, MojoTreesModel** out_model, MojoTreesError* error) {
+  return guarded(error, [&]() -> int32_t {
+    if (!bins || !labels || !out_model || !nccl_id) throw InvalidArgument("null pointer argument");
+    if (n_rows < 1 || n_features < 1) throw InvalidArgument("n_rows and n_features must be positive");
+    if (n_bins < 2 || n_bins > 256) throw InvalidArgument("n_bins must be in [2, 256]");
+    if (world < 1 || rank < 0 || rank >= world) throw InvalidArgument("invalid rank / world size");
+    if (row_offset < 0 || row_offset + n_rows > n_rows_global) throw InvalidArgument("row_offset out of range");
+    TrainConfig cfg = parse_config(parameters, true);
+    if (weights) throw mtb::Unsupported("sample weights are not covered by the device path");
+    std::vector<int> missing(n_features, -1), ncats(n_features, -1);
+    for (int64_t f = 0; f < n_features; ++f) {
+      if (missing_bin) missing[f] = missing_bin[f];
+      if (n_categories) ncats[f] = n_categories[f];
+      if (missing[f] >= n_bins) throw InvalidArgument("missing_bin out of range");
+    }
+    if (mtb::cuda_device_count() < 1) throw mtb::Unsupported("no CUDA device is available");
+    if (cfg.gpu_device_id >= 0 && cudaSetDevice(cfg.gpu_device_id) != cudaSuccess)
+      throw mtb::Unsupported("cannot select the CUDA device");
+    mtb::Collective coll(nccl_id, rank, world);
+    return train_binned(bins, n_rows, n_features, n_bins, missing, ncats, labels, cfg, out_model, nullptr, &coll,
+                        row_offset, n_rows_global);
+  });
+}
+
+int32_t mojotrees_b200_round_times(const MojoTreesModel* model, double* out_values, int64_t out_len, int64_t* out_n,
+                                   MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!model || !out_n) throw InvalidArgument("null pointer argument");
+        const auto& r = model->m.stats.round_ms;
+        *out_n = (int64_t)r.size();
+        if (out_values) {
+          int64_t n = std::min<int64_t>(out_len, (int64_t)r.size());
+          for (int64_t i = 0; i < n; ++i) out_values[i] = r[i];
+        }
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
 }
 
 int32_t mojotrees_b200_bin_dense(const double* data, int64_t n_rows, int64_t n_features, const char* parameters,

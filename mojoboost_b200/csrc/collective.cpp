@@ -1,0 +1,133 @@
+// NCCL loaded with dlopen; see collective.h.
+#include "collective.h"
+
+#include <dlfcn.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
+namespace mtb {
+
+namespace {
+
+// The few NCCL types and entry points used here (nccl.h, NCCL 2.x ABI).
+typedef int nccl_result_t;
+typedef struct {
+  char internal[128];
+} nccl_unique_id_t;
+typedef void* nccl_comm_t;
+enum { kNcclSuccess = 0, kNcclInt32 = 2, kNcclUint64 = 5, kNcclFloat64 = 8 };
+enum { kNcclSum = 0, kNcclMax = 2 };
+
+struct Api {
+  nccl_result_t (*get_unique_id)(nccl_unique_id_t*);
+  nccl_result_t (*comm_init_rank)(nccl_comm_t*, int, nccl_unique_id_t, int);
+  nccl_result_t (*comm_destroy)(nccl_comm_t);
+  nccl_result_t (*comm_abort)(nccl_comm_t);
+  nccl_result_t (*all_reduce)(const void*, void*, size_t, int, int, nccl_comm_t, cudaStream_t);
+  nccl_result_t (*all_gather)(const void*, void*, size_t, int, nccl_comm_t, cudaStream_t);
+  nccl_result_t (*get_async_error)(nccl_comm_t, nccl_result_t*);
+  const char* (*error_string)(nccl_result_t);
+};
+
+Api g_api;
+bool g_loaded = false;
+std::string g_why;
+std::once_flag g_once;
+
+void do_load() {
+  const char* env = getenv("MOJOTREES_NCCL_LIB");
+  const char* names[] = {env, "libnccl.so.2", "libnccl.so"};
+  void* h = nullptr;
+  for (const char* n : names) {
+    if (!n || !*n) continue;
+    h = dlopen(n, RTLD_NOW | RTLD_GLOBAL);
+    if (h) break;
+  }
+  if (!h) {
+    g_why = "libnccl.so.2 could not be loaded (set MOJOTREES_NCCL_LIB or import torch first)";
+    return;
+  }
+  auto sym = [&](const char* s) {
+    void* p = dlsym(h, s);
+    if (!p && g_why.empty()) g_why = std::string("NCCL symbol missing: ") + s;
+    return p;
+  };
+  g_api.get_unique_id = (decltype(g_api.get_unique_id))sym("ncclGetUniqueId");
+  g_api.comm_init_rank = (decltype(g_api.comm_init_rank))sym("ncclCommInitRank");
+  g_api.comm_destroy = (decltype(g_api.comm_destroy))sym("ncclCommDestroy");
+  g_api.comm_abort = (decltype(g_api.comm_abort))sym("ncclCommAbort");
+  g_api.all_reduce = (decltype(g_api.all_reduce))sym("ncclAllReduce");
+  g_api.all_gather = (decltype(g_api.all_gather))sym("ncclAllGather");
+  g_api.get_async_error = (decltype(g_api.get_async_error))sym("ncclCommGetAsyncError");
+  g_api.error_string = (decltype(g_api.error_string))sym("ncclGetErrorString");
+  g_loaded = g_why.empty();
+}
+
+void ck(nccl_result_t r, const char* what) {
+  if (r != kNcclSuccess)
+    throw std::runtime_error(std::string("NCCL ") + what + " failed: " +
+                             (g_api.error_string ? g_api.error_string(r) : "unknown error"));
+}
+
+}  // namespace
+
+bool Collective::load(std::string* why) {
+  std::call_once(g_once, do_load);
+  if (!g_loaded && why) *why = g_why;
+  return g_loaded;
+}
+
+void Collective::unique_id(uint8_t out[128]) {
+  std::string why;
+  if (!load(&why)) throw std::runtime_error(why);
+  nccl_unique_id_t id;
+  ck(g_api.get_unique_id(&id), "ncclGetUniqueId");
+  memcpy(out, id.internal, 128);
+}
+
+Collective::Collective(const uint8_t id[128], int rank, int world) : rank_(rank), world_(world) {
+  std::string why;
+  if (!load(&why)) throw std::runtime_error(why);
+  if (world < 1 || rank < 0 || rank >= world) throw std::runtime_error("invalid rank / world size");
+  nccl_unique_id_t uid;
+  memcpy(uid.internal, id, 128);
+  nccl_comm_t c = nullptr;
+  ck(g_api.comm_init_rank(&c, world, uid, rank), "ncclCommInitRank");
+  comm_ = c;
+}
+
+Collective::~Collective() {
+  if (comm_) g_api.comm_destroy((nccl_comm_t)comm_);
+}
+
+void Collective::allreduce_sum_i32(int* buf, size_t n, cudaStream_t st) {
+  ck(g_api.all_reduce(buf, buf, n, kNcclInt32, kNcclSum, (nccl_comm_t)comm_, st), "ncclAllReduce");
+}
+
+void Collective::allreduce_max_u64(unsigned long long* buf, size_t n, cudaStream_t st) {
+  ck(g_api.all_reduce(buf, buf, n, kNcclUint64, kNcclMax, (nccl_comm_t)comm_, st), "ncclAllReduce");
+}
+
+void Collective::allreduce_sum_f64(double* buf, size_t n, cudaStream_t st) {
+  ck(g_api.all_reduce(buf, buf, n, kNcclFloat64, kNcclSum, (nccl_comm_t)comm_, st), "ncclAllReduce");
+}
+
+void Collective::allgather_f64(const double* send, double* recv, size_t n_per_rank, cudaStream_t st) {
+  ck(g_api.all_gather(send, recv, n_per_rank, kNcclFloat64, (nccl_comm_t)comm_, st), "ncclAllGather");
+}
+
+void Collective::check() {
+  nccl_result_t e = kNcclSuccess;
+  ck(g_api.get_async_error((nccl_comm_t)comm_, &e), "ncclCommGetAsyncError");
+  if (e != kNcclSuccess) {
+    g_api.comm_abort((nccl_comm_t)comm_);
+    comm_ = nullptr;
+    ck(e, "asynchronous operation");
+  }
+}
+
+}  // namespace mtb

@@ -1,0 +1,46 @@
+// Cross-device reductions for data-parallel training (one process per GPU).
+//
+// Replaces the reference's CPU data-parallel exchange (distributed.mojo:505-533:
+// allreduce of each node's Float64 gradient/hessian sums and Int counts) with
+// NCCL collectives over NVLink on integer histogram cells, following the
+// device contract the reference recorded but never built
+// (distributed_gpu.mojo:34-78: one global fixed-point scale, then an exact
+// integer sum in any order).  NCCL is loaded at run time (libnccl.so.2, the
+// copy PyTorch ships or the system one), so a single-GPU fit never needs it.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace mtb {
+
+class Collective {
+ public:
+  // Loads NCCL; false (with the reason) when it cannot be loaded.
+  static bool load(std::string* why);
+  // Writes a fresh 128-byte NCCL unique id (call on one rank, broadcast it).
+  static void unique_id(uint8_t out[128]);
+
+  Collective(const uint8_t id[128], int rank, int world);
+  ~Collective();
+  Collective(const Collective&) = delete;
+  Collective& operator=(const Collective&) = delete;
+
+  int rank() const { return rank_; }
+  int world() const { return world_; }
+
+  void allreduce_sum_i32(int* buf, size_t n, cudaStream_t st);
+  void allreduce_max_u64(unsigned long long* buf, size_t n, cudaStream_t st);
+  void allreduce_sum_f64(double* buf, size_t n, cudaStream_t st);
+  void allgather_f64(const double* send, double* recv, size_t n_per_rank, cudaStream_t st);
+  // Throws if the communicator reported an asynchronous error (and aborts it).
+  void check();
+
+ private:
+  void* comm_ = nullptr;
+  int rank_ = 0;
+  int world_ = 1;
+};
+
+}  // namespace mtb

@@ -114,6 +114,8 @@ struct TreeHeader {
   int n_nodes;
   int done;
   int error;
+  unsigned int scan_ticket;  // blocks of the current scan launch that have finished
+  int pad;
 };
 
 struct TreeState {

@@ -13,6 +13,7 @@
 // The translation unit is compiled with -fmad=false so no multiply-add is
 // contracted behind the arithmetic spelled here.
 #pragma once
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -266,6 +267,7 @@ __global__ void k_tree_init(TreeState* ts, long long n_local) {
   ts->hdr.n_nodes = 1;
   ts->hdr.done = 0;
   ts->hdr.error = 0;
+  ts->hdr.scan_ticket = 0;
   LeafRec& L = ts->leaves[0];
   L.node = 0;
   L.buf = 0;
@@ -294,12 +296,16 @@ __global__ void k_tree_init(TreeState* ts, long long n_local) {
 
 // Leaf pick (growth_policy.mojo:659-677): max gain > 0, lowest frontier slot
 // on ties.  Records the split in the tree and lays out the children.
-__global__ void __launch_bounds__(256) k_pick(TreeState* ts, const int* __restrict__ missing_bin) {
+// Runs on one 256-thread block.
+__device__ void block_pick(TreeState* ts, const int* __restrict__ missing_bin, int num_leaves) {
   __shared__ double s_gain[256];
   __shared__ int s_slot[256];
   int t = threadIdx.x;
-  if (ts->hdr.done) {
-    if (t == 0) ts->plan.active = 0;
+  if (ts->hdr.done || ts->hdr.n_leaves >= num_leaves) {
+    if (t == 0) {
+      ts->hdr.done = 1;
+      ts->plan.active = 0;
+    }
     return;
   }
   int nl = ts->hdr.n_leaves;
@@ -417,12 +423,12 @@ template <typename PairT, int ITEMS>
 __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t* __restrict__ bins_cm, long long n,
                                                    int* __restrict__ rows0, int* __restrict__ rows1,
                                                    PairT* __restrict__ pairs0, PairT* __restrict__ pairs1,
-                                                   long long* __restrict__ hist, long long slot_cells) {
+                                                   int* __restrict__ hist, long long slot_cells, int work_slot) {
   const Plan& P = ts->plan;
   if (!P.active) return;
-  // zero the built child's histogram slot
+  // zero the work slot the built child accumulates into
   {
-    long long* hs = hist + (long long)P.built_hist * slot_cells;
+    int* hs = hist + (long long)work_slot * slot_cells;
     long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     long long stride = (long long)gridDim.x * blockDim.x;
     for (long long i = tid; i < slot_cells; i += stride) hs[i] = 0;
@@ -528,18 +534,19 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
 // flushed with global integer atomics.
 // ---------------------------------------------------------------------------
 
-// Cells per mode:
-//   QUANT           one 64-bit word per cell: g << 42 | h << 20 | count
-//   FIXED, const h  one 64-bit word: g << 32 | count
-//   FIXED           one 64-bit word g << 32 | h, plus a 32-bit count plane
-constexpr int kQuantCountBits = 20;
-constexpr int kQuantHessBits = 22;
-constexpr int kQuantGradShift = kQuantCountBits + kQuantHessBits;  // 42
+// Shared-memory cells (32-bit atomics only; one CTA owns FG features):
+//   QUANT           plane 0: g * 2^15 + count (signed, exact while a flush
+//                   covers < 32768 rows and |sum g| < 2^16), plane 1: h
+//   FIXED, const h  plane 0: g, plane 1: count
+//   FIXED           plane 0: g, plane 1: h, plane 2: count
+// Global cells are int32 [slot][F][3][B] (g, h, count): every sum is bounded
+// by 2^30 + n (FIXED, quantized_gradient.mojo:98-99) or by B * n (QUANT).
+constexpr int kQuantCountBits = 15;
 constexpr long long kMinRowsPerCta = 2048;
 
 struct HistJob {
   long long begin, count;
-  int buf, slot;
+  int buf;
 };
 
 __device__ __forceinline__ HistJob hist_job(const TreeState* ts) {
@@ -554,103 +561,124 @@ __device__ __forceinline__ HistJob hist_job(const TreeState* ts) {
     j.count = P.count - nl;
   }
   j.buf = P.dst_buf;
-  j.slot = P.built_hist;
   return j;
 }
 
+// CTAs of one feature group are launched in thread-block clusters of CS along
+// grid y.  Each CTA accumulates its rows into its own shared-memory cells;
+// the cluster then merges the CS copies through distributed shared memory
+// (each CTA sums one CS-th of the cells across its peers) and only the
+// merged cells reach global memory, with one int32 atomic per plane.  Small
+// leaves activate fewer clusters (>= kMinRowsPerCta rows per CTA); a cluster
+// that has no rows exits as a whole.  Every build lands in the work slot;
+// the scan kernel moves it into the child's slot after any cross-device sum.
 template <int VPR, int MODE, bool CONST_H>
 __global__ void __launch_bounds__(1024) k_hist(const TreeState* __restrict__ ts, const uint8_t* __restrict__ bins_rm,
                                                int Fp, int F, int B, const int* __restrict__ rows0,
                                                const int* __restrict__ rows1, const void* __restrict__ pairs0,
-                                               const void* __restrict__ pairs1, long long* __restrict__ hist,
-                                               long long slot_cells, long long rows_per_flush) {
+                                               const void* __restrict__ pairs1, int* __restrict__ hist,
+                                               long long slot_cells, long long rows_per_flush, int work_slot) {
+  namespace cg = cooperative_groups;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   constexpr int FG = VPR * 16;
-  if (!ts->plan.active) return;
+  constexpr int NPLANE = (MODE == MODE_FIXED && !CONST_H) ? 3 : 2;
+  if (!ts->plan.active) return;  // uniform across the grid
   const HistJob job = hist_job(ts);
   if (job.count <= 0) return;
-  long long want = (job.count + kMinRowsPerCta - 1) / kMinRowsPerCta;
-  long long nr = want < (long long)gridDim.y ? want : (long long)gridDim.y;
-  if ((long long)blockIdx.y >= nr) return;
-  long long chunk = (job.count + nr - 1) / nr;
-  long long s = job.begin + (long long)blockIdx.y * chunk;
-  long long e = s + chunk;
-  if (e > job.begin + job.count) e = job.begin + job.count;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int cs = (int)cluster.num_blocks();
+  const int crank = (int)cluster.block_rank();
+  const long long n_clusters = gridDim.y / cs;
+  const long long cid = blockIdx.y / cs;
+  long long want = (job.count + kMinRowsPerCta * cs - 1) / (kMinRowsPerCta * cs);
+  long long nce = want < n_clusters ? want : n_clusters;
+  if (cid >= nce) return;  // the whole cluster leaves together
+  const long long cchunk = (job.count + nce - 1) / nce;
+  const long long c0 = job.begin + cid * cchunk;
+  long long c1 = c0 + cchunk;
+  if (c1 > job.begin + job.count) c1 = job.begin + job.count;
+  const long long sub = (cchunk + cs - 1) / cs;  // rows per CTA, identical across the cluster
+  const long long s = c0 + crank * sub;
+  long long e = s + sub;
+  if (e > c1) e = c1;
+  const long long n_pass = (sub + rows_per_flush - 1) / rows_per_flush;
   const int f0 = blockIdx.x * FG;
   const int cells = FG * B;
-  unsigned long long* c64 = reinterpret_cast<unsigned long long*>(smem_raw);
-  unsigned int* c32 = reinterpret_cast<unsigned int*>(smem_raw + (size_t)cells * 8);
+  unsigned int* p0 = reinterpret_cast<unsigned int*>(smem_raw);
+  unsigned int* p1 = p0 + cells;
+  unsigned int* p2 = p1 + cells;
   const int* rows = job.buf ? rows1 : rows0;
   const void* pairs = job.buf ? pairs1 : pairs0;
   const int v = threadIdx.x % VPR;
   const int rsub = threadIdx.x / VPR;
-  const bool vec_ok = f0 + v * 16 < Fp;  // the last group may extend past the row
   const int rpi = blockDim.x / VPR;  // rows per iteration
-  long long* hs = hist + (long long)job.slot * slot_cells;
-  for (long long ps = s; ps < e; ps += rows_per_flush) {
+  // threads beyond rpi * VPR idle (blockDim need not divide by VPR); the last
+  // group may extend past the row
+  const bool vec_ok = f0 + v * 16 < Fp && rsub < rpi;
+  int* hs = hist + (long long)work_slot * slot_cells;
+  const int slice = (cells + cs - 1) / cs;
+  const int m0 = crank * slice;
+  const int m1 = m0 + slice < cells ? m0 + slice : cells;
+  for (long long pass = 0; pass < n_pass; ++pass) {
+    long long ps = s + pass * rows_per_flush;
     long long pe = ps + rows_per_flush < e ? ps + rows_per_flush : e;
-    for (int c = threadIdx.x; c < cells; c += blockDim.x) {
-      c64[c] = 0ull;
-      if (MODE == MODE_FIXED && !CONST_H) c32[c] = 0u;
-    }
+    for (int c = threadIdx.x; c < cells * NPLANE; c += blockDim.x) p0[c] = 0u;
     __syncthreads();
     for (long long i = ps + rsub; vec_ok && i < pe; i += rpi) {
       int r = __ldg(rows + i);
-      unsigned long long inc;
-      unsigned int hinc = 0;
+      unsigned int a0, a1, a2 = 1u;
       if (MODE == MODE_QUANT) {
         uint16_t pr = __ldg(reinterpret_cast<const uint16_t*>(pairs) + i);
-        long long g = (long long)(int8_t)(pr & 0xff);
-        long long h = (long long)(pr >> 8);
-        inc = (unsigned long long)(g * (1ll << kQuantGradShift) + h * (1ll << kQuantCountBits) + 1);
+        int g = (int)(int8_t)(pr & 0xff);
+        a0 = (unsigned int)(g * (1 << kQuantCountBits) + 1);
+        a1 = (unsigned int)(pr >> 8);
       } else {
         int2 pr = __ldg(reinterpret_cast<const int2*>(pairs) + i);
-        if (CONST_H) {
-          inc = (unsigned long long)((long long)pr.x * 4294967296ll + 1);
-        } else {
-          inc = (unsigned long long)((long long)pr.x * 4294967296ll + (long long)(unsigned int)pr.y);
-          hinc = 1;
-        }
+        a0 = (unsigned int)pr.x;
+        a1 = CONST_H ? 1u : (unsigned int)pr.y;
       }
       uint4 bv = __ldg(reinterpret_cast<const uint4*>(bins_rm + (long long)r * Fp + f0 + v * 16));
-      const uint8_t* b = reinterpret_cast<const uint8_t*>(&bv);
+      const unsigned int w[4] = {bv.x, bv.y, bv.z, bv.w};
       const int base = v * 16 * B;
 #pragma unroll
       for (int k = 0; k < 16; ++k) {
-        int cell = base + k * B + b[k];
-        atomicAdd(&c64[cell], inc);
-        if (MODE == MODE_FIXED && !CONST_H) atomicAdd(&c32[cell], hinc);
+        int cell = base + k * B + (int)((w[k >> 2] >> (8 * (k & 3))) & 0xffu);
+        atomicAdd(&p0[cell], a0);
+        atomicAdd(&p1[cell], a1);
+        if (NPLANE == 3) atomicAdd(&p2[cell], a2);
       }
     }
-    __syncthreads();
-    for (int c = threadIdx.x; c < cells; c += blockDim.x) {
+    cluster.sync();
+    for (int c = m0 + threadIdx.x; c < m1; c += blockDim.x) {
       int fl = c / B;
       int f = f0 + fl;
       if (f >= F) continue;
-      int bin = c - fl * B;
-      unsigned long long x = c64[c];
-      long long g, h, cnt;
-      if (MODE == MODE_QUANT) {
-        cnt = (long long)(x & ((1ull << kQuantCountBits) - 1));
-        h = (long long)((x >> kQuantCountBits) & ((1ull << kQuantHessBits) - 1));
-        g = (long long)x >> kQuantGradShift;
-      } else if (CONST_H) {
-        cnt = (long long)(x & 0xffffffffull);
-        g = (long long)x >> 32;
-        h = 0;
-      } else {
-        cnt = (long long)c32[c];
-        h = (long long)(x & 0xffffffffull);
-        g = (long long)x >> 32;
+      int g = 0, h = 0, cnt = 0;
+      for (int rk = 0; rk < cs; ++rk) {
+        const unsigned int* q0 = cluster.map_shared_rank(p0, rk);
+        const unsigned int* q1 = q0 + cells;
+        if (MODE == MODE_QUANT) {
+          unsigned int x = q0[c];
+          cnt += (int)(x & ((1u << kQuantCountBits) - 1u));
+          g += (int)x >> kQuantCountBits;
+          h += (int)q1[c];
+        } else if (CONST_H) {
+          g += (int)q0[c];
+          cnt += (int)q1[c];
+        } else {
+          g += (int)q0[c];
+          h += (int)q1[c];
+          cnt += (int)q1[c + cells];
+        }
       }
       if (cnt == 0) continue;
-      long long* cellp = hs + ((long long)f * 3) * B + bin;
-      atomicAdd(reinterpret_cast<unsigned long long*>(cellp), (unsigned long long)g);
-      if (!(MODE == MODE_FIXED && CONST_H))
-        atomicAdd(reinterpret_cast<unsigned long long*>(cellp + B), (unsigned long long)h);
-      atomicAdd(reinterpret_cast<unsigned long long*>(cellp + 2 * B), (unsigned long long)cnt);
+      int bin = c - fl * B;
+      int* cellp = hs + (f * 3) * B + bin;
+      atomicAdd(cellp, g);
+      if (!(MODE == MODE_FIXED && CONST_H)) atomicAdd(cellp + B, h);
+      atomicAdd(cellp + 2 * B, cnt);
     }
-    __syncthreads();
+    cluster.sync();  // peers finished reading before anyone re-zeroes
   }
 }
 
@@ -689,13 +717,11 @@ __device__ __forceinline__ double deq(long long q, int mode, double inv, double 
 
 constexpr int kScanWarps = 8;
 
-__global__ void __launch_bounds__(kScanWarps * 32) k_scan(TreeState* __restrict__ ts, long long* __restrict__ hist,
-                                                           long long slot_cells, const int* __restrict__ feats,
-                                                           const int* __restrict__ missing_bin,
-                                                           const int* __restrict__ n_cats,
-                                                           const RoundScales* __restrict__ sc, ScanParams sp,
-                                                           FeatBest* __restrict__ out, int root) {
-  __shared__ long long s_cells[kScanWarps][3][256];
+__device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, long long slot_cells,
+                          const int* __restrict__ feats, const int* __restrict__ missing_bin,
+                          const int* __restrict__ n_cats, const RoundScales* __restrict__ sc, ScanParams sp,
+                          FeatBest* __restrict__ out, int root, int work_slot) {
+  __shared__ int s_cells[kScanWarps][3][256];  // int32 cells, widened when summed
   const Plan& P = ts->plan;
   if (!P.active) return;
   int c = blockIdx.x;
@@ -705,23 +731,35 @@ __global__ void __launch_bounds__(kScanWarps * 32) k_scan(TreeState* __restrict_
   if (j >= sp.n_active) return;
   const int B = sp.B;
   const int f = feats[j];
-  long long* hs = hist + (long long)P.child_hist[c] * slot_cells + (long long)f * 3 * B;
-  const bool subtract = !root && P.child_hist[c] == P.sib_hist;
-  const long long* hb = hist + (long long)P.built_hist * slot_cells + (long long)f * 3 * B;
+  int* hs = hist + (long long)P.child_hist[c] * slot_cells + (long long)f * 3 * B;
+  const bool built = root || P.child_hist[c] != P.sib_hist;
+  const int* wk = hist + (long long)work_slot * slot_cells + (long long)f * 3 * B;
   const double g_inv = sc->g_inv, h_inv = sc->h_inv, gu = sc->g_units, hu = sc->h_units;
   const int mode = sp.mode;
-  for (int i = lane; i < 3 * B; i += 32) {
-    long long v = hs[i];
-    if (subtract) {
-      v -= hb[i];
-      hs[i] = v;
+  {
+    // built child: the (reduced) work slot; sibling: parent - built, in
+    // place.  All loads are issued before any store (the slots alias).
+    constexpr int kPer = (3 * 256 + 31) / 32;
+    int vals[kPer];
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      int i = lane + 32 * q;
+      vals[q] = 0;
+      if (i < 3 * B) vals[q] = built ? __ldcg(wk + i) : __ldcg(hs + i) - __ldcg(wk + i);
     }
-    s_cells[w][i / B][i % B] = v;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      int i = lane + 32 * q;
+      if (i < 3 * B) {
+        hs[i] = vals[q];
+        s_cells[w][i / B][i % B] = vals[q];
+      }
+    }
   }
   __syncwarp();
   if (sp.const_hess && mode == MODE_FIXED) {
     long long hq = sc->hq_const;
-    for (int b = lane; b < B; b += 32) s_cells[w][1][b] = hq * s_cells[w][2][b];
+    for (int b = lane; b < B; b += 32) s_cells[w][1][b] = (int)(hq * s_cells[w][2][b]);
   }
   __syncwarp();
   // lane owns bins [lane*8, lane*8 + 8)
@@ -951,9 +989,9 @@ __global__ void __launch_bounds__(kScanWarps * 32) k_scan(TreeState* __restrict_
 
 // Cross-feature fold (ascending feature, strict >), guards, leaf values and
 // the children's ranges.
-__global__ void __launch_bounds__(256) k_finish(TreeState* __restrict__ ts, const FeatBest* __restrict__ fbs,
-                                               const int* __restrict__ feats, const RoundScales* __restrict__ sc,
-                                               ScanParams sp, int root) {
+__device__ void block_finish(TreeState* __restrict__ ts, const FeatBest* __restrict__ fbs,
+                             const int* __restrict__ feats, const RoundScales* __restrict__ sc, ScanParams sp,
+                             int root) {
   __shared__ double s_gain[256];
   __shared__ int s_j[256];
   Plan& P = ts->plan;
@@ -1029,6 +1067,36 @@ __global__ void __launch_bounds__(256) k_finish(TreeState* __restrict__ ts, cons
     }
     __syncthreads();
   }
+}
+
+// Subtract + scan of every (child, active feature); the last block to finish
+// then folds the per-feature bests (block_finish) and picks the next leaf to
+// split (block_pick), so one split costs three launches: partition,
+// histogram, scan.
+__global__ void __launch_bounds__(kScanWarps * 32) k_scan(TreeState* __restrict__ ts, int* __restrict__ hist,
+                                                           long long slot_cells, const int* __restrict__ feats,
+                                                           const int* __restrict__ missing_bin,
+                                                           const int* __restrict__ n_cats,
+                                                           const RoundScales* __restrict__ sc, ScanParams sp,
+                                                           FeatBest* __restrict__ out, int root, int work_slot,
+                                                           int num_leaves) {
+  __shared__ int s_last;
+  scan_body(ts, hist, slot_cells, feats, missing_bin, n_cats, sc, sp, out, root, work_slot);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    unsigned int total = gridDim.x * gridDim.y;
+    unsigned int ticket = atomicAdd(&ts->hdr.scan_ticket, 1u);
+    s_last = ticket == total - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  block_finish(ts, out, feats, sc, sp, root);
+  __syncthreads();
+  block_pick(ts, missing_bin, num_leaves);
+  __syncthreads();
+  if (threadIdx.x == 0) ts->hdr.scan_ticket = 0;
 }
 
 // After the last split: leaves sorted by range start, for the raw update.

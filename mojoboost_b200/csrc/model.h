@@ -67,6 +67,7 @@ struct TrainStats {
   int hist_launches = 0;
   int kernel_launches = 0;          // kernels this library launched
   int rounds = 0;
+  std::vector<double> round_ms;     // device time of each round (CUDA events on the trainer's stream)
 };
 
 struct Model {

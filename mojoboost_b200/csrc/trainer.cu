@@ -18,6 +18,7 @@
 
 #include "gbdt_device.cuh"
 #include "gbdt_kernels.cuh"
+#include "collective.h"
 #include "trainer.h"
 
 namespace mtb {
@@ -96,6 +97,7 @@ struct EventTimer {
 };
 
 struct HistLaunch {
+  int cluster = 1;  // CTAs per thread-block cluster along grid y
   int vpr = 1;
   int groups = 1;
   int threads = 512;
@@ -103,32 +105,66 @@ struct HistLaunch {
   size_t smem = 0;
 };
 
+cudaLaunchConfig_t hist_config(const HistLaunch& hl, int cs, int row_ctas, cudaStream_t st, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(hl.groups, row_ctas);
+  lc.blockDim = dim3(hl.threads);
+  lc.dynamicSmemBytes = hl.smem;
+  lc.stream = st;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = cs;
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  return lc;
+}
+
+template <int VPR, int MODE, bool CH>
+cudaError_t prepare_hist_t(const HistLaunch& hl, int cs, int* n_clusters) {
+  auto k = k_hist<VPR, MODE, CH>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (e != cudaSuccess) return e;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t lc = hist_config(hl, cs, hl.row_ctas / cs * cs, 0, attr);
+  return cudaOccupancyMaxActiveClusters(n_clusters, k, &lc);
+}
+
 template <int VPR, int MODE, bool CH>
 void launch_hist_t(const HistLaunch& hl, cudaStream_t st, const TreeState* ts, const uint8_t* bins_rm, int Fp, int F,
-                   int B, const int* r0, const int* r1, const void* p0, const void* p1, long long* hist,
-                   long long slot_cells, long long rpf) {
-  auto k = k_hist<VPR, MODE, CH>;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    configured = true;
+                   int B, const int* r0, const int* r1, const void* p0, const void* p1, int* hist,
+                   long long slot_cells, long long rpf, int ws) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t lc = hist_config(hl, hl.cluster, hl.row_ctas, st, attr);
+  MTB_CUDA(cudaLaunchKernelEx(&lc, k_hist<VPR, MODE, CH>, ts, bins_rm, Fp, F, B, r0, r1, p0, p1, hist, slot_cells,
+                              rpf, ws));
+}
+
+#define MTB_VPR_SWITCH(EXPR)                                                                  \
+  switch (hl.vpr) {                                                                            \
+    case 1: { constexpr int V = 1; EXPR; } break;                                              \
+    case 2: { constexpr int V = 2; EXPR; } break;                                              \
+    case 3: { constexpr int V = 3; EXPR; } break;                                              \
+    case 4: { constexpr int V = 4; EXPR; } break;                                              \
+    case 5: { constexpr int V = 5; EXPR; } break;                                              \
+    case 6: { constexpr int V = 6; EXPR; } break;                                              \
+    case 7: { constexpr int V = 7; EXPR; } break;                                              \
+    case 8: { constexpr int V = 8; EXPR; } break;                                              \
+    default: throw std::runtime_error("bad histogram vector count");                           \
   }
-  dim3 grid(hl.groups, hl.row_ctas);
-  k<<<grid, hl.threads, hl.smem, st>>>(ts, bins_rm, Fp, F, B, r0, r1, p0, p1, hist, slot_cells, rpf);
+
+template <int MODE, bool CH>
+cudaError_t prepare_hist(const HistLaunch& hl, int cs, int* n_clusters) {
+  cudaError_t e = cudaErrorInvalidValue;
+  MTB_VPR_SWITCH(e = (prepare_hist_t<V, MODE, CH>(hl, cs, n_clusters)))
+  return e;
 }
 
 template <int MODE, bool CH>
-void launch_hist_v(const HistLaunch& hl, cudaStream_t st, const TreeState* ts, const uint8_t* bins_rm, int Fp, int F,
-                   int B, const int* r0, const int* r1, const void* p0, const void* p1, long long* hist,
-                   long long slot_cells, long long rpf) {
-#define MTB_V(V) \
-  case V:        \
-    launch_hist_t<V, MODE, CH>(hl, st, ts, bins_rm, Fp, F, B, r0, r1, p0, p1, hist, slot_cells, rpf); break;
-  switch (hl.vpr) {
-    MTB_V(1) MTB_V(2) MTB_V(3) MTB_V(4) MTB_V(5) MTB_V(6) MTB_V(7) MTB_V(8)
-    default: throw std::runtime_error("bad histogram vector count");
-  }
-#undef MTB_V
+void launch_hist(const HistLaunch& hl, cudaStream_t st, const TreeState* ts, const uint8_t* bins_rm, int Fp, int F,
+                 int B, const int* r0, const int* r1, const void* p0, const void* p1, int* hist, long long slot_cells,
+                 long long rpf, int ws) {
+  MTB_VPR_SWITCH((launch_hist_t<V, MODE, CH>(hl, st, ts, bins_rm, Fp, F, B, r0, r1, p0, p1, hist, slot_cells, rpf, ws)))
 }
 
 }  // namespace
@@ -188,19 +224,50 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   d_raw.alloc((size_t)N * K);
   if (K > 1) d_prob.alloc((size_t)N * K);
 
-  // Initial scores (boosting.mojo:521-577; multiclass :4207-4225).
+  // Initial scores (boosting.mojo:521-577; multiclass :4207-4225).  Across
+  // devices the label sum is each shard's sequential sum combined in rank
+  // order (exact for binary and class labels, whose sums are integers).
+  Collective* coll = in.coll;
+  const int world = coll ? coll->world() : 1;
+  const long long N_global = coll ? in.n_rows_global : N;
+  DevBuf<double> d_red;
+  d_red.alloc(2 * (size_t)std::max(world, K) + 8);
+  // every rank learns whether any rank's input is invalid before any throws
+  auto agree = [&](const std::string& local_error) {
+    if (!coll) {
+      if (!local_error.empty()) throw std::runtime_error(local_error);
+      return;
+    }
+    unsigned long long flag = local_error.empty() ? 0ull : 1ull;
+    MTB_CUDA(cudaMemcpyAsync(d_red.p, &flag, 8, cudaMemcpyHostToDevice, st));
+    coll->allreduce_max_u64(reinterpret_cast<unsigned long long*>(d_red.p), 1, st);
+    MTB_CUDA(cudaMemcpyAsync(&flag, d_red.p, 8, cudaMemcpyDeviceToHost, st));
+    MTB_CUDA(cudaStreamSynchronize(st));
+    if (flag) throw std::runtime_error(local_error.empty() ? "invalid input on another rank" : local_error);
+  };
+  agree(coll && coll->rank() < world - 1 && N % 1024 != 0
+            ? "data-parallel shards other than the last must hold a multiple of 1024 rows"
+            : "");
   std::vector<double> base(K);
   if (K == 1) {
-    double mean = 0.0, tw = 0.0;
-    for (long long r = 0; r < N; ++r) {
-      mean += 1.0 * in.labels[r];
-      tw += 1.0;
+    double mean = 0.0;
+    for (long long r = 0; r < N; ++r) mean += 1.0 * in.labels[r];
+    std::string err;
+    if (cfg.objective == OBJECTIVE_BINARY)
+      for (long long r = 0; r < N && err.empty(); ++r)
+        if (!(in.labels[r] == 0.0 || in.labels[r] == 1.0)) err = "binary labels must be 0 or 1";
+    agree(err);
+    if (coll) {
+      MTB_CUDA(cudaMemcpyAsync(d_red.p + world, &mean, 8, cudaMemcpyHostToDevice, st));
+      coll->allgather_f64(d_red.p + world, d_red.p, 1, st);
+      std::vector<double> parts(world);
+      MTB_CUDA(cudaMemcpyAsync(parts.data(), d_red.p, 8 * world, cudaMemcpyDeviceToHost, st));
+      MTB_CUDA(cudaStreamSynchronize(st));
+      mean = parts[0];
+      for (int q = 1; q < world; ++q) mean += parts[q];
     }
-    mean /= tw;
+    mean /= (double)N_global;
     if (cfg.objective == OBJECTIVE_BINARY) {
-      for (long long r = 0; r < N; ++r)
-        if (!(in.labels[r] == 0.0 || in.labels[r] == 1.0))
-          throw std::runtime_error("binary labels must be 0 or 1");
       double p = mean < 1e-15 ? 1e-15 : (mean > 1.0 - 1e-15 ? 1.0 - 1e-15 : mean);
       base[0] = std::log(p / (1.0 - p));
     } else {
@@ -208,14 +275,24 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     }
   } else {
     std::vector<double> cw(K, 0.0);
-    double tw = 0.0;
+    std::string err;
     for (long long r = 0; r < N; ++r) {
       double y = in.labels[r];
       int k = (int)y;
-      if (!(y >= 0.0) || (double)k != y || k >= K) throw std::runtime_error("class labels must be in 0..num_class-1");
+      if (!(y >= 0.0) || (double)k != y || k >= K) {
+        err = "class labels must be in 0..num_class-1";
+        break;
+      }
       cw[k] += 1.0;
-      tw += 1.0;
     }
+    agree(err);
+    if (coll) {
+      MTB_CUDA(cudaMemcpyAsync(d_red.p, cw.data(), 8 * K, cudaMemcpyHostToDevice, st));
+      coll->allreduce_sum_f64(d_red.p, K, st);
+      MTB_CUDA(cudaMemcpyAsync(cw.data(), d_red.p, 8 * K, cudaMemcpyDeviceToHost, st));
+      MTB_CUDA(cudaStreamSynchronize(st));
+    }
+    double tw = (double)N_global;
     for (int k = 0; k < K; ++k) {
       double q = cw[k] / tw;
       q = q < 1e-15 ? 1e-15 : (q > 1.0 - 1e-15 ? 1.0 - 1e-15 : q);
@@ -247,10 +324,27 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   DevBuf<float> d_g, d_h;
   d_g.alloc(N);
   d_h.alloc(N);
-  const long long n_part = (N + 1023) / 1024;
-  DevBuf<double> d_pg, d_ph, d_tg, d_th;
-  d_pg.alloc(n_part);
-  d_ph.alloc(n_part);
+  // FIXED-mode |g|, |h| partials: one per 1024 global rows.  Across devices
+  // every rank gathers all ranks' partials (P per rank, the last rank's tail
+  // zero-padded) so all reduce the same global pairwise tree.
+  long long n_part = (N + 1023) / 1024;
+  long long P_rank = n_part;
+  if (coll) {
+    unsigned long long mx = (unsigned long long)n_part;
+    MTB_CUDA(cudaMemcpyAsync(d_red.p, &mx, 8, cudaMemcpyHostToDevice, st));
+    coll->allreduce_max_u64(reinterpret_cast<unsigned long long*>(d_red.p), 1, st);
+    MTB_CUDA(cudaMemcpyAsync(&mx, d_red.p, 8, cudaMemcpyDeviceToHost, st));
+    MTB_CUDA(cudaStreamSynchronize(st));
+    P_rank = (long long)mx;
+    n_part = P_rank * world;
+  }
+  DevBuf<double> d_pg, d_ph, d_tg, d_th, d_pg_all, d_ph_all;
+  d_pg.alloc(P_rank);
+  d_ph.alloc(P_rank);
+  if (coll) {
+    d_pg_all.alloc(n_part);
+    d_ph_all.alloc(n_part);
+  }
   d_tg.alloc(n_part / 1000 + 16);
   d_th.alloc(n_part / 1000 + 16);
   DevBuf<RoundScales> d_sc;
@@ -258,8 +352,9 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   DevBuf<TreeState> d_ts;
   d_ts.alloc(1);
   const long long slot_cells = (long long)F * 3 * B;
-  DevBuf<long long> d_hist;
-  d_hist.alloc((size_t)slot_cells * cfg.num_leaves);
+  DevBuf<int> d_hist;
+  d_hist.alloc((size_t)slot_cells * (cfg.num_leaves + 1));
+  const int work_slot = cfg.num_leaves;  // histogram builds land here first
   DevBuf<FeatBest> d_fb;
   d_fb.alloc((size_t)2 * F);
   DevBuf<long long> d_begins;
@@ -270,10 +365,11 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   stats.upload_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
 
   // Histogram launch geometry: as many features per CTA as one SM's shared
-  // memory holds, row chunks sized to fill every SM.
+  // memory holds, row chunks sized to fill every SM, CTAs of a feature group
+  // in clusters of up to 8 that merge through DSMEM.
   HistLaunch hl;
   {
-    size_t cell_bytes = (mode == MODE_QUANT || const_h) ? 8 : 12;
+    size_t cell_bytes = (mode == MODE_QUANT || const_h) ? 8 : 12;  // two or three 32-bit planes
     size_t budget = 200 * 1024;
     int fg_max = (int)(budget / ((size_t)B * cell_bytes)) / 16 * 16;
     fg_max = std::max(16, std::min(128, fg_max));
@@ -286,11 +382,27 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     hl.threads = per_sm >= 2 ? 512 : 1024;
     per_sm = std::min(per_sm, 2048 / hl.threads);
     hl.row_ctas = std::max(1, (n_sm * per_sm + hl.groups - 1) / hl.groups);
+    hl.cluster = 1;
+    for (int cs : {8, 4, 2, 1}) {
+      if (hl.row_ctas < cs) continue;
+      int n_clusters = 0;
+      cudaError_t oe;
+      if (mode == MODE_QUANT) oe = prepare_hist<MODE_QUANT, false>(hl, cs, &n_clusters);
+      else if (const_h) oe = prepare_hist<MODE_FIXED, true>(hl, cs, &n_clusters);
+      else oe = prepare_hist<MODE_FIXED, false>(hl, cs, &n_clusters);
+      if (oe == cudaSuccess && n_clusters >= 1) {
+        hl.cluster = cs;
+        break;
+      }
+      cudaGetLastError();
+    }
+    hl.row_ctas = std::max(hl.cluster, hl.row_ctas / hl.cluster * hl.cluster);
   }
   long long rows_per_flush = 1ll << 40;
   if (mode == MODE_QUANT) {
-    long long gl = cfg.num_grad_quant_bins / 2, hlim = const_h ? 1 : cfg.num_grad_quant_bins;
-    rows_per_flush = std::min<long long>((1ll << 20) - 1, std::min(((1ll << 21) - 1) / gl, ((1ll << 22) - 1) / hlim));
+    // plane 0 holds g * 2^15 + count: count < 2^15 and |sum g| < 2^16 per flush
+    long long gl = cfg.num_grad_quant_bins / 2;
+    rows_per_flush = std::min<long long>((1ll << 15) - 1, ((1ll << 16) - 1) / gl);
   }
   const int part_grid = n_sm * 4;
   const int part_threads = 256;
@@ -323,25 +435,49 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
 
   auto t_fit = std::chrono::steady_clock::now();
   int launches = 0;
-  auto hist = [&](const int* r0, const int* r1, const void* p0, const void* p1) {
+  auto hist = [&]() {
     timer.begin(&stats.hist_ms);
     if (mode == MODE_QUANT)
-      launch_hist_v<MODE_QUANT, false>(hl, st, d_ts.p, d_bins_rm.p, Fp, F, B, r0, r1, p0, p1, d_hist.p, slot_cells,
-                                       rows_per_flush);
+      launch_hist<MODE_QUANT, false>(hl, st, d_ts.p, d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
+                                     d_pairs1.p, d_hist.p, slot_cells, rows_per_flush, work_slot);
     else if (const_h)
-      launch_hist_v<MODE_FIXED, true>(hl, st, d_ts.p, d_bins_rm.p, Fp, F, B, r0, r1, p0, p1, d_hist.p, slot_cells,
-                                      rows_per_flush);
+      launch_hist<MODE_FIXED, true>(hl, st, d_ts.p, d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
+                                    d_pairs1.p, d_hist.p, slot_cells, rows_per_flush, work_slot);
     else
-      launch_hist_v<MODE_FIXED, false>(hl, st, d_ts.p, d_bins_rm.p, Fp, F, B, r0, r1, p0, p1, d_hist.p, slot_cells,
-                                       rows_per_flush);
+      launch_hist<MODE_FIXED, false>(hl, st, d_ts.p, d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
+                                     d_pairs1.p, d_hist.p, slot_cells, rows_per_flush, work_slot);
     timer.end();
-    stats.hist_launches++;
-    launches++;
+  };
+  // the built child's cells summed over every device's rows (exact int32)
+  auto reduce_work = [&]() {
+    if (coll) coll->allreduce_sum_i32(d_hist.p + (size_t)work_slot * slot_cells, (size_t)slot_cells, st);
   };
 
   const long long grid1024 = (N + 1023) / 1024;
   const unsigned grid256 = (unsigned)((N + 255) / 256);
-  int n_trees_total = 0;
+  const bool use_graph = !cfg.profile_phases;
+  std::vector<cudaGraphExec_t> graphs(K, nullptr);
+  struct GraphGuard {
+    std::vector<cudaGraphExec_t>& g;
+    ~GraphGuard() {
+      for (auto x : g)
+        if (x) cudaGraphExecDestroy(x);
+    }
+  } gg{graphs};
+  std::vector<cudaEvent_t> round_ev;
+  struct EventGuard {
+    std::vector<cudaEvent_t>& e;
+    ~EventGuard() {
+      for (auto x : e) cudaEventDestroy(x);
+    }
+  } eg{round_ev};
+  auto mark_round = [&]() {
+    cudaEvent_t e;
+    MTB_CUDA(cudaEventCreate(&e));
+    round_ev.push_back(e);
+    MTB_CUDA(cudaEventRecord(e, st));
+  };
+  mark_round();
   for (int it = 0; it < cfg.num_iterations; ++it) {
     if (K > 1) {
       k_softmax<<<grid256, 256, 0, st>>>(d_raw.p, d_prob.p, N, K);
@@ -353,6 +489,10 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       // ---- derivatives, scales, quantized pairs
       timer.begin(&stats.grad_ms);
       MTB_CUDA(cudaMemsetAsync(d_sc.p, 0, sizeof(RoundScales), st));
+      if (coll && mode == MODE_FIXED) {
+        MTB_CUDA(cudaMemsetAsync(d_pg.p, 0, sizeof(double) * P_rank, st));
+        MTB_CUDA(cudaMemsetAsync(d_ph.p, 0, sizeof(double) * P_rank, st));
+      }
       if (K == 1)
         k_grad<<<(unsigned)grid1024, 1024, 0, st>>>(d_raw.p, d_y.p, d_g.p, d_h.p, N, cfg.objective, mode, d_pg.p,
                                                     d_ph.p, d_sc.p);
@@ -362,11 +502,19 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       launches++;
       const double* tot_g = d_pg.p;
       const double* tot_h = d_ph.p;
+      if (mode == MODE_QUANT && coll)
+        coll->allreduce_max_u64(reinterpret_cast<unsigned long long*>(&d_sc.p->g_total), 2, st);
       if (mode == MODE_FIXED) {
         // pairwise levels: 1024 partials -> 1, outputs packed one after another
         long long n = n_part, off = 0;
         const double* ig = d_pg.p;
         const double* ih = d_ph.p;
+        if (coll) {
+          coll->allgather_f64(d_pg.p, d_pg_all.p, P_rank, st);
+          coll->allgather_f64(d_ph.p, d_ph_all.p, P_rank, st);
+          ig = d_pg_all.p;
+          ih = d_ph_all.p;
+        }
         while (n > 1) {
           long long nb = (n + 1023) / 1024;
           double* og = d_tg.p + off;
@@ -385,11 +533,11 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       uint64_t gs = mt_quant_stream(cfg.quant_seed, it, k, 0);
       uint64_t hs = mt_quant_stream(cfg.quant_seed, it, k, 1);
       if (mode == MODE_QUANT)
-        k_quantize<MODE_QUANT><<<grid256, 256, 0, st>>>(d_g.p, d_h.p, N, 0, d_sc.p, const_h, gs, hs, d_rows0.p,
-                                                         d_pairs0.p);
+        k_quantize<MODE_QUANT><<<grid256, 256, 0, st>>>(d_g.p, d_h.p, N, in.row_offset, d_sc.p, const_h, gs, hs,
+                                                         d_rows0.p, d_pairs0.p);
       else
-        k_quantize<MODE_FIXED><<<grid256, 256, 0, st>>>(d_g.p, d_h.p, N, 0, d_sc.p, const_h, gs, hs, d_rows0.p,
-                                                         d_pairs0.p);
+        k_quantize<MODE_FIXED><<<grid256, 256, 0, st>>>(d_g.p, d_h.p, N, in.row_offset, d_sc.p, const_h, gs, hs,
+                                                         d_rows0.p, d_pairs0.p);
       launches += 2;
       timer.end();
 
@@ -427,54 +575,72 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       sp.n_active = n_active;
       const dim3 scan_grid(2, (unsigned)((n_active + kScanWarps - 1) / kScanWarps));
 
-      // ---- grow the tree
-      MTB_CUDA(cudaMemsetAsync(d_hist.p, 0, sizeof(long long) * slot_cells, st));
-      k_tree_init<<<1, 32, 0, st>>>(d_ts.p, N);
-      launches++;
-      hist(d_rows0.p, d_rows1.p, d_pairs0.p, d_pairs1.p);
-      timer.begin(&stats.scan_ms);
-      k_scan<<<scan_grid, kScanWarps * 32, 0, st>>>(d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p,
-                                                    d_ncats.p, d_sc.p, sp, d_fb.p, 1);
-      k_finish<<<1, 256, 0, st>>>(d_ts.p, d_fb.p, d_feats.p, d_sc.p, sp, 1);
-      timer.end();
-      launches += 2;
-      for (int s = 1; s < cfg.num_leaves; ++s) {
-        k_pick<<<1, 256, 0, st>>>(d_ts.p, d_missing.p);
-        timer.begin(&stats.partition_ms);
-        if (mode == MODE_QUANT)
-          k_partition<uint16_t, 8><<<part_grid, part_threads, 0, st>>>(
-              d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<uint16_t*>(d_pairs0.p),
-              reinterpret_cast<uint16_t*>(d_pairs1.p), d_hist.p, slot_cells);
-        else
-          k_partition<int2, 8><<<part_grid, part_threads, 0, st>>>(
-              d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<int2*>(d_pairs0.p),
-              reinterpret_cast<int2*>(d_pairs1.p), d_hist.p, slot_cells);
-        timer.end();
-        hist(d_rows0.p, d_rows1.p, d_pairs0.p, d_pairs1.p);
+      // ---- grow the tree: a fixed launch sequence, replayed as a CUDA graph
+      // (one per class and feature count) unless per-phase timing is requested
+      auto grow = [&]() {
+        MTB_CUDA(cudaMemsetAsync(d_hist.p + (size_t)work_slot * slot_cells, 0, sizeof(int) * slot_cells, st));
+        k_tree_init<<<1, 32, 0, st>>>(d_ts.p, N);
+        hist();
+        reduce_work();
         timer.begin(&stats.scan_ms);
         k_scan<<<scan_grid, kScanWarps * 32, 0, st>>>(d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p,
-                                                      d_ncats.p, d_sc.p, sp, d_fb.p, 0);
-        k_finish<<<1, 256, 0, st>>>(d_ts.p, d_fb.p, d_feats.p, d_sc.p, sp, 0);
+                                                      d_ncats.p, d_sc.p, sp, d_fb.p, 1, work_slot, cfg.num_leaves);
         timer.end();
-        launches += 4;
+        for (int s = 1; s < cfg.num_leaves; ++s) {
+          timer.begin(&stats.partition_ms);
+          if (mode == MODE_QUANT)
+            k_partition<uint16_t, 8><<<part_grid, part_threads, 0, st>>>(
+                d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<uint16_t*>(d_pairs0.p),
+                reinterpret_cast<uint16_t*>(d_pairs1.p), d_hist.p, slot_cells, work_slot);
+          else
+            k_partition<int2, 8><<<part_grid, part_threads, 0, st>>>(
+                d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<int2*>(d_pairs0.p),
+                reinterpret_cast<int2*>(d_pairs1.p), d_hist.p, slot_cells, work_slot);
+          timer.end();
+          hist();
+          reduce_work();
+          timer.begin(&stats.scan_ms);
+          k_scan<<<scan_grid, kScanWarps * 32, 0, st>>>(d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p,
+                                                        d_ncats.p, d_sc.p, sp, d_fb.p, 0, work_slot, cfg.num_leaves);
+          timer.end();
+        }
+        k_leaf_table<<<1, 1024, 0, st>>>(d_ts.p, d_begins.p, d_order.p);
+        k_update_raw<<<grid256, 256, 0, st>>>(d_ts.p, d_begins.p, d_order.p, d_rows0.p, d_rows1.p, d_raw.p, N, K,
+                                              k, cfg.learning_rate);
+      };
+      const int tree_launches = 3 + 3 * (cfg.num_leaves - 1) + 2;
+      // the scan grid depends on the active feature count, fixed per fit
+      // unless feature_fraction draws a different count (then no graph)
+      const bool graph_ok = use_graph && (cfg.feature_fraction >= 1.0);
+      if (graph_ok) {
+        if (!graphs[k]) {
+          cudaGraph_t g;
+          MTB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+          grow();
+          MTB_CUDA(cudaStreamEndCapture(st, &g));
+          cudaError_t ie = cudaGraphInstantiate(&graphs[k], g, 0);
+          cudaGraphDestroy(g);
+          MTB_CUDA(ie);
+        }
+        MTB_CUDA(cudaGraphLaunch(graphs[k], st));
+      } else {
+        grow();
       }
-      k_leaf_table<<<1, 1024, 0, st>>>(d_ts.p, d_begins.p, d_order.p);
-      k_update_raw<<<grid256, 256, 0, st>>>(d_ts.p, d_begins.p, d_order.p, d_rows0.p, d_rows1.p, d_raw.p, N, K, k,
-                                            cfg.learning_rate);
-      launches += 2;
+      launches += tree_launches;
       MTB_CUDA(cudaGetLastError());
       MTB_CUDA(cudaMemcpyAsync(&hdr, &d_ts.p->hdr, sizeof(TreeHeader), cudaMemcpyDeviceToHost, st));
       MTB_CUDA(cudaMemcpyAsync(nodes_host.data(), d_ts.p->nodes, sizeof(HostNode) * M, cudaMemcpyDeviceToHost, st));
       MTB_CUDA(cudaStreamSynchronize(st));
       timer.collect();
       if (hdr.error) throw std::runtime_error("device trainer reported an internal error");
+      if (coll) coll->check();
       std::vector<HostNode> tree(nodes_host.begin(), nodes_host.begin() + hdr.n_nodes);
       bool trivial = hdr.n_leaves == 1 && std::fabs(tree[0].value) < 1e-12;
       if (!trivial) progress = true;
       model.trees.push_back(std::move(tree));
-      ++n_trees_total;
     }
     stats.rounds++;
+    mark_round();
     if (!progress) {
       // boosting.mojo:2898-2907 / :4153-4162: a round that grew nothing ends the fit
       model.trees.resize(first_tree);
@@ -482,8 +648,14 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     }
   }
   MTB_CUDA(cudaStreamSynchronize(st));
+  for (size_t i = 0; i + 1 < round_ev.size(); ++i) {
+    float ms = 0.f;
+    MTB_CUDA(cudaEventElapsedTime(&ms, round_ev[i], round_ev[i + 1]));
+    stats.round_ms.push_back(ms);
+  }
   stats.fit_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t_fit).count();
   stats.kernel_launches += launches;
+  stats.hist_launches = (int)(model.trees.size() * (size_t)cfg.num_leaves);
   // rows read by histogram builds: every root plus the smaller child of every split
   for (size_t t = 0; t < model.trees.size(); ++t) {
     const auto& tr = model.trees[t];

@@ -20,6 +20,12 @@ struct BinnedInput {
   const int* missing_bin;   // [n_features], -1 when none
   const int* n_cats;        // [n_features], -1 numeric, else kept categories
   const double* labels;     // [n_rows]
+  // Data-parallel fits (one process per GPU): this device's rows are global
+  // rows [row_offset, row_offset + n_rows); every shard but the last holds a
+  // multiple of 1024 rows.  coll == nullptr for a single-device fit.
+  long long row_offset = 0;
+  long long n_rows_global = 0;
+  class Collective* coll = nullptr;
 };
 
 // Trains on the current (or configured) CUDA device; fills model.trees,

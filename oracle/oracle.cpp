@@ -295,8 +295,13 @@ void dequantize(const Ctx& c, const RoundState& st, Hist& h, const std::vector<i
     g_inv = 1.0 / (double)st.gsf;
     h_inv = 1.0 / (double)st.hsf;
   } else {
-    g_inv = 1.0 / st.g_units;
-    h_inv = 1.0 / st.h_units;
+    for (int f : feats)
+      for (int b = 0; b < B; ++b) {
+        size_t i = (size_t)f * B + b;
+        h.gh[2 * i] = (double)h.qg[i] / st.g_units;
+        h.gh[2 * i + 1] = (double)h.qh[i] / st.h_units;
+      }
+    return;
   }
   for (int f : feats)
     for (int b = 0; b < B; ++b) {
@@ -566,6 +571,167 @@ CatResult categorical_split(const Ctx& c, const Hist& h, int f, int n_cat, Total
   return best;
 }
 
+// MODE_QUANT split scan: the reference's quantized gain
+// (quantized_gradient.mojo:3252-3309, dequant f64(q) / units at :1324-1328)
+// evaluated on exact integer prefix sums; the threshold loop, guards, missing
+// handling and tie rules are find_best_split's.
+inline double dq(int64_t q, double units) { return (double)q / units; }
+
+Split find_best_split_quant(const Ctx& c, const RoundState& st, const Hist& h, const std::vector<int>& feats) {
+  const mt_oracle_params& p = c.p;
+  int B = c.d.B;
+  int nf = (int)feats.size();
+  const double gu = st.g_units, hu = st.h_units, l1 = p.lambda_l1, l2 = p.lambda_l2, mch = p.min_child_hess;
+  std::vector<Split> res(nf);
+  for (int j = 0; j < nf; ++j) {
+    int f = feats[j];
+    const int64_t* qg = h.qg.data() + (size_t)f * B;
+    const int64_t* qh = h.qh.data() + (size_t)f * B;
+    const int64_t* cn = h.cnt.data() + (size_t)f * B;
+    int64_t Tg = 0, Th = 0, Tc = 0;
+    for (int b = 0; b < B; ++b) {
+      Tg += qg[b];
+      Th += qh[b];
+      Tc += cn[b];
+    }
+    double tg = dq(Tg, gu), th = dq(Th, hu);
+    Split s;
+    if (c.d.n_cats[f] >= 0) {
+      int n_cat = c.d.n_cats[f];
+      double parent = leaf_score(tg, th, l1, l2);
+      CatResult best;
+      if (n_cat >= 2 && n_cat + 1 <= p.max_cat_to_onehot) {
+        for (int t = 1; t <= n_cat && t < B; ++t) {
+          double lgv = dq(qg[t], gu), lhv = dq(qh[t], hu);
+          if (cn[t] < p.min_data_in_leaf || lhv < mch) continue;
+          if (Tc - cn[t] < p.min_data_in_leaf) continue;
+          double rh = dq(Th - qh[t], hu);
+          if (rh < mch) continue;
+          double rg = dq(Tg - qg[t], gu);
+          double gain = leaf_score(lgv, lhv, l1, l2) + leaf_score(rg, rh, l1, l2) - parent;
+          if (gain > best.gain) {
+            best = CatResult();
+            best.gain = gain;
+            cat_add(best.bits, t);
+            best.found = true;
+          }
+        }
+      } else if (n_cat >= 2) {
+        std::vector<int> cand;
+        std::vector<double> keys;
+        for (int t = 1; t <= n_cat && t < B; ++t) {
+          if (!((double)cn[t] >= p.cat_smooth)) continue;
+          cand.push_back(t);
+          keys.push_back(dq(qg[t], gu) / (dq(qh[t], hu) + p.cat_smooth));
+        }
+        int used = (int)cand.size();
+        if (used >= 2) {
+          std::vector<int> order(used);
+          for (int i = 0; i < used; ++i) order[i] = i;
+          std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return keys[a] < keys[b]; });
+          std::vector<int> sb(used);
+          for (int i = 0; i < used; ++i) sb[i] = cand[order[i]];
+          int max_num_cat = std::min(p.max_cat_threshold, (used + 1) / 2);
+          if (max_num_cat < 0) max_num_cat = 0;
+          double cl2 = l2 + p.cat_l2;
+          for (int dd = 0; dd < 2; ++dd) {
+            int dir = dd == 0 ? 1 : -1, start = dd == 0 ? 0 : used - 1, pos = start;
+            int64_t cnt_group = 0, lq = 0, lh = 0, lc = 0;
+            int steps = used < max_num_cat ? used : max_num_cat;
+            for (int i = 0; i < steps; ++i) {
+              int t = sb[pos];
+              pos += dir;
+              lq += qg[t];
+              lh += qh[t];
+              lc += cn[t];
+              cnt_group += cn[t];
+              double lgv = dq(lq, gu), lhv = dq(lh, hu);
+              if (lc < p.min_data_in_leaf || lhv < mch) continue;
+              int64_t rc = Tc - lc;
+              if (rc < p.min_data_in_leaf || rc < p.min_data_per_group) break;
+              double rh = dq(Th - lh, hu);
+              if (rh < mch) break;
+              if (cnt_group < p.min_data_per_group) continue;
+              cnt_group = 0;
+              double rg = dq(Tg - lq, gu);
+              double gain = leaf_score(lgv, lhv, l1, cl2) + leaf_score(rg, rh, l1, cl2) - parent;
+              if (gain > best.gain) {
+                best = CatResult();
+                best.gain = gain;
+                int q = start;
+                for (int k = 0; k <= i; ++k) {
+                  cat_add(best.bits, sb[q]);
+                  q += dir;
+                }
+                best.found = true;
+              }
+            }
+          }
+        }
+      }
+      if (best.found) {
+        s.feature = f;
+        s.gain = best.gain;
+        s.found = true;
+        s.is_cat = true;
+        memcpy(s.bits, best.bits, sizeof s.bits);
+      }
+      res[j] = s;
+      continue;
+    }
+    int mb = c.d.missing_bin[f];
+    int n_scan = mb >= 0 ? mb : B;
+    int64_t mg = 0, mh = 0, mc = 0;
+    if (mb >= 0) {
+      mg = qg[mb];
+      mh = qh[mb];
+      mc = cn[mb];
+    }
+    int64_t Lg = 0, Lh = 0, Lc = 0;
+    double f_gain = 0.0;
+    for (int b = 0; b < n_scan; ++b) {
+      if (b == n_scan - 1 && mc == 0) break;
+      Lg += qg[b];
+      Lh += qh[b];
+      Lc += cn[b];
+      if (mb >= 0) {
+        int64_t Dg = Lg + mg, Dh = Lh + mh, Dc = Lc + mc;
+        double dlg = dq(Dg, gu), dlh = dq(Dh, hu), drg = dq(Tg - Dg, gu), drh = dq(Th - Dh, hu);
+        if (!(dlh < mch || drh < mch || Dc < p.min_data_in_leaf || Tc - Dc < p.min_data_in_leaf)) {
+          double gain = leaf_score(dlg, dlh, l1, l2) + leaf_score(drg, drh, l1, l2) - leaf_score(tg, th, l1, l2);
+          if (gain > f_gain) {
+            f_gain = gain;
+            s.bin = b;
+            s.default_left = true;
+            s.found = true;
+          }
+        }
+      }
+      if (mb < 0 || mc > 0) {
+        double lgv = dq(Lg, gu), lhv = dq(Lh, hu), rg = dq(Tg - Lg, gu), rh = dq(Th - Lh, hu);
+        if (!(lhv < mch || rh < mch || Lc < p.min_data_in_leaf || Tc - Lc < p.min_data_in_leaf)) {
+          double gain = leaf_score(lgv, lhv, l1, l2) + leaf_score(rg, rh, l1, l2) - leaf_score(tg, th, l1, l2);
+          if (gain > f_gain) {
+            f_gain = gain;
+            s.bin = b;
+            s.default_left = false;
+            s.found = true;
+          }
+        }
+      }
+    }
+    if (s.found) {
+      s.feature = f;
+      s.gain = f_gain;
+    }
+    res[j] = s;
+  }
+  Split best;
+  for (int j = 0; j < nf; ++j)
+    if (res[j].found && res[j].gain > best.gain) best = res[j];
+  return best;
+}
+
 Split find_best_split(const Ctx& c, const Hist& h, const std::vector<int>& feats) {
   const mt_oracle_params& p = c.p;
   int B = c.d.B;
@@ -657,8 +823,17 @@ Split find_best_split(const Ctx& c, const Hist& h, const std::vector<int>& feats
   return best;
 }
 
-double leaf_value(const Ctx& c, const Hist& h, int value_feature) {
+double leaf_value(const Ctx& c, const RoundState& st, const Hist& h, int value_feature) {
   int B = c.d.B;
+  if (c.p.mode == MODE_QUANT) {
+    // quantized_leaf_output (quantized_gradient.mojo:3312-3333) on the node totals
+    int64_t G = 0, H = 0;
+    for (int b = 0; b < B; ++b) {
+      G += h.qg[(size_t)value_feature * B + b];
+      H += h.qh[(size_t)value_feature * B + b];
+    }
+    return -soft_l1(dq(G, st.g_units), c.p.lambda_l1) / (dq(H, st.h_units) + c.p.lambda_l2);
+  }
   const double* gh = h.gh.data() + (size_t)2 * value_feature * B;
   double g = 0.0, hh = 0.0;
   for (int b = 0; b < B; ++b) {
@@ -687,8 +862,9 @@ struct Leaf {
   Split split;
 };
 
-Split search(const Ctx& c, const Hist& h, int64_t n_rows, const std::vector<int>& feats) {
+Split search(const Ctx& c, const RoundState& st, const Hist& h, int64_t n_rows, const std::vector<int>& feats) {
   if (n_rows < 2 * (int64_t)c.p.min_data_in_leaf || n_rows < 2) return Split();
+  if (c.p.mode == MODE_QUANT) return find_best_split_quant(c, st, h, feats);
   return find_best_split(c, h, feats);
 }
 
@@ -708,8 +884,8 @@ Tree grow_tree(const Ctx& c, const RoundState& st, const std::vector<int64_t>& b
   }
   build_hist(c, st, root.rows, feats, root.hist);
   int value_feature = feats[0];
-  root.node = tree.add_node(leaf_value(c, root.hist, value_feature), (int64_t)root.rows.size());
-  root.split = search(c, root.hist, (int64_t)root.rows.size(), feats);
+  root.node = tree.add_node(leaf_value(c, st, root.hist, value_feature), (int64_t)root.rows.size());
+  root.split = search(c, st, root.hist, (int64_t)root.rows.size(), feats);
   int n_leaves = 1;
   while (n_leaves < p.num_leaves) {
     int best_i = -1;
@@ -739,8 +915,8 @@ Tree grow_tree(const Ctx& c, const RoundState& st, const std::vector<int64_t>& b
       build_hist(c, st, R.rows, feats, R.hist);
       subtract_hist(c, st, parent.hist, R.hist, feats, L.hist);
     }
-    double lv = leaf_value(c, L.hist, value_feature);
-    double rv = leaf_value(c, R.hist, value_feature);
+    double lv = leaf_value(c, st, L.hist, value_feature);
+    double rv = leaf_value(c, st, R.hist, value_feature);
     L.node = tree.add_node(lv, (int64_t)L.rows.size());
     R.node = tree.add_node(rv, (int64_t)R.rows.size());
     int pn = parent.node;
@@ -759,8 +935,8 @@ Tree grow_tree(const Ctx& c, const RoundState& st, const std::vector<int64_t>& b
       tree.dleft[pn] = split.default_left;
       tree.mbin[pn] = mbin;
     }
-    L.split = search(c, L.hist, (int64_t)L.rows.size(), feats);
-    R.split = search(c, R.hist, (int64_t)R.rows.size(), feats);
+    L.split = search(c, st, L.hist, (int64_t)L.rows.size(), feats);
+    R.split = search(c, st, R.hist, (int64_t)R.rows.size(), feats);
     frontier[best_i] = std::move(L);
     frontier.push_back(std::move(R));
     ++n_leaves;

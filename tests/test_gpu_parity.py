@@ -1,0 +1,106 @@
+"""GPU trainer (through the C ABI) vs the CPU oracle: bit-exact trees.
+
+Both integer histogram modes are exact by construction, so every tree array,
+every leaf value and gain (as IEEE bits) and every training raw score must be
+identical to the oracle run in the same mode on the same bins.  Cases follow
+the reference's own test strategy (tests/test_gpu_training.mojo,
+tests/test_host_replica.mojo): several objectives, missing values,
+categorical splits, feature sampling, tiny and ragged shapes.
+"""
+import numpy as np
+import pytest
+
+from parity_util import assert_models_identical, make_data, oracle_kwargs, params_for
+
+pytestmark = pytest.mark.gpu
+
+CASES = {
+    # name: (data kwargs, params kwargs, max_bin)
+    "l2_fixed": (dict(seed=1, n=50_000, f=28), dict(objective="regression", rounds=4, leaves=63), 255),
+    "l2_quant": (dict(seed=2, n=40_000, f=28), dict(objective="regression", rounds=4, leaves=63, quant=True), 255),
+    "binary_fixed": (dict(seed=3, n=30_000, f=20, kind="binary"), dict(objective="binary", rounds=4, leaves=31), 255),
+    "binary_quant": (dict(seed=4, n=30_000, f=20, kind="binary"),
+                     dict(objective="binary", rounds=5, leaves=63, quant=True), 255),
+    "binary_quant_large": (dict(seed=16, n=300_000, f=100, kind="binary"),
+                           dict(objective="binary", rounds=2, leaves=255, quant=True), 255),
+    "multiclass_fixed": (dict(seed=5, n=20_000, f=12, kind="multiclass", n_classes=4),
+                         dict(objective="multiclass", rounds=3, leaves=15, n_classes=4), 255),
+    "multiclass_quant": (dict(seed=6, n=20_000, f=12, kind="multiclass", n_classes=4),
+                         dict(objective="multiclass", rounds=3, leaves=15, n_classes=4, quant=True), 255),
+    "missing_cat_fixed": (dict(seed=7, n=20_000, f=8, nan_frac=0.1, cat_cols=(2, 5), n_cat=12),
+                          dict(objective="regression", rounds=4, leaves=31,
+                               extra={"categorical_feature": "2,5", "min_data_per_group": 20, "cat_smooth": 5.0}), 63),
+    "missing_cat_quant": (dict(seed=8, n=20_000, f=8, nan_frac=0.1, cat_cols=(2, 5), n_cat=3, kind="binary"),
+                          dict(objective="binary", rounds=4, leaves=31, quant=True,
+                               extra={"categorical_feature": "2,5"}), 63),
+    "feature_fraction": (dict(seed=9, n=20_000, f=24), dict(objective="regression", rounds=4, leaves=31,
+                                                            extra={"feature_fraction": 0.5}), 255),
+    "wide_features": (dict(seed=10, n=10_000, f=150), dict(objective="regression", rounds=2, leaves=31), 255),
+    "tiny_ragged": (dict(seed=11, n=37, f=3), dict(objective="regression", rounds=3, leaves=4, min_data=3), 255),
+    "two_leaves": (dict(seed=12, n=5_000, f=5, kind="binary"), dict(objective="binary", rounds=3, leaves=2), 255),
+}
+
+
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_gpu_matches_oracle(case, mtlib, oracle):
+    dkw, pkw, max_bin = CASES[case]
+    pkw = dict(pkw)
+    X, y = make_data(**dkw)
+    extra = pkw.pop("extra", {})
+    p = params_for(pkw.pop("objective"), pkw.pop("rounds"), pkw.pop("leaves"), extra=extra, **pkw)
+    p["max_bin"] = max_bin
+    bins, mbin, ncat, nb = mtlib.bin_dense(X, {k: v for k, v in p.items() if k in ("max_bin", "categorical_feature")})
+    gm = mtlib.train_binned(bins, nb, y, p, missing_bin=mbin, n_categories=ncat)
+    om = oracle.train(bins, nb, y, missing_bin=mbin, n_cats=ncat, **oracle_kwargs(p))
+    assert_models_identical(gm, om, len(y))
+
+
+def test_gpu_no_split_single_leaf_trees(mtlib, oracle):
+    """min_data_in_leaf above n/2: the root never splits; every tree is one
+    leaf, identical to the oracle's (its value is the Float32-narrowed
+    gradient sum, not exactly 0, so the fit does not stop early)."""
+    X, y = make_data(13, 1000, 4)
+    p = params_for("regression", 5, 31, min_data=600)
+    bins, mbin, ncat, nb = mtlib.bin_dense(X, {"max_bin": 255})
+    gm = mtlib.train_binned(bins, nb, y, p, missing_bin=mbin, n_categories=ncat)
+    om = oracle.train(bins, nb, y, missing_bin=mbin, n_cats=ncat, **oracle_kwargs(p))
+    assert_models_identical(gm, om, len(y))
+    assert all(len(gm.tree(t)["feature"]) == 1 for t in range(gm.num_trees))
+
+
+def test_gpu_constant_target_stops(mtlib, oracle):
+    """A constant L2 target: gradients are exactly 0, the first tree is a
+    zero-valued leaf and the fit stops with no tree (boosting.mojo:2898-2907)."""
+    X, _ = make_data(15, 2000, 4)
+    y = np.full(2000, 0.25)
+    p = params_for("regression", 5, 31)
+    bins, mbin, ncat, nb = mtlib.bin_dense(X, {"max_bin": 255})
+    gm = mtlib.train_binned(bins, nb, y, p, missing_bin=mbin, n_categories=ncat)
+    om = oracle.train(bins, nb, y, missing_bin=mbin, n_cats=ncat, **oracle_kwargs(p))
+    assert gm.num_trees == om.n_trees == 0
+
+
+def test_gpu_dense_entry_matches_binned(mtlib):
+    """mojotrees_train_dense (host binning + device) equals the binned entry."""
+    X, y = make_data(14, 8000, 6, kind="binary", nan_frac=0.05)
+    p = params_for("binary", 3, 15)
+    dm = mtlib.train_dense(X, y, p)
+    bins, mbin, ncat, nb = mtlib.bin_dense(X, {})
+    bm = mtlib.train_binned(bins, nb, y, p, missing_bin=mbin, n_categories=ncat)
+    assert dm.num_trees == bm.num_trees
+    for t in range(dm.num_trees):
+        a, b = dm.tree(t), bm.tree(t)
+        for k in a:
+            np.testing.assert_array_equal(a[k], b[k])
+    np.testing.assert_array_equal(dm.predict(X, raw_score=True), bm.predict_binned(bins))
+
+
+def test_gpu_round_times_and_stats(mtlib):
+    X, y = make_data(17, 20_000, 10, kind="binary")
+    bins, mbin, ncat, nb = mtlib.bin_dense(X, {})
+    m = mtlib.train_binned(bins, nb, y, params_for("binary", 4, 31, quant=True), missing_bin=mbin,
+                           n_categories=ncat)
+    rt = m.round_times_ms()
+    assert len(rt) == 4 and np.all(rt > 0)
+    st = m.stats()
+    assert st["hist_rows"] >= 4 * 20_000 and st["kernel_launches"] > 0
