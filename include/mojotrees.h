@@ -188,6 +188,19 @@ int32_t mojotrees_b200_train_binned_u8_dp(const uint8_t *bins, int64_t n_rows, i
                                           const uint8_t *nccl_id, int32_t rank, int32_t world, int64_t row_offset,
                                           int64_t n_rows_global, MojoTreesModel **out_model, MojoTreesError *error);
 
+/* One quantized-gradient histogram, built by the trainer's per-leaf kernel:
+ * for the selected rows (rows = NULL: all rows), per feature and bin, the
+ * sums of grad_q and hess_q and the row count.  bins is feature-major
+ * (bins[f * n_rows + r] < n_bins); grad_q[r] in [-q/2, q/2] and hess_q[r] in
+ * [0, q] for q = num_grad_quant_bins (the int8 packer's range).  out_hist
+ * receives n_features * 3 * n_bins int32, laid out [feature][g, h, count][bin].
+ * Host buffers; the call allocates device memory.  The device kernel behind
+ * gpu_active_rows.mojo:3903 (_range_hist_atomic_kernel) in the reference. */
+int32_t mojotrees_b200_histogram_u8(const uint8_t *bins, int64_t n_rows, int64_t n_features, int32_t n_bins,
+                                    const int32_t *rows, int64_t n_sel, const int8_t *grad_q,
+                                    const uint8_t *hess_q, int32_t num_grad_quant_bins, int32_t *out_hist,
+                                    MojoTreesError *error);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

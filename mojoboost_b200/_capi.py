@@ -57,6 +57,7 @@ SIGNATURES = {
     "mojotrees_b200_train_stats": (_I32, [_P, _P, _I64, _P, _P]),
     "mojotrees_b200_round_times": (_I32, [_P, _P, _I64, _P, _P]),
     "mojotrees_b200_nccl_unique_id": (_I32, [_P, _P]),
+    "mojotrees_b200_histogram_u8": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _I32, _P, _P]),
     "mojotrees_b200_train_binned_u8_dp": (_I32, [_P, _I64, _I64, _I32, _P, _P, _P, _P, ctypes.c_char_p, _P, _I32,
                                                  _I32, _I64, _I64, _P, _P]),
 }
@@ -281,6 +282,20 @@ def train_binned(bins_fm, n_bins, y, params=None, missing_bin=None, n_categories
     e.check(lib().mojotrees_b200_train_binned_u8(_ptr(bins_fm), n, f, n_bins, _ptr(mb), _ptr(nc), _ptr(y), None,
                                                  params_string(params), ctypes.byref(h), e.h))
     return Model(h.value)
+
+
+def histogram_u8(bins_fm, n_bins, grad_q, hess_q, rows=None, num_grad_quant_bins=4):
+    """Quantized histogram [n_features, 3, n_bins] (sum g, sum h, count) of the selected rows."""
+    bins_fm = np.ascontiguousarray(bins_fm, dtype=np.uint8)
+    f, n = bins_fm.shape
+    g = np.ascontiguousarray(grad_q, dtype=np.int8)
+    h = np.ascontiguousarray(hess_q, dtype=np.uint8)
+    r = None if rows is None else np.ascontiguousarray(rows, dtype=np.int32)
+    out = np.zeros((f, 3, n_bins), np.int32)
+    e = _Err()
+    e.check(lib().mojotrees_b200_histogram_u8(_ptr(bins_fm), n, f, n_bins, _ptr(r), 0 if r is None else r.size,
+                                              _ptr(g), _ptr(h), num_grad_quant_bins, _ptr(out), e.h))
+    return out
 
 
 def nccl_unique_id():

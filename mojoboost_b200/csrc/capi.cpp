@@ -23,6 +23,7 @@
 
 #include "../../include/mojotrees.h"
 #include "binning.h"
+#include "capi_util.h"
 #include "collective.h"
 #include "model.h"
 #include "trainer.h"
@@ -34,6 +35,15 @@ struct MojoTreesError {
 struct MojoTreesModel {
   mtb::Model m;
 };
+
+namespace mtb {
+void capi_set_error(MojoTreesError* e, const std::string& msg) {
+  if (e) e->message = msg;
+}
+void capi_clear_error(MojoTreesError* e) {
+  if (e) e->message.clear();
+}
+}  // namespace mtb
 
 namespace {
 

@@ -21,6 +21,9 @@
 #include "mt_math.h"
 
 namespace mtb {
+// Kernels have internal linkage: each translation unit that launches them
+// (trainer.cu, histogram_api.cu) carries its own instantiation.
+namespace {
 
 // ---------------------------------------------------------------------------
 // Layout kernels
@@ -542,15 +545,13 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
 // Global cells are int32 [slot][F][3][B] (g, h, count): every sum is bounded
 // by 2^30 + n (FIXED, quantized_gradient.mojo:98-99) or by B * n (QUANT).
 constexpr int kQuantCountBits = 15;
-constexpr long long kMinRowsPerCta = 2048;
 
 struct HistJob {
   long long begin, count;
   int buf;
 };
 
-__device__ __forceinline__ HistJob hist_job(const TreeState* ts) {
-  const Plan& P = ts->plan;
+__device__ __forceinline__ HistJob hist_job(const Plan& P) {
   HistJob j;
   long long nl = (long long)P.cursor_left;
   if (P.built_is_left) {
@@ -569,28 +570,30 @@ __device__ __forceinline__ HistJob hist_job(const TreeState* ts) {
 // the cluster then merges the CS copies through distributed shared memory
 // (each CTA sums one CS-th of the cells across its peers) and only the
 // merged cells reach global memory, with one int32 atomic per plane.  Small
-// leaves activate fewer clusters (>= kMinRowsPerCta rows per CTA); a cluster
+// leaves activate fewer clusters (>= min_rows_per_cta rows per CTA); a cluster
 // that has no rows exits as a whole.  Every build lands in the work slot;
 // the scan kernel moves it into the child's slot after any cross-device sum.
 template <int VPR, int MODE, bool CONST_H>
-__global__ void __launch_bounds__(1024) k_hist(const TreeState* __restrict__ ts, const uint8_t* __restrict__ bins_rm,
+__global__ void __launch_bounds__(1024) k_hist(const Plan* __restrict__ plan, const uint8_t* __restrict__ bins_rm,
                                                int Fp, int F, int B, const int* __restrict__ rows0,
                                                const int* __restrict__ rows1, const void* __restrict__ pairs0,
                                                const void* __restrict__ pairs1, int* __restrict__ hist,
-                                               long long slot_cells, long long rows_per_flush, int work_slot) {
+                                               long long slot_cells, long long rows_per_flush, int work_slot,
+                                               int min_rows_per_cta) {
   namespace cg = cooperative_groups;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   constexpr int FG = VPR * 16;
   constexpr int NPLANE = (MODE == MODE_FIXED && !CONST_H) ? 3 : 2;
-  if (!ts->plan.active) return;  // uniform across the grid
-  const HistJob job = hist_job(ts);
+  if (!plan->active) return;  // uniform across the grid
+  const HistJob job = hist_job(*plan);
   if (job.count <= 0) return;
   cg::cluster_group cluster = cg::this_cluster();
   const int cs = (int)cluster.num_blocks();
   const int crank = (int)cluster.block_rank();
   const long long n_clusters = gridDim.y / cs;
   const long long cid = blockIdx.y / cs;
-  long long want = (job.count + kMinRowsPerCta * cs - 1) / (kMinRowsPerCta * cs);
+  const long long mrc = min_rows_per_cta;
+  long long want = (job.count + mrc * cs - 1) / (mrc * cs);
   long long nce = want < n_clusters ? want : n_clusters;
   if (cid >= nce) return;  // the whole cluster leaves together
   const long long cchunk = (job.count + nce - 1) / nce;
@@ -624,28 +627,44 @@ __global__ void __launch_bounds__(1024) k_hist(const TreeState* __restrict__ ts,
     long long pe = ps + rows_per_flush < e ? ps + rows_per_flush : e;
     for (int c = threadIdx.x; c < cells * NPLANE; c += blockDim.x) p0[c] = 0u;
     __syncthreads();
-    for (long long i = ps + rsub; vec_ok && i < pe; i += rpi) {
-      int r = __ldg(rows + i);
-      unsigned int a0, a1, a2 = 1u;
-      if (MODE == MODE_QUANT) {
-        uint16_t pr = __ldg(reinterpret_cast<const uint16_t*>(pairs) + i);
-        int g = (int)(int8_t)(pr & 0xff);
-        a0 = (unsigned int)(g * (1 << kQuantCountBits) + 1);
-        a1 = (unsigned int)(pr >> 8);
-      } else {
-        int2 pr = __ldg(reinterpret_cast<const int2*>(pairs) + i);
-        a0 = (unsigned int)pr.x;
-        a1 = CONST_H ? 1u : (unsigned int)pr.y;
+    // two rows in flight per thread: both gathers are issued before the
+    // shared-memory atomics of either, so the atomic pipe stays fed
+    for (long long i = ps + rsub; vec_ok && i < pe; i += 2 * rpi) {
+      const long long i2 = i + rpi;
+      const bool two = i2 < pe;
+      int r0 = __ldg(rows + i);
+      int r1 = two ? __ldg(rows + i2) : r0;
+      unsigned int a0[2], a1[2];
+      const unsigned int a2 = 1u;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        long long ii = u == 0 ? i : (two ? i2 : i);
+        if (MODE == MODE_QUANT) {
+          uint16_t pr = __ldg(reinterpret_cast<const uint16_t*>(pairs) + ii);
+          int g = (int)(int8_t)(pr & 0xff);
+          a0[u] = (unsigned int)(g * (1 << kQuantCountBits) + 1);
+          a1[u] = (unsigned int)(pr >> 8);
+        } else {
+          int2 pr = __ldg(reinterpret_cast<const int2*>(pairs) + ii);
+          a0[u] = (unsigned int)pr.x;
+          a1[u] = CONST_H ? 1u : (unsigned int)pr.y;
+        }
       }
-      uint4 bv = __ldg(reinterpret_cast<const uint4*>(bins_rm + (long long)r * Fp + f0 + v * 16));
-      const unsigned int w[4] = {bv.x, bv.y, bv.z, bv.w};
+      uint4 bv0 = __ldg(reinterpret_cast<const uint4*>(bins_rm + (long long)r0 * Fp + f0 + v * 16));
+      uint4 bv1 = __ldg(reinterpret_cast<const uint4*>(bins_rm + (long long)r1 * Fp + f0 + v * 16));
       const int base = v * 16 * B;
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        int cell = base + k * B + (int)((w[k >> 2] >> (8 * (k & 3))) & 0xffu);
-        atomicAdd(&p0[cell], a0);
-        atomicAdd(&p1[cell], a1);
-        if (NPLANE == 3) atomicAdd(&p2[cell], a2);
+      for (int u = 0; u < 2; ++u) {
+        if (u == 1 && !two) break;
+        const uint4 bv = u == 0 ? bv0 : bv1;
+        const unsigned int w[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          int cell = base + k * B + (int)((w[k >> 2] >> (8 * (k & 3))) & 0xffu);
+          atomicAdd(&p0[cell], a0[u]);
+          atomicAdd(&p1[cell], a1[u]);
+          if (NPLANE == 3) atomicAdd(&p2[cell], a2);
+        }
       }
     }
     cluster.sync();
@@ -715,99 +734,105 @@ __device__ __forceinline__ double deq(long long q, int mode, double inv, double 
   return mode == MODE_FIXED ? (double)q * inv : (double)q / units;
 }
 
-constexpr int kScanWarps = 8;
+constexpr int kScanThreads = 256;  // one thread per bin (B <= 256)
 
+// Block-wide inclusive sum of three int64 values per thread (bin order).
+__device__ __forceinline__ void block_scan3(long long& a, long long& b, long long& c, long long* sw /*[3][8]*/) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int k = 1; k < 32; k <<= 1) {
+    long long oa = __shfl_up_sync(0xffffffffu, a, k);
+    long long ob = __shfl_up_sync(0xffffffffu, b, k);
+    long long oc = __shfl_up_sync(0xffffffffu, c, k);
+    if (lane >= k) {
+      a += oa;
+      b += ob;
+      c += oc;
+    }
+  }
+  if (lane == 31) {
+    sw[w] = a;
+    sw[8 + w] = b;
+    sw[16 + w] = c;
+  }
+  __syncthreads();
+  long long pa = 0, pb = 0, pc = 0;
+  for (int q = 0; q < w; ++q) {
+    pa += sw[q];
+    pb += sw[8 + q];
+    pc += sw[16 + q];
+  }
+  a += pa;
+  b += pb;
+  c += pc;
+}
+
+// One block per (child, active feature), one thread per bin: sibling
+// subtraction, exact integer prefix sums, the reference gain per candidate
+// threshold, and a block arg-max that keeps the serial scan's tie rule
+// (first maximum in bin order, missing-left candidate before default-right).
 __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, long long slot_cells,
                           const int* __restrict__ feats, const int* __restrict__ missing_bin,
                           const int* __restrict__ n_cats, const RoundScales* __restrict__ sc, ScanParams sp,
                           FeatBest* __restrict__ out, int root, int work_slot) {
-  __shared__ int s_cells[kScanWarps][3][256];  // int32 cells, widened when summed
+  __shared__ int s_cells[3][256];
+  __shared__ long long s_w[24];
+  __shared__ double s_gain[8];
+  __shared__ int s_key[8];
+  __shared__ long long s_nl[8];
   const Plan& P = ts->plan;
-  if (!P.active) return;
-  int c = blockIdx.x;
-  if (c >= P.n_children) return;
-  int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int j = blockIdx.y * kScanWarps + w;
-  if (j >= sp.n_active) return;
+  if (!P.active) return;  // uniform
+  const int c = blockIdx.x;
+  if (c >= P.n_children) return;  // uniform
+  const int j = blockIdx.y;
+  const int t = threadIdx.x;
+  const int lane = t & 31, w = t >> 5;
   const int B = sp.B;
   const int f = feats[j];
   int* hs = hist + (long long)P.child_hist[c] * slot_cells + (long long)f * 3 * B;
   const bool built = root || P.child_hist[c] != P.sib_hist;
   const int* wk = hist + (long long)work_slot * slot_cells + (long long)f * 3 * B;
-  const double g_inv = sc->g_inv, h_inv = sc->h_inv, gu = sc->g_units, hu = sc->h_units;
   const int mode = sp.mode;
-  {
-    // built child: the (reduced) work slot; sibling: parent - built, in
-    // place.  All loads are issued before any store (the slots alias).
-    constexpr int kPer = (3 * 256 + 31) / 32;
-    int vals[kPer];
-#pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-      int i = lane + 32 * q;
-      vals[q] = 0;
-      if (i < 3 * B) vals[q] = built ? __ldcg(wk + i) : __ldcg(hs + i) - __ldcg(wk + i);
+  // built child: the (reduced) work slot; sibling: parent - built, in place
+  int vg = 0, vh = 0, vc = 0;
+  if (t < B) {
+    int wg = __ldcg(wk + t), wh = __ldcg(wk + B + t), wc = __ldcg(wk + 2 * B + t);
+    if (built) {
+      vg = wg;
+      vh = wh;
+      vc = wc;
+    } else {
+      vg = __ldcg(hs + t) - wg;
+      vh = __ldcg(hs + B + t) - wh;
+      vc = __ldcg(hs + 2 * B + t) - wc;
     }
-#pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-      int i = lane + 32 * q;
-      if (i < 3 * B) {
-        hs[i] = vals[q];
-        s_cells[w][i / B][i % B] = vals[q];
-      }
-    }
+    hs[t] = vg;
+    hs[B + t] = vh;
+    hs[2 * B + t] = vc;
+    if (sp.const_hess && mode == MODE_FIXED) vh = (int)((long long)sc->hq_const * vc);
   }
-  __syncwarp();
-  if (sp.const_hess && mode == MODE_FIXED) {
-    long long hq = sc->hq_const;
-    for (int b = lane; b < B; b += 32) s_cells[w][1][b] = (int)(hq * s_cells[w][2][b]);
+  s_cells[0][t] = vg;
+  s_cells[1][t] = vh;
+  s_cells[2][t] = vc;
+  long long Lg = vg, Lh = vh, Lc = vc;  // inclusive prefix through bin t
+  block_scan3(Lg, Lh, Lc, s_w);
+  __shared__ long long s_tot[3];
+  if (t == kScanThreads - 1) {
+    s_tot[0] = Lg;
+    s_tot[1] = Lh;
+    s_tot[2] = Lc;
   }
-  __syncwarp();
-  // lane owns bins [lane*8, lane*8 + 8)
-  long long lg[8], lh[8], lc[8];
-  long long ag = 0, ah = 0, ac = 0;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    int b = lane * 8 + k;
-    long long vg = 0, vh = 0, vc = 0;
-    if (b < B) {
-      vg = s_cells[w][0][b];
-      vh = s_cells[w][1][b];
-      vc = s_cells[w][2][b];
-    }
-    ag += vg;
-    ah += vh;
-    ac += vc;
-    lg[k] = ag;
-    lh[k] = ah;
-    lc[k] = ac;
-  }
-  // exclusive warp scan of lane totals
-  long long xg = ag, xh = ah, xc = ac;
-  for (int k = 1; k < 32; k <<= 1) {
-    long long og = __shfl_up_sync(0xffffffffu, xg, k);
-    long long oh = __shfl_up_sync(0xffffffffu, xh, k);
-    long long oc = __shfl_up_sync(0xffffffffu, xc, k);
-    if (lane >= k) {
-      xg += og;
-      xh += oh;
-      xc += oc;
-    }
-  }
-  long long Tg = __shfl_sync(0xffffffffu, xg, 31);
-  long long Th = __shfl_sync(0xffffffffu, xh, 31);
-  long long Tc = __shfl_sync(0xffffffffu, xc, 31);
-  long long eg = xg - ag, eh = xh - ah, ec = xc - ac;  // exclusive prefix before this lane
-  if (j == 0 && lane == 0) {
+  __syncthreads();
+  const long long Tg = s_tot[0], Th = s_tot[1], Tc = s_tot[2];
+  if (j == 0 && t == 0) {
     ts->totals[c].g = Tg;
     ts->totals[c].h = Th;
     ts->totals[c].c = Tc;
   }
+  const double g_inv = sc->g_inv, h_inv = sc->h_inv, gu = sc->g_units, hu = sc->h_units;
   const double l1 = sp.lambda_l1, l2 = sp.lambda_l2, mch = sp.min_child_hess;
   const long long mdl = sp.min_data_in_leaf;
-  double tg = deq(Tg, mode, g_inv, gu), th = deq(Th, mode, h_inv, hu);
-  double best_gain = 0.0;
-  int best_key = 0x7fffffff;  // 2*bin + order
-  long long best_nl = 0;
+  const double tg = deq(Tg, mode, g_inv, gu), th = deq(Th, mode, h_inv, hu);
   FeatBest fb;
   fb.gain = 0.0;
   fb.bin = -1;
@@ -815,18 +840,17 @@ __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, lo
   fb.n_left = 0;
   fb.bits[0] = fb.bits[1] = fb.bits[2] = fb.bits[3] = 0;
   if (n_cats[f] >= 0) {
-    // categorical: serial search on lane 0 (categorical.mojo:478-780) over
-    // exact dequantized per-category values.
-    if (lane == 0) {
+    // categorical: serial search on thread 0 (categorical.mojo:478-780) over
+    // the exact per-category sums
+    if (t == 0) {
       int n_cat = n_cats[f];
       double parent = leaf_score(tg, th, l1, l2);
       if (n_cat >= 2 && n_cat + 1 <= sp.max_cat_to_onehot) {
-        for (int t = 1; t <= n_cat && t < B; ++t) {
-          long long qg = s_cells[w][0][t], qh = s_cells[w][1][t], cc = s_cells[w][2][t];
+        for (int q = 1; q <= n_cat && q < B; ++q) {
+          long long qg = s_cells[0][q], qh = s_cells[1][q], cc = s_cells[2][q];
           double lgv = deq(qg, mode, g_inv, gu), lhv = deq(qh, mode, h_inv, hu);
           if (cc < mdl || lhv < mch) continue;
-          long long rc = Tc - cc;
-          if (rc < mdl) continue;
+          if (Tc - cc < mdl) continue;
           double rh = mode == MODE_FIXED ? th - lhv : deq(Th - qh, mode, h_inv, hu);
           if (rh < mch) continue;
           double rg = mode == MODE_FIXED ? tg - lgv : deq(Tg - qg, mode, g_inv, gu);
@@ -836,50 +860,46 @@ __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, lo
             fb.flags = 1 | 4;
             fb.n_left = cc;
             fb.bits[0] = fb.bits[1] = fb.bits[2] = fb.bits[3] = 0;
-            fb.bits[t >> 6] |= 1ull << (t & 63);
+            fb.bits[q >> 6] |= 1ull << (q & 63);
           }
         }
       } else if (n_cat >= 2) {
         int cand[256];
         double key[256];
         int used = 0;
-        for (int t = 1; t <= n_cat && t < B; ++t) {
-          if (!((double)s_cells[w][2][t] >= sp.cat_smooth)) continue;
-          double gv = deq(s_cells[w][0][t], mode, g_inv, gu);
-          double hv = deq(s_cells[w][1][t], mode, h_inv, hu);
-          // insertion keeps equal keys in ascending category order (stable)
+        for (int q = 1; q <= n_cat && q < B; ++q) {
+          if (!((double)s_cells[2][q] >= sp.cat_smooth)) continue;
+          double gv = deq(s_cells[0][q], mode, g_inv, gu);
+          double hv = deq(s_cells[1][q], mode, h_inv, hu);
           double kv = gv / (hv + sp.cat_smooth);
-          int p = used;
+          int p = used;  // insertion keeps equal keys in category order (stable)
           while (p > 0 && key[p - 1] > kv) {
             key[p] = key[p - 1];
             cand[p] = cand[p - 1];
             --p;
           }
           key[p] = kv;
-          cand[p] = t;
+          cand[p] = q;
           ++used;
         }
         if (used >= 2) {
           int max_num_cat = sp.max_cat_threshold < (used + 1) / 2 ? sp.max_cat_threshold : (used + 1) / 2;
           if (max_num_cat < 0) max_num_cat = 0;
           double cl2 = l2 + sp.cat_l2;
-          double parent_c = leaf_score(tg, th, l1, l2);
           for (int d = 0; d < 2; ++d) {
             int dir = d == 0 ? 1 : -1;
             int start = d == 0 ? 0 : used - 1;
             int pos = start;
             long long cnt_group = 0, qg = 0, qh = 0, qc = 0;
-            double lgv = 0.0, lhv = 0.0;
             int steps = used < max_num_cat ? used : max_num_cat;
             for (int i = 0; i < steps; ++i) {
-              int t = cand[pos];
+              int q = cand[pos];
               pos += dir;
-              qg += s_cells[w][0][t];
-              qh += s_cells[w][1][t];
-              qc += s_cells[w][2][t];
-              cnt_group += s_cells[w][2][t];
-              lgv = deq(qg, mode, g_inv, gu);
-              lhv = deq(qh, mode, h_inv, hu);
+              qg += s_cells[0][q];
+              qh += s_cells[1][q];
+              qc += s_cells[2][q];
+              cnt_group += s_cells[2][q];
+              double lgv = deq(qg, mode, g_inv, gu), lhv = deq(qh, mode, h_inv, hu);
               if (qc < mdl || lhv < mch) continue;
               long long rc = Tc - qc;
               if (rc < mdl || rc < sp.min_data_per_group) break;
@@ -888,17 +908,17 @@ __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, lo
               if (cnt_group < sp.min_data_per_group) continue;
               cnt_group = 0;
               double rg = mode == MODE_FIXED ? tg - lgv : deq(Tg - qg, mode, g_inv, gu);
-              double gain = leaf_score(lgv, lhv, l1, cl2) + leaf_score(rg, rh, l1, cl2) - parent_c;
+              double gain = leaf_score(lgv, lhv, l1, cl2) + leaf_score(rg, rh, l1, cl2) - parent;
               if (gain > fb.gain) {
                 fb.gain = gain;
                 fb.flags = 1 | 4;
                 fb.n_left = qc;
                 fb.bits[0] = fb.bits[1] = fb.bits[2] = fb.bits[3] = 0;
-                int q = start;
+                int q2 = start;
                 for (int k = 0; k <= i; ++k) {
-                  int tt = cand[q];
+                  int tt = cand[q2];
                   fb.bits[tt >> 6] |= 1ull << (tt & 63);
-                  q += dir;
+                  q2 += dir;
                 }
               }
             }
@@ -913,18 +933,18 @@ __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, lo
   const int n_scan = mb >= 0 ? mb : B;
   long long mg = 0, mh = 0, mc = 0;
   if (mb >= 0) {
-    mg = s_cells[w][0][mb];
-    mh = s_cells[w][1][mb];
-    mc = s_cells[w][2][mb];
+    mg = s_cells[0][mb];
+    mh = s_cells[1][mb];
+    mc = s_cells[2][mb];
   }
-  double pg = soft_l1(tg, l1);
-  double parent = pg * pg / (th + l2);
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    int b = lane * 8 + k;
-    if (b >= n_scan) break;
-    if (b == n_scan - 1 && mc == 0) break;
-    long long Lg = eg + lg[k], Lh = eh + lh[k], Lc = ec + lc[k];
+  const double pg = soft_l1(tg, l1);
+  const double parent = pg * pg / (th + l2);
+  const double parent_q = leaf_score(tg, th, l1, l2);
+  double best_gain = 0.0;
+  int best_key = 0x7fffffff;  // 2*bin + order
+  long long best_nl = 0;
+  const int b = t;
+  if (b < n_scan && !(b == n_scan - 1 && mc == 0)) {
     if (mb >= 0) {
       long long Dg = Lg + mg, Dh = Lh + mh, Dc = Lc + mc;
       double dlg = deq(Dg, mode, g_inv, gu), dlh = deq(Dh, mode, h_inv, hu);
@@ -936,7 +956,7 @@ __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, lo
           double tl = soft_l1(dlg, l1), tr = soft_l1(drg, l1);
           gain = tl * tl / (dlh + l2) + tr * tr / (drh + l2) - parent;
         } else {
-          gain = leaf_score(dlg, dlh, l1, l2) + leaf_score(drg, drh, l1, l2) - leaf_score(tg, th, l1, l2);
+          gain = leaf_score(dlg, dlh, l1, l2) + leaf_score(drg, drh, l1, l2) - parent_q;
         }
         if (gain > best_gain) {
           best_gain = gain;
@@ -955,7 +975,7 @@ __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, lo
           double tl = soft_l1(lgv, l1), tr = soft_l1(rg, l1);
           gain = tl * tl / (lhv + l2) + tr * tr / (rh + l2) - parent;
         } else {
-          gain = leaf_score(lgv, lhv, l1, l2) + leaf_score(rg, rh, l1, l2) - leaf_score(tg, th, l1, l2);
+          gain = leaf_score(lgv, lhv, l1, l2) + leaf_score(rg, rh, l1, l2) - parent_q;
         }
         if (gain > best_gain) {
           best_gain = gain;
@@ -965,7 +985,7 @@ __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, lo
       }
     }
   }
-  // warp arg-max: higher gain, then lower key (earlier in the serial scan)
+  // block arg-max: higher gain, then lower key (earlier in the serial scan)
   for (int k = 16; k > 0; k >>= 1) {
     double og = __shfl_xor_sync(0xffffffffu, best_gain, k);
     int ok = __shfl_xor_sync(0xffffffffu, best_key, k);
@@ -977,6 +997,19 @@ __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, lo
     }
   }
   if (lane == 0) {
+    s_gain[w] = best_gain;
+    s_key[w] = best_key;
+    s_nl[w] = best_nl;
+  }
+  __syncthreads();
+  if (t == 0) {
+    for (int q = 1; q < kScanThreads / 32; ++q) {
+      if (s_gain[q] > best_gain || (s_gain[q] == best_gain && s_key[q] < best_key)) {
+        best_gain = s_gain[q];
+        best_key = s_key[q];
+        best_nl = s_nl[q];
+      }
+    }
     if (best_key != 0x7fffffff && best_gain > 0.0) {
       fb.gain = best_gain;
       fb.bin = best_key >> 1;
@@ -1073,7 +1106,7 @@ __device__ void block_finish(TreeState* __restrict__ ts, const FeatBest* __restr
 // then folds the per-feature bests (block_finish) and picks the next leaf to
 // split (block_pick), so one split costs three launches: partition,
 // histogram, scan.
-__global__ void __launch_bounds__(kScanWarps * 32) k_scan(TreeState* __restrict__ ts, int* __restrict__ hist,
+__global__ void __launch_bounds__(kScanThreads) k_scan(TreeState* __restrict__ ts, int* __restrict__ hist,
                                                            long long slot_cells, const int* __restrict__ feats,
                                                            const int* __restrict__ missing_bin,
                                                            const int* __restrict__ n_cats,
@@ -1141,4 +1174,5 @@ __global__ void k_update_raw(const TreeState* __restrict__ ts, const long long* 
   *p = fma(lr, v, *p);
 }
 
+}  // namespace
 }  // namespace mtb

@@ -1,0 +1,121 @@
+// Standalone entry point of the per-leaf histogram kernel (the hot kernel of
+// the trainer) for callers and tests that want one histogram of one row set:
+// the quantized-gradient build of gpu_active_rows.mojo:3903
+// (_range_hist_atomic_kernel) over int8 gradient / hessian pairs.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/mojotrees.h"
+#include "capi_util.h"
+#include "gbdt_device.cuh"
+#include "gbdt_kernels.cuh"
+#include "hist_launch.cuh"
+#include "trainer.h"
+
+namespace mtb {
+namespace {
+
+struct DevMem {
+  void* p = nullptr;
+  explicit DevMem(size_t bytes) { MTB_CUDA(cudaMalloc(&p, bytes ? bytes : 1)); }
+  ~DevMem() { cudaFree(p); }
+};
+
+// Largest flush span for packed cells (g * 2^15 + count) given |g| <= bins/2.
+long long quant_rows_per_flush(int quant_bins) {
+  long long gl = quant_bins / 2;
+  return std::min<long long>((1ll << 15) - 1, ((1ll << 16) - 1) / gl);
+}
+
+// Launches the histogram kernel for positions [0, n_sel) of rows/pairs into
+// `work` (zeroed here); `plan` is device memory for the job descriptor.
+void launch_leaf_hist(const uint8_t* d_bins_rm, int F, int Fp, int B, const int* d_rows, const uint16_t* d_pairs,
+                      long long n_sel, int quant_bins, Plan* d_plan, int* d_work, cudaStream_t st) {
+  Plan P;
+  memset(&P, 0, sizeof P);
+  P.active = 1;
+  P.built_is_left = 1;
+  P.begin = 0;
+  P.count = n_sel;
+  P.cursor_left = (unsigned long long)n_sel;
+  P.dst_buf = 0;
+  MTB_CUDA(cudaMemcpyAsync(d_plan, &P, sizeof P, cudaMemcpyHostToDevice, st));
+  const long long cells = (long long)F * 3 * B;
+  MTB_CUDA(cudaMemsetAsync(d_work, 0, sizeof(int) * cells, st));
+  int dev = 0, n_sm = 0;
+  MTB_CUDA(cudaGetDevice(&dev));
+  MTB_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+  HistLaunch hl = choose_hist_launch(MODE_QUANT, false, B, Fp, n_sm);
+  launch_hist<MODE_QUANT, false>(hl, st, d_plan, d_bins_rm, Fp, F, B, d_rows, d_rows, d_pairs, d_pairs, d_work,
+                                 cells, quant_rows_per_flush(quant_bins), 0);
+  MTB_CUDA(cudaGetLastError());
+}
+
+}  // namespace
+}  // namespace mtb
+
+extern "C" int32_t mojotrees_b200_histogram_u8(const uint8_t* bins, int64_t n_rows, int64_t n_features,
+                                               int32_t n_bins, const int32_t* rows, int64_t n_sel,
+                                               const int8_t* grad_q, const uint8_t* hess_q,
+                                               int32_t num_grad_quant_bins, int32_t* out_hist,
+                                               MojoTreesError* error) {
+  using namespace mtb;
+  capi_clear_error(error);
+  try {
+    if (!bins || !grad_q || !hess_q || !out_hist) throw std::invalid_argument("null pointer argument");
+    if (n_rows < 1 || n_features < 1 || n_sel < 0) throw std::invalid_argument("sizes must be positive");
+    if (n_rows >= (1ll << 31)) throw std::invalid_argument("more than 2^31-1 rows");
+    if (n_bins < 2 || n_bins > 256) throw std::invalid_argument("n_bins must be in [2, 256]");
+    if (num_grad_quant_bins < 2 || num_grad_quant_bins > 254 || num_grad_quant_bins % 2)
+      throw std::invalid_argument("num_grad_quant_bins must be even and in [2, 254]");
+    if (!rows) n_sel = n_rows;
+    const int F = (int)n_features, B = n_bins, Fp = (F + 15) / 16 * 16;
+    const int lim = num_grad_quant_bins / 2;
+    std::vector<int> rsel((size_t)n_sel);
+    std::vector<uint16_t> pairs((size_t)n_sel);
+    for (int64_t i = 0; i < n_sel; ++i) {
+      int64_t r = rows ? rows[i] : i;
+      if (r < 0 || r >= n_rows) throw std::invalid_argument("row id out of range");
+      if (grad_q[r] < -lim || grad_q[r] > lim || hess_q[r] > num_grad_quant_bins)
+        throw std::invalid_argument("quantized gradient outside [-bins/2, bins/2] or hessian above bins");
+      rsel[i] = (int)r;
+      pairs[i] = (uint16_t)((uint8_t)grad_q[r]) | (uint16_t)((uint16_t)hess_q[r] << 8);
+    }
+    for (int64_t k = 0; k < n_rows * n_features; ++k)
+      if (bins[k] >= B) throw std::invalid_argument("bin value >= n_bins");
+    if (cuda_device_count() < 1) throw Unsupported("no CUDA device is available");
+    // row-major bins with a 16-byte row stride, as the trainer keeps them
+    std::vector<uint8_t> rm((size_t)n_rows * Fp, 0);
+    for (int64_t f = 0; f < F; ++f)
+      for (int64_t r = 0; r < n_rows; ++r) rm[(size_t)r * Fp + f] = bins[f * n_rows + r];
+    const size_t cells = (size_t)F * 3 * B;
+    DevMem d_bins(rm.size()), d_rows(sizeof(int) * rsel.size()), d_pairs(sizeof(uint16_t) * pairs.size()),
+        d_plan(sizeof(Plan)), d_work(sizeof(int) * cells);
+    cudaStream_t st = 0;
+    MTB_CUDA(cudaMemcpy(d_bins.p, rm.data(), rm.size(), cudaMemcpyHostToDevice));
+    MTB_CUDA(cudaMemcpy(d_rows.p, rsel.data(), sizeof(int) * rsel.size(), cudaMemcpyHostToDevice));
+    MTB_CUDA(cudaMemcpy(d_pairs.p, pairs.data(), sizeof(uint16_t) * pairs.size(), cudaMemcpyHostToDevice));
+    if (n_sel > 0)
+      launch_leaf_hist((const uint8_t*)d_bins.p, F, Fp, B, (const int*)d_rows.p, (const uint16_t*)d_pairs.p, n_sel,
+                       num_grad_quant_bins, (Plan*)d_plan.p, (int*)d_work.p, st);
+    else
+      MTB_CUDA(cudaMemset(d_work.p, 0, sizeof(int) * cells));
+    MTB_CUDA(cudaMemcpy(out_hist, d_work.p, sizeof(int) * cells, cudaMemcpyDeviceToHost));
+    return MOJOTREES_OK;
+  } catch (const std::invalid_argument& e) {
+    capi_set_error(error, e.what());
+    return MOJOTREES_ERROR_INVALID_ARGUMENT;
+  } catch (const Unsupported& e) {
+    capi_set_error(error, e.what());
+    return MOJOTREES_ERROR_UNSUPPORTED;
+  } catch (const std::exception& e) {
+    capi_set_error(error, e.what());
+    return MOJOTREES_ERROR_TRAINING;
+  }
+}
+

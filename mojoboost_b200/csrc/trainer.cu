@@ -7,6 +7,7 @@
 // synchronisation until the round ends, where the tree's node table is read
 // back and the early-stop rule of boosting.mojo:2898-2907 is applied.
 #include <cuda_runtime.h>
+#include <stdlib.h>
 
 #include <algorithm>
 #include <chrono>
@@ -18,6 +19,7 @@
 
 #include "gbdt_device.cuh"
 #include "gbdt_kernels.cuh"
+#include "hist_launch.cuh"
 #include "collective.h"
 #include "trainer.h"
 
@@ -95,77 +97,6 @@ struct EventTimer {
     accs.clear();
   }
 };
-
-struct HistLaunch {
-  int cluster = 1;  // CTAs per thread-block cluster along grid y
-  int vpr = 1;
-  int groups = 1;
-  int threads = 512;
-  int row_ctas = 1;
-  size_t smem = 0;
-};
-
-cudaLaunchConfig_t hist_config(const HistLaunch& hl, int cs, int row_ctas, cudaStream_t st, cudaLaunchAttribute* attr) {
-  cudaLaunchConfig_t lc = {};
-  lc.gridDim = dim3(hl.groups, row_ctas);
-  lc.blockDim = dim3(hl.threads);
-  lc.dynamicSmemBytes = hl.smem;
-  lc.stream = st;
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = cs;
-  attr[0].val.clusterDim.z = 1;
-  lc.attrs = attr;
-  lc.numAttrs = 1;
-  return lc;
-}
-
-template <int VPR, int MODE, bool CH>
-cudaError_t prepare_hist_t(const HistLaunch& hl, int cs, int* n_clusters) {
-  auto k = k_hist<VPR, MODE, CH>;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  if (e != cudaSuccess) return e;
-  cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t lc = hist_config(hl, cs, hl.row_ctas / cs * cs, 0, attr);
-  return cudaOccupancyMaxActiveClusters(n_clusters, k, &lc);
-}
-
-template <int VPR, int MODE, bool CH>
-void launch_hist_t(const HistLaunch& hl, cudaStream_t st, const TreeState* ts, const uint8_t* bins_rm, int Fp, int F,
-                   int B, const int* r0, const int* r1, const void* p0, const void* p1, int* hist,
-                   long long slot_cells, long long rpf, int ws) {
-  cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t lc = hist_config(hl, hl.cluster, hl.row_ctas, st, attr);
-  MTB_CUDA(cudaLaunchKernelEx(&lc, k_hist<VPR, MODE, CH>, ts, bins_rm, Fp, F, B, r0, r1, p0, p1, hist, slot_cells,
-                              rpf, ws));
-}
-
-#define MTB_VPR_SWITCH(EXPR)                                                                  \
-  switch (hl.vpr) {                                                                            \
-    case 1: { constexpr int V = 1; EXPR; } break;                                              \
-    case 2: { constexpr int V = 2; EXPR; } break;                                              \
-    case 3: { constexpr int V = 3; EXPR; } break;                                              \
-    case 4: { constexpr int V = 4; EXPR; } break;                                              \
-    case 5: { constexpr int V = 5; EXPR; } break;                                              \
-    case 6: { constexpr int V = 6; EXPR; } break;                                              \
-    case 7: { constexpr int V = 7; EXPR; } break;                                              \
-    case 8: { constexpr int V = 8; EXPR; } break;                                              \
-    default: throw std::runtime_error("bad histogram vector count");                           \
-  }
-
-template <int MODE, bool CH>
-cudaError_t prepare_hist(const HistLaunch& hl, int cs, int* n_clusters) {
-  cudaError_t e = cudaErrorInvalidValue;
-  MTB_VPR_SWITCH(e = (prepare_hist_t<V, MODE, CH>(hl, cs, n_clusters)))
-  return e;
-}
-
-template <int MODE, bool CH>
-void launch_hist(const HistLaunch& hl, cudaStream_t st, const TreeState* ts, const uint8_t* bins_rm, int Fp, int F,
-                 int B, const int* r0, const int* r1, const void* p0, const void* p1, int* hist, long long slot_cells,
-                 long long rpf, int ws) {
-  MTB_VPR_SWITCH((launch_hist_t<V, MODE, CH>(hl, st, ts, bins_rm, Fp, F, B, r0, r1, p0, p1, hist, slot_cells, rpf, ws)))
-}
 
 }  // namespace
 
@@ -367,37 +298,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   // Histogram launch geometry: as many features per CTA as one SM's shared
   // memory holds, row chunks sized to fill every SM, CTAs of a feature group
   // in clusters of up to 8 that merge through DSMEM.
-  HistLaunch hl;
-  {
-    size_t cell_bytes = (mode == MODE_QUANT || const_h) ? 8 : 12;  // two or three 32-bit planes
-    size_t budget = 200 * 1024;
-    int fg_max = (int)(budget / ((size_t)B * cell_bytes)) / 16 * 16;
-    fg_max = std::max(16, std::min(128, fg_max));
-    int vmax = fg_max / 16;
-    int vecs = Fp / 16;
-    hl.groups = (vecs + vmax - 1) / vmax;
-    hl.vpr = (vecs + hl.groups - 1) / hl.groups;
-    hl.smem = (size_t)hl.vpr * 16 * B * cell_bytes;
-    int per_sm = std::max(1, (int)((228 * 1024) / (hl.smem + 1024)));
-    hl.threads = per_sm >= 2 ? 512 : 1024;
-    per_sm = std::min(per_sm, 2048 / hl.threads);
-    hl.row_ctas = std::max(1, (n_sm * per_sm + hl.groups - 1) / hl.groups);
-    hl.cluster = 1;
-    for (int cs : {8, 4, 2, 1}) {
-      if (hl.row_ctas < cs) continue;
-      int n_clusters = 0;
-      cudaError_t oe;
-      if (mode == MODE_QUANT) oe = prepare_hist<MODE_QUANT, false>(hl, cs, &n_clusters);
-      else if (const_h) oe = prepare_hist<MODE_FIXED, true>(hl, cs, &n_clusters);
-      else oe = prepare_hist<MODE_FIXED, false>(hl, cs, &n_clusters);
-      if (oe == cudaSuccess && n_clusters >= 1) {
-        hl.cluster = cs;
-        break;
-      }
-      cudaGetLastError();
-    }
-    hl.row_ctas = std::max(hl.cluster, hl.row_ctas / hl.cluster * hl.cluster);
-  }
+  HistLaunch hl = choose_hist_launch(mode, const_h, B, Fp, n_sm);
   long long rows_per_flush = 1ll << 40;
   if (mode == MODE_QUANT) {
     // plane 0 holds g * 2^15 + count: count < 2^15 and |sum g| < 2^16 per flush
@@ -406,6 +307,24 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   }
   const int part_grid = n_sm * 4;
   const int part_threads = 256;
+  int part_items = 2;  // rows per thread per partition tile
+  if (const char* e = getenv("MOJOTREES_PART_ITEMS")) part_items = atoi(e);
+  auto launch_partition = [&]() {
+#define MTB_PART(IT)                                                                                      \
+  if (mode == MODE_QUANT)                                                                                 \
+    k_partition<uint16_t, IT><<<part_grid, part_threads, 0, st>>>(                                        \
+        d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<uint16_t*>(d_pairs0.p),            \
+        reinterpret_cast<uint16_t*>(d_pairs1.p), d_hist.p, slot_cells, work_slot);                        \
+  else                                                                                                    \
+    k_partition<int2, IT><<<part_grid, part_threads, 0, st>>>(                                            \
+        d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<int2*>(d_pairs0.p),                \
+        reinterpret_cast<int2*>(d_pairs1.p), d_hist.p, slot_cells, work_slot);
+    if (part_items <= 1) { MTB_PART(1) }
+    else if (part_items == 2) { MTB_PART(2) }
+    else if (part_items <= 4) { MTB_PART(4) }
+    else { MTB_PART(8) }
+#undef MTB_PART
+  };
 
   model.objective = cfg.objective;
   model.num_class = K;
@@ -438,13 +357,13 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   auto hist = [&]() {
     timer.begin(&stats.hist_ms);
     if (mode == MODE_QUANT)
-      launch_hist<MODE_QUANT, false>(hl, st, d_ts.p, d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
+      launch_hist<MODE_QUANT, false>(hl, st, plan_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
                                      d_pairs1.p, d_hist.p, slot_cells, rows_per_flush, work_slot);
     else if (const_h)
-      launch_hist<MODE_FIXED, true>(hl, st, d_ts.p, d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
+      launch_hist<MODE_FIXED, true>(hl, st, plan_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
                                     d_pairs1.p, d_hist.p, slot_cells, rows_per_flush, work_slot);
     else
-      launch_hist<MODE_FIXED, false>(hl, st, d_ts.p, d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
+      launch_hist<MODE_FIXED, false>(hl, st, plan_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
                                      d_pairs1.p, d_hist.p, slot_cells, rows_per_flush, work_slot);
     timer.end();
   };
@@ -573,7 +492,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       const int n_active = (int)feats.size();
       MTB_CUDA(cudaMemcpyAsync(d_feats.p, feats.data(), sizeof(int) * n_active, cudaMemcpyHostToDevice, st));
       sp.n_active = n_active;
-      const dim3 scan_grid(2, (unsigned)((n_active + kScanWarps - 1) / kScanWarps));
+      const dim3 scan_grid(2, (unsigned)n_active);
 
       // ---- grow the tree: a fixed launch sequence, replayed as a CUDA graph
       // (one per class and feature count) unless per-phase timing is requested
@@ -583,24 +502,17 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
         hist();
         reduce_work();
         timer.begin(&stats.scan_ms);
-        k_scan<<<scan_grid, kScanWarps * 32, 0, st>>>(d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p,
+        k_scan<<<scan_grid, kScanThreads, 0, st>>>(d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p,
                                                       d_ncats.p, d_sc.p, sp, d_fb.p, 1, work_slot, cfg.num_leaves);
         timer.end();
         for (int s = 1; s < cfg.num_leaves; ++s) {
           timer.begin(&stats.partition_ms);
-          if (mode == MODE_QUANT)
-            k_partition<uint16_t, 8><<<part_grid, part_threads, 0, st>>>(
-                d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<uint16_t*>(d_pairs0.p),
-                reinterpret_cast<uint16_t*>(d_pairs1.p), d_hist.p, slot_cells, work_slot);
-          else
-            k_partition<int2, 8><<<part_grid, part_threads, 0, st>>>(
-                d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<int2*>(d_pairs0.p),
-                reinterpret_cast<int2*>(d_pairs1.p), d_hist.p, slot_cells, work_slot);
+          launch_partition();
           timer.end();
           hist();
           reduce_work();
           timer.begin(&stats.scan_ms);
-          k_scan<<<scan_grid, kScanWarps * 32, 0, st>>>(d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p,
+          k_scan<<<scan_grid, kScanThreads, 0, st>>>(d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p,
                                                         d_ncats.p, d_sc.p, sp, d_fb.p, 0, work_slot, cfg.num_leaves);
           timer.end();
         }
