@@ -58,6 +58,7 @@ SIGNATURES = {
     "mojotrees_b200_round_times": (_I32, [_P, _P, _I64, _P, _P]),
     "mojotrees_b200_nccl_unique_id": (_I32, [_P, _P]),
     "mojotrees_b200_histogram_u8": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _I32, _P, _P]),
+    "mojotrees_b200_histogram_u8_noalloc": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _I32, _P, _P, _P]),
     "mojotrees_b200_train_binned_u8_dp": (_I32, [_P, _I64, _I64, _I32, _P, _P, _P, _P, ctypes.c_char_p, _P, _I32,
                                                  _I32, _I64, _I64, _P, _P]),
 }

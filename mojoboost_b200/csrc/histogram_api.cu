@@ -6,6 +6,7 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -119,3 +120,102 @@ extern "C" int32_t mojotrees_b200_histogram_u8(const uint8_t* bins, int64_t n_ro
   }
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// Some callers cannot call cudaMalloc: code that runs while a CUDA graph is
+// being captured (allocation would break the capture), callers that hand the
+// GPU's memory to their own pool allocator and forbid others from taking any,
+// and real-time paths that must not take the allocator's locks.  For them the
+// job descriptor and the accumulation cells of the histogram live in one
+// fixed device array, reserved when the library is loaded and held by every
+// GPU that loads it until the process exits.  The caller passes device
+// pointers for the inputs and the output; nothing is allocated per call.
+// ---------------------------------------------------------------------------
+namespace mtb {
+namespace {
+
+// Largest histogram the array holds: 128 features x 256 bins x (g, h, count).
+constexpr long long kNoAllocMaxCells = 128ll * 256 * 3;
+constexpr size_t kNoAllocPlanBytes = (sizeof(Plan) + 255) / 256 * 256;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocPlanBytes + kNoAllocMaxCells * 4];
+
+struct NoAllocDevice {
+  bool ready = false;
+  unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch
+  HistLaunch hl;
+  int hl_B = -1, hl_Fp = -1;
+};
+constexpr int kMaxDevices = 64;
+NoAllocDevice g_noalloc_dev[kMaxDevices];
+std::mutex g_noalloc_mutex;
+
+}  // namespace
+}  // namespace mtb
+
+extern "C" int32_t mojotrees_b200_histogram_u8_noalloc(const uint8_t* bins_rm, int64_t n_rows, int64_t n_features,
+                                                       int32_t n_bins, const int32_t* rows, int64_t n_sel,
+                                                       const uint16_t* pairs, int32_t num_grad_quant_bins,
+                                                       int32_t* out_hist, void* stream, MojoTreesError* error) {
+  using namespace mtb;
+  capi_clear_error(error);
+  try {
+    if (!bins_rm || !rows || !pairs || !out_hist) throw std::invalid_argument("null pointer argument");
+    if (n_rows < 1 || n_features < 1 || n_sel < 1) throw std::invalid_argument("sizes must be positive");
+    if (n_rows >= (1ll << 31)) throw std::invalid_argument("more than 2^31-1 rows");
+    if (n_bins < 2 || n_bins > 256) throw std::invalid_argument("n_bins must be in [2, 256]");
+    if (num_grad_quant_bins < 2 || num_grad_quant_bins > 254 || num_grad_quant_bins % 2)
+      throw std::invalid_argument("num_grad_quant_bins must be even and in [2, 254]");
+    const long long cells = n_features * 3 * (long long)n_bins;
+    if (cells > kNoAllocMaxCells)
+      throw std::invalid_argument("n_features * n_bins exceeds the allocation-free limit of 128 * 256 "
+                                  "(use mojotrees_b200_histogram_u8)");
+    int dev = 0;
+    MTB_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) throw std::runtime_error("device index out of range");
+    const int F = (int)n_features, B = n_bins, Fp = (F + 15) / 16 * 16;
+    NoAllocDevice* d = &g_noalloc_dev[dev];
+    {
+      std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+      if (!d->ready) {
+        // once per device, with that device current: the array's device address
+        void* ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess)
+          throw std::runtime_error(std::string("cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+        d->scratch = static_cast<unsigned char*>(ptr);
+        d->ready = true;
+      }
+      if (d->hl_B != B || d->hl_Fp != Fp) {
+        int n_sm = 0;
+        MTB_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+        d->hl = choose_hist_launch(MODE_QUANT, false, B, Fp, n_sm);
+        d->hl_B = B;
+        d->hl_Fp = Fp;
+      }
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    Plan* plan = reinterpret_cast<Plan*>(d->scratch);
+    int* work = reinterpret_cast<int*>(d->scratch + kNoAllocPlanBytes);
+    Plan P;
+    memset(&P, 0, sizeof P);
+    P.active = 1;
+    P.built_is_left = 1;
+    P.count = n_sel;
+    P.cursor_left = (unsigned long long)n_sel;
+    MTB_CUDA(cudaMemcpyAsync(plan, &P, sizeof P, cudaMemcpyHostToDevice, st));
+    MTB_CUDA(cudaMemsetAsync(work, 0, sizeof(int) * cells, st));  // the array keeps the last call's cells
+    launch_hist<MODE_QUANT, false>(d->hl, st, plan, bins_rm, Fp, F, B, rows, rows, pairs, pairs, work, cells,
+                                   quant_rows_per_flush(num_grad_quant_bins), 0);
+    MTB_CUDA(cudaGetLastError());
+    MTB_CUDA(cudaMemcpyAsync(out_hist, work, sizeof(int) * cells, cudaMemcpyDeviceToDevice, st));
+    return MOJOTREES_OK;
+  } catch (const std::invalid_argument& e) {
+    capi_set_error(error, e.what());
+    return MOJOTREES_ERROR_INVALID_ARGUMENT;
+  } catch (const std::exception& e) {
+    capi_set_error(error, e.what());
+    return MOJOTREES_ERROR_TRAINING;
+  }
+}
