@@ -198,7 +198,8 @@ def run_gpu(args):
     phases = None
     if pm is not None:
         ps = pm.stats()
-        phases = {k: ps[k] for k in ("hist_ms", "partition_ms", "scan_ms", "grad_ms", "hist_bytes")}
+        phases = {k: ps[k] for k in ("hist_ms", "partition_ms", "scan_ms", "commit_ms", "grad_ms", "hist_bytes",
+                                      "iterations", "expansions", "rounds")}
         hist_gbs = ps["hist_bytes"] / (ps["hist_ms"] / 1000.0) / 1e9 if ps["hist_ms"] > 0 else None
     peak, peak_kind = measured_peak()
     e2e = None

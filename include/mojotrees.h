@@ -159,7 +159,9 @@ int32_t mojotrees_b200_training_scores(const MojoTreesModel *model, double *out_
 
 /* Training statistics: fills up to out_len doubles in this order:
  * fit_seconds, upload_seconds, hist_ms, partition_ms, scan_ms, grad_ms,
- * hist_rows, hist_bytes, hist_launches, kernel_launches, rounds.  The phase
+ * hist_rows, hist_bytes, hist_launches, kernel_launches, rounds, commit_ms,
+ * iterations (batch iterations that did work), expansions (leaves whose
+ * children were computed; exceeds the splits by the speculative ones).  The phase
  * times are measured with CUDA events only when the fit ran with
  * profile_phases=true.  Returns the number of values written via *out_n. */
 int32_t mojotrees_b200_train_stats(const MojoTreesModel *model, double *out_values, int64_t out_len,

@@ -46,22 +46,33 @@ struct SplitRec {
   unsigned long long bits[4];
 };
 
+constexpr int kMaxBatch = 32;                              // leaves expanded per iteration
+constexpr int kMaxPool = 4 * kMaxLeaves;  // leaf records of one tree (1 + 2 per expansion)
+
+// One leaf of the tree being grown (frontier leaves, speculative children).
 struct LeafRec {
-  int node;
-  int buf;        // which ping-pong row buffer holds this leaf's rows
-  int hist_slot;  // histogram slot of this leaf
-  int depth;
+  int node;         // node id once the leaf is part of the tree, else -1
+  int buf;          // ping-pong row buffer holding the leaf's rows
+  int hist_slot;    // histogram slot, -1 when none
+  int state;        // 0 leaf, 1 expanded (children computed, split not committed), 2 split committed
+  int child[2];     // leaf ids of the children once expanded
+  int exp_buf;      // buffer holding this leaf's rows after its expansion
+  int pad;
   long long begin;  // local range [begin, begin + count) in rows[buf]
   long long count;  // local rows (this device)
+  long long gcount; // global rows (histogram count)
+  double value;     // leaf output
   SplitRec split;   // best split; split.found == 0 when none
 };
 
-struct Plan {
-  int active;        // 1 when this iteration applies a split
-  int parent_slot;   // frontier slot of the leaf being split
-  int built_hist;    // histogram slot of the child built from rows
-  int sib_hist;      // histogram slot of the child derived by subtraction (= parent's)
-  int built_is_left; // decided from global counts, identical on every device
+// One leaf expansion of the current iteration.
+struct BatchItem {
+  int leaf;           // leaf id being expanded
+  int child[2];       // leaf ids of the left and right children
+  int built_is_left;  // decided from global counts, identical on every device
+  int work;           // work-slot index of the built child
+  int built_hist;     // histogram slot of the built child
+  int sib_hist;       // histogram slot of the derived child (= the parent's)
   int feature;
   int threshold;
   int default_left;
@@ -70,16 +81,18 @@ struct Plan {
   unsigned long long bits[4];
   int src_buf;
   int dst_buf;
-  int depth;
-  int pad;
-  long long begin;   // parent local range
+  long long begin;    // parent local range
   long long count;
-  unsigned long long cursor_left;   // local rows placed left so far (final = local n_left)
-  unsigned long long cursor_right;  // local rows placed right so far
-  int n_children;    // 1 for the root, 2 after a split
-  int child_slot[2]; // frontier slots of the children (left, right)
-  int child_hist[2];
-  int child_node[2];
+  long long tile0;    // first partition tile of this item
+  unsigned long long cursor_left;   // local rows placed left (final = local n_left)
+  unsigned long long cursor_right;  // local rows placed right
+};
+
+struct Batch {
+  int n_items;
+  int root;           // 1 for the root build (no partition; the child is the root itself)
+  long long n_tiles;  // partition tiles over all items
+  BatchItem items[kMaxBatch];
 };
 
 struct ChildTotals {
@@ -110,19 +123,22 @@ struct NodeRec {
 };
 
 struct TreeHeader {
-  int n_leaves;
+  int n_leaves;              // frontier size (= leaves of the committed tree)
   int n_nodes;
   int done;
   int error;
   unsigned int scan_ticket;  // blocks of the current scan launch that have finished
-  int pad;
+  int n_pool;                // leaf records used
+  int n_hist;                // histogram slots used
+  int iterations;            // expansion iterations run for this tree
 };
 
 struct TreeState {
   TreeHeader hdr;
-  Plan plan;
-  ChildTotals totals[2];
-  LeafRec leaves[kMaxLeaves];
+  Batch batch;
+  ChildTotals totals[2 * kMaxBatch];
+  int slot_leaf[kMaxLeaves];  // frontier slot -> leaf id
+  LeafRec pool[kMaxPool];
   NodeRec nodes[kMaxNodes];
 };
 

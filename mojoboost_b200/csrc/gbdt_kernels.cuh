@@ -244,8 +244,24 @@ __global__ void k_quantize(const float* __restrict__ g32, const float* __restric
   }
 }
 
+
 // ---------------------------------------------------------------------------
-// Tree control
+// Tree control: speculative leaf batching
+//
+// The reference grows a tree one split at a time (growth_policy.mojo:659-677,
+// tree.mojo:3767-4256): pick the frontier leaf with the largest gain, split
+// it, compute both children's best splits, repeat.  A leaf's children and
+// their best splits depend only on that leaf's rows, so they can be computed
+// before the leaf is picked.  Each iteration here therefore expands up to K
+// frontier leaves at once (the K largest gains, never more than the remaining
+// leaf budget): one partition launch, one histogram launch and one scan
+// launch for all of them.  The scan's last block then replays the reference's
+// sequential pick loop over the known gains and commits every split whose
+// children are already computed, in exactly the reference's order (node ids,
+// frontier slots and tie rules unchanged), stopping at the first pick that
+// still needs an expansion.  The committed tree is identical to the
+// sequential one; a leaf expanded but never committed (the leaf budget ran
+// out first) stays a leaf.
 // ---------------------------------------------------------------------------
 
 __device__ __forceinline__ void clear_node(NodeRec& nd, double value, long long count) {
@@ -263,154 +279,67 @@ __device__ __forceinline__ void clear_node(NodeRec& nd, double value, long long 
   nd.count = count;
 }
 
-// Tree start: one leaf (the root) covering this device's rows in buffer 0.
+__device__ __forceinline__ void clear_split(SplitRec& s) {
+  s.found = 0;
+  s.gain = 0.0;
+  s.feature = -1;
+  s.bin = -1;
+  s.default_left = 0;
+  s.is_cat = 0;
+  s.pad = 0;
+  s.n_left = 0;
+  s.bits[0] = s.bits[1] = s.bits[2] = s.bits[3] = 0;
+}
+
+// Tree start: the root is leaf 0 / node 0 / frontier slot 0 / histogram slot
+// 0, covering this device's rows in buffer 0; the first batch builds it.
 __global__ void k_tree_init(TreeState* ts, long long n_local) {
   if (threadIdx.x != 0) return;
-  ts->hdr.n_leaves = 1;
-  ts->hdr.n_nodes = 1;
-  ts->hdr.done = 0;
-  ts->hdr.error = 0;
-  ts->hdr.scan_ticket = 0;
-  LeafRec& L = ts->leaves[0];
+  TreeHeader& H = ts->hdr;
+  H.n_leaves = 1;
+  H.n_nodes = 1;
+  H.done = 0;
+  H.error = 0;
+  H.scan_ticket = 0;
+  H.n_pool = 1;
+  H.n_hist = 1;
+  H.iterations = 0;
+  LeafRec& L = ts->pool[0];
   L.node = 0;
   L.buf = 0;
   L.hist_slot = 0;
-  L.depth = 0;
+  L.state = 0;
+  L.child[0] = L.child[1] = -1;
+  L.exp_buf = 0;
   L.begin = 0;
   L.count = n_local;
-  L.split.found = 0;
-  L.split.gain = 0.0;
+  L.gcount = 0;
+  L.value = 0.0;
+  clear_split(L.split);
+  ts->slot_leaf[0] = 0;
   clear_node(ts->nodes[0], 0.0, 0);
-  Plan& P = ts->plan;
-  P.active = 1;
-  P.n_children = 1;
-  P.child_slot[0] = 0;
-  P.child_hist[0] = 0;
-  P.child_node[0] = 0;
+  Batch& Bt = ts->batch;
+  Bt.n_items = 1;
+  Bt.root = 1;
+  Bt.n_tiles = 0;
+  BatchItem& P = Bt.items[0];
+  P.leaf = 0;
+  P.child[0] = 0;
+  P.child[1] = -1;
+  P.built_is_left = 1;
+  P.work = 0;
   P.built_hist = 0;
   P.sib_hist = -1;
-  P.built_is_left = 1;
+  P.src_buf = 0;
+  P.dst_buf = 0;
   P.begin = 0;
   P.count = n_local;
-  P.dst_buf = 0;
+  P.tile0 = 0;
   P.cursor_left = (unsigned long long)n_local;
   P.cursor_right = 0;
 }
 
-// Leaf pick (growth_policy.mojo:659-677): max gain > 0, lowest frontier slot
-// on ties.  Records the split in the tree and lays out the children.
-// Runs on one 256-thread block.
-__device__ void block_pick(TreeState* ts, const int* __restrict__ missing_bin, int num_leaves) {
-  __shared__ double s_gain[256];
-  __shared__ int s_slot[256];
-  int t = threadIdx.x;
-  if (ts->hdr.done || ts->hdr.n_leaves >= num_leaves) {
-    if (t == 0) {
-      ts->hdr.done = 1;
-      ts->plan.active = 0;
-    }
-    return;
-  }
-  int nl = ts->hdr.n_leaves;
-  double bg = 0.0;
-  int bs = -1;
-  for (int i = t; i < nl; i += 256) {
-    const SplitRec& s = ts->leaves[i].split;
-    if (s.found && s.gain > 0.0 && s.gain > bg) {
-      bg = s.gain;
-      bs = i;
-    }
-  }
-  s_gain[t] = bg;
-  s_slot[t] = bs;
-  __syncthreads();
-  for (int w = 128; w > 0; w >>= 1) {
-    if (t < w) {
-      double og = s_gain[t + w];
-      int os = s_slot[t + w];
-      if (os >= 0 && (s_slot[t] < 0 || og > s_gain[t] || (og == s_gain[t] && os < s_slot[t]))) {
-        s_gain[t] = og;
-        s_slot[t] = os;
-      }
-    }
-    __syncthreads();
-  }
-  if (t != 0) return;
-  Plan& P = ts->plan;
-  int best = s_slot[0];
-  if (best < 0) {
-    ts->hdr.done = 1;
-    P.active = 0;
-    return;
-  }
-  LeafRec L = ts->leaves[best];
-  const SplitRec& s = L.split;
-  long long n_parent = ts->nodes[L.node].count;
-  long long n_left = s.n_left;
-  long long n_right = n_parent - n_left;
-  int left_node = ts->hdr.n_nodes;
-  int right_node = left_node + 1;
-  ts->hdr.n_nodes += 2;
-  NodeRec& pn = ts->nodes[L.node];
-  pn.feature = s.feature;
-  pn.gain = s.gain;
-  pn.left = left_node;
-  pn.right = right_node;
-  pn.is_cat = s.is_cat;
-  if (s.is_cat) {
-    pn.thr = -1;
-    pn.dleft = 0;
-    pn.mbin = -1;
-    for (int w = 0; w < 4; ++w) pn.bits[w] = s.bits[w];
-  } else {
-    pn.thr = s.bin;
-    pn.dleft = s.default_left;
-    pn.mbin = missing_bin[s.feature];
-  }
-  clear_node(ts->nodes[left_node], 0.0, n_left);
-  clear_node(ts->nodes[right_node], 0.0, n_right);
-  int new_slot = nl;
-  int built_is_left = n_left <= n_right ? 1 : 0;
-  P.active = 1;
-  P.parent_slot = best;
-  P.built_hist = new_slot;
-  P.sib_hist = L.hist_slot;
-  P.built_is_left = built_is_left;
-  P.feature = s.feature;
-  P.threshold = s.bin;
-  P.default_left = s.default_left;
-  P.missing_bin = s.is_cat ? -1 : missing_bin[s.feature];
-  P.is_cat = s.is_cat;
-  for (int w = 0; w < 4; ++w) P.bits[w] = s.bits[w];
-  P.src_buf = L.buf;
-  P.dst_buf = 1 - L.buf;
-  P.depth = L.depth + 1;
-  P.begin = L.begin;
-  P.count = L.count;
-  P.cursor_left = 0;
-  P.cursor_right = 0;
-  P.n_children = 2;
-  P.child_slot[0] = best;
-  P.child_slot[1] = new_slot;
-  P.child_hist[0] = built_is_left ? new_slot : L.hist_slot;
-  P.child_hist[1] = built_is_left ? L.hist_slot : new_slot;
-  P.child_node[0] = left_node;
-  P.child_node[1] = right_node;
-  // Children take their frontier slots now; ranges are completed by the
-  // finish kernel once the partition has counted this device's rows.
-  for (int c = 0; c < 2; ++c) {
-    LeafRec& C = ts->leaves[P.child_slot[c]];
-    C.node = P.child_node[c];
-    C.buf = P.dst_buf;
-    C.hist_slot = P.child_hist[c];
-    C.depth = P.depth;
-    C.split.found = 0;
-    C.split.gain = 0.0;
-  }
-  ts->hdr.n_leaves = nl + 1;
-}
-
-__device__ __forceinline__ bool goes_left(const Plan& P, int bin) {
+__device__ __forceinline__ bool goes_left(const BatchItem& P, int bin) {
   if (P.is_cat) {
     if (bin <= 0 || bin >= 256) return false;
     return (P.bits[bin >> 6] >> (bin & 63)) & 1ull;
@@ -419,36 +348,41 @@ __device__ __forceinline__ bool goes_left(const Plan& P, int bin) {
   return bin <= P.threshold;
 }
 
-// Partition of the parent range into this device's left rows (from the front,
-// each tile's rows in order) and right rows (from the back).  Also zeroes the
-// histogram slot the built child will accumulate into.
+// Partition of every expanded leaf's range into this device's left rows (from
+// the front, each tile's rows in order) and right rows (from the back), into
+// the other ping-pong buffer.  Tiles of all items are one flat index space.
+// Also zeroes the work slots the built children accumulate into.
 template <typename PairT, int ITEMS>
 __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t* __restrict__ bins_cm, long long n,
                                                    int* __restrict__ rows0, int* __restrict__ rows1,
                                                    PairT* __restrict__ pairs0, PairT* __restrict__ pairs1,
-                                                   int* __restrict__ hist, long long slot_cells, int work_slot) {
-  const Plan& P = ts->plan;
-  if (!P.active) return;
-  // zero the work slot the built child accumulates into
+                                                   int* __restrict__ hist, long long slot_cells, int work_base) {
+  Batch& Bt = ts->batch;
+  const int n_items = Bt.n_items;
+  if (n_items == 0) return;
   {
-    int* hs = hist + (long long)work_slot * slot_cells;
+    int* hs = hist + (long long)work_base * slot_cells;
+    long long total = (long long)n_items * slot_cells;
     long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     long long stride = (long long)gridDim.x * blockDim.x;
-    for (long long i = tid; i < slot_cells; i += stride) hs[i] = 0;
+    for (long long i = tid; i < total; i += stride) hs[i] = 0;
   }
-  const int* src_rows = P.src_buf ? rows1 : rows0;
-  int* dst_rows = P.src_buf ? rows0 : rows1;
-  const PairT* src_pairs = P.src_buf ? pairs1 : pairs0;
-  PairT* dst_pairs = P.src_buf ? pairs0 : pairs1;
-  const uint8_t* col = bins_cm + (long long)P.feature * n;
-  const long long begin = P.begin, count = P.count, end = P.begin + P.count;
+  if (Bt.root) return;  // the root's rows are already in place
   constexpr int TILE = 256 * ITEMS;
-  long long n_tiles = (count + TILE - 1) / TILE;
-  __shared__ int s_warp_l[8];
+  __shared__ int s_warp_l[8], s_wv[8], s_cl[8], s_cr[8];
   __shared__ unsigned long long s_base_l, s_base_r;
-  int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-    long long t0 = begin + tile * TILE;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (long long tile = blockIdx.x; tile < Bt.n_tiles; tile += gridDim.x) {
+    int it = 0;
+    while (it + 1 < n_items && Bt.items[it + 1].tile0 <= tile) ++it;
+    BatchItem& P = Bt.items[it];
+    const int* src_rows = P.src_buf ? rows1 : rows0;
+    int* dst_rows = P.src_buf ? rows0 : rows1;
+    const PairT* src_pairs = P.src_buf ? pairs1 : pairs0;
+    PairT* dst_pairs = P.src_buf ? pairs0 : pairs1;
+    const uint8_t* col = bins_cm + (long long)P.feature * n;
+    const long long begin = P.begin, end = P.begin + P.count;
+    const long long t0 = begin + (tile - P.tile0) * TILE;
     int rr[ITEMS];
     PairT pp[ITEMS];
     bool valid[ITEMS], left[ITEMS];
@@ -457,23 +391,20 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
     for (int j = 0; j < ITEMS; ++j) {
       long long i = t0 + (long long)j * 256 + threadIdx.x;
       valid[j] = i < end;
+      left[j] = false;
       if (valid[j]) {
         rr[j] = src_rows[i];
         pp[j] = src_pairs[i];
         left[j] = goes_left(P, col[rr[j]]);
-      } else {
-        left[j] = false;
       }
       my_l += left[j];
       my_valid += valid[j];
     }
-    // tile totals
     int wl = my_l, wv = my_valid;
     for (int k = 16; k > 0; k >>= 1) {
       wl += __shfl_xor_sync(0xffffffffu, wl, k);
       wv += __shfl_xor_sync(0xffffffffu, wv, k);
     }
-    __shared__ int s_wv[8];
     if (lane == 0) {
       s_warp_l[w] = wl;
       s_wv[w] = wv;
@@ -485,20 +416,18 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
         tl += s_warp_l[k];
         tv += s_wv[k];
       }
-      s_base_l = atomicAdd(&ts->plan.cursor_left, (unsigned long long)tl);
+      s_base_l = atomicAdd(&P.cursor_left, (unsigned long long)tl);
       unsigned long long nr = (unsigned long long)(tv - tl);
-      unsigned long long o = atomicAdd(&ts->plan.cursor_right, nr);
+      unsigned long long o = atomicAdd(&P.cursor_right, nr);
       s_base_r = (unsigned long long)end - o - nr;  // rights fill from the back
     }
     __syncthreads();
-    // ranks in element order (j major, thread minor)
-    int run_l = 0, run_r = 0;
+    int run_l = 0, run_r = 0;  // ranks in element order (j major, thread minor)
 #pragma unroll
     for (int j = 0; j < ITEMS; ++j) {
       unsigned bl = __ballot_sync(0xffffffffu, left[j]);
       unsigned bv = __ballot_sync(0xffffffffu, valid[j]);
       unsigned br = bv & ~bl;
-      __shared__ int s_cl[8], s_cr[8];
       if (lane == 0) {
         s_cl[w] = __popc(bl);
         s_cr[w] = __popc(br);
@@ -515,15 +444,10 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
       }
       unsigned below = (1u << lane) - 1u;
       if (valid[j]) {
-        if (left[j]) {
-          long long dst = begin + (long long)s_base_l + run_l + pre_l + __popc(bl & below);
-          dst_rows[dst] = rr[j];
-          dst_pairs[dst] = pp[j];
-        } else {
-          long long dst = (long long)s_base_r + run_r + pre_r + __popc(br & below);
-          dst_rows[dst] = rr[j];
-          dst_pairs[dst] = pp[j];
-        }
+        long long dst = left[j] ? begin + (long long)s_base_l + run_l + pre_l + __popc(bl & below)
+                                : (long long)s_base_r + run_r + pre_r + __popc(br & below);
+        dst_rows[dst] = rr[j];
+        dst_pairs[dst] = pp[j];
       }
       run_l += tot_l;
       run_r += tot_r;
@@ -533,8 +457,9 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
 }
 
 // ---------------------------------------------------------------------------
-// Histogram of one leaf: privatised shared-memory integer cells per CTA,
-// flushed with global integer atomics.
+// Histograms of the batch's built children: privatised shared-memory integer
+// cells per CTA, merged across a thread-block cluster through DSMEM, flushed
+// with int32 global atomics into each item's work slot.
 // ---------------------------------------------------------------------------
 
 // Shared-memory cells (32-bit atomics only; one CTA owns FG features):
@@ -546,131 +471,156 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
 // by 2^30 + n (FIXED, quantized_gradient.mojo:98-99) or by B * n (QUANT).
 constexpr int kQuantCountBits = 15;
 
-struct HistJob {
-  long long begin, count;
-  int buf;
-};
-
-__device__ __forceinline__ HistJob hist_job(const Plan& P) {
-  HistJob j;
+__device__ __forceinline__ void built_range(const BatchItem& P, long long& b, long long& cnt) {
   long long nl = (long long)P.cursor_left;
   if (P.built_is_left) {
-    j.begin = P.begin;
-    j.count = nl;
+    b = P.begin;
+    cnt = nl;
   } else {
-    j.begin = P.begin + nl;
-    j.count = P.count - nl;
+    b = P.begin + nl;
+    cnt = P.count - nl;
   }
-  j.buf = P.dst_buf;
-  return j;
 }
 
-// CTAs of one feature group are launched in thread-block clusters of CS along
-// grid y.  Each CTA accumulates its rows into its own shared-memory cells;
-// the cluster then merges the CS copies through distributed shared memory
-// (each CTA sums one CS-th of the cells across its peers) and only the
-// merged cells reach global memory, with one int32 atomic per plane.  Small
-// leaves activate fewer clusters (>= min_rows_per_cta rows per CTA); a cluster
-// that has no rows exits as a whole.  Every build lands in the work slot;
-// the scan kernel moves it into the child's slot after any cross-device sum.
-template <int VPR, int MODE, bool CONST_H>
-__global__ void __launch_bounds__(1024) k_hist(const Plan* __restrict__ plan, const uint8_t* __restrict__ bins_rm,
-                                               int Fp, int F, int B, const int* __restrict__ rows0,
-                                               const int* __restrict__ rows1, const void* __restrict__ pairs0,
-                                               const void* __restrict__ pairs1, int* __restrict__ hist,
-                                               long long slot_cells, long long rows_per_flush, int work_slot,
-                                               int min_rows_per_cta) {
-  namespace cg = cooperative_groups;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  constexpr int FG = VPR * 16;
+// Shared-memory layout, one bank per lane.  A warp takes one row at a time;
+// lane l owns the NPL consecutive features f0 + l*NPL + j (j < NPL) of the
+// CTA's feature group (FG = 32*NPL features) and loads their NPL bin bytes
+// with one load.  Cell (feature l*NPL + j, bin b) of plane p is word
+//   ((p * NPL + j) * B + b) * 32 + l
+// so the 32 atomics of one warp instruction fall in 32 different banks
+// whatever the bin values are: no bank conflicts and no same-address
+// collisions inside an instruction.
+template <int NPL>
+__device__ __forceinline__ int lane_cell(int j, int b, int B, int lane) {
+  return (j * B + b) * 32 + lane;
+}
+
+template <int NPL>
+struct BinWord;
+template <>
+struct BinWord<1> {
+  static __device__ __forceinline__ unsigned int load(const uint8_t* p) { return __ldg(p); }
+};
+template <>
+struct BinWord<2> {
+  static __device__ __forceinline__ unsigned int load(const uint8_t* p) {
+    return __ldg(reinterpret_cast<const unsigned short*>(p));
+  }
+};
+template <>
+struct BinWord<4> {
+  static __device__ __forceinline__ unsigned int load(const uint8_t* p) {
+    return __ldg(reinterpret_cast<const unsigned int*>(p));
+  }
+};
+
+#ifndef MTB_HIST_UNROLL
+#define MTB_HIST_UNROLL 8
+#endif
+constexpr int kHistUnroll = MTB_HIST_UNROLL;  // bin loads in flight per warp (divides 32)
+constexpr int kHistThreads = 1024;
+
+// One cluster accumulates rows [seg_b, seg_b + seg_n) of one item's built
+// child into the item's work slot.
+template <int NPL, int MODE, bool CONST_H>
+__device__ void hist_segment(cooperative_groups::cluster_group& cluster, const BatchItem& P, long long seg_b,
+                             long long seg_n, const uint8_t* __restrict__ bins_rm, int Fp, int F, int B,
+                             const int* __restrict__ rows0, const int* __restrict__ rows1,
+                             const void* __restrict__ pairs0, const void* __restrict__ pairs1, int* hs,
+                             long long rows_per_flush, unsigned int* p0) {
+  constexpr int FG = 32 * NPL;
   constexpr int NPLANE = (MODE == MODE_FIXED && !CONST_H) ? 3 : 2;
-  if (!plan->active) return;  // uniform across the grid
-  const HistJob job = hist_job(*plan);
-  if (job.count <= 0) return;
-  cg::cluster_group cluster = cg::this_cluster();
+  constexpr int U = kHistUnroll;
   const int cs = (int)cluster.num_blocks();
   const int crank = (int)cluster.block_rank();
-  const long long n_clusters = gridDim.y / cs;
-  const long long cid = blockIdx.y / cs;
-  const long long mrc = min_rows_per_cta;
-  long long want = (job.count + mrc * cs - 1) / (mrc * cs);
-  long long nce = want < n_clusters ? want : n_clusters;
-  if (cid >= nce) return;  // the whole cluster leaves together
-  const long long cchunk = (job.count + nce - 1) / nce;
-  const long long c0 = job.begin + cid * cchunk;
-  long long c1 = c0 + cchunk;
-  if (c1 > job.begin + job.count) c1 = job.begin + job.count;
-  const long long sub = (cchunk + cs - 1) / cs;  // rows per CTA, identical across the cluster
-  const long long s = c0 + crank * sub;
+  const long long sub = (seg_n + cs - 1) / cs;  // rows per CTA, identical across the cluster
+  const long long s = seg_b + crank * sub;
   long long e = s + sub;
-  if (e > c1) e = c1;
+  if (e > seg_b + seg_n) e = seg_b + seg_n;
   const long long n_pass = (sub + rows_per_flush - 1) / rows_per_flush;
   const int f0 = blockIdx.x * FG;
-  const int cells = FG * B;
-  unsigned int* p0 = reinterpret_cast<unsigned int*>(smem_raw);
+  const int cells = NPL * B * 32;  // words per plane
   unsigned int* p1 = p0 + cells;
   unsigned int* p2 = p1 + cells;
-  const int* rows = job.buf ? rows1 : rows0;
-  const void* pairs = job.buf ? pairs1 : pairs0;
-  const int v = threadIdx.x % VPR;
-  const int rsub = threadIdx.x / VPR;
-  const int rpi = blockDim.x / VPR;  // rows per iteration
-  // threads beyond rpi * VPR idle (blockDim need not divide by VPR); the last
-  // group may extend past the row
-  const bool vec_ok = f0 + v * 16 < Fp && rsub < rpi;
-  int* hs = hist + (long long)work_slot * slot_cells;
+  const int* rows = P.dst_buf ? rows1 : rows0;
+  const void* pairs = P.dst_buf ? pairs1 : pairs0;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int n_warps = blockDim.x >> 5;
+  // lanes past the padded row width load nothing (NPL divides 16, so a lane
+  // that starts inside the row ends inside it)
+  const bool lane_ok = f0 + lane * NPL < Fp;
+  const uint8_t* bcol = bins_rm + f0 + lane * NPL;
   const int slice = (cells + cs - 1) / cs;
   const int m0 = crank * slice;
   const int m1 = m0 + slice < cells ? m0 + slice : cells;
   for (long long pass = 0; pass < n_pass; ++pass) {
-    long long ps = s + pass * rows_per_flush;
-    long long pe = ps + rows_per_flush < e ? ps + rows_per_flush : e;
+    const long long ps = s + pass * rows_per_flush;
+    const long long pe = ps + rows_per_flush < e ? ps + rows_per_flush : e;
     for (int c = threadIdx.x; c < cells * NPLANE; c += blockDim.x) p0[c] = 0u;
     __syncthreads();
-    // two rows in flight per thread: both gathers are issued before the
-    // shared-memory atomics of either, so the atomic pipe stays fed
-    for (long long i = ps + rsub; vec_ok && i < pe; i += 2 * rpi) {
-      const long long i2 = i + rpi;
-      const bool two = i2 < pe;
-      int r0 = __ldg(rows + i);
-      int r1 = two ? __ldg(rows + i2) : r0;
-      unsigned int a0[2], a1[2];
-      const unsigned int a2 = 1u;
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        long long ii = u == 0 ? i : (two ? i2 : i);
+    // Each warp takes chunks of 32 consecutive positions: lane k loads the
+    // row id and gradient pair of position k (coalesced; the next chunk's are
+    // fetched while this one is processed), then the warp walks the chunk with
+    // U bin loads in flight before their atomics.
+    const long long stride = (long long)n_warps * 32;
+    long long c0 = ps + (long long)warp * 32;
+    int nr = -1;
+    unsigned int na0 = 0u, na1 = 0u;
+    auto fetch = [&](long long base, int& r, unsigned int& x0, unsigned int& x1) {
+      const long long i = base + lane;
+      r = -1;
+      x0 = 0u;
+      x1 = 0u;
+      if (i < pe) {
+        r = __ldg(rows + i);
         if (MODE == MODE_QUANT) {
-          uint16_t pr = __ldg(reinterpret_cast<const uint16_t*>(pairs) + ii);
+          uint16_t pr = __ldg(reinterpret_cast<const uint16_t*>(pairs) + i);
           int g = (int)(int8_t)(pr & 0xff);
-          a0[u] = (unsigned int)(g * (1 << kQuantCountBits) + 1);
-          a1[u] = (unsigned int)(pr >> 8);
+          x0 = (unsigned int)(g * (1 << kQuantCountBits) + 1);
+          x1 = (unsigned int)(pr >> 8);
         } else {
-          int2 pr = __ldg(reinterpret_cast<const int2*>(pairs) + ii);
-          a0[u] = (unsigned int)pr.x;
-          a1[u] = CONST_H ? 1u : (unsigned int)pr.y;
+          int2 pr = __ldg(reinterpret_cast<const int2*>(pairs) + i);
+          x0 = (unsigned int)pr.x;
+          x1 = CONST_H ? 1u : (unsigned int)pr.y;
         }
       }
-      uint4 bv0 = __ldg(reinterpret_cast<const uint4*>(bins_rm + (long long)r0 * Fp + f0 + v * 16));
-      uint4 bv1 = __ldg(reinterpret_cast<const uint4*>(bins_rm + (long long)r1 * Fp + f0 + v * 16));
-      const int base = v * 16 * B;
+    };
+    if (c0 < pe) fetch(c0, nr, na0, na1);
+    for (; c0 < pe; c0 += stride) {
+      const int cr = nr;
+      const unsigned int ca0 = na0, ca1 = na1;
+      if (c0 + stride < pe) fetch(c0 + stride, nr, na0, na1);
+      const int n_in = pe - c0 < 32 ? (int)(pe - c0) : 32;
+      for (int u0 = 0; u0 < n_in; u0 += U) {
+        unsigned int bw[U];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        if (u == 1 && !two) break;
-        const uint4 bv = u == 0 ? bv0 : bv1;
-        const unsigned int w[4] = {bv.x, bv.y, bv.z, bv.w};
+        for (int u = 0; u < U; ++u) {
+          const int r = __shfl_sync(0xffffffffu, cr, u0 + u);
+          bw[u] = (u0 + u < n_in && lane_ok) ? BinWord<NPL>::load(bcol + (long long)r * Fp) : 0u;
+        }
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          int cell = base + k * B + (int)((w[k >> 2] >> (8 * (k & 3))) & 0xffu);
-          atomicAdd(&p0[cell], a0[u]);
-          atomicAdd(&p1[cell], a1[u]);
-          if (NPLANE == 3) atomicAdd(&p2[cell], a2);
+        for (int u = 0; u < U; ++u) {
+          const unsigned int x0 = __shfl_sync(0xffffffffu, ca0, u0 + u);
+          const unsigned int x1 = __shfl_sync(0xffffffffu, ca1, u0 + u);
+          if (!(u0 + u < n_in && lane_ok)) continue;
+#pragma unroll
+          for (int j = 0; j < NPL; ++j) {
+            const int cell = lane_cell<NPL>(j, (int)((bw[u] >> (8 * j)) & 0xffu), B, lane);
+            atomicAdd(&p0[cell], x0);
+            atomicAdd(&p1[cell], x1);
+            if (NPLANE == 3) atomicAdd(&p2[cell], 1u);
+          }
         }
       }
     }
     cluster.sync();
     for (int c = m0 + threadIdx.x; c < m1; c += blockDim.x) {
-      int fl = c / B;
-      int f = f0 + fl;
+      const int l = c & 31;
+      const int jb = c >> 5;
+      const int j = jb / B;
+      const int bin = jb - j * B;
+      const int f = f0 + l * NPL + j;
       if (f >= F) continue;
       int g = 0, h = 0, cnt = 0;
       for (int rk = 0; rk < cs; ++rk) {
@@ -691,7 +641,6 @@ __global__ void __launch_bounds__(1024) k_hist(const Plan* __restrict__ plan, co
         }
       }
       if (cnt == 0) continue;
-      int bin = c - fl * B;
       int* cellp = hs + (f * 3) * B + bin;
       atomicAdd(cellp, g);
       if (!(MODE == MODE_FIXED && CONST_H)) atomicAdd(cellp + B, h);
@@ -701,8 +650,55 @@ __global__ void __launch_bounds__(1024) k_hist(const Plan* __restrict__ plan, co
   }
 }
 
+// CTAs of one feature group form clusters of CS along grid y.  The batch's
+// built rows, taken as one sequence (item after item), are split evenly among
+// ceil(rows / (min_rows_per_cta * CS)) clusters at most; a cluster whose share
+// spans several items accumulates one segment per item.
+template <int NPL, int MODE, bool CONST_H>
+__global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__ batch, const uint8_t* __restrict__ bins_rm,
+                                               int Fp, int F, int B, const int* __restrict__ rows0,
+                                               const int* __restrict__ rows1, const void* __restrict__ pairs0,
+                                               const void* __restrict__ pairs1, int* __restrict__ hist,
+                                               long long slot_cells, long long rows_per_flush, int work_base,
+                                               int min_rows_per_cta) {
+  namespace cg = cooperative_groups;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  unsigned int* p0 = reinterpret_cast<unsigned int*>(smem_raw);
+  const int n_items = batch->n_items;  // uniform across the grid
+  if (n_items == 0) return;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int cs = (int)cluster.num_blocks();
+  const long long n_clusters = gridDim.y / cs;
+  const long long cid = blockIdx.y / cs;
+  long long S = 0;
+  for (int i = 0; i < n_items; ++i) {
+    long long b, c;
+    built_range(batch->items[i], b, c);
+    S += c;
+  }
+  if (S == 0) return;
+  const long long per_cluster = (long long)min_rows_per_cta * cs;
+  long long cap = (S + per_cluster - 1) / per_cluster;
+  if (cap > n_clusters) cap = n_clusters;
+  if (cid >= cap) return;  // the whole cluster leaves together
+  const long long lo = S * cid / cap, hi = S * (cid + 1) / cap;
+  long long acc = 0;
+  for (int i = 0; i < n_items && acc < hi; ++i) {
+    const BatchItem& P = batch->items[i];
+    long long b, c;
+    built_range(P, b, c);
+    const long long s0 = lo > acc ? lo : acc;
+    const long long s1 = hi < acc + c ? hi : acc + c;
+    if (s1 > s0)
+      hist_segment<NPL, MODE, CONST_H>(cluster, P, b + (s0 - acc), s1 - s0, bins_rm, Fp, F, B, rows0, rows1, pairs0,
+                                       pairs1, hist + (long long)(work_base + P.work) * slot_cells, rows_per_flush,
+                                       p0);
+    acc += c;
+  }
+}
+
 // ---------------------------------------------------------------------------
-// Subtract + split scan: one warp per (child, active feature).
+// Subtract + split scan: one block per (child, active feature).
 // ---------------------------------------------------------------------------
 
 struct ScanParams {
@@ -734,97 +730,85 @@ __device__ __forceinline__ double deq(long long q, int mode, double inv, double 
   return mode == MODE_FIXED ? (double)q * inv : (double)q / units;
 }
 
-constexpr int kScanThreads = 256;  // one thread per bin (B <= 256)
-
-// Block-wide inclusive sum of three int64 values per thread (bin order).
-__device__ __forceinline__ void block_scan3(long long& a, long long& b, long long& c, long long* sw /*[3][8]*/) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-#pragma unroll
-  for (int k = 1; k < 32; k <<= 1) {
-    long long oa = __shfl_up_sync(0xffffffffu, a, k);
-    long long ob = __shfl_up_sync(0xffffffffu, b, k);
-    long long oc = __shfl_up_sync(0xffffffffu, c, k);
-    if (lane >= k) {
-      a += oa;
-      b += ob;
-      c += oc;
-    }
-  }
-  if (lane == 31) {
-    sw[w] = a;
-    sw[8 + w] = b;
-    sw[16 + w] = c;
-  }
-  __syncthreads();
-  long long pa = 0, pb = 0, pc = 0;
-  for (int q = 0; q < w; ++q) {
-    pa += sw[q];
-    pb += sw[8 + q];
-    pc += sw[16 + q];
-  }
-  a += pa;
-  b += pb;
-  c += pc;
-}
-
-// One block per (child, active feature), one thread per bin: sibling
+// One warp per (child, active feature), 8 bins per lane: sibling
 // subtraction, exact integer prefix sums, the reference gain per candidate
-// threshold, and a block arg-max that keeps the serial scan's tie rule
-// (first maximum in bin order, missing-left candidate before default-right).
-__device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, long long slot_cells,
-                          const int* __restrict__ feats, const int* __restrict__ missing_bin,
-                          const int* __restrict__ n_cats, const RoundScales* __restrict__ sc, ScanParams sp,
-                          FeatBest* __restrict__ out, int root, int work_slot) {
-  __shared__ int s_cells[3][256];
-  __shared__ long long s_w[24];
-  __shared__ double s_gain[8];
-  __shared__ int s_key[8];
-  __shared__ long long s_nl[8];
-  const Plan& P = ts->plan;
-  if (!P.active) return;  // uniform
-  const int c = blockIdx.x;
-  if (c >= P.n_children) return;  // uniform
-  const int j = blockIdx.y;
-  const int t = threadIdx.x;
-  const int lane = t & 31, w = t >> 5;
+// threshold, and a warp arg-max that keeps the serial scan's tie rule (first
+// maximum in bin order, missing-left candidate before default-right).  Pair
+// p = child * n_active + j, child = 2 * item + side.
+constexpr int kScanWarps = 8;    // pairs per block
+constexpr int kBinsPerLane = 8;  // 32 x 8 = 256 bins at most
+
+__global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan(TreeState* __restrict__ ts, int* __restrict__ hist,
+                                                          long long slot_cells, const int* __restrict__ feats,
+                                                          const int* __restrict__ missing_bin,
+                                                          const int* __restrict__ n_cats,
+                                                          const RoundScales* __restrict__ sc, ScanParams sp,
+                                                          FeatBest* __restrict__ out, int work_base) {
+  __shared__ int s_cells[kScanWarps][3][256];  // categorical searches only
+  const Batch& Bt = ts->batch;
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const long long pair = (long long)blockIdx.x * kScanWarps + wib;
+  const int c = (int)(pair / sp.n_active);
+  const int j = (int)(pair - (long long)c * sp.n_active);
+  const int item = c >> 1, side = c & 1;
+  if (item >= Bt.n_items) return;  // warp-uniform; the kernel has no block barrier
+  if (Bt.root && side) return;
+  const BatchItem& P = Bt.items[item];
   const int B = sp.B;
   const int f = feats[j];
-  int* hs = hist + (long long)P.child_hist[c] * slot_cells + (long long)f * 3 * B;
-  const bool built = root || P.child_hist[c] != P.sib_hist;
-  const int* wk = hist + (long long)work_slot * slot_cells + (long long)f * 3 * B;
+  const bool built = Bt.root || side == (P.built_is_left ? 0 : 1);
+  int* hs = hist + (long long)(built ? P.built_hist : P.sib_hist) * slot_cells + (long long)f * 3 * B;
+  const int* wk = hist + (long long)(work_base + P.work) * slot_cells + (long long)f * 3 * B;
   const int mode = sp.mode;
+  const bool ch_fixed = sp.const_hess && mode == MODE_FIXED;
+  const int hq = ch_fixed ? sc->hq_const : 0;
+  const int b0 = lane * kBinsPerLane;
   // built child: the (reduced) work slot; sibling: parent - built, in place
-  int vg = 0, vh = 0, vc = 0;
-  if (t < B) {
-    int wg = __ldcg(wk + t), wh = __ldcg(wk + B + t), wc = __ldcg(wk + 2 * B + t);
-    if (built) {
-      vg = wg;
-      vh = wh;
-      vc = wc;
-    } else {
-      vg = __ldcg(hs + t) - wg;
-      vh = __ldcg(hs + B + t) - wh;
-      vc = __ldcg(hs + 2 * B + t) - wc;
+  int vg[kBinsPerLane], vh[kBinsPerLane], vc[kBinsPerLane];
+  long long sg = 0, sh = 0, scn = 0;
+#pragma unroll
+  for (int q = 0; q < kBinsPerLane; ++q) {
+    const int b = b0 + q;
+    vg[q] = 0;
+    vh[q] = 0;
+    vc[q] = 0;
+    if (b < B) {
+      const int wg = wk[b], wh = wk[B + b], wc = wk[2 * B + b];
+      if (built) {
+        vg[q] = wg;
+        vh[q] = wh;
+        vc[q] = wc;
+      } else {
+        vg[q] = hs[b] - wg;
+        vh[q] = hs[B + b] - wh;
+        vc[q] = hs[2 * B + b] - wc;
+      }
+      hs[b] = vg[q];
+      hs[B + b] = vh[q];
+      hs[2 * B + b] = vc[q];
+      if (ch_fixed) vh[q] = (int)((long long)hq * vc[q]);
     }
-    hs[t] = vg;
-    hs[B + t] = vh;
-    hs[2 * B + t] = vc;
-    if (sp.const_hess && mode == MODE_FIXED) vh = (int)((long long)sc->hq_const * vc);
+    sg += vg[q];
+    sh += vh[q];
+    scn += vc[q];
   }
-  s_cells[0][t] = vg;
-  s_cells[1][t] = vh;
-  s_cells[2][t] = vc;
-  long long Lg = vg, Lh = vh, Lc = vc;  // inclusive prefix through bin t
-  block_scan3(Lg, Lh, Lc, s_w);
-  __shared__ long long s_tot[3];
-  if (t == kScanThreads - 1) {
-    s_tot[0] = Lg;
-    s_tot[1] = Lh;
-    s_tot[2] = Lc;
+  // warp scan of the lane totals: exclusive prefix = sums of earlier lanes
+  long long ig = sg, ih = sh, ic = scn;
+#pragma unroll
+  for (int k = 1; k < 32; k <<= 1) {
+    const long long og = __shfl_up_sync(0xffffffffu, ig, k);
+    const long long oh = __shfl_up_sync(0xffffffffu, ih, k);
+    const long long oc = __shfl_up_sync(0xffffffffu, ic, k);
+    if (lane >= k) {
+      ig += og;
+      ih += oh;
+      ic += oc;
+    }
   }
-  __syncthreads();
-  const long long Tg = s_tot[0], Th = s_tot[1], Tc = s_tot[2];
-  if (j == 0 && t == 0) {
+  const long long Tg = __shfl_sync(0xffffffffu, ig, 31);
+  const long long Th = __shfl_sync(0xffffffffu, ih, 31);
+  const long long Tc = __shfl_sync(0xffffffffu, ic, 31);
+  if (j == 0 && lane == 0) {
     ts->totals[c].g = Tg;
     ts->totals[c].h = Th;
     ts->totals[c].c = Tc;
@@ -839,15 +823,23 @@ __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, lo
   fb.flags = 0;
   fb.n_left = 0;
   fb.bits[0] = fb.bits[1] = fb.bits[2] = fb.bits[3] = 0;
+  int(*cw)[256] = s_cells[wib];
   if (n_cats[f] >= 0) {
+#pragma unroll
+    for (int q = 0; q < kBinsPerLane; ++q) {
+      cw[0][b0 + q] = vg[q];
+      cw[1][b0 + q] = vh[q];
+      cw[2][b0 + q] = vc[q];
+    }
+    __syncwarp();
     // categorical: serial search on thread 0 (categorical.mojo:478-780) over
     // the exact per-category sums
-    if (t == 0) {
+    if (lane == 0) {
       int n_cat = n_cats[f];
       double parent = leaf_score(tg, th, l1, l2);
       if (n_cat >= 2 && n_cat + 1 <= sp.max_cat_to_onehot) {
         for (int q = 1; q <= n_cat && q < B; ++q) {
-          long long qg = s_cells[0][q], qh = s_cells[1][q], cc = s_cells[2][q];
+          long long qg = cw[0][q], qh = cw[1][q], cc = cw[2][q];
           double lgv = deq(qg, mode, g_inv, gu), lhv = deq(qh, mode, h_inv, hu);
           if (cc < mdl || lhv < mch) continue;
           if (Tc - cc < mdl) continue;
@@ -868,9 +860,9 @@ __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, lo
         double key[256];
         int used = 0;
         for (int q = 1; q <= n_cat && q < B; ++q) {
-          if (!((double)s_cells[2][q] >= sp.cat_smooth)) continue;
-          double gv = deq(s_cells[0][q], mode, g_inv, gu);
-          double hv = deq(s_cells[1][q], mode, h_inv, hu);
+          if (!((double)cw[2][q] >= sp.cat_smooth)) continue;
+          double gv = deq(cw[0][q], mode, g_inv, gu);
+          double hv = deq(cw[1][q], mode, h_inv, hu);
           double kv = gv / (hv + sp.cat_smooth);
           int p = used;  // insertion keeps equal keys in category order (stable)
           while (p > 0 && key[p - 1] > kv) {
@@ -895,10 +887,10 @@ __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, lo
             for (int i = 0; i < steps; ++i) {
               int q = cand[pos];
               pos += dir;
-              qg += s_cells[0][q];
-              qh += s_cells[1][q];
-              qc += s_cells[2][q];
-              cnt_group += s_cells[2][q];
+              qg += cw[0][q];
+              qh += cw[1][q];
+              qc += cw[2][q];
+              cnt_group += cw[2][q];
               double lgv = deq(qg, mode, g_inv, gu), lhv = deq(qh, mode, h_inv, hu);
               if (qc < mdl || lhv < mch) continue;
               long long rc = Tc - qc;
@@ -933,9 +925,18 @@ __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, lo
   const int n_scan = mb >= 0 ? mb : B;
   long long mg = 0, mh = 0, mc = 0;
   if (mb >= 0) {
-    mg = s_cells[0][mb];
-    mh = s_cells[1][mb];
-    mc = s_cells[2][mb];
+    int xg = 0, xh = 0, xc = 0;
+#pragma unroll
+    for (int q = 0; q < kBinsPerLane; ++q)
+      if (b0 + q == mb) {
+        xg = vg[q];
+        xh = vh[q];
+        xc = vc[q];
+      }
+    const int src = mb / kBinsPerLane;
+    mg = __shfl_sync(0xffffffffu, xg, src);
+    mh = __shfl_sync(0xffffffffu, xh, src);
+    mc = __shfl_sync(0xffffffffu, xc, src);
   }
   const double pg = soft_l1(tg, l1);
   const double parent = pg * pg / (th + l2);
@@ -943,8 +944,14 @@ __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, lo
   double best_gain = 0.0;
   int best_key = 0x7fffffff;  // 2*bin + order
   long long best_nl = 0;
-  const int b = t;
-  if (b < n_scan && !(b == n_scan - 1 && mc == 0)) {
+  long long Lg = ig - sg, Lh = ih - sh, Lc = ic - scn;  // prefix before this lane's bins
+#pragma unroll
+  for (int q = 0; q < kBinsPerLane; ++q) {
+    const int b = b0 + q;
+    Lg += vg[q];  // inclusive prefix through bin b
+    Lh += vh[q];
+    Lc += vc[q];
+    if (!(b < n_scan && !(b == n_scan - 1 && mc == 0))) continue;
     if (mb >= 0) {
       long long Dg = Lg + mg, Dh = Lh + mh, Dc = Lc + mc;
       double dlg = deq(Dg, mode, g_inv, gu), dlh = deq(Dh, mode, h_inv, hu);
@@ -985,7 +992,7 @@ __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, lo
       }
     }
   }
-  // block arg-max: higher gain, then lower key (earlier in the serial scan)
+  // warp arg-max: higher gain, then lower key (earlier in the serial scan)
   for (int k = 16; k > 0; k >>= 1) {
     double og = __shfl_xor_sync(0xffffffffu, best_gain, k);
     int ok = __shfl_xor_sync(0xffffffffu, best_key, k);
@@ -997,19 +1004,6 @@ __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, lo
     }
   }
   if (lane == 0) {
-    s_gain[w] = best_gain;
-    s_key[w] = best_key;
-    s_nl[w] = best_nl;
-  }
-  __syncthreads();
-  if (t == 0) {
-    for (int q = 1; q < kScanThreads / 32; ++q) {
-      if (s_gain[q] > best_gain || (s_gain[q] == best_gain && s_key[q] < best_key)) {
-        best_gain = s_gain[q];
-        best_key = s_key[q];
-        best_nl = s_nl[q];
-      }
-    }
     if (best_key != 0x7fffffff && best_gain > 0.0) {
       fb.gain = best_gain;
       fb.bin = best_key >> 1;
@@ -1020,55 +1014,114 @@ __device__ void scan_body(TreeState* __restrict__ ts, int* __restrict__ hist, lo
   }
 }
 
-// Cross-feature fold (ascending feature, strict >), guards, leaf values and
-// the children's ranges.
-__device__ void block_finish(TreeState* __restrict__ ts, const FeatBest* __restrict__ fbs,
-                             const int* __restrict__ feats, const RoundScales* __restrict__ sc, ScanParams sp,
-                             int root) {
-  __shared__ double s_gain[256];
-  __shared__ int s_j[256];
-  Plan& P = ts->plan;
-  if (!P.active) return;
-  int t = threadIdx.x;
-  for (int c = 0; c < P.n_children; ++c) {
+// ---------------------------------------------------------------------------
+// Commit: one 1024-thread block after every scan.
+//
+// 1. Fold each new child's per-feature bests (ascending feature, strict >),
+//    apply the leaf guards, write its split, value and local row range.
+// 2. Replay the reference's pick loop (growth_policy.mojo:659-677: largest
+//    gain > 0, lowest frontier slot on ties) over the frontier, committing
+//    every pick whose children are already computed, until the leaf budget is
+//    spent, no leaf has a positive gain (tree done), or the pick still needs
+//    its expansion.
+// 3. Select the next batch: the first m frontier leaves in pick order,
+//    m = min(batch capacity, leaves still to add); those not yet expanded
+//    become the batch (the current pick is always among them).
+// ---------------------------------------------------------------------------
+
+constexpr int kCommitThreads = 1024;
+
+struct CommitParams {
+  int num_leaves;
+  int batch_cap;       // leaves expanded per iteration at most (<= kMaxBatch)
+  int hist_slots;      // histogram slots available for leaves
+  int tile_rows;       // rows per partition tile
+};
+
+// (gain, slot) order of the pick: larger gain first, then lower slot.
+__device__ __forceinline__ bool pick_before(double ga, int sa, double gb, int sb) {
+  if (sb < 0) return sa >= 0;
+  if (sa < 0) return false;
+  return ga > gb || (ga == gb && sa < sb);
+}
+
+__device__ __forceinline__ double frontier_gain(const LeafRec& L) {
+  return (L.split.found && L.split.gain > 0.0) ? L.split.gain : -1.0;
+}
+
+// Per frontier slot shared-memory bytes of k_commit (dynamic, sized by the
+// leaf budget): gain, children's gains, leaf id, children's ids, commit
+// list (slot, leaf), expanded flag.
+constexpr int kCommitSlotBytes = 3 * 8 + 5 * 4 + 1;
+
+inline size_t commit_smem_bytes(int num_leaves) {
+  return (size_t)num_leaves * kCommitSlotBytes + 64;
+}
+
+__global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict__ ts,
+                                                           const FeatBest* __restrict__ fbs,
+                                                           const int* __restrict__ feats,
+                                                           const int* __restrict__ missing_bin,
+                                                           const RoundScales* __restrict__ sc, ScanParams sp,
+                                                           CommitParams cp, int* __restrict__ host_done,
+                                                           int host_done_index) {
+  extern __shared__ __align__(16) unsigned char commit_smem[];
+  const int L_max = cp.num_leaves;
+  double* s_g = reinterpret_cast<double*>(commit_smem);  // frontier gain, -1 when the leaf cannot split
+  double* s_cg0 = s_g + L_max;                            // expanded slot: children's gains
+  double* s_cg1 = s_cg0 + L_max;
+  int* s_leaf = reinterpret_cast<int*>(s_cg1 + L_max);   // slot -> leaf id
+  int* s_c0 = s_leaf + L_max;                             // expanded slot: children's leaf ids
+  int* s_c1 = s_c0 + L_max;
+  // commit k of this launch splits frontier slot s_cslot[k] (leaf s_cpar[k]);
+  // its right child takes slot nl0 + k
+  int* s_cslot = s_c1 + L_max;
+  int* s_cpar = s_cslot + L_max;
+  unsigned char* s_x = reinterpret_cast<unsigned char*>(s_cpar + L_max);  // expanded
+  __shared__ int s_ncommit, s_stop, s_nl;
+  __shared__ int s_rank_slot[kMaxBatch];
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  TreeHeader& H = ts->hdr;
+  Batch& Bt = ts->batch;
+  const int n_items = Bt.n_items;
+  const bool root = Bt.root != 0;
+#ifdef MTB_COMMIT_CLOCKS
+  long long clk[8];
+  int n_clk = 0;
+  clk[n_clk++] = clock64();
+#define MTB_CLK() if (t == 0) clk[n_clk++] = clock64()
+#else
+#define MTB_CLK()
+#endif
+
+  // ---- 1. children of this iteration's expansions (one warp per child)
+  for (int c = w; c < 2 * n_items; c += kCommitThreads / 32) {
+    const int item = c >> 1, side = c & 1;
+    if (root && side) continue;
+    const BatchItem& P = Bt.items[item];
     double bg = 0.0;
     int bj = -1;
-    for (int j = t; j < sp.n_active; j += 256) {
+    for (int j = lane; j < sp.n_active; j += 32) {
       const FeatBest& fb = fbs[(long long)c * sp.n_active + j];
       if ((fb.flags & 1) && fb.gain > bg) {
         bg = fb.gain;
         bj = j;
       }
     }
-    s_gain[t] = bg;
-    s_j[t] = bj;
-    __syncthreads();
-    for (int w = 128; w > 0; w >>= 1) {
-      if (t < w) {
-        double og = s_gain[t + w];
-        int oj = s_j[t + w];
-        if (oj >= 0 && (s_j[t] < 0 || og > s_gain[t] || (og == s_gain[t] && oj < s_j[t]))) {
-          s_gain[t] = og;
-          s_j[t] = oj;
-        }
+    for (int k = 16; k > 0; k >>= 1) {
+      double og = __shfl_xor_sync(0xffffffffu, bg, k);
+      int oj = __shfl_xor_sync(0xffffffffu, bj, k);
+      if (oj >= 0 && (bj < 0 || og > bg || (og == bg && oj < bj))) {
+        bg = og;
+        bj = oj;
       }
-      __syncthreads();
     }
-    if (t == 0) {
-      LeafRec& L = ts->leaves[P.child_slot[c]];
+    if (lane == 0) {
+      LeafRec& L = ts->pool[P.child[side]];
       const ChildTotals tot = ts->totals[c];
-      long long n_rows = tot.c;
+      const long long n_rows = tot.c;
       SplitRec s;
-      s.found = 0;
-      s.gain = 0.0;
-      s.feature = -1;
-      s.bin = -1;
-      s.default_left = 0;
-      s.is_cat = 0;
-      s.pad = 0;
-      s.n_left = 0;
-      s.bits[0] = s.bits[1] = s.bits[2] = s.bits[3] = 0;
-      int bj = s_j[0];
+      clear_split(s);
       if (bj >= 0 && !(n_rows < 2 * (long long)sp.min_data_in_leaf || n_rows < 2)) {
         const FeatBest& fb = fbs[(long long)c * sp.n_active + bj];
         s.found = 1;
@@ -1083,76 +1136,291 @@ __device__ void block_finish(TreeState* __restrict__ ts, const FeatBest* __restr
       L.split = s;
       double gd = sp.mode == MODE_FIXED ? (double)tot.g * sc->g_inv : (double)tot.g / sc->g_units;
       double hd = sp.mode == MODE_FIXED ? (double)tot.h * sc->h_inv : (double)tot.h / sc->h_units;
-      double value = -soft_l1(gd, sp.lambda_l1) / (hd + sp.lambda_l2);
-      NodeRec& nd = ts->nodes[P.child_node[c]];
-      nd.value = value;
-      nd.count = n_rows;
-      if (!root) {
-        long long nl = (long long)P.cursor_left;
-        if (c == 0) {
-          L.begin = P.begin;
-          L.count = nl;
-        } else {
-          L.begin = P.begin + nl;
-          L.count = P.count - nl;
-        }
+      L.value = -soft_l1(gd, sp.lambda_l1) / (hd + sp.lambda_l2);
+      L.gcount = n_rows;
+      if (root) {
+        NodeRec& nd = ts->nodes[L.node];
+        nd.value = L.value;
+        nd.count = n_rows;
+      } else {
+        const long long nl = (long long)P.cursor_left;
+        L.begin = side == 0 ? P.begin : P.begin + nl;
+        L.count = side == 0 ? nl : P.count - nl;
       }
     }
+  }
+  __syncthreads();
+  if (!root && t < n_items) {
+    const BatchItem& P = Bt.items[t];
+    LeafRec& L = ts->pool[P.leaf];
+    L.state = 1;
+    L.exp_buf = P.dst_buf;
+  }
+  __syncthreads();
+  MTB_CLK();
+
+  // ---- 2. the frontier into shared memory
+  const int nl0 = H.n_leaves;
+  for (int i = t; i < nl0; i += kCommitThreads) {
+    const int leaf = ts->slot_leaf[i];
+    const LeafRec& L = ts->pool[leaf];
+    s_leaf[i] = leaf;
+    s_g[i] = frontier_gain(L);
+    const bool x = L.state == 1;
+    s_x[i] = x ? 1 : 0;
+    if (x) {
+      s_c0[i] = L.child[0];
+      s_c1[i] = L.child[1];
+      s_cg0[i] = frontier_gain(ts->pool[L.child[0]]);
+      s_cg1[i] = frontier_gain(ts->pool[L.child[1]]);
+    }
+  }
+  __syncthreads();
+  MTB_CLK();
+
+  // ---- 3. the pick loop, on one warp over shared memory only
+  if (w == 0) {
+    int nl = nl0;
+    int n_commit = 0;
+    int stop = H.done;
+    while (!stop && nl < L_max) {
+      double bg = -1.0;
+      int bs = -1;
+      for (int i = lane; i < nl; i += 32) {
+        const double g = s_g[i];
+        if (g > 0.0 && pick_before(g, i, bg, bs)) {
+          bg = g;
+          bs = i;
+        }
+      }
+      for (int k = 16; k > 0; k >>= 1) {
+        const double og = __shfl_xor_sync(0xffffffffu, bg, k);
+        const int os = __shfl_xor_sync(0xffffffffu, bs, k);
+        if (pick_before(og, os, bg, bs)) {
+          bg = og;
+          bs = os;
+        }
+      }
+      if (bs < 0) {
+        stop = 1;
+        break;
+      }
+      if (!s_x[bs]) break;  // the pick still needs its expansion
+      if (lane == 0) {
+        s_cslot[n_commit] = bs;
+        s_cpar[n_commit] = s_leaf[bs];
+        s_g[nl] = s_cg1[bs];
+        s_leaf[nl] = s_c1[bs];
+        s_x[nl] = 0;
+        s_g[bs] = s_cg0[bs];
+        s_leaf[bs] = s_c0[bs];
+        s_x[bs] = 0;
+      }
+      __syncwarp();
+      ++n_commit;
+      ++nl;
+    }
+    if (nl >= L_max) stop = 1;
+    if (lane == 0) {
+      s_ncommit = n_commit;
+      s_nl = nl;
+      s_stop = stop;
+    }
+  }
+  __syncthreads();
+  MTB_CLK();
+
+  // ---- 4. the commits' writes, one thread each
+  const int n_commit = s_ncommit;
+  const int nl = s_nl;
+  const int nodes0 = H.n_nodes;
+  for (int k = t; k < n_commit; k += kCommitThreads) {
+    const int slot = s_cslot[k];
+    LeafRec& L = ts->pool[s_cpar[k]];
+    const SplitRec& s = L.split;
+    const int left_node = nodes0 + 2 * k, right_node = left_node + 1;
+    NodeRec& pn = ts->nodes[L.node];
+    pn.feature = s.feature;
+    pn.gain = s.gain;
+    pn.left = left_node;
+    pn.right = right_node;
+    pn.is_cat = s.is_cat;
+    if (s.is_cat) {
+      pn.thr = -1;
+      pn.dleft = 0;
+      pn.mbin = -1;
+      for (int q = 0; q < 4; ++q) pn.bits[q] = s.bits[q];
+    } else {
+      pn.thr = s.bin;
+      pn.dleft = s.default_left;
+      pn.mbin = missing_bin[s.feature];
+    }
+    L.state = 2;
+    LeafRec& CL = ts->pool[L.child[0]];
+    LeafRec& CR = ts->pool[L.child[1]];
+    CL.node = left_node;
+    CR.node = right_node;
+    clear_node(ts->nodes[left_node], CL.value, CL.gcount);
+    clear_node(ts->nodes[right_node], CR.value, CR.gcount);
+    ts->slot_leaf[slot] = L.child[0];
+    ts->slot_leaf[nl0 + k] = L.child[1];
+  }
+  if (t == 0) {
+    H.n_nodes = nodes0 + 2 * n_commit;
+    H.n_leaves = nl;
+  }
+
+  MTB_CLK();
+  // ---- 5. next batch
+  if (s_stop) {
+    if (t == 0) {
+      H.done = 1;
+      Bt.n_items = 0;
+      Bt.root = 0;
+      Bt.n_tiles = 0;
+    }
+  } else {
+    int m = cp.num_leaves - nl;
+    if (m > cp.batch_cap) m = cp.batch_cap;
+    if (t < kMaxBatch) s_rank_slot[t] = -1;
     __syncthreads();
+    // rank of every splittable frontier leaf in pick order (one warp per
+    // leaf); the first m are kept
+    for (int i = w; i < nl; i += kCommitThreads / 32) {
+      const double g = s_g[i];
+      if (!(g > 0.0)) continue;  // warp-uniform
+      int ahead = 0;
+      for (int k = lane; k < nl; k += 32) {
+        const double gk = s_g[k];
+        ahead += (gk > 0.0 && pick_before(gk, k, g, i)) ? 1 : 0;
+      }
+      const int rank = __reduce_add_sync(0xffffffffu, ahead);
+      if (lane == 0 && rank < m) s_rank_slot[rank] = i;
+    }
+    __syncthreads();
+    if (w == 0) {
+      const int slot = s_rank_slot[lane];
+      const bool want = lane < m && slot >= 0 && !s_x[slot];
+      const unsigned ballot = __ballot_sync(0xffffffffu, want);
+      int n_new = __popc(ballot);
+      // never more leaf records or histogram slots than reserved
+      const int pool0 = H.n_pool, hist0 = H.n_hist;
+      int room = (kMaxPool - pool0) / 2;
+      if (cp.hist_slots - hist0 < room) room = cp.hist_slots - hist0;
+      if (n_new > room) n_new = room < 0 ? 0 : room;
+      const int idx = __popc(ballot & ((1u << lane) - 1u));
+      const bool take = want && idx < n_new;
+      long long tiles = 0;
+      if (take) {
+        const int leaf = s_leaf[slot];
+        LeafRec& L = ts->pool[leaf];
+        const SplitRec& s = L.split;
+        BatchItem& P = Bt.items[idx];
+        const long long n_left = s.n_left, n_right = L.gcount - s.n_left;
+        P.leaf = leaf;
+        P.child[0] = pool0 + 2 * idx;
+        P.child[1] = pool0 + 2 * idx + 1;
+        P.built_is_left = n_left <= n_right ? 1 : 0;
+        P.work = idx;
+        P.built_hist = hist0 + idx;
+        P.sib_hist = L.hist_slot;
+        P.feature = s.feature;
+        P.threshold = s.bin;
+        P.default_left = s.default_left;
+        P.missing_bin = s.is_cat ? -1 : missing_bin[s.feature];
+        P.is_cat = s.is_cat;
+        for (int q = 0; q < 4; ++q) P.bits[q] = s.bits[q];
+        P.src_buf = L.buf;
+        P.dst_buf = 1 - L.buf;
+        P.begin = L.begin;
+        P.count = L.count;
+        P.cursor_left = 0;
+        P.cursor_right = 0;
+        L.child[0] = P.child[0];
+        L.child[1] = P.child[1];
+        for (int side = 0; side < 2; ++side) {
+          LeafRec& C = ts->pool[P.child[side]];
+          C.node = -1;
+          C.buf = P.dst_buf;
+          C.hist_slot = (side == 0) == (P.built_is_left != 0) ? P.built_hist : P.sib_hist;
+          C.state = 0;
+          C.child[0] = C.child[1] = -1;
+          C.exp_buf = 0;
+          C.pad = 0;
+          C.begin = 0;
+          C.count = 0;
+          C.gcount = 0;
+          C.value = 0.0;
+          clear_split(C.split);
+        }
+        tiles = (L.count + cp.tile_rows - 1) / cp.tile_rows;
+      }
+      // exclusive prefix of tiles over the items (lane order = item order;
+      // lanes that are not items add 0)
+      long long incl = tiles;
+      for (int k = 1; k < 32; k <<= 1) {
+        long long o = __shfl_up_sync(0xffffffffu, incl, k);
+        if (lane >= k) incl += o;
+      }
+      if (take) Bt.items[idx].tile0 = incl - tiles;
+      const long long total = __shfl_sync(0xffffffffu, incl, 31);
+      if (lane == 0) {
+        if (n_new == 0) {
+          H.error = 1;  // reserved space exhausted (cannot happen within the bounds above)
+          H.done = 1;
+        }
+        Bt.n_items = n_new;
+        Bt.root = 0;
+        Bt.n_tiles = total;
+        H.n_pool = pool0 + 2 * n_new;
+        H.n_hist = hist0 + n_new;
+      }
+    }
+  }
+  __syncthreads();
+  MTB_CLK();
+#ifdef MTB_COMMIT_CLOCKS
+  if (t == 0)
+    printf("commit it=%d items=%d commits=%d nl=%d | %lld %lld %lld %lld %lld\n", H.iterations, n_items, n_commit, nl,
+           clk[1] - clk[0], clk[2] - clk[1], clk[3] - clk[2], clk[4] - clk[3], clk[5] - clk[4]);
+#endif
+#undef MTB_CLK
+  if (t == 0) {
+    H.iterations += 1;
+    if (host_done) {
+      // mapped host memory: the host learns without a copy in the stream
+      volatile int* hd = host_done;
+      hd[host_done_index] = H.done ? 1 : 0;
+      __threadfence_system();
+    }
   }
 }
 
-// Subtract + scan of every (child, active feature); the last block to finish
-// then folds the per-feature bests (block_finish) and picks the next leaf to
-// split (block_pick), so one split costs three launches: partition,
-// histogram, scan.
-__global__ void __launch_bounds__(kScanThreads) k_scan(TreeState* __restrict__ ts, int* __restrict__ hist,
-                                                           long long slot_cells, const int* __restrict__ feats,
-                                                           const int* __restrict__ missing_bin,
-                                                           const int* __restrict__ n_cats,
-                                                           const RoundScales* __restrict__ sc, ScanParams sp,
-                                                           FeatBest* __restrict__ out, int root, int work_slot,
-                                                           int num_leaves) {
-  __shared__ int s_last;
-  scan_body(ts, hist, slot_cells, feats, missing_bin, n_cats, sc, sp, out, root, work_slot);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    unsigned int total = gridDim.x * gridDim.y;
-    unsigned int ticket = atomicAdd(&ts->hdr.scan_ticket, 1u);
-    s_last = ticket == total - 1;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  block_finish(ts, out, feats, sc, sp, root);
-  __syncthreads();
-  block_pick(ts, missing_bin, num_leaves);
-  __syncthreads();
-  if (threadIdx.x == 0) ts->hdr.scan_ticket = 0;
-}
-
-// After the last split: leaves sorted by range start, for the raw update.
+// After the last iteration: frontier leaves sorted by range start, for the
+// raw update.
 __global__ void __launch_bounds__(1024) k_leaf_table(const TreeState* __restrict__ ts, long long* __restrict__ begins,
                                                      int* __restrict__ order) {
-  int nl = ts->hdr.n_leaves;
+  const int nl = ts->hdr.n_leaves;
   // Sort key: range start, then empty leaves before the non-empty one that
   // shares the start, then slot.  The raw update's search for the last start
   // <= position then always lands on the leaf that owns the position.
   for (int i = threadIdx.x; i < nl; i += blockDim.x) {
-    long long bi = ts->leaves[i].begin * 2 + (ts->leaves[i].count > 0 ? 1 : 0);
+    const LeafRec& Li = ts->pool[ts->slot_leaf[i]];
+    long long bi = Li.begin * 2 + (Li.count > 0 ? 1 : 0);
     int rank = 0;
     for (int k = 0; k < nl; ++k) {
-      long long bk = ts->leaves[k].begin * 2 + (ts->leaves[k].count > 0 ? 1 : 0);
+      const LeafRec& Lk = ts->pool[ts->slot_leaf[k]];
+      long long bk = Lk.begin * 2 + (Lk.count > 0 ? 1 : 0);
       if (bk < bi || (bk == bi && k < i)) ++rank;
     }
-    begins[rank] = ts->leaves[i].begin;
-    order[rank] = i;
+    begins[rank] = Li.begin;
+    order[rank] = ts->slot_leaf[i];
   }
 }
 
 // raw[row * K + k] = fma(lr, value(leaf of row), raw[row * K + k])
-// (boosting.mojo:1991-2111, explicit fused multiply-add).
+// (boosting.mojo:1991-2111, explicit fused multiply-add).  A leaf expanded
+// but never split still holds its rows in its own buffer.
 __global__ void k_update_raw(const TreeState* __restrict__ ts, const long long* __restrict__ begins,
                              const int* __restrict__ order, const int* __restrict__ rows0,
                              const int* __restrict__ rows1, double* __restrict__ raw, long long n, int K, int k,
@@ -1166,12 +1434,11 @@ __global__ void k_update_raw(const TreeState* __restrict__ ts, const long long* 
     if (begins[mid] <= i) lo = mid;
     else hi = mid - 1;
   }
-  const LeafRec* L = &ts->leaves[order[lo]];
+  const LeafRec* L = &ts->pool[order[lo]];
   const int* rows = L->buf ? rows1 : rows0;
   int r = rows[i];
-  double v = ts->nodes[L->node].value;
   double* p = raw + (long long)r * K + k;
-  *p = fma(lr, v, *p);
+  *p = fma(lr, L->value, *p);
 }
 
 }  // namespace

@@ -4,6 +4,7 @@
 // (_range_hist_atomic_kernel) over int8 gradient / hessian pairs.
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stddef.h>
 #include <string.h>
 
 #include <mutex>
@@ -33,26 +34,36 @@ long long quant_rows_per_flush(int quant_bins) {
   return std::min<long long>((1ll << 15) - 1, ((1ll << 16) - 1) / gl);
 }
 
-// Launches the histogram kernel for positions [0, n_sel) of rows/pairs into
-// `work` (zeroed here); `plan` is device memory for the job descriptor.
-void launch_leaf_hist(const uint8_t* d_bins_rm, int F, int Fp, int B, const int* d_rows, const uint16_t* d_pairs,
-                      long long n_sel, int quant_bins, Plan* d_plan, int* d_work, cudaStream_t st) {
-  Plan P;
-  memset(&P, 0, sizeof P);
-  P.active = 1;
+// Job descriptor of one histogram build over positions [0, n_sel) of
+// rows/pairs: a one-item batch whose built child is the whole selection.
+Batch one_item_batch(long long n_sel) {
+  Batch b;
+  memset(&b, 0, sizeof b);
+  b.n_items = 1;
+  b.root = 1;
+  BatchItem& P = b.items[0];
   P.built_is_left = 1;
-  P.begin = 0;
   P.count = n_sel;
   P.cursor_left = (unsigned long long)n_sel;
-  P.dst_buf = 0;
-  MTB_CUDA(cudaMemcpyAsync(d_plan, &P, sizeof P, cudaMemcpyHostToDevice, st));
+  return b;
+}
+
+// Bytes of the descriptor the kernel reads for a one-item batch.
+constexpr size_t kOneItemBatchBytes = offsetof(Batch, items) + sizeof(BatchItem);
+
+// Launches the histogram kernel for positions [0, n_sel) of rows/pairs into
+// `work` (zeroed here); `d_batch` is device memory for the job descriptor.
+void launch_leaf_hist(const uint8_t* d_bins_rm, int F, int Fp, int B, const int* d_rows, const uint16_t* d_pairs,
+                      long long n_sel, int quant_bins, Batch* d_batch, int* d_work, cudaStream_t st) {
+  Batch b = one_item_batch(n_sel);
+  MTB_CUDA(cudaMemcpyAsync(d_batch, &b, kOneItemBatchBytes, cudaMemcpyHostToDevice, st));
   const long long cells = (long long)F * 3 * B;
   MTB_CUDA(cudaMemsetAsync(d_work, 0, sizeof(int) * cells, st));
   int dev = 0, n_sm = 0;
   MTB_CUDA(cudaGetDevice(&dev));
   MTB_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
   HistLaunch hl = choose_hist_launch(MODE_QUANT, false, B, Fp, n_sm);
-  launch_hist<MODE_QUANT, false>(hl, st, d_plan, d_bins_rm, Fp, F, B, d_rows, d_rows, d_pairs, d_pairs, d_work,
+  launch_hist<MODE_QUANT, false>(hl, st, d_batch, d_bins_rm, Fp, F, B, d_rows, d_rows, d_pairs, d_pairs, d_work,
                                  cells, quant_rows_per_flush(quant_bins), 0);
   MTB_CUDA(cudaGetLastError());
 }
@@ -96,14 +107,14 @@ extern "C" int32_t mojotrees_b200_histogram_u8(const uint8_t* bins, int64_t n_ro
       for (int64_t r = 0; r < n_rows; ++r) rm[(size_t)r * Fp + f] = bins[f * n_rows + r];
     const size_t cells = (size_t)F * 3 * B;
     DevMem d_bins(rm.size()), d_rows(sizeof(int) * rsel.size()), d_pairs(sizeof(uint16_t) * pairs.size()),
-        d_plan(sizeof(Plan)), d_work(sizeof(int) * cells);
+        d_batch(kOneItemBatchBytes), d_work(sizeof(int) * cells);
     cudaStream_t st = 0;
     MTB_CUDA(cudaMemcpy(d_bins.p, rm.data(), rm.size(), cudaMemcpyHostToDevice));
     MTB_CUDA(cudaMemcpy(d_rows.p, rsel.data(), sizeof(int) * rsel.size(), cudaMemcpyHostToDevice));
     MTB_CUDA(cudaMemcpy(d_pairs.p, pairs.data(), sizeof(uint16_t) * pairs.size(), cudaMemcpyHostToDevice));
     if (n_sel > 0)
       launch_leaf_hist((const uint8_t*)d_bins.p, F, Fp, B, (const int*)d_rows.p, (const uint16_t*)d_pairs.p, n_sel,
-                       num_grad_quant_bins, (Plan*)d_plan.p, (int*)d_work.p, st);
+                       num_grad_quant_bins, (Batch*)d_batch.p, (int*)d_work.p, st);
     else
       MTB_CUDA(cudaMemset(d_work.p, 0, sizeof(int) * cells));
     MTB_CUDA(cudaMemcpy(out_hist, d_work.p, sizeof(int) * cells, cudaMemcpyDeviceToHost));
@@ -137,9 +148,9 @@ namespace {
 
 // Largest histogram the array holds: 128 features x 256 bins x (g, h, count).
 constexpr long long kNoAllocMaxCells = 128ll * 256 * 3;
-constexpr size_t kNoAllocPlanBytes = (sizeof(Plan) + 255) / 256 * 256;
+constexpr size_t kNoAllocBatchBytes = (kOneItemBatchBytes + 255) / 256 * 256;
 
-static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocPlanBytes + kNoAllocMaxCells * 4];
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBatchBytes + kNoAllocMaxCells * 4];
 
 struct NoAllocDevice {
   bool ready = false;
@@ -196,17 +207,12 @@ extern "C" int32_t mojotrees_b200_histogram_u8_noalloc(const uint8_t* bins_rm, i
       }
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    Plan* plan = reinterpret_cast<Plan*>(d->scratch);
-    int* work = reinterpret_cast<int*>(d->scratch + kNoAllocPlanBytes);
-    Plan P;
-    memset(&P, 0, sizeof P);
-    P.active = 1;
-    P.built_is_left = 1;
-    P.count = n_sel;
-    P.cursor_left = (unsigned long long)n_sel;
-    MTB_CUDA(cudaMemcpyAsync(plan, &P, sizeof P, cudaMemcpyHostToDevice, st));
+    Batch* batch = reinterpret_cast<Batch*>(d->scratch);
+    int* work = reinterpret_cast<int*>(d->scratch + kNoAllocBatchBytes);
+    Batch b = one_item_batch(n_sel);
+    MTB_CUDA(cudaMemcpyAsync(batch, &b, kOneItemBatchBytes, cudaMemcpyHostToDevice, st));
     MTB_CUDA(cudaMemsetAsync(work, 0, sizeof(int) * cells, st));  // the array keeps the last call's cells
-    launch_hist<MODE_QUANT, false>(d->hl, st, plan, bins_rm, Fp, F, B, rows, rows, pairs, pairs, work, cells,
+    launch_hist<MODE_QUANT, false>(d->hl, st, batch, bins_rm, Fp, F, B, rows, rows, pairs, pairs, work, cells,
                                    quant_rows_per_flush(num_grad_quant_bins), 0);
     MTB_CUDA(cudaGetLastError());
     MTB_CUDA(cudaMemcpyAsync(out_hist, work, sizeof(int) * cells, cudaMemcpyDeviceToDevice, st));

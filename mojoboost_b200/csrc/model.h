@@ -62,9 +62,12 @@ struct TrainStats {
   double partition_ms = 0.0;
   double scan_ms = 0.0;
   double grad_ms = 0.0;
+  double commit_ms = 0.0;
   double hist_rows = 0.0;           // rows read by histogram builds (built children + roots)
   double hist_bytes = 0.0;          // algorithmic bytes: hist_rows * (F + pair bytes)
-  int hist_launches = 0;
+  int hist_launches = 0;            // histogram launches (one per batch iteration)
+  int iterations = 0;               // batch iterations that did work, summed over trees
+  int expansions = 0;               // leaves whose children were computed, summed over trees
   int kernel_launches = 0;          // kernels this library launched
   int rounds = 0;
   std::vector<double> round_ms;     // device time of each round (CUDA events on the trainer's stream)

@@ -7,6 +7,7 @@
 // synchronisation until the round ends, where the tree's node table is read
 // back and the early-stop rule of boosting.mojo:2898-2907 is applied.
 #include <cuda_runtime.h>
+#include <stdio.h>
 #include <stdlib.h>
 
 #include <algorithm>
@@ -283,11 +284,19 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   DevBuf<TreeState> d_ts;
   d_ts.alloc(1);
   const long long slot_cells = (long long)F * 3 * B;
+  // Leaves expanded per iteration (speculative leaf batching); 1 grows one
+  // split per iteration as the reference does.  MOJOTREES_BATCH overrides.
+  int batch_cap = 16;
+  if (const char* e = getenv("MOJOTREES_BATCH")) batch_cap = atoi(e);
+  batch_cap = std::max(1, std::min(std::min(batch_cap, kMaxBatch), cfg.num_leaves - 1));
+  // Histogram slots: a tree uses at most 1 + (expansions) <= 2 * num_leaves
+  // leaf slots, then batch_cap work slots the builds land in first.
+  const int hist_slots = 2 * cfg.num_leaves;
+  const int work_base = hist_slots;
   DevBuf<int> d_hist;
-  d_hist.alloc((size_t)slot_cells * (cfg.num_leaves + 1));
-  const int work_slot = cfg.num_leaves;  // histogram builds land here first
+  d_hist.alloc((size_t)slot_cells * (hist_slots + batch_cap));
   DevBuf<FeatBest> d_fb;
-  d_fb.alloc((size_t)2 * F);
+  d_fb.alloc((size_t)2 * batch_cap * F);
   DevBuf<long long> d_begins;
   DevBuf<int> d_order;
   d_begins.alloc(kMaxLeaves);
@@ -309,22 +318,55 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   const int part_threads = 256;
   int part_items = 2;  // rows per thread per partition tile
   if (const char* e = getenv("MOJOTREES_PART_ITEMS")) part_items = atoi(e);
+  part_items = part_items <= 1 ? 1 : part_items == 2 ? 2 : part_items <= 4 ? 4 : 8;
   auto launch_partition = [&]() {
 #define MTB_PART(IT)                                                                                      \
   if (mode == MODE_QUANT)                                                                                 \
     k_partition<uint16_t, IT><<<part_grid, part_threads, 0, st>>>(                                        \
         d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<uint16_t*>(d_pairs0.p),            \
-        reinterpret_cast<uint16_t*>(d_pairs1.p), d_hist.p, slot_cells, work_slot);                        \
+        reinterpret_cast<uint16_t*>(d_pairs1.p), d_hist.p, slot_cells, work_base);                        \
   else                                                                                                    \
     k_partition<int2, IT><<<part_grid, part_threads, 0, st>>>(                                            \
         d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<int2*>(d_pairs0.p),                \
-        reinterpret_cast<int2*>(d_pairs1.p), d_hist.p, slot_cells, work_slot);
-    if (part_items <= 1) { MTB_PART(1) }
+        reinterpret_cast<int2*>(d_pairs1.p), d_hist.p, slot_cells, work_base);
+    if (part_items == 1) { MTB_PART(1) }
     else if (part_items == 2) { MTB_PART(2) }
-    else if (part_items <= 4) { MTB_PART(4) }
+    else if (part_items == 4) { MTB_PART(4) }
     else { MTB_PART(8) }
 #undef MTB_PART
   };
+  // MOJOTREES_TRACE=1 prints every tree iteration to stderr (with
+  // CUDA_LAUNCH_BLOCKING=1 the last line names the iteration that stalled)
+  const bool trace = getenv("MOJOTREES_TRACE") != nullptr;
+  CommitParams cp;
+  cp.num_leaves = cfg.num_leaves;
+  cp.batch_cap = batch_cap;
+  cp.hist_slots = hist_slots;
+  cp.tile_rows = 256 * part_items;
+  const size_t commit_smem = commit_smem_bytes(cfg.num_leaves);
+  MTB_CUDA(cudaFuncSetAttribute(k_commit, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)commit_smem));
+
+  // The host learns that a tree is done through mapped host memory written by
+  // the commit kernel; it stays at most kLookahead iterations ahead of the
+  // device, so at most that many no-op iterations run after the last one.
+  constexpr int kRing = 64, kLookahead = 2;
+  int* h_done = nullptr;
+  int* d_done = nullptr;
+  MTB_CUDA(cudaHostAlloc(&h_done, sizeof(int) * kRing, cudaHostAllocMapped));
+  struct HostGuard {
+    int* p;
+    ~HostGuard() { cudaFreeHost(p); }
+  } hg{h_done};
+  MTB_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&d_done), h_done, 0));
+  std::vector<cudaEvent_t> iter_ev(kRing, nullptr);
+  struct IterEventGuard {
+    std::vector<cudaEvent_t>& e;
+    ~IterEventGuard() {
+      for (auto x : e)
+        if (x) cudaEventDestroy(x);
+    }
+  } ieg{iter_ev};
+  for (auto& e : iter_ev) MTB_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
 
   model.objective = cfg.objective;
   model.num_class = K;
@@ -357,32 +399,24 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   auto hist = [&]() {
     timer.begin(&stats.hist_ms);
     if (mode == MODE_QUANT)
-      launch_hist<MODE_QUANT, false>(hl, st, plan_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
-                                     d_pairs1.p, d_hist.p, slot_cells, rows_per_flush, work_slot);
+      launch_hist<MODE_QUANT, false>(hl, st, batch_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
+                                     d_pairs1.p, d_hist.p, slot_cells, rows_per_flush, work_base);
     else if (const_h)
-      launch_hist<MODE_FIXED, true>(hl, st, plan_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
-                                    d_pairs1.p, d_hist.p, slot_cells, rows_per_flush, work_slot);
+      launch_hist<MODE_FIXED, true>(hl, st, batch_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
+                                    d_pairs1.p, d_hist.p, slot_cells, rows_per_flush, work_base);
     else
-      launch_hist<MODE_FIXED, false>(hl, st, plan_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
-                                     d_pairs1.p, d_hist.p, slot_cells, rows_per_flush, work_slot);
+      launch_hist<MODE_FIXED, false>(hl, st, batch_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
+                                     d_pairs1.p, d_hist.p, slot_cells, rows_per_flush, work_base);
     timer.end();
   };
-  // the built child's cells summed over every device's rows (exact int32)
+  // the built children's cells summed over every device's rows (exact int32)
   auto reduce_work = [&]() {
-    if (coll) coll->allreduce_sum_i32(d_hist.p + (size_t)work_slot * slot_cells, (size_t)slot_cells, st);
+    if (coll)
+      coll->allreduce_sum_i32(d_hist.p + (size_t)work_base * slot_cells, (size_t)slot_cells * batch_cap, st);
   };
 
   const long long grid1024 = (N + 1023) / 1024;
   const unsigned grid256 = (unsigned)((N + 255) / 256);
-  const bool use_graph = !cfg.profile_phases;
-  std::vector<cudaGraphExec_t> graphs(K, nullptr);
-  struct GraphGuard {
-    std::vector<cudaGraphExec_t>& g;
-    ~GraphGuard() {
-      for (auto x : g)
-        if (x) cudaGraphExecDestroy(x);
-    }
-  } gg{graphs};
   std::vector<cudaEvent_t> round_ev;
   struct EventGuard {
     std::vector<cudaEvent_t>& e;
@@ -492,59 +526,52 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       const int n_active = (int)feats.size();
       MTB_CUDA(cudaMemcpyAsync(d_feats.p, feats.data(), sizeof(int) * n_active, cudaMemcpyHostToDevice, st));
       sp.n_active = n_active;
-      const dim3 scan_grid(2, (unsigned)n_active);
+      const unsigned scan_grid = (unsigned)((2ll * batch_cap * n_active + kScanWarps - 1) / kScanWarps);
 
-      // ---- grow the tree: a fixed launch sequence, replayed as a CUDA graph
-      // (one per class and feature count) unless per-phase timing is requested
-      auto grow = [&]() {
-        MTB_CUDA(cudaMemsetAsync(d_hist.p + (size_t)work_slot * slot_cells, 0, sizeof(int) * slot_cells, st));
-        k_tree_init<<<1, 32, 0, st>>>(d_ts.p, N);
+      // ---- grow the tree: iterations of partition -> histogram -> scan ->
+      // commit, each expanding up to batch_cap leaves, until the commit
+      // kernel reports the tree done
+      k_tree_init<<<1, 32, 0, st>>>(d_ts.p, N);
+      launches++;
+      int launched = 0;
+      for (int i = 0;; ++i) {
+        if (i >= kLookahead) {
+          const int q = (i - kLookahead) % kRing;
+          MTB_CUDA(cudaEventSynchronize(iter_ev[q]));
+          if (reinterpret_cast<volatile int*>(h_done)[q]) break;
+        }
+        if (i > cfg.num_leaves) break;  // bound: every iteration after the root commits a split
+        if (trace) fprintf(stderr, "mojotrees trace: tree %zu iteration %d\n", model.trees.size(), i);
+        timer.begin(&stats.partition_ms);
+        launch_partition();
+        timer.end();
         hist();
         reduce_work();
         timer.begin(&stats.scan_ms);
-        k_scan<<<scan_grid, kScanThreads, 0, st>>>(d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p,
-                                                      d_ncats.p, d_sc.p, sp, d_fb.p, 1, work_slot, cfg.num_leaves);
+        k_scan<<<scan_grid, kScanWarps * 32, 0, st>>>(d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p, d_ncats.p,
+                                                    d_sc.p, sp, d_fb.p, work_base);
         timer.end();
-        for (int s = 1; s < cfg.num_leaves; ++s) {
-          timer.begin(&stats.partition_ms);
-          launch_partition();
-          timer.end();
-          hist();
-          reduce_work();
-          timer.begin(&stats.scan_ms);
-          k_scan<<<scan_grid, kScanThreads, 0, st>>>(d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p,
-                                                        d_ncats.p, d_sc.p, sp, d_fb.p, 0, work_slot, cfg.num_leaves);
-          timer.end();
-        }
-        k_leaf_table<<<1, 1024, 0, st>>>(d_ts.p, d_begins.p, d_order.p);
-        k_update_raw<<<grid256, 256, 0, st>>>(d_ts.p, d_begins.p, d_order.p, d_rows0.p, d_rows1.p, d_raw.p, N, K,
-                                              k, cfg.learning_rate);
-      };
-      const int tree_launches = 3 + 3 * (cfg.num_leaves - 1) + 2;
-      // the scan grid depends on the active feature count, fixed per fit
-      // unless feature_fraction draws a different count (then no graph)
-      const bool graph_ok = use_graph && (cfg.feature_fraction >= 1.0);
-      if (graph_ok) {
-        if (!graphs[k]) {
-          cudaGraph_t g;
-          MTB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-          grow();
-          MTB_CUDA(cudaStreamEndCapture(st, &g));
-          cudaError_t ie = cudaGraphInstantiate(&graphs[k], g, 0);
-          cudaGraphDestroy(g);
-          MTB_CUDA(ie);
-        }
-        MTB_CUDA(cudaGraphLaunch(graphs[k], st));
-      } else {
-        grow();
+        timer.begin(&stats.commit_ms);
+        k_commit<<<1, kCommitThreads, commit_smem, st>>>(d_ts.p, d_fb.p, d_feats.p, d_missing.p, d_sc.p, sp, cp, d_done,
+                                              i % kRing);
+        timer.end();
+        MTB_CUDA(cudaEventRecord(iter_ev[i % kRing], st));
+        launches += 4;
+        launched++;
       }
-      launches += tree_launches;
+      stats.hist_launches += launched;
+      k_leaf_table<<<1, 1024, 0, st>>>(d_ts.p, d_begins.p, d_order.p);
+      k_update_raw<<<grid256, 256, 0, st>>>(d_ts.p, d_begins.p, d_order.p, d_rows0.p, d_rows1.p, d_raw.p, N, K, k,
+                                            cfg.learning_rate);
+      launches += 2;
       MTB_CUDA(cudaGetLastError());
       MTB_CUDA(cudaMemcpyAsync(&hdr, &d_ts.p->hdr, sizeof(TreeHeader), cudaMemcpyDeviceToHost, st));
       MTB_CUDA(cudaMemcpyAsync(nodes_host.data(), d_ts.p->nodes, sizeof(HostNode) * M, cudaMemcpyDeviceToHost, st));
       MTB_CUDA(cudaStreamSynchronize(st));
       timer.collect();
-      if (hdr.error) throw std::runtime_error("device trainer reported an internal error");
+      if (hdr.error || !hdr.done) throw std::runtime_error("device trainer reported an internal error");
+      stats.iterations += hdr.iterations;
+      stats.expansions += (hdr.n_pool - 1) / 2;
       if (coll) coll->check();
       std::vector<HostNode> tree(nodes_host.begin(), nodes_host.begin() + hdr.n_nodes);
       bool trivial = hdr.n_leaves == 1 && std::fabs(tree[0].value) < 1e-12;
@@ -567,7 +594,6 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   }
   stats.fit_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t_fit).count();
   stats.kernel_launches += launches;
-  stats.hist_launches = (int)(model.trees.size() * (size_t)cfg.num_leaves);
   // rows read by histogram builds: every root plus the smaller child of every split
   for (size_t t = 0; t < model.trees.size(); ++t) {
     const auto& tr = model.trees[t];
