@@ -462,14 +462,26 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
 // with int32 global atomics into each item's work slot.
 // ---------------------------------------------------------------------------
 
-// Shared-memory cells (32-bit atomics only; one CTA owns FG features):
-//   QUANT           plane 0: g * 2^15 + count (signed, exact while a flush
-//                   covers < 32768 rows and |sum g| < 2^16), plane 1: h
-//   FIXED, const h  plane 0: g, plane 1: count
-//   FIXED           plane 0: g, plane 1: h, plane 2: count
+// Shared-memory cells use 32-bit atomics only; one CTA owns FG features.
 // Global cells are int32 [slot][F][3][B] (g, h, count): every sum is bounded
 // by 2^30 + n (FIXED, quantized_gradient.mojo:98-99) or by B * n (QUANT).
 constexpr int kQuantCountBits = 15;
+
+// Shared-memory cell layouts of the histogram kernel.
+//   HL_QUANT     plane 0: g * 2^15 + count (exact while a flush covers
+//                < 32768 rows and |sum g| < 2^16), plane 1: h
+//   HL_QUANT16   plane A: (g + g_lim) | count << 16 per cell; plane B (half
+//                size): h of features 2k (low half) and 2k+1 (high half).
+//                Every field is a 16-bit unsigned sum, exact while a flush
+//                covers at most 65535 / max(2 g_lim, h_lim) rows; 6 bytes a
+//                cell, so twice the features of HL_QUANT fit one CTA.
+//   HL_FIXED_CH  plane 0: g, plane 1: count (hessian constant)
+//   HL_FIXED     planes g, h, count
+enum HistLayout : int { HL_QUANT = 0, HL_QUANT16 = 1, HL_FIXED_CH = 2, HL_FIXED = 3 };
+
+__host__ __device__ constexpr int hist_layout_words(int layout, int cells) {
+  return layout == HL_QUANT16 ? cells + cells / 2 : layout == HL_FIXED ? 3 * cells : 2 * cells;
+}
 
 __device__ __forceinline__ void built_range(const BatchItem& P, long long& b, long long& cnt) {
   long long nl = (long long)P.cursor_left;
@@ -519,17 +531,25 @@ struct BinWord<4> {
 #endif
 constexpr int kHistUnroll = MTB_HIST_UNROLL;  // bin loads in flight per warp (divides 32)
 constexpr int kHistThreads = 1024;
+constexpr int kHistBinsPad = 256;  // bins per feature in the shared-memory layout
+
+// Atomic add to a shared-memory word whose result is not needed.
+__device__ __forceinline__ void shared_red_add(uint32_t addr, unsigned int v) {
+  asm volatile("red.shared.add.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
 
 // One cluster accumulates rows [seg_b, seg_b + seg_n) of one item's built
 // child into the item's work slot.
-template <int NPL, int MODE, bool CONST_H>
+template <int NPL, int LAYOUT>
 __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const BatchItem& P, long long seg_b,
                              long long seg_n, const uint8_t* __restrict__ bins_rm, int Fp, int F, int B,
                              const int* __restrict__ rows0, const int* __restrict__ rows1,
                              const void* __restrict__ pairs0, const void* __restrict__ pairs1, int* hs,
-                             long long rows_per_flush, unsigned int* p0) {
+                             long long rows_per_flush, int g_lim, unsigned int* p0) {
+  static_assert(LAYOUT != HL_QUANT16 || NPL % 2 == 0, "packed cells pair features");
   constexpr int FG = 32 * NPL;
-  constexpr int NPLANE = (MODE == MODE_FIXED && !CONST_H) ? 3 : 2;
+  constexpr int MODE = (LAYOUT == HL_QUANT || LAYOUT == HL_QUANT16) ? MODE_QUANT : MODE_FIXED;
+  constexpr bool CONST_H = LAYOUT == HL_FIXED_CH;
   constexpr int U = kHistUnroll;
   const int cs = (int)cluster.num_blocks();
   const int crank = (int)cluster.block_rank();
@@ -539,25 +559,47 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
   if (e > seg_b + seg_n) e = seg_b + seg_n;
   const long long n_pass = (sub + rows_per_flush - 1) / rows_per_flush;
   const int f0 = blockIdx.x * FG;
-  const int cells = NPL * B * 32;  // words per plane
-  unsigned int* p1 = p0 + cells;
-  unsigned int* p2 = p1 + cells;
+  // cells are laid out for 256 bins whatever B is, so every plane and
+  // feature offset below is a compile-time constant
+  constexpr int cells = NPL * kHistBinsPad * 32;  // words per full plane
+  constexpr int words = hist_layout_words(LAYOUT, cells);
   const int* rows = P.dst_buf ? rows1 : rows0;
   const void* pairs = P.dst_buf ? pairs1 : pairs0;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int n_warps = blockDim.x >> 5;
-  // lanes past the padded row width load nothing (NPL divides 16, so a lane
-  // that starts inside the row ends inside it)
+  // A lane past the padded row width reads the row's first bytes instead (a
+  // valid address) and accumulates them into cells of features >= Fp, which
+  // the merge never reads; so the row loop needs no per-lane test.
   const bool lane_ok = f0 + lane * NPL < Fp;
-  const uint8_t* bcol = bins_rm + f0 + lane * NPL;
+  const uint8_t* bcol = bins_rm + (lane_ok ? f0 + lane * NPL : 0);
   const int slice = (cells + cs - 1) / cs;
   const int m0 = crank * slice;
   const int m1 = m0 + slice < cells ? m0 + slice : cells;
+  // Shared-memory byte address of this lane's cell (feature 0, bin 0) of
+  // plane A; cell (j, bin) of a plane is that plus a constant plus bin * 128
+  // (32 lanes x 4 bytes).
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(p0) + 4u * lane;
+  constexpr uint32_t kFeat = 128u * kHistBinsPad;  // bytes between features of a plane
+  // one row of this lane's features: NPL cells in each plane
+  auto add_row = [&](unsigned int bw, unsigned int x0, unsigned int x1) {
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+      const uint32_t a = sbase + (((bw >> (8 * j)) & 0xffu) << 7);
+      shared_red_add(a + j * kFeat, x0);
+      if (LAYOUT == HL_QUANT16) {
+        // plane B: features 2k and 2k+1 share a word (low and high half)
+        shared_red_add(a + 4u * cells + (j >> 1) * kFeat, (j & 1) ? x1 << 16 : x1);
+      } else {
+        shared_red_add(a + 4u * cells + j * kFeat, x1);
+        if (LAYOUT == HL_FIXED) shared_red_add(a + 8u * cells + j * kFeat, 1u);
+      }
+    }
+  };
   for (long long pass = 0; pass < n_pass; ++pass) {
     const long long ps = s + pass * rows_per_flush;
     const long long pe = ps + rows_per_flush < e ? ps + rows_per_flush : e;
-    for (int c = threadIdx.x; c < cells * NPLANE; c += blockDim.x) p0[c] = 0u;
+    for (int c = threadIdx.x; c < words; c += blockDim.x) p0[c] = 0u;
     __syncthreads();
     // Each warp takes chunks of 32 consecutive positions: lane k loads the
     // row id and gradient pair of position k (coalesced; the next chunk's are
@@ -565,11 +607,11 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
     // U bin loads in flight before their atomics.
     const long long stride = (long long)n_warps * 32;
     long long c0 = ps + (long long)warp * 32;
-    int nr = -1;
+    int nr = 0;
     unsigned int na0 = 0u, na1 = 0u;
     auto fetch = [&](long long base, int& r, unsigned int& x0, unsigned int& x1) {
       const long long i = base + lane;
-      r = -1;
+      r = 0;
       x0 = 0u;
       x1 = 0u;
       if (i < pe) {
@@ -577,7 +619,8 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
         if (MODE == MODE_QUANT) {
           uint16_t pr = __ldg(reinterpret_cast<const uint16_t*>(pairs) + i);
           int g = (int)(int8_t)(pr & 0xff);
-          x0 = (unsigned int)(g * (1 << kQuantCountBits) + 1);
+          x0 = LAYOUT == HL_QUANT16 ? (unsigned int)(g + g_lim) | (1u << 16)
+                                    : (unsigned int)(g * (1 << kQuantCountBits) + 1);
           x1 = (unsigned int)(pr >> 8);
         } else {
           int2 pr = __ldg(reinterpret_cast<const int2*>(pairs) + i);
@@ -591,26 +634,31 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
       const int cr = nr;
       const unsigned int ca0 = na0, ca1 = na1;
       if (c0 + stride < pe) fetch(c0 + stride, nr, na0, na1);
-      const int n_in = pe - c0 < 32 ? (int)(pe - c0) : 32;
-      for (int u0 = 0; u0 < n_in; u0 += U) {
-        unsigned int bw[U];
+      if (pe - c0 >= 32) {
+        // full chunk: no bounds tests
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int r = __shfl_sync(0xffffffffu, cr, u0 + u);
-          bw[u] = (u0 + u < n_in && lane_ok) ? BinWord<NPL>::load(bcol + (long long)r * Fp) : 0u;
-        }
+        for (int u0 = 0; u0 < 32; u0 += U) {
+          unsigned int bw[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const unsigned int x0 = __shfl_sync(0xffffffffu, ca0, u0 + u);
-          const unsigned int x1 = __shfl_sync(0xffffffffu, ca1, u0 + u);
-          if (!(u0 + u < n_in && lane_ok)) continue;
-#pragma unroll
-          for (int j = 0; j < NPL; ++j) {
-            const int cell = lane_cell<NPL>(j, (int)((bw[u] >> (8 * j)) & 0xffu), B, lane);
-            atomicAdd(&p0[cell], x0);
-            atomicAdd(&p1[cell], x1);
-            if (NPLANE == 3) atomicAdd(&p2[cell], 1u);
+          for (int u = 0; u < U; ++u) {
+            const int r = __shfl_sync(0xffffffffu, cr, u0 + u);
+            bw[u] = BinWord<NPL>::load(bcol + (size_t)(unsigned int)r * (unsigned int)Fp);
           }
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const unsigned int x0 = __shfl_sync(0xffffffffu, ca0, u0 + u);
+            const unsigned int x1 =
+                (MODE == MODE_FIXED && CONST_H) ? 1u : __shfl_sync(0xffffffffu, ca1, u0 + u);
+            add_row(bw[u], x0, x1);
+          }
+        }
+      } else {
+        const int n_in = (int)(pe - c0);
+        for (int u = 0; u < n_in; ++u) {
+          const int r = __shfl_sync(0xffffffffu, cr, u);
+          const unsigned int x0 = __shfl_sync(0xffffffffu, ca0, u);
+          const unsigned int x1 = __shfl_sync(0xffffffffu, ca1, u);
+          add_row(BinWord<NPL>::load(bcol + (size_t)(unsigned int)r * (unsigned int)Fp), x0, x1);
         }
       }
     }
@@ -618,15 +666,20 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
     for (int c = m0 + threadIdx.x; c < m1; c += blockDim.x) {
       const int l = c & 31;
       const int jb = c >> 5;
-      const int j = jb / B;
-      const int bin = jb - j * B;
+      const int j = jb / kHistBinsPad;
+      const int bin = jb % kHistBinsPad;
       const int f = f0 + l * NPL + j;
-      if (f >= F) continue;
+      if (f >= F || bin >= B) continue;
       int g = 0, h = 0, cnt = 0;
       for (int rk = 0; rk < cs; ++rk) {
         const unsigned int* q0 = cluster.map_shared_rank(p0, rk);
         const unsigned int* q1 = q0 + cells;
-        if (MODE == MODE_QUANT) {
+        if (LAYOUT == HL_QUANT16) {
+          const unsigned int x = q0[c];
+          cnt += (int)(x >> 16);
+          g += (int)(x & 0xffffu);
+          h += (int)((q1[(((j >> 1) * kHistBinsPad + bin) << 5) + l] >> (16 * (j & 1))) & 0xffffu);
+        } else if (LAYOUT == HL_QUANT) {
           unsigned int x = q0[c];
           cnt += (int)(x & ((1u << kQuantCountBits) - 1u));
           g += (int)x >> kQuantCountBits;
@@ -641,6 +694,7 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
         }
       }
       if (cnt == 0) continue;
+      if (LAYOUT == HL_QUANT16) g -= g_lim * cnt;  // sum of (g + g_lim) -> sum of g
       int* cellp = hs + (f * 3) * B + bin;
       atomicAdd(cellp, g);
       if (!(MODE == MODE_FIXED && CONST_H)) atomicAdd(cellp + B, h);
@@ -654,13 +708,13 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
 // built rows, taken as one sequence (item after item), are split evenly among
 // ceil(rows / (min_rows_per_cta * CS)) clusters at most; a cluster whose share
 // spans several items accumulates one segment per item.
-template <int NPL, int MODE, bool CONST_H>
+template <int NPL, int LAYOUT>
 __global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__ batch, const uint8_t* __restrict__ bins_rm,
                                                int Fp, int F, int B, const int* __restrict__ rows0,
                                                const int* __restrict__ rows1, const void* __restrict__ pairs0,
                                                const void* __restrict__ pairs1, int* __restrict__ hist,
-                                               long long slot_cells, long long rows_per_flush, int work_base,
-                                               int min_rows_per_cta) {
+                                               long long slot_cells, long long rows_per_flush, int g_lim,
+                                               int work_base, int min_rows_per_cta) {
   namespace cg = cooperative_groups;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   unsigned int* p0 = reinterpret_cast<unsigned int*>(smem_raw);
@@ -690,9 +744,9 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__
     const long long s0 = lo > acc ? lo : acc;
     const long long s1 = hi < acc + c ? hi : acc + c;
     if (s1 > s0)
-      hist_segment<NPL, MODE, CONST_H>(cluster, P, b + (s0 - acc), s1 - s0, bins_rm, Fp, F, B, rows0, rows1, pairs0,
-                                       pairs1, hist + (long long)(work_base + P.work) * slot_cells, rows_per_flush,
-                                       p0);
+      hist_segment<NPL, LAYOUT>(cluster, P, b + (s0 - acc), s1 - s0, bins_rm, Fp, F, B, rows0, rows1, pairs0,
+                                pairs1, hist + (long long)(work_base + P.work) * slot_cells, rows_per_flush, g_lim,
+                                p0);
     acc += c;
   }
 }

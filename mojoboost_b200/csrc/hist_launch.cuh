@@ -31,13 +31,16 @@ inline const Batch* batch_of(const TreeState* ts) {
 }
 
 struct HistLaunch {
-  int cluster = 1;  // CTAs per thread-block cluster along grid y
-  int min_rows_per_cta = 512;  // a leaf uses ceil(rows / this) CTAs at most
-  int npl = 1;  // features per lane (feature group = 32 * npl)
+  int layout = HL_QUANT;       // shared-memory cell layout (HistLayout)
+  int cluster = 1;             // CTAs per thread-block cluster along grid y
+  int min_rows_per_cta = 512;  // a batch uses ceil(rows / this) CTAs at most
+  int npl = 1;                 // features per lane (feature group = 32 * npl)
   int groups = 1;
   int threads = 512;
   int row_ctas = 1;
   size_t smem = 0;
+  long long rows_per_flush = 1ll << 40;
+  int g_lim = 0;               // HL_QUANT16: offset making g non-negative
 };
 
 cudaLaunchConfig_t hist_config(const HistLaunch& hl, int cs, int row_ctas, cudaStream_t st, cudaLaunchAttribute* attr) {
@@ -55,9 +58,9 @@ cudaLaunchConfig_t hist_config(const HistLaunch& hl, int cs, int row_ctas, cudaS
   return lc;
 }
 
-template <int NPL, int MODE, bool CH>
+template <int NPL, int L>
 cudaError_t prepare_hist_t(const HistLaunch& hl, int cs, int* n_clusters) {
-  auto k = k_hist<NPL, MODE, CH>;
+  auto k = k_hist<NPL, L>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
@@ -65,63 +68,91 @@ cudaError_t prepare_hist_t(const HistLaunch& hl, int cs, int* n_clusters) {
   return cudaOccupancyMaxActiveClusters(n_clusters, k, &lc);
 }
 
-template <int NPL, int MODE, bool CH>
+template <int NPL, int L>
 void launch_hist_t(const HistLaunch& hl, cudaStream_t st, const Batch* batch, const uint8_t* bins_rm, int Fp, int F,
                    int B, const int* r0, const int* r1, const void* p0, const void* p1, int* hist,
-                   long long slot_cells, long long rpf, int ws) {
+                   long long slot_cells, int ws) {
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t lc = hist_config(hl, hl.cluster, hl.row_ctas, st, attr);
-  MTB_CUDA(cudaLaunchKernelEx(&lc, k_hist<NPL, MODE, CH>, batch, bins_rm, Fp, F, B, r0, r1, p0, p1, hist, slot_cells,
-                              rpf, ws, hl.min_rows_per_cta));
+  MTB_CUDA(cudaLaunchKernelEx(&lc, k_hist<NPL, L>, batch, bins_rm, Fp, F, B, r0, r1, p0, p1, hist, slot_cells,
+                              hl.rows_per_flush, hl.g_lim, ws, hl.min_rows_per_cta));
 }
 
-#define MTB_NPL_SWITCH(EXPR)                                                                  \
-  switch (hl.npl) {                                                                            \
-    case 1: { constexpr int V = 1; EXPR; } break;                                              \
-    case 2: { constexpr int V = 2; EXPR; } break;                                              \
-    case 4: { constexpr int V = 4; EXPR; } break;                                              \
-    default: throw std::runtime_error("bad histogram features per lane");                      \
+// Every (layout, features per lane) instance the launch geometry can pick.
+#define MTB_HIST_SWITCH(EXPR)                                                                         \
+  switch (hl.layout * 8 + hl.npl) {                                                                    \
+    case HL_QUANT * 8 + 1: { constexpr int V = 1, L = HL_QUANT; EXPR; } break;                        \
+    case HL_QUANT * 8 + 2: { constexpr int V = 2, L = HL_QUANT; EXPR; } break;                        \
+    case HL_QUANT * 8 + 4: { constexpr int V = 4, L = HL_QUANT; EXPR; } break;                        \
+    case HL_QUANT16 * 8 + 2: { constexpr int V = 2, L = HL_QUANT16; EXPR; } break;                    \
+    case HL_QUANT16 * 8 + 4: { constexpr int V = 4, L = HL_QUANT16; EXPR; } break;                    \
+    case HL_FIXED_CH * 8 + 1: { constexpr int V = 1, L = HL_FIXED_CH; EXPR; } break;                  \
+    case HL_FIXED_CH * 8 + 2: { constexpr int V = 2, L = HL_FIXED_CH; EXPR; } break;                  \
+    case HL_FIXED_CH * 8 + 4: { constexpr int V = 4, L = HL_FIXED_CH; EXPR; } break;                  \
+    case HL_FIXED * 8 + 1: { constexpr int V = 1, L = HL_FIXED; EXPR; } break;                        \
+    case HL_FIXED * 8 + 2: { constexpr int V = 2, L = HL_FIXED; EXPR; } break;                        \
+    case HL_FIXED * 8 + 4: { constexpr int V = 4, L = HL_FIXED; EXPR; } break;                        \
+    default: throw std::runtime_error("bad histogram layout");                                         \
   }
 
-template <int MODE, bool CH>
-cudaError_t prepare_hist(const HistLaunch& hl, int cs, int* n_clusters) {
+inline cudaError_t prepare_hist(const HistLaunch& hl, int cs, int* n_clusters) {
   cudaError_t e = cudaErrorInvalidValue;
-  MTB_NPL_SWITCH(e = (prepare_hist_t<V, MODE, CH>(hl, cs, n_clusters)))
+  MTB_HIST_SWITCH(e = (prepare_hist_t<V, L>(hl, cs, n_clusters)))
   return e;
 }
 
-template <int MODE, bool CH>
-void launch_hist(const HistLaunch& hl, cudaStream_t st, const Batch* batch, const uint8_t* bins_rm, int Fp, int F,
-                 int B, const int* r0, const int* r1, const void* p0, const void* p1, int* hist, long long slot_cells,
-                 long long rpf, int ws) {
-  MTB_NPL_SWITCH((launch_hist_t<V, MODE, CH>(hl, st, batch, bins_rm, Fp, F, B, r0, r1, p0, p1, hist, slot_cells, rpf, ws)))
+inline void launch_hist(const HistLaunch& hl, cudaStream_t st, const Batch* batch, const uint8_t* bins_rm, int Fp,
+                        int F, int B, const int* r0, const int* r1, const void* p0, const void* p1, int* hist,
+                        long long slot_cells, int ws) {
+  MTB_HIST_SWITCH((launch_hist_t<V, L>(hl, st, batch, bins_rm, Fp, F, B, r0, r1, p0, p1, hist, slot_cells, ws)))
 }
 
+// Cell layout and flush span for a fit.  quant_bins: the int8 gradient range
+// (|g| <= quant_bins / 2, h <= quant_bins); 0 for the fixed-point modes.
+inline void choose_hist_layout(HistLaunch& hl, int mode, bool const_h, int quant_bins) {
+  if (mode == MODE_QUANT) {
+    const long long gl = quant_bins / 2, hlim = quant_bins;
+    const long long rpf16 = std::min<long long>(65535 / (2 * gl), 65535 / hlim);
+    if (rpf16 >= 2048 && !getenv("MOJOTREES_HIST_NO_PACK")) {
+      hl.layout = HL_QUANT16;
+      hl.rows_per_flush = rpf16;
+      hl.g_lim = (int)gl;
+    } else {
+      // plane 0 holds g * 2^15 + count: count < 2^15 and |sum g| < 2^16 per flush
+      hl.layout = HL_QUANT;
+      hl.rows_per_flush = std::min<long long>((1ll << 15) - 1, ((1ll << 16) - 1) / gl);
+    }
+  } else {
+    hl.layout = const_h ? HL_FIXED_CH : HL_FIXED;
+    hl.rows_per_flush = 1ll << 40;
+  }
+}
 
 // Features per lane: the fewest feature groups (each group re-reads the
 // rows) whose cells fit the shared-memory budget, then the smallest such
 // group.  Row chunks are sized to fill every SM; CTAs of a feature group form
 // clusters of up to 8 that merge through DSMEM.
-inline HistLaunch choose_hist_launch(int mode, bool const_h, int B, int Fp, int n_sm) {
+inline HistLaunch choose_hist_launch(int mode, bool const_h, int quant_bins, int B, int Fp, int n_sm) {
   HistLaunch hl;
-  size_t cell_bytes = (mode == MODE_QUANT || const_h) ? 8 : 12;  // two or three 32-bit planes
+  choose_hist_layout(hl, mode, const_h, quant_bins);
   // MOJOTREES_HIST_SMEM_KB / MOJOTREES_HIST_CLUSTER override the shared-memory
   // budget per CTA and the largest cluster size (tuning knobs)
   size_t budget = 220 * 1024;
   if (const char* e = getenv("MOJOTREES_HIST_SMEM_KB")) budget = (size_t)atoi(e) * 1024;
   int max_cs = 8;
   if (const char* e = getenv("MOJOTREES_HIST_CLUSTER")) max_cs = atoi(e);
-  hl.npl = 1;
-  hl.groups = (Fp + 31) / 32;
-  for (int npl : {2, 4}) {
-    size_t smem = (size_t)32 * npl * B * cell_bytes;
+  auto smem_of = [&](int npl) { return (size_t)4 * hist_layout_words(hl.layout, 32 * npl * kHistBinsPad); };
+  hl.npl = 0;
+  hl.groups = 1 << 30;
+  for (int npl : {1, 2, 4}) {
+    if (hl.layout == HL_QUANT16 && npl == 1) continue;
     int groups = (Fp + 32 * npl - 1) / (32 * npl);
-    if (smem <= budget && groups < hl.groups) {
+    if ((smem_of(npl) <= budget || hl.npl == 0) && groups < hl.groups) {
       hl.npl = npl;
       hl.groups = groups;
     }
   }
-  hl.smem = (size_t)32 * hl.npl * B * cell_bytes;
+  hl.smem = smem_of(hl.npl);
   int per_sm = std::max(1, (int)((228 * 1024) / (hl.smem + 1024)));
   hl.threads = kHistThreads;
   per_sm = std::min(per_sm, 2048 / hl.threads);
@@ -138,10 +169,7 @@ inline HistLaunch choose_hist_launch(int mode, bool const_h, int B, int Fp, int 
     int n_clusters = 0;
     HistLaunch probe = hl;
     probe.row_ctas = cs;
-    cudaError_t oe;
-    if (mode == MODE_QUANT) oe = prepare_hist<MODE_QUANT, false>(probe, cs, &n_clusters);
-    else if (const_h) oe = prepare_hist<MODE_FIXED, true>(probe, cs, &n_clusters);
-    else oe = prepare_hist<MODE_FIXED, false>(probe, cs, &n_clusters);
+    cudaError_t oe = prepare_hist(probe, cs, &n_clusters);
     if (oe != cudaSuccess) {
       cudaGetLastError();
       continue;

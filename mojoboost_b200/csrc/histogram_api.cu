@@ -28,12 +28,6 @@ struct DevMem {
   ~DevMem() { cudaFree(p); }
 };
 
-// Largest flush span for packed cells (g * 2^15 + count) given |g| <= bins/2.
-long long quant_rows_per_flush(int quant_bins) {
-  long long gl = quant_bins / 2;
-  return std::min<long long>((1ll << 15) - 1, ((1ll << 16) - 1) / gl);
-}
-
 // Job descriptor of one histogram build over positions [0, n_sel) of
 // rows/pairs: a one-item batch whose built child is the whole selection.
 Batch one_item_batch(long long n_sel) {
@@ -62,9 +56,8 @@ void launch_leaf_hist(const uint8_t* d_bins_rm, int F, int Fp, int B, const int*
   int dev = 0, n_sm = 0;
   MTB_CUDA(cudaGetDevice(&dev));
   MTB_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
-  HistLaunch hl = choose_hist_launch(MODE_QUANT, false, B, Fp, n_sm);
-  launch_hist<MODE_QUANT, false>(hl, st, d_batch, d_bins_rm, Fp, F, B, d_rows, d_rows, d_pairs, d_pairs, d_work,
-                                 cells, quant_rows_per_flush(quant_bins), 0);
+  HistLaunch hl = choose_hist_launch(MODE_QUANT, false, quant_bins, B, Fp, n_sm);
+  launch_hist(hl, st, d_batch, d_bins_rm, Fp, F, B, d_rows, d_rows, d_pairs, d_pairs, d_work, cells, 0);
   MTB_CUDA(cudaGetLastError());
 }
 
@@ -156,7 +149,7 @@ struct NoAllocDevice {
   bool ready = false;
   unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch
   HistLaunch hl;
-  int hl_B = -1, hl_Fp = -1;
+  int hl_B = -1, hl_Fp = -1, hl_qb = -1;
 };
 constexpr int kMaxDevices = 64;
 NoAllocDevice g_noalloc_dev[kMaxDevices];
@@ -198,12 +191,13 @@ extern "C" int32_t mojotrees_b200_histogram_u8_noalloc(const uint8_t* bins_rm, i
         d->scratch = static_cast<unsigned char*>(ptr);
         d->ready = true;
       }
-      if (d->hl_B != B || d->hl_Fp != Fp) {
+      if (d->hl_B != B || d->hl_Fp != Fp || d->hl_qb != num_grad_quant_bins) {
         int n_sm = 0;
         MTB_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
-        d->hl = choose_hist_launch(MODE_QUANT, false, B, Fp, n_sm);
+        d->hl = choose_hist_launch(MODE_QUANT, false, num_grad_quant_bins, B, Fp, n_sm);
         d->hl_B = B;
         d->hl_Fp = Fp;
+        d->hl_qb = num_grad_quant_bins;
       }
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -212,8 +206,7 @@ extern "C" int32_t mojotrees_b200_histogram_u8_noalloc(const uint8_t* bins_rm, i
     Batch b = one_item_batch(n_sel);
     MTB_CUDA(cudaMemcpyAsync(batch, &b, kOneItemBatchBytes, cudaMemcpyHostToDevice, st));
     MTB_CUDA(cudaMemsetAsync(work, 0, sizeof(int) * cells, st));  // the array keeps the last call's cells
-    launch_hist<MODE_QUANT, false>(d->hl, st, batch, bins_rm, Fp, F, B, rows, rows, pairs, pairs, work, cells,
-                                   quant_rows_per_flush(num_grad_quant_bins), 0);
+    launch_hist(d->hl, st, batch, bins_rm, Fp, F, B, rows, rows, pairs, pairs, work, cells, 0);
     MTB_CUDA(cudaGetLastError());
     MTB_CUDA(cudaMemcpyAsync(out_hist, work, sizeof(int) * cells, cudaMemcpyDeviceToDevice, st));
     return MOJOTREES_OK;

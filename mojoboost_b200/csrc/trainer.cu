@@ -307,13 +307,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   // Histogram launch geometry: as many features per CTA as one SM's shared
   // memory holds, row chunks sized to fill every SM, CTAs of a feature group
   // in clusters of up to 8 that merge through DSMEM.
-  HistLaunch hl = choose_hist_launch(mode, const_h, B, Fp, n_sm);
-  long long rows_per_flush = 1ll << 40;
-  if (mode == MODE_QUANT) {
-    // plane 0 holds g * 2^15 + count: count < 2^15 and |sum g| < 2^16 per flush
-    long long gl = cfg.num_grad_quant_bins / 2;
-    rows_per_flush = std::min<long long>((1ll << 15) - 1, ((1ll << 16) - 1) / gl);
-  }
+  HistLaunch hl = choose_hist_launch(mode, const_h, mode == MODE_QUANT ? cfg.num_grad_quant_bins : 0, B, Fp, n_sm);
   const int part_grid = n_sm * 4;
   const int part_threads = 256;
   int part_items = 2;  // rows per thread per partition tile
@@ -398,15 +392,8 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   int launches = 0;
   auto hist = [&]() {
     timer.begin(&stats.hist_ms);
-    if (mode == MODE_QUANT)
-      launch_hist<MODE_QUANT, false>(hl, st, batch_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
-                                     d_pairs1.p, d_hist.p, slot_cells, rows_per_flush, work_base);
-    else if (const_h)
-      launch_hist<MODE_FIXED, true>(hl, st, batch_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
-                                    d_pairs1.p, d_hist.p, slot_cells, rows_per_flush, work_base);
-    else
-      launch_hist<MODE_FIXED, false>(hl, st, batch_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p,
-                                     d_pairs1.p, d_hist.p, slot_cells, rows_per_flush, work_base);
+    launch_hist(hl, st, batch_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p, d_pairs1.p,
+                d_hist.p, slot_cells, work_base);
     timer.end();
   };
   // the built children's cells summed over every device's rows (exact int32)

@@ -54,6 +54,8 @@ def oracle_kwargs(p):
             kw[k] = p[k]
     if "min_sum_hessian_in_leaf" in p:
         kw["min_child_hess"] = p["min_sum_hessian_in_leaf"]
+    if "num_grad_quant_bins" in p:
+        kw["quant_bins"] = p["num_grad_quant_bins"]
     return kw
 
 

@@ -39,3 +39,20 @@ def test_histogram_all_rows_and_errors(mtlib):
     np.testing.assert_array_equal(got, host_histogram(bins, 255, g, h, np.arange(40_000)))
     with pytest.raises(mtlib.MojoTreesError):
         mtlib.histogram_u8(bins, 255, (g * 3).astype(np.int8), h)
+
+
+@pytest.mark.parametrize("qb", [2, 16, 64, 254])
+def test_histogram_quantizer_widths(mtlib, qb):
+    """Every quantizer width, at the extremes of its range, over more rows
+    than one flush of the packed 16-bit cells covers."""
+    rng = np.random.default_rng(qb)
+    n, F, B = 150_000, 40, 256
+    bins = rng.integers(0, B, size=(F, n), dtype=np.uint8)
+    lim = qb // 2
+    g = rng.choice(np.array([-lim, lim, 0, 1 - lim], np.int64), size=n).astype(np.int8)
+    h = rng.choice(np.array([qb, 0, qb - 1], np.int64), size=n).astype(np.uint8)
+    # most rows in one bin of every feature: the largest per-cell sums
+    bins[:, : n // 2] = 7
+    rows = np.arange(n, dtype=np.int32)
+    got = mtlib.histogram_u8(bins, B, g, h, rows=rows, num_grad_quant_bins=qb)
+    np.testing.assert_array_equal(got, host_histogram(bins, B, g, h, rows))

@@ -33,6 +33,16 @@ CASES = {
     "missing_cat_quant": (dict(seed=8, n=20_000, f=8, nan_frac=0.1, cat_cols=(2, 5), n_cat=3, kind="binary"),
                           dict(objective="binary", rounds=4, leaves=31, quant=True,
                                extra={"categorical_feature": "2,5"}), 63),
+    # quantizer widths that select each shared-memory cell layout of the
+    # histogram: 16 keeps 16-bit packed cells, 64 and 254 the 32-bit ones
+    "binary_quant16": (dict(seed=12, n=60_000, f=40, kind="binary"),
+                       dict(objective="binary", rounds=3, leaves=63, quant=True,
+                            extra={"num_grad_quant_bins": 16}), 255),
+    "binary_quant64": (dict(seed=13, n=60_000, f=40, kind="binary"),
+                       dict(objective="binary", rounds=3, leaves=63, quant=True,
+                            extra={"num_grad_quant_bins": 64}), 255),
+    "l2_quant254": (dict(seed=14, n=40_000, f=20), dict(objective="regression", rounds=3, leaves=31, quant=True,
+                                                       extra={"num_grad_quant_bins": 254}), 127),
     "feature_fraction": (dict(seed=9, n=20_000, f=24), dict(objective="regression", rounds=4, leaves=31,
                                                             extra={"feature_fraction": 0.5}), 255),
     "wide_features": (dict(seed=10, n=10_000, f=150), dict(objective="regression", rounds=2, leaves=31), 255),
