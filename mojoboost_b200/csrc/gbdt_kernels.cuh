@@ -83,6 +83,35 @@ __device__ __forceinline__ void atomic_max_nonneg(double* addr, double v) {
   atomicMax(reinterpret_cast<unsigned long long*>(addr), (unsigned long long)__double_as_longlong(v));
 }
 
+// Block maxima of two non-negative values folded into the round's scales: one
+// atomic per block and value (same-address atomics from every warp would
+// serialise in L2).  sm holds 32 doubles; every thread of the block calls it.
+__device__ __forceinline__ void block_max_to(double ag, double ah, double* sm, RoundScales* sc) {
+  __shared__ double smh[32];
+  for (int k = 16; k > 0; k >>= 1) {
+    ag = fmax(ag, __shfl_down_sync(0xffffffffu, ag, k));
+    ah = fmax(ah, __shfl_down_sync(0xffffffffu, ah, k));
+  }
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (lane == 0) {
+    sm[w] = ag;
+    smh[w] = ah;
+  }
+  __syncthreads();
+  if (w == 0) {
+    ag = lane < (int)(blockDim.x >> 5) ? sm[lane] : 0.0;
+    ah = lane < (int)(blockDim.x >> 5) ? smh[lane] : 0.0;
+    for (int k = 16; k > 0; k >>= 1) {
+      ag = fmax(ag, __shfl_down_sync(0xffffffffu, ag, k));
+      ah = fmax(ah, __shfl_down_sync(0xffffffffu, ah, k));
+    }
+    if (lane == 0) {
+      atomic_max_nonneg(&sc->g_total, ag);
+      atomic_max_nonneg(&sc->h_total, ah);
+    }
+  }
+}
+
 // Per-row derivatives for L2 / logistic, narrowed to Float32.  1024 threads,
 // one row each.  FIXED mode writes per-block pairwise |g|, |h| partials;
 // QUANT mode folds max |g|, max |h| into the round's scales.
@@ -116,15 +145,7 @@ __global__ void __launch_bounds__(1024) k_grad(const double* __restrict__ raw, c
     double sh = block_pairwise_1024(fabs(h), sm);
     if (threadIdx.x == 0) part_h[blockIdx.x] = sh;
   } else {
-    double ag = fabs(g), ah = fabs(h);
-    for (int k = 16; k > 0; k >>= 1) {
-      ag = fmax(ag, __shfl_down_sync(0xffffffffu, ag, k));
-      ah = fmax(ah, __shfl_down_sync(0xffffffffu, ah, k));
-    }
-    if ((threadIdx.x & 31) == 0) {
-      atomic_max_nonneg(&sc->g_total, ag);
-      atomic_max_nonneg(&sc->h_total, ah);
-    }
+    block_max_to(fabs(g), fabs(h), sm, sc);
   }
 }
 
@@ -173,15 +194,7 @@ __global__ void __launch_bounds__(1024) k_grad_softmax(const double* __restrict_
     double sh = block_pairwise_1024(fabs(h), sm);
     if (threadIdx.x == 0) part_h[blockIdx.x] = sh;
   } else {
-    double ag = fabs(g), ah = fabs(h);
-    for (int s = 16; s > 0; s >>= 1) {
-      ag = fmax(ag, __shfl_down_sync(0xffffffffu, ag, s));
-      ah = fmax(ah, __shfl_down_sync(0xffffffffu, ah, s));
-    }
-    if ((threadIdx.x & 31) == 0) {
-      atomic_max_nonneg(&sc->g_total, ag);
-      atomic_max_nonneg(&sc->h_total, ah);
-    }
+    block_max_to(fabs(g), fabs(h), sm, sc);
   }
 }
 
@@ -1139,14 +1152,6 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
   Batch& Bt = ts->batch;
   const int n_items = Bt.n_items;
   const bool root = Bt.root != 0;
-#ifdef MTB_COMMIT_CLOCKS
-  long long clk[8];
-  int n_clk = 0;
-  clk[n_clk++] = clock64();
-#define MTB_CLK() if (t == 0) clk[n_clk++] = clock64()
-#else
-#define MTB_CLK()
-#endif
 
   // ---- 1. children of this iteration's expansions (one warp per child)
   for (int c = w; c < 2 * n_items; c += kCommitThreads / 32) {
@@ -1211,7 +1216,6 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
     L.exp_buf = P.dst_buf;
   }
   __syncthreads();
-  MTB_CLK();
 
   // ---- 2. the frontier into shared memory
   const int nl0 = H.n_leaves;
@@ -1230,7 +1234,6 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
     }
   }
   __syncthreads();
-  MTB_CLK();
 
   // ---- 3. the pick loop, on one warp over shared memory only
   if (w == 0) {
@@ -1282,7 +1285,6 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
     }
   }
   __syncthreads();
-  MTB_CLK();
 
   // ---- 4. the commits' writes, one thread each
   const int n_commit = s_ncommit;
@@ -1324,7 +1326,6 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
     H.n_leaves = nl;
   }
 
-  MTB_CLK();
   // ---- 5. next batch
   if (s_stop) {
     if (t == 0) {
@@ -1432,13 +1433,6 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
     }
   }
   __syncthreads();
-  MTB_CLK();
-#ifdef MTB_COMMIT_CLOCKS
-  if (t == 0)
-    printf("commit it=%d items=%d commits=%d nl=%d | %lld %lld %lld %lld %lld\n", H.iterations, n_items, n_commit, nl,
-           clk[1] - clk[0], clk[2] - clk[1], clk[3] - clk[2], clk[4] - clk[3], clk[5] - clk[4]);
-#endif
-#undef MTB_CLK
   if (t == 0) {
     H.iterations += 1;
     if (host_done) {

@@ -308,9 +308,13 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   // memory holds, row chunks sized to fill every SM, CTAs of a feature group
   // in clusters of up to 8 that merge through DSMEM.
   HistLaunch hl = choose_hist_launch(mode, const_h, mode == MODE_QUANT ? cfg.num_grad_quant_bins : 0, B, Fp, n_sm);
-  const int part_grid = n_sm * 4;
+  // partition geometry (MOJOTREES_PART_ITEMS / MOJOTREES_PART_BLOCKS_PER_SM
+  // override the rows per thread of a tile and the resident blocks per SM)
+  int part_bps = 4;
+  if (const char* e = getenv("MOJOTREES_PART_BLOCKS_PER_SM")) part_bps = std::max(1, atoi(e));
+  const int part_grid = n_sm * part_bps;
   const int part_threads = 256;
-  int part_items = 2;  // rows per thread per partition tile
+  int part_items = 4;  // rows per thread per partition tile
   if (const char* e = getenv("MOJOTREES_PART_ITEMS")) part_items = atoi(e);
   part_items = part_items <= 1 ? 1 : part_items == 2 ? 2 : part_items <= 4 ? 4 : 8;
   auto launch_partition = [&]() {
