@@ -207,9 +207,15 @@ def run_gpu(args):
         t0 = time.perf_counter()
         m2 = mb.train_dense(X64, y, params(args.steps, extra={"gpu_device_id": local}))
         e2e_s = time.perf_counter() - t0
+        s2 = m2.stats()
+        # copied to the device per fit: uint8 bins (F x N), labels and initial
+        # scores (float64); read back per round: the tree's node table
+        h2d = N_ROWS * N_FEAT + 8 * N_ROWS + 8 * N_ROWS
         e2e = {"value": m2.num_trees / e2e_s, "unit": UNIT,
-               "h2d_bytes_per_step": (X64.nbytes + y.nbytes) / max(1, args.steps),
+               "h2d_bytes_per_step": h2d / max(1, args.steps),
                "d2h_bytes_per_step": 88 * (2 * LEAVES - 1), "seconds": e2e_s, "rounds": int(m2.num_trees),
+               "host_binning_s": s2["binning_seconds"], "upload_s": s2["upload_seconds"],
+               "device_loop_s": s2["fit_seconds"],
                "api": "mojotrees_train_dense (host float64 matrix; includes host binning)"}
     if rank != 0:
         return

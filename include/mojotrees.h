@@ -134,6 +134,14 @@ int32_t mojotrees_b200_bin_dense(const double *data, int64_t n_rows, int64_t n_f
                                  uint8_t *out_bins, int32_t *out_missing_bin, int32_t *out_n_categories,
                                  int32_t *out_n_bins, MojoTreesError *error);
 
+/* The same bins as mojotrees_b200_bin_dense, with the columns binned on the
+ * current CUDA device (the transform mojotrees_train_dense uses): edges are
+ * fitted on the host, the float64 columns are copied in feature chunks and
+ * binned by a kernel.  MOJOTREES_ERROR_UNSUPPORTED without a device. */
+int32_t mojotrees_b200_bin_dense_gpu(const double *data, int64_t n_rows, int64_t n_features,
+                                     const char *parameters, uint8_t *out_bins, int32_t *out_missing_bin,
+                                     int32_t *out_n_categories, int32_t *out_n_bins, MojoTreesError *error);
+
 /* Raw-score prediction on pre-binned feature-major data (any model). */
 int32_t mojotrees_b200_predict_binned_u8(const MojoTreesModel *model, const uint8_t *bins, int64_t n_rows,
                                          int64_t n_features, double *out_values, int64_t out_len,
@@ -161,7 +169,8 @@ int32_t mojotrees_b200_training_scores(const MojoTreesModel *model, double *out_
  * fit_seconds, upload_seconds, hist_ms, partition_ms, scan_ms, grad_ms,
  * hist_rows, hist_bytes, hist_launches, kernel_launches, rounds, commit_ms,
  * iterations (batch iterations that did work), expansions (leaves whose
- * children were computed; exceeds the splits by the speculative ones).  The phase
+ * children were computed; exceeds the splits by the speculative ones),
+ * binning_seconds (host bin fitting and transform of mojotrees_train_dense).  The phase
  * times are measured with CUDA events only when the fit ran with
  * profile_phases=true.  Returns the number of values written via *out_n. */
 int32_t mojotrees_b200_train_stats(const MojoTreesModel *model, double *out_values, int64_t out_len,

@@ -23,7 +23,7 @@ IMPORTANCE_SPLIT, IMPORTANCE_GAIN = 0, 1
 
 STAT_NAMES = ("fit_seconds", "upload_seconds", "hist_ms", "partition_ms", "scan_ms", "grad_ms",
               "hist_rows", "hist_bytes", "hist_launches", "kernel_launches", "rounds",
-              "commit_ms", "iterations", "expansions")
+              "commit_ms", "iterations", "expansions", "binning_seconds")
 
 # Every symbol include/mojotrees.h declares, with its ctypes signature.
 _P, _I32, _I64, _D = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_double
@@ -51,6 +51,7 @@ SIGNATURES = {
     "mojotrees_model_free": (None, [_P]),
     "mojotrees_b200_train_binned_u8": (_I32, [_P, _I64, _I64, _I32, _P, _P, _P, _P, ctypes.c_char_p, _P, _P]),
     "mojotrees_b200_bin_dense": (_I32, [_P, _I64, _I64, ctypes.c_char_p, _P, _P, _P, _P, _P]),
+    "mojotrees_b200_bin_dense_gpu": (_I32, [_P, _I64, _I64, ctypes.c_char_p, _P, _P, _P, _P, _P]),
     "mojotrees_b200_predict_binned_u8": (_I32, [_P, _P, _I64, _I64, _P, _I64, _P]),
     "mojotrees_b200_tree_nodes": (_I32, [_P, _I64, _P, _P, _P, _P, _I64, _P, _P]),
     "mojotrees_b200_base_scores": (_I32, [_P, _P, _I64, _P]),
@@ -325,8 +326,9 @@ def train_binned_dp(bins_fm, n_bins, y, nccl_id, rank, world, row_offset, n_rows
     return Model(h.value)
 
 
-def bin_dense(X, params=None):
-    """Host binning as train_dense does it: (bins [F, N] uint8, missing_bin, n_categories, n_bins)."""
+def bin_dense(X, params=None, device=False):
+    """Binning as train_dense does it: (bins [F, N] uint8, missing_bin, n_categories, n_bins).
+    device=True bins the columns on the GPU (mojotrees_b200_bin_dense_gpu)."""
     X = np.asarray(X, dtype=np.float64)
     n, f = X.shape
     Xc = np.asfortranarray(X)
@@ -335,8 +337,9 @@ def bin_dense(X, params=None):
     nc = np.zeros(f, np.int32)
     nb = ctypes.c_int32(0)
     e = _Err()
-    e.check(lib().mojotrees_b200_bin_dense(Xc.ctypes.data_as(ctypes.c_void_p), n, f, params_string(params),
-                                           _ptr(bins), _ptr(mb), _ptr(nc), ctypes.byref(nb), e.h))
+    fn = lib().mojotrees_b200_bin_dense_gpu if device else lib().mojotrees_b200_bin_dense
+    e.check(fn(Xc.ctypes.data_as(ctypes.c_void_p), n, f, params_string(params), _ptr(bins), _ptr(mb), _ptr(nc),
+               ctypes.byref(nb), e.h))
     return bins, mb, nc, nb.value
 
 

@@ -2,6 +2,7 @@
 #include "binning.h"
 
 #include <algorithm>
+#include <exception>
 #include <cmath>
 #include <stdexcept>
 
@@ -123,98 +124,116 @@ BinMapper fit_bins(const double* x, int64_t n_rows, int n_features, const Binnin
     if (m.is_cat[f]) throw std::runtime_error("categorical feature listed twice");
     m.is_cat[f] = 1;
   }
-  m.cat_offsets.push_back(0);
-  for (int f = 0; f < n_features; ++f) {
-    if (m.is_cat[f]) {
-      auto kept = kept_codes(x + (int64_t)f * n_rows, n_rows, p.max_bins);
-      m.cat_codes.insert(m.cat_codes.end(), kept.begin(), kept.end());
-    }
-    m.cat_offsets.push_back((int64_t)m.cat_codes.size());
-  }
+  // Features are independent: each one's codes or edges are computed on its
+  // own thread with its own scratch, then laid out in feature order (the
+  // result does not depend on the thread count).
+  std::vector<std::vector<int64_t>> codes_f((size_t)n_features);
+  std::vector<std::vector<double>> edges_f((size_t)n_features);
+  std::vector<int> missing_f((size_t)n_features, -1);
   std::vector<int64_t> sample = sample_rows(n_rows, p.bin_construct_sample_cnt, p.data_random_seed);
-  bool sampled = !sample.empty();
-  int64_t n_sample = sampled ? (int64_t)sample.size() : n_rows;
-  m.edge_offsets.push_back(0);
-  std::vector<double> col, below, above, out, levels;
-  std::vector<int64_t> level_counts;
-  for (int f = 0; f < n_features; ++f) {
-    if (m.is_cat[f]) {
-      m.edge_offsets.push_back((int64_t)m.edges.size());
-      continue;
-    }
-    const double* base = x + (int64_t)f * n_rows;
-    col.clear();
-    if (sampled) {
-      for (int64_t i = 0; i < n_sample; ++i) {
-        double v = base[sample[i]];
-        if (!std::isnan(v)) col.push_back(v);
-      }
-    } else {
-      for (int64_t r = 0; r < n_rows; ++r)
-        if (!std::isnan(base[r])) col.push_back(base[r]);
-    }
-    int64_t n_valid = (int64_t)col.size();
-    bool reserve = p.use_missing && n_valid < n_sample;
-    int n_ordinary = reserve ? p.max_bins - 1 : p.max_bins;
-    below.clear();
-    above.clear();
-    // Sort once; -0.0 and 0.0 compare equal and are one level.
-    std::sort(col.begin(), col.end());
-    levels.clear();
-    level_counts.clear();
-    bool distinct_fits = n_valid >= 1;
-    for (int64_t i = 0; i < n_valid && distinct_fits; ++i) {
-      double v = col[i] == 0.0 ? 0.0 : col[i];
-      if (!levels.empty() && levels.back() == v) {
-        level_counts.back() += 1;
+  const bool sampled = !sample.empty();
+  const int64_t n_sample = sampled ? (int64_t)sample.size() : n_rows;
+  // an exception must not leave an OpenMP region: the first one is kept and
+  // rethrown after it
+  std::exception_ptr failure;
+#pragma omp parallel
+  {
+    std::vector<double> col, below, above, out, levels;
+    std::vector<int64_t> level_counts;
+#pragma omp for schedule(dynamic, 1)
+    for (int f = 0; f < n_features; ++f) {
+      if (m.is_cat[f]) {
+        try {
+          codes_f[f] = kept_codes(x + (int64_t)f * n_rows, n_rows, p.max_bins);
+        } catch (...) {
+#pragma omp critical(mtb_fit_bins_failure)
+          if (!failure) failure = std::current_exception();
+        }
         continue;
       }
-      if ((int)levels.size() >= n_ordinary) {
-        distinct_fits = false;
-        break;
-      }
-      levels.push_back(v);
-      level_counts.push_back(1);
-    }
-    if (distinct_fits) {
-      // binning.mojo:3850-3868
-      if (p.min_data_in_bin <= 1) {
-        for (size_t j = 0; j + 1 < levels.size(); ++j) {
-          below.push_back(levels[j]);
-          above.push_back(levels[j + 1]);
+      const double* base = x + (int64_t)f * n_rows;
+      col.clear();
+      if (sampled) {
+        for (int64_t i = 0; i < n_sample; ++i) {
+          double v = base[sample[i]];
+          if (!std::isnan(v)) col.push_back(v);
         }
       } else {
-        int64_t acc = 0;
-        for (size_t j = 0; j + 1 < levels.size(); ++j) {
-          acc += level_counts[j];
-          if (acc >= p.min_data_in_bin) {
+        for (int64_t r = 0; r < n_rows; ++r)
+          if (!std::isnan(base[r])) col.push_back(base[r]);
+      }
+      int64_t n_valid = (int64_t)col.size();
+      bool reserve = p.use_missing && n_valid < n_sample;
+      int n_ordinary = reserve ? p.max_bins - 1 : p.max_bins;
+      below.clear();
+      above.clear();
+      // Sort once; -0.0 and 0.0 compare equal and are one level.
+      std::sort(col.begin(), col.end());
+      levels.clear();
+      level_counts.clear();
+      bool distinct_fits = n_valid >= 1;
+      for (int64_t i = 0; i < n_valid && distinct_fits; ++i) {
+        double v = col[i] == 0.0 ? 0.0 : col[i];
+        if (!levels.empty() && levels.back() == v) {
+          level_counts.back() += 1;
+          continue;
+        }
+        if ((int)levels.size() >= n_ordinary) {
+          distinct_fits = false;
+          break;
+        }
+        levels.push_back(v);
+        level_counts.push_back(1);
+      }
+      if (distinct_fits) {
+        // binning.mojo:3850-3868
+        if (p.min_data_in_bin <= 1) {
+          for (size_t j = 0; j + 1 < levels.size(); ++j) {
             below.push_back(levels[j]);
             above.push_back(levels[j + 1]);
-            acc = 0;
+          }
+        } else {
+          int64_t acc = 0;
+          for (size_t j = 0; j + 1 < levels.size(); ++j) {
+            acc += level_counts[j];
+            if (acc >= p.min_data_in_bin) {
+              below.push_back(levels[j]);
+              above.push_back(levels[j + 1]);
+              acc = 0;
+            }
           }
         }
+      } else {
+        // binning.mojo:3876-3957
+        int64_t n_ord = n_ordinary;
+        if (p.min_data_in_bin > 1) {
+          int64_t cap = n_valid / p.min_data_in_bin;
+          if (cap < 1) cap = 1;
+          if (cap < n_ord) n_ord = cap;
+        }
+        for (int64_t b = 1; b < n_ord; ++b) {
+          int64_t idx = b * n_valid / n_ord;
+          if (idx <= 0 || idx >= n_valid) continue;
+          double w = col[idx - 1];
+          below.push_back(w);
+          auto it = std::upper_bound(col.begin() + idx, col.end(), w);
+          above.push_back(it != col.end() ? *it : w);
+        }
       }
-    } else {
-      // binning.mojo:3876-3957
-      int64_t n_ord = n_ordinary;
-      if (p.min_data_in_bin > 1) {
-        int64_t cap = n_valid / p.min_data_in_bin;
-        if (cap < 1) cap = 1;
-        if (cap < n_ord) n_ord = cap;
-      }
-      for (int64_t b = 1; b < n_ord; ++b) {
-        int64_t idx = b * n_valid / n_ord;
-        if (idx <= 0 || idx >= n_valid) continue;
-        double w = col[idx - 1];
-        below.push_back(w);
-        auto it = std::upper_bound(col.begin() + idx, col.end(), w);
-        above.push_back(it != col.end() ? *it : w);
-      }
+      emit_edges(below, above, out);
+      edges_f[f] = out;
+      missing_f[f] = reserve ? (int)out.size() + 1 : -1;
     }
-    emit_edges(below, above, out);
-    m.edges.insert(m.edges.end(), out.begin(), out.end());
+  }
+  if (failure) std::rethrow_exception(failure);
+  m.cat_offsets.push_back(0);
+  m.edge_offsets.push_back(0);
+  for (int f = 0; f < n_features; ++f) {
+    m.cat_codes.insert(m.cat_codes.end(), codes_f[f].begin(), codes_f[f].end());
+    m.cat_offsets.push_back((int64_t)m.cat_codes.size());
+    m.edges.insert(m.edges.end(), edges_f[f].begin(), edges_f[f].end());
     m.edge_offsets.push_back((int64_t)m.edges.size());
-    m.missing_bin[f] = reserve ? (int)out.size() + 1 : -1;
+    m.missing_bin[f] = missing_f[f];
   }
   return m;
 }

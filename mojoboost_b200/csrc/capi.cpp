@@ -10,6 +10,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cctype>
 #include <fstream>
 #include <map>
@@ -26,6 +27,7 @@
 #include "capi_util.h"
 #include "collective.h"
 #include "model.h"
+#include "device_binning.h"
 #include "trainer.h"
 
 struct MojoTreesError {
@@ -362,10 +364,13 @@ char* dup_string(const std::string& s) {
 int32_t train_binned(const uint8_t* bins, int64_t n_rows, int64_t n_features, int32_t n_bins,
                      const std::vector<int>& missing, const std::vector<int>& ncats, const double* labels,
                      const TrainConfig& cfg, MojoTreesModel** out_model, const mtb::BinMapper* mapper,
-                     mtb::Collective* coll = nullptr, int64_t row_offset = 0, int64_t n_rows_global = 0) {
+                     mtb::Collective* coll = nullptr, int64_t row_offset = 0, int64_t n_rows_global = 0,
+                     const double* dense = nullptr) {
   for (int64_t r = 0; r < n_rows; ++r)
     if (!std::isfinite(labels[r])) throw InvalidArgument("labels must be finite");
   mtb::BinnedInput in{bins, n_rows, (int)n_features, n_bins, missing.data(), ncats.data(), labels};
+  in.dense_fm = dense;
+  in.mapper = dense ? mapper : nullptr;
   in.coll = coll;
   in.row_offset = row_offset;
   in.n_rows_global = coll ? n_rows_global : n_rows;
@@ -407,14 +412,18 @@ int32_t mojotrees_train_dense(const double* data, int64_t n_rows, int64_t n_feat
     if (n_rows < 1 || n_features < 1) throw InvalidArgument("n_rows and n_features must be positive");
     TrainConfig cfg = parse_config(parameters, true);
     if (weights) throw mtb::Unsupported("sample weights are not covered by the device path");
+    // bin edges are fitted on the host from a row sample; the columns
+    // themselves are binned on the device (device_binning.cu)
+    auto t0 = std::chrono::steady_clock::now();
     mtb::BinMapper mapper = mtb::fit_bins(data, n_rows, (int)n_features, cfg.binning);
-    std::vector<uint8_t> bins((size_t)n_rows * n_features);
-    mtb::transform(mapper, data, n_rows, bins.data());
+    const double bin_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     std::vector<int> ncats(n_features, -1);
     for (int f = 0; f < n_features; ++f)
       if (mapper.is_cat[f]) ncats[f] = mapper.n_categories(f);
-    return train_binned(bins.data(), n_rows, n_features, mapper.n_bins, mapper.missing_bin, ncats, labels, cfg,
-                        out_model, &mapper);
+    int32_t rc = train_binned(nullptr, n_rows, n_features, mapper.n_bins, mapper.missing_bin, ncats, labels, cfg,
+                              out_model, &mapper, nullptr, 0, 0, data);
+    if (rc == MOJOTREES_OK && *out_model) (*out_model)->m.stats.binning_seconds = bin_s;
+    return rc;
   });
 }
 
@@ -507,6 +516,38 @@ int32_t mojotrees_b200_bin_dense(const double* data, int64_t n_rows, int64_t n_f
         TrainConfig cfg = parse_config(parameters, false);
         mtb::BinMapper m = mtb::fit_bins(data, n_rows, (int)n_features, cfg.binning);
         mtb::transform(m, data, n_rows, out_bins);
+        for (int64_t f = 0; f < n_features; ++f) {
+          if (out_missing_bin) out_missing_bin[f] = m.missing_bin[f];
+          if (out_n_categories) out_n_categories[f] = m.is_cat[f] ? m.n_categories((int)f) : -1;
+        }
+        if (out_n_bins) *out_n_bins = m.n_bins;
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+
+int32_t mojotrees_b200_bin_dense_gpu(const double* data, int64_t n_rows, int64_t n_features, const char* parameters,
+                                     uint8_t* out_bins, int32_t* out_missing_bin, int32_t* out_n_categories,
+                                     int32_t* out_n_bins, MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!data || !out_bins) throw InvalidArgument("null pointer argument");
+        if (n_rows < 1 || n_features < 1) throw InvalidArgument("n_rows and n_features must be positive");
+        TrainConfig cfg = parse_config(parameters, false);
+        if (mtb::cuda_device_count() < 1) throw mtb::Unsupported("no CUDA device is available");
+        mtb::BinMapper m = mtb::fit_bins(data, n_rows, (int)n_features, cfg.binning);
+        const size_t bytes = (size_t)n_rows * (size_t)n_features;
+        uint8_t* d_bins = nullptr;
+        if (cudaMalloc(&d_bins, bytes) != cudaSuccess) throw std::runtime_error("cudaMalloc failed");
+        struct Free {
+          uint8_t* p;
+          ~Free() { cudaFree(p); }
+        } fr{d_bins};
+        mtb::transform_on_device(m, data, n_rows, d_bins, 0);
+        if (cudaMemcpy(out_bins, d_bins, bytes, cudaMemcpyDeviceToHost) != cudaSuccess)
+          throw std::runtime_error("cudaMemcpy failed");
         for (int64_t f = 0; f < n_features; ++f) {
           if (out_missing_bin) out_missing_bin[f] = m.missing_bin[f];
           if (out_n_categories) out_n_categories[f] = m.is_cat[f] ? m.n_categories((int)f) : -1;
@@ -831,7 +872,7 @@ int32_t mojotrees_b200_train_stats(const MojoTreesModel* model, double* out_valu
         const double v[] = {s.fit_seconds, s.upload_seconds, s.hist_ms,   s.partition_ms,
                             s.scan_ms,     s.grad_ms,        s.hist_rows, s.hist_bytes,
                             (double)s.hist_launches, (double)s.kernel_launches, (double)s.rounds,
-                            s.commit_ms,   (double)s.iterations, (double)s.expansions};
+                            s.commit_ms,   (double)s.iterations, (double)s.expansions, s.binning_seconds};
         int64_t n = std::min<int64_t>(out_len, (int64_t)(sizeof v / sizeof v[0]));
         for (int64_t i = 0; i < n; ++i) out_values[i] = v[i];
         if (out_n) *out_n = n;

@@ -63,6 +63,7 @@ struct TrainStats {
   double scan_ms = 0.0;
   double grad_ms = 0.0;
   double commit_ms = 0.0;
+  double binning_seconds = 0.0;     // host bin fitting + transform (dense entry point)
   double hist_rows = 0.0;           // rows read by histogram builds (built children + roots)
   double hist_bytes = 0.0;          // algorithmic bytes: hist_rows * (F + pair bytes)
   int hist_launches = 0;            // histogram launches (one per batch iteration)

@@ -22,6 +22,7 @@
 #include "gbdt_kernels.cuh"
 #include "hist_launch.cuh"
 #include "collective.h"
+#include "device_binning.h"
 #include "trainer.h"
 
 namespace mtb {
@@ -144,7 +145,12 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   DevBuf<uint8_t> d_bins_cm, d_bins_rm;
   d_bins_cm.alloc((size_t)F * N);
   d_bins_rm.alloc((size_t)Fp * N);
-  MTB_CUDA(cudaMemcpyAsync(d_bins_cm.p, in.bins_fm, (size_t)F * N, cudaMemcpyHostToDevice, st));
+  if (in.dense_fm) {
+    if (!in.mapper) throw std::runtime_error("dense input without a bin mapper");
+    transform_on_device(*in.mapper, in.dense_fm, N, d_bins_cm.p, st);
+  } else {
+    MTB_CUDA(cudaMemcpyAsync(d_bins_cm.p, in.bins_fm, (size_t)F * N, cudaMemcpyHostToDevice, st));
+  }
   {
     dim3 grid((unsigned)((N + 255) / 256), Fp / 16);
     k_transpose_bins<<<grid, 256, 0, st>>>(d_bins_cm.p, d_bins_rm.p, N, F, Fp);

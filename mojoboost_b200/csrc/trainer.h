@@ -12,6 +12,8 @@ struct Unsupported : std::runtime_error {
   explicit Unsupported(const std::string& m) : std::runtime_error(m) {}
 };
 
+struct BinMapper;
+
 struct BinnedInput {
   const uint8_t* bins_fm;   // feature-major bins[f * n_rows + r], host memory
   long long n_rows;
@@ -26,6 +28,10 @@ struct BinnedInput {
   long long row_offset = 0;
   long long n_rows_global = 0;
   class Collective* coll = nullptr;
+  // Dense entry point: instead of bins_fm, float64 columns dense_fm[f * n_rows
+  // + r] (host memory) binned on the device with `mapper`.
+  const double* dense_fm = nullptr;
+  const BinMapper* mapper = nullptr;
 };
 
 // Trains on the current (or configured) CUDA device; fills model.trees,

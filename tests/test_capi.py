@@ -139,3 +139,13 @@ def test_bin_dense_edges_monotone_and_sampled(mtlib):
         assert np.all(np.diff(bins[f][order].astype(int)) >= 0)
         assert bins[f].max() <= 254
     assert list(mb) == [-1, -1]
+
+
+def test_bin_dense_reports_bad_categorical_code(mtlib):
+    """A categorical code beyond int32 is an input error (raised on one of the
+    binning threads, reported through the error object)."""
+    X = np.zeros((100, 3))
+    X[:, 1] = np.arange(100) % 5
+    X[7, 1] = 3e9
+    with pytest.raises(mtlib.MojoTreesError):
+        mtlib.bin_dense(X, {"categorical_feature": "1"})

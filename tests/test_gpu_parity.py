@@ -105,6 +105,38 @@ def test_gpu_dense_entry_matches_binned(mtlib):
     np.testing.assert_array_equal(dm.predict(X, raw_score=True), bm.predict_binned(bins))
 
 
+def test_gpu_device_binning_matches_host(mtlib):
+    """Columns binned on the device equal the host transform: NaNs (with and
+    without a missing bin), categorical codes (kept, unseen, negative, huge,
+    fractional), values on the edges, +-0 and infinities."""
+    rng = np.random.default_rng(21)
+    n = 70_000
+    X = rng.normal(size=(n, 7))
+    X[rng.random(n) < 0.1, 0] = np.nan
+    X[:, 1] = np.round(rng.normal(size=n), 1)  # few distinct levels
+    X[: n // 3, 1] = -0.0
+    X[n // 3 : n // 2, 1] = 0.0
+    X[:, 2] = rng.integers(0, 40, size=n).astype(np.float64)
+    X[::97, 2] = -3.0
+    X[::89, 2] = 1e6  # unseen code
+    X[::83, 2] = 2.5
+    X[::79, 2] = np.nan
+    X[::71, 3] = np.inf
+    X[::73, 3] = -np.inf
+    X[:, 4] = 1.0  # constant
+    X[:, 5] = rng.integers(0, 600, size=n).astype(np.float64)  # more codes than bins
+    X[:, 6] = rng.exponential(size=n)
+    params = {"categorical_feature": "2,5", "max_bin": 63}
+    host = mtlib.bin_dense(X, params)
+    dev = mtlib.bin_dense(X, params, device=True)
+    for a, b in zip(host, dev):
+        np.testing.assert_array_equal(a, b)
+    X[5, 2] = 1e12  # a categorical code beyond int32 is an input error on both paths
+    for device in (False, True):
+        with pytest.raises(mtlib.MojoTreesError):
+            mtlib.bin_dense(X, params, device=device)
+
+
 def test_gpu_round_times_and_stats(mtlib):
     X, y = make_data(17, 20_000, 10, kind="binary")
     bins, mbin, ncat, nb = mtlib.bin_dense(X, {})
