@@ -68,6 +68,7 @@ struct LeafRec {
 // One leaf expansion of the current iteration.
 struct BatchItem {
   int leaf;           // leaf id being expanded
+  int slot;           // its frontier slot
   int child[2];       // leaf ids of the left and right children
   int built_is_left;  // decided from global counts, identical on every device
   int work;           // work-slot index of the built child
@@ -133,10 +134,23 @@ struct TreeHeader {
   int iterations;            // expansion iterations run for this tree
 };
 
+// Compact per-slot view of the frontier the commit kernel loads in one pass:
+// the leaf, whether its children are computed, its gain (-1 when it cannot
+// split) and its children's ids and gains.
+struct FrontierSlot {
+  int leaf;
+  int expanded;
+  int child[2];
+  double gain;
+  double child_gain[2];
+};
+
 struct TreeState {
   TreeHeader hdr;
   Batch batch;
   ChildTotals totals[2 * kMaxBatch];
+  unsigned int child_done[2 * kMaxBatch];  // scan warps finished per child (reset by the folding warp)
+  FrontierSlot front[kMaxLeaves];
   int slot_leaf[kMaxLeaves];  // frontier slot -> leaf id
   LeafRec pool[kMaxPool];
   NodeRec nodes[kMaxNodes];

@@ -330,6 +330,13 @@ __global__ void k_tree_init(TreeState* ts, long long n_local) {
   L.value = 0.0;
   clear_split(L.split);
   ts->slot_leaf[0] = 0;
+  FrontierSlot& F0 = ts->front[0];
+  F0.leaf = 0;
+  F0.expanded = 0;
+  F0.child[0] = F0.child[1] = -1;
+  F0.gain = -1.0;
+  F0.child_gain[0] = F0.child_gain[1] = -1.0;
+  for (int c = 0; c < 2 * kMaxBatch; ++c) ts->child_done[c] = 0;
   clear_node(ts->nodes[0], 0.0, 0);
   Batch& Bt = ts->batch;
   Bt.n_items = 1;
@@ -337,6 +344,7 @@ __global__ void k_tree_init(TreeState* ts, long long n_local) {
   Bt.n_tiles = 0;
   BatchItem& P = Bt.items[0];
   P.leaf = 0;
+  P.slot = 0;
   P.child[0] = 0;
   P.child[1] = -1;
   P.built_is_left = 1;
@@ -797,6 +805,87 @@ __device__ __forceinline__ double deq(long long q, int mode, double inv, double 
   return mode == MODE_FIXED ? (double)q * inv : (double)q / units;
 }
 
+// Called by every (child, feature) warp once its FeatBest is written; the
+// warp that completes child c folds the child's per-feature bests (ascending
+// feature, strict >: the first maximum), applies the leaf guards and writes
+// the child's split, value, global count and local row range, and its entry
+// in the frontier table (the parent's slot, or slot 0 for the root).
+// FeatBest and totals written by other SMs in this launch are read through
+// L2 (__ldcg): L1 is not coherent inside a kernel.
+__device__ void scan_pair_done(TreeState* __restrict__ ts, int c, const FeatBest* __restrict__ fbs,
+                               const int* __restrict__ feats, const RoundScales* __restrict__ sc,
+                               const ScanParams& sp) {
+  const int lane = threadIdx.x & 31;
+  unsigned int last = 0;
+  if (lane == 0) {
+    __threadfence();
+    last = atomicAdd(&ts->child_done[c], 1u) == (unsigned int)(sp.n_active - 1) ? 1u : 0u;
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  __threadfence();
+  const Batch& Bt = ts->batch;
+  const int item = c >> 1, side = c & 1;
+  const bool root = Bt.root != 0;
+  const BatchItem& P = Bt.items[item];
+  const FeatBest* fc = fbs + (long long)c * sp.n_active;
+  double bg = 0.0;
+  int bj = -1;
+  for (int j = lane; j < sp.n_active; j += 32) {
+    const int flags = __ldcg(&fc[j].flags);
+    const double g = __ldcg(&fc[j].gain);
+    if ((flags & 1) && g > bg) {
+      bg = g;
+      bj = j;
+    }
+  }
+  for (int k = 16; k > 0; k >>= 1) {
+    const double og = __shfl_xor_sync(0xffffffffu, bg, k);
+    const int oj = __shfl_xor_sync(0xffffffffu, bj, k);
+    if (oj >= 0 && (bj < 0 || og > bg || (og == bg && oj < bj))) {
+      bg = og;
+      bj = oj;
+    }
+  }
+  if (lane != 0) return;
+  ts->child_done[c] = 0;
+  const int leaf = P.child[side];
+  LeafRec& L = ts->pool[leaf];
+  const long long tg = __ldcg(&ts->totals[c].g), th = __ldcg(&ts->totals[c].h), n_rows = __ldcg(&ts->totals[c].c);
+  SplitRec sr;
+  clear_split(sr);
+  if (bj >= 0 && !(n_rows < 2 * (long long)sp.min_data_in_leaf || n_rows < 2)) {
+    const FeatBest* fb = fc + bj;
+    sr.found = 1;
+    sr.gain = __ldcg(&fb->gain);
+    sr.feature = feats[bj];
+    sr.bin = __ldcg(&fb->bin);
+    const int flags = __ldcg(&fb->flags);
+    sr.default_left = (flags & 2) ? 1 : 0;
+    sr.is_cat = (flags & 4) ? 1 : 0;
+    sr.n_left = __ldcg(&fb->n_left);
+    for (int q = 0; q < 4; ++q) sr.bits[q] = __ldcg(&fb->bits[q]);
+  }
+  L.split = sr;
+  const double gd = sp.mode == MODE_FIXED ? (double)tg * sc->g_inv : (double)tg / sc->g_units;
+  const double hd = sp.mode == MODE_FIXED ? (double)th * sc->h_inv : (double)th / sc->h_units;
+  L.value = -soft_l1(gd, sp.lambda_l1) / (hd + sp.lambda_l2);
+  L.gcount = n_rows;
+  const double fg = (sr.found && sr.gain > 0.0) ? sr.gain : -1.0;
+  if (root) {
+    NodeRec& nd = ts->nodes[L.node];
+    nd.value = L.value;
+    nd.count = n_rows;
+    ts->front[0].gain = fg;
+  } else {
+    const long long nl = (long long)P.cursor_left;
+    L.begin = side == 0 ? P.begin : P.begin + nl;
+    L.count = side == 0 ? nl : P.count - nl;
+    ts->front[P.slot].child[side] = leaf;
+    ts->front[P.slot].child_gain[side] = fg;
+  }
+}
+
 // One warp per (child, active feature), 8 bins per lane: sibling
 // subtraction, exact integer prefix sums, the reference gain per candidate
 // threshold, and a warp arg-max that keeps the serial scan's tie rule (first
@@ -986,6 +1075,7 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan(TreeState* __restri
       }
       out[(long long)c * sp.n_active + j] = fb;
     }
+    scan_pair_done(ts, c, out, feats, sc, sp);
     return;
   }
   const int mb = missing_bin[f];
@@ -1079,6 +1169,7 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan(TreeState* __restri
     }
     out[(long long)c * sp.n_active + j] = fb;
   }
+  scan_pair_done(ts, c, out, feats, sc, sp);
 }
 
 // ---------------------------------------------------------------------------
@@ -1126,12 +1217,8 @@ inline size_t commit_smem_bytes(int num_leaves) {
 }
 
 __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict__ ts,
-                                                           const FeatBest* __restrict__ fbs,
-                                                           const int* __restrict__ feats,
-                                                           const int* __restrict__ missing_bin,
-                                                           const RoundScales* __restrict__ sc, ScanParams sp,
-                                                           CommitParams cp, int* __restrict__ host_done,
-                                                           int host_done_index) {
+                                                           const int* __restrict__ missing_bin, CommitParams cp,
+                                                           int* __restrict__ host_done, int host_done_index) {
   extern __shared__ __align__(16) unsigned char commit_smem[];
   const int L_max = cp.num_leaves;
   double* s_g = reinterpret_cast<double*>(commit_smem);  // frontier gain, -1 when the leaf cannot split
@@ -1153,89 +1240,24 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
   const int n_items = Bt.n_items;
   const bool root = Bt.root != 0;
 
-  // ---- 1. children of this iteration's expansions (one warp per child)
-  for (int c = w; c < 2 * n_items; c += kCommitThreads / 32) {
-    const int item = c >> 1, side = c & 1;
-    if (root && side) continue;
-    const BatchItem& P = Bt.items[item];
-    double bg = 0.0;
-    int bj = -1;
-    for (int j = lane; j < sp.n_active; j += 32) {
-      const FeatBest& fb = fbs[(long long)c * sp.n_active + j];
-      if ((fb.flags & 1) && fb.gain > bg) {
-        bg = fb.gain;
-        bj = j;
-      }
-    }
-    for (int k = 16; k > 0; k >>= 1) {
-      double og = __shfl_xor_sync(0xffffffffu, bg, k);
-      int oj = __shfl_xor_sync(0xffffffffu, bj, k);
-      if (oj >= 0 && (bj < 0 || og > bg || (og == bg && oj < bj))) {
-        bg = og;
-        bj = oj;
-      }
-    }
-    if (lane == 0) {
-      LeafRec& L = ts->pool[P.child[side]];
-      const ChildTotals tot = ts->totals[c];
-      const long long n_rows = tot.c;
-      SplitRec s;
-      clear_split(s);
-      if (bj >= 0 && !(n_rows < 2 * (long long)sp.min_data_in_leaf || n_rows < 2)) {
-        const FeatBest& fb = fbs[(long long)c * sp.n_active + bj];
-        s.found = 1;
-        s.gain = fb.gain;
-        s.feature = feats[bj];
-        s.bin = fb.bin;
-        s.default_left = (fb.flags & 2) ? 1 : 0;
-        s.is_cat = (fb.flags & 4) ? 1 : 0;
-        s.n_left = fb.n_left;
-        for (int q = 0; q < 4; ++q) s.bits[q] = fb.bits[q];
-      }
-      L.split = s;
-      double gd = sp.mode == MODE_FIXED ? (double)tot.g * sc->g_inv : (double)tot.g / sc->g_units;
-      double hd = sp.mode == MODE_FIXED ? (double)tot.h * sc->h_inv : (double)tot.h / sc->h_units;
-      L.value = -soft_l1(gd, sp.lambda_l1) / (hd + sp.lambda_l2);
-      L.gcount = n_rows;
-      if (root) {
-        NodeRec& nd = ts->nodes[L.node];
-        nd.value = L.value;
-        nd.count = n_rows;
-      } else {
-        const long long nl = (long long)P.cursor_left;
-        L.begin = side == 0 ? P.begin : P.begin + nl;
-        L.count = side == 0 ? nl : P.count - nl;
-      }
-    }
-  }
-  __syncthreads();
-  if (!root && t < n_items) {
-    const BatchItem& P = Bt.items[t];
-    LeafRec& L = ts->pool[P.leaf];
-    L.state = 1;
-    L.exp_buf = P.dst_buf;
-  }
-  __syncthreads();
-
-  // ---- 2. the frontier into shared memory
+  // ---- 1. the frontier into shared memory; this iteration's expanded leaves
+  // (whose children the scan just folded) are marked
   const int nl0 = H.n_leaves;
   for (int i = t; i < nl0; i += kCommitThreads) {
-    const int leaf = ts->slot_leaf[i];
-    const LeafRec& L = ts->pool[leaf];
-    s_leaf[i] = leaf;
-    s_g[i] = frontier_gain(L);
-    const bool x = L.state == 1;
-    s_x[i] = x ? 1 : 0;
-    if (x) {
-      s_c0[i] = L.child[0];
-      s_c1[i] = L.child[1];
-      s_cg0[i] = frontier_gain(ts->pool[L.child[0]]);
-      s_cg1[i] = frontier_gain(ts->pool[L.child[1]]);
-    }
+    const FrontierSlot fs = ts->front[i];
+    s_leaf[i] = fs.leaf;
+    s_g[i] = fs.gain;
+    s_x[i] = fs.expanded ? 1 : 0;
+    s_c0[i] = fs.child[0];
+    s_c1[i] = fs.child[1];
+    s_cg0[i] = fs.child_gain[0];
+    s_cg1[i] = fs.child_gain[1];
   }
   __syncthreads();
+  if (!root && t < n_items) s_x[Bt.items[t].slot] = 1;
+  __syncthreads();
 
-  // ---- 3. the pick loop, on one warp over shared memory only
+  // ---- 2. the pick loop, on one warp over shared memory only
   if (w == 0) {
     int nl = nl0;
     int n_commit = 0;
@@ -1286,7 +1308,7 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
   }
   __syncthreads();
 
-  // ---- 4. the commits' writes, one thread each
+  // ---- 3. the commits' writes, one thread each
   const int n_commit = s_ncommit;
   const int nl = s_nl;
   const int nodes0 = H.n_nodes;
@@ -1325,8 +1347,21 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
     H.n_nodes = nodes0 + 2 * n_commit;
     H.n_leaves = nl;
   }
+  // the updated frontier back to its table (children ids and gains only
+  // matter for expanded slots)
+  for (int i = t; i < nl; i += kCommitThreads) {
+    FrontierSlot fs;
+    fs.leaf = s_leaf[i];
+    fs.expanded = s_x[i];
+    fs.child[0] = s_x[i] ? s_c0[i] : -1;
+    fs.child[1] = s_x[i] ? s_c1[i] : -1;
+    fs.gain = s_g[i];
+    fs.child_gain[0] = s_x[i] ? s_cg0[i] : -1.0;
+    fs.child_gain[1] = s_x[i] ? s_cg1[i] : -1.0;
+    ts->front[i] = fs;
+  }
 
-  // ---- 5. next batch
+  // ---- 4. next batch
   if (s_stop) {
     if (t == 0) {
       H.done = 1;
@@ -1373,6 +1408,7 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
         BatchItem& P = Bt.items[idx];
         const long long n_left = s.n_left, n_right = L.gcount - s.n_left;
         P.leaf = leaf;
+        P.slot = slot;
         P.child[0] = pool0 + 2 * idx;
         P.child[1] = pool0 + 2 * idx + 1;
         P.built_is_left = n_left <= n_right ? 1 : 0;

@@ -292,7 +292,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   const long long slot_cells = (long long)F * 3 * B;
   // Leaves expanded per iteration (speculative leaf batching); 1 grows one
   // split per iteration as the reference does.  MOJOTREES_BATCH overrides.
-  int batch_cap = 16;
+  int batch_cap = 32;
   if (const char* e = getenv("MOJOTREES_BATCH")) batch_cap = atoi(e);
   batch_cap = std::max(1, std::min(std::min(batch_cap, kMaxBatch), cfg.num_leaves - 1));
   // Histogram slots: a tree uses at most 1 + (expansions) <= 2 * num_leaves
@@ -549,8 +549,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
                                                     d_sc.p, sp, d_fb.p, work_base);
         timer.end();
         timer.begin(&stats.commit_ms);
-        k_commit<<<1, kCommitThreads, commit_smem, st>>>(d_ts.p, d_fb.p, d_feats.p, d_missing.p, d_sc.p, sp, cp, d_done,
-                                              i % kRing);
+        k_commit<<<1, kCommitThreads, commit_smem, st>>>(d_ts.p, d_missing.p, cp, d_done, i % kRing);
         timer.end();
         MTB_CUDA(cudaEventRecord(iter_ev[i % kRing], st));
         launches += 4;
