@@ -12,8 +12,10 @@ of one fit, after W warm-up rounds of the same fit); inputs are resident in
 HBM (binning and upload precede the first round).  The 1.1 GB row-major bin
 matrix exceeds L2 (126 MB), so no flush is needed between rounds.  `e2e` is
 the same metric through the public C ABI (mojotrees_train_dense) with host
-buffers: host binning, host->device copies and the tree read-back are inside
-the timed wall-clock region.
+buffers: bin fitting (host), the float64 column copies and their binning on
+the device, and the tree read-back are inside the timed wall-clock region.
+The histogram roofline comes from the same timed rounds: CUDA events around
+every histogram launch on the trainer's stream.
 
 Multi-GPU (torchrun, one process per GPU): every GPU holds its own 10M-row
 shard of one global dataset (weak scaling) and the ranks grow one shared
@@ -41,6 +43,10 @@ N_ROWS = 10_000_000
 N_FEAT = 100
 MAX_BIN = 255
 LEAVES = 255
+# DRAM bytes (read + write) per row built, from the ncu capture of the root
+# histogram launch of the 2M-row case (k_hist, 16-bit packed cells):
+# 236.5 MB read + 4.2 MB written for 2,000,000 rows
+HIST_DRAM_BYTES_PER_ROW = (236.53e6 + 4.20e6) / 2.0e6
 METRIC = "boosting rounds/sec (binary logistic, quantized gradients, 10M x 100 per GPU, 255 leaves)"
 UNIT = "rounds/s"
 
@@ -171,7 +177,9 @@ def run_gpu(args):
     # one bin mapper for all shards: fitted on rank 0's rows, shared
     bins, mbin, ncat, nb = mb.bin_dense(X64, {"max_bin": MAX_BIN})
     rounds = args.warmup + args.steps
-    p = params(rounds, extra={"gpu_device_id": local})
+    # CUDA events around every histogram launch (profile_phases) give the
+    # kernel's time inside the timed rounds themselves
+    p = params(rounds, extra={"gpu_device_id": local, "profile_histogram": not args.no_phase_events})
     with ClockSampler(local) as clocks:
         if world > 1:
             import torch
@@ -181,26 +189,29 @@ def run_gpu(args):
                                        missing_bin=mbin, n_categories=ncat)
         else:
             model = mb.train_binned(bins, nb, y, p, missing_bin=mbin, n_categories=ncat)
-    rt = model.round_times_ms()
-    timed = rt[args.warmup:args.warmup + args.steps]
+    rs = model.round_stats()[args.warmup:args.warmup + args.steps]
     st = model.stats()
-    dev_ms = float(np.sum(timed))
+    dev_ms = float(np.sum(rs[:, 0]))
     if world > 1:
         import torch
         t = torch.tensor([dev_ms], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dev_ms = float(t.item())
-    value = world * len(timed) / (dev_ms / 1000.0)
-    # histogram roofline: a second short fit with CUDA events around every histogram launch
-    pm = mb.train_binned(bins, nb, y, params(args.warmup, extra={"gpu_device_id": local, "profile_phases": True}),
-                         missing_bin=mbin, n_categories=ncat) if world == 1 else None
-    hist_gbs = None
-    phases = None
-    if pm is not None:
-        ps = pm.stats()
-        phases = {k: ps[k] for k in ("hist_ms", "partition_ms", "scan_ms", "commit_ms", "grad_ms", "hist_bytes",
-                                      "iterations", "expansions", "rounds")}
-        hist_gbs = ps["hist_bytes"] / (ps["hist_ms"] / 1000.0) / 1e9 if ps["hist_ms"] > 0 else None
+    value = world * len(rs) / (dev_ms / 1000.0)
+    # histogram roofline over the timed rounds (this rank)
+    hist_ms = float(np.sum(rs[:, 1]))
+    hist_launches = float(np.sum(rs[:, 2]))
+    hist_rows = float(np.sum(rs[:, 3]))
+    hist_bytes = hist_rows * (N_FEAT + 2)
+    hist_gbs = hist_bytes / (hist_ms / 1000.0) / 1e9 if hist_ms > 0 else None
+    per_round = 1.0 / max(1, st["rounds"])
+    phases = {"hist_ms": st["hist_ms"] * per_round}
+    phases.update({"iterations_per_tree": st["iterations"] * per_round,
+                   "expansions_per_tree": st["expansions"] * per_round,
+                   "hist_launches_timed": hist_launches, "hist_rows_timed": hist_rows})
+    smem_peak = mb.shared_atomic_peak() if hist_ms > 0 else None
+    # useful shared atomics of the histogram: (g+count word, h word) per row and feature
+    smem_achieved = hist_rows * N_FEAT * 2 / (hist_ms / 1000.0) if hist_ms > 0 else None
     peak, peak_kind = measured_peak()
     e2e = None
     if world == 1:
@@ -208,9 +219,9 @@ def run_gpu(args):
         m2 = mb.train_dense(X64, y, params(args.steps, extra={"gpu_device_id": local}))
         e2e_s = time.perf_counter() - t0
         s2 = m2.stats()
-        # copied to the device per fit: uint8 bins (F x N), labels and initial
-        # scores (float64); read back per round: the tree's node table
-        h2d = N_ROWS * N_FEAT + 8 * N_ROWS + 8 * N_ROWS
+        # copied to the device per fit; read back per round: the tree's node table
+        # float64 columns (binned on the device), labels, initial scores
+        h2d = 8 * N_ROWS * N_FEAT + 8 * N_ROWS + 8 * N_ROWS
         e2e = {"value": m2.num_trees / e2e_s, "unit": UNIT,
                "h2d_bytes_per_step": h2d / max(1, args.steps),
                "d2h_bytes_per_step": 88 * (2 * LEAVES - 1), "seconds": e2e_s, "rounds": int(m2.num_trees),
@@ -220,20 +231,29 @@ def run_gpu(args):
     if rank != 0:
         return
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": len(timed),
-        "warmup": args.warmup, "ms_per_step": dev_ms / max(1, len(timed)), "higher_is_better": True,
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": len(rs),
+        "warmup": args.warmup, "ms_per_step": dev_ms / max(1, len(rs)), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8-grad/int32-hist",
         "data": "synthetic",
         "config": {"workload": "configs[1]: binary logistic, quantized int8 gradients, 10M x 100 per GPU, "
                                "max_bin 255, num_leaves 255", "rows_per_gpu": N_ROWS, "features": N_FEAT,
                    "l2": "inputs (1.1 GB row-major bins) larger than L2; no flush", "parallelism": f"dp{world}"},
         "roofline": {"bound": "hbm", "achieved": hist_gbs, "peak": peak, "unit": "GB/s",
-                     "frac": (hist_gbs / peak) if hist_gbs else None, "traffic": None,
+                     "frac": (hist_gbs / peak) if hist_gbs else None,
+                     "traffic": (HIST_DRAM_BYTES_PER_ROW * hist_rows / hist_launches) if hist_launches else None,
                      "peak_source": peak_kind, "kernel": "k_hist",
-                     "algorithmic_bytes": "rows read by histogram builds x (100 bin bytes + 2 gradient bytes)"},
-        "phase_ms_profiled_fit": phases,
+                     "algorithmic_bytes": "per launch: rows of the built children x (100 bin bytes + 2 gradient "
+                                          "bytes); achieved = their sum over the timed rounds / the summed "
+                                          "CUDA-event time of the histogram launches",
+                     "traffic_source": "ncu dram read+write bytes per row of the k_hist capture "
+                                       "(profiles/k_hist_quant16_root_2M.txt) x rows per launch",
+                     "shared_atomics": {"achieved": smem_achieved, "peak": smem_peak, "unit": "lane atomics/s",
+                                        "frac": (smem_achieved / smem_peak) if smem_achieved and smem_peak
+                                        else None,
+                                        "peak_source": "mojotrees_b200_shared_atomic_peak on this GPU"}},
+        "phase_ms_per_round": phases,
         "e2e": e2e,
-        "gpu_launches": int(st["kernel_launches"] * len(timed) / max(1, st["rounds"])),
+        "gpu_launches": int(np.sum(rs[:, 4])),
         "clocks": clocks.summary(),
     }
     if not args.no_cpu_baseline and world == 1:
@@ -251,6 +271,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-phase-events", action="store_true",
+                    help="no CUDA events around the histogram launches (no roofline)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":

@@ -142,6 +142,13 @@ int32_t mojotrees_b200_bin_dense_gpu(const double *data, int64_t n_rows, int64_t
                                      const char *parameters, uint8_t *out_bins, int32_t *out_missing_bin,
                                      int32_t *out_n_categories, int32_t *out_n_bins, MojoTreesError *error);
 
+/* Measured roofline of the histogram kernel's inner loop: the rate (lane
+ * atomics per second, whole GPU) at which the SMs sustain conflict-free
+ * red.shared.add.u32 in the histogram's shared-memory layout and launch
+ * geometry, with no global traffic.  Runs a few short kernels on the current
+ * device. */
+int32_t mojotrees_b200_shared_atomic_peak(double *out_lane_atomics_per_s, MojoTreesError *error);
+
 /* Raw-score prediction on pre-binned feature-major data (any model). */
 int32_t mojotrees_b200_predict_binned_u8(const MojoTreesModel *model, const uint8_t *bins, int64_t n_rows,
                                          int64_t n_features, double *out_values, int64_t out_len,
@@ -180,6 +187,15 @@ int32_t mojotrees_b200_train_stats(const MojoTreesModel *model, double *out_valu
  * with CUDA events on the trainer's stream (one round = the K trees of a
  * multiclass iteration).  *out_n receives the number of rounds. */
 int32_t mojotrees_b200_round_times(const MojoTreesModel *model, double *out_values, int64_t out_len,
+                                   int64_t *out_n, MojoTreesError *error);
+
+/* Per-round statistics of the fit, 5 doubles per round (row-major, *out_n =
+ * rounds): device time (ms, CUDA events), histogram-kernel time (ms; CUDA
+ * events around every histogram launch, only when the fit ran with
+ * profile_phases=true, else 0), histogram launches, rows read by histogram
+ * builds (the root and the smaller child of every split), kernels launched.
+ * out_values may be NULL to query the count. */
+int32_t mojotrees_b200_round_stats(const MojoTreesModel *model, double *out_values, int64_t out_len,
                                    int64_t *out_n, MojoTreesError *error);
 
 /* Data-parallel training (one process per GPU, rows sharded): a fresh

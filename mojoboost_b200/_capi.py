@@ -52,12 +52,14 @@ SIGNATURES = {
     "mojotrees_b200_train_binned_u8": (_I32, [_P, _I64, _I64, _I32, _P, _P, _P, _P, ctypes.c_char_p, _P, _P]),
     "mojotrees_b200_bin_dense": (_I32, [_P, _I64, _I64, ctypes.c_char_p, _P, _P, _P, _P, _P]),
     "mojotrees_b200_bin_dense_gpu": (_I32, [_P, _I64, _I64, ctypes.c_char_p, _P, _P, _P, _P, _P]),
+    "mojotrees_b200_shared_atomic_peak": (_I32, [_P, _P]),
     "mojotrees_b200_predict_binned_u8": (_I32, [_P, _P, _I64, _I64, _P, _I64, _P]),
     "mojotrees_b200_tree_nodes": (_I32, [_P, _I64, _P, _P, _P, _P, _I64, _P, _P]),
     "mojotrees_b200_base_scores": (_I32, [_P, _P, _I64, _P]),
     "mojotrees_b200_training_scores": (_I32, [_P, _P, _I64, _P]),
     "mojotrees_b200_train_stats": (_I32, [_P, _P, _I64, _P, _P]),
     "mojotrees_b200_round_times": (_I32, [_P, _P, _I64, _P, _P]),
+    "mojotrees_b200_round_stats": (_I32, [_P, _P, _I64, _P, _P]),
     "mojotrees_b200_nccl_unique_id": (_I32, [_P, _P]),
     "mojotrees_b200_histogram_u8": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _I32, _P, _P]),
     "mojotrees_b200_histogram_u8_noalloc": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _I32, _P, _P, _P]),
@@ -223,6 +225,15 @@ class Model:
         e.check(lib().mojotrees_b200_train_stats(self.h, _ptr(out), out.size, ctypes.byref(n), e.h))
         return dict(zip(STAT_NAMES, out[: n.value].tolist()))
 
+    def round_stats(self):
+        """Per round: (device ms, histogram ms, histogram launches, histogram rows, kernel launches)."""
+        n = ctypes.c_int64(0)
+        e = _Err()
+        e.check(lib().mojotrees_b200_round_stats(self.h, None, 0, ctypes.byref(n), e.h))
+        out = np.zeros((n.value, 5), np.float64)
+        e.check(lib().mojotrees_b200_round_stats(self.h, _ptr(out), out.size, ctypes.byref(n), e.h))
+        return out
+
     def round_times_ms(self):
         n = ctypes.c_int64(0)
         e = _Err()
@@ -341,6 +352,14 @@ def bin_dense(X, params=None, device=False):
     e.check(fn(Xc.ctypes.data_as(ctypes.c_void_p), n, f, params_string(params), _ptr(bins), _ptr(mb), _ptr(nc),
                ctypes.byref(nb), e.h))
     return bins, mb, nc, nb.value
+
+
+def shared_atomic_peak():
+    """Lane atomics per second the GPU sustains in the histogram's shared-memory layout."""
+    v = ctypes.c_double(0.0)
+    e = _Err()
+    e.check(lib().mojotrees_b200_shared_atomic_peak(ctypes.byref(v), e.h))
+    return v.value
 
 
 def gpu_available():

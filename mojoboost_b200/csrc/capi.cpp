@@ -112,6 +112,7 @@ const std::vector<std::pair<std::string, std::vector<std::string>>>& param_table
       {"num_threads", {"num_thread", "nthread", "nthreads", "n_jobs"}},
       {"keep_training_scores", {}},
       {"profile_phases", {}},
+      {"profile_histogram", {}},
   };
   return t;
 }
@@ -229,6 +230,7 @@ TrainConfig parse_config(const char* params, bool need_training) {
       if (lower(v) != "bagging") throw mtb::Unsupported("data_sample_strategy '" + v + "' (GOSS) is not covered by the device path");
     } else if (k == "keep_training_scores") c.keep_training_scores = to_bool(k, v);
     else if (k == "profile_phases") c.profile_phases = to_bool(k, v);
+    else if (k == "profile_histogram") c.profile_histogram = to_bool(k, v);
     else if (k == "verbosity" || k == "seed" || k == "num_threads") {
       to_int(k, v);
     }
@@ -499,6 +501,31 @@ int32_t mojotrees_b200_round_times(const MojoTreesModel* model, double* out_valu
         if (out_values) {
           int64_t n = std::min<int64_t>(out_len, (int64_t)r.size());
           for (int64_t i = 0; i < n; ++i) out_values[i] = r[i];
+        }
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+
+int32_t mojotrees_b200_round_stats(const MojoTreesModel* model, double* out_values, int64_t out_len, int64_t* out_n,
+                                   MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!model || !out_n) throw InvalidArgument("null pointer argument");
+        const mtb::TrainStats& s = model->m.stats;
+        const size_t n = s.round_ms.size();
+        *out_n = (int64_t)n;
+        if (out_values) {
+          auto at = [](const std::vector<double>& v, size_t i) { return i < v.size() ? v[i] : 0.0; };
+          for (size_t i = 0; i < n && (int64_t)(5 * i + 4) < out_len; ++i) {
+            out_values[5 * i + 0] = s.round_ms[i];
+            out_values[5 * i + 1] = at(s.round_hist_ms, i);
+            out_values[5 * i + 2] = at(s.round_hist_launches, i);
+            out_values[5 * i + 3] = at(s.round_hist_rows, i);
+            out_values[5 * i + 4] = at(s.round_launches, i);
+          }
         }
         return MOJOTREES_OK;
       },

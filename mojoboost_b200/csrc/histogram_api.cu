@@ -218,3 +218,85 @@ extern "C" int32_t mojotrees_b200_histogram_u8_noalloc(const uint8_t* bins_rm, i
     return MOJOTREES_ERROR_TRAINING;
   }
 }
+
+// ---------------------------------------------------------------------------
+// Shared-memory atomic throughput probe: the roofline of the histogram kernel.
+//
+// The histogram's inner loop is one red.shared.add.u32 per (row, feature,
+// plane) into a bank-per-lane layout (no bank conflicts, no same-address
+// collisions in an instruction).  This probe issues the same instruction
+// pattern at the same geometry (1024 threads, the same shared memory per
+// CTA, one CTA per SM) with no global traffic, and reports the rate the SMs
+// sustain: lane-atomics per second over the whole GPU.
+// ---------------------------------------------------------------------------
+namespace mtb {
+namespace {
+
+constexpr int kProbeWords = 48 * 1024;  // 192 KB, the HL_QUANT16 histogram's shared memory
+
+__global__ void __launch_bounds__(1024) k_smem_red_probe(int iters, unsigned int* sink) {
+  extern __shared__ __align__(16) unsigned int probe_smem[];
+  for (int i = threadIdx.x; i < kProbeWords; i += blockDim.x) probe_smem[i] = 0u;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const uint32_t base = (uint32_t)__cvta_generic_to_shared(probe_smem) + 4u * lane;
+  uint32_t x = 2654435761u * (threadIdx.x + 1) + blockIdx.x;
+  for (int it = 0; it < iters; ++it) {
+    x = x * 1664525u + 1013904223u;  // pseudo-random bins, as rows bring them
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t a = base + (((x >> (8 * j)) & 0xffu) << 7);
+      shared_red_add(a + j * 32768u, 1u);
+      shared_red_add(a + 131072u + (j >> 1) * 32768u, 2u);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) atomicAdd(sink, probe_smem[blockIdx.x & 1023]);
+}
+
+}  // namespace
+}  // namespace mtb
+
+extern "C" int32_t mojotrees_b200_shared_atomic_peak(double* out_lane_atomics_per_s, MojoTreesError* error) {
+  using namespace mtb;
+  capi_clear_error(error);
+  try {
+    if (!out_lane_atomics_per_s) throw std::invalid_argument("null pointer argument");
+    if (cuda_device_count() < 1) throw Unsupported("no CUDA device is available");
+    int dev = 0, n_sm = 0;
+    MTB_CUDA(cudaGetDevice(&dev));
+    MTB_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+    const size_t smem = sizeof(unsigned int) * kProbeWords;
+    MTB_CUDA(cudaFuncSetAttribute(k_smem_red_probe, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    DevMem sink(sizeof(unsigned int));
+    const int iters = 4096;
+    cudaEvent_t a, b;
+    MTB_CUDA(cudaEventCreate(&a));
+    MTB_CUDA(cudaEventCreate(&b));
+    float best = 1e30f;
+    for (int rep = 0; rep < 4; ++rep) {  // the first launch warms up
+      MTB_CUDA(cudaEventRecord(a, 0));
+      k_smem_red_probe<<<n_sm, 1024, smem, 0>>>(iters, (unsigned int*)sink.p);
+      MTB_CUDA(cudaEventRecord(b, 0));
+      MTB_CUDA(cudaEventSynchronize(b));
+      float ms = 0.f;
+      MTB_CUDA(cudaEventElapsedTime(&ms, a, b));
+      if (rep > 0 && ms < best) best = ms;
+    }
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    MTB_CUDA(cudaGetLastError());
+    const double lane_atomics = (double)n_sm * 1024.0 * iters * 8.0;
+    *out_lane_atomics_per_s = lane_atomics / (best * 1e-3);
+    return MOJOTREES_OK;
+  } catch (const std::invalid_argument& e) {
+    capi_set_error(error, e.what());
+    return MOJOTREES_ERROR_INVALID_ARGUMENT;
+  } catch (const Unsupported& e) {
+    capi_set_error(error, e.what());
+    return MOJOTREES_ERROR_UNSUPPORTED;
+  } catch (const std::exception& e) {
+    capi_set_error(error, e.what());
+    return MOJOTREES_ERROR_TRAINING;
+  }
+}

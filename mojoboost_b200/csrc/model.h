@@ -51,7 +51,8 @@ struct TrainConfig {
   int quant_seed = 11;
   int gpu_device_id = -1;      // -1: current device
   bool keep_training_scores = false;
-  bool profile_phases = false;
+  bool profile_phases = false;    // CUDA events around every kernel phase
+  bool profile_histogram = false; // CUDA events around the histogram launches only
   BinningParams binning;
 };
 
@@ -72,6 +73,9 @@ struct TrainStats {
   int kernel_launches = 0;          // kernels this library launched
   int rounds = 0;
   std::vector<double> round_ms;     // device time of each round (CUDA events on the trainer's stream)
+  // per round: histogram-kernel time (profile_phases), histogram launches,
+  // rows read by histogram builds, kernels launched
+  std::vector<double> round_hist_ms, round_hist_launches, round_hist_rows, round_launches;
 };
 
 struct Model {

@@ -66,37 +66,42 @@ struct DevBuf {
   ~DevBuf() { free(); }
 };
 
+// CUDA events around launches (profile_phases): a pool of events reused
+// across trees, so timing adds two event records per launch and nothing else.
 struct EventTimer {
   bool on;
   cudaStream_t s;
-  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev;
-  double* acc;
+  std::vector<cudaEvent_t> pool;
   std::vector<double*> accs;
-  EventTimer(bool enabled, cudaStream_t st) : on(enabled), s(st), acc(nullptr) {}
+  size_t used = 0;
+  EventTimer(bool enabled, cudaStream_t st) : on(enabled), s(st) {}
+  ~EventTimer() {
+    for (auto e : pool) cudaEventDestroy(e);
+  }
   void begin(double* target) {
     if (!on) return;
-    cudaEvent_t a, b;
-    cudaEventCreate(&a);
-    cudaEventCreate(&b);
-    cudaEventRecord(a, s);
-    ev.push_back({a, b});
+    while (pool.size() < used + 2) {
+      cudaEvent_t e;
+      cudaEventCreate(&e);
+      pool.push_back(e);
+    }
+    cudaEventRecord(pool[used], s);
     accs.push_back(target);
   }
   void end() {
     if (!on) return;
-    cudaEventRecord(ev.back().second, s);
+    cudaEventRecord(pool[used + 1], s);
+    used += 2;
   }
   void collect() {
-    for (size_t i = 0; i < ev.size(); ++i) {
+    for (size_t i = 0; i < accs.size(); ++i) {
       float ms = 0.f;
-      cudaEventSynchronize(ev[i].second);
-      cudaEventElapsedTime(&ms, ev[i].first, ev[i].second);
+      cudaEventSynchronize(pool[2 * i + 1]);
+      cudaEventElapsedTime(&ms, pool[2 * i], pool[2 * i + 1]);
       *accs[i] += ms;
-      cudaEventDestroy(ev[i].first);
-      cudaEventDestroy(ev[i].second);
     }
-    ev.clear();
     accs.clear();
+    used = 0;
   }
 };
 
@@ -383,6 +388,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   std::vector<HostNode> nodes_host((size_t)M);
   TreeHeader hdr;
   EventTimer timer(cfg.profile_phases, st);
+  EventTimer hist_timer(cfg.profile_phases || cfg.profile_histogram, st);
 
   ScanParams sp;
   sp.B = B;
@@ -401,10 +407,10 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   auto t_fit = std::chrono::steady_clock::now();
   int launches = 0;
   auto hist = [&]() {
-    timer.begin(&stats.hist_ms);
+    hist_timer.begin(&stats.hist_ms);
     launch_hist(hl, st, batch_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p, d_pairs1.p,
                 d_hist.p, slot_cells, work_base);
-    timer.end();
+    hist_timer.end();
   };
   // the built children's cells summed over every device's rows (exact int32)
   auto reduce_work = [&]() {
@@ -428,6 +434,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     MTB_CUDA(cudaEventRecord(e, st));
   };
   mark_round();
+  std::vector<size_t> round_trees;  // trees after each round
   for (int it = 0; it < cfg.num_iterations; ++it) {
     if (K > 1) {
       k_softmax<<<grid256, 256, 0, st>>>(d_raw.p, d_prob.p, N, K);
@@ -565,6 +572,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       MTB_CUDA(cudaMemcpyAsync(nodes_host.data(), d_ts.p->nodes, sizeof(HostNode) * M, cudaMemcpyDeviceToHost, st));
       MTB_CUDA(cudaStreamSynchronize(st));
       timer.collect();
+      hist_timer.collect();
       if (hdr.error || !hdr.done) throw std::runtime_error("device trainer reported an internal error");
       stats.iterations += hdr.iterations;
       stats.expansions += (hdr.n_pool - 1) / 2;
@@ -576,6 +584,10 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     }
     stats.rounds++;
     mark_round();
+    stats.round_hist_ms.push_back(stats.hist_ms);  // cumulative; differenced below
+    stats.round_hist_launches.push_back((double)stats.hist_launches);
+    stats.round_launches.push_back((double)launches);
+    round_trees.push_back(model.trees.size());
     if (!progress) {
       // boosting.mojo:2898-2907 / :4153-4162: a round that grew nothing ends the fit
       model.trees.resize(first_tree);
@@ -598,6 +610,21 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       if (nd.feature >= 0) stats.hist_rows += (double)std::min(tr[nd.left].count, tr[nd.right].count);
   }
   stats.hist_bytes = stats.hist_rows * (double)(F + (mode == MODE_QUANT ? 2 : 8));
+  for (size_t r = stats.round_hist_ms.size(); r-- > 1;) {
+    stats.round_hist_ms[r] -= stats.round_hist_ms[r - 1];
+    stats.round_hist_launches[r] -= stats.round_hist_launches[r - 1];
+    stats.round_launches[r] -= stats.round_launches[r - 1];
+  }
+  stats.round_hist_rows.assign(round_trees.size(), 0.0);
+  for (size_t r = 0; r < round_trees.size(); ++r) {
+    const size_t t0 = r ? round_trees[r - 1] : 0;
+    for (size_t t = t0; t < std::min(round_trees[r], model.trees.size()); ++t) {
+      const auto& tr = model.trees[t];
+      stats.round_hist_rows[r] += (double)tr[0].count;
+      for (const auto& nd : tr)
+        if (nd.feature >= 0) stats.round_hist_rows[r] += (double)std::min(tr[nd.left].count, tr[nd.right].count);
+    }
+  }
   if (cfg.keep_training_scores) {
     model.train_scores.resize((size_t)N * K);
     MTB_CUDA(cudaMemcpy(model.train_scores.data(), d_raw.p, sizeof(double) * N * K, cudaMemcpyDeviceToHost));
