@@ -1,11 +1,11 @@
-// Device-side state and kernels of the B200 GBDT training path.
+// Device-side state of the B200 GBDT training path.
 //
-// One tree is grown entirely from device-resident state.  The host launches a
-// fixed sequence of kernels per split (pick -> partition -> histogram ->
-// subtract+scan -> finish) whose grids do not depend on any device value, so
-// no host synchronisation is needed inside a tree and the sequence can be
-// replayed as a CUDA graph.  Every kernel reads what it needs (the leaf range,
-// the split being applied, which histogram slot to fill) from `TreeState`.
+// One tree is grown entirely from device-resident state.  Each iteration is
+// four launches whose grids do not depend on any device value (partition ->
+// histogram -> subtract+scan -> commit); every kernel reads what it needs (the
+// batch of leaves being expanded, their ranges and splits, which histogram
+// slots to fill) from `TreeState`, and the commit kernel lays out the next
+// batch.  The host learns that a tree is done through mapped host memory.
 //
 // HBM layout (see the trainer for sizes):
 //   bins_rm   uint8 [N][Fp]  row-major, Fp = F rounded up to 16 (histograms)
@@ -14,13 +14,15 @@
 //                            range [begin, begin+count) of one of them
 //   pairs[2]  quantized (g,h) per row, kept in the same order as rows:
 //             QUANT mode int16 (int8 g | uint8 h << 8), FIXED mode int2
-//   hist      int64 [slots][F][3][B]  integer (g, h, count) cells per leaf
+//   hist      int32 [slots][F][3][B]  integer (g, h, count) cells per leaf,
+//             then one work slot per batch item
 //
 // Reference map: the per-leaf histogram is gpu_active_rows.mojo:3903
 // (_range_hist_atomic_kernel); the stable partition :1054-1707; sibling
-// subtraction gpu_leaf_batching.mojo:1364 / histogram.mojo:3747; the split
-// scan split.mojo:601-1360 (restated in integer prefix sums, exact); leaf pick
-// growth_policy.mojo:659-677; tree grower tree.mojo:3767-4256.
+// subtraction gpu_leaf_batching.mojo:1364 / histogram.mojo:3747; leaf batching
+// gpu_leaf_batching.mojo:2438; the split scan split.mojo:601-1360 (restated in
+// integer prefix sums, exact); leaf pick growth_policy.mojo:659-677; tree
+// grower tree.mojo:3767-4256.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>

@@ -547,16 +547,32 @@ struct BinWord<4> {
   }
 };
 
+#ifndef MTB_HIST_RED_CLOBBER
+#define MTB_HIST_RED_CLOBBER 0
+#endif
+#ifndef MTB_HIST_PIPELINE
+#define MTB_HIST_PIPELINE 0
+#endif
 #ifndef MTB_HIST_UNROLL
 #define MTB_HIST_UNROLL 8
 #endif
 constexpr int kHistUnroll = MTB_HIST_UNROLL;  // bin loads in flight per warp (divides 32)
-constexpr int kHistThreads = 1024;
+#ifndef MTB_HIST_THREADS
+#define MTB_HIST_THREADS 1024
+#endif
+constexpr int kHistThreads = MTB_HIST_THREADS;
 constexpr int kHistBinsPad = 256;  // bins per feature in the shared-memory layout
 
-// Atomic add to a shared-memory word whose result is not needed.
+// Atomic add to a shared-memory word whose result is not needed.  No memory
+// clobber: the cells are read only after a block or cluster barrier (which
+// orders them), and without it the compiler may issue the next rows' global
+// loads ahead of these atomics.
 __device__ __forceinline__ void shared_red_add(uint32_t addr, unsigned int v) {
+#if MTB_HIST_RED_CLOBBER
   asm volatile("red.shared.add.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+#else
+  asm volatile("red.shared.add.u32 [%0], %1;" ::"r"(addr), "r"(v));
+#endif
 }
 
 // One cluster accumulates rows [seg_b, seg_b + seg_n) of one item's built
@@ -657,6 +673,34 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
       if (c0 + stride < pe) fetch(c0 + stride, nr, na0, na1);
       if (pe - c0 >= 32) {
         // full chunk: no bounds tests
+#if MTB_HIST_PIPELINE
+        // the next group's bin loads are issued before this group's atomics
+        unsigned int bw[U], nb[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int r = __shfl_sync(0xffffffffu, cr, u);
+          bw[u] = BinWord<NPL>::load(bcol + (size_t)(unsigned int)r * (unsigned int)Fp);
+        }
+#pragma unroll
+        for (int u0 = 0; u0 < 32; u0 += U) {
+          if (u0 + U < 32) {
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+              const int r = __shfl_sync(0xffffffffu, cr, u0 + U + u);
+              nb[u] = BinWord<NPL>::load(bcol + (size_t)(unsigned int)r * (unsigned int)Fp);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const unsigned int x0 = __shfl_sync(0xffffffffu, ca0, u0 + u);
+            const unsigned int x1 =
+                (MODE == MODE_FIXED && CONST_H) ? 1u : __shfl_sync(0xffffffffu, ca1, u0 + u);
+            add_row(bw[u], x0, x1);
+          }
+#pragma unroll
+          for (int u = 0; u < U; ++u) bw[u] = nb[u];
+        }
+#else
 #pragma unroll
         for (int u0 = 0; u0 < 32; u0 += U) {
           unsigned int bw[U];
@@ -673,6 +717,7 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
             add_row(bw[u], x0, x1);
           }
         }
+#endif
       } else {
         const int n_in = (int)(pe - c0);
         for (int u = 0; u < n_in; ++u) {
