@@ -49,17 +49,19 @@ struct SplitRec {
 };
 
 constexpr int kMaxBatch = 32;                              // leaves expanded per iteration
-constexpr int kMaxPool = 4 * kMaxLeaves;  // leaf records of one tree (1 + 2 per expansion)
+// leaf records of one tree: 1 + 2 per expansion, expansions bounded by the
+// histogram slots (2 * num_leaves + batch)
+constexpr int kMaxPool = 4 * kMaxLeaves + 2 * kMaxBatch + 2;
 
 // One leaf of the tree being grown (frontier leaves, speculative children).
 struct LeafRec {
   int node;         // node id once the leaf is part of the tree, else -1
+  int parent;       // leaf record of the parent, -1 for the root
   int buf;          // ping-pong row buffer holding the leaf's rows
   int hist_slot;    // histogram slot, -1 when none
   int state;        // 0 leaf, 1 expanded (children computed, split not committed), 2 split committed
   int child[2];     // leaf ids of the children once expanded
   int exp_buf;      // buffer holding this leaf's rows after its expansion
-  int pad;
   long long begin;  // local range [begin, begin + count) in rows[buf]
   long long count;  // local rows (this device)
   long long gcount; // global rows (histogram count)
@@ -70,7 +72,6 @@ struct LeafRec {
 // One leaf expansion of the current iteration.
 struct BatchItem {
   int leaf;           // leaf id being expanded
-  int slot;           // its frontier slot
   int child[2];       // leaf ids of the left and right children
   int built_is_left;  // decided from global counts, identical on every device
   int work;           // work-slot index of the built child
@@ -134,17 +135,17 @@ struct TreeHeader {
   int n_pool;                // leaf records used
   int n_hist;                // histogram slots used
   int iterations;            // expansion iterations run for this tree
+  int n_table;               // entries of the final row -> leaf table
+  int pad;
 };
 
-// Compact per-slot view of the frontier the commit kernel loads in one pass:
-// the leaf, whether its children are computed, its gain (-1 when it cannot
-// split) and its children's ids and gains.
-struct FrontierSlot {
-  int leaf;
-  int expanded;
-  int child[2];
+// Compact per-leaf view the commit kernel loads in one pass: the leaf's gain
+// (-1 when it cannot split), whether its children are computed, and their ids.
+struct LeafInfo {
   double gain;
-  double child_gain[2];
+  int child[2];
+  int expanded;
+  int pad;
 };
 
 struct TreeState {
@@ -152,7 +153,7 @@ struct TreeState {
   Batch batch;
   ChildTotals totals[2 * kMaxBatch];
   unsigned int child_done[2 * kMaxBatch];  // scan warps finished per child (reset by the folding warp)
-  FrontierSlot front[kMaxLeaves];
+  LeafInfo info[kMaxPool];
   int slot_leaf[kMaxLeaves];  // frontier slot -> leaf id
   LeafRec pool[kMaxPool];
   NodeRec nodes[kMaxNodes];

@@ -319,6 +319,7 @@ __global__ void k_tree_init(TreeState* ts, long long n_local) {
   H.iterations = 0;
   LeafRec& L = ts->pool[0];
   L.node = 0;
+  L.parent = -1;
   L.buf = 0;
   L.hist_slot = 0;
   L.state = 0;
@@ -330,12 +331,11 @@ __global__ void k_tree_init(TreeState* ts, long long n_local) {
   L.value = 0.0;
   clear_split(L.split);
   ts->slot_leaf[0] = 0;
-  FrontierSlot& F0 = ts->front[0];
-  F0.leaf = 0;
-  F0.expanded = 0;
-  F0.child[0] = F0.child[1] = -1;
-  F0.gain = -1.0;
-  F0.child_gain[0] = F0.child_gain[1] = -1.0;
+  LeafInfo& I0 = ts->info[0];
+  I0.gain = -1.0;
+  I0.child[0] = I0.child[1] = -1;
+  I0.expanded = 0;
+  I0.pad = 0;
   for (int c = 0; c < 2 * kMaxBatch; ++c) ts->child_done[c] = 0;
   clear_node(ts->nodes[0], 0.0, 0);
   Batch& Bt = ts->batch;
@@ -344,7 +344,6 @@ __global__ void k_tree_init(TreeState* ts, long long n_local) {
   Bt.n_tiles = 0;
   BatchItem& P = Bt.items[0];
   P.leaf = 0;
-  P.slot = 0;
   P.child[0] = 0;
   P.child[1] = -1;
   P.built_is_left = 1;
@@ -853,8 +852,8 @@ __device__ __forceinline__ double deq(long long q, int mode, double inv, double 
 // Called by every (child, feature) warp once its FeatBest is written; the
 // warp that completes child c folds the child's per-feature bests (ascending
 // feature, strict >: the first maximum), applies the leaf guards and writes
-// the child's split, value, global count and local row range, and its entry
-// in the frontier table (the parent's slot, or slot 0 for the root).
+// the child's split, value, global count and local row range, and its gain
+// in the per-leaf table.
 // FeatBest and totals written by other SMs in this launch are read through
 // L2 (__ldcg): L1 is not coherent inside a kernel.
 __device__ void scan_pair_done(TreeState* __restrict__ ts, int c, const FeatBest* __restrict__ fbs,
@@ -916,18 +915,20 @@ __device__ void scan_pair_done(TreeState* __restrict__ ts, int c, const FeatBest
   const double hd = sp.mode == MODE_FIXED ? (double)th * sc->h_inv : (double)th / sc->h_units;
   L.value = -soft_l1(gd, sp.lambda_l1) / (hd + sp.lambda_l2);
   L.gcount = n_rows;
-  const double fg = (sr.found && sr.gain > 0.0) ? sr.gain : -1.0;
+  LeafInfo& I = ts->info[leaf];
+  I.gain = (sr.found && sr.gain > 0.0) ? sr.gain : -1.0;
+  I.child[0] = I.child[1] = -1;
+  I.expanded = 0;
+  I.pad = 0;
   if (root) {
     NodeRec& nd = ts->nodes[L.node];
     nd.value = L.value;
     nd.count = n_rows;
-    ts->front[0].gain = fg;
   } else {
     const long long nl = (long long)P.cursor_left;
     L.begin = side == 0 ? P.begin : P.begin + nl;
     L.count = side == 0 ? nl : P.count - nl;
-    ts->front[P.slot].child[side] = leaf;
-    ts->front[P.slot].child_gain[side] = fg;
+    ts->info[P.leaf].child[side] = leaf;
   }
 }
 
@@ -1241,104 +1242,133 @@ struct CommitParams {
   int tile_rows;       // rows per partition tile
 };
 
-// (gain, slot) order of the pick: larger gain first, then lower slot.
-__device__ __forceinline__ bool pick_before(double ga, int sa, double gb, int sb) {
-  if (sb < 0) return sa >= 0;
-  if (sa < 0) return false;
-  return ga > gb || (ga == gb && sa < sb);
-}
 
 __device__ __forceinline__ double frontier_gain(const LeafRec& L) {
   return (L.split.found && L.split.gain > 0.0) ? L.split.gain : -1.0;
 }
 
-// Per frontier slot shared-memory bytes of k_commit (dynamic, sized by the
-// leaf budget): gain, children's gains, leaf id, children's ids, commit
-// list (slot, leaf), expanded flag.
-constexpr int kCommitSlotBytes = 3 * 8 + 5 * 4 + 1;
+// Shared memory of k_commit (dynamic): per leaf of the budget, the frontier
+// (slot -> leaf, gain), the commit list (slot, leaf) and the simulated
+// frontier (leaf, gain); then the per-leaf table for the first leaf records
+// (records beyond it are read from global memory).
+constexpr int kCommitSlotBytes = 8 + 4 + 4 + 4 + 4 + 8 + 4 + 4;
+
+// Leaf records whose table entries k_commit keeps in shared memory: every
+// record a tree of num_leaves can allocate, within about 200 KB.
+inline int commit_info_cap(int num_leaves) {
+  const long long slots = (long long)num_leaves * kCommitSlotBytes;
+  const long long fit = (200ll * 1024 - slots) / (long long)sizeof(LeafInfo);
+  const long long want = 4ll * num_leaves + 2 * kMaxBatch + 2;
+  return (int)std::max(0ll, std::min(want, fit));
+}
 
 inline size_t commit_smem_bytes(int num_leaves) {
-  return (size_t)num_leaves * kCommitSlotBytes + 64;
+  return (size_t)num_leaves * kCommitSlotBytes + (size_t)commit_info_cap(num_leaves) * sizeof(LeafInfo);
 }
 
 __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict__ ts,
                                                            const int* __restrict__ missing_bin, CommitParams cp,
-                                                           int* __restrict__ host_done, int host_done_index) {
+                                                           int info_cap, int* __restrict__ host_done,
+                                                           int host_done_index) {
   extern __shared__ __align__(16) unsigned char commit_smem[];
   const int L_max = cp.num_leaves;
-  double* s_g = reinterpret_cast<double*>(commit_smem);  // frontier gain, -1 when the leaf cannot split
-  double* s_cg0 = s_g + L_max;                            // expanded slot: children's gains
-  double* s_cg1 = s_cg0 + L_max;
-  int* s_leaf = reinterpret_cast<int*>(s_cg1 + L_max);   // slot -> leaf id
-  int* s_c0 = s_leaf + L_max;                             // expanded slot: children's leaf ids
-  int* s_c1 = s_c0 + L_max;
-  // commit k of this launch splits frontier slot s_cslot[k] (leaf s_cpar[k]);
-  // its right child takes slot nl0 + k
-  int* s_cslot = s_c1 + L_max;
-  int* s_cpar = s_cslot + L_max;
-  unsigned char* s_x = reinterpret_cast<unsigned char*>(s_cpar + L_max);  // expanded
-  __shared__ int s_ncommit, s_stop, s_nl;
-  __shared__ int s_rank_slot[kMaxBatch];
+  double* s_g = reinterpret_cast<double*>(commit_smem);   // slot -> gain (-1: cannot split)
+  double* s_vg = s_g + L_max;                              // simulated frontier: gain
+  LeafInfo* s_info = reinterpret_cast<LeafInfo*>(s_vg + L_max);  // leaf records [0, info_cap)
+  int* s_slot_leaf = reinterpret_cast<int*>(s_info + info_cap);  // slot -> leaf
+  int* s_cslot = s_slot_leaf + L_max;                      // commit k: slot ...
+  int* s_cpar = s_cslot + L_max;                           // ... and the leaf split there
+  int* s_vleaf = s_cpar + L_max;                           // simulated frontier: leaf
+  int* s_slot_node = s_vleaf + L_max;                      // slot -> node id of its leaf
+  int* s_cnode = s_slot_node + L_max;                      // commit k: node id of the split leaf
+  __shared__ int s_ncommit, s_stop, s_nl, s_nsel;
+  __shared__ int s_sel[kMaxBatch];
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
   TreeHeader& H = ts->hdr;
   Batch& Bt = ts->batch;
   const int n_items = Bt.n_items;
   const bool root = Bt.root != 0;
+  const int n_pool = H.n_pool;
+  const int cap = n_pool < info_cap ? n_pool : info_cap;
+  auto info = [&](int leaf) -> LeafInfo& { return leaf < cap ? s_info[leaf] : ts->info[leaf]; };
 
-  // ---- 1. the frontier into shared memory; this iteration's expanded leaves
-  // (whose children the scan just folded) are marked
+  // ---- 1. leaf table and frontier into shared memory; this iteration's
+  // expanded leaves (whose children the scan just folded) are marked
+  for (int i = t; i < cap; i += kCommitThreads) s_info[i] = ts->info[i];
   const int nl0 = H.n_leaves;
-  for (int i = t; i < nl0; i += kCommitThreads) {
-    const FrontierSlot fs = ts->front[i];
-    s_leaf[i] = fs.leaf;
-    s_g[i] = fs.gain;
-    s_x[i] = fs.expanded ? 1 : 0;
-    s_c0[i] = fs.child[0];
-    s_c1[i] = fs.child[1];
-    s_cg0[i] = fs.child_gain[0];
-    s_cg1[i] = fs.child_gain[1];
+  for (int i = t; i < nl0; i += kCommitThreads) s_slot_leaf[i] = ts->slot_leaf[i];
+  __syncthreads();
+  if (!root && t < n_items) {
+    const int leaf = Bt.items[t].leaf;
+    info(leaf).expanded = 1;
+    ts->info[leaf].expanded = 1;
+    ts->pool[leaf].state = 1;
   }
   __syncthreads();
-  if (!root && t < n_items) s_x[Bt.items[t].slot] = 1;
+  for (int i = t; i < nl0; i += kCommitThreads) {
+    s_g[i] = info(s_slot_leaf[i]).gain;
+    s_slot_node[i] = ts->pool[s_slot_leaf[i]].node;
+  }
   __syncthreads();
 
-  // ---- 2. the pick loop, on one warp over shared memory only
+  // Arg-max of the pick order over gains g[0, n) (larger gain, then lower
+  // slot; only gains > 0 count), on one warp.  A positive double orders like
+  // its bit pattern, so the warp reduces 64-bit keys with two max reductions
+  // of 32-bit halves and takes the lowest slot holding the maximum.
+  auto warp_pick = [&](const double* g, int n) -> int {
+    unsigned long long best = 0ull;
+    int best_i = 0x7fffffff;
+    for (int i0 = 0; i0 < n; i0 += 256) {
+      double x[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int i = i0 + q * 32 + lane;
+        x[q] = i < n ? g[i] : -1.0;
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const unsigned long long k = x[q] > 0.0 ? (unsigned long long)__double_as_longlong(x[q]) : 0ull;
+        if (k > best) {  // strict: the lane's lowest slot wins ties
+          best = k;
+          best_i = i0 + q * 32 + lane;
+        }
+      }
+    }
+    const unsigned int hi = __reduce_max_sync(0xffffffffu, (unsigned int)(best >> 32));
+    const unsigned int lo =
+        __reduce_max_sync(0xffffffffu, (unsigned int)(best >> 32) == hi ? (unsigned int)best : 0u);
+    const unsigned long long top = ((unsigned long long)hi << 32) | lo;
+    if (top == 0ull) return -1;
+    return __reduce_min_sync(0xffffffffu, best == top ? best_i : 0x7fffffff);
+  };
+
+  // ---- 2. the pick loop (growth_policy.mojo:659-677), on one warp over
+  // shared memory: commit every pick whose children are computed
   if (w == 0) {
     int nl = nl0;
     int n_commit = 0;
     int stop = H.done;
     while (!stop && nl < L_max) {
-      double bg = -1.0;
-      int bs = -1;
-      for (int i = lane; i < nl; i += 32) {
-        const double g = s_g[i];
-        if (g > 0.0 && pick_before(g, i, bg, bs)) {
-          bg = g;
-          bs = i;
-        }
-      }
-      for (int k = 16; k > 0; k >>= 1) {
-        const double og = __shfl_xor_sync(0xffffffffu, bg, k);
-        const int os = __shfl_xor_sync(0xffffffffu, bs, k);
-        if (pick_before(og, os, bg, bs)) {
-          bg = og;
-          bs = os;
-        }
-      }
+      const int bs = warp_pick(s_g, nl);
       if (bs < 0) {
         stop = 1;
         break;
       }
-      if (!s_x[bs]) break;  // the pick still needs its expansion
+      const int leaf = s_slot_leaf[bs];
+      const LeafInfo I = info(leaf);
+      if (!I.expanded) break;  // the pick still needs its expansion
       if (lane == 0) {
+        // node ids are assigned here, in commit order: a child committed in
+        // the same launch as its parent finds its id in s_slot_node
         s_cslot[n_commit] = bs;
-        s_cpar[n_commit] = s_leaf[bs];
-        s_g[nl] = s_cg1[bs];
-        s_leaf[nl] = s_c1[bs];
-        s_x[nl] = 0;
-        s_g[bs] = s_cg0[bs];
-        s_leaf[bs] = s_c0[bs];
-        s_x[bs] = 0;
+        s_cpar[n_commit] = leaf;
+        s_cnode[n_commit] = s_slot_node[bs];
+        s_slot_leaf[bs] = I.child[0];
+        s_g[bs] = info(I.child[0]).gain;
+        s_slot_node[bs] = H.n_nodes + 2 * n_commit;
+        s_slot_leaf[nl] = I.child[1];
+        s_g[nl] = info(I.child[1]).gain;
+        s_slot_node[nl] = H.n_nodes + 2 * n_commit + 1;
       }
       __syncwarp();
       ++n_commit;
@@ -1353,16 +1383,28 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
   }
   __syncthreads();
 
-  // ---- 3. the commits' writes, one thread each
+  // ---- 3. the commits' writes, one thread each, and the frontier back
   const int n_commit = s_ncommit;
   const int nl = s_nl;
   const int nodes0 = H.n_nodes;
+  // children's node records first: a leaf committed in the same launch as
+  // its parent has its record reset here and its split written below
   for (int k = t; k < n_commit; k += kCommitThreads) {
-    const int slot = s_cslot[k];
+    LeafRec& L = ts->pool[s_cpar[k]];
+    const int left_node = nodes0 + 2 * k, right_node = left_node + 1;
+    LeafRec& CL = ts->pool[L.child[0]];
+    LeafRec& CR = ts->pool[L.child[1]];
+    CL.node = left_node;
+    CR.node = right_node;
+    clear_node(ts->nodes[left_node], CL.value, CL.gcount);
+    clear_node(ts->nodes[right_node], CR.value, CR.gcount);
+  }
+  __syncthreads();
+  for (int k = t; k < n_commit; k += kCommitThreads) {
     LeafRec& L = ts->pool[s_cpar[k]];
     const SplitRec& s = L.split;
     const int left_node = nodes0 + 2 * k, right_node = left_node + 1;
-    NodeRec& pn = ts->nodes[L.node];
+    NodeRec& pn = ts->nodes[s_cnode[k]];
     pn.feature = s.feature;
     pn.gain = s.gain;
     pn.left = left_node;
@@ -1379,34 +1421,19 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
       pn.mbin = missing_bin[s.feature];
     }
     L.state = 2;
-    LeafRec& CL = ts->pool[L.child[0]];
-    LeafRec& CR = ts->pool[L.child[1]];
-    CL.node = left_node;
-    CR.node = right_node;
-    clear_node(ts->nodes[left_node], CL.value, CL.gcount);
-    clear_node(ts->nodes[right_node], CR.value, CR.gcount);
-    ts->slot_leaf[slot] = L.child[0];
-    ts->slot_leaf[nl0 + k] = L.child[1];
   }
+  for (int i = t; i < nl; i += kCommitThreads) ts->slot_leaf[i] = s_slot_leaf[i];
   if (t == 0) {
     H.n_nodes = nodes0 + 2 * n_commit;
     H.n_leaves = nl;
   }
-  // the updated frontier back to its table (children ids and gains only
-  // matter for expanded slots)
-  for (int i = t; i < nl; i += kCommitThreads) {
-    FrontierSlot fs;
-    fs.leaf = s_leaf[i];
-    fs.expanded = s_x[i];
-    fs.child[0] = s_x[i] ? s_c0[i] : -1;
-    fs.child[1] = s_x[i] ? s_c1[i] : -1;
-    fs.gain = s_g[i];
-    fs.child_gain[0] = s_x[i] ? s_cg0[i] : -1.0;
-    fs.child_gain[1] = s_x[i] ? s_cg1[i] : -1.0;
-    ts->front[i] = fs;
-  }
 
-  // ---- 4. next batch
+  // ---- 4. next batch: the leaves the pick loop will need next, in order.
+  // The loop is simulated past this point on a copy of the frontier: an
+  // expanded leaf is committed virtually (its children, with their known
+  // gains, take its slot and the next one), an unexpanded one is taken into
+  // the batch and leaves the simulated frontier.  The first leaf taken is the
+  // one the real loop stopped at, so every iteration commits a split.
   if (s_stop) {
     if (t == 0) {
       H.done = 1;
@@ -1415,45 +1442,61 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
       Bt.n_tiles = 0;
     }
   } else {
-    int m = cp.num_leaves - nl;
-    if (m > cp.batch_cap) m = cp.batch_cap;
-    if (t < kMaxBatch) s_rank_slot[t] = -1;
-    __syncthreads();
-    // rank of every splittable frontier leaf in pick order (one warp per
-    // leaf); the first m are kept
-    for (int i = w; i < nl; i += kCommitThreads / 32) {
-      const double g = s_g[i];
-      if (!(g > 0.0)) continue;  // warp-uniform
-      int ahead = 0;
-      for (int k = lane; k < nl; k += 32) {
-        const double gk = s_g[k];
-        ahead += (gk > 0.0 && pick_before(gk, k, g, i)) ? 1 : 0;
-      }
-      const int rank = __reduce_add_sync(0xffffffffu, ahead);
-      if (lane == 0 && rank < m) s_rank_slot[rank] = i;
+    for (int i = t; i < nl; i += kCommitThreads) {
+      s_vleaf[i] = s_slot_leaf[i];
+      s_vg[i] = s_g[i];
     }
     __syncthreads();
     if (w == 0) {
-      const int slot = s_rank_slot[lane];
-      const bool want = lane < m && slot >= 0 && !s_x[slot];
-      const unsigned ballot = __ballot_sync(0xffffffffu, want);
-      int n_new = __popc(ballot);
-      // never more leaf records or histogram slots than reserved
+      int vn = nl, vleaves = nl, n_sel = 0;
+      while (n_sel < cp.batch_cap && vleaves < L_max) {
+        const int bs = warp_pick(s_vg, vn);
+        if (bs < 0) break;
+        const int leaf = s_vleaf[bs];
+        const LeafInfo I = info(leaf);
+        if (lane == 0) {
+          if (I.expanded) {
+            s_vleaf[bs] = I.child[0];
+            s_vg[bs] = info(I.child[0]).gain;
+            s_vleaf[vn] = I.child[1];
+            s_vg[vn] = info(I.child[1]).gain;
+          } else {
+            s_sel[n_sel] = leaf;
+            s_vg[bs] = -1.0;
+          }
+        }
+        __syncwarp();
+        if (I.expanded) ++vn;
+        else ++n_sel;
+        ++vleaves;
+      }
+      if (lane == 0) s_nsel = n_sel;
+    }
+    __syncthreads();
+    if (w == 0) {
+      const int n_sel = s_nsel;
+      // histogram slots: every later real commit may need one expansion, so
+      // speculative items only use slots beyond that reserve; leaf records
+      // take two per item
       const int pool0 = H.n_pool, hist0 = H.n_hist;
-      int room = (kMaxPool - pool0) / 2;
-      if (cp.hist_slots - hist0 < room) room = cp.hist_slots - hist0;
-      if (n_new > room) n_new = room < 0 ? 0 : room;
-      const int idx = __popc(ballot & ((1u << lane) - 1u));
-      const bool take = want && idx < n_new;
+      const int free_slots = cp.hist_slots - hist0;
+      const int reserve = cp.num_leaves - nl;
+      int n_new = n_sel;
+      const int spec = free_slots - reserve;
+      if (n_new > 1 + (spec > 0 ? spec : 0)) n_new = 1 + (spec > 0 ? spec : 0);
+      if (n_new > free_slots) n_new = free_slots;
+      if (n_new > (kMaxPool - pool0) / 2) n_new = (kMaxPool - pool0) / 2;
+      if (n_new < 0) n_new = 0;
+      const bool take = lane < n_new;
       long long tiles = 0;
       if (take) {
-        const int leaf = s_leaf[slot];
+        const int idx = lane;
+        const int leaf = s_sel[idx];
         LeafRec& L = ts->pool[leaf];
         const SplitRec& s = L.split;
         BatchItem& P = Bt.items[idx];
         const long long n_left = s.n_left, n_right = L.gcount - s.n_left;
         P.leaf = leaf;
-        P.slot = slot;
         P.child[0] = pool0 + 2 * idx;
         P.child[1] = pool0 + 2 * idx + 1;
         P.built_is_left = n_left <= n_right ? 1 : 0;
@@ -1474,31 +1517,36 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
         P.cursor_right = 0;
         L.child[0] = P.child[0];
         L.child[1] = P.child[1];
+        L.exp_buf = P.dst_buf;
         for (int side = 0; side < 2; ++side) {
           LeafRec& C = ts->pool[P.child[side]];
           C.node = -1;
+          C.parent = leaf;
           C.buf = P.dst_buf;
           C.hist_slot = (side == 0) == (P.built_is_left != 0) ? P.built_hist : P.sib_hist;
           C.state = 0;
           C.child[0] = C.child[1] = -1;
           C.exp_buf = 0;
-          C.pad = 0;
           C.begin = 0;
           C.count = 0;
           C.gcount = 0;
           C.value = 0.0;
           clear_split(C.split);
+          LeafInfo& CI = ts->info[P.child[side]];
+          CI.gain = -1.0;
+          CI.child[0] = CI.child[1] = -1;
+          CI.expanded = 0;
+          CI.pad = 0;
         }
         tiles = (L.count + cp.tile_rows - 1) / cp.tile_rows;
       }
-      // exclusive prefix of tiles over the items (lane order = item order;
-      // lanes that are not items add 0)
+      // exclusive prefix of tiles over the items (lane = item)
       long long incl = tiles;
       for (int k = 1; k < 32; k <<= 1) {
         long long o = __shfl_up_sync(0xffffffffu, incl, k);
         if (lane >= k) incl += o;
       }
-      if (take) Bt.items[idx].tile0 = incl - tiles;
+      if (take) Bt.items[lane].tile0 = incl - tiles;
       const long long total = __shfl_sync(0xffffffffu, incl, 31);
       if (lane == 0) {
         if (n_new == 0) {
@@ -1525,39 +1573,50 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
   }
 }
 
-// After the last iteration: frontier leaves sorted by range start, for the
-// raw update.
-__global__ void __launch_bounds__(1024) k_leaf_table(const TreeState* __restrict__ ts, long long* __restrict__ begins,
-                                                     int* __restrict__ order) {
-  const int nl = ts->hdr.n_leaves;
-  // Sort key: range start, then empty leaves before the non-empty one that
-  // shares the start, then slot.  The raw update's search for the last start
-  // <= position then always lands on the leaf that owns the position.
-  for (int i = threadIdx.x; i < nl; i += blockDim.x) {
-    const LeafRec& Li = ts->pool[ts->slot_leaf[i]];
-    long long bi = Li.begin * 2 + (Li.count > 0 ? 1 : 0);
+// After the last iteration: the row -> leaf-value map.  The unexpanded leaf
+// records (committed leaves and speculative children) tile this device's rows:
+// an unexpanded record's range in its own buffer was written by its parent's
+// partition and nothing has written there since.  A committed leaf that was
+// expanded but never split may have lost its own buffer to a speculative
+// grandchild's partition, so its rows are taken from its unexpanded
+// descendants, each of which takes the value of its nearest committed
+// ancestor (the first record up the chain with a node id).  The table holds
+// the non-empty records sorted by range start (their starts are distinct).
+__global__ void __launch_bounds__(1024) k_leaf_table(TreeState* __restrict__ ts, long long* __restrict__ begins,
+                                                     int* __restrict__ order, double* __restrict__ values) {
+  __shared__ int s_n;
+  const int n_pool = ts->hdr.n_pool;
+  if (threadIdx.x == 0) s_n = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < n_pool; i += blockDim.x) {
+    const LeafRec& Li = ts->pool[i];
+    if (Li.state != 0 || Li.count <= 0) continue;
     int rank = 0;
-    for (int k = 0; k < nl; ++k) {
-      const LeafRec& Lk = ts->pool[ts->slot_leaf[k]];
-      long long bk = Lk.begin * 2 + (Lk.count > 0 ? 1 : 0);
-      if (bk < bi || (bk == bi && k < i)) ++rank;
+    for (int k = 0; k < n_pool; ++k) {
+      const LeafRec& Lk = ts->pool[k];
+      if (Lk.state == 0 && Lk.count > 0 && Lk.begin < Li.begin) ++rank;
     }
+    int a = i;
+    while (ts->pool[a].node < 0) a = ts->pool[a].parent;
     begins[rank] = Li.begin;
-    order[rank] = ts->slot_leaf[i];
+    order[rank] = i;
+    values[rank] = ts->pool[a].value;
+    atomicAdd(&s_n, 1);
   }
+  __syncthreads();
+  if (threadIdx.x == 0) ts->hdr.n_table = s_n;
 }
 
 // raw[row * K + k] = fma(lr, value(leaf of row), raw[row * K + k])
-// (boosting.mojo:1991-2111, explicit fused multiply-add).  A leaf expanded
-// but never split still holds its rows in its own buffer.
+// (boosting.mojo:1991-2111, explicit fused multiply-add).
 __global__ void k_update_raw(const TreeState* __restrict__ ts, const long long* __restrict__ begins,
-                             const int* __restrict__ order, const int* __restrict__ rows0,
-                             const int* __restrict__ rows1, double* __restrict__ raw, long long n, int K, int k,
-                             double lr) {
+                             const int* __restrict__ order, const double* __restrict__ values,
+                             const int* __restrict__ rows0, const int* __restrict__ rows1, double* __restrict__ raw,
+                             long long n, int K, int k, double lr) {
   long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
-  int nl = ts->hdr.n_leaves;
-  int lo = 0, hi = nl - 1;
+  const int nt = ts->hdr.n_table;
+  int lo = 0, hi = nt - 1;
   while (lo < hi) {
     int mid = (lo + hi + 1) >> 1;
     if (begins[mid] <= i) lo = mid;
@@ -1567,7 +1626,7 @@ __global__ void k_update_raw(const TreeState* __restrict__ ts, const long long* 
   const int* rows = L->buf ? rows1 : rows0;
   int r = rows[i];
   double* p = raw + (long long)r * K + k;
-  *p = fma(lr, L->value, *p);
+  *p = fma(lr, values[lo], *p);
 }
 
 }  // namespace

@@ -300,9 +300,10 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   int batch_cap = 32;
   if (const char* e = getenv("MOJOTREES_BATCH")) batch_cap = atoi(e);
   batch_cap = std::max(1, std::min(std::min(batch_cap, kMaxBatch), cfg.num_leaves - 1));
-  // Histogram slots: a tree uses at most 1 + (expansions) <= 2 * num_leaves
-  // leaf slots, then batch_cap work slots the builds land in first.
-  const int hist_slots = 2 * cfg.num_leaves;
+  // Histogram slots: the root, one per expansion (at most num_leaves - 1
+  // committed splits, plus speculative ones the commit kernel keeps within
+  // the remaining budget), then batch_cap work slots the builds land in.
+  const int hist_slots = 2 * cfg.num_leaves + batch_cap;
   const int work_base = hist_slots;
   DevBuf<int> d_hist;
   d_hist.alloc((size_t)slot_cells * (hist_slots + batch_cap));
@@ -310,8 +311,10 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   d_fb.alloc((size_t)2 * batch_cap * F);
   DevBuf<long long> d_begins;
   DevBuf<int> d_order;
-  d_begins.alloc(kMaxLeaves);
-  d_order.alloc(kMaxLeaves);
+  DevBuf<double> d_values;
+  d_begins.alloc(kMaxPool);
+  d_order.alloc(kMaxPool);
+  d_values.alloc(kMaxPool);
   MTB_CUDA(cudaStreamSynchronize(st));
   stats.upload_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
 
@@ -353,6 +356,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   cp.hist_slots = hist_slots;
   cp.tile_rows = 256 * part_items;
   const size_t commit_smem = commit_smem_bytes(cfg.num_leaves);
+  const int commit_cap = commit_info_cap(cfg.num_leaves);
   MTB_CUDA(cudaFuncSetAttribute(k_commit, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)commit_smem));
 
   // The host learns that a tree is done through mapped host memory written by
@@ -556,15 +560,17 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
                                                     d_sc.p, sp, d_fb.p, work_base);
         timer.end();
         timer.begin(&stats.commit_ms);
-        k_commit<<<1, kCommitThreads, commit_smem, st>>>(d_ts.p, d_missing.p, cp, d_done, i % kRing);
+        k_commit<<<1, kCommitThreads, commit_smem, st>>>(d_ts.p, d_missing.p, cp, commit_cap, d_done,
+                                                          i % kRing);
         timer.end();
         MTB_CUDA(cudaEventRecord(iter_ev[i % kRing], st));
         launches += 4;
         launched++;
       }
       stats.hist_launches += launched;
-      k_leaf_table<<<1, 1024, 0, st>>>(d_ts.p, d_begins.p, d_order.p);
-      k_update_raw<<<grid256, 256, 0, st>>>(d_ts.p, d_begins.p, d_order.p, d_rows0.p, d_rows1.p, d_raw.p, N, K, k,
+      k_leaf_table<<<1, 1024, 0, st>>>(d_ts.p, d_begins.p, d_order.p, d_values.p);
+      k_update_raw<<<grid256, 256, 0, st>>>(d_ts.p, d_begins.p, d_order.p, d_values.p, d_rows0.p, d_rows1.p,
+                                            d_raw.p, N, K, k,
                                             cfg.learning_rate);
       launches += 2;
       MTB_CUDA(cudaGetLastError());
