@@ -280,6 +280,16 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     MTB_CUDA(cudaStreamSynchronize(st));
     P_rank = (long long)mx;
     n_part = P_rank * world;
+    // The gathered partials are block r * P_rank + j of rank r, so the global
+    // tree equals the single-device one only when every shard but the last
+    // holds exactly P_rank blocks and starts at global row r * P_rank * 1024
+    // (the last shard's missing blocks are the zero padding at the end).
+    std::string err;
+    if (coll->rank() < world - 1 && (N != P_rank * 1024))
+      err = "data-parallel shards other than the last must all hold the same number of rows";
+    else if (in.row_offset != (long long)coll->rank() * P_rank * 1024)
+      err = "row_offset of a data-parallel shard must be its rank times the common shard size";
+    agree(err);
   }
   DevBuf<double> d_pg, d_ph, d_tg, d_th, d_pg_all, d_ph_all;
   d_pg.alloc(P_rank);
