@@ -188,8 +188,10 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     MTB_CUDA(cudaStreamSynchronize(st));
     if (flag) throw std::runtime_error(local_error.empty() ? "invalid input on another rank" : local_error);
   };
-  agree(coll && coll->rank() < world - 1 && N % 1024 != 0
-            ? "data-parallel shards other than the last must hold a multiple of 1024 rows"
+  // FIXED mode sums |g| over 1024-row blocks of global rows, so its shards
+  // must align to them; QUANT mode only needs global row ids (max is exact)
+  agree(coll && mode == MODE_FIXED && coll->rank() < world - 1 && N % 1024 != 0
+            ? "fixed-point data-parallel shards other than the last must hold a multiple of 1024 rows"
             : "");
   std::vector<double> base(K);
   if (K == 1) {
@@ -285,10 +287,10 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     // holds exactly P_rank blocks and starts at global row r * P_rank * 1024
     // (the last shard's missing blocks are the zero padding at the end).
     std::string err;
-    if (coll->rank() < world - 1 && (N != P_rank * 1024))
-      err = "data-parallel shards other than the last must all hold the same number of rows";
-    else if (in.row_offset != (long long)coll->rank() * P_rank * 1024)
-      err = "row_offset of a data-parallel shard must be its rank times the common shard size";
+    if (mode == MODE_FIXED && coll->rank() < world - 1 && (N != P_rank * 1024))
+      err = "fixed-point data-parallel shards other than the last must all hold the same number of rows";
+    else if (mode == MODE_FIXED && in.row_offset != (long long)coll->rank() * P_rank * 1024)
+      err = "row_offset of a fixed-point data-parallel shard must be its rank times the common shard size";
     agree(err);
   }
   DevBuf<double> d_pg, d_ph, d_tg, d_th, d_pg_all, d_ph_all;
