@@ -655,9 +655,14 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
         if (MODE == MODE_QUANT) {
           uint16_t pr = __ldg(reinterpret_cast<const uint16_t*>(pairs) + i);
           int g = (int)(int8_t)(pr & 0xff);
-          x0 = LAYOUT == HL_QUANT16 ? (unsigned int)(g + g_lim) | (1u << 16)
-                                    : (unsigned int)(g * (1 << kQuantCountBits) + 1);
-          x1 = (unsigned int)(pr >> 8);
+          if (LAYOUT == HL_QUANT16) {
+            // g + g_lim and h both fit 8 bits here: carry both in one word
+            // (bits 0-7 and 8-15) so the chunk walk needs one shuffle for them
+            x0 = (unsigned int)(g + g_lim) | ((unsigned int)(pr >> 8) << 8) | (1u << 16);
+          } else {
+            x0 = (unsigned int)(g * (1 << kQuantCountBits) + 1);
+            x1 = (unsigned int)(pr >> 8);
+          }
         } else {
           int2 pr = __ldg(reinterpret_cast<const int2*>(pairs) + i);
           x0 = (unsigned int)pr.x;
@@ -691,9 +696,13 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
           }
 #pragma unroll
           for (int u = 0; u < U; ++u) {
-            const unsigned int x0 = __shfl_sync(0xffffffffu, ca0, u0 + u);
-            const unsigned int x1 =
-                (MODE == MODE_FIXED && CONST_H) ? 1u : __shfl_sync(0xffffffffu, ca1, u0 + u);
+            unsigned int x0 = __shfl_sync(0xffffffffu, ca0, u0 + u), x1;
+            if (LAYOUT == HL_QUANT16) {
+              x1 = (x0 >> 8) & 0xffu;
+              x0 &= 0xffff00ffu;
+            } else {
+              x1 = (MODE == MODE_FIXED && CONST_H) ? 1u : __shfl_sync(0xffffffffu, ca1, u0 + u);
+            }
             add_row(bw[u], x0, x1);
           }
 #pragma unroll
@@ -710,9 +719,13 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
           }
 #pragma unroll
           for (int u = 0; u < U; ++u) {
-            const unsigned int x0 = __shfl_sync(0xffffffffu, ca0, u0 + u);
-            const unsigned int x1 =
-                (MODE == MODE_FIXED && CONST_H) ? 1u : __shfl_sync(0xffffffffu, ca1, u0 + u);
+            unsigned int x0 = __shfl_sync(0xffffffffu, ca0, u0 + u), x1;
+            if (LAYOUT == HL_QUANT16) {
+              x1 = (x0 >> 8) & 0xffu;
+              x0 &= 0xffff00ffu;
+            } else {
+              x1 = (MODE == MODE_FIXED && CONST_H) ? 1u : __shfl_sync(0xffffffffu, ca1, u0 + u);
+            }
             add_row(bw[u], x0, x1);
           }
         }
@@ -721,8 +734,13 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
         const int n_in = (int)(pe - c0);
         for (int u = 0; u < n_in; ++u) {
           const int r = __shfl_sync(0xffffffffu, cr, u);
-          const unsigned int x0 = __shfl_sync(0xffffffffu, ca0, u);
-          const unsigned int x1 = __shfl_sync(0xffffffffu, ca1, u);
+          unsigned int x0 = __shfl_sync(0xffffffffu, ca0, u), x1;
+          if (LAYOUT == HL_QUANT16) {
+            x1 = (x0 >> 8) & 0xffu;
+            x0 &= 0xffff00ffu;
+          } else {
+            x1 = __shfl_sync(0xffffffffu, ca1, u);
+          }
           add_row(BinWord<NPL>::load(bcol + (size_t)(unsigned int)r * (unsigned int)Fp), x0, x1);
         }
       }
