@@ -1,9 +1,12 @@
 // Device transform of float64 columns into uint8 bins (see device_binning.h).
 #include "device_binning.h"
 
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
+#include <chrono>
+#include <cstdio>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -33,11 +36,13 @@ struct FeatureBins {
 
 constexpr int kBinThreads = 256;
 
-// One block per (row chunk, feature of the chunk): the feature's edges (at
+// One block per (row block, feature of the chunk): the feature's edges (at
 // most 255) or kept codes staged in shared memory, then every value binned
-// exactly as BinMapper::bin_value does.
-__global__ void __launch_bounds__(kBinThreads) k_bin_columns(const double* __restrict__ x, int64_t n_rows,
-                                                             int f0, const FeatureBins* __restrict__ fb,
+// exactly as BinMapper::bin_value does.  The chunk holds rows [r0, r0 +
+// chunk_rows) of features f0.. as consecutive columns of chunk_rows values.
+__global__ void __launch_bounds__(kBinThreads) k_bin_columns(const double* __restrict__ x, int64_t chunk_rows,
+                                                             int64_t r0_chunk, int64_t n_rows, int f0,
+                                                             const FeatureBins* __restrict__ fb,
                                                              const double* __restrict__ edges,
                                                              const int64_t* __restrict__ codes,
                                                              uint8_t* __restrict__ out, int64_t rows_per_block) {
@@ -51,10 +56,10 @@ __global__ void __launch_bounds__(kBinThreads) k_bin_columns(const double* __res
     for (int i = threadIdx.x; i < d.n_edges; i += blockDim.x) s_edge[i] = edges[d.edge_off + i];
   }
   __syncthreads();
-  const double* col = x + (int64_t)fl * n_rows;
-  uint8_t* dst = out + (int64_t)(f0 + fl) * n_rows;
+  const double* col = x + (int64_t)fl * chunk_rows;
+  uint8_t* dst = out + (int64_t)(f0 + fl) * n_rows + r0_chunk;
   const int64_t r0 = (int64_t)blockIdx.x * rows_per_block;
-  const int64_t r1 = r0 + rows_per_block < n_rows ? r0 + rows_per_block : n_rows;
+  const int64_t r1 = r0 + rows_per_block < chunk_rows ? r0 + rows_per_block : chunk_rows;
   for (int64_t r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
     const double v = col[r];
     int bin;
@@ -121,50 +126,101 @@ void transform_on_device(const BinMapper& m, const double* x, int64_t n_rows, ui
     MTB_CUDA_BIN(cudaMemcpyAsync(d_codes.p, m.cat_codes.data(), sizeof(int64_t) * m.cat_codes.size(),
                                  cudaMemcpyHostToDevice, st));
 
-  // chunks of whole features, about 256 MB of float64 each
-  const int64_t col_bytes = n_rows * (int64_t)sizeof(double);
-  const int per_chunk = (int)std::max<int64_t>(1, std::min<int64_t>(F, (256ll << 20) / col_bytes));
-  const int64_t chunk_elems = (int64_t)per_chunk * n_rows;
-  double* h_stage[2] = {nullptr, nullptr};
-  DeviceArray<double> d_stage0(chunk_elems), d_stage1(chunk_elems);
-  double* d_stage[2] = {d_stage0.p, d_stage1.p};
-  cudaEvent_t done[2] = {nullptr, nullptr};
-  struct Cleanup {
-    double** h;
-    cudaEvent_t* e;
-    ~Cleanup() {
-      for (int i = 0; i < 2; ++i) {
-        if (h[i]) cudaFreeHost(h[i]);
-        if (e[i]) cudaEventDestroy(e[i]);
+  // The column-major matrix is streamed in chunks of kChunkBytes: several
+  // whole features when a column is short, else a row range of one feature.
+  // Each chunk is copied by all host threads into one of kStages page-locked
+  // buffers, sent to the device and binned there; the memcpy of a chunk
+  // overlaps the DMA of the previous one.  The buffers are ordinary
+  // allocations registered with the driver, which pins pages several times
+  // faster than cudaHostAlloc.
+  // MOJOTREES_TRACE_UPLOAD=1 prints the phase times of this function to stderr
+  const bool trace = getenv("MOJOTREES_TRACE_UPLOAD") != nullptr;
+  auto clk = [] { return std::chrono::steady_clock::now(); };
+  const auto tt0 = clk();
+  double t_wait = 0.0, t_copy = 0.0;
+  constexpr int kStages = 3;
+  constexpr int64_t kChunkBytes = 32ll << 20;
+  const int64_t chunk_elems_max = kChunkBytes / (int64_t)sizeof(double);
+  int64_t chunk_rows, per_chunk;
+  if (n_rows >= chunk_elems_max) {
+    chunk_rows = chunk_elems_max;
+    per_chunk = 1;
+  } else {
+    chunk_rows = std::max<int64_t>(1, n_rows);
+    per_chunk = std::max<int64_t>(1, std::min<int64_t>({(int64_t)F, chunk_elems_max / chunk_rows, 65535}));
+  }
+  const int64_t stage_elems = chunk_rows * per_chunk;
+  struct Stages {
+    double* h[kStages] = {};
+    bool reg[kStages] = {};
+    double* d[kStages] = {};
+    cudaEvent_t e[kStages] = {};
+    ~Stages() {
+      for (int i = 0; i < kStages; ++i) {
+        if (e[i]) {
+          cudaEventSynchronize(e[i]);
+          cudaEventDestroy(e[i]);
+        }
+        if (reg[i]) cudaHostUnregister(h[i]);
+        free(h[i]);
+        if (d[i]) cudaFree(d[i]);
       }
     }
-  } cleanup{h_stage, done};
-  for (int i = 0; i < 2; ++i) {
-    MTB_CUDA_BIN(cudaHostAlloc(&h_stage[i], sizeof(double) * chunk_elems, cudaHostAllocDefault));
-    MTB_CUDA_BIN(cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming));
+  } sg;
+  const size_t stage_bytes = ((size_t)stage_elems * sizeof(double) + 4095) & ~(size_t)4095;
+  for (int i = 0; i < kStages; ++i) {
+    sg.h[i] = static_cast<double*>(aligned_alloc(4096, stage_bytes));
+    if (!sg.h[i]) throw std::runtime_error("host staging allocation failed");
+    MTB_CUDA_BIN(cudaHostRegister(sg.h[i], stage_bytes, cudaHostRegisterDefault));
+    sg.reg[i] = true;
+    MTB_CUDA_BIN(cudaMalloc(&sg.d[i], stage_bytes));
+    MTB_CUDA_BIN(cudaEventCreateWithFlags(&sg.e[i], cudaEventDisableTiming));
   }
   const int64_t rows_per_block = 8192;
-  const unsigned row_blocks = (unsigned)((n_rows + rows_per_block - 1) / rows_per_block);
+  const auto tt1 = clk();
   int k = 0;
-  for (int f0 = 0; f0 < F; f0 += per_chunk, k ^= 1) {
-    const int nf = std::min(per_chunk, F - f0);
-    const int64_t elems = (int64_t)nf * n_rows;
-    // the buffer's previous DMA must have finished before it is refilled
-    MTB_CUDA_BIN(cudaEventSynchronize(done[k]));
-    const double* src = x + (int64_t)f0 * n_rows;
-    double* dst = h_stage[k];
+  for (int f0 = 0; f0 < F; f0 += (int)per_chunk) {
+    const int nf = (int)std::min<int64_t>(per_chunk, F - f0);
+    for (int64_t r0 = 0; r0 < n_rows; r0 += chunk_rows) {
+      const int64_t nr = std::min<int64_t>(chunk_rows, n_rows - r0);
+      // the buffer's previous DMA must have finished before it is refilled
+      const auto ta = clk();
+      MTB_CUDA_BIN(cudaEventSynchronize(sg.e[k]));
+      const auto tb = clk();
+      double* dst = sg.h[k];
+      // nf columns of nr values each, packed back to back
+      const int64_t elems = (int64_t)nf * nr;
+      const int64_t piece = 1 << 17;
 #pragma omp parallel for schedule(static)
-    for (int64_t b = 0; b < elems; b += (1 << 20)) {
-      const int64_t n = std::min<int64_t>(1 << 20, elems - b);
-      memcpy(dst + b, src + b, sizeof(double) * n);
+      for (int64_t b = 0; b < elems; b += piece) {
+        int64_t o = b;
+        const int64_t end = std::min<int64_t>(b + piece, elems);
+        while (o < end) {
+          const int64_t fl = o / nr, r = o - fl * nr;
+          const int64_t n = std::min<int64_t>(end - o, nr - r);
+          memcpy(dst + o, x + (int64_t)(f0 + fl) * n_rows + r0 + r, sizeof(double) * n);
+          o += n;
+        }
+      }
+      if (trace) {
+        t_wait += std::chrono::duration<double>(tb - ta).count();
+        t_copy += std::chrono::duration<double>(clk() - tb).count();
+      }
+      MTB_CUDA_BIN(cudaMemcpyAsync(sg.d[k], dst, sizeof(double) * elems, cudaMemcpyHostToDevice, st));
+      MTB_CUDA_BIN(cudaEventRecord(sg.e[k], st));
+      const unsigned row_blocks = (unsigned)((nr + rows_per_block - 1) / rows_per_block);
+      k_bin_columns<<<dim3(row_blocks, nf), kBinThreads, 0, st>>>(sg.d[k], nr, r0, n_rows, f0, d_fb.p,
+                                                                 d_edges.p, d_codes.p, d_bins, rows_per_block);
+      MTB_CUDA_BIN(cudaGetLastError());
+      k = (k + 1) % kStages;
     }
-    MTB_CUDA_BIN(cudaMemcpyAsync(d_stage[k], h_stage[k], sizeof(double) * elems, cudaMemcpyHostToDevice, st));
-    MTB_CUDA_BIN(cudaEventRecord(done[k], st));
-    k_bin_columns<<<dim3(row_blocks, nf), kBinThreads, 0, st>>>(d_stage[k], n_rows, f0, d_fb.p, d_edges.p,
-                                                               d_codes.p, d_bins, rows_per_block);
-    MTB_CUDA_BIN(cudaGetLastError());
   }
   MTB_CUDA_BIN(cudaStreamSynchronize(st));
+  if (trace)
+    fprintf(stderr, "upload: setup %.1f ms, stream %.1f ms (buffer waits %.1f, host copies %.1f), %lld x %d values\n",
+            std::chrono::duration<double>(tt1 - tt0).count() * 1e3,
+            std::chrono::duration<double>(clk() - tt1).count() * 1e3, t_wait * 1e3, t_copy * 1e3,
+            (long long)n_rows, F);
 }
 
 }  // namespace mtb

@@ -46,6 +46,12 @@ int cuda_device_count() {
 
 namespace {
 
+// Initial raw scores: every row's K scores set to the per-class base.
+__global__ void k_fill_raw(double* __restrict__ raw, const double* __restrict__ base, long long n, int K) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    raw[i] = base[i % K];
+}
+
 template <typename T>
 struct DevBuf {
   T* p = nullptr;
@@ -245,10 +251,15 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     }
   }
   {
-    std::vector<double> init((size_t)N * K);
-    for (long long r = 0; r < N; ++r)
-      for (int k = 0; k < K; ++k) init[(size_t)r * K + k] = base[k];
-    MTB_CUDA(cudaMemcpyAsync(d_raw.p, init.data(), sizeof(double) * init.size(), cudaMemcpyHostToDevice, st));
+    // raw[r * K + k] = base[k], filled on the device
+    MTB_CUDA(cudaMemcpyAsync(d_red.p, base.data(), sizeof(double) * K, cudaMemcpyHostToDevice, st));
+    const long long n_raw = N * (long long)K;
+    const unsigned blocks = (unsigned)std::min<long long>((n_raw + 255) / 256, 148ll * 16);
+    if (n_raw > 0) {
+      k_fill_raw<<<blocks, 256, 0, st>>>(d_raw.p, d_red.p, n_raw, K);
+      MTB_CUDA(cudaGetLastError());
+      stats.kernel_launches++;
+    }
     MTB_CUDA(cudaStreamSynchronize(st));
   }
 

@@ -48,6 +48,14 @@ CASES = {
     "wide_features": (dict(seed=10, n=10_000, f=150), dict(objective="regression", rounds=2, leaves=31), 255),
     "tiny_ragged": (dict(seed=11, n=37, f=3), dict(objective="regression", rounds=3, leaves=4, min_data=3), 255),
     "two_leaves": (dict(seed=12, n=5_000, f=5, kind="binary"), dict(objective="binary", rounds=3, leaves=2), 255),
+    # L1 shrinkage, no L2 and a binding minimum hessian: the split scan's
+    # integer hessian thresholds and its pruning bounds under soft thresholds
+    "regularised_fixed": (dict(seed=17, n=30_000, f=16), dict(objective="regression", rounds=4, leaves=31, min_data=2,
+                                                             extra={"lambda_l1": 0.5, "lambda_l2": 0.0,
+                                                                    "min_sum_hessian_in_leaf": 40.0}), 255),
+    "regularised_quant": (dict(seed=18, n=30_000, f=16, kind="binary"),
+                          dict(objective="binary", rounds=4, leaves=31, quant=True, min_data=2,
+                               extra={"lambda_l1": 0.2, "lambda_l2": 0.0, "min_sum_hessian_in_leaf": 3.0}), 255),
 }
 
 
@@ -135,6 +143,24 @@ def test_gpu_device_binning_matches_host(mtlib):
     for device in (False, True):
         with pytest.raises(mtlib.MojoTreesError):
             mtlib.bin_dense(X, params, device=device)
+
+
+def test_gpu_device_binning_row_chunks(mtlib):
+    """Columns longer than one 32 MB staging chunk (4,194,304 float64 values)
+    are streamed as row ranges of one feature; the last range is ragged.  The
+    device bins equal the host transform."""
+    rng = np.random.default_rng(22)
+    n = 4_500_001
+    X = np.empty((n, 3))
+    X[:, 0] = rng.normal(size=n)
+    X[:, 1] = rng.integers(0, 30, size=n).astype(np.float64)
+    X[:, 2] = rng.exponential(size=n)
+    X[::101, 2] = np.nan
+    params = {"categorical_feature": "1", "max_bin": 255}
+    host = mtlib.bin_dense(X, params)
+    dev = mtlib.bin_dense(X, params, device=True)
+    for a, b in zip(host, dev):
+        np.testing.assert_array_equal(a, b)
 
 
 def test_gpu_round_times_and_stats(mtlib):
