@@ -2,6 +2,7 @@
 #include "binning.h"
 
 #include <algorithm>
+#include <cstring>
 #include <exception>
 #include <cmath>
 #include <stdexcept>
@@ -20,25 +21,72 @@ static double avoid_inf(double x) {
 }
 
 // binning.mojo:1745-1786: sequential selection sampling with splitmix64 draws.
+// The draw of row r depends only on r, so the draws of a block of rows are
+// computed in parallel; the accept decisions then run in row order.
 static std::vector<int64_t> sample_rows(int64_t n_rows, int64_t cnt, int seed) {
   std::vector<int64_t> out;
   if (n_rows < 1 || cnt <= 0 || cnt >= n_rows) return out;
   out.reserve((size_t)cnt);
-  uint64_t base = (uint64_t)(int64_t)seed * MT_GOLDEN;
+  const uint64_t base = (uint64_t)(int64_t)seed * MT_GOLDEN;
+  constexpr int64_t kBlock = 1 << 20;
+  std::vector<double> u((size_t)std::min<int64_t>(kBlock, n_rows));
   int64_t need = cnt;
-  for (int64_t r = 0; r < n_rows && need > 0; ++r) {
-    int64_t left = n_rows - r;
-    if (need >= left) {
-      out.push_back(r);
-      --need;
-      continue;
-    }
-    if (mt_uniform(base + (uint64_t)r) * (double)left < (double)need) {
-      out.push_back(r);
-      --need;
+  for (int64_t b0 = 0; b0 < n_rows && need > 0; b0 += kBlock) {
+    const int64_t nb = std::min<int64_t>(kBlock, n_rows - b0);
+#pragma omp parallel for schedule(static) if (nb >= 65536)
+    for (int64_t i = 0; i < nb; ++i) u[(size_t)i] = mt_uniform(base + (uint64_t)(b0 + i));
+    for (int64_t i = 0; i < nb && need > 0; ++i) {
+      const int64_t r = b0 + i;
+      const int64_t left = n_rows - r;
+      if (need >= left || u[(size_t)i] * (double)left < (double)need) {
+        out.push_back(r);
+        --need;
+      }
     }
   }
   return out;
+}
+
+// Ascending sort of non-NaN doubles: LSD radix sort (11-bit digits) of keys
+// whose unsigned order is the numeric order (-0.0 sorts just before +0.0,
+// which compare equal).  Digits that every key shares are skipped.
+static void sort_doubles(std::vector<double>& v, std::vector<uint64_t>& k0, std::vector<uint64_t>& k1) {
+  const size_t n = v.size();
+  if (n < 512) {
+    std::sort(v.begin(), v.end());
+    return;
+  }
+  k0.resize(n);
+  k1.resize(n);
+  for (size_t i = 0; i < n; ++i) {
+    uint64_t b;
+    memcpy(&b, &v[i], 8);
+    k0[i] = (b >> 63) ? ~b : (b | 0x8000000000000000ull);
+  }
+  constexpr int kBits = 11, kBuckets = 1 << kBits, kPasses = (64 + kBits - 1) / kBits;
+  std::vector<uint32_t> cnt((size_t)kPasses * kBuckets, 0u);
+  for (size_t i = 0; i < n; ++i)
+    for (int p = 0; p < kPasses; ++p) ++cnt[(size_t)p * kBuckets + ((k0[i] >> (p * kBits)) & (kBuckets - 1))];
+  uint64_t* src = k0.data();
+  uint64_t* dst = k1.data();
+  for (int p = 0; p < kPasses; ++p) {
+    uint32_t* c = &cnt[(size_t)p * kBuckets];
+    const int shift = p * kBits;
+    if (c[(src[0] >> shift) & (kBuckets - 1)] == n) continue;  // one digit value: order unchanged
+    uint32_t acc = 0;
+    for (int d = 0; d < kBuckets; ++d) {
+      const uint32_t t = c[d];
+      c[d] = acc;
+      acc += t;
+    }
+    for (size_t i = 0; i < n; ++i) dst[c[(src[i] >> shift) & (kBuckets - 1)]++] = src[i];
+    std::swap(src, dst);
+  }
+  for (size_t i = 0; i < n; ++i) {
+    const uint64_t key = src[i];
+    const uint64_t b = (key >> 63) ? (key & 0x7fffffffffffffffull) : ~key;
+    memcpy(&v[i], &b, 8);
+  }
 }
 
 static void emit_edges(const std::vector<double>& below, const std::vector<double>& above,
@@ -140,6 +188,7 @@ BinMapper fit_bins(const double* x, int64_t n_rows, int n_features, const Binnin
   {
     std::vector<double> col, below, above, out, levels;
     std::vector<int64_t> level_counts;
+    std::vector<uint64_t> key0, key1;
 #pragma omp for schedule(dynamic, 1)
     for (int f = 0; f < n_features; ++f) {
       if (m.is_cat[f]) {
@@ -168,7 +217,7 @@ BinMapper fit_bins(const double* x, int64_t n_rows, int n_features, const Binnin
       below.clear();
       above.clear();
       // Sort once; -0.0 and 0.0 compare equal and are one level.
-      std::sort(col.begin(), col.end());
+      sort_doubles(col, key0, key1);
       levels.clear();
       level_counts.clear();
       bool distinct_fits = n_valid >= 1;
