@@ -389,10 +389,17 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
   }
   if (Bt.root) return;  // the root's rows are already in place
   constexpr int TILE = 256 * ITEMS;
-  __shared__ int s_warp_l[8], s_wv[8], s_cl[8], s_cr[8];
-  __shared__ unsigned long long s_base_l, s_base_r;
+  // Per-warp left/right counts of each item row of a tile, and the tile's
+  // cursor bases; double-buffered by tile parity, so a tile needs two block
+  // barriers: counts written -> cursors claimed -> scatter.  (A warp can only
+  // refill a buffer after both barriers of the next tile, which every warp
+  // reaches only after finishing its reads of this one.)
+  __shared__ int s_cl[2][ITEMS][8], s_cr[2][ITEMS][8];
+  __shared__ unsigned long long s_base_l[2], s_base_r[2];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  for (long long tile = blockIdx.x; tile < Bt.n_tiles; tile += gridDim.x) {
+  const unsigned below = (1u << lane) - 1u;
+  int par = 0;
+  for (long long tile = blockIdx.x; tile < Bt.n_tiles; tile += gridDim.x, par ^= 1) {
     int it = 0;
     while (it + 1 < n_items && Bt.items[it + 1].tile0 <= tile) ++it;
     BatchItem& P = Bt.items[it];
@@ -405,11 +412,11 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
     const long long t0 = begin + (tile - P.tile0) * TILE;
     int rr[ITEMS];
     PairT pp[ITEMS];
+    unsigned bl[ITEMS], br[ITEMS];
     bool valid[ITEMS], left[ITEMS];
-    int my_l = 0, my_valid = 0;
 #pragma unroll
-    for (int j = 0; j < ITEMS; ++j) {
-      long long i = t0 + (long long)j * 256 + threadIdx.x;
+    for (int j = 0; j < ITEMS; ++j) {  // every gather in flight before the first ballot
+      const long long i = t0 + (long long)j * 256 + threadIdx.x;
       valid[j] = i < end;
       left[j] = false;
       if (valid[j]) {
@@ -417,61 +424,53 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
         pp[j] = src_pairs[i];
         left[j] = goes_left(P, col[rr[j]]);
       }
-      my_l += left[j];
-      my_valid += valid[j];
     }
-    int wl = my_l, wv = my_valid;
-    for (int k = 16; k > 0; k >>= 1) {
-      wl += __shfl_xor_sync(0xffffffffu, wl, k);
-      wv += __shfl_xor_sync(0xffffffffu, wv, k);
-    }
-    if (lane == 0) {
-      s_warp_l[w] = wl;
-      s_wv[w] = wv;
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+      bl[j] = __ballot_sync(0xffffffffu, left[j]);
+      br[j] = __ballot_sync(0xffffffffu, valid[j]) & ~bl[j];
+      if (lane == 0) {
+        s_cl[par][j][w] = __popc(bl[j]);
+        s_cr[par][j][w] = __popc(br[j]);
+      }
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-      int tl = 0, tv = 0;
-      for (int k = 0; k < 8; ++k) {
-        tl += s_warp_l[k];
-        tv += s_wv[k];
-      }
-      s_base_l = atomicAdd(&P.cursor_left, (unsigned long long)tl);
-      unsigned long long nr = (unsigned long long)(tv - tl);
-      unsigned long long o = atomicAdd(&P.cursor_right, nr);
-      s_base_r = (unsigned long long)end - o - nr;  // rights fill from the back
+      int tl = 0, tr = 0;
+      for (int j = 0; j < ITEMS; ++j)
+        for (int k = 0; k < 8; ++k) {
+          tl += s_cl[par][j][k];
+          tr += s_cr[par][j][k];
+        }
+      s_base_l[par] = atomicAdd(&P.cursor_left, (unsigned long long)tl);
+      const unsigned long long o = atomicAdd(&P.cursor_right, (unsigned long long)tr);
+      s_base_r[par] = (unsigned long long)end - o - (unsigned long long)tr;  // rights fill from the back
     }
     __syncthreads();
-    int run_l = 0, run_r = 0;  // ranks in element order (j major, thread minor)
+    // ranks in element order (item row j major, then warp, then lane)
+    long long run_l = begin + (long long)s_base_l[par], run_r = (long long)s_base_r[par];
 #pragma unroll
     for (int j = 0; j < ITEMS; ++j) {
-      unsigned bl = __ballot_sync(0xffffffffu, left[j]);
-      unsigned bv = __ballot_sync(0xffffffffu, valid[j]);
-      unsigned br = bv & ~bl;
-      if (lane == 0) {
-        s_cl[w] = __popc(bl);
-        s_cr[w] = __popc(br);
-      }
-      __syncthreads();
       int pre_l = 0, pre_r = 0, tot_l = 0, tot_r = 0;
+#pragma unroll
       for (int k = 0; k < 8; ++k) {
+        const int cl = s_cl[par][j][k], cr = s_cr[par][j][k];
         if (k < w) {
-          pre_l += s_cl[k];
-          pre_r += s_cr[k];
+          pre_l += cl;
+          pre_r += cr;
         }
-        tot_l += s_cl[k];
-        tot_r += s_cr[k];
+        tot_l += cl;
+        tot_r += cr;
       }
-      unsigned below = (1u << lane) - 1u;
-      if (valid[j]) {
-        long long dst = left[j] ? begin + (long long)s_base_l + run_l + pre_l + __popc(bl & below)
-                                : (long long)s_base_r + run_r + pre_r + __popc(br & below);
+      const unsigned m = 1u << lane;
+      if ((bl[j] | br[j]) & m) {
+        const long long dst = (bl[j] & m) ? run_l + pre_l + __popc(bl[j] & below)
+                                          : run_r + pre_r + __popc(br[j] & below);
         dst_rows[dst] = rr[j];
         dst_pairs[dst] = pp[j];
       }
       run_l += tot_l;
       run_r += tot_r;
-      __syncthreads();
     }
   }
 }

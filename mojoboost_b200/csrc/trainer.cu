@@ -152,6 +152,14 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
 
   TrainStats stats;
   auto t0 = std::chrono::steady_clock::now();
+  // MOJOTREES_TRACE_UPLOAD=1 prints the set-up phases to stderr
+  const bool trace_up = getenv("MOJOTREES_TRACE_UPLOAD") != nullptr;
+  auto mark = [&](const char* what) {
+    if (!trace_up) return;
+    cudaStreamSynchronize(st);
+    fprintf(stderr, "setup: %-28s %8.1f ms\n", what,
+            std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() * 1e3);
+  };
   const int Fp = (F + 15) / 16 * 16;
   DevBuf<uint8_t> d_bins_cm, d_bins_rm;
   d_bins_cm.alloc((size_t)F * N);
@@ -168,6 +176,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     stats.kernel_launches++;
   }
   DevBuf<double> d_y, d_raw, d_prob;
+  mark("bins uploaded, transposed");
   d_y.alloc(N);
   MTB_CUDA(cudaMemcpyAsync(d_y.p, in.labels, sizeof(double) * N, cudaMemcpyHostToDevice, st));
   d_raw.alloc((size_t)N * K);
@@ -179,6 +188,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   Collective* coll = in.coll;
   const int world = coll ? coll->world() : 1;
   const long long N_global = coll ? in.n_rows_global : N;
+  mark("labels, raw allocated");
   DevBuf<double> d_red;
   d_red.alloc(2 * (size_t)std::max(world, K) + 8);
   // every rank learns whether any rank's input is invalid before any throws
@@ -263,6 +273,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     MTB_CUDA(cudaStreamSynchronize(st));
   }
 
+  mark("initial scores");
   DevBuf<int> d_missing, d_ncats, d_feats;
   d_missing.alloc(F);
   d_ncats.alloc(F);
@@ -339,6 +350,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   d_order.alloc(kMaxPool);
   d_values.alloc(kMaxPool);
   MTB_CUDA(cudaStreamSynchronize(st));
+  mark("work buffers");
   stats.upload_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
 
   // Histogram launch geometry: as many features per CTA as one SM's shared
