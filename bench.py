@@ -72,27 +72,51 @@ def params(rounds, quant=True, extra=None):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clock and throttle reasons, read through NVML every ~10 ms with host
+    timestamps (reads only), so the summary can cover just the timed rounds.
+    Falls back to nvidia-smi queries when NVML is not importable."""
 
-    def __init__(self, gpu_index):
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
+
+    def __init__(self, gpu_index, period=0.01):
         self.gpu = gpu_index
-        self.samples = []
+        self.period = period
+        self.samples = []  # (monotonic time, sm MHz, max sm MHz, reason names)
         self._stop = threading.Event()
         self._t = threading.Thread(target=self._run, daemon=True)
 
     def _run(self):
-        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-             "clocks_event_reasons.sw_power_cap")
-        while not self._stop.is_set():
-            try:
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+
+            def read():
+                sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                return sm, mx, {n for n, b in self.REASONS if bits & b}
+        except Exception:
+            q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap")
+
+            def read():
                 out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}",
                                       "--format=csv,noheader,nounits"], capture_output=True, text=True,
                                      timeout=5).stdout.strip()
-                self.samples.append([v.strip() for v in out.split(",")])
+                v = [x.strip() for x in out.split(",")]
+                return float(v[0]), float(v[1]), {n for (n, _), x in zip(self.REASONS, v[2:6])
+                                                  if x.lower() == "active"}
+        while not self._stop.is_set():
+            try:
+                t = time.monotonic()
+                sm, mx_, rs = read()
+                self.samples.append(((t + time.monotonic()) / 2, sm, mx_, rs))
             except Exception:
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(self.period)
 
     def __enter__(self):
         self._t.start()
@@ -102,20 +126,20 @@ class ClockSampler:
         self._stop.set()
         self._t.join(timeout=10)
 
-    def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for s in self.samples:
-            try:
-                sm.append(float(s[0]))
-                mx = float(s[1])
-                for n, v in zip(names, s[3:7]):
-                    if v.lower() == "active":
-                        reasons.add(n)
-            except (ValueError, IndexError):
-                continue
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+    def summary(self, window=None):
+        """Median SM clock and the reasons seen, over the samples inside
+        window = (t0, t1) (monotonic seconds) when given."""
+        sel = [s for s in self.samples if window is None or window[0] <= s[0] <= window[1]]
+        sm = [s[1] for s in sel]
+        reasons = set()
+        for s in sel:
+            reasons |= s[3]
+        mx = self.samples[-1][2] if self.samples else None
+        out = {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+               "samples": len(sm)}
+        if window is not None:
+            out["window"] = "timed rounds (host window ending when the fit returned, their device time long)"
+        return out
 
 
 def measured_peak():
@@ -205,6 +229,7 @@ def run_gpu(args):
                                        missing_bin=mbin, n_categories=ncat)
         else:
             model = mb.train_binned(bins, nb, y, p, missing_bin=mbin, n_categories=ncat)
+        t_fit_end = time.monotonic()
     rs = model.round_stats()[args.warmup:args.warmup + args.steps]
     st = model.stats()
     dev_ms = float(np.sum(rs[:, 0]))
@@ -270,7 +295,7 @@ def run_gpu(args):
         "phase_ms_per_round": phases,
         "e2e": e2e,
         "gpu_launches": int(np.sum(rs[:, 4])),
-        "clocks": clocks.summary(),
+        "clocks": clocks.summary((t_fit_end - dev_ms / 1000.0 - 0.005, t_fit_end)),
     }
     if not args.no_cpu_baseline and world == 1:
         try:

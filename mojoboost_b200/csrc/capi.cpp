@@ -381,6 +381,24 @@ int32_t train_binned(const uint8_t* bins, int64_t n_rows, int64_t n_features, in
   if (mapper) {
     h->m.has_mapper = true;
     h->m.mapper = *mapper;
+  } else {
+    // pre-binned columns: an edge-free mapper records the bin width, the
+    // missing bins and the categorical bins 1..n (codes 0..n-1), so the
+    // model can be written to a model file; raw values cannot be binned
+    mtb::BinMapper& mp = h->m.mapper;
+    mp.n_features = (int)n_features;
+    mp.n_bins = n_bins;
+    mp.edge_offsets.assign((size_t)n_features + 1, 0);
+    mp.missing_bin = missing;
+    mp.is_cat.assign((size_t)n_features, 0);
+    mp.cat_offsets.assign(1, 0);
+    for (int64_t f = 0; f < n_features; ++f) {
+      if (ncats[f] >= 0) {
+        mp.is_cat[f] = 1;
+        for (int c = 0; c < ncats[f]; ++c) mp.cat_codes.push_back(c);
+      }
+      mp.cat_offsets.push_back((int64_t)mp.cat_codes.size());
+    }
   }
   *out_model = h.release();
   return MOJOTREES_OK;
@@ -622,46 +640,20 @@ int32_t mojotrees_b200_predict_binned_u8(const MojoTreesModel* model, const uint
 
 static const char kMagic[] = "mojotrees-b200 v1";
 
+// Model files use the reference's text format v4 (serialize.mojo:999-1119):
+// floats as their IEEE-754 bit patterns, so a round trip is bit-exact.
 int32_t mojotrees_save_model(const MojoTreesModel* model, const char* path, MojoTreesError* error) {
   return guarded(
       error,
       [&]() -> int32_t {
         if (!model || !path) throw InvalidArgument("null pointer argument");
-        const mtb::Model& m = model->m;
-        std::ofstream os(path);
-        if (!os) throw std::runtime_error(std::string("cannot open '") + path + "' for writing");
-        os << kMagic << "\n";
-        os.precision(17);
-        os << m.objective << " " << m.num_class << " " << m.n_features << " " << std::hexfloat << m.learning_rate
-           << std::defaultfloat << " " << m.trees.size() << " " << (m.has_mapper ? 1 : 0) << "\n";
-        for (double b : m.base_scores) os << std::hexfloat << b << " ";
-        os << std::defaultfloat << "\n";
-        if (m.has_mapper) {
-          const mtb::BinMapper& mp = m.mapper;
-          os << mp.n_bins << " " << mp.edges.size() << " " << mp.cat_codes.size() << "\n";
-          for (double e : mp.edges) os << std::hexfloat << e << " ";
-          os << std::defaultfloat << "\n";
-          for (auto o : mp.edge_offsets) os << o << " ";
-          os << "\n";
-          for (int v : mp.missing_bin) os << v << " ";
-          os << "\n";
-          for (auto v : mp.is_cat) os << (int)v << " ";
-          os << "\n";
-          for (auto v : mp.cat_codes) os << v << " ";
-          os << "\n";
-          for (auto v : mp.cat_offsets) os << v << " ";
-          os << "\n";
-        }
-        for (auto& t : m.trees) {
-          os << t.size() << "\n";
-          for (auto& nd : t) {
-            os << nd.feature << " " << nd.thr << " " << nd.left << " " << nd.right << " " << nd.dleft << " "
-               << nd.mbin << " " << nd.is_cat << " " << nd.bits[0] << " " << nd.bits[1] << " " << nd.bits[2] << " "
-               << nd.bits[3] << " " << std::hexfloat << nd.value << " " << nd.gain << std::defaultfloat << " "
-               << nd.count << "\n";
-          }
-        }
-        if (!os) throw std::runtime_error("write failed");
+        std::ostringstream os;
+        mtb::save_model_v4(model->m, os);
+        std::ofstream f(path);
+        if (!f) throw std::runtime_error(std::string("cannot open '") + path + "' for writing");
+        f << os.str();
+        f.flush();
+        if (!f) throw std::runtime_error("write failed");
         return MOJOTREES_OK;
       },
       MOJOTREES_ERROR_IO);
@@ -682,7 +674,16 @@ int32_t mojotrees_load_model(const char* path, MojoTreesModel** out_model, MojoT
         if (!is) throw std::runtime_error(std::string("cannot open '") + path + "'");
         std::string magic;
         std::getline(is, magic);
-        if (magic != kMagic) throw std::runtime_error("not a mojotrees-b200 v1 model file");
+        if (magic != kMagic) {
+          // the reference's token format (v1-v4)
+          std::ostringstream all;
+          all << magic << '\n' << is.rdbuf();
+          std::unique_ptr<MojoTreesModel> h(new MojoTreesModel());
+          h->m = mtb::load_model_text(all.str());
+          *out_model = h.release();
+          return MOJOTREES_OK;
+        }
+        // this library's earlier private format
         std::unique_ptr<MojoTreesModel> h(new MojoTreesModel());
         mtb::Model& m = h->m;
         size_t n_trees;

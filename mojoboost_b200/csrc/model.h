@@ -3,6 +3,7 @@
 #pragma once
 #include <stdint.h>
 
+#include <iosfwd>
 #include <memory>
 #include <string>
 #include <vector>
@@ -90,5 +91,12 @@ struct Model {
   std::vector<double> train_scores;  // when keep_training_scores
   TrainStats stats;
 };
+
+// Model files in the reference's token format (model_io.cpp): v4 written,
+// v1-v4 read.  A model trained on pre-binned columns carries an edge-free
+// mapper (its bin width, missing bins and categorical counts) and
+// has_mapper = false.
+void save_model_v4(const Model& m, std::ostream& os);
+Model load_model_text(const std::string& content);
 
 }  // namespace mtb

@@ -1,0 +1,404 @@
+// Model files in the reference's text format (src/mojotrees/serialize.mojo):
+// a whitespace-separated token stream, every float written as the decimal
+// value of its IEEE-754 bit pattern, so a save/load round trip is bit-exact.
+//
+// Writer: format v4 (serialize.mojo:999-1119 save_model /
+// save_multiclass_model, :431-446 mapper, :485-543 trees, :545-572
+// categorical).  Reader: v1-v4 (serialize.mojo:1121-1370, 1463-1580).  v5
+// files carry linear leaves, CTR tables or a narrowed feature pool, none of
+// which this library trains or predicts with, and are refused by name.
+#include <stdint.h>
+#include <string.h>
+
+#include <cmath>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "model.h"
+#include "trainer.h"
+
+namespace mtb {
+namespace {
+
+constexpr int kCatWords = 4;  // 256-bit category sets (categorical.mojo:115)
+
+std::string f64_token(double x) {
+  uint64_t b;
+  memcpy(&b, &x, 8);
+  return std::to_string(b);
+}
+
+// A tree as the format lays it out, from this library's node records.
+struct TreeArrays {
+  std::vector<long long> feature, thr, left, right, dleft, mbin, cat_off;
+  std::vector<double> value, gain, count;
+  std::vector<uint64_t> pool;
+  int n_leaves = 0;
+};
+
+TreeArrays to_arrays(const std::vector<HostNode>& t) {
+  TreeArrays a;
+  for (const HostNode& nd : t) {
+    const bool leaf = nd.feature < 0;
+    a.n_leaves += leaf ? 1 : 0;
+    a.feature.push_back(leaf ? -1 : nd.feature);
+    a.left.push_back(leaf ? -1 : nd.left);
+    a.right.push_back(leaf ? -1 : nd.right);
+    a.value.push_back(nd.value);
+    a.gain.push_back(leaf ? 0.0 : nd.gain);
+    a.count.push_back((double)nd.count);
+    // tree.mojo:461-480: a categorical node routes by its set alone
+    if (!leaf && nd.is_cat) {
+      a.thr.push_back(-1);
+      a.dleft.push_back(0);
+      a.mbin.push_back(-1);
+      a.cat_off.push_back((long long)a.pool.size());
+      for (int w = 0; w < kCatWords; ++w) a.pool.push_back(nd.bits[w]);
+    } else {
+      a.thr.push_back(leaf ? -1 : nd.thr);
+      a.dleft.push_back(!leaf && nd.dleft ? 1 : 0);
+      a.mbin.push_back(leaf ? -1 : nd.mbin);
+      a.cat_off.push_back(-1);
+    }
+  }
+  return a;
+}
+
+template <typename T>
+void write_row(std::ostream& os, const std::vector<T>& v) {
+  for (const T& x : v) os << x << ' ';
+  os << '\n';
+}
+
+void write_f64_row(std::ostream& os, const std::vector<double>& v) {
+  for (double x : v) os << f64_token(x) << ' ';
+  os << '\n';
+}
+
+}  // namespace
+
+void save_model_v4(const Model& m, std::ostream& os) {
+  const BinMapper& mp = m.mapper;
+  if (mp.n_features != m.n_features || (int64_t)mp.edge_offsets.size() != (int64_t)m.n_features + 1)
+    throw std::runtime_error("model has no bin mapper to write");
+  os << "mojotrees v4\n";
+  if (m.objective == OBJECTIVE_MULTICLASS) {
+    os << "multiclass " << m.num_class << '\n';
+    os << "learning_rate " << f64_token(m.learning_rate) << '\n';
+    os << "base_scores";
+    for (int k = 0; k < m.num_class; ++k) os << ' ' << f64_token(m.base_scores[k]);
+    os << '\n';
+  } else {
+    os << "objective " << m.objective << '\n';
+    os << "learning_rate " << f64_token(m.learning_rate) << '\n';
+    os << "base_score " << f64_token(m.base_scores[0]) << '\n';
+  }
+  // mapper: header, edges, offsets, per-feature missing bins
+  os << "mapper " << mp.n_features << ' ' << mp.n_bins << ' ' << mp.edges.size() << '\n';
+  write_f64_row(os, mp.edges);
+  write_row(os, mp.edge_offsets);
+  write_row(os, mp.missing_bin);
+  // categorical tables, only when a feature is categorical
+  bool any_cat = false;
+  for (uint8_t c : mp.is_cat) any_cat = any_cat || c;
+  if (any_cat) {
+    os << "categorical " << mp.n_features << ' ' << mp.cat_codes.size() << '\n';
+    for (int f = 0; f < mp.n_features; ++f) os << (mp.is_cat[f] ? 1 : 0) << ' ';
+    os << '\n';
+    write_row(os, mp.cat_codes);
+    if (mp.cat_offsets.empty()) {
+      for (int f = 0; f <= mp.n_features; ++f) os << "0 ";
+      os << '\n';
+    } else {
+      write_row(os, mp.cat_offsets);
+    }
+  }
+  os << "trees " << m.trees.size() << '\n';
+  for (const auto& t : m.trees) {
+    const TreeArrays a = to_arrays(t);
+    os << "tree " << t.size() << ' ' << a.n_leaves << '\n';
+    write_row(os, a.feature);
+    write_row(os, a.thr);
+    write_row(os, a.left);
+    write_row(os, a.right);
+    write_f64_row(os, a.value);
+    write_row(os, a.dleft);
+    write_row(os, a.mbin);
+    bool covers = !a.count.empty();
+    for (double c : a.count) covers = covers && c > 0.0;
+    os << "counts " << (covers ? 1 : 0) << '\n';
+    if (covers) write_f64_row(os, a.count);
+    bool gains = false;
+    for (double g : a.gain) gains = gains || g > 0.0;
+    os << "gains " << (gains ? 1 : 0) << '\n';
+    if (gains) write_f64_row(os, a.gain);
+    if (!a.pool.empty()) {
+      os << "cat " << a.pool.size() << '\n';
+      write_row(os, a.cat_off);
+      write_row(os, a.pool);
+    }
+  }
+}
+
+namespace {
+
+struct Tokens {
+  std::vector<std::string> t;
+  size_t pos = 0;
+  explicit Tokens(const std::string& content) {
+    std::istringstream is(content);
+    std::string s;
+    while (is >> s) t.push_back(s);
+  }
+  const std::string& next() {
+    if (pos >= t.size()) throw std::runtime_error("unexpected end of model file");
+    return t[pos++];
+  }
+  std::string peek() const { return pos < t.size() ? t[pos] : std::string(); }
+  void expect(const char* tag) {
+    if (next() != tag) throw std::runtime_error(std::string("corrupt model file: expected '") + tag + "'");
+  }
+  long long next_int() {
+    const std::string& s = next();
+    size_t i = 0;
+    bool neg = false;
+    if (!s.empty() && s[0] == '-') {
+      neg = true;
+      i = 1;
+    }
+    if (i >= s.size()) throw std::runtime_error("corrupt model file: empty integer token");
+    unsigned long long v = 0;
+    for (; i < s.size(); ++i) {
+      if (s[i] < '0' || s[i] > '9') throw std::runtime_error("corrupt model file: invalid integer token '" + s + "'");
+      const unsigned long long d = (unsigned long long)(s[i] - '0');
+      if (v > (9223372036854775807ull - d) / 10) throw std::runtime_error("corrupt model file: integer out of range");
+      v = v * 10 + d;
+    }
+    return neg ? -(long long)v : (long long)v;
+  }
+  // serialize.mojo:218-242: the whole u64 range, exactly
+  uint64_t next_u64() {
+    const std::string& s = next();
+    if (s.empty()) throw std::runtime_error("corrupt model file: empty integer token");
+    uint64_t v = 0;
+    for (char c : s) {
+      if (c < '0' || c > '9') throw std::runtime_error("corrupt model file: invalid digit in '" + s + "'");
+      const uint64_t d = (uint64_t)(c - '0');
+      if (v > (~0ull - d) / 10) throw std::runtime_error("corrupt model file: integer token does not fit in 64 bits");
+      v = v * 10 + d;
+    }
+    return v;
+  }
+  double next_f64() {
+    const uint64_t b = next_u64();
+    double x;
+    memcpy(&x, &b, 8);
+    return x;
+  }
+};
+
+// validation.mojo:1308+ check_tree_topology: internal nodes have two
+// distinct children after them, leaves none, every node but the root is a
+// child exactly once, the leaf count matches the header.
+void check_topology(const std::vector<HostNode>& t, long long n_leaves, int n_features) {
+  const long long n = (long long)t.size();
+  std::vector<int> parents((size_t)n, 0);
+  long long leaves = 0;
+  for (long long i = 0; i < n; ++i) {
+    const HostNode& nd = t[(size_t)i];
+    if (nd.feature >= n_features) throw std::runtime_error("corrupt tree: split feature out of range");
+    if (nd.feature < 0) {
+      ++leaves;
+      continue;
+    }
+    if (nd.left <= i || nd.right <= i || nd.left >= n || nd.right >= n || nd.left == nd.right)
+      throw std::runtime_error("corrupt tree: child index out of order or out of range");
+    ++parents[(size_t)nd.left];
+    ++parents[(size_t)nd.right];
+  }
+  if (n > 0 && parents[0] != 0) throw std::runtime_error("corrupt tree: the root is some node's child");
+  for (long long i = 1; i < n; ++i)
+    if (parents[(size_t)i] != 1) throw std::runtime_error("corrupt tree: a node is not a child exactly once");
+  if (leaves != n_leaves) throw std::runtime_error("corrupt tree: leaf count does not match the header");
+}
+
+}  // namespace
+
+Model load_model_text(const std::string& content) {
+  Tokens r(content);
+  if (r.next() != "mojotrees") throw std::runtime_error("not a mojotrees model file");
+  const std::string ver = r.next();
+  int version;
+  if (ver == "v1") version = 1;
+  else if (ver == "v2") version = 2;
+  else if (ver == "v3") version = 3;
+  else if (ver == "v4") version = 4;
+  else if (ver == "v5")
+    throw Unsupported("format v5 model files (linear leaves, CTR tables or a narrowed feature pool) are not "
+                      "covered by this library");
+  else
+    throw std::runtime_error("unsupported model format version '" + ver + "'");
+  if (r.peek() == "feature_names") {  // names are not part of a model here
+    r.next();
+    const long long n = r.next_int();
+    if (n < 1) throw std::runtime_error("corrupt feature_names section");
+    for (long long i = 0; i < n; ++i) r.next();
+  }
+  Model m;
+  const std::string kind = r.next();
+  if (kind == "objective") {
+    const long long obj = r.next_int();
+    if (obj != OBJECTIVE_L2 && obj != OBJECTIVE_BINARY)
+      throw Unsupported("objective code " + std::to_string(obj) + " is not covered by this library");
+    m.objective = (int)obj;
+    m.num_class = 1;
+    r.expect("learning_rate");
+    m.learning_rate = r.next_f64();
+    r.expect("base_score");
+    m.base_scores = {r.next_f64()};
+  } else if (kind == "multiclass") {
+    const long long k = r.next_int();
+    if (k < 2 || k > 1000000) throw std::runtime_error("corrupt model file: n_classes must be at least 2");
+    m.objective = OBJECTIVE_MULTICLASS;
+    m.num_class = (int)k;
+    r.expect("learning_rate");
+    m.learning_rate = r.next_f64();
+    r.expect("base_scores");
+    for (long long i = 0; i < k; ++i) m.base_scores.push_back(r.next_f64());
+  } else {
+    throw std::runtime_error("corrupt model file: unknown model kind");
+  }
+  // mapper (serialize.mojo:1121-1194)
+  BinMapper& mp = m.mapper;
+  r.expect("mapper");
+  const long long nf = r.next_int(), nb = r.next_int(), ne = r.next_int();
+  if (nf < 1 || nf > (1ll << 24) || ne < 0 || ne > (1ll << 32)) throw std::runtime_error("corrupt mapper header");
+  if (nb < 1 || nb > 256) throw std::runtime_error("corrupt mapper: n_bins must be in [1, 256]");
+  mp.n_features = (int)nf;
+  mp.n_bins = (int)nb;
+  mp.edges.resize((size_t)ne);
+  for (auto& e : mp.edges) e = r.next_f64();
+  mp.edge_offsets.resize((size_t)nf + 1);
+  for (auto& o : mp.edge_offsets) o = r.next_int();
+  if (mp.edge_offsets[0] != 0 || mp.edge_offsets[(size_t)nf] != ne) throw std::runtime_error("corrupt mapper offsets");
+  for (long long f = 0; f < nf; ++f) {
+    const long long w = mp.edge_offsets[(size_t)f + 1] - mp.edge_offsets[(size_t)f];
+    if (w < 0 || w > nb - 1) throw std::runtime_error("corrupt mapper offsets");
+  }
+  mp.missing_bin.assign((size_t)nf, -1);
+  if (version >= 2)
+    for (auto& v : mp.missing_bin) {
+      const long long b = r.next_int();
+      if (b < -1 || b >= nb) throw std::runtime_error("corrupt mapper: missing bin out of range");
+      v = (int)b;
+    }
+  mp.is_cat.assign((size_t)nf, 0);
+  mp.cat_offsets.assign((size_t)nf + 1, 0);
+  if (r.peek() == "categorical") {
+    r.next();
+    const long long n_flags = r.next_int(), n_codes = r.next_int();
+    if (n_flags != nf || n_codes < 0 || n_codes > (1ll << 32)) throw std::runtime_error("corrupt categorical header");
+    for (auto& c : mp.is_cat) c = r.next_int() != 0 ? 1 : 0;
+    mp.cat_codes.resize((size_t)n_codes);
+    for (auto& c : mp.cat_codes) c = r.next_int();
+    for (auto& o : mp.cat_offsets) o = r.next_int();
+    if (mp.cat_offsets[0] != 0 || mp.cat_offsets[(size_t)nf] != n_codes)
+      throw std::runtime_error("corrupt categorical offsets");
+    for (long long f = 0; f < nf; ++f) {
+      const long long a = mp.cat_offsets[(size_t)f], b = mp.cat_offsets[(size_t)f + 1];
+      if (b < a || b - a >= nb) throw std::runtime_error("corrupt categorical offsets");
+      if (b > a && !mp.is_cat[(size_t)f]) throw std::runtime_error("corrupt categorical: table on a numerical feature");
+      for (long long i = a + 1; i < b; ++i)
+        if (mp.cat_codes[(size_t)i] <= mp.cat_codes[(size_t)i - 1])
+          throw std::runtime_error("corrupt categorical: codes are not ascending");
+    }
+  }
+  if (r.peek() == "monotone") {  // constraints bind training only; prediction ignores them
+    r.next();
+    const long long n = r.next_int();
+    if (n != nf) throw std::runtime_error("corrupt model file: monotone section size");
+    for (long long i = 0; i < n; ++i) r.next_int();
+  }
+  m.n_features = (int)nf;
+  // trees (serialize.mojo:1235-1370)
+  r.expect("trees");
+  const long long n_trees = r.next_int();
+  if (n_trees < 0 || n_trees > (1ll << 24)) throw std::runtime_error("corrupt model file: tree count");
+  if (n_trees % m.num_class != 0) throw std::runtime_error("corrupt model file: tree count not divisible by classes");
+  bool mapper_fits = true;  // every split is one this mapper's bins can express
+  m.trees.resize((size_t)n_trees);
+  for (auto& t : m.trees) {
+    r.expect("tree");
+    const long long nn = r.next_int(), n_leaves = r.next_int();
+    if (nn < 1 || nn > (1ll << 24) || n_leaves < 1 || n_leaves > nn) throw std::runtime_error("corrupt tree header");
+    t.assign((size_t)nn, HostNode{});
+    for (auto& nd : t) nd.feature = (int)r.next_int();
+    for (auto& nd : t) nd.thr = (int)r.next_int();
+    for (auto& nd : t) nd.left = (int)r.next_int();
+    for (auto& nd : t) nd.right = (int)r.next_int();
+    for (auto& nd : t) nd.value = r.next_f64();
+    if (version >= 2) {
+      for (auto& nd : t) nd.dleft = r.next_int() != 0 ? 1 : 0;
+      for (auto& nd : t) {
+        const long long b = r.next_int();
+        if (b < -1 || b >= nb) throw std::runtime_error("corrupt tree: missing bin out of range");
+        nd.mbin = (int)b;
+      }
+    } else {
+      for (auto& nd : t) nd.mbin = -1;
+    }
+    bool has_counts = version == 3;
+    if (version >= 4) {
+      r.expect("counts");
+      has_counts = r.next_int() != 0;
+    }
+    if (has_counts)
+      for (auto& nd : t) {
+        const double c = r.next_f64();
+        if (!(c >= 0.0)) throw std::runtime_error("corrupt tree: node cover must be positive");
+        nd.count = (long long)c;
+      }
+    if (version >= 4) {
+      r.expect("gains");
+      if (r.next_int() != 0)
+        for (auto& nd : t) {
+          nd.gain = r.next_f64();
+          if (nd.gain != nd.gain) throw std::runtime_error("corrupt tree: split gain is NaN");
+        }
+    }
+    if (version >= 2 && r.peek() == "cat") {
+      r.next();
+      const long long nw = r.next_int();
+      if (nw < 0 || nw % kCatWords != 0 || nw > (1ll << 30)) throw std::runtime_error("corrupt tree: category bitset size");
+      std::vector<long long> off((size_t)nn);
+      for (auto& o : off) {
+        o = r.next_int();
+        if (o < -1 || o > nw - kCatWords || (o >= 0 && o % kCatWords != 0))
+          throw std::runtime_error("corrupt tree: category set offset");
+      }
+      std::vector<uint64_t> pool((size_t)nw);
+      for (auto& w : pool) w = r.next_u64();
+      for (long long i = 0; i < nn; ++i)
+        if (off[(size_t)i] >= 0 && t[(size_t)i].feature >= 0) {
+          HostNode& nd = t[(size_t)i];
+          nd.is_cat = 1;
+          for (int w = 0; w < kCatWords; ++w) nd.bits[w] = pool[(size_t)off[(size_t)i] + w];
+        }
+    }
+    check_topology(t, n_leaves, (int)nf);
+    for (const auto& nd : t) {
+      if (nd.feature < 0) continue;
+      const long long k = mp.edge_offsets[(size_t)nd.feature + 1] - mp.edge_offsets[(size_t)nd.feature];
+      if (nd.is_cat ? !mp.is_cat[(size_t)nd.feature] : nd.thr > k) mapper_fits = false;
+    }
+  }
+  // A model trained on pre-binned columns is written with an edge-free
+  // mapper; its splits then name bins that mapper cannot produce, and
+  // raw-value prediction of it is refused rather than answered wrongly.
+  m.has_mapper = mapper_fits;
+  return m;
+}
+
+}  // namespace mtb
