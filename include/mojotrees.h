@@ -21,7 +21,9 @@
  * "device=gpu" (the default here) never falls back to the CPU; a request the
  * device path does not cover returns MOJOTREES_ERROR_UNSUPPORTED naming what
  * is uncovered.  "device=cpu" is MOJOTREES_ERROR_UNSUPPORTED as well: this
- * library is the accelerated path only.  Prediction runs on the host.
+ * library is the accelerated path only.  Prediction runs on the host unless
+ * mojotrees_predict_ex asks for MOJOTREES_DEVICE_GPU (the same bits; an error
+ * without a CUDA device, never a host fallback).
  */
 #ifndef MOJOTREES_H
 #define MOJOTREES_H
@@ -84,7 +86,8 @@ int32_t mojotrees_predict(const MojoTreesModel *model, const double *data, int64
 /* reference capi/mojotrees.h:205-208 */
 int32_t mojotrees_predict_raw(const MojoTreesModel *model, const double *data, int64_t n_rows,
                               int64_t n_features, double *out_values, int64_t out_len, MojoTreesError *error);
-/* reference capi/mojotrees.h:227-233.  device must be CPU or AUTO (host). */
+/* reference capi/mojotrees.h:227-233.  device CPU or AUTO: host; GPU: rows binned
+ * and trees walked on the current CUDA device, bit-identical to the host. */
 int32_t mojotrees_predict_ex(const MojoTreesModel *model, const double *data, int64_t n_rows, int64_t n_features,
                              int64_t start_iteration, int64_t num_iteration, int32_t flags, int32_t device,
                              double *out_values, int64_t out_len, MojoTreesError *error);

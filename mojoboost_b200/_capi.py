@@ -167,8 +167,11 @@ class Model:
     def num_iterations(self):
         return self._int("mojotrees_model_num_iterations")
 
-    def predict(self, X, raw_score=False, start_iteration=0, num_iteration=0):
-        """X: float64 array [n_rows, n_features] (any layout)."""
+    def predict(self, X, raw_score=False, start_iteration=0, num_iteration=0, device="cpu"):
+        """X: float64 array [n_rows, n_features] (any layout).  device "gpu"
+        bins the rows and walks the trees on the current CUDA device (the
+        same bits as "cpu"); there is no fallback between the two."""
+        dev = {"cpu": DEVICE_CPU, "gpu": DEVICE_GPU, "auto": DEVICE_AUTO}[device]
         X = np.asarray(X, dtype=np.float64)
         n, f = X.shape
         Xc = np.asfortranarray(X)  # column-major: data[f * n + r]
@@ -177,7 +180,7 @@ class Model:
         e = _Err()
         e.check(lib().mojotrees_predict_ex(self.h, Xc.ctypes.data_as(ctypes.c_void_p), n, f, start_iteration,
                                            num_iteration, PREDICT_RAW if raw_score else PREDICT_RESPONSE,
-                                           DEVICE_CPU, _ptr(out), out.size, e.h))
+                                           dev, _ptr(out), out.size, e.h))
         return out.reshape(n, k) if k > 1 else out
 
     def predict_binned(self, bins_fm):

@@ -27,6 +27,7 @@
 #include "capi_util.h"
 #include "collective.h"
 #include "model.h"
+#include "predict.h"
 #include "device_binning.h"
 #include "trainer.h"
 
@@ -333,9 +334,7 @@ int32_t predict_impl(const MojoTreesModel* model, const double* data, int64_t n_
         if (!model || !data || !out) throw InvalidArgument("null pointer argument");
         if (flags != MOJOTREES_PREDICT_RESPONSE && flags != MOJOTREES_PREDICT_RAW)
           throw InvalidArgument("unknown predict flags");
-        if (device == MOJOTREES_DEVICE_GPU)
-          throw mtb::Unsupported("prediction runs on the host in this library; pass MOJOTREES_DEVICE_CPU or AUTO");
-        if (device != MOJOTREES_DEVICE_CPU && device != MOJOTREES_DEVICE_AUTO) throw InvalidArgument("unknown device");
+        if (device != MOJOTREES_DEVICE_CPU && device != MOJOTREES_DEVICE_GPU && device != MOJOTREES_DEVICE_AUTO) throw InvalidArgument("unknown device");
         const mtb::Model& m = model->m;
         if (n_rows < 0) throw InvalidArgument("n_rows must be non-negative");
         if (n_features != m.n_features) throw InvalidArgument("n_features does not match the model");
@@ -345,10 +344,17 @@ int32_t predict_impl(const MojoTreesModel* model, const double* data, int64_t n_
         int64_t iters = (int64_t)m.trees.size() / m.num_class;
         int64_t it0 = std::max<int64_t>(0, std::min(start_iteration, iters));
         int64_t it1 = num_iteration <= 0 ? iters : std::min(iters, it0 + num_iteration);
-        std::vector<uint8_t> bins((size_t)n_rows * n_features);
-        mtb::transform(m.mapper, data, n_rows, bins.data());
         std::vector<double> tmp((size_t)n_rows * m.num_class);
-        raw_scores(m, bins.data(), n_rows, it0, it1, tmp.data());
+        if (device == MOJOTREES_DEVICE_GPU) {
+          // binning and tree walks on the current CUDA device; the response
+          // below stays on the host, so both devices return the same bits
+          if (mtb::cuda_device_count() < 1) throw mtb::Unsupported("device=gpu prediction: no CUDA device is available");
+          mtb::predict_raw_device(m, data, n_rows, it0, it1, tmp.data());
+        } else {
+          std::vector<uint8_t> bins((size_t)n_rows * n_features);
+          mtb::transform(m.mapper, data, n_rows, bins.data());
+          raw_scores(m, bins.data(), n_rows, it0, it1, tmp.data());
+        }
         if (flags == MOJOTREES_PREDICT_RESPONSE) response(m, n_rows, tmp.data());
         memcpy(out, tmp.data(), sizeof(double) * tmp.size());
         return MOJOTREES_OK;
