@@ -496,10 +496,13 @@ constexpr int kQuantCountBits = 15;
 //                cell, so twice the features of HL_QUANT fit one CTA.
 //   HL_FIXED_CH  plane 0: g, plane 1: count (hessian constant)
 //   HL_FIXED     planes g, h, count
-enum HistLayout : int { HL_QUANT = 0, HL_QUANT16 = 1, HL_FIXED_CH = 2, HL_FIXED = 3 };
+//   HL_QUANT16R  the cells of HL_QUANT16; a chunk's row id, g + g_lim and h
+//                travel as one shuffled word (row << 6 | h << 3 | g + g_lim),
+//                for fewer than 2^26 rows and 2 g_lim, h_lim <= 7
+enum HistLayout : int { HL_QUANT = 0, HL_QUANT16 = 1, HL_FIXED_CH = 2, HL_FIXED = 3, HL_QUANT16R = 4 };
 
 __host__ __device__ constexpr int hist_layout_words(int layout, int cells) {
-  return layout == HL_QUANT16 ? cells + cells / 2 : layout == HL_FIXED ? 3 * cells : 2 * cells;
+  return (layout == HL_QUANT16 || layout == HL_QUANT16R) ? cells + cells / 2 : layout == HL_FIXED ? 3 * cells : 2 * cells;
 }
 
 __device__ __forceinline__ void built_range(const BatchItem& P, long long& b, long long& cnt) {
@@ -581,9 +584,12 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
                              const int* __restrict__ rows0, const int* __restrict__ rows1,
                              const void* __restrict__ pairs0, const void* __restrict__ pairs1, int* hs,
                              long long rows_per_flush, int g_lim, unsigned int* p0) {
-  static_assert(LAYOUT != HL_QUANT16 || NPL % 2 == 0, "packed cells pair features");
+  constexpr bool PR = LAYOUT == HL_QUANT16R;          // row id packed with the gradient pair
+  constexpr bool Q16 = LAYOUT == HL_QUANT16 || PR;     // 16-bit packed cells
+  static_assert(!Q16 || NPL % 2 == 0, "packed cells pair features");
+  static_assert(!(PR && MTB_HIST_PIPELINE), "the pipelined walk does not unpack row words");
   constexpr int FG = 32 * NPL;
-  constexpr int MODE = (LAYOUT == HL_QUANT || LAYOUT == HL_QUANT16) ? MODE_QUANT : MODE_FIXED;
+  constexpr int MODE = (LAYOUT == HL_QUANT || Q16) ? MODE_QUANT : MODE_FIXED;
   constexpr bool CONST_H = LAYOUT == HL_FIXED_CH;
   constexpr int U = kHistUnroll;
   const int cs = (int)cluster.num_blocks();
@@ -622,7 +628,7 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
     for (int j = 0; j < NPL; ++j) {
       const uint32_t a = sbase + (((bw >> (8 * j)) & 0xffu) << 7);
       shared_red_add(a + j * kFeat, x0);
-      if (LAYOUT == HL_QUANT16) {
+      if (Q16) {
         // plane B: features 2k and 2k+1 share a word (low and high half)
         shared_red_add(a + 4u * cells + (j >> 1) * kFeat, (j & 1) ? x1 << 16 : x1);
       } else {
@@ -654,7 +660,9 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
         if (MODE == MODE_QUANT) {
           uint16_t pr = __ldg(reinterpret_cast<const uint16_t*>(pairs) + i);
           int g = (int)(int8_t)(pr & 0xff);
-          if (LAYOUT == HL_QUANT16) {
+          if (PR) {
+            x0 = ((unsigned int)r << 6) | ((unsigned int)(pr >> 8) << 3) | (unsigned int)(g + g_lim);
+          } else if (Q16) {
             // g + g_lim and h both fit 8 bits here: carry both in one word
             // (bits 0-7 and 8-15) so the chunk walk needs one shuffle for them
             x0 = (unsigned int)(g + g_lim) | ((unsigned int)(pr >> 8) << 8) | (1u << 16);
@@ -696,7 +704,7 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
 #pragma unroll
           for (int u = 0; u < U; ++u) {
             unsigned int x0 = __shfl_sync(0xffffffffu, ca0, u0 + u), x1;
-            if (LAYOUT == HL_QUANT16) {
+            if (Q16) {
               x1 = (x0 >> 8) & 0xffu;
               x0 &= 0xffff00ffu;
             } else {
@@ -710,16 +718,29 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
 #else
 #pragma unroll
         for (int u0 = 0; u0 < 32; u0 += U) {
-          unsigned int bw[U];
+          unsigned int bw[U], pw[U];
 #pragma unroll
           for (int u = 0; u < U; ++u) {
-            const int r = __shfl_sync(0xffffffffu, cr, u0 + u);
+            int r;
+            if (PR) {
+              pw[u] = __shfl_sync(0xffffffffu, ca0, u0 + u);
+              r = (int)(pw[u] >> 6);
+            } else {
+              r = __shfl_sync(0xffffffffu, cr, u0 + u);
+            }
             bw[u] = BinWord<NPL>::load(bcol + (size_t)(unsigned int)r * (unsigned int)Fp);
           }
 #pragma unroll
           for (int u = 0; u < U; ++u) {
-            unsigned int x0 = __shfl_sync(0xffffffffu, ca0, u0 + u), x1;
-            if (LAYOUT == HL_QUANT16) {
+            unsigned int x0, x1;
+            if (PR) {
+              x0 = (pw[u] & 7u) | (1u << 16);
+              x1 = (pw[u] >> 3) & 7u;
+              add_row(bw[u], x0, x1);
+              continue;
+            }
+            x0 = __shfl_sync(0xffffffffu, ca0, u0 + u);
+            if (Q16) {
               x1 = (x0 >> 8) & 0xffu;
               x0 &= 0xffff00ffu;
             } else {
@@ -732,9 +753,15 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
       } else {
         const int n_in = (int)(pe - c0);
         for (int u = 0; u < n_in; ++u) {
+          if (PR) {
+            const unsigned int w = __shfl_sync(0xffffffffu, ca0, u);
+            add_row(BinWord<NPL>::load(bcol + (size_t)(w >> 6) * (unsigned int)Fp), (w & 7u) | (1u << 16),
+                    (w >> 3) & 7u);
+            continue;
+          }
           const int r = __shfl_sync(0xffffffffu, cr, u);
           unsigned int x0 = __shfl_sync(0xffffffffu, ca0, u), x1;
-          if (LAYOUT == HL_QUANT16) {
+          if (Q16) {
             x1 = (x0 >> 8) & 0xffu;
             x0 &= 0xffff00ffu;
           } else {
@@ -756,7 +783,7 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
       for (int rk = 0; rk < cs; ++rk) {
         const unsigned int* q0 = cluster.map_shared_rank(p0, rk);
         const unsigned int* q1 = q0 + cells;
-        if (LAYOUT == HL_QUANT16) {
+        if (Q16) {
           const unsigned int x = q0[c];
           cnt += (int)(x >> 16);
           g += (int)(x & 0xffffu);
@@ -776,7 +803,7 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
         }
       }
       if (cnt == 0) continue;
-      if (LAYOUT == HL_QUANT16) g -= g_lim * cnt;  // sum of (g + g_lim) -> sum of g
+      if (Q16) g -= g_lim * cnt;  // sum of (g + g_lim) -> sum of g
       int* cellp = hs + (f * 3) * B + bin;
       atomicAdd(cellp, g);
       if (!(MODE == MODE_FIXED && CONST_H)) atomicAdd(cellp + B, h);

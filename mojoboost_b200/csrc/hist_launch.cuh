@@ -86,6 +86,8 @@ void launch_hist_t(const HistLaunch& hl, cudaStream_t st, const Batch* batch, co
     case HL_QUANT * 8 + 4: { constexpr int V = 4, L = HL_QUANT; EXPR; } break;                        \
     case HL_QUANT16 * 8 + 2: { constexpr int V = 2, L = HL_QUANT16; EXPR; } break;                    \
     case HL_QUANT16 * 8 + 4: { constexpr int V = 4, L = HL_QUANT16; EXPR; } break;                    \
+    case HL_QUANT16R * 8 + 2: { constexpr int V = 2, L = HL_QUANT16R; EXPR; } break;                  \
+    case HL_QUANT16R * 8 + 4: { constexpr int V = 4, L = HL_QUANT16R; EXPR; } break;                  \
     case HL_FIXED_CH * 8 + 1: { constexpr int V = 1, L = HL_FIXED_CH; EXPR; } break;                  \
     case HL_FIXED_CH * 8 + 2: { constexpr int V = 2, L = HL_FIXED_CH; EXPR; } break;                  \
     case HL_FIXED_CH * 8 + 4: { constexpr int V = 4, L = HL_FIXED_CH; EXPR; } break;                  \
@@ -132,9 +134,15 @@ inline void choose_hist_layout(HistLaunch& hl, int mode, bool const_h, int quant
 // rows) whose cells fit the shared-memory budget, then the smallest such
 // group.  Row chunks are sized to fill every SM; CTAs of a feature group form
 // clusters of up to 8 that merge through DSMEM.
-inline HistLaunch choose_hist_launch(int mode, bool const_h, int quant_bins, int B, int Fp, int n_sm) {
+// n_rows > 0 (row ids below it) lets 16-bit packed cells with narrow
+// quantizers use HL_QUANT16R; MOJOTREES_HIST_NO_ROWPACK turns that off.
+inline HistLaunch choose_hist_launch(int mode, bool const_h, int quant_bins, int B, int Fp, int n_sm,
+                                     long long n_rows = 0) {
   HistLaunch hl;
   choose_hist_layout(hl, mode, const_h, quant_bins);
+  if (hl.layout == HL_QUANT16 && n_rows > 0 && n_rows <= (1ll << 26) && quant_bins <= 7
+      && !getenv("MOJOTREES_HIST_NO_ROWPACK"))
+    hl.layout = HL_QUANT16R;
   // MOJOTREES_HIST_SMEM_KB / MOJOTREES_HIST_CLUSTER override the shared-memory
   // budget per CTA and the largest cluster size (tuning knobs)
   size_t budget = 220 * 1024;
@@ -145,7 +153,7 @@ inline HistLaunch choose_hist_launch(int mode, bool const_h, int quant_bins, int
   hl.npl = 0;
   hl.groups = 1 << 30;
   for (int npl : {1, 2, 4}) {
-    if (hl.layout == HL_QUANT16 && npl == 1) continue;
+    if ((hl.layout == HL_QUANT16 || hl.layout == HL_QUANT16R) && npl == 1) continue;
     int groups = (Fp + 32 * npl - 1) / (32 * npl);
     if ((smem_of(npl) <= budget || hl.npl == 0) && groups < hl.groups) {
       hl.npl = npl;
