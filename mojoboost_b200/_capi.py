@@ -252,6 +252,13 @@ class Model:
         e.check(lib().mojotrees_feature_importance(self.h, t, _ptr(out), out.size, e.h))
         return out
 
+    @property
+    def objective_name(self):
+        """'regression', 'binary' or 'multiclass'."""
+        import json
+        code = json.loads(self.dump_json())["objective"]
+        return {0: "regression", 1: "binary", 2: "multiclass"}[int(code)]
+
     def dump_json(self):
         e = _Err()
         p = ctypes.c_void_p()

@@ -91,5 +91,171 @@ def resolve_device(device, n_rows=0, n_features=0, n_outputs=1):
     raise NotImplementedError("device='cpu': the B200 library is the GPU path only")
 
 
+def gpu_available():
+    return bool(_capi.gpu_available())
+
+
+# ---- prediction (bindings/_mojotrees.mojo:4223-4296) ----------------------
+
+_DEVICES = {"cpu": _capi.DEVICE_CPU, "gpu": _capi.DEVICE_GPU, "cuda": _capi.DEVICE_GPU, "auto": _capi.DEVICE_AUTO}
+
+
+def _predict_into(model, x_addr, n_rows, n_features, params, out_addr):
+    """Predictions of a column-major float64 batch over the half-open
+    iteration range [start, stop) (clamped to the ensemble), written to the
+    float64 buffer at out_addr ([r * n_classes + k]).  Returns the backend
+    that ran, or None for an empty batch."""
+    n_rows, n_features = int(n_rows), int(n_features)
+    if n_rows == 0:
+        return None
+    device = str(params.get("device", "cpu")).lower()
+    if device not in _DEVICES:
+        raise ValueError(f"unknown device {device!r}")
+    k = model.num_classes
+    iters = model.num_iterations
+    start = min(max(int(params.get("start", 0)), 0), iters)
+    stop = params.get("stop", iters)
+    stop = iters if stop is None or int(stop) < 0 else min(int(stop), iters)
+    raw = int(params.get("raw_score", 0)) != 0
+    out = _f64(int(out_addr), n_rows * k)
+    if stop <= start:
+        # an empty range: the base scores (from iteration 0) or nothing
+        base = model.base_scores() if start == 0 else np.zeros(k)
+        vals = np.tile(base, (n_rows, 1))
+        if not raw:
+            vals = _response(model, vals)
+        out[:] = vals.reshape(-1)
+        return "cpu" if _DEVICES[device] != _capi.DEVICE_GPU else "gpu"
+    X = _f64(int(x_addr), n_rows * n_features)
+    e = _capi._Err()
+    e.check(_capi.lib().mojotrees_predict_ex(model.h, X.ctypes.data_as(ctypes.c_void_p), n_rows, n_features, start,
+                                             stop - start, _capi.PREDICT_RAW if raw else _capi.PREDICT_RESPONSE,
+                                             _DEVICES[device], out.ctypes.data_as(ctypes.c_void_p), out.size, e.h))
+    return "gpu" if _DEVICES[device] == _capi.DEVICE_GPU else "cpu"
+
+
+def _response(model, raw):
+    if model.num_classes > 1:
+        z = np.exp(raw - raw.max(axis=1, keepdims=True))
+        return z / z.sum(axis=1, keepdims=True)
+    if model.objective_name == "binary":
+        return 1.0 / (1.0 + np.exp(-raw))
+    return raw
+
+
+def predict_batch(model, x_addr, n_rows, n_features, params, out_addr):
+    """Single-output predictions (response, or raw with params["raw_score"])."""
+    return _predict_into(model, x_addr, n_rows, n_features, params, out_addr)
+
+
+def predict_proba_batch(model, x_addr, n_rows, n_features, params, out_addr):
+    """Multiclass probabilities (or per-class raw scores), row-major."""
+    return _predict_into(model, x_addr, n_rows, n_features, params, out_addr)
+
+
+# ---- model accessors -------------------------------------------------------
+
+def n_features(model):
+    return model.num_features
+
+
+def n_classes(model):
+    return model.num_classes
+
+
+def num_iterations(model):
+    return model.num_iterations
+
+
+n_features_multiclass = n_features
+num_iterations_multiclass = num_iterations
+
+
+def feature_importance(model, importance_type="split"):
+    return model.feature_importance(importance_type)
+
+
+feature_importance_multiclass = feature_importance
+
+
+# ---- model files (src/mojotrees/serialize.mojo) ----------------------------
+
+_ESC = {" ": "\\s", "\t": "\\t", "\n": "\\n", "\r": "\\r", "\\": "\\\\"}
+_UNESC = {"s": " ", "t": "\t", "n": "\n", "r": "\r", "\\": "\\"}
+
+
+def _escape_name(name):
+    """serialize.mojo:276-318: one whitespace-free token per name."""
+    if name == "":
+        return "\\e"
+    out = []
+    for ch in name:
+        if ch in _ESC:
+            out.append(_ESC[ch])
+        elif ord(ch) < 32 or ord(ch) == 127:
+            raise ValueError(f"feature name contains control byte {ord(ch)}, which the model file format cannot carry")
+        else:
+            out.append(ch)
+    return "".join(out)
+
+
+def _unescape_name(token):
+    """serialize.mojo:321-355, the inverse of _escape_name."""
+    if token == "\\e":
+        return ""
+    out, i = [], 0
+    while i < len(token):
+        if token[i] != "\\":
+            out.append(token[i])
+            i += 1
+            continue
+        if i + 1 >= len(token) or token[i + 1] not in _UNESC:
+            raise ValueError("corrupt feature name escape")
+        out.append(_UNESC[token[i + 1]])
+        i += 2
+    return "".join(out)
+
+
+def save(model, path, names=(), n_names=None):
+    """Format v4 through mojotrees_save_model, with the optional
+    feature_names section (serialize.mojo:389-398) when names are given."""
+    names = [str(n) for n in (names or [])]
+    if names and len(names) != model.num_features:
+        raise ValueError(f"{len(names)} feature names for {model.num_features} features")
+    model.save(str(path))
+    if names:
+        with open(path) as f:
+            head, rest = f.read().split("\n", 1)
+        section = f"feature_names {len(names)}\n" + "".join(_escape_name(n) + " " for n in names) + "\n"
+        with open(path, "w") as f:
+            f.write(head + "\n" + section + rest)
+
+
+save_multiclass = save
+
+
+def load(path):
+    return _capi.Model.load(str(path))
+
+
+load_multiclass = load
+
+
+def model_feature_names(path):
+    """The names a model file carries (serialize.mojo:1448), or []."""
+    with open(path) as f:
+        tok = f.read().split()
+    if len(tok) < 4 or tok[2] != "feature_names":
+        return []
+    n = int(tok[3])
+    return [_unescape_name(t) for t in tok[4:4 + n]]
+
+
+class HookNotProvided(AttributeError, NotImplementedError):
+    """An extension hook this library does not provide.  An AttributeError,
+    so the estimators' optional-hook probes (getattr(_mojotrees, name, None))
+    fall back, and a NotImplementedError for direct calls."""
+
+
 def __getattr__(name):
-    raise NotImplementedError(f"_mojotrees.{name} is not provided by the B200 training library")
+    raise HookNotProvided(f"_mojotrees.{name} is not provided by the B200 training library")

@@ -1,0 +1,65 @@
+"""The `_mojotrees` shim's prediction, model-file and accessor hooks, called as
+the reference estimators call them (raw addresses, column-major float64,
+half-open iteration ranges; bindings/_mojotrees.mojo:4223-4296)."""
+import numpy as np
+import pytest
+
+from test_model_io import RAW_A, X_A, model_a, write
+
+
+@pytest.fixture()
+def shim(mtlib):
+    from mojoboost_b200 import _mojotrees
+    return _mojotrees
+
+
+def _predict(shim, m, X, **params):
+    Xc = np.asfortranarray(X, dtype=np.float64)
+    out = np.full(X.shape[0] * m.num_classes, np.nan)
+    ran = shim.predict_batch(m, Xc.ctypes.data, X.shape[0], X.shape[1],
+                             {"device": "cpu", "start": 0, "stop": m.num_iterations, "raw_score": 0, **params},
+                             out.ctypes.data)
+    return ran, out
+
+
+def test_predict_batch_on_the_host(shim, tmp_path):
+    m = shim.load(write(tmp_path, "a.mbst", model_a(4)))
+    ran, out = _predict(shim, m, X_A)
+    assert ran == "cpu"
+    np.testing.assert_array_equal(out, RAW_A)  # regression: response == raw
+    # an empty iteration range leaves the base score
+    _, out = _predict(shim, m, X_A, stop=0)
+    np.testing.assert_array_equal(out, np.full(len(X_A), 0.25))
+    # an empty batch selects no backend and writes nothing
+    assert shim.predict_batch(m, 0, 0, 2, {"device": "cpu", "start": 0, "stop": 1, "raw_score": 1}, 0) is None
+
+
+def test_accessors_and_names(shim, tmp_path):
+    m = shim.load(write(tmp_path, "a.mbst", model_a(4)))
+    assert (shim.n_features(m), shim.n_classes(m), shim.num_iterations(m)) == (2, 1, 1)
+    p = str(tmp_path / "named.mbst")
+    names = ["x 0", "tab\there\\"]
+    shim.save(m, p, names, len(names))
+    assert shim.model_feature_names(p) == names
+    assert open(p).read().split("\n")[1] == "feature_names 2"
+    m2 = shim.load(p)
+    np.testing.assert_array_equal(_predict(shim, m2, X_A)[1], RAW_A)
+    assert shim.model_feature_names(write(tmp_path, "plain.mbst", model_a(4))) == []
+    with pytest.raises(ValueError):
+        shim.save(m, p, ["bad\x01name", "b"], 2)
+
+
+def test_missing_hooks_probe_as_absent(shim):
+    """The estimators probe optional hooks with getattr(..., None); a hook
+    this library lacks reads as absent there and raises on a direct call."""
+    assert getattr(shim, "predict_contrib", None) is None
+    with pytest.raises(NotImplementedError):
+        shim.predict_contrib
+
+
+@pytest.mark.gpu
+def test_predict_batch_on_the_device(shim, tmp_path):
+    m = shim.load(write(tmp_path, "a.mbst", model_a(4)))
+    ran, out = _predict(shim, m, X_A, device="gpu", raw_score=1)
+    assert ran == "gpu"
+    np.testing.assert_array_equal(out, RAW_A)
