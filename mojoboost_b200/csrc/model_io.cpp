@@ -157,6 +157,13 @@ struct Tokens {
     return t[pos++];
   }
   std::string peek() const { return pos < t.size() ? t[pos] : std::string(); }
+  size_t left() const { return t.size() - pos; }
+  // a count the rest of the file must hold at least per_item tokens for;
+  // checked before anything is sized by it
+  void need(long long count, long long per_item) const {
+    if (count < 0 || (per_item > 0 && (unsigned long long)count > left() / (unsigned long long)per_item))
+      throw std::runtime_error("corrupt model file: a count exceeds what the file holds");
+  }
   void expect(const char* tag) {
     if (next() != tag) throw std::runtime_error(std::string("corrupt model file: expected '") + tag + "'");
   }
@@ -244,6 +251,7 @@ Model load_model_text(const std::string& content) {
     r.next();
     const long long n = r.next_int();
     if (n < 1) throw std::runtime_error("corrupt feature_names section");
+    r.need(n, 1);
     for (long long i = 0; i < n; ++i) r.next();
   }
   Model m;
@@ -266,6 +274,7 @@ Model load_model_text(const std::string& content) {
     r.expect("learning_rate");
     m.learning_rate = r.next_f64();
     r.expect("base_scores");
+    r.need(k, 1);
     for (long long i = 0; i < k; ++i) m.base_scores.push_back(r.next_f64());
   } else {
     throw std::runtime_error("corrupt model file: unknown model kind");
@@ -275,6 +284,7 @@ Model load_model_text(const std::string& content) {
   r.expect("mapper");
   const long long nf = r.next_int(), nb = r.next_int(), ne = r.next_int();
   if (nf < 1 || nf > (1ll << 24) || ne < 0 || ne > (1ll << 32)) throw std::runtime_error("corrupt mapper header");
+  r.need(ne + nf + 1, 1);
   if (nb < 1 || nb > 256) throw std::runtime_error("corrupt mapper: n_bins must be in [1, 256]");
   mp.n_features = (int)nf;
   mp.n_bins = (int)nb;
@@ -300,6 +310,7 @@ Model load_model_text(const std::string& content) {
     r.next();
     const long long n_flags = r.next_int(), n_codes = r.next_int();
     if (n_flags != nf || n_codes < 0 || n_codes > (1ll << 32)) throw std::runtime_error("corrupt categorical header");
+    r.need(nf + n_codes + nf + 1, 1);
     for (auto& c : mp.is_cat) c = r.next_int() != 0 ? 1 : 0;
     mp.cat_codes.resize((size_t)n_codes);
     for (auto& c : mp.cat_codes) c = r.next_int();
@@ -327,12 +338,14 @@ Model load_model_text(const std::string& content) {
   const long long n_trees = r.next_int();
   if (n_trees < 0 || n_trees > (1ll << 24)) throw std::runtime_error("corrupt model file: tree count");
   if (n_trees % m.num_class != 0) throw std::runtime_error("corrupt model file: tree count not divisible by classes");
+  r.need(n_trees, 3);  // "tree", node count, leaf count at least
   bool mapper_fits = true;  // every split is one this mapper's bins can express
   m.trees.resize((size_t)n_trees);
   for (auto& t : m.trees) {
     r.expect("tree");
     const long long nn = r.next_int(), n_leaves = r.next_int();
     if (nn < 1 || nn > (1ll << 24) || n_leaves < 1 || n_leaves > nn) throw std::runtime_error("corrupt tree header");
+    r.need(nn, version >= 2 ? 7 : 5);  // the per-node rows that always follow
     t.assign((size_t)nn, HostNode{});
     for (auto& nd : t) nd.feature = (int)r.next_int();
     for (auto& nd : t) nd.thr = (int)r.next_int();
@@ -357,7 +370,7 @@ Model load_model_text(const std::string& content) {
     if (has_counts)
       for (auto& nd : t) {
         const double c = r.next_f64();
-        if (!(c >= 0.0)) throw std::runtime_error("corrupt tree: node cover must be positive");
+        if (!(c >= 0.0) || !(c < 9.0e18)) throw std::runtime_error("corrupt tree: node cover out of range");
         nd.count = (long long)c;
       }
     if (version >= 4) {
@@ -372,6 +385,7 @@ Model load_model_text(const std::string& content) {
       r.next();
       const long long nw = r.next_int();
       if (nw < 0 || nw % kCatWords != 0 || nw > (1ll << 30)) throw std::runtime_error("corrupt tree: category bitset size");
+      r.need(nn + nw, 1);
       std::vector<long long> off((size_t)nn);
       for (auto& o : off) {
         o = r.next_int();

@@ -180,3 +180,41 @@ def test_gpu_prebinned_model_round_trip(mtlib, tmp_path):
     np.testing.assert_array_equal(m2.predict_binned(bins), m.predict_binned(bins))
     with pytest.raises(mtlib.MojoTreesError):
         m2.predict(X, raw_score=True)
+
+
+def test_corrupted_files_never_crash(mtlib, tmp_path):
+    """Seeded token-level corruption of valid files (replaced, dropped and
+    repeated tokens, truncation): every load either fails with a status or
+    yields a model whose host prediction runs."""
+    rng = np.random.default_rng(7)
+    base = model_a(4).split()
+    repl = ["-1", "0", "1", "2", "3", "7", "255", "256", "-2", "4294967299", "9223372036854775807",
+            "18446744073709551615", "99999999999999999999", "x", "tree", "cat", "counts", "gains", "mapper"]
+    p = str(tmp_path / "fuzz.mbst")
+    loaded = 0
+    for _ in range(600):
+        tok = list(base)
+        for _ in range(rng.integers(1, 4)):
+            i = int(rng.integers(0, len(tok)))
+            op = rng.integers(0, 4)
+            if op == 0:
+                tok[i] = repl[int(rng.integers(0, len(repl)))]
+            elif op == 1:
+                del tok[i]
+            elif op == 2:
+                tok.insert(i, tok[i])
+            else:
+                tok = tok[:i]
+            if not tok:
+                tok = ["mojotrees"]
+        open(p, "w").write(" ".join(tok))
+        try:
+            m = mtlib.Model.load(p)
+        except mtlib.MojoTreesError:
+            continue
+        loaded += 1
+        try:
+            m.predict(X_A, raw_score=True)
+        except mtlib.MojoTreesError:
+            pass
+    assert loaded > 0
