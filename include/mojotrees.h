@@ -200,6 +200,23 @@ int32_t mojotrees_b200_round_times(const MojoTreesModel *model, double *out_valu
  * out_values may be NULL to query the count. */
 int32_t mojotrees_b200_round_stats(const MojoTreesModel *model, double *out_values, int64_t out_len,
                                    int64_t *out_n, MojoTreesError *error);
+/* Which features the model splits by category set, from its bin mapper: one
+ * flag (1 categorical, 0 numerical) per feature into out_flags[0, n_features).
+ * The reference's `categorical_features` (bindings/_mojotrees.mojo:4802). */
+int32_t mojotrees_b200_model_categorical(const MojoTreesModel *model, int32_t *out_flags, int64_t out_len,
+                                         MojoTreesError *error);
+
+/* Row-major float64 (src[r * n_features + f]) into a caller-allocated
+ * column-major buffer (dst[f * n_rows + r]) on all host threads, with
+ * *out_has_infinite (may be NULL) = 1 when any value is +inf or -inf (NaN is
+ * not reported).  The reference's `ingest_column_major`
+ * (bindings/_mojotrees.mojo:682). */
+int32_t mojotrees_b200_ingest_column_major(const double *src, double *dst, int64_t n_rows, int64_t n_features,
+                                           int32_t *out_has_infinite, MojoTreesError *error);
+/* *out_has_infinite = 1 when data[0, n) holds +inf or -inf.  The reference's
+ * `buffer_has_infinite` (bindings/_mojotrees.mojo:722). */
+int32_t mojotrees_b200_buffer_has_infinite(const double *data, int64_t n, int32_t *out_has_infinite,
+                                           MojoTreesError *error);
 
 /* Data-parallel training (one process per GPU, rows sharded): a fresh
  * 128-byte NCCL unique id, created on one rank and broadcast by the caller. */

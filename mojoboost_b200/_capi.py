@@ -60,6 +60,9 @@ SIGNATURES = {
     "mojotrees_b200_train_stats": (_I32, [_P, _P, _I64, _P, _P]),
     "mojotrees_b200_round_times": (_I32, [_P, _P, _I64, _P, _P]),
     "mojotrees_b200_round_stats": (_I32, [_P, _P, _I64, _P, _P]),
+    "mojotrees_b200_model_categorical": (_I32, [_P, _P, _I64, _P]),
+    "mojotrees_b200_ingest_column_major": (_I32, [_P, _P, _I64, _I64, _P, _P]),
+    "mojotrees_b200_buffer_has_infinite": (_I32, [_P, _I64, _P, _P]),
     "mojotrees_b200_nccl_unique_id": (_I32, [_P, _P]),
     "mojotrees_b200_histogram_u8": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _I32, _P, _P]),
     "mojotrees_b200_histogram_u8_noalloc": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _I32, _P, _P, _P]),
@@ -251,6 +254,13 @@ class Model:
         t = IMPORTANCE_GAIN if importance_type == "gain" else IMPORTANCE_SPLIT
         e.check(lib().mojotrees_feature_importance(self.h, t, _ptr(out), out.size, e.h))
         return out
+
+    def categorical_features(self):
+        """Indices of the features the model splits by category set."""
+        out = np.zeros(self.num_features, np.int32)
+        e = _Err()
+        e.check(lib().mojotrees_b200_model_categorical(self.h, _ptr(out), out.size, e.h))
+        return [int(i) for i in np.flatnonzero(out)]
 
     @property
     def objective_name(self):

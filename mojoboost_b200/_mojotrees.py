@@ -12,6 +12,9 @@ import ctypes
 import numpy as np
 
 from . import _capi
+from ._registry import (metric_code_of_name, objective_code_of_name, objective_name_status_of,  # noqa: F401
+                        registry_metric_aliases, registry_metrics, registry_objective_aliases,
+                        registry_objective_unimplemented, registry_objectives, registry_vocabulary)
 
 # objective codes of the reference package (python/mojotrees/sklearn.py:33-55)
 SQUARED_ERROR = 0
@@ -176,6 +179,36 @@ def feature_importance(model, importance_type="split"):
 
 
 feature_importance_multiclass = feature_importance
+
+
+def categorical_features(model):
+    """Indices of the features the model splits by category set
+    (bindings/_mojotrees.mojo:4802)."""
+    return model.categorical_features()
+
+
+categorical_features_multiclass = categorical_features
+
+
+# ---- host ingestion (bindings/_mojotrees.mojo:682-739) ---------------------
+
+def ingest_column_major(src_addr, dst_addr, n_rows, n_features):
+    """Row-major float64 at src_addr into the column-major buffer at
+    dst_addr, on all host threads; 1 when any value is +inf or -inf."""
+    found = ctypes.c_int32(0)
+    e = _capi._Err()
+    e.check(_capi.lib().mojotrees_b200_ingest_column_major(ctypes.c_void_p(int(src_addr)), ctypes.c_void_p(int(dst_addr)),
+                                                           int(n_rows), int(n_features), ctypes.byref(found), e.h))
+    return int(found.value)
+
+
+def buffer_has_infinite(addr, n):
+    """1 when the float64 buffer at addr holds +inf or -inf."""
+    found = ctypes.c_int32(0)
+    e = _capi._Err()
+    e.check(_capi.lib().mojotrees_b200_buffer_has_infinite(ctypes.c_void_p(int(addr)), int(n), ctypes.byref(found),
+                                                           e.h))
+    return int(found.value)
 
 
 # ---- model files (src/mojotrees/serialize.mojo) ----------------------------

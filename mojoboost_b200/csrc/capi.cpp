@@ -556,6 +556,71 @@ int32_t mojotrees_b200_round_stats(const MojoTreesModel* model, double* out_valu
       MOJOTREES_ERROR_INVALID_ARGUMENT);
 }
 
+int32_t mojotrees_b200_model_categorical(const MojoTreesModel* model, int32_t* out_flags, int64_t out_len,
+                                         MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!model || !out_flags) throw InvalidArgument("null pointer argument");
+        const mtb::Model& m = model->m;
+        if (out_len < m.n_features) throw InvalidArgument("output buffer too small");
+        for (int f = 0; f < m.n_features; ++f)
+          out_flags[f] = (f < (int)m.mapper.is_cat.size() && m.mapper.is_cat[f]) ? 1 : 0;
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+// Host ingestion of a caller's float64 matrix (the reference's
+// ingest_column_major / buffer_has_infinite, bindings/_mojotrees.mojo:682-739):
+// a tiled row-major -> column-major transpose on all host threads that also
+// reports whether any value is +inf or -inf (NaN marks missing values and is
+// not reported).
+int32_t mojotrees_b200_ingest_column_major(const double* src, double* dst, int64_t n_rows, int64_t n_features,
+                                           int32_t* out_has_infinite, MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (n_rows < 0 || n_features < 0) throw InvalidArgument("n_rows and n_features must be non-negative");
+        if ((!src || !dst) && n_rows > 0 && n_features > 0) throw InvalidArgument("null pointer argument");
+        constexpr int64_t kTile = 64;  // 32 KB read and 32 KB written per tile
+        const int64_t rt = (n_rows + kTile - 1) / kTile, ft = (n_features + kTile - 1) / kTile;
+        int found = 0;
+#pragma omp parallel for schedule(static) reduction(| : found)
+        for (int64_t t = 0; t < rt * ft; ++t) {
+          const int64_t r0 = (t / ft) * kTile, f0 = (t % ft) * kTile;
+          const int64_t r1 = std::min(n_rows, r0 + kTile), f1 = std::min(n_features, f0 + kTile);
+          for (int64_t f = f0; f < f1; ++f) {
+            double* col = dst + f * n_rows;
+            for (int64_t r = r0; r < r1; ++r) {
+              const double v = src[r * n_features + f];
+              found |= std::isinf(v) ? 1 : 0;
+              col[r] = v;
+            }
+          }
+        }
+        if (out_has_infinite) *out_has_infinite = found;
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+int32_t mojotrees_b200_buffer_has_infinite(const double* data, int64_t n, int32_t* out_has_infinite,
+                                           MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!out_has_infinite || (!data && n > 0)) throw InvalidArgument("null pointer argument");
+        if (n < 0) throw InvalidArgument("n must be non-negative");
+        int found = 0;
+#pragma omp parallel for schedule(static) reduction(| : found)
+        for (int64_t i = 0; i < n; ++i) found |= std::isinf(data[i]) ? 1 : 0;
+        *out_has_infinite = found;
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
 int32_t mojotrees_b200_bin_dense(const double* data, int64_t n_rows, int64_t n_features, const char* parameters,
                                  uint8_t* out_bins, int32_t* out_missing_bin, int32_t* out_n_categories,
                                  int32_t* out_n_bins, MojoTreesError* error) {
