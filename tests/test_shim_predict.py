@@ -63,3 +63,18 @@ def test_predict_batch_on_the_device(shim, tmp_path):
     ran, out = _predict(shim, m, X_A, device="gpu", raw_score=1)
     assert ran == "gpu"
     np.testing.assert_array_equal(out, RAW_A)
+
+
+def test_ingest_column_major(shim):
+    rng = np.random.default_rng(3)
+    for n, f in ((1, 1), (65, 3), (130, 70), (1000, 1)):
+        X = np.ascontiguousarray(rng.normal(size=(n, f)))
+        X[rng.random((n, f)) < 0.05] = np.nan
+        out = np.empty((n, f), order="F")
+        assert shim.ingest_column_major(X.ctypes.data, out.ctypes.data, n, f) == 0
+        np.testing.assert_array_equal(out, X)
+        assert shim.buffer_has_infinite(out.ctypes.data, n * f) == 0
+        X[n // 2, f - 1] = -np.inf
+        assert shim.ingest_column_major(X.ctypes.data, out.ctypes.data, n, f) == 1
+        assert shim.buffer_has_infinite(out.ctypes.data, n * f) == 1
+    assert shim.ingest_column_major(0, 0, 0, 5) == 0
