@@ -22,7 +22,8 @@ BINARY_LOGISTIC = 1
 MULTICLASS = -1
 _OBJECTIVE_NAMES = {SQUARED_ERROR: "regression", BINARY_LOGISTIC: "binary", MULTICLASS: "multiclass"}
 
-# reference params-dict keys -> parameter-string keys of the C ABI
+# reference params-dict keys (python/mojotrees/sklearn.py `_Base._params`)
+# -> parameter-string keys of the C ABI
 _KEY_MAP = {
     "n_estimators": "num_iterations", "learning_rate": "learning_rate", "num_leaves": "num_leaves",
     "min_data_in_leaf": "min_data_in_leaf", "lambda_l2": "lambda_l2", "lambda_l1": "lambda_l1",
@@ -35,9 +36,35 @@ _KEY_MAP = {
     "num_grad_quant_bins": "num_grad_quant_bins", "stochastic_rounding": "stochastic_rounding",
     "num_class": "num_class",
 }
-# keys whose value must stay at the default for the device path
-_MUST_BE = {"bagging_fraction": 1.0, "bagging_freq": 0, "max_depth": -1, "goss": 0, "linear_tree": 0,
-            "ordered": 0, "feature_fraction_bynode": 1.0}
+# Options that change training and that the device path does not implement:
+# they must stay at the value meaning "off", and anything else is refused by
+# name rather than silently trained without.
+_MUST_BE = {
+    "bagging_fraction": 1.0, "bagging_freq": 0, "bootstrap_type": "no", "goss": 0, "boosting": "gbdt",
+    "max_depth": -1, "linear_tree": 0, "ordered": 0, "feature_fraction_bynode": 1.0, "enable_bundle": 0,
+    "ctr": "off", "catboost_mode_defaults": 0, "grow_policy": "lossguide", "score_function": "l2",
+    "random_strength": 0.0, "leaf_estimation_iterations": 1, "auto_learning_rate": 0, "boost_from_average": 1,
+    "min_gain_to_split": 0.0, "max_delta_step": 0.0, "path_smooth": 0.0, "extra_trees": 0,
+    "monotone_penalty": 0.0, "cegb_tradeoff": 1.0, "cegb_penalty_split": 0.0, "forced_splits": "",
+    "monotone_addr": 0, "interaction_flat_addr": 0, "interaction_flat_len": 0, "interaction_offsets_addr": 0,
+    "interaction_offsets_len": 0, "feature_contri_addr": 0, "cegb_penalty_feature_coupled_addr": 0,
+    "cegb_penalty_feature_lazy_addr": 0, "sample_weight_addr": 0, "derivative_precision": "float32",
+}
+# Keys that only matter when one of the options above is on (their seeds and
+# knobs), or for objectives this library does not train: read and ignored.
+_INERT = {
+    "alpha", "bagging_seed", "bagging_temperature", "boost_from_average_set", "bootstrap_explicit",
+    "bootstrap_seed", "bootstrap_subsample", "bundle_missing", "ctr_set", "ctr_target_border_count",
+    "ctr_target_border_type", "drop_rate", "drop_seed", "extra_seed", "fold_len_multiplier",
+    "fold_permutation_block", "goss_seed", "goss_warmup_rounds", "linear_lambda", "max_bundle_bins",
+    "max_bundle_size", "max_conflict_rate", "max_drop", "max_nondefault_rate", "min_reduction",
+    "monotone_constraints_method", "mvs_reg", "one_hot_max_size", "ordered_seed", "other_rate",
+    "permutation_count", "random_strength_seed", "random_strength_set", "skip_drop", "top_rate", "uniform_drop",
+    "xgboost_dart_mode", "leaf_estimation_iterations_set", "auto_learning_rate_l2_set",
+    "auto_learning_rate_leaf_iters_set", "auto_learning_rate_required", "device", "categorical_addr",
+    "categorical_len", "categorical_features", "categorical_feature", "objective", "fair_c",
+    "tweedie_variance_power",
+}
 
 
 def _f64(addr, n):
@@ -45,7 +72,20 @@ def _f64(addr, n):
     return np.frombuffer(buf, dtype=np.float64, count=n)
 
 
+def _same(value, default):
+    if isinstance(default, str):
+        return str(value).lower() == default
+    try:
+        return float(value) == float(default)
+    except (TypeError, ValueError):
+        return False
+
+
 def param_string(objective, params):
+    """The C ABI parameter string for the reference estimators' params dict.
+    Every key is mapped, checked to be off, or known to be inert; an option
+    the device path does not cover, or a key this mapping does not know, is
+    refused by name."""
     if objective not in _OBJECTIVE_NAMES:
         raise NotImplementedError(f"objective code {objective} is not covered by the B200 device path")
     device = str(params.get("device", "gpu")).lower()
@@ -53,11 +93,18 @@ def param_string(objective, params):
         raise NotImplementedError("device='cpu': the B200 library is the GPU path only")
     out = {"objective": _OBJECTIVE_NAMES[objective], "device": "gpu"}
     for k, v in params.items():
-        if k in _KEY_MAP and v is not None:
+        if v is None:
+            continue
+        if k in _KEY_MAP:
             out[_KEY_MAP[k]] = v
-        elif k in _MUST_BE and v is not None and float(v) != float(_MUST_BE[k]):
-            raise NotImplementedError(f"{k}={v} is not covered by the B200 device path")
+        elif k in _MUST_BE:
+            if not _same(v, _MUST_BE[k]):
+                raise NotImplementedError(f"{k}={v!r} is not covered by the B200 device path")
+        elif k not in _INERT:
+            raise NotImplementedError(f"parameter {k!r} is not covered by the B200 device path")
     cats = params.get("categorical_features") or params.get("categorical_feature")
+    if params.get("categorical_addr") and params.get("categorical_len"):
+        cats = [int(c) for c in _f64(int(params["categorical_addr"]), int(params["categorical_len"]))]
     if cats:
         out["categorical_feature"] = ",".join(str(int(c)) for c in cats)
     return _capi.params_string(out)
@@ -188,6 +235,39 @@ def categorical_features(model):
 
 
 categorical_features_multiclass = categorical_features
+
+
+def extra_params_check(params, shape):
+    """The extra tree options (min_gain_to_split, max_delta_step, path_smooth,
+    extra_trees, monotone penalty, CEGB, forced splits): the device path
+    implements none of them, so any value other than "off" is refused; with
+    all of them off nothing is active (bindings/basic_bindings.mojo:268)."""
+    for k in ("min_gain_to_split", "max_delta_step", "path_smooth", "extra_trees", "monotone_penalty",
+              "cegb_tradeoff", "cegb_penalty_split", "forced_splits", "feature_contri_addr",
+              "cegb_penalty_feature_coupled_addr", "cegb_penalty_feature_lazy_addr"):
+        if k in params and params[k] is not None and not _same(params[k], _MUST_BE[k]):
+            raise NotImplementedError(f"{k}={params[k]!r} is not covered by the B200 device path")
+    return {"is_active": False, "needs_leaf_finish": False, "needs_node_identity": False,
+            "needs_grower_support": False}
+
+
+def efb_check(params, cpu=0):
+    """Exclusive feature bundling is not part of the device path."""
+    if params.get("enable_bundle") and not _same(params["enable_bundle"], 0):
+        raise NotImplementedError("enable_bundle: exclusive feature bundling is not covered by the B200 device path")
+    return None
+
+
+def extra_option_supported(name):
+    """Every other LightGBM option name: not this function's to refuse."""
+    return None
+
+
+def efb_defaults():
+    """Exclusive-feature-bundling knob defaults (EfbParams.default,
+    efb.mojo:373).  Bundling itself is not part of the device path."""
+    return {"max_conflict_rate": 0.0, "max_bundle_bins": 256, "max_bundle_size": 0,
+            "max_nondefault_rate": 0.95, "min_reduction": 0.0, "bundle_missing": False}
 
 
 # ---- host ingestion (bindings/_mojotrees.mojo:682-739) ---------------------

@@ -74,3 +74,86 @@ def test_gpu_fit_without_a_device_is_refused(ref, mtlib):
     with pytest.raises(Exception) as ei:
         est.fit(np.random.default_rng(0).random((200, 3)), np.random.default_rng(1).random(200))
     assert "CUDA" in str(ei.value) or "device" in str(ei.value)
+
+
+@pytest.fixture()
+def captured_fit(ref, monkeypatch):
+    """The estimators' call into `_mojotrees.fit` / `fit_multiclass`, stopped
+    there (no device needed): (objective code, params dict)."""
+    from mojoboost_b200 import _mojotrees as shim
+    param_string = shim.param_string
+    cap = {}
+
+    def fake(*a):
+        cap["objective"] = shim.MULTICLASS if len(a) == 6 and "num_class" in a[5] else a[4]
+        cap["params"] = dict(a[5])
+        # built here, as the real hook does: the categorical index buffer the
+        # dict points at lives only while the estimator's fit runs
+        try:
+            cap["string"] = param_string(cap["objective"], cap["params"]).decode()
+        except NotImplementedError as e:
+            cap["refused"] = e
+        raise RuntimeError("captured")
+
+    def fake_mc(x, n, f, y, k, params):
+        p = dict(params)
+        p["num_class"] = k
+        return fake(x, n, f, y, shim.MULTICLASS, p)
+
+    monkeypatch.setattr(shim, "fit", fake)
+    monkeypatch.setattr(shim, "fit_multiclass", fake_mc)
+    monkeypatch.setattr(shim, "resolve_device", lambda *a, **k: "gpu")
+    return cap
+
+
+def _fit(est, X, y):
+    with pytest.raises(Exception):
+        est.fit(X, y)
+
+
+@pytest.mark.parametrize("kind", ["regressor", "binary", "multiclass"])
+def test_estimator_params_reach_the_c_abi(ref, captured_fit, mtlib, kind):
+    """The params dict each estimator builds becomes a parameter string the C
+    ABI's own parser accepts (without a device the call then stops at the
+    device check, never at a parameter)."""
+    from mojoboost_b200 import _mojotrees as shim
+    rng = np.random.default_rng(0)
+    X = rng.random((300, 4))
+    X[:, 2] = rng.integers(0, 5, 300)
+    if kind == "regressor":
+        est, y = ref.MojoTreesRegressor(n_estimators=4, categorical_feature=[2]), rng.random(300)
+    else:
+        k = 2 if kind == "binary" else 3
+        est, y = ref.MojoTreesClassifier(n_estimators=4, categorical_feature=[2]), rng.integers(0, k, 300)
+    _fit(est, X, y.astype(float))
+    s = captured_fit["string"]
+    assert "categorical_feature=2" in s and "num_iterations=4" in s
+    if kind == "multiclass":
+        assert "num_class=3" in s and "objective=multiclass" in s
+    if mtlib.gpu_available():
+        return
+    with pytest.raises(mtlib.MojoTreesError) as ei:
+        mtlib.train_dense(X, y.astype(float), dict(kv.split("=", 1) for kv in s.split()))
+    assert ei.value.code == -4 and "CUDA" in str(ei.value)
+
+
+@pytest.mark.parametrize("kw", [dict(max_depth=5), dict(boosting="dart"), dict(min_gain_to_split=0.5),
+                                dict(bagging_fraction=0.5, bagging_freq=1), dict(extra_trees=True),
+                                dict(path_smooth=1.0)])
+def test_uncovered_estimator_options_are_refused(ref, captured_fit, kw):
+    """An option the device path does not implement is refused by name, never
+    trained without."""
+    from mojoboost_b200 import _mojotrees as shim
+    try:
+        est = ref.MojoTreesRegressor(n_estimators=3, **kw)
+    except TypeError:
+        pytest.skip(f"the reference estimator takes no {kw}")
+    rng = np.random.default_rng(1)
+    try:
+        est.fit(rng.random((200, 3)), rng.random(200))
+    except RuntimeError as e:
+        if str(e) != "captured":
+            return  # refused before the fit hook
+        assert "refused" in captured_fit, "an uncovered option reached the parameter string"
+    except (ValueError, NotImplementedError):
+        return  # refused by the estimator's preflight through the shim
