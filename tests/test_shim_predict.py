@@ -78,3 +78,26 @@ def test_ingest_column_major(shim):
         assert shim.ingest_column_major(X.ctypes.data, out.ctypes.data, n, f) == 1
         assert shim.buffer_has_infinite(out.ctypes.data, n * f) == 1
     assert shim.ingest_column_major(0, 0, 0, 5) == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("objective", [0, 1])
+def test_gpu_fit_through_the_shim(shim, mtlib, objective):
+    """`_mojotrees.fit` at raw addresses (column-major X, as the estimators
+    pass it) trains the model `mojotrees_train_dense` trains for the same
+    parameters, and `predict_batch` on either device returns its predictions."""
+    from parity_util import make_data
+    X, y = make_data(51, 5000, 6, kind="binary" if objective == 1 else "regression", nan_frac=0.05)
+    Xf = np.asfortranarray(X)
+    y = np.ascontiguousarray(y, dtype=np.float64)
+    params = {"n_estimators": 4, "num_leaves": 15, "min_data_in_leaf": 20}
+    m = shim.fit(Xf.ctypes.data, X.shape[0], X.shape[1], y.ctypes.data, objective, params)
+    ref = mtlib.train_dense(X, y, dict(kv.split("=", 1) for kv in
+                                       shim.param_string(objective, params).decode().split()))
+    for t in range(ref.num_trees):
+        for k, v in ref.tree(t).items():
+            np.testing.assert_array_equal(m.tree(t)[k], v)
+    for device in ("cpu", "gpu"):
+        ran, out = _predict(shim, m, X, device=device)
+        assert ran == device
+        np.testing.assert_array_equal(out, m.predict(X))
