@@ -217,6 +217,15 @@ int32_t mojotrees_b200_ingest_column_major(const double *src, double *dst, int64
  * `buffer_has_infinite` (bindings/_mojotrees.mojo:722). */
 int32_t mojotrees_b200_buffer_has_infinite(const double *data, int64_t n, int32_t *out_has_infinite,
                                            MojoTreesError *error);
+/* Leaf ordinals (a leaf's rank among its tree's leaves in node order) of
+ * column-major rows over iterations [start_iteration, start_iteration +
+ * num_iteration) (num_iteration <= 0: to the end), as float64:
+ * out[r * (n * K) + i * K + k] for class k's tree of iteration i.  On the
+ * host.  The reference's `predict_leaf` / `predict_leaf_multiclass`
+ * (bindings/_mojotrees.mojo:3960-4010, tree.mojo:558-580). */
+int32_t mojotrees_b200_predict_leaf(const MojoTreesModel *model, const double *data, int64_t n_rows,
+                                    int64_t n_features, int64_t start_iteration, int64_t num_iteration,
+                                    double *out_values, int64_t out_len, MojoTreesError *error);
 
 /* Data-parallel training (one process per GPU, rows sharded): a fresh
  * 128-byte NCCL unique id, created on one rank and broadcast by the caller. */

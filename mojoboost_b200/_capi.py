@@ -63,6 +63,7 @@ SIGNATURES = {
     "mojotrees_b200_model_categorical": (_I32, [_P, _P, _I64, _P]),
     "mojotrees_b200_ingest_column_major": (_I32, [_P, _P, _I64, _I64, _P, _P]),
     "mojotrees_b200_buffer_has_infinite": (_I32, [_P, _I64, _P, _P]),
+    "mojotrees_b200_predict_leaf": (_I32, [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P]),
     "mojotrees_b200_nccl_unique_id": (_I32, [_P, _P]),
     "mojotrees_b200_histogram_u8": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _I32, _P, _P]),
     "mojotrees_b200_histogram_u8_noalloc": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _I32, _P, _P, _P]),

@@ -193,6 +193,43 @@ def _response(model, raw):
     return raw
 
 
+def predict_leaf(model, x_addr, n_rows, n_features, start, stop, out_addr):
+    """Per-tree leaf ordinals over [start, stop), row-major and round-major
+    within a row (bindings/_mojotrees.mojo:3960-4010), on the host."""
+    n_rows, n_features = int(n_rows), int(n_features)
+    iters = model.num_iterations
+    start = min(max(int(start), 0), iters)
+    stop = iters if stop is None or int(stop) < 0 else min(int(stop), iters)
+    if n_rows == 0 or stop <= start:
+        return None
+    cols = (stop - start) * model.num_classes
+    X = _f64(int(x_addr), n_rows * n_features)
+    out = _f64(int(out_addr), n_rows * cols)
+    e = _capi._Err()
+    e.check(_capi.lib().mojotrees_b200_predict_leaf(model.h, X.ctypes.data_as(ctypes.c_void_p), n_rows, n_features,
+                                                    start, stop - start, out.ctypes.data_as(ctypes.c_void_p),
+                                                    out.size, e.h))
+    return None
+
+
+predict_leaf_multiclass = predict_leaf
+
+
+def predict_leaf_batch(model, x_addr, n_rows, n_features, params, out_addr):
+    """Leaf ordinals for a batch; the walk runs on the host, so an explicit
+    device request is refused rather than answered from the host."""
+    device = str(params.get("device", "cpu")).lower()
+    if device in ("gpu", "cuda"):
+        raise NotImplementedError("leaf prediction runs on the host in the B200 library")
+    if int(n_rows) == 0:
+        return None
+    predict_leaf(model, x_addr, n_rows, n_features, params.get("start", 0), params.get("stop", -1), out_addr)
+    return "cpu"
+
+
+predict_leaf_multiclass_batch = predict_leaf_batch
+
+
 def predict_batch(model, x_addr, n_rows, n_features, params, out_addr):
     """Single-output predictions (response, or raw with params["raw_score"])."""
     return _predict_into(model, x_addr, n_rows, n_features, params, out_addr)
@@ -221,8 +258,12 @@ n_features_multiclass = n_features
 num_iterations_multiclass = num_iterations
 
 
-def feature_importance(model, importance_type="split"):
-    return model.feature_importance(importance_type)
+def feature_importance(model, n_features, kind, out_addr):
+    """Split-count (kind 0) or total-gain (kind 1) importance into the float64
+    buffer at out_addr (bindings/_mojotrees.mojo:4881)."""
+    vals = model.feature_importance("gain" if int(kind) == 1 else "split")
+    _f64(int(out_addr), int(n_features))[:] = vals[: int(n_features)]
+    return None
 
 
 feature_importance_multiclass = feature_importance

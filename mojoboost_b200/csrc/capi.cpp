@@ -284,6 +284,21 @@ inline double tree_value(const std::vector<mtb::HostNode>& t, const uint8_t* row
   return t[node].value;
 }
 
+// The node a row of bins reaches (the walk of tree_value).
+inline int tree_leaf_node(const std::vector<mtb::HostNode>& t, const uint8_t* row_bins, int64_t stride) {
+  int node = 0;
+  while (t[node].feature >= 0) {
+    const mtb::HostNode& nd = t[node];
+    int b = row_bins[(int64_t)nd.feature * stride];
+    bool left;
+    if (nd.is_cat) left = b > 0 && b < 256 && ((nd.bits[b >> 6] >> (b & 63)) & 1ull);
+    else if (b == nd.mbin) left = nd.dleft != 0;
+    else left = b <= nd.thr;
+    node = left ? nd.left : nd.right;
+  }
+  return node;
+}
+
 // Raw scores of feature-major bins over iterations [it0, it1)
 // (boosting.mojo:1722-1727, 3747-3757; the sum is a fused multiply-add).
 void raw_scores(const mtb::Model& m, const uint8_t* bins, int64_t n, int64_t it0, int64_t it1, double* out) {
@@ -616,6 +631,50 @@ int32_t mojotrees_b200_buffer_has_infinite(const double* data, int64_t n, int32_
 #pragma omp parallel for schedule(static) reduction(| : found)
         for (int64_t i = 0; i < n; ++i) found |= std::isinf(data[i]) ? 1 : 0;
         *out_has_infinite = found;
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+// Leaf ordinals (a leaf's rank among its tree's leaves in node order,
+// tree.mojo:558-580) of column-major float64 rows over iterations
+// [it0, it0 + n): out[r * (n * K) + i * K + k] is class k's tree of the
+// range's iteration i (bindings/_mojotrees.mojo:3960-4010).  Host walk.
+int32_t mojotrees_b200_predict_leaf(const MojoTreesModel* model, const double* data, int64_t n_rows,
+                                    int64_t n_features, int64_t start_iteration, int64_t num_iteration,
+                                    double* out_values, int64_t out_len, MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!model || (!data && n_rows > 0) || (!out_values && n_rows > 0)) throw InvalidArgument("null pointer argument");
+        const mtb::Model& m = model->m;
+        if (n_rows < 0) throw InvalidArgument("n_rows must be non-negative");
+        if (n_features != m.n_features) throw InvalidArgument("n_features does not match the model");
+        if (!m.has_mapper)
+          throw mtb::Unsupported("model was trained on pre-binned data; raw values cannot be binned");
+        const int K = m.num_class;
+        const int64_t iters = (int64_t)m.trees.size() / K;
+        const int64_t it0 = std::max<int64_t>(0, std::min(start_iteration, iters));
+        const int64_t it1 = num_iteration <= 0 ? iters : std::min(iters, it0 + num_iteration);
+        const int64_t cols = (it1 - it0) * K;
+        if (out_len < n_rows * cols) throw InvalidArgument("output buffer too small");
+        if (n_rows == 0 || cols == 0) return MOJOTREES_OK;
+        std::vector<std::vector<int>> ord((size_t)cols);
+        for (int64_t j = 0; j < cols; ++j) {
+          const auto& t = m.trees[(size_t)(it0 * K + j)];
+          ord[(size_t)j].assign(t.size(), -1);
+          int next = 0;
+          for (size_t i = 0; i < t.size(); ++i)
+            if (t[i].feature < 0) ord[(size_t)j][i] = next++;
+        }
+        std::vector<uint8_t> bins((size_t)n_rows * n_features);
+        mtb::transform(m.mapper, data, n_rows, bins.data());
+#pragma omp parallel for schedule(static)
+        for (int64_t r = 0; r < n_rows; ++r)
+          for (int64_t j = 0; j < cols; ++j) {
+            const auto& t = m.trees[(size_t)(it0 * K + j)];
+            out_values[r * cols + j] = (double)ord[(size_t)j][(size_t)tree_leaf_node(t, bins.data() + r, n_rows)];
+          }
         return MOJOTREES_OK;
       },
       MOJOTREES_ERROR_INVALID_ARGUMENT);

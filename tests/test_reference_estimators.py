@@ -157,3 +157,9 @@ def test_uncovered_estimator_options_are_refused(ref, captured_fit, kw):
         assert "refused" in captured_fit, "an uncovered option reached the parameter string"
     except (ValueError, NotImplementedError):
         return  # refused by the estimator's preflight through the shim
+
+
+def test_regressor_leaves_and_importances(ref, tmp_path):
+    est = ref.MojoTreesRegressor.load(write(tmp_path, "a.mbst", model_a(4)))
+    np.testing.assert_array_equal(np.asarray(est.predict(X_A, pred_leaf=True)).reshape(-1), [1, 2, 0, 1, 1, 1, 2])
+    np.testing.assert_array_equal(est.feature_importances_, [1, 1])

@@ -101,3 +101,37 @@ def test_gpu_fit_through_the_shim(shim, mtlib, objective):
         ran, out = _predict(shim, m, X, device=device)
         assert ran == device
         np.testing.assert_array_equal(out, m.predict(X))
+
+
+def test_predict_leaf(shim, mtlib, tmp_path):
+    """Leaf ordinals: a leaf's rank among its tree's leaves in node order
+    (tree.mojo:558-580).  Tree A's leaves are nodes 2, 3, 4."""
+    m = shim.load(write(tmp_path, "a.mbst", model_a(4)))
+    Xc = np.asfortranarray(X_A)
+    out = np.full(len(X_A), -9.0)
+    assert shim.predict_leaf_batch(m, Xc.ctypes.data, len(X_A), 2, {"device": "cpu", "start": 0, "stop": 1},
+                                   out.ctypes.data) == "cpu"
+    np.testing.assert_array_equal(out, [1, 2, 0, 1, 1, 1, 2])
+    with pytest.raises(NotImplementedError):
+        shim.predict_leaf_batch(m, Xc.ctypes.data, len(X_A), 2, {"device": "gpu", "start": 0, "stop": 1},
+                                out.ctypes.data)
+    imp = np.zeros(2)
+    shim.feature_importance(m, 2, 0, imp.ctypes.data)
+    np.testing.assert_array_equal(imp, [1, 1])
+    shim.feature_importance(m, 2, 1, imp.ctypes.data)
+    np.testing.assert_array_equal(imp, [5.0, 2.0])
+
+
+def test_predict_leaf_multiclass_range(shim, tmp_path):
+    # 2 iterations x 2 classes of one-leaf trees: every ordinal is 0; the
+    # range [1, 2) has K = 2 columns a row
+    from test_model_io import b, row, frow
+    s = "mojotrees v4\nmulticlass 2\n" + f"learning_rate {b(1.0)}\nbase_scores {b(0.0)} {b(0.0)}\n"
+    s += "mapper 1 255 1\n" + frow([0.0]) + row([0, 1]) + row([-1]) + "trees 4\n"
+    for v in (1.0, 2.0, 3.0, 4.0):
+        s += "tree 1 1\n" + row([-1]) * 4 + frow([v]) + row([0]) + row([-1]) + "counts 0\ngains 0\n"
+    m = shim.load(write(tmp_path, "mc.mbst", s))
+    X = np.zeros((3, 1), order="F")
+    out = np.full(3 * 2, -1.0)
+    shim.predict_leaf_multiclass(m, X.ctypes.data, 3, 1, 1, 2, out.ctypes.data)
+    np.testing.assert_array_equal(out, np.zeros(6))
