@@ -227,6 +227,24 @@ int32_t mojotrees_b200_predict_leaf(const MojoTreesModel *model, const double *d
                                     int64_t n_features, int64_t start_iteration, int64_t num_iteration,
                                     double *out_values, int64_t out_len, MojoTreesError *error);
 
+/* Validation scoring, the round loop of the reference's metric fits
+ * (custom_metric.mojo:1087-1280, which scores validation sets after every
+ * tree): bin the rows once with the model's mapper (feature-major uint8,
+ * out_bins[f * n_rows + r]), then add one iteration at a time to raw scores
+ * that start at the base scores.  Each step is the host predictor's
+ * raw = fma(learning_rate, leaf, raw), so after i steps the scores equal
+ * mojotrees_predict_ex's raw scores of the first i iterations bit for bit. */
+int32_t mojotrees_b200_model_bin(const MojoTreesModel *model, const double *data, int64_t n_rows,
+                                 int64_t n_features, uint8_t *out_bins, int64_t out_len, MojoTreesError *error);
+int32_t mojotrees_b200_add_iteration_raw(const MojoTreesModel *model, const uint8_t *bins, int64_t n_rows,
+                                         int64_t n_features, int64_t iteration, double *raw_inout, int64_t len,
+                                         MojoTreesError *error);
+/* A new model with the first n_iterations iterations of `model` (the
+ * early-stopping cut, custom_metric.mojo:1270-1280); free it with
+ * mojotrees_model_free. */
+int32_t mojotrees_b200_model_prefix(const MojoTreesModel *model, int64_t n_iterations, MojoTreesModel **out_model,
+                                    MojoTreesError *error);
+
 /* Data-parallel training (one process per GPU, rows sharded): a fresh
  * 128-byte NCCL unique id, created on one rank and broadcast by the caller. */
 int32_t mojotrees_b200_nccl_unique_id(uint8_t *out_id, MojoTreesError *error);

@@ -64,6 +64,9 @@ SIGNATURES = {
     "mojotrees_b200_ingest_column_major": (_I32, [_P, _P, _I64, _I64, _P, _P]),
     "mojotrees_b200_buffer_has_infinite": (_I32, [_P, _I64, _P, _P]),
     "mojotrees_b200_predict_leaf": (_I32, [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P]),
+    "mojotrees_b200_model_bin": (_I32, [_P, _P, _I64, _I64, _P, _I64, _P]),
+    "mojotrees_b200_add_iteration_raw": (_I32, [_P, _P, _I64, _I64, _I64, _P, _I64, _P]),
+    "mojotrees_b200_model_prefix": (_I32, [_P, _I64, _P, _P]),
     "mojotrees_b200_nccl_unique_id": (_I32, [_P, _P]),
     "mojotrees_b200_histogram_u8": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _I32, _P, _P]),
     "mojotrees_b200_histogram_u8_noalloc": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _I32, _P, _P, _P]),
@@ -255,6 +258,32 @@ class Model:
         t = IMPORTANCE_GAIN if importance_type == "gain" else IMPORTANCE_SPLIT
         e.check(lib().mojotrees_feature_importance(self.h, t, _ptr(out), out.size, e.h))
         return out
+
+    def bin_rows(self, X):
+        """Feature-major uint8 bins [n_features, n_rows] of float64 rows,
+        with this model's mapper."""
+        X = np.asfortranarray(np.asarray(X, dtype=np.float64))
+        n, f = X.shape
+        out = np.empty((f, n), np.uint8)
+        e = _Err()
+        e.check(lib().mojotrees_b200_model_bin(self.h, X.ctypes.data_as(ctypes.c_void_p), n, f, _ptr(out), out.size,
+                                               e.h))
+        return out
+
+    def add_iteration_raw(self, bins_fm, iteration, raw):
+        """raw (float64 [n_rows * num_classes]) += iteration's trees, in
+        place, with the predictor's fused multiply-add."""
+        f, n = bins_fm.shape
+        e = _Err()
+        e.check(lib().mojotrees_b200_add_iteration_raw(self.h, _ptr(bins_fm), n, f, int(iteration), _ptr(raw),
+                                                       raw.size, e.h))
+
+    def prefix(self, n_iterations):
+        """A new model with the first n_iterations iterations."""
+        e = _Err()
+        h = ctypes.c_void_p()
+        e.check(lib().mojotrees_b200_model_prefix(self.h, int(n_iterations), ctypes.byref(h), e.h))
+        return Model(h.value)
 
     def categorical_features(self):
         """Indices of the features the model splits by category set."""

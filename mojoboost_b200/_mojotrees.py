@@ -130,6 +130,95 @@ def fit_multiclass(x_addr, n_rows, n_features, y_addr, n_classes, params):
     return fit(x_addr, n_rows, n_features, y_addr, MULTICLASS, p)
 
 
+# ---- fits scored on validation sets (bindings/_mojotrees.mojo:2709-3060;
+# the round loop and early stopping of custom_metric.mojo:1000-1290) --------
+
+_METRIC_PARAM_KEYS = {"valid_sets", "n_valid", "metrics", "n_metrics", "primary_metric", "early_stopping_rounds",
+                      "min_delta", "pred_addr", "reset_addr", "evals_addr", "callback", "has_callback"}
+
+
+def _fit_scored(x_addr, n_rows, n_features, y_addr, objective, bridge, params):
+    """Train on the device, then score the validation sets after every
+    iteration on the host.  Training is deterministic and no round depends on
+    a later one, so the first i iterations of the full fit are the model the
+    reference's round loop holds after i trees; scoring them in order,
+    stopping when any flagged (set, metric) pair has gone
+    early_stopping_rounds rounds without a strict improvement beyond
+    min_delta, and cutting to the primary metric's best round on the first
+    set is the reference's metric fit.  Callbacks can change a round's
+    hyperparameters and are not covered."""
+    if int(params.get("has_callback", 0)):
+        raise NotImplementedError("training callbacks are not covered by the B200 device path")
+    esr = int(params.get("early_stopping_rounds", 0))
+    min_delta = float(params.get("min_delta", 0.0))
+    if esr < 0:
+        raise ValueError("early_stopping_rounds must not be negative")
+    if min_delta < 0.0:
+        raise ValueError("min_delta must not be negative")
+    metrics = [tuple(params["metrics"][m]) for m in range(int(params["n_metrics"]))]
+    valid = [tuple(params["valid_sets"][v]) for v in range(int(params["n_valid"]))]
+    primary = int(params.get("primary_metric", 0))
+    if metrics and not 0 <= primary < len(metrics):
+        raise ValueError("primary_metric out of range")
+    train_params = {k: v for k, v in params.items() if k not in _METRIC_PARAM_KEYS}
+    model = fit(x_addr, n_rows, n_features, y_addr, objective, train_params)
+    K = model.num_classes
+    n_features = int(n_features)
+    pred = _f64(int(params["pred_addr"]), max([int(v[2]) for v in valid] + [0]) * K)
+    bins, raws = [], []
+    for name, vx, vn, vy in valid:
+        vn = int(vn)
+        X = _f64(int(vx), vn * n_features).reshape(n_features, vn).T  # column-major rows
+        bins.append(model.bin_rows(X))
+        raws.append(np.tile(model.base_scores(), vn))
+    n_v, n_m = len(valid), len(metrics)
+    values, best_value, best_round = [], [0.0] * (n_v * n_m), [0] * (n_v * n_m)
+
+    def score(rnd):
+        for v in range(n_v):
+            pred[: raws[v].size] = raws[v]
+            for m in range(n_m):
+                value = float(bridge(m, v))
+                if not np.isfinite(value):
+                    raise ValueError(f"metric {metrics[m][0]} returned a non-finite value on validation set "
+                                     f"{valid[v][0]} at round {rnd}")
+                values.append(value)
+                i = v * n_m + m
+                if rnd == 0:
+                    best_value[i], best_round[i] = value, 0
+                elif (value > best_value[i] + min_delta) if int(metrics[m][1]) else \
+                        (value < best_value[i] - min_delta):
+                    best_value[i], best_round[i] = value, rnd
+
+    score(0)
+    stopped = False
+    iters = model.num_iterations
+    for it in range(iters):
+        for v in range(n_v):
+            model.add_iteration_raw(bins[v], it, raws[v])
+        score(it + 1)
+        if esr > 0 and any(int(metrics[i % n_m][2]) and (it + 1) - best_round[i] >= esr
+                           for i in range(n_v * n_m)):
+            stopped = True
+            break
+    best = best_round[primary] if n_m else 0
+    best_score = best_value[primary] if n_m else 0.0
+    if esr > 0 and best < iters:
+        model = model.prefix(best)
+    n_rounds = len(values) // (n_v * n_m) if n_v * n_m else 0
+    return [model, values, n_rounds, best, best_score, int(stopped)]
+
+
+def fit_with_metrics(x_addr, n_rows, n_features, y_addr, objective, bridge, params):
+    return _fit_scored(x_addr, n_rows, n_features, y_addr, int(objective), bridge, dict(params))
+
+
+def fit_multiclass_with_metrics(x_addr, n_rows, n_features, y_addr, n_classes, bridge, params):
+    p = dict(params)
+    p["num_class"] = int(n_classes)
+    return _fit_scored(x_addr, n_rows, n_features, y_addr, MULTICLASS, bridge, p)
+
+
 def resolve_device(device, n_rows=0, n_features=0, n_outputs=1):
     """`gpu` when a CUDA device is present; an explicit `gpu` request without
     one raises instead of falling back (capi/mojotrees.h:99-106)."""

@@ -680,6 +680,75 @@ int32_t mojotrees_b200_predict_leaf(const MojoTreesModel* model, const double* d
       MOJOTREES_ERROR_INVALID_ARGUMENT);
 }
 
+// Rows binned with the model's own mapper, feature-major
+// (out[f * n_rows + r]), for repeated scoring of one matrix.
+int32_t mojotrees_b200_model_bin(const MojoTreesModel* model, const double* data, int64_t n_rows, int64_t n_features,
+                                 uint8_t* out_bins, int64_t out_len, MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!model || ((!data || !out_bins) && n_rows > 0)) throw InvalidArgument("null pointer argument");
+        const mtb::Model& m = model->m;
+        if (n_rows < 0) throw InvalidArgument("n_rows must be non-negative");
+        if (n_features != m.n_features) throw InvalidArgument("n_features does not match the model");
+        if (!m.has_mapper)
+          throw mtb::Unsupported("model was trained on pre-binned data; raw values cannot be binned");
+        if (out_len < n_rows * n_features) throw InvalidArgument("output buffer too small");
+        if (n_rows > 0) mtb::transform(m.mapper, data, n_rows, out_bins);
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+// raw[r * K + k] = fma(learning_rate, tree(iteration * K + k)(row r),
+// raw[r * K + k]) for feature-major bins: one step of the host predictor's
+// sum, so adding iterations 0..i-1 to the base scores gives the raw scores
+// of the first i iterations bit for bit.
+int32_t mojotrees_b200_add_iteration_raw(const MojoTreesModel* model, const uint8_t* bins, int64_t n_rows,
+                                         int64_t n_features, int64_t iteration, double* raw_inout, int64_t len,
+                                         MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!model || ((!bins || !raw_inout) && n_rows > 0)) throw InvalidArgument("null pointer argument");
+        const mtb::Model& m = model->m;
+        if (n_features != m.n_features) throw InvalidArgument("n_features does not match the model");
+        const int K = m.num_class;
+        const int64_t iters = (int64_t)m.trees.size() / K;
+        if (iteration < 0 || iteration >= iters) throw InvalidArgument("iteration out of range");
+        if (n_rows < 0 || len < n_rows * K) throw InvalidArgument("raw buffer too small");
+#pragma omp parallel for schedule(static)
+        for (int64_t r = 0; r < n_rows; ++r)
+          for (int k = 0; k < K; ++k)
+            raw_inout[r * K + k] =
+                fma(m.learning_rate, tree_value(m.trees[(size_t)(iteration * K + k)], bins + r, n_rows),
+                    raw_inout[r * K + k]);
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+// A new model holding the first n_iterations iterations of `model` (the cut
+// early stopping makes); `model` itself is unchanged.
+int32_t mojotrees_b200_model_prefix(const MojoTreesModel* model, int64_t n_iterations, MojoTreesModel** out_model,
+                                    MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!model || !out_model) throw InvalidArgument("null pointer argument");
+        const mtb::Model& m = model->m;
+        const int64_t iters = (int64_t)m.trees.size() / m.num_class;
+        if (n_iterations < 0 || n_iterations > iters) throw InvalidArgument("n_iterations out of range");
+        std::unique_ptr<MojoTreesModel> h(new MojoTreesModel());
+        h->m = m;
+        h->m.trees.resize((size_t)(n_iterations * m.num_class));
+        h->m.train_scores.clear();
+        *out_model = h.release();
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
 int32_t mojotrees_b200_bin_dense(const double* data, int64_t n_rows, int64_t n_features, const char* parameters,
                                  uint8_t* out_bins, int32_t* out_missing_bin, int32_t* out_n_categories,
                                  int32_t* out_n_bins, MojoTreesError* error) {
