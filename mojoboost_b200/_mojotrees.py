@@ -258,12 +258,17 @@ def _predict_into(model, x_addr, n_rows, n_features, params, out_addr):
     raw = int(params.get("raw_score", 0)) != 0
     out = _f64(int(out_addr), n_rows * k)
     if stop <= start:
-        # an empty range: the base scores (from iteration 0) or nothing
-        base = model.base_scores() if start == 0 else np.zeros(k)
-        vals = np.tile(base, (n_rows, 1))
-        if not raw:
-            vals = _response(model, vals)
-        out[:] = vals.reshape(-1)
+        # an empty range scores no tree: from iteration 0 that is the base
+        # scores, answered by the C predictor on a zero-iteration copy (so
+        # the response is its arithmetic); from a later start, raw scores of
+        # zero, whose responses are exact (sigmoid 0.5, softmax 1/K)
+        if start == 0:
+            X = _f64(int(x_addr), n_rows * n_features).reshape(n_features, n_rows).T
+            out[:] = model.prefix(0).predict(X, raw_score=raw).reshape(-1)
+        elif raw or model.objective_name == "regression":
+            out[:] = 0.0
+        else:
+            out[:] = 0.5 if k == 1 else 1.0 / k
         return "cpu" if _DEVICES[device] != _capi.DEVICE_GPU else "gpu"
     X = _f64(int(x_addr), n_rows * n_features)
     e = _capi._Err()
@@ -271,15 +276,6 @@ def _predict_into(model, x_addr, n_rows, n_features, params, out_addr):
                                              stop - start, _capi.PREDICT_RAW if raw else _capi.PREDICT_RESPONSE,
                                              _DEVICES[device], out.ctypes.data_as(ctypes.c_void_p), out.size, e.h))
     return "gpu" if _DEVICES[device] == _capi.DEVICE_GPU else "cpu"
-
-
-def _response(model, raw):
-    if model.num_classes > 1:
-        z = np.exp(raw - raw.max(axis=1, keepdims=True))
-        return z / z.sum(axis=1, keepdims=True)
-    if model.objective_name == "binary":
-        return 1.0 / (1.0 + np.exp(-raw))
-    return raw
 
 
 def predict_leaf(model, x_addr, n_rows, n_features, start, stop, out_addr):

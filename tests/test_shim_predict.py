@@ -135,3 +135,17 @@ def test_predict_leaf_multiclass_range(shim, tmp_path):
     out = np.full(3 * 2, -1.0)
     shim.predict_leaf_multiclass(m, X.ctypes.data, 3, 1, 1, 2, out.ctypes.data)
     np.testing.assert_array_equal(out, np.zeros(6))
+
+
+def test_empty_range_response(shim, tmp_path):
+    """An empty iteration range scores no tree: from iteration 0 the response
+    of the base score (the C predictor's sigmoid), from a later start the
+    response of a zero raw score."""
+    import math
+    m = shim.load(write(tmp_path, "b.mbst", model_a(4).replace("objective 0", "objective 1")))
+    _, out = _predict(shim, m, X_A, stop=0)
+    assert np.all(out == 1.0 / (1.0 + math.exp(-0.25)))
+    _, out = _predict(shim, m, X_A, start=1, stop=1)
+    assert np.all(out == 0.5)
+    _, out = _predict(shim, m, X_A, stop=0, raw_score=1)
+    assert np.all(out == 0.25)
