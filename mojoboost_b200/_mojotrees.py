@@ -219,6 +219,94 @@ def fit_multiclass_with_metrics(x_addr, n_rows, n_features, y_addr, n_classes, b
     return _fit_scored(x_addr, n_rows, n_features, y_addr, MULTICLASS, bridge, p)
 
 
+# ---- sparse input (bindings/_mojotrees.mojo:3335-3510) --------------------
+
+_SPARSE_KEYS = {"sparse_data_addr", "sparse_indices_addr", "sparse_indptr_addr", "sparse_nnz", "n_rows",
+                "n_features"}
+
+
+def _i64(addr, n):
+    if n == 0:
+        return np.zeros(0, np.int64)
+    buf = (ctypes.c_int64 * n).from_address(int(addr))
+    return np.frombuffer(buf, dtype=np.int64, count=n)
+
+
+def _densify(params, compressed_columns):
+    """The dense float64 matrix [n_rows, n_features] (column-major) of a CSC
+    (compressed_columns) or CSR matrix given by buffer addresses: absent
+    entries are the value 0.0 and a stored NaN is missing, the semantics the
+    reference's sparse path shares with its dense one (sparse.mojo:535-570:
+    bit-identical bins to the densified matrix).  Needs n_rows x n_features
+    x 8 bytes of host memory."""
+    n, f, nnz = int(params["n_rows"]), int(params["n_features"]), int(params["sparse_nnz"])
+    if n < 0 or f < 0 or nnz < 0:
+        raise ValueError("sparse matrix: negative shape or nnz")
+    n_major = f if compressed_columns else n
+    n_minor = n if compressed_columns else f
+    indptr = _i64(params["sparse_indptr_addr"], n_major + 1)
+    indices = _i64(params["sparse_indices_addr"], nnz)
+    data = _f64(int(params["sparse_data_addr"]), nnz) if nnz else np.zeros(0)
+    if indptr[0] != 0 or indptr[-1] != nnz or np.any(np.diff(indptr) < 0):
+        raise ValueError("sparse matrix: indptr is not a valid offset array")
+    if nnz and (indices.min() < 0 or indices.max() >= n_minor):
+        raise ValueError("sparse matrix: an index is out of range")
+    major = np.repeat(np.arange(n_major), np.diff(indptr))
+    if nnz > 1:
+        same = major[1:] == major[:-1]
+        if np.any(same & (indices[1:] <= indices[:-1])):
+            raise ValueError("sparse matrix: indices must be strictly increasing within each "
+                             + ("column" if compressed_columns else "row"))
+    dense = np.zeros((n, f), order="F")
+    if compressed_columns:
+        dense[indices, major] = data
+    else:
+        dense[major, indices] = data
+    return dense
+
+
+def _dense_params(params):
+    return {k: v for k, v in params.items() if k not in _SPARSE_KEYS}
+
+
+def fit_csc(y_addr, objective, params):
+    """A fit on a CSC matrix: the densified matrix through the dense device
+    path (the same bins and trees as the reference's sparse fit of it)."""
+    X = _densify(params, True)
+    n, f = X.shape
+    return fit(X.ctypes.data, n, f, y_addr, int(objective), _dense_params(params))
+
+
+def fit_multiclass_csc(y_addr, n_classes, params):
+    X = _densify(params, True)
+    n, f = X.shape
+    return fit_multiclass(X.ctypes.data, n, f, y_addr, n_classes, _dense_params(params))
+
+
+def _predict_csr(model, params, out_addr, raw):
+    device = str(params.get("device", "cpu")).lower()
+    if device in ("gpu", "cuda"):
+        # as the reference does (`_refuse_gpu_sparse`): sparse prediction
+        # has no device walk, and densifying behind the caller is not done
+        raise NotImplementedError("device='gpu' prediction of sparse input: the sparse walk runs on the host")
+    X = _densify(params, False)
+    n, f = X.shape
+    return _predict_into(model, X.ctypes.data, n, f, {"device": "cpu", "start": 0, "stop": model.num_iterations,
+                                                      "raw_score": int(raw)}, out_addr)
+
+
+def predict_csr(model, params, out_addr):
+    _predict_csr(model, params, out_addr, False)
+
+
+def predict_raw_csr(model, params, out_addr):
+    _predict_csr(model, params, out_addr, True)
+
+
+def predict_proba_csr(model, params, out_addr):
+    _predict_csr(model, params, out_addr, bool(int(params.get("raw_score", 0))))
+
+
 def resolve_device(device, n_rows=0, n_features=0, n_outputs=1):
     """`gpu` when a CUDA device is present; an explicit `gpu` request without
     one raises instead of falling back (capi/mojotrees.h:99-106)."""

@@ -163,3 +163,15 @@ def test_regressor_leaves_and_importances(ref, tmp_path):
     est = ref.MojoTreesRegressor.load(write(tmp_path, "a.mbst", model_a(4)))
     np.testing.assert_array_equal(np.asarray(est.predict(X_A, pred_leaf=True)).reshape(-1), [1, 2, 0, 1, 1, 1, 2])
     np.testing.assert_array_equal(est.feature_importances_, [1, 1])
+
+
+def test_sparse_input_through_the_estimators(ref, captured_fit, tmp_path):
+    """SciPy sparse input: prediction equals the dense prediction, and a
+    sparse fit reaches the device fit with the estimator's parameters."""
+    sp = pytest.importorskip("scipy.sparse")
+    est = ref.MojoTreesRegressor.load(write(tmp_path, "a.mbst", model_a(4)))
+    X = np.nan_to_num(X_A)
+    np.testing.assert_array_equal(est.predict(sp.csr_matrix(X)), est.predict(X))
+    fit_est = ref.MojoTreesRegressor(n_estimators=3, device="gpu")
+    _fit(fit_est, sp.random(100, 4, density=0.3, format="csc", random_state=0), np.random.default_rng(2).random(100))
+    assert "num_iterations=3" in captured_fit["string"]
