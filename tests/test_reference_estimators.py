@@ -14,7 +14,7 @@ import pytest
 
 from test_model_io import RAW_A, X_A, model_a, write
 
-REF_PY = "/root/reference/python"
+REF_PY = os.environ.get("MOJOTREES_REFERENCE_PYTHON", "/root/reference/python")
 pytestmark = pytest.mark.skipif(not os.path.isdir(os.path.join(REF_PY, "mojotrees")),
                                 reason="the reference package is not mounted")
 
