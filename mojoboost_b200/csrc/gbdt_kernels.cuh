@@ -981,10 +981,36 @@ __device__ void scan_pair_done(TreeState* __restrict__ ts, int c, const FeatBest
 // threshold, and a warp arg-max that keeps the serial scan's tie rule (first
 // maximum in bin order, missing-left candidate before default-right).  Pair
 // p = child * n_active + j, child = 2 * item + side.
+// One numerical split candidate (left sums Dg, Dh, Dc): the leaf guards and
+// the gain, exactly the inline arithmetic of k_scan (same operations in the
+// same order; the file is compiled without FMA contraction), or -infinity
+// when a guard rejects it.  Out of line so the correctly rounded divisions
+// appear once in the code rather than at every unrolled candidate site: the
+// inline form makes k_scan instruction-fetch bound.
+struct ScanCandCtx {
+  int mode;
+  double g_inv, h_inv, gu, hu, tg, th, l1, l2, mch, parent, parent_q;
+  long long Tg, Th, Tc, mdl;
+};
+
+__device__ __noinline__ double scan_candidate_gain(long long Dg, long long Dh, long long Dc,
+                                                   const ScanCandCtx& c) {
+  const double dlg = deq(Dg, c.mode, c.g_inv, c.gu), dlh = deq(Dh, c.mode, c.h_inv, c.hu);
+  const double drg = c.mode == MODE_FIXED ? c.tg - dlg : deq(c.Tg - Dg, c.mode, c.g_inv, c.gu);
+  const double drh = c.mode == MODE_FIXED ? c.th - dlh : deq(c.Th - Dh, c.mode, c.h_inv, c.hu);
+  if (dlh < c.mch || drh < c.mch || Dc < c.mdl || c.Tc - Dc < c.mdl) return -INFINITY;
+  if (c.mode == MODE_FIXED) {
+    const double tl = soft_l1(dlg, c.l1), tr = soft_l1(drg, c.l1);
+    return tl * tl / (dlh + c.l2) + tr * tr / (drh + c.l2) - c.parent;
+  }
+  return leaf_score(dlg, dlh, c.l1, c.l2) + leaf_score(drg, drh, c.l1, c.l2) - c.parent_q;
+}
+
 constexpr int kScanWarps = 8;    // pairs per block
 constexpr int kBinsPerLane = 8;  // 32 x 8 = 256 bins at most
 
-__global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan(TreeState* __restrict__ ts, int* __restrict__ hist,
+template <bool COMPACT>
+__global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan_t(TreeState* __restrict__ ts, int* __restrict__ hist,
                                                           long long slot_cells, const int* __restrict__ feats,
                                                           const int* __restrict__ missing_bin,
                                                           const int* __restrict__ n_cats,
@@ -1192,6 +1218,7 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan(TreeState* __restri
   int best_key = 0x7fffffff;  // 2*bin + order
   long long best_nl = 0;
   long long Lg = ig - sg, Lh = ih - sh, Lc = ic - scn;  // prefix before this lane's bins
+  const ScanCandCtx cx{mode, g_inv, h_inv, gu, hu, tg, th, l1, l2, mch, parent, parent_q, Tg, Th, Tc, mdl};
 #pragma unroll
   for (int q = 0; q < kBinsPerLane; ++q) {
     const int b = b0 + q;
@@ -1199,6 +1226,25 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan(TreeState* __restri
     Lh += vh[q];
     Lc += vc[q];
     if (!(b < n_scan && !(b == n_scan - 1 && mc == 0))) continue;
+    if (COMPACT) {
+      if (mb >= 0) {
+        const double gain = scan_candidate_gain(Lg + mg, Lh + mh, Lc + mc, cx);
+        if (gain > best_gain) {
+          best_gain = gain;
+          best_key = 2 * b;
+          best_nl = Lc + mc;
+        }
+      }
+      if (mb < 0 || mc > 0) {
+        const double gain = scan_candidate_gain(Lg, Lh, Lc, cx);
+        if (gain > best_gain) {
+          best_gain = gain;
+          best_key = 2 * b + 1;
+          best_nl = Lc;
+        }
+      }
+      continue;
+    }
     if (mb >= 0) {
       long long Dg = Lg + mg, Dh = Lh + mh, Dc = Lc + mc;
       double dlg = deq(Dg, mode, g_inv, gu), dlh = deq(Dh, mode, h_inv, hu);

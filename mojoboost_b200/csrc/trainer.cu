@@ -332,6 +332,10 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   // Leaves expanded per iteration (speculative leaf batching); 1 grows one
   // split per iteration as the reference does.  MOJOTREES_BATCH overrides.
   int batch_cap = 32;
+  // MOJOTREES_SCAN=compact selects the split scan whose candidate evaluation
+  // is one out-of-line routine (same arithmetic, smaller code)
+  const char* scan_env = getenv("MOJOTREES_SCAN");
+  const bool scan_compact = scan_env && std::string(scan_env) == "compact";
   if (const char* e = getenv("MOJOTREES_BATCH")) batch_cap = atoi(e);
   batch_cap = std::max(1, std::min(std::min(batch_cap, kMaxBatch), cfg.num_leaves - 1));
   // Histogram slots: the root, one per expansion (at most num_leaves - 1
@@ -591,8 +595,8 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
         hist();
         reduce_work();
         timer.begin(&stats.scan_ms);
-        k_scan<<<scan_grid, kScanWarps * 32, 0, st>>>(d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p, d_ncats.p,
-                                                    d_sc.p, sp, d_fb.p, work_base);
+        (scan_compact ? k_scan_t<true> : k_scan_t<false>)<<<scan_grid, kScanWarps * 32, 0, st>>>(
+            d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p, d_ncats.p, d_sc.p, sp, d_fb.p, work_base);
         timer.end();
         timer.begin(&stats.commit_ms);
         k_commit<<<1, kCommitThreads, commit_smem, st>>>(d_ts.p, d_missing.p, cp, commit_cap, d_done,

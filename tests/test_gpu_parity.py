@@ -7,6 +7,8 @@ the reference's own test strategy (tests/test_gpu_training.mojo,
 tests/test_host_replica.mojo): several objectives, missing values,
 categorical splits, feature sampling, tiny and ragged shapes.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -172,3 +174,13 @@ def test_gpu_round_times_and_stats(mtlib):
     assert len(rt) == 4 and np.all(rt > 0)
     st = m.stats()
     assert st["hist_rows"] >= 4 * 20_000 and st["kernel_launches"] > 0
+
+
+@pytest.mark.skipif(os.environ.get("MOJOTREES_TEST_SCAN_COMPACT") != "1",
+                    reason="the compact split scan is an opt-in variant; set MOJOTREES_TEST_SCAN_COMPACT=1")
+@pytest.mark.parametrize("case", ["binary_quant", "missing_cat_fixed", "regularised_quant", "binary_quant_large"])
+def test_gpu_compact_scan_matches_oracle(case, mtlib, oracle, monkeypatch):
+    """MOJOTREES_SCAN=compact (candidate evaluation out of line) grows the
+    oracle's trees bit for bit, like the default scan."""
+    monkeypatch.setenv("MOJOTREES_SCAN", "compact")
+    test_gpu_matches_oracle(case, mtlib, oracle)
