@@ -296,8 +296,8 @@ class Model:
     def objective_name(self):
         """'regression', 'binary' or 'multiclass'."""
         import json
-        code = json.loads(self.dump_json())["objective"]
-        return {0: "regression", 1: "binary", 2: "multiclass"}[int(code)]
+        code = json.loads(self.dump_json())["objective_code"]
+        return "multiclass" if code is None else {0: "regression", 1: "binary"}[int(code)]
 
     def dump_json(self):
         e = _Err()

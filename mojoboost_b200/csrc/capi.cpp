@@ -959,28 +959,7 @@ int32_t mojotrees_model_dump_json(const MojoTreesModel* model, char** out_text, 
       error,
       [&]() -> int32_t {
         if (!model || !out_text) throw InvalidArgument("null pointer argument");
-        const mtb::Model& m = model->m;
-        std::ostringstream os;
-        os.precision(17);
-        os << "{\"schema\":\"mojotrees-b200\",\"objective\":" << m.objective << ",\"num_class\":" << m.num_class
-           << ",\"num_features\":" << m.n_features << ",\"learning_rate\":" << m.learning_rate << ",\"base_scores\":[";
-        for (size_t i = 0; i < m.base_scores.size(); ++i) os << (i ? "," : "") << m.base_scores[i];
-        os << "],\"feature_names\":[";
-        for (int f = 0; f < m.n_features; ++f) os << (f ? "," : "") << "\"Column_" << f << "\"";
-        os << "],\"trees\":[";
-        for (size_t t = 0; t < m.trees.size(); ++t) {
-          os << (t ? "," : "") << "{\"nodes\":[";
-          for (size_t i = 0; i < m.trees[t].size(); ++i) {
-            const auto& nd = m.trees[t][i];
-            os << (i ? "," : "") << "{\"feature\":" << nd.feature << ",\"threshold_bin\":" << nd.thr
-               << ",\"left\":" << nd.left << ",\"right\":" << nd.right << ",\"default_left\":" << nd.dleft
-               << ",\"missing_bin\":" << nd.mbin << ",\"categorical\":" << nd.is_cat << ",\"value\":" << nd.value
-               << ",\"gain\":" << nd.gain << ",\"count\":" << nd.count << "}";
-          }
-          os << "]}";
-        }
-        os << "]}";
-        *out_text = dup_string(os.str());
+        *out_text = dup_string(mtb::dump_model_json(model->m));
         return MOJOTREES_OK;
       },
       MOJOTREES_ERROR_INVALID_ARGUMENT);

@@ -98,5 +98,7 @@ struct Model {
 // has_mapper = false.
 void save_model_v4(const Model& m, std::ostream& os);
 Model load_model_text(const std::string& content);
+// The reference's inspection dump of a model, as JSON (model_io.cpp).
+std::string dump_model_json(const Model& m);
 
 }  // namespace mtb

@@ -11,6 +11,8 @@
 #include <string.h>
 
 #include <cmath>
+#include <cstdio>
+#include <algorithm>
 #include <sstream>
 #include <stdexcept>
 #include <string>
@@ -413,6 +415,157 @@ Model load_model_text(const std::string& content) {
   // raw-value prediction of it is refused rather than answered wrongly.
   m.has_mapper = mapper_fits;
   return m;
+}
+
+// ---------------------------------------------------------------------------
+// The reference's inspection dump (src/mojotrees/model_dump.mojo :99-760,
+// written as JSON by inspection.mojo :78-330): the model, its binning and
+// every node, with thresholds as raw values and category sets as codes.
+// Numbers are written to round-trip exactly ("%.17g"); NaN and infinities
+// become null.
+// ---------------------------------------------------------------------------
+namespace {
+
+std::string jnum(double x) {
+  if (!std::isfinite(x)) return "null";
+  char buf[40];
+  snprintf(buf, sizeof buf, "%.17g", x);
+  return buf;
+}
+
+struct DumpCtx {
+  const Model& m;
+  bool has_gain;
+  std::vector<std::string> names;
+};
+
+void dump_node(std::string& out, const DumpCtx& c, const std::vector<HostNode>& t, const std::vector<int>& depth,
+               const std::vector<int>& leaf_ord, const std::vector<int>& split_ord, int node) {
+  const HostNode& nd = t[(size_t)node];
+  const BinMapper& mp = c.m.mapper;
+  out += "{\"node_index\":" + std::to_string(node);
+  if (nd.feature < 0) {
+    out += ",\"leaf_index\":" + std::to_string(leaf_ord[(size_t)node]);
+    out += ",\"leaf_value\":" + jnum(nd.value) + ",\"leaf_count\":" + jnum((double)nd.count);
+    out += ",\"depth\":" + std::to_string(depth[(size_t)node]) + "}";
+    return;
+  }
+  const int f = nd.feature;
+  out += ",\"split_index\":" + std::to_string(split_ord[(size_t)node]);
+  out += ",\"split_feature\":" + std::to_string(f) + ",\"split_feature_name\":\"" + c.names[(size_t)f] + "\"";
+  out += std::string(",\"decision_type\":") + (nd.is_cat ? "\"==\"" : "\"<=\"");
+  // threshold_value (model_dump.mojo:456-486): the split bin's upper edge
+  const bool feature_cat = f < (int)mp.is_cat.size() && mp.is_cat[(size_t)f];
+  const long long e0 = mp.edge_offsets[(size_t)f], e1 = mp.edge_offsets[(size_t)f + 1];
+  const bool has_thr = !nd.is_cat && !feature_cat && nd.thr >= 0 && nd.thr < e1 - e0;
+  out += ",\"threshold\":" + (has_thr ? jnum(mp.edges[(size_t)(e0 + nd.thr)]) : std::string("null"));
+  out += ",\"threshold_bin\":" + std::to_string(nd.is_cat ? -1 : nd.thr);
+  if (nd.is_cat) {
+    // category_bins / category_codes (model_dump.mojo:410-453)
+    std::string bins = "[", codes = "[";
+    const long long c0 = mp.cat_offsets.empty() ? 0 : mp.cat_offsets[(size_t)f];
+    const long long nc = mp.n_categories(f);
+    bool first = true;
+    for (int b = 0; b < 256; ++b)
+      if ((nd.bits[b >> 6] >> (b & 63)) & 1ull) {
+        if (b < 1 || b > nc) throw std::runtime_error("dump: a category set names a bin with no category");
+        bins += (first ? "" : ",") + std::to_string(b);
+        codes += (first ? "" : ",") + std::to_string(mp.cat_codes[(size_t)(c0 + b - 1)]);
+        first = false;
+      }
+    out += ",\"categories\":" + codes + "],\"category_bins\":" + bins + "]";
+  } else {
+    out += ",\"categories\":null,\"category_bins\":null";
+  }
+  const int mb = nd.is_cat ? -1 : nd.mbin;
+  out += std::string(",\"default_left\":") + (!nd.is_cat && nd.dleft ? "true" : "false");
+  out += ",\"missing_bin\":" + std::to_string(mb);
+  out += std::string(",\"missing_type\":") + (mb >= 0 ? "\"NaN\"" : "\"None\"");
+  out += ",\"split_gain\":" + (c.has_gain ? jnum(nd.gain) : std::string("null"));
+  out += ",\"internal_value\":" + jnum(nd.value) + ",\"internal_count\":" + jnum((double)nd.count);
+  out += ",\"depth\":" + std::to_string(depth[(size_t)node]);
+  out += ",\"left_child\":";
+  dump_node(out, c, t, depth, leaf_ord, split_ord, nd.left);
+  out += ",\"right_child\":";
+  dump_node(out, c, t, depth, leaf_ord, split_ord, nd.right);
+  out += "}";
+}
+
+}  // namespace
+
+std::string dump_model_json(const Model& m) {
+  const BinMapper& mp = m.mapper;
+  const int K = m.num_class, F = m.n_features;
+  if ((int64_t)mp.edge_offsets.size() != (int64_t)F + 1) throw std::runtime_error("model has no bin mapper to dump");
+  DumpCtx c{m, false, {}};
+  bool has_count = !m.trees.empty();
+  for (const auto& t : m.trees)
+    for (const auto& nd : t) {
+      if (nd.feature >= 0 && nd.gain > 0.0) c.has_gain = true;
+      if (!(nd.count > 0)) has_count = false;
+    }
+  for (int f = 0; f < F; ++f) c.names.push_back("Column_" + std::to_string(f));
+  std::string out = "{\"dump_format_version\":1,\"producer\":\"mojotrees\",\"model_format_version\":4";
+  out += ",\"source\":\"native\",\"objective_code\":";
+  out += m.objective == OBJECTIVE_MULTICLASS ? std::string("null") : std::to_string(m.objective);
+  out += ",\"num_class\":" + std::to_string(K) + ",\"num_tree_per_iteration\":" + std::to_string(K);
+  out += ",\"num_iteration\":" + std::to_string(m.trees.size() / (size_t)K);
+  out += ",\"learning_rate\":" + jnum(m.learning_rate) + ",\"base_score\":[";
+  for (int k = 0; k < K; ++k) out += (k ? "," : "") + jnum(m.base_scores[(size_t)k]);
+  out += "],\"leaf_value_is_shrunk\":false,\"num_feature\":" + std::to_string(F);
+  out += ",\"max_feature_idx\":" + std::to_string(F - 1) + ",\"num_bin\":" + std::to_string(mp.n_bins);
+  out += ",\"feature_names\":[";
+  for (int f = 0; f < F; ++f) out += (f ? ",\"" : "\"") + c.names[(size_t)f] + "\"";
+  out += "],\"feature_infos\":[";
+  for (int f = 0; f < F; ++f) {
+    const bool cat = f < (int)mp.is_cat.size() && mp.is_cat[(size_t)f];
+    const int mb = mp.missing_bin[(size_t)f];
+    out += (f ? ",{" : "{") + std::string("\"index\":") + std::to_string(f) + ",\"name\":\"" + c.names[(size_t)f] + "\"";
+    out += ",\"missing_bin\":" + std::to_string(mb) + std::string(",\"missing_type\":") + (mb >= 0 ? "\"NaN\"" : "\"None\"");
+    out += ",\"monotone\":0";
+    if (cat) {
+      const long long c0 = mp.cat_offsets[(size_t)f], nc = mp.n_categories(f);
+      out += ",\"type\":\"categorical\",\"categories\":[";
+      for (long long i = 0; i < nc; ++i) out += (i ? "," : "") + std::to_string(mp.cat_codes[(size_t)(c0 + i)]);
+      out += "],\"bin_upper_bounds\":null,\"num_bin\":" + std::to_string(nc + 1) + "}";
+    } else {
+      const long long e0 = mp.edge_offsets[(size_t)f], e1 = mp.edge_offsets[(size_t)f + 1];
+      out += ",\"type\":\"numerical\",\"categories\":null,\"bin_upper_bounds\":[";
+      for (long long i = e0; i < e1; ++i) out += (i > e0 ? "," : "") + jnum(mp.edges[(size_t)i]);
+      out += "],\"num_bin\":" + std::to_string(e1 - e0 + 1 + (mb >= 0 ? 1 : 0)) + "}";
+    }
+  }
+  out += "],\"monotone_constraints\":null";
+  out += std::string(",\"has_split_gain\":") + (c.has_gain ? "true" : "false");
+  out += std::string(",\"has_node_count\":") + (has_count ? "true" : "false");
+  out += ",\"linear_tree\":false,\"tree_info\":[";
+  for (size_t ti = 0; ti < m.trees.size(); ++ti) {
+    const auto& t = m.trees[ti];
+    const size_t n = t.size();
+    std::vector<int> depth(n, 0), leaf_ord(n, -1), split_ord(n, -1);
+    int leaves = 0, splits = 0, n_cat = 0, max_depth = 0;
+    for (size_t i = 0; i < n; ++i) {
+      if (t[i].feature < 0) {
+        leaf_ord[i] = leaves++;
+        continue;
+      }
+      split_ord[i] = splits++;
+      n_cat += t[i].is_cat ? 1 : 0;
+      depth[(size_t)t[i].left] = depth[i] + 1;  // children follow their parent in node order
+      depth[(size_t)t[i].right] = depth[i] + 1;
+    }
+    for (size_t i = 0; i < n; ++i) max_depth = std::max(max_depth, depth[i]);
+    out += (ti ? ",{" : "{") + std::string("\"tree_index\":") + std::to_string(ti);
+    out += ",\"iteration\":" + std::to_string(ti / (size_t)K) + ",\"class_id\":" + std::to_string(ti % (size_t)K);
+    out += ",\"num_leaves\":" + std::to_string(leaves) + ",\"num_nodes\":" + std::to_string(n);
+    out += ",\"num_cat\":" + std::to_string(n_cat) + ",\"max_depth\":" + std::to_string(max_depth);
+    out += ",\"shrinkage\":" + jnum(m.learning_rate) + ",\"tree_structure\":";
+    if (n) dump_node(out, c, t, depth, leaf_ord, split_ord, 0);
+    else out += "null";
+    out += "}";
+  }
+  out += "]}";
+  return out;
 }
 
 }  // namespace mtb

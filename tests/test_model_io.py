@@ -218,3 +218,51 @@ def test_corrupted_files_never_crash(mtlib, tmp_path):
         except mtlib.MojoTreesError:
             pass
     assert loaded > 0
+
+
+def test_dump_json_inspection_schema(mtlib, tmp_path):
+    """mojotrees_model_dump_json writes the reference's inspection schema
+    (model_dump.mojo, inspection.mojo): thresholds as the split bins' upper
+    edges, category sets as codes, leaf ordinals, depths."""
+    import json
+    d = json.loads(mtlib.Model.load(write(tmp_path, "a.mbst", model_a(4))).dump_json())
+    assert (d["dump_format_version"], d["producer"], d["model_format_version"]) == (1, "mojotrees", 4)
+    assert (d["objective_code"], d["num_class"], d["num_iteration"], d["num_feature"]) == (0, 1, 1, 2)
+    assert d["learning_rate"] == 0.5 and d["base_score"] == [0.25]
+    f0, f1 = d["feature_infos"]
+    assert f0["bin_upper_bounds"] == [0.5, 1.5] and f0["missing_type"] == "NaN" and f0["num_bin"] == 4
+    assert f1["bin_upper_bounds"] == [0.0] and f1["missing_type"] == "None" and f1["num_bin"] == 2
+    assert d["has_split_gain"] and d["has_node_count"]
+    t = d["tree_info"][0]
+    assert (t["num_leaves"], t["num_nodes"], t["max_depth"], t["num_cat"]) == (3, 5, 2, 0)
+    root = t["tree_structure"]
+    assert (root["split_feature"], root["threshold"], root["threshold_bin"], root["default_left"]) == (0, 1.5, 1, True)
+    assert root["split_gain"] == 5.0 and root["missing_bin"] == 3 and root["decision_type"] == "<="
+    node1 = root["left_child"]
+    assert (node1["split_feature"], node1["threshold"], node1["depth"]) == (1, 0.0, 1)
+    assert root["right_child"] == {"node_index": 2, "leaf_index": 0, "leaf_value": 3.0, "leaf_count": 40.0, "depth": 1}
+    assert node1["left_child"]["leaf_index"] == 1 and node1["right_child"]["leaf_value"] == 2.0
+
+
+def test_dump_json_categorical_and_multiclass(mtlib, tmp_path):
+    import json
+    s = "mojotrees v4\nobjective 0\n" + f"learning_rate {b(1.0)}\nbase_score {b(0.0)}\n"
+    s += "mapper 1 255 0\n\n" + row([0, 0]) + row([-1])
+    s += "categorical 1 3\n" + row([1]) + row([3, 7, 9]) + row([0, 3])
+    s += "trees 1\ntree 3 2\n" + row([0, -1, -1]) + row([-1, -1, -1]) + row([1, -1, -1]) + row([2, -1, -1])
+    s += frow([0.0, 1.0, 2.0]) + row([0, 0, 0]) + row([-1, -1, -1])
+    s += "counts 1\n" + frow([9.0, 4.0, 5.0]) + "gains 1\n" + frow([1.5, 0.0, 0.0])
+    s += "cat 4\n" + row([0, -1, -1]) + row([4, 0, 0, 0])
+    d = json.loads(mtlib.Model.load(write(tmp_path, "cat.mbst", s)).dump_json())
+    assert d["feature_infos"][0]["type"] == "categorical" and d["feature_infos"][0]["categories"] == [3, 7, 9]
+    root = d["tree_info"][0]["tree_structure"]
+    assert (root["decision_type"], root["categories"], root["category_bins"], root["threshold"]) == ("==", [7], [2], None)
+    assert d["tree_info"][0]["num_cat"] == 1
+    s = "mojotrees v4\nmulticlass 2\n" + f"learning_rate {b(1.0)}\nbase_scores {b(0.0)} {b(0.5)}\n"
+    s += "mapper 1 255 1\n" + frow([0.0]) + row([0, 1]) + row([-1]) + "trees 2\n"
+    for v in (1.0, 2.0):
+        s += "tree 1 1\n" + row([-1]) * 4 + frow([v]) + row([0]) + row([-1]) + "counts 1\n" + frow([3.0]) + "gains 0\n"
+    d = json.loads(mtlib.Model.load(write(tmp_path, "mc.mbst", s)).dump_json())
+    assert d["objective_code"] is None and d["num_tree_per_iteration"] == 2 and d["base_score"] == [0.0, 0.5]
+    assert [(t["iteration"], t["class_id"]) for t in d["tree_info"]] == [(0, 0), (0, 1)]
+    assert d["has_split_gain"] is False and d["tree_info"][1]["tree_structure"]["leaf_value"] == 2.0
