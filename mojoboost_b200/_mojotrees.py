@@ -427,8 +427,13 @@ def num_iterations(model):
     return model.num_iterations
 
 
+def num_trees(model):
+    return model.num_trees
+
+
 n_features_multiclass = n_features
 num_iterations_multiclass = num_iterations
+num_trees_multiclass = num_trees
 
 
 def feature_importance(model, n_features, kind, out_addr):

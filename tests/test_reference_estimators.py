@@ -175,3 +175,14 @@ def test_sparse_input_through_the_estimators(ref, captured_fit, tmp_path):
     fit_est = ref.MojoTreesRegressor(n_estimators=3, device="gpu")
     _fit(fit_est, sp.random(100, 4, density=0.3, format="csc", random_state=0), np.random.default_rng(2).random(100))
     assert "num_iterations=3" in captured_fit["string"]
+
+
+def test_booster_inspection(ref, tmp_path):
+    """The reference Booster's inspection API over a model this library
+    wrote: its own model_to_string parser reads the v4 text."""
+    b = ref.MojoTreesRegressor.load(write(tmp_path, "a.mbst", model_a(4))).booster_
+    assert b.num_trees() == 1 and b.num_feature() == 2 and b.current_iteration() == 1
+    d = b.dump_model()
+    assert d["tree_info"][0]["num_leaves"] == 3
+    df = b.trees_to_dataframe()
+    assert len(df) == 5
