@@ -1189,4 +1189,16 @@ double mt_oracle_pow2_abs_total(const double* v, int64_t n) {
 
 double mt_oracle_exp(double x) { return mt_exp(x); }
 
+// The quantizer primitives the device kernels share (mt_math.h), exposed for
+// the known-answer tests ported from the reference's quantized-gradient tests.
+uint64_t mt_oracle_splitmix64(uint64_t state) { return mt_splitmix64(state); }
+double mt_oracle_uniform(uint64_t counter) { return mt_uniform(counter); }
+uint64_t mt_oracle_quant_stream(long long seed, long long round_index, long long class_index, int plane) {
+  return mt_quant_stream(seed, round_index, class_index, plane);
+}
+long long mt_oracle_quantize_stochastic(double value, double units, double lim, uint64_t counter) {
+  return mt_quantize_stochastic(value, units, lim, counter);
+}
+double mt_oracle_fixed_point_scale(double total) { return (double)mt_fixed_point_scale(total); }
+
 }  // extern "C"

@@ -86,6 +86,17 @@ def lib():
         _lib.mt_oracle_pow2_abs_total.argtypes = [ctypes.c_void_p, ctypes.c_int64]
         _lib.mt_oracle_exp.restype = ctypes.c_double
         _lib.mt_oracle_exp.argtypes = [ctypes.c_double]
+        _lib.mt_oracle_splitmix64.restype = ctypes.c_uint64
+        _lib.mt_oracle_splitmix64.argtypes = [ctypes.c_uint64]
+        _lib.mt_oracle_uniform.restype = ctypes.c_double
+        _lib.mt_oracle_uniform.argtypes = [ctypes.c_uint64]
+        _lib.mt_oracle_quant_stream.restype = ctypes.c_uint64
+        _lib.mt_oracle_quant_stream.argtypes = [ctypes.c_longlong, ctypes.c_longlong, ctypes.c_longlong, ctypes.c_int]
+        _lib.mt_oracle_quantize_stochastic.restype = ctypes.c_longlong
+        _lib.mt_oracle_quantize_stochastic.argtypes = [ctypes.c_double, ctypes.c_double, ctypes.c_double,
+                                                       ctypes.c_uint64]
+        _lib.mt_oracle_fixed_point_scale.restype = ctypes.c_double
+        _lib.mt_oracle_fixed_point_scale.argtypes = [ctypes.c_double]
     return _lib
 
 
