@@ -73,3 +73,22 @@ def test_fixed_point_scale_is_the_largest_power_of_two(q):
     for t in (0.7, 123.456, 9.9e8):
         s = q.mt_oracle_fixed_point_scale(t)
         assert s <= 2.0 ** 30 / t < 2 * s and np.log2(s) == int(np.log2(s))
+
+
+def test_fixed_point_scale_shape(q):
+    """tests/test_fixed_point_scale_shape.mojo procedures: the scaled total
+    stays within 2^30 (half the int32 range), flooring to a power of two costs
+    at most one bit, and both the float32 product g * s and its dequantizing
+    reciprocal are exact."""
+    rng = np.random.default_rng(9)
+    for _ in range(200):
+        g = rng.normal(size=64) * 10.0 ** rng.uniform(-6, 6)
+        total = float(np.sum(np.abs(g)))
+        s = q.mt_oracle_fixed_point_scale(total)
+        assert total * s <= 2.0 ** 30
+        assert total * s > 2.0 ** 29  # at most one bit below the bound
+        g32 = g.astype(np.float32)
+        prod = g32 * np.float32(s)
+        assert np.array_equal(prod.astype(np.float64), g32.astype(np.float64) * s)  # exact product
+        inv = 1.0 / s
+        assert inv * s == 1.0 and np.log2(inv) == int(np.log2(inv))
