@@ -19,7 +19,7 @@ typedef struct {
   char internal[128];
 } nccl_unique_id_t;
 typedef void* nccl_comm_t;
-enum { kNcclSuccess = 0, kNcclInt32 = 2, kNcclUint64 = 5, kNcclFloat64 = 8 };
+enum { kNcclSuccess = 0, kNcclInt8 = 0, kNcclInt32 = 2, kNcclUint64 = 5, kNcclFloat64 = 8 };
 enum { kNcclSum = 0, kNcclMax = 2 };
 
 struct Api {
@@ -29,6 +29,9 @@ struct Api {
   nccl_result_t (*comm_abort)(nccl_comm_t);
   nccl_result_t (*all_reduce)(const void*, void*, size_t, int, int, nccl_comm_t, cudaStream_t);
   nccl_result_t (*all_gather)(const void*, void*, size_t, int, nccl_comm_t, cudaStream_t);
+  nccl_result_t (*reduce_scatter)(const void*, void*, size_t, int, int, nccl_comm_t, cudaStream_t);
+  nccl_result_t (*group_start)();
+  nccl_result_t (*group_end)();
   nccl_result_t (*get_async_error)(nccl_comm_t, nccl_result_t*);
   const char* (*error_string)(nccl_result_t);
 };
@@ -62,6 +65,9 @@ void do_load() {
   g_api.comm_abort = (decltype(g_api.comm_abort))sym("ncclCommAbort");
   g_api.all_reduce = (decltype(g_api.all_reduce))sym("ncclAllReduce");
   g_api.all_gather = (decltype(g_api.all_gather))sym("ncclAllGather");
+  g_api.reduce_scatter = (decltype(g_api.reduce_scatter))sym("ncclReduceScatter");
+  g_api.group_start = (decltype(g_api.group_start))sym("ncclGroupStart");
+  g_api.group_end = (decltype(g_api.group_end))sym("ncclGroupEnd");
   g_api.get_async_error = (decltype(g_api.get_async_error))sym("ncclCommGetAsyncError");
   g_api.error_string = (decltype(g_api.error_string))sym("ncclGetErrorString");
   g_loaded = g_why.empty();
@@ -128,6 +134,24 @@ void Collective::check() {
     comm_ = nullptr;
     ck(e, "asynchronous operation");
   }
+}
+
+void Collective::allgather_bytes(const void* send, void* recv, size_t bytes_per_rank, cudaStream_t st) {
+  ck(g_api.all_gather(send, recv, bytes_per_rank, kNcclInt8, (nccl_comm_t)comm_, st), "ncclAllGather");
+}
+
+void Collective::reduce_scatter_slots_i32(int* base, size_t n_slots, size_t slot_len, size_t chunk, cudaStream_t st) {
+  if (chunk * (size_t)world_ != slot_len) throw std::runtime_error("reduce-scatter: slot length is not world x chunk");
+  ck(g_api.group_start(), "ncclGroupStart");
+  nccl_result_t r = kNcclSuccess;
+  for (size_t i = 0; i < n_slots && r == kNcclSuccess; ++i) {
+    int* slot = base + i * slot_len;
+    // in place: rank r's result lands on its own chunk of the slot
+    r = g_api.reduce_scatter(slot, slot + (size_t)rank_ * chunk, chunk, kNcclInt32, kNcclSum, (nccl_comm_t)comm_, st);
+  }
+  const nccl_result_t e = g_api.group_end();
+  ck(r, "ncclReduceScatter");
+  ck(e, "ncclGroupEnd");
 }
 
 }  // namespace mtb

@@ -34,6 +34,12 @@ class Collective {
   void allreduce_max_u64(unsigned long long* buf, size_t n, cudaStream_t st);
   void allreduce_sum_f64(double* buf, size_t n, cudaStream_t st);
   void allgather_f64(const double* send, double* recv, size_t n_per_rank, cudaStream_t st);
+  void allgather_bytes(const void* send, void* recv, size_t bytes_per_rank, cudaStream_t st);
+  // In place, for each of n_slots slots of slot_len int32 (slots back to
+  // back from `base`): the sum over ranks of this rank's chunk
+  // [rank * chunk, (rank + 1) * chunk) of every slot, slot_len = world * chunk.
+  // One NCCL group.
+  void reduce_scatter_slots_i32(int* base, size_t n_slots, size_t slot_len, size_t chunk, cudaStream_t st);
   // Throws if the communicator reported an asynchronous error (and aborts it).
   void check();
 

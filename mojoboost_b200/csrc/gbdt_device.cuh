@@ -111,6 +111,16 @@ struct FeatBest {
   unsigned long long bits[4];
 };
 
+// Feature-sharded data-parallel exchange: one rank's best split of a child
+// over the features it owns, and the child's totals.
+struct ChildRec {
+  double gain;            // > 0 when found
+  long long n_left;
+  long long tg, th, tc;   // the child's totals (when has_totals)
+  unsigned long long bits[4];
+  int feature, bin, flags, found, has_totals, pad;
+};
+
 struct NodeRec {
   int feature;   // -1 for a leaf
   int thr;       // threshold bin, -1 for categorical and leaves

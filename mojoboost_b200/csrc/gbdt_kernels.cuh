@@ -981,6 +981,61 @@ __device__ void scan_pair_done(TreeState* __restrict__ ts, int c, const FeatBest
 // threshold, and a warp arg-max that keeps the serial scan's tie rule (first
 // maximum in bin order, missing-left candidate before default-right).  Pair
 // p = child * n_active + j, child = 2 * item + side.
+// The feature-sharded exchange's end of a child: the warp that completes
+// child c folds this rank's per-feature bests exactly as scan_pair_done does
+// (ascending active feature, strict >, the first maximum) and writes the
+// result and the child's totals to rec[c]; the leaf itself is written by
+// k_merge_children once every rank's record is gathered.
+__device__ void scan_pair_done_exchange(TreeState* __restrict__ ts, int c, const FeatBest* __restrict__ fbs,
+                                        const int* __restrict__ feats, const ScanParams& sp,
+                                        ChildRec* __restrict__ rec) {
+  const int lane = threadIdx.x & 31;
+  unsigned int last = 0;
+  if (lane == 0) {
+    __threadfence();
+    last = atomicAdd(&ts->child_done[c], 1u) == (unsigned int)(sp.n_active - 1) ? 1u : 0u;
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  __threadfence();
+  const FeatBest* fc = fbs + (long long)c * sp.n_active;
+  double bg = 0.0;
+  int bj = -1;
+  for (int j = lane; j < sp.n_active; j += 32) {
+    const int flags = __ldcg(&fc[j].flags);
+    const double g = __ldcg(&fc[j].gain);
+    if ((flags & 1) && g > bg) {
+      bg = g;
+      bj = j;
+    }
+  }
+  for (int k = 16; k > 0; k >>= 1) {
+    const double og = __shfl_xor_sync(0xffffffffu, bg, k);
+    const int oj = __shfl_xor_sync(0xffffffffu, bj, k);
+    if (oj >= 0 && (bj < 0 || og > bg || (og == bg && oj < bj))) {
+      bg = og;
+      bj = oj;
+    }
+  }
+  if (lane != 0) return;
+  ts->child_done[c] = 0;
+  ChildRec& R = rec[c];
+  R.tg = __ldcg(&ts->totals[c].g);
+  R.th = __ldcg(&ts->totals[c].h);
+  R.tc = __ldcg(&ts->totals[c].c);
+  R.has_totals = 1;
+  R.found = bj >= 0 ? 1 : 0;
+  if (bj >= 0) {
+    const FeatBest* fb = fc + bj;
+    R.gain = __ldcg(&fb->gain);
+    R.feature = feats[bj];
+    R.bin = __ldcg(&fb->bin);
+    R.flags = __ldcg(&fb->flags);
+    R.n_left = __ldcg(&fb->n_left);
+    for (int q = 0; q < 4; ++q) R.bits[q] = __ldcg(&fb->bits[q]);
+  }
+}
+
 // One numerical split candidate (left sums Dg, Dh, Dc): the leaf guards and
 // the gain, exactly the inline arithmetic of k_scan (same operations in the
 // same order; the file is compiled without FMA contraction), or -infinity
@@ -1009,13 +1064,14 @@ __device__ __noinline__ double scan_candidate_gain(long long Dg, long long Dh, l
 constexpr int kScanWarps = 8;    // pairs per block
 constexpr int kBinsPerLane = 8;  // 32 x 8 = 256 bins at most
 
-template <bool COMPACT>
+template <bool COMPACT, bool EXCHANGE>
 __global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan_t(TreeState* __restrict__ ts, int* __restrict__ hist,
                                                           long long slot_cells, const int* __restrict__ feats,
                                                           const int* __restrict__ missing_bin,
                                                           const int* __restrict__ n_cats,
                                                           const RoundScales* __restrict__ sc, ScanParams sp,
-                                                          FeatBest* __restrict__ out, int work_base) {
+                                                          FeatBest* __restrict__ out, int work_base,
+                                                          ChildRec* __restrict__ rec) {
   __shared__ int s_cells[kScanWarps][3][256];  // categorical searches only
   const Batch& Bt = ts->batch;
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
@@ -1191,7 +1247,8 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan_t(TreeState* __rest
       }
       out[(long long)c * sp.n_active + j] = fb;
     }
-    scan_pair_done(ts, c, out, feats, sc, sp);
+    if (EXCHANGE) scan_pair_done_exchange(ts, c, out, feats, sp, rec);
+    else scan_pair_done(ts, c, out, feats, sc, sp);
     return;
   }
   const int mb = missing_bin[f];
@@ -1305,7 +1362,78 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan_t(TreeState* __rest
     }
     out[(long long)c * sp.n_active + j] = fb;
   }
-  scan_pair_done(ts, c, out, feats, sc, sp);
+  if (EXCHANGE) scan_pair_done_exchange(ts, c, out, feats, sp, rec);
+  else scan_pair_done(ts, c, out, feats, sc, sp);
+}
+
+// Feature-sharded exchange: every rank's ChildRec of this iteration, gathered
+// rank-major (all[r * stride + c]).  One thread per child folds the ranks in
+// ascending order with a strict > (ranks own ascending feature blocks, so this
+// keeps the first maximum over all features, the single-device rule), takes
+// the totals from the first rank that has them, and writes the child's leaf
+// exactly as scan_pair_done does.  Every rank runs it on the same gathered
+// records, so every rank holds the same tree.
+__global__ void k_merge_children(TreeState* __restrict__ ts, const ChildRec* __restrict__ all, int world,
+                                 int stride, const RoundScales* __restrict__ sc, ScanParams sp) {
+  const Batch& Bt = ts->batch;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= 2 * Bt.n_items) return;
+  const int item = c >> 1, side = c & 1;
+  const bool root = Bt.root != 0;
+  if (root && side) return;
+  int best = -1, tot = -1;
+  double bg = 0.0;
+  for (int r = 0; r < world; ++r) {
+    const ChildRec& R = all[(long long)r * stride + c];
+    if (tot < 0 && R.has_totals) tot = r;
+    if (R.found && R.gain > bg) {
+      bg = R.gain;
+      best = r;
+    }
+  }
+  if (tot < 0) {  // no rank scanned this child: nothing to build its leaf from
+    ts->hdr.error = 1;
+    ts->hdr.done = 1;
+    return;
+  }
+  const ChildRec& T = all[(long long)tot * stride + c];
+  const BatchItem& P = Bt.items[item];
+  const int leaf = P.child[side];
+  LeafRec& L = ts->pool[leaf];
+  const long long tg = T.tg, th = T.th, n_rows = T.tc;
+  SplitRec sr;
+  clear_split(sr);
+  if (best >= 0 && !(n_rows < 2 * (long long)sp.min_data_in_leaf || n_rows < 2)) {
+    const ChildRec& R = all[(long long)best * stride + c];
+    sr.found = 1;
+    sr.gain = R.gain;
+    sr.feature = R.feature;
+    sr.bin = R.bin;
+    sr.default_left = (R.flags & 2) ? 1 : 0;
+    sr.is_cat = (R.flags & 4) ? 1 : 0;
+    sr.n_left = R.n_left;
+    for (int q = 0; q < 4; ++q) sr.bits[q] = R.bits[q];
+  }
+  L.split = sr;
+  const double gd = sp.mode == MODE_FIXED ? (double)tg * sc->g_inv : (double)tg / sc->g_units;
+  const double hd = sp.mode == MODE_FIXED ? (double)th * sc->h_inv : (double)th / sc->h_units;
+  L.value = -soft_l1(gd, sp.lambda_l1) / (hd + sp.lambda_l2);
+  L.gcount = n_rows;
+  LeafInfo& I = ts->info[leaf];
+  I.gain = (sr.found && sr.gain > 0.0) ? sr.gain : -1.0;
+  I.child[0] = I.child[1] = -1;
+  I.expanded = 0;
+  I.pad = 0;
+  if (root) {
+    NodeRec& nd = ts->nodes[L.node];
+    nd.value = L.value;
+    nd.count = n_rows;
+  } else {
+    const long long nl = (long long)P.cursor_left;
+    L.begin = side == 0 ? P.begin : P.begin + nl;
+    L.count = side == 0 ? nl : P.count - nl;
+    ts->info[P.leaf].child[side] = leaf;
+  }
 }
 
 // ---------------------------------------------------------------------------

@@ -328,7 +328,15 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   d_sc.alloc(1);
   DevBuf<TreeState> d_ts;
   d_ts.alloc(1);
-  const long long slot_cells = (long long)F * 3 * B;
+  // Data-parallel histogram exchange.  Default: all-reduce of the batch's
+  // work slots, every rank scanning every feature.  MOJOTREES_DP_EXCHANGE=
+  // feature: each rank owns a block of Fb feature ids; the work slots are
+  // reduce-scattered by those blocks, each rank scans its own active
+  // features, and the per-child bests are all-gathered and merged.
+  const char* dpx = getenv("MOJOTREES_DP_EXCHANGE");
+  const bool dp_feature = coll && world > 1 && dpx && std::string(dpx) == "feature";
+  const int Fb = dp_feature ? (F + world - 1) / world : F;  // feature ids a rank owns
+  const long long slot_cells = (long long)(dp_feature ? Fb * world : F) * 3 * B;
   // Leaves expanded per iteration (speculative leaf batching); 1 grows one
   // split per iteration as the reference does.  MOJOTREES_BATCH overrides.
   int batch_cap = 32;
@@ -457,9 +465,17 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   };
   // the built children's cells summed over every device's rows (exact int32)
   auto reduce_work = [&]() {
-    if (coll)
+    if (dp_feature)
+      coll->reduce_scatter_slots_i32(d_hist.p + (size_t)work_base * slot_cells, (size_t)batch_cap,
+                                     (size_t)slot_cells, (size_t)Fb * 3 * B, st);
+    else if (coll)
       coll->allreduce_sum_i32(d_hist.p + (size_t)work_base * slot_cells, (size_t)slot_cells * batch_cap, st);
   };
+  DevBuf<ChildRec> d_rec, d_rec_all;
+  if (dp_feature) {
+    d_rec.alloc(2 * (size_t)kMaxBatch);
+    d_rec_all.alloc(2 * (size_t)kMaxBatch * world);
+  }
 
   const long long grid1024 = (N + 1023) / 1024;
   const unsigned grid256 = (unsigned)((N + 255) / 256);
@@ -570,8 +586,15 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
           }
         }
       }
+      if (dp_feature) {  // this rank scans the active features of its own block
+        std::vector<int> own;
+        for (int f : feats)
+          if (f / Fb == coll->rank()) own.push_back(f);
+        feats.swap(own);
+      }
       const int n_active = (int)feats.size();
-      MTB_CUDA(cudaMemcpyAsync(d_feats.p, feats.data(), sizeof(int) * n_active, cudaMemcpyHostToDevice, st));
+      if (n_active > 0)
+        MTB_CUDA(cudaMemcpyAsync(d_feats.p, feats.data(), sizeof(int) * n_active, cudaMemcpyHostToDevice, st));
       sp.n_active = n_active;
       const unsigned scan_grid = (unsigned)((2ll * batch_cap * n_active + kScanWarps - 1) / kScanWarps);
 
@@ -595,8 +618,21 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
         hist();
         reduce_work();
         timer.begin(&stats.scan_ms);
-        (scan_compact ? k_scan_t<true> : k_scan_t<false>)<<<scan_grid, kScanWarps * 32, 0, st>>>(
-            d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p, d_ncats.p, d_sc.p, sp, d_fb.p, work_base);
+        if (!dp_feature) {
+          (scan_compact ? k_scan_t<true, false> : k_scan_t<false, false>)<<<scan_grid, kScanWarps * 32, 0, st>>>(
+              d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p, d_ncats.p, d_sc.p, sp, d_fb.p, work_base,
+              nullptr);
+        } else {
+          // this rank's per-child bests -> every rank's -> the merged leaves
+          MTB_CUDA(cudaMemsetAsync(d_rec.p, 0, sizeof(ChildRec) * 2 * (size_t)batch_cap, st));
+          if (n_active > 0)
+            (scan_compact ? k_scan_t<true, true> : k_scan_t<false, true>)<<<scan_grid, kScanWarps * 32, 0, st>>>(
+                d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p, d_ncats.p, d_sc.p, sp, d_fb.p, work_base,
+                d_rec.p);
+          coll->allgather_bytes(d_rec.p, d_rec_all.p, sizeof(ChildRec) * 2 * (size_t)batch_cap, st);
+          k_merge_children<<<1, 2 * kMaxBatch, 0, st>>>(d_ts.p, d_rec_all.p, world, 2 * batch_cap, d_sc.p, sp);
+          launches += 1;
+        }
         timer.end();
         timer.begin(&stats.commit_ms);
         k_commit<<<1, kCommitThreads, commit_smem, st>>>(d_ts.p, d_missing.p, cp, commit_cap, d_done,

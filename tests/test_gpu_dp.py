@@ -35,9 +35,11 @@ def _data(quant, n_shard=N_SHARD):
     return bins, y, params
 
 
-def _rank_main(rank, world, port, quant, n_shard, out_q):
+def _rank_main(rank, world, port, quant, n_shard, out_q, exchange="allreduce", extra=None):
     import torch.distributed as dist
 
+    if exchange == "feature":
+        os.environ["MOJOTREES_DP_EXCHANGE"] = "feature"
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
@@ -46,7 +48,7 @@ def _rank_main(rank, world, port, quant, n_shard, out_q):
         import mojoboost_b200 as mb
 
         bins, y, params = _data(quant, n_shard)
-        params = dict(params, gpu_device_id=rank)
+        params = dict(params, gpu_device_id=rank, **(extra or {}))
         nid = torch.from_numpy(mb.nccl_unique_id() if rank == 0 else np.zeros(128, np.uint8))
         dist.broadcast(nid, 0)
         lo, hi = rank * n_shard, (rank + 1) * n_shard
@@ -57,18 +59,27 @@ def _rank_main(rank, world, port, quant, n_shard, out_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("quant,n_shard", [(True, N_SHARD), (False, N_SHARD), (True, N_SHARD_RAGGED)])
-def test_two_gpu_fit_equals_single_gpu(mtlib, quant, n_shard):
+# exchange "allreduce" (the default) sums every work slot on every rank;
+# "feature" reduce-scatters them by feature block and merges per-child bests
+# (MOJOTREES_DP_EXCHANGE=feature).  feature_fraction 0.25 leaves some trees
+# with no active feature in one rank's block.
+@pytest.mark.parametrize("quant,n_shard,exchange,extra", [
+    (True, N_SHARD, "allreduce", None), (False, N_SHARD, "allreduce", None), (True, N_SHARD_RAGGED, "allreduce", None),
+    (True, N_SHARD, "feature", None), (False, N_SHARD, "feature", None), (True, N_SHARD_RAGGED, "feature", None),
+    (True, N_SHARD, "feature", {"feature_fraction": 0.25}),
+])
+def test_two_gpu_fit_equals_single_gpu(mtlib, quant, n_shard, exchange, extra):
     import torch.multiprocessing as mp
 
     bins, y, params = _data(quant, n_shard)
-    single = mtlib.train_binned(bins, 63, y, dict(params, gpu_device_id=0))
+    single = mtlib.train_binned(bins, 63, y, dict(params, gpu_device_id=0, **(extra or {})))
     ref = [single.tree(t) for t in range(single.num_trees)]
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, quant, n_shard, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, quant, n_shard, q, exchange, extra))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=300) for _ in range(world))
