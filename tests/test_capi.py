@@ -149,3 +149,32 @@ def test_bin_dense_reports_bad_categorical_code(mtlib):
     X[7, 1] = 3e9
     with pytest.raises(mtlib.MojoTreesError):
         mtlib.bin_dense(X, {"categorical_feature": "1"})
+
+
+def test_extension_argument_checks(mtlib, tmp_path):
+    """The host-side extensions refuse bad arguments with a status, never a
+    crash: null pointers, short buffers, out-of-range iterations, a model
+    without a raw-value mapper."""
+    from test_model_io import X_A, model_a, write
+    lib = mtlib.lib()
+    m = mtlib.Model.load(write(tmp_path, "a.mbst", model_a(4)))
+    e = lib.mojotrees_error_create()
+    X = np.asfortranarray(X_A)
+    out = np.zeros(1)
+    try:
+        assert lib.mojotrees_b200_predict_leaf(m.h, X.ctypes.data, len(X), 2, 0, 0, out.ctypes.data, 1, e) == -1
+        assert lib.mojotrees_b200_predict_leaf(m.h, X.ctypes.data, len(X), 3, 0, 0, out.ctypes.data, 99, e) == -1
+        assert lib.mojotrees_b200_model_bin(m.h, None, 5, 2, None, 10, e) == -1
+        raw = np.zeros(len(X))
+        bins = m.bin_rows(X)
+        assert lib.mojotrees_b200_add_iteration_raw(m.h, bins.ctypes.data, len(X), 2, 1, raw.ctypes.data, raw.size,
+                                                    e) == -1  # iteration 1 of a 1-iteration model
+        assert lib.mojotrees_b200_add_iteration_raw(m.h, bins.ctypes.data, len(X), 2, 0, raw.ctypes.data, 3, e) == -1
+        h = ctypes.c_void_p()
+        assert lib.mojotrees_b200_model_prefix(m.h, 2, ctypes.byref(h), e) == -1
+        assert lib.mojotrees_b200_model_prefix(m.h, -1, ctypes.byref(h), e) == -1
+        assert lib.mojotrees_b200_ingest_column_major(None, None, -1, 2, None, e) == -1
+        assert lib.mojotrees_b200_buffer_has_infinite(None, 4, None, e) == -1
+        assert lib.mojotrees_b200_model_categorical(m.h, out.ctypes.data, 1, e) == -1  # 2 features, room for 1
+    finally:
+        lib.mojotrees_error_free(e)
