@@ -278,7 +278,8 @@ def run_gpu(args):
         "data": "synthetic",
         "config": {"workload": "configs[1]: binary logistic, quantized int8 gradients, 10M x 100 per GPU, "
                                "max_bin 255, num_leaves 255", "rows_per_gpu": N_ROWS, "features": N_FEAT,
-                   "l2": "inputs (1.1 GB row-major bins) larger than L2; no flush", "parallelism": f"dp{world}"},
+                   "l2": "inputs (1.1 GB row-major bins) larger than L2; no flush", "parallelism": f"dp{world}",
+                   **({"dp_exchange": os.environ.get("MOJOTREES_DP_EXCHANGE", "allreduce")} if world > 1 else {})},
         "roofline": {"bound": "hbm", "achieved": hist_gbs, "peak": peak, "unit": "GB/s",
                      "frac": (hist_gbs / peak) if hist_gbs else None,
                      "traffic": (HIST_DRAM_BYTES_PER_ROW * hist_rows / hist_launches) if hist_launches else None,
