@@ -307,6 +307,96 @@ def predict_proba_csr(model, params, out_addr):
     _predict_csr(model, params, out_addr, bool(int(params.get("raw_score", 0))))
 
 
+# ---- the LightGBM-style Dataset / train API (python/mojotrees/basic.py over
+# bindings/_mojotrees.mojo:4993-5310, dataset_bindings.mojo:263) ------------
+
+class _Dataset:
+    """A constructed training set: a copy of the column-major float64 matrix,
+    the label and the binning parameters.  Binning itself happens in the
+    device fit, from the same parameters, so the trees are those a fit of the
+    matrix grows."""
+
+    def __init__(self, X, label, max_bin, use_missing, categorical, names):
+        self.X, self.label = X, label
+        self.max_bin, self.use_missing = int(max_bin), int(use_missing)
+        self.categorical, self.names = list(categorical), list(names)
+
+    @property
+    def n_rows(self):
+        return self.X.shape[0]
+
+    @property
+    def n_features(self):
+        return self.X.shape[1]
+
+
+def dataset_create(x_addr, n_rows, n_features, params):
+    n, f = int(n_rows), int(n_features)
+    for key, what in (("weight_addr", "sample weights"), ("init_score_addr", "init scores"),
+                      ("group_addr", "query groups")):
+        if int(params.get(key, 0) or 0):
+            raise NotImplementedError(f"a Dataset with {what} is not covered by the B200 device path")
+    if str(params.get("ctr", "off")).lower() != "off":
+        raise NotImplementedError("ctr: CatBoost target statistics are not covered by the B200 device path")
+    X = _f64(int(x_addr), n * f).reshape(f, n).T.copy(order="F")  # column-major, owned
+    label = _f64(int(params["label_addr"]), n).copy() if int(params.get("label_addr", 0) or 0) else None
+    cats = []
+    if params.get("categorical_addr") and params.get("categorical_len"):
+        cats = [int(c) for c in _f64(int(params["categorical_addr"]), int(params["categorical_len"]))]
+    names = [str(x) for x in (params.get("feature_names") or [])][: int(params.get("n_names", 0) or 0)]
+    return _Dataset(X, label, params.get("max_bin", 255), params.get("use_missing", 1), cats, names)
+
+
+def dataset_metadata(dataset):
+    d = dataset
+    return {"num_data": d.n_rows, "num_feature": d.n_features, "num_bin": d.max_bin, "max_bin": d.max_bin,
+            "is_sparse": False, "nnz": d.n_rows * d.n_features, "has_raw": False, "use_missing": d.use_missing,
+            "n_groups": 0, "n_categorical": len(d.categorical), "has_names": bool(d.names),
+            "n_label": 0 if d.label is None else d.n_rows, "n_weight": 0, "n_init_score": 0}
+
+
+def dataset_num_data(dataset):
+    return dataset.n_rows
+
+
+def dataset_num_feature(dataset):
+    return dataset.n_features
+
+
+def dataset_feature_names(dataset):
+    return list(dataset.names)
+
+
+def dataset_categorical_features(dataset):
+    return list(dataset.categorical)
+
+
+def _dataset_fit(dataset, params, multiclass):
+    if dataset.label is None:
+        raise ValueError("the Dataset has no label to train on")
+    p = dict(params)
+    objective = int(p.pop("objective", 0))
+    n_classes = int(p.pop("n_classes", 0) or 0)
+    for k in ("categorical_addr", "categorical_len"):
+        p.pop(k, None)
+    p["max_bin"], p["use_missing"] = dataset.max_bin, dataset.use_missing
+    if dataset.categorical:
+        p["categorical_features"] = dataset.categorical
+    X, y = dataset.X, np.ascontiguousarray(dataset.label)
+    if multiclass:
+        return fit_multiclass(X.ctypes.data, dataset.n_rows, dataset.n_features, y.ctypes.data, n_classes, p)
+    return fit(X.ctypes.data, dataset.n_rows, dataset.n_features, y.ctypes.data, objective, p)
+
+
+def train_dataset(dataset, params):
+    """A single-output fit on a constructed Dataset (bindings/_mojotrees.mojo:5122)."""
+    return _dataset_fit(dataset, params, False)
+
+
+def train_dataset_multiclass(dataset, params):
+    return _dataset_fit(dataset, params, True)
+
+
 def resolve_device(device, n_rows=0, n_features=0, n_outputs=1):
     """`gpu` when a CUDA device is present; an explicit `gpu` request without
     one raises instead of falling back (capi/mojotrees.h:99-106)."""

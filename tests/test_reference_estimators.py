@@ -186,3 +186,59 @@ def test_booster_inspection(ref, tmp_path):
     assert d["tree_info"][0]["num_leaves"] == 3
     df = b.trees_to_dataframe()
     assert len(df) == 5
+
+
+@pytest.fixture()
+def captured_dataset_fit(ref, monkeypatch, tmp_path):
+    """`_mojotrees.fit` / `fit_multiclass` as the Dataset route reaches them:
+    the parameter string and matrix are recorded and a model file stands in
+    for the device fit."""
+    from mojoboost_b200 import _mojotrees as shim
+    cap = {}
+    path = write(tmp_path, "a.mbst", model_a(4))
+    param_string = shim.param_string
+
+    def fake(x, n, f, y, objective, params):
+        cap["string"] = param_string(objective, params).decode()
+        cap["X"] = shim._f64(x, n * f).reshape(f, n).T.copy()
+        cap["y"] = shim._f64(y, n).copy()
+        return shim.load(path)
+
+    def fake_mc(x, n, f, y, k, params):
+        return fake(x, n, f, y, shim.MULTICLASS, dict(params, num_class=k))
+
+    monkeypatch.setattr(shim, "fit", fake)
+    monkeypatch.setattr(shim, "fit_multiclass", fake_mc)
+    monkeypatch.setattr(shim, "resolve_device", lambda *a, **k: "gpu")
+    return cap
+
+
+def test_lightgbm_style_train_over_the_shim(ref, captured_dataset_fit):
+    """mojotrees.train(params, Dataset(X, label)) builds the device fit's
+    parameters from the params dict and the Dataset's binning, hands over the
+    matrix and label unchanged, and the Booster it returns predicts."""
+    rng = np.random.default_rng(3)
+    X, y = rng.normal(size=(400, 2)), rng.normal(size=400)
+    bst = ref.train({"objective": "regression", "device": "gpu", "num_leaves": 7},
+                    ref.Dataset(X, label=y, params={"max_bin": 63}), num_boost_round=3)
+    s = captured_dataset_fit["string"]
+    assert "objective=regression" in s and "num_iterations=3" in s and "num_leaves=7" in s and "max_bin=63" in s
+    np.testing.assert_array_equal(captured_dataset_fit["X"], X)
+    np.testing.assert_array_equal(captured_dataset_fit["y"], y)
+    np.testing.assert_array_equal(bst.predict(X_A), RAW_A)
+
+
+def test_lightgbm_style_train_multiclass_and_refusals(ref, captured_dataset_fit):
+    rng = np.random.default_rng(4)
+    X, y = rng.normal(size=(300, 2)), rng.integers(0, 3, 300).astype(float)
+    try:
+        ref.train({"objective": "multiclass", "num_class": 3, "device": "gpu"}, ref.Dataset(X, label=y),
+                  num_boost_round=2)
+    except Exception:
+        pass  # the stand-in model is single-output; only the parameters matter here
+    assert "objective=multiclass" in captured_dataset_fit["string"]
+    assert "num_class=3" in captured_dataset_fit["string"]
+    with pytest.raises(Exception) as ei:
+        ref.train({"objective": "regression", "device": "gpu"},
+                  ref.Dataset(X, label=y, weight=np.ones(300)), num_boost_round=2)
+    assert "weight" in str(ei.value)
