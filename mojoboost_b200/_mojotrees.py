@@ -663,6 +663,32 @@ def load(path):
 load_multiclass = load
 
 
+def model_file_kind(path):
+    """Which loader a saved model needs, "objective" or "multiclass", from
+    the file header (serialize.mojo:1408-1428)."""
+    with open(path) as f:
+        tok = f.read(1 << 20).split()
+    if tok and tok[0] == "mojotrees-dataset":
+        raise ValueError("this is a prepared dataset file, not a model; read it with load_dataset")
+    if len(tok) < 2 or tok[0] != "mojotrees" or tok[1] not in ("v1", "v2", "v3", "v4", "v5"):
+        raise ValueError("not a mojotrees model file")
+    i = 2
+    if i < len(tok) and tok[i] == "feature_names":
+        i += 2 + int(tok[i + 1])
+    kind = tok[i] if i < len(tok) else ""
+    if kind not in ("objective", "multiclass"):
+        raise ValueError("corrupt model file: unknown model kind")
+    return kind
+
+
+def file_kind(path):
+    with open(path) as f:
+        head = f.read(64).split()
+    if head and head[0] == "mojotrees-dataset":
+        return "dataset"
+    return model_file_kind(path)
+
+
 def model_feature_names(path):
     """The names a model file carries (serialize.mojo:1448), or []."""
     with open(path) as f:

@@ -242,3 +242,19 @@ def test_lightgbm_style_train_multiclass_and_refusals(ref, captured_dataset_fit)
         ref.train({"objective": "regression", "device": "gpu"},
                   ref.Dataset(X, label=y, weight=np.ones(300)), num_boost_round=2)
     assert "weight" in str(ei.value)
+
+
+def test_booster_save_and_reload(ref, captured_dataset_fit, tmp_path):
+    rng = np.random.default_rng(5)
+    X, y = rng.normal(size=(200, 2)), rng.normal(size=200)
+    bst = ref.train({"objective": "regression", "device": "gpu"}, ref.Dataset(X, label=y), num_boost_round=2)
+    out = str(tmp_path / "saved.mbst")
+    bst.save_model(out)
+    back = ref.Booster(model_file=out)
+    np.testing.assert_array_equal(back.predict(X_A), RAW_A)
+    from mojoboost_b200 import _mojotrees as shim
+    assert shim.model_file_kind(out) == "objective"
+    mc = out.replace("saved", "mc")
+    with open(mc, "w") as f:
+        f.write("mojotrees v4\nfeature_names 2\na b \nmulticlass 3\n")
+    assert shim.model_file_kind(mc) == "multiclass"
