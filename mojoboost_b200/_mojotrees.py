@@ -374,6 +374,17 @@ def dataset_categorical_features(dataset):
 def _dataset_fit(dataset, params, multiclass):
     if dataset.label is None:
         raise ValueError("the Dataset has no label to train on")
+    model = _dataset_fit_once(dataset, params, multiclass)
+    # what booster_update needs to continue this fit exactly
+    model._continue = (dataset, multiclass, _without_rounds(params))
+    return model
+
+
+def _without_rounds(params):
+    return {k: v for k, v in params.items() if k != "n_estimators"}
+
+
+def _dataset_fit_once(dataset, params, multiclass):
     p = dict(params)
     objective = int(p.pop("objective", 0))
     n_classes = int(p.pop("n_classes", 0) or 0)
@@ -386,6 +397,137 @@ def _dataset_fit(dataset, params, multiclass):
     if multiclass:
         return fit_multiclass(X.ctypes.data, dataset.n_rows, dataset.n_features, y.ctypes.data, n_classes, p)
     return fit(X.ctypes.data, dataset.n_rows, dataset.n_features, y.ctypes.data, objective, p)
+
+
+def _booster_update(model, dataset, params, multiclass):
+    """Append params["n_estimators"] more rounds to a model trained on
+    `dataset` through train_dataset, returning how many were added
+    (bindings/_mojotrees.mojo:5406-5560).  The reference continues from the
+    existing trees; training here is deterministic and no round depends on a
+    later one, so a fresh fit of (current + n) rounds holds the same first
+    rounds and is that continued model.  Exact only when nothing but the
+    round count changed, so any other change is refused."""
+    state = getattr(model, "_continue", None)
+    if state is None or state[0] is not dataset or state[1] != multiclass:
+        raise NotImplementedError("continued training needs a model trained on this Dataset through "
+                                  "mojotrees.train() with the B200 library")
+    if _without_rounds(params) != state[2]:
+        raise NotImplementedError("continued training with changed parameters is not covered by the B200 "
+                                  "device path (only the round count may change)")
+    before = model.num_iterations
+    grown = _dataset_fit_once(dataset, dict(params, n_estimators=before + int(params["n_estimators"])),
+                              multiclass)
+    model.h, grown.h = grown.h, model.h  # the booster's handle now holds the longer model
+    return model.num_iterations - before
+
+
+def booster_update(model, dataset, params):
+    return _booster_update(model, dataset, params, False)
+
+
+def booster_update_multiclass(model, dataset, params):
+    return _booster_update(model, dataset, params, True)
+
+
+# ---- built-in metrics (bindings/_mojotrees.mojo:3168-3270, metrics.mojo) ----
+
+def _seq_sum(terms):
+    """Left-to-right double sum, the reference metrics' accumulation order."""
+    return float(np.cumsum(terms)[-1]) if len(terms) else 0.0
+
+
+def _metric_weight(weight, n):
+    """check_metric_weight (metrics.mojo:112-130): the weight total."""
+    if weight is None:
+        return float(n)
+    if not np.all(np.isfinite(weight)) or np.any(weight < 0.0):
+        raise ValueError("weights must be finite and nonnegative")
+    total = _seq_sum(weight)
+    if total <= 0.0:
+        raise ValueError("weights must have a positive sum")
+    return total
+
+
+def _sigmoid(x):
+    """boosting.mojo:261-268, the sign-split logistic."""
+    out = np.empty_like(x)
+    pos = x >= 0.0
+    out[pos] = 1.0 / (1.0 + np.exp(-x[pos]))
+    e = np.exp(x[~pos])
+    out[~pos] = e / (1.0 + e)
+    return out
+
+
+def _clamp(p):
+    return np.minimum(np.maximum(p, 1e-15), 1.0 - 1e-15)
+
+
+def eval_metric(code, params):
+    """One built-in metric over the caller's raw predictions, after the
+    objective's link (bindings/_mojotrees.mojo:3168): l2, rmse, l1,
+    binary_logloss, binary_error, auc, multi_logloss and multi_error, the
+    metrics of the objectives this library trains.  Sums run left to right
+    as metrics.mojo's loops do; log and exp are the platform's."""
+    code = int(code)
+    n = int(params["n_rows"])
+    if n <= 0:
+        raise ValueError("metrics need at least one row")
+    w_addr = int(params.get("weight_addr", 0) or 0)
+    weight = _f64(w_addr, n).copy() if w_addr else None
+    total_w = _metric_weight(weight, n)
+    w = np.ones(n) if weight is None else weight
+    y = _f64(int(params["y_addr"]), n).copy()
+    if code in (8, 9):  # multi_logloss, multi_error
+        k = int(params["n_classes"])
+        raw = _f64(int(params["pred_addr"]), n * k).reshape(n, k).copy()
+        labels = y.astype(np.int64)
+        if np.any(labels < 0) or np.any(labels >= k):
+            raise ValueError("label out of range")
+        # _softmax_inplace (boosting.mojo:3515): max, exp, sequential total
+        e = np.exp(raw - raw.max(axis=1, keepdims=True))
+        tot = np.cumsum(e, axis=1)[:, -1:]
+        prob = e / tot
+        if code == 8:
+            return _seq_sum(-(w * np.log(_clamp(prob[np.arange(n), labels])))) / total_w
+        correct = np.where(np.argmax(prob, axis=1) == labels, w, 0.0)
+        return 1.0 - _seq_sum(correct) / total_w
+    raw = _f64(int(params["pred_addr"]), n).copy()
+    objective = int(params.get("objective", 0))
+    pred = _sigmoid(raw) if objective == BINARY_LOGISTIC else raw  # response_scale
+    if code in (0, 1):  # l2, rmse
+        d = pred - y
+        v = _seq_sum((w * d) * d) / total_w
+        return float(np.sqrt(v)) if code == 1 else v
+    if code == 2:  # l1
+        return _seq_sum(w * np.abs(pred - y)) / total_w
+    if code == 5:  # binary_logloss
+        p = _clamp(pred)
+        return _seq_sum(-(w * np.where(y > 0.5, np.log(p), np.log(1.0 - p)))) / total_w
+    if code == 6:  # binary_error: 1 - accuracy at threshold 0.5
+        predicted = np.where(pred >= 0.5, 1.0, 0.0)
+        return 1.0 - _seq_sum(np.where(np.abs(predicted - y) < 0.5, w, 0.0)) / total_w
+    if code == 7:  # auc (metrics.mojo binary_auc): stable ascending order, tie blocks
+        pos = y > 0.5
+        w_pos, w_neg = _seq_sum(np.where(pos, w, 0.0)), _seq_sum(np.where(pos, 0.0, w))
+        if w_pos <= 0.0 or w_neg <= 0.0:
+            raise ValueError("AUC needs at least one positive and one negative")
+        order = np.argsort(pred, kind="stable")
+        seen_neg, total, i = 0.0, 0.0, 0
+        while i < n:
+            j = i
+            while j + 1 < n and pred[order[j + 1]] == pred[order[i]]:
+                j += 1
+            block_pos = block_neg = 0.0
+            for t in range(i, j + 1):
+                if pos[order[t]]:
+                    block_pos += w[order[t]]
+                else:
+                    block_neg += w[order[t]]
+            total += block_pos * (seen_neg + 0.5 * block_neg)
+            seen_neg += block_neg
+            i = j + 1
+        return total / (w_pos * w_neg)
+    raise NotImplementedError(f"metric code {code} is not covered by the B200 library's metrics")
 
 
 def train_dataset(dataset, params):

@@ -258,3 +258,32 @@ def test_booster_save_and_reload(ref, captured_dataset_fit, tmp_path):
     with open(mc, "w") as f:
         f.write("mojotrees v4\nfeature_names 2\na b \nmulticlass 3\n")
     assert shim.model_file_kind(mc) == "multiclass"
+
+
+def test_cv_over_the_shim(ref, monkeypatch, tmp_path):
+    """mojotrees.cv: folds of the Dataset trained through train_dataset and
+    grown one round at a time through booster_update (a fresh fit of the
+    longer run, exact because no round depends on a later one), scored with
+    eval_metric.  Stand-in fits return models of the requested length."""
+    import re
+    from mojoboost_b200 import _mojotrees as shim
+    from test_fit_with_metrics import model_text
+    lengths = []
+
+    def fake(x, n, f, y, objective, params):
+        k = int(re.search(r"num_iterations=(\d+)", shim.param_string(objective, params).decode()).group(1))
+        lengths.append(k)
+        return shim.load(write(tmp_path, f"m{k}.mbst", model_text(k)))
+
+    monkeypatch.setattr(shim, "fit", fake)
+    monkeypatch.setattr(shim, "resolve_device", lambda *a, **k: "gpu")
+    rng = np.random.default_rng(7)
+    X, y = rng.normal(size=(300, 2)), rng.normal(size=300)
+    res = ref.cv({"objective": "regression", "device": "gpu"}, ref.Dataset(X, label=y), num_boost_round=3, nfold=3)
+    assert len(res["valid l2-mean"]) == 3 and all(np.isfinite(res["valid l2-mean"]))
+    assert lengths == [0, 0, 0, 1, 1, 1, 2, 2, 2, 3, 3, 3]
+    # continuing with changed parameters is refused, not trained as something else
+    ds = ref.Dataset(X, label=y)
+    bst = ref.train({"objective": "regression", "device": "gpu"}, ds, num_boost_round=1)
+    with pytest.raises(NotImplementedError):
+        shim.booster_update(bst._handle, ds._constructed(), {"n_estimators": 1, "learning_rate": 0.5})

@@ -149,3 +149,46 @@ def test_empty_range_response(shim, tmp_path):
     assert np.all(out == 0.5)
     _, out = _predict(shim, m, X_A, stop=0, raw_score=1)
     assert np.all(out == 0.25)
+
+
+def _metric(shim, code, pred, y, objective=0, weight=None, n_classes=0):
+    pred = np.ascontiguousarray(pred, dtype=np.float64)
+    y = np.ascontiguousarray(y, dtype=np.float64)
+    w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float64)
+    return shim.eval_metric(code, {"pred_addr": pred.ctypes.data, "y_addr": y.ctypes.data, "n_rows": len(y),
+                                   "weight_addr": 0 if w is None else w.ctypes.data, "objective": objective,
+                                   "n_classes": n_classes, "alpha": 0.9})
+
+
+def test_eval_metric_values(shim):
+    """metrics.mojo's definitions on small hand-worked cases."""
+    import math
+    pred, y = [1.0, 2.0, 4.0], [1.0, 3.0, 2.0]
+    assert _metric(shim, 0, pred, y) == (0.0 + 1.0 + 4.0) / 3                      # l2
+    assert _metric(shim, 1, pred, y) == math.sqrt(5.0 / 3)                         # rmse
+    assert _metric(shim, 2, pred, y) == (0.0 + 1.0 + 2.0) / 3                      # l1
+    assert _metric(shim, 0, pred, y, weight=[1.0, 0.0, 2.0]) == (0.0 + 0.0 + 2.0 * 4.0) / 3.0
+    raw, lab = [0.0, 2.0, -1.0, 3.0], [1.0, 0.0, 0.0, 1.0]
+    p = [0.5, 1 / (1 + math.exp(-2.0)), math.exp(-1.0) / (1 + math.exp(-1.0)), 1 / (1 + math.exp(-3.0))]
+    want = -(math.log(p[0]) + math.log(1 - p[1]) + math.log(1 - p[2]) + math.log(p[3])) / 4
+    assert abs(_metric(shim, 5, raw, lab, objective=1) - want) < 1e-15               # binary_logloss
+    assert _metric(shim, 6, raw, lab, objective=1) == 0.25                         # binary_error: row 1 wrong
+    # multiclass: 2 rows x 3 classes of raw scores
+    mraw = [0.0, 1.0, 2.0, 3.0, 0.0, 0.0]
+    e0 = np.exp(np.array([0.0, 1.0, 2.0]) - 2.0)
+    e1 = np.exp(np.array([3.0, 0.0, 0.0]) - 3.0)
+    want = -(math.log(e0[1] / e0.sum()) + math.log(e1[0] / e1.sum())) / 2
+    assert abs(_metric(shim, 8, mraw, [1.0, 0.0], n_classes=3) - want) < 1e-15     # multi_logloss
+    assert _metric(shim, 9, mraw, [1.0, 0.0], n_classes=3) == 0.5                   # multi_error
+
+
+def test_eval_metric_auc_matches_sklearn(shim):
+    metrics = pytest.importorskip("sklearn.metrics")
+    rng = np.random.default_rng(6)
+    s = np.round(rng.normal(size=500), 1)  # many ties
+    y = (rng.random(500) < 0.4).astype(float)
+    w = rng.random(500)
+    assert abs(_metric(shim, 7, s, y) - metrics.roc_auc_score(y, s)) < 1e-12
+    assert abs(_metric(shim, 7, s, y, weight=w) - metrics.roc_auc_score(y, s, sample_weight=w)) < 1e-12
+    with pytest.raises(NotImplementedError):
+        _metric(shim, 10, s, y)
