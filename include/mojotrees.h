@@ -276,22 +276,27 @@ int32_t mojotrees_b200_histogram_u8(const uint8_t *bins, int64_t n_rows, int64_t
                                     MojoTreesError *error);
 
 /* The histogram of mojotrees_b200_histogram_u8 for callers that cannot
- * allocate GPU memory: code running while a CUDA graph is captured, callers
- * whose own pool allocator owns the device memory, latency-critical paths that
+ * allocate GPU memory: callers whose own pool allocator owns the device
+ * memory and forbids others from taking any, and latency-critical paths that
  * must not take the allocator's locks.  It has no counterpart in the
  * reference.  Everything is device memory the caller owns: bins_rm is
  * row-major uint8 with a row stride of n_features rounded up to 16 bytes,
  * rows holds n_sel row ids, pairs holds n_sel packed gradients (low byte the
  * int8 gradient, high byte the hessian, in the order of rows), out_hist
  * receives n_features * 3 * n_bins int32 as in mojotrees_b200_histogram_u8.
+ * Preconditions the call cannot check (the data is on the device): every
+ * rows[i] is in [0, n_rows), every bin is below n_bins, and with
+ * q = num_grad_quant_bins every gradient is in [-q/2, q/2] and every hessian
+ * in [0, q]; values outside these ranges read out of bounds or carry into
+ * neighbouring packed counters.
  * The work runs on `stream` (a cudaStream_t; NULL = the legacy stream).
  * The library keeps the job descriptor and the accumulation cells in one
  * fixed device array (about 385 KB, held by every GPU that loads the library
  * until exit), so n_features * n_bins may not exceed 128 * 256; larger
  * requests return MOJOTREES_ERROR_INVALID_ARGUMENT.  The first call on a
- * device looks up the array's device address; make that first call before
- * any stream capture.  Every call shares the array and clears the cells it
- * uses; calls whose GPU work overlaps (two streams, two threads) race on it. */
+ * device looks up the array's device address.  Every call shares the array
+ * and clears the cells it uses; calls whose GPU work overlaps (two streams,
+ * two threads) race on it. */
 int32_t mojotrees_b200_histogram_u8_noalloc(const uint8_t *bins_rm, int64_t n_rows, int64_t n_features,
                                             int32_t n_bins, const int32_t *rows, int64_t n_sel,
                                             const uint16_t *pairs, int32_t num_grad_quant_bins, int32_t *out_hist,

@@ -127,14 +127,15 @@ extern "C" int32_t mojotrees_b200_histogram_u8(const uint8_t* bins, int64_t n_ro
 // ---------------------------------------------------------------------------
 // Allocation-free variant.
 //
-// Some callers cannot call cudaMalloc: code that runs while a CUDA graph is
-// being captured (allocation would break the capture), callers that hand the
-// GPU's memory to their own pool allocator and forbid others from taking any,
-// and real-time paths that must not take the allocator's locks.  For them the
-// job descriptor and the accumulation cells of the histogram live in one
+// Some callers cannot call cudaMalloc: callers that hand the GPU's memory to
+// their own pool allocator and forbid others from taking any, and
+// latency-critical paths that must not take the allocator's locks.  For them
+// the job descriptor and the accumulation cells of the histogram live in one
 // fixed device array, reserved when the library is loaded and held by every
 // GPU that loads it until the process exits.  The caller passes device
 // pointers for the inputs and the output; nothing is allocated per call.
+// The job descriptor is written by a one-thread kernel on the call's stream,
+// so the call makes no host-to-device copy.
 // ---------------------------------------------------------------------------
 namespace mtb {
 namespace {
@@ -154,6 +155,17 @@ struct NoAllocDevice {
 constexpr int kMaxDevices = 64;
 NoAllocDevice g_noalloc_dev[kMaxDevices];
 std::mutex g_noalloc_mutex;
+
+// Writes the one-item job descriptor of one_item_batch() on the device.
+__global__ void k_noalloc_descriptor(Batch* b, long long n_sel) {
+  unsigned char* p = reinterpret_cast<unsigned char*>(b);
+  for (size_t i = 0; i < kOneItemBatchBytes; ++i) p[i] = 0;
+  b->n_items = 1;
+  b->root = 1;
+  b->items[0].built_is_left = 1;
+  b->items[0].count = n_sel;
+  b->items[0].cursor_left = (unsigned long long)n_sel;
+}
 
 }  // namespace
 }  // namespace mtb
@@ -180,6 +192,8 @@ extern "C" int32_t mojotrees_b200_histogram_u8_noalloc(const uint8_t* bins_rm, i
     if (dev < 0 || dev >= kMaxDevices) throw std::runtime_error("device index out of range");
     const int F = (int)n_features, B = n_bins, Fp = (F + 15) / 16 * 16;
     NoAllocDevice* d = &g_noalloc_dev[dev];
+    HistLaunch hl;  // this call's launch geometry, copied while the lock is held
+    unsigned char* scratch = nullptr;
     {
       std::lock_guard<std::mutex> lock(g_noalloc_mutex);
       if (!d->ready) {
@@ -199,14 +213,16 @@ extern "C" int32_t mojotrees_b200_histogram_u8_noalloc(const uint8_t* bins_rm, i
         d->hl_Fp = Fp;
         d->hl_qb = num_grad_quant_bins;
       }
+      hl = d->hl;
+      scratch = d->scratch;
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    Batch* batch = reinterpret_cast<Batch*>(d->scratch);
-    int* work = reinterpret_cast<int*>(d->scratch + kNoAllocBatchBytes);
-    Batch b = one_item_batch(n_sel);
-    MTB_CUDA(cudaMemcpyAsync(batch, &b, kOneItemBatchBytes, cudaMemcpyHostToDevice, st));
+    Batch* batch = reinterpret_cast<Batch*>(scratch);
+    int* work = reinterpret_cast<int*>(scratch + kNoAllocBatchBytes);
+    k_noalloc_descriptor<<<1, 1, 0, st>>>(batch, n_sel);
+    MTB_CUDA(cudaGetLastError());
     MTB_CUDA(cudaMemsetAsync(work, 0, sizeof(int) * cells, st));  // the array keeps the last call's cells
-    launch_hist(d->hl, st, batch, bins_rm, Fp, F, B, rows, rows, pairs, pairs, work, cells, 0);
+    launch_hist(hl, st, batch, bins_rm, Fp, F, B, rows, rows, pairs, pairs, work, cells, 0);
     MTB_CUDA(cudaGetLastError());
     MTB_CUDA(cudaMemcpyAsync(out_hist, work, sizeof(int) * cells, cudaMemcpyDeviceToDevice, st));
     return MOJOTREES_OK;

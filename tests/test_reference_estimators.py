@@ -3,8 +3,9 @@ library's `_mojotrees` shim: it imports (the objective/metric registry
 queries), loads model files, predicts, saves with feature names, and a
 `device="gpu"` fit without a CUDA device refuses instead of falling back.
 
-Runs where the reference tree is mounted (this test reads its Python package
-at run time); skipped elsewhere.
+Runs when MOJOTREES_REFERENCE_PYTHON names the directory that holds the
+reference's `mojotrees` package (this test reads it at run time); skipped
+otherwise.
 """
 import os
 import sys
@@ -14,7 +15,7 @@ import pytest
 
 from test_model_io import RAW_A, X_A, model_a, write
 
-REF_PY = os.environ.get("MOJOTREES_REFERENCE_PYTHON", "/root/reference/python")
+REF_PY = os.environ.get("MOJOTREES_REFERENCE_PYTHON", "")
 pytestmark = pytest.mark.skipif(not os.path.isdir(os.path.join(REF_PY, "mojotrees")),
                                 reason="the reference package is not mounted")
 

@@ -1,7 +1,7 @@
 """The allocation-free histogram entry point (mojotrees_b200_histogram_u8_noalloc).
 
-Callers that cannot allocate GPU memory -- code inside a CUDA graph capture,
-applications whose pool allocator owns the device, latency-critical paths --
+Callers that cannot allocate GPU memory -- applications whose pool allocator
+owns the device, latency-critical paths that must not take allocator locks --
 get the same histogram as mojotrees_b200_histogram_u8 from device buffers they
 own, with the library's fixed device array as the only scratch.  This file is
 collected last so that a stop-at-first-failure run has already run every
