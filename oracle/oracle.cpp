@@ -92,6 +92,8 @@ typedef struct {
   int64_t* count;
   double* raw;            // [n_rows * n_classes]
   double* base_scores;    // [n_classes]
+  double* round_seconds;  // [num_rounds] wall-clock seconds at the end of each round since the fit
+                          // began (the CPU baseline's per-round timing), or NULL
 } mt_oracle_out;
 
 }  // extern "C"
@@ -1038,6 +1040,10 @@ void store_tree(const Tree& t, int ti, mt_oracle_out* out) {
 }
 
 void train(const Data& d, const double* y, const mt_oracle_params& p, mt_oracle_out* out) {
+  const double t_start = omp_get_wtime();
+  auto mark_round = [&](int it) {
+    if (out->round_seconds) out->round_seconds[it] = omp_get_wtime() - t_start;
+  };
   Ctx c(d, p);
   int64_t n = d.n;
   int K = p.objective == OBJ_SOFTMAX ? p.n_classes : 1;
@@ -1074,6 +1080,7 @@ void train(const Data& d, const double* y, const mt_oracle_params& p, mt_oracle_
       Tree t = grow_tree(c, st, bagged ? bag : std::vector<int64_t>(), feats, leaf_rows, leaf_nodes);
       int nl = (int)leaf_nodes.size();
       if (nl == 1 && fabs(t.value[0]) < 1e-12) {
+        mark_round(it);
         if (bagged) continue;
         break;
       }
@@ -1089,6 +1096,7 @@ void train(const Data& d, const double* y, const mt_oracle_params& p, mt_oracle_
         }
       }
       store_tree(t, n_trees++, out);
+      mark_round(it);
     }
   } else {
     // boosting.mojo:4167-4249 and :3876-4164
@@ -1152,6 +1160,7 @@ void train(const Data& d, const double* y, const mt_oracle_params& p, mt_oracle_
         n_trees = first;
         break;
       }
+      mark_round(it);
     }
   }
   out->n_trees = n_trees;

@@ -65,6 +65,7 @@ class OracleOut(ctypes.Structure):
         ("count", ctypes.c_void_p),
         ("raw", ctypes.c_void_p),
         ("base_scores", ctypes.c_void_p),
+        ("round_seconds", ctypes.c_void_p),
     ]
 
 
@@ -159,9 +160,10 @@ def train(bins_fm, n_bins, labels, missing_bin=None, n_cats=None, **kw):
     }
     raw = np.zeros(N * K, np.float64)
     base = np.zeros(K, np.float64)
+    round_s = np.full(p["num_rounds"], np.nan)
     out = OracleOut(0, M, n_nodes.ctypes.data, *(arrs[k].ctypes.data for k in (
         "feature", "threshold_bin", "left", "right", "default_left", "missing_bin",
-        "cat_bits", "value", "gain", "count")), raw.ctypes.data, base.ctypes.data)
+        "cat_bits", "value", "gain", "count")), raw.ctypes.data, base.ctypes.data, round_s.ctypes.data)
     err = ctypes.create_string_buffer(512)
     rc = lib().mt_oracle_train(
         bins_fm.ctypes.data_as(ctypes.c_void_p), ctypes.c_int64(N), ctypes.c_int(F),
@@ -170,7 +172,31 @@ def train(bins_fm, n_bins, labels, missing_bin=None, n_cats=None, **kw):
         ctypes.byref(params), ctypes.byref(out), err, 512)
     if rc != 0:
         raise RuntimeError("oracle: " + err.value.decode())
-    return OracleModel(out.n_trees, n_nodes, arrs, raw.reshape(N, K) if K > 1 else raw, base)
+    m = OracleModel(out.n_trees, n_nodes, arrs, raw.reshape(N, K) if K > 1 else raw, base)
+    m.round_seconds = round_s  # wall-clock seconds since the fit began, at the end of each round
+    return m
+
+
+def bin_dense(X, max_bin=255, categorical=(), min_data_in_bin=3, sample_cnt=200_000, seed=1, use_missing=True):
+    """The oracle's restatement of the reference binner: X [N, F] float64 ->
+    (bins [F, N] uint8, missing_bin, n_categories, n_bins)."""
+    X = np.asarray(X, dtype=np.float64)
+    n, f = X.shape
+    Xc = np.asfortranarray(X)
+    cats = np.zeros(f, np.int32)
+    for c in categorical:
+        cats[c] = 1
+    bins = np.zeros((f, n), np.uint8)
+    mb = np.zeros(f, np.int32)
+    nc = np.zeros(f, np.int32)
+    P = ctypes.c_void_p
+    rc = lib().mt_oracle_bin_dense(Xc.ctypes.data_as(P), ctypes.c_int64(n), ctypes.c_int(f), ctypes.c_int(max_bin),
+                                   ctypes.c_int(min_data_in_bin), ctypes.c_int64(sample_cnt), ctypes.c_int(seed),
+                                   ctypes.c_int(1 if use_missing else 0), cats.ctypes.data_as(P),
+                                   bins.ctypes.data_as(P), mb.ctypes.data_as(P), nc.ctypes.data_as(P))
+    if rc != 0:
+        raise ValueError("oracle binning: invalid arguments")
+    return bins, mb, nc, max_bin
 
 
 def predict_raw_bins(model, bins_fm, fma=False):

@@ -35,23 +35,22 @@ def unbits(h):
     return struct.unpack("<d", struct.pack("<Q", int(h, 16)))[0]
 
 
-def _bins(fx, mtlib):
+def _bins(fx, oracle):
+    """The fixture's bins through the oracle's own restatement of the
+    reference binner (so the golden bits pin it)."""
     if fx["binning"][0] == "equal":
         b = bin_equal_width(fx["x"], fx["binning"][1])
         F = b.shape[0]
         return b, fx["binning"][1], np.full(F, -1), np.full(F, -1)
     _, max_bins, cats = fx["binning"]
-    p = {"max_bin": max_bins}
-    if cats:
-        p["categorical_feature"] = cats
-    bins, mb, nc, nb = mtlib.bin_dense(fx["x"].T, p)
+    bins, mb, nc, nb = oracle.bin_dense(fx["x"].T, max_bin=max_bins, categorical=list(cats))
     return bins, nb, mb, nc
 
 
 @pytest.mark.parametrize("name", ["l2", "bag", "ffrac", "misscat", "large", "logit", "multi"])
-def test_golden_fixture(name, oracle, mtlib):
+def test_golden_fixture(name, oracle):
     fx = fixture(name)
-    bins, nb, mbin, ncat = _bins(fx, mtlib)
+    bins, nb, mbin, ncat = _bins(fx, oracle)
     K = fx.get("n_classes", 1)
     kw = dict(objective=fx["objective"], n_classes=K, num_rounds=fx["rounds"], learning_rate=fx["lr"],
               num_leaves=fx["leaves"], min_data_in_leaf=fx["min_data"], base_override=REFERENCE_BASE.get(name))
