@@ -205,6 +205,10 @@ TrainConfig parse_config(const char* params, bool need_training) {
       if (!(d == "gpu" || d == "cuda" || d == "auto"))
         throw InvalidArgument("device must be cpu, gpu or auto, got '" + v + "'");
     } else if (k == "gpu_device_id") c.gpu_device_id = (int)to_int(k, v);
+    else if (k == "dp_timeout_seconds") {
+      c.dp_timeout_seconds = to_double(k, v);
+      if (!(c.dp_timeout_seconds > 0.0)) throw InvalidArgument("dp_timeout_seconds must be positive");
+    }
     else if (k == "use_quantized_grad") c.use_quantized_grad = to_bool(k, v);
     else if (k == "num_grad_quant_bins") c.num_grad_quant_bins = (int)to_int(k, v);
     else if (k == "stochastic_rounding") {
@@ -523,9 +527,16 @@ int32_t mojotrees_b200_train_binned_u8_dp(const uint8_t* bins, int64_t n_rows, i
     if (mtb::cuda_device_count() < 1) throw mtb::Unsupported("no CUDA device is available");
     if (cfg.gpu_device_id >= 0 && cudaSetDevice(cfg.gpu_device_id) != cudaSuccess)
       throw mtb::Unsupported("cannot select the CUDA device");
-    mtb::Collective coll(nccl_id, rank, world);
-    return train_binned(bins, n_rows, n_features, n_bins, missing, ncats, labels, cfg, out_model, nullptr, &coll,
-                        row_offset, n_rows_global);
+    mtb::Collective coll(nccl_id, rank, world, cfg.dp_timeout_seconds);
+    try {
+      return train_binned(bins, n_rows, n_features, n_bins, missing, ncats, labels, cfg, out_model, nullptr, &coll,
+                          row_offset, n_rows_global);
+    } catch (...) {
+      // the other ranks may be gone or waiting: end this rank's share of the
+      // communicator without waiting for them
+      coll.abort();
+      throw;
+    }
   });
 }
 

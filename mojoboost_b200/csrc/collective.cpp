@@ -5,9 +5,11 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <chrono>
 #include <mutex>
 #include <stdexcept>
 #include <string>
+#include <thread>
 
 namespace mtb {
 
@@ -19,12 +21,26 @@ typedef struct {
   char internal[128];
 } nccl_unique_id_t;
 typedef void* nccl_comm_t;
-enum { kNcclSuccess = 0, kNcclInt8 = 0, kNcclInt32 = 2, kNcclUint64 = 5, kNcclFloat64 = 8 };
+enum { kNcclSuccess = 0, kNcclInProgress = 7, kNcclInt8 = 0, kNcclInt32 = 2, kNcclUint64 = 5, kNcclFloat64 = 8 };
+// The leading fields of ncclConfig_t as NCCL 2.14 laid them out; newer
+// libraries read `size` and treat the fields past it as unset.
+struct nccl_config_t {
+  size_t size;
+  unsigned int magic;
+  unsigned int version;
+  int blocking;
+  int cga_cluster_size;
+  int min_ctas;
+  int max_ctas;
+  const char* net_name;
+};
+constexpr int kNcclConfigUndefInt = -2147483647 - 1;
 enum { kNcclSum = 0, kNcclMax = 2 };
 
 struct Api {
   nccl_result_t (*get_unique_id)(nccl_unique_id_t*);
   nccl_result_t (*comm_init_rank)(nccl_comm_t*, int, nccl_unique_id_t, int);
+  nccl_result_t (*comm_init_rank_config)(nccl_comm_t*, int, nccl_unique_id_t, int, nccl_config_t*);
   nccl_result_t (*comm_destroy)(nccl_comm_t);
   nccl_result_t (*comm_abort)(nccl_comm_t);
   nccl_result_t (*all_reduce)(const void*, void*, size_t, int, int, nccl_comm_t, cudaStream_t);
@@ -61,6 +77,8 @@ void do_load() {
   };
   g_api.get_unique_id = (decltype(g_api.get_unique_id))sym("ncclGetUniqueId");
   g_api.comm_init_rank = (decltype(g_api.comm_init_rank))sym("ncclCommInitRank");
+  // optional: without it joining is not bounded by the timeout
+  g_api.comm_init_rank_config = (decltype(g_api.comm_init_rank_config))dlsym(h, "ncclCommInitRankConfig");
   g_api.comm_destroy = (decltype(g_api.comm_destroy))sym("ncclCommDestroy");
   g_api.comm_abort = (decltype(g_api.comm_abort))sym("ncclCommAbort");
   g_api.all_reduce = (decltype(g_api.all_reduce))sym("ncclAllReduce");
@@ -95,38 +113,128 @@ void Collective::unique_id(uint8_t out[128]) {
   memcpy(out, id.internal, 128);
 }
 
-Collective::Collective(const uint8_t id[128], int rank, int world) : rank_(rank), world_(world) {
+Collective::Collective(const uint8_t id[128], int rank, int world, double timeout_s)
+    : rank_(rank), world_(world), timeout_s_(timeout_s > 0 ? timeout_s : 300.0) {
   std::string why;
   if (!load(&why)) throw std::runtime_error(why);
   if (world < 1 || rank < 0 || rank >= world) throw std::runtime_error("invalid rank / world size");
   nccl_unique_id_t uid;
   memcpy(uid.internal, id, 128);
   nccl_comm_t c = nullptr;
-  ck(g_api.comm_init_rank(&c, world, uid, rank), "ncclCommInitRank");
-  comm_ = c;
+  if (g_api.comm_init_rank_config) {
+    // non-blocking: the join returns at once and is polled, so a rank that
+    // never joins costs the timeout, not the process
+    nccl_config_t cfg = {sizeof(nccl_config_t), 0xcafebeefu, 21400u, 0, kNcclConfigUndefInt,
+                         kNcclConfigUndefInt, kNcclConfigUndefInt, nullptr};
+    const nccl_result_t r = g_api.comm_init_rank_config(&c, world, uid, rank, &cfg);
+    if (r != kNcclSuccess && r != kNcclInProgress) {
+      if (c) g_api.comm_abort(c);
+      ck(r, "ncclCommInitRankConfig");
+    }
+    comm_ = c;
+    settle("joining the communicator");
+  } else {
+    ck(g_api.comm_init_rank(&c, world, uid, rank), "ncclCommInitRank");
+    comm_ = c;
+  }
+  if (cudaEventCreateWithFlags(&ev_, cudaEventDisableTiming) != cudaSuccess) {
+    abort();
+    throw std::runtime_error("cudaEventCreate failed");
+  }
 }
 
 Collective::~Collective() {
+  if (ev_) cudaEventDestroy(ev_);
   if (comm_) g_api.comm_destroy((nccl_comm_t)comm_);
 }
 
+void Collective::abort() {
+  if (!comm_) return;
+  g_api.comm_abort((nccl_comm_t)comm_);
+  comm_ = nullptr;
+}
+
+void Collective::settle(const char* what) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    if (!comm_) throw std::runtime_error(std::string("NCCL communicator was aborted before ") + what);
+    nccl_result_t st = kNcclSuccess;
+    const nccl_result_t r = g_api.get_async_error((nccl_comm_t)comm_, &st);
+    if (r != kNcclSuccess || (st != kNcclSuccess && st != kNcclInProgress)) {
+      abort();
+      ck(r != kNcclSuccess ? r : st, what);
+    }
+    if (st == kNcclSuccess) return;
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > timeout_s_) {
+      abort();
+      throw std::runtime_error(std::string("NCCL timed out after ") + std::to_string(timeout_s_) + " s " + what +
+                               " (a rank did not join or stopped participating); the communicator was aborted");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+  }
+}
+
+void Collective::wait(cudaEvent_t ev) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t q = cudaEventQuery(ev);
+    if (q == cudaSuccess) return;
+    if (q != cudaErrorNotReady)
+      throw std::runtime_error(std::string("CUDA error while waiting: ") + cudaGetErrorString(q));
+    if (comm_) {
+      nccl_result_t st = kNcclSuccess;
+      g_api.get_async_error((nccl_comm_t)comm_, &st);
+      if (st != kNcclSuccess && st != kNcclInProgress) {
+        abort();
+        ck(st, "asynchronous operation");
+      }
+    }
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > timeout_s_) {
+      // the queued NCCL kernels wait for a peer that is gone: aborting ends
+      // them, and the work queued behind them then drains
+      abort();
+      cudaEventSynchronize(ev);
+      throw std::runtime_error("data-parallel fit timed out after " + std::to_string(timeout_s_) +
+                               " s waiting for the other ranks (a rank stopped participating); the NCCL "
+                               "communicator was aborted");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+void Collective::sync(cudaStream_t st) {
+  if (cudaEventRecord(ev_, st) != cudaSuccess) throw std::runtime_error("cudaEventRecord failed");
+  wait(ev_);
+}
+
+#define MTB_NCCL_CALL(call, what)                                         \
+  do {                                                                    \
+    if (!comm_) throw std::runtime_error("NCCL communicator was aborted"); \
+    const nccl_result_t r_ = (call);                                      \
+    if (r_ == kNcclInProgress)                                            \
+      settle(what);                                                       \
+    else                                                                  \
+      ck(r_, what);                                                       \
+  } while (0)
+
 void Collective::allreduce_sum_i32(int* buf, size_t n, cudaStream_t st) {
-  ck(g_api.all_reduce(buf, buf, n, kNcclInt32, kNcclSum, (nccl_comm_t)comm_, st), "ncclAllReduce");
+  MTB_NCCL_CALL(g_api.all_reduce(buf, buf, n, kNcclInt32, kNcclSum, (nccl_comm_t)comm_, st), "ncclAllReduce");
 }
 
 void Collective::allreduce_max_u64(unsigned long long* buf, size_t n, cudaStream_t st) {
-  ck(g_api.all_reduce(buf, buf, n, kNcclUint64, kNcclMax, (nccl_comm_t)comm_, st), "ncclAllReduce");
+  MTB_NCCL_CALL(g_api.all_reduce(buf, buf, n, kNcclUint64, kNcclMax, (nccl_comm_t)comm_, st), "ncclAllReduce");
 }
 
 void Collective::allreduce_sum_f64(double* buf, size_t n, cudaStream_t st) {
-  ck(g_api.all_reduce(buf, buf, n, kNcclFloat64, kNcclSum, (nccl_comm_t)comm_, st), "ncclAllReduce");
+  MTB_NCCL_CALL(g_api.all_reduce(buf, buf, n, kNcclFloat64, kNcclSum, (nccl_comm_t)comm_, st), "ncclAllReduce");
 }
 
 void Collective::allgather_f64(const double* send, double* recv, size_t n_per_rank, cudaStream_t st) {
-  ck(g_api.all_gather(send, recv, n_per_rank, kNcclFloat64, (nccl_comm_t)comm_, st), "ncclAllGather");
+  MTB_NCCL_CALL(g_api.all_gather(send, recv, n_per_rank, kNcclFloat64, (nccl_comm_t)comm_, st), "ncclAllGather");
 }
 
 void Collective::check() {
+  if (!comm_) throw std::runtime_error("NCCL communicator was aborted");
   nccl_result_t e = kNcclSuccess;
   ck(g_api.get_async_error((nccl_comm_t)comm_, &e), "ncclCommGetAsyncError");
   if (e != kNcclSuccess) {
@@ -137,11 +245,12 @@ void Collective::check() {
 }
 
 void Collective::allgather_bytes(const void* send, void* recv, size_t bytes_per_rank, cudaStream_t st) {
-  ck(g_api.all_gather(send, recv, bytes_per_rank, kNcclInt8, (nccl_comm_t)comm_, st), "ncclAllGather");
+  MTB_NCCL_CALL(g_api.all_gather(send, recv, bytes_per_rank, kNcclInt8, (nccl_comm_t)comm_, st), "ncclAllGather");
 }
 
 void Collective::reduce_scatter_slots_i32(int* base, size_t n_slots, size_t slot_len, size_t chunk, cudaStream_t st) {
   if (chunk * (size_t)world_ != slot_len) throw std::runtime_error("reduce-scatter: slot length is not world x chunk");
+  if (!comm_) throw std::runtime_error("NCCL communicator was aborted");
   ck(g_api.group_start(), "ncclGroupStart");
   nccl_result_t r = kNcclSuccess;
   for (size_t i = 0; i < n_slots && r == kNcclSuccess; ++i) {
@@ -150,8 +259,11 @@ void Collective::reduce_scatter_slots_i32(int* base, size_t n_slots, size_t slot
     r = g_api.reduce_scatter(slot, slot + (size_t)rank_ * chunk, chunk, kNcclInt32, kNcclSum, (nccl_comm_t)comm_, st);
   }
   const nccl_result_t e = g_api.group_end();
-  ck(r, "ncclReduceScatter");
-  ck(e, "ncclGroupEnd");
+  if (r != kNcclInProgress) ck(r, "ncclReduceScatter");
+  if (e == kNcclInProgress || r == kNcclInProgress)
+    settle("ncclGroupEnd");
+  else
+    ck(e, "ncclGroupEnd");
 }
 
 }  // namespace mtb

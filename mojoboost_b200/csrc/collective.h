@@ -22,7 +22,12 @@ class Collective {
   // Writes a fresh 128-byte NCCL unique id (call on one rank, broadcast it).
   static void unique_id(uint8_t out[128]);
 
-  Collective(const uint8_t id[128], int rank, int world);
+  // Joins the communicator.  `timeout_s` bounds every host wait of this
+  // communicator: joining (a rank that never joins), the completion of work
+  // queued behind a collective (a rank that stopped participating) and NCCL's
+  // own asynchronous set-up.  Past it the communicator is aborted (its queued
+  // kernels end) and the wait throws, so no rank blocks forever on another.
+  Collective(const uint8_t id[128], int rank, int world, double timeout_s);
   ~Collective();
   Collective(const Collective&) = delete;
   Collective& operator=(const Collective&) = delete;
@@ -42,9 +47,23 @@ class Collective {
   void reduce_scatter_slots_i32(int* base, size_t n_slots, size_t slot_len, size_t chunk, cudaStream_t st);
   // Throws if the communicator reported an asynchronous error (and aborts it).
   void check();
+  // Host waits bounded by the timeout (see the constructor): until the
+  // stream's queued work (or the event) completes.
+  void sync(cudaStream_t st);
+  void wait(cudaEvent_t ev);
+  // Aborts the communicator (idempotent): NCCL kernels still waiting for a
+  // peer end, and the communicator is unusable afterwards.
+  void abort();
+  bool aborted() const { return comm_ == nullptr; }
+  double timeout_s() const { return timeout_s_; }
 
  private:
+  // Polls until NCCL's asynchronous state leaves "in progress" (non-blocking
+  // communicator), within the timeout.
+  void settle(const char* what);
   void* comm_ = nullptr;
+  double timeout_s_ = 300.0;
+  cudaEvent_t ev_ = nullptr;
   int rank_ = 0;
   int world_ = 1;
 };

@@ -51,6 +51,7 @@ struct TrainConfig {
   int num_grad_quant_bins = 4;
   int quant_seed = 11;
   int gpu_device_id = -1;      // -1: current device
+  double dp_timeout_seconds = 300.0;  // data-parallel fits: bound of every wait on the other ranks
   bool keep_training_scores = false;
   bool profile_phases = false;    // CUDA events around every kernel phase
   bool profile_histogram = false; // CUDA events around the histogram launches only

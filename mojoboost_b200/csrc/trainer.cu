@@ -12,6 +12,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <thread>
 #include <cmath>
 #include <cstring>
 #include <stdexcept>
@@ -187,6 +188,19 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   // order (exact for binary and class labels, whose sums are integers).
   Collective* coll = in.coll;
   const int world = coll ? coll->world() : 1;
+  // Host waits: with other ranks, bounded by the communicator's timeout
+  // (past it the communicator is aborted and the wait throws).
+  const char* stall_env = getenv("MOJOTREES_DP_TEST_STALL_RANK");
+  const int test_stall_rank = stall_env ? atoi(stall_env) : -1;
+  const int test_stall_after =
+      getenv("MOJOTREES_DP_TEST_STALL_AFTER_ROUNDS") ? atoi(getenv("MOJOTREES_DP_TEST_STALL_AFTER_ROUNDS")) : 1;
+  const double test_stall_s = getenv("MOJOTREES_DP_TEST_STALL_S") ? atof(getenv("MOJOTREES_DP_TEST_STALL_S")) : 0.0;
+  auto host_sync = [&]() {
+    if (coll)
+      coll->sync(st);
+    else
+      MTB_CUDA(cudaStreamSynchronize(st));
+  };
   const long long N_global = coll ? in.n_rows_global : N;
   mark("labels, raw allocated");
   DevBuf<double> d_red;
@@ -201,7 +215,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     MTB_CUDA(cudaMemcpyAsync(d_red.p, &flag, 8, cudaMemcpyHostToDevice, st));
     coll->allreduce_max_u64(reinterpret_cast<unsigned long long*>(d_red.p), 1, st);
     MTB_CUDA(cudaMemcpyAsync(&flag, d_red.p, 8, cudaMemcpyDeviceToHost, st));
-    MTB_CUDA(cudaStreamSynchronize(st));
+    host_sync();
     if (flag) throw std::runtime_error(local_error.empty() ? "invalid input on another rank" : local_error);
   };
   // FIXED mode sums |g| over 1024-row blocks of global rows, so its shards
@@ -223,7 +237,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       coll->allgather_f64(d_red.p + world, d_red.p, 1, st);
       std::vector<double> parts(world);
       MTB_CUDA(cudaMemcpyAsync(parts.data(), d_red.p, 8 * world, cudaMemcpyDeviceToHost, st));
-      MTB_CUDA(cudaStreamSynchronize(st));
+      host_sync();
       mean = parts[0];
       for (int q = 1; q < world; ++q) mean += parts[q];
     }
@@ -251,7 +265,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       MTB_CUDA(cudaMemcpyAsync(d_red.p, cw.data(), 8 * K, cudaMemcpyHostToDevice, st));
       coll->allreduce_sum_f64(d_red.p, K, st);
       MTB_CUDA(cudaMemcpyAsync(cw.data(), d_red.p, 8 * K, cudaMemcpyDeviceToHost, st));
-      MTB_CUDA(cudaStreamSynchronize(st));
+      host_sync();
     }
     double tw = (double)N_global;
     for (int k = 0; k < K; ++k) {
@@ -270,7 +284,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       MTB_CUDA(cudaGetLastError());
       stats.kernel_launches++;
     }
-    MTB_CUDA(cudaStreamSynchronize(st));
+    host_sync();
   }
 
   mark("initial scores");
@@ -301,7 +315,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     MTB_CUDA(cudaMemcpyAsync(d_red.p, &mx, 8, cudaMemcpyHostToDevice, st));
     coll->allreduce_max_u64(reinterpret_cast<unsigned long long*>(d_red.p), 1, st);
     MTB_CUDA(cudaMemcpyAsync(&mx, d_red.p, 8, cudaMemcpyDeviceToHost, st));
-    MTB_CUDA(cudaStreamSynchronize(st));
+    host_sync();
     P_rank = (long long)mx;
     n_part = P_rank * world;
     // The gathered partials are block r * P_rank + j of rank r, so the global
@@ -361,7 +375,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   d_begins.alloc(kMaxPool);
   d_order.alloc(kMaxPool);
   d_values.alloc(kMaxPool);
-  MTB_CUDA(cudaStreamSynchronize(st));
+  host_sync();
   mark("work buffers");
   stats.upload_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
 
@@ -545,6 +559,11 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
         tot_g = ig;
         tot_h = ih;
       }
+      // With other ranks, wait for the tree's first exchange before queueing
+      // work that depends on it: a rank that stopped participating between
+      // trees is detected here (the bounded wait aborts the communicator),
+      // with none of this rank's work queued behind the aborted collective.
+      if (coll) coll->sync(st);
       k_scales<<<1, 32, 0, st>>>(d_sc.p, tot_g, tot_h, mode, const_h ? 1 : 0, cfg.num_grad_quant_bins);
       uint64_t gs = mt_quant_stream(cfg.quant_seed, it, k, 0);
       uint64_t hs = mt_quant_stream(cfg.quant_seed, it, k, 1);
@@ -607,7 +626,10 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       for (int i = 0;; ++i) {
         if (i >= kLookahead) {
           const int q = (i - kLookahead) % kRing;
-          MTB_CUDA(cudaEventSynchronize(iter_ev[q]));
+          if (coll)
+            coll->wait(iter_ev[q]);
+          else
+            MTB_CUDA(cudaEventSynchronize(iter_ev[q]));
           if (reinterpret_cast<volatile int*>(h_done)[q]) break;
         }
         if (i > cfg.num_leaves) break;  // bound: every iteration after the root commits a split
@@ -651,7 +673,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       MTB_CUDA(cudaGetLastError());
       MTB_CUDA(cudaMemcpyAsync(&hdr, &d_ts.p->hdr, sizeof(TreeHeader), cudaMemcpyDeviceToHost, st));
       MTB_CUDA(cudaMemcpyAsync(nodes_host.data(), d_ts.p->nodes, sizeof(HostNode) * M, cudaMemcpyDeviceToHost, st));
-      MTB_CUDA(cudaStreamSynchronize(st));
+      host_sync();
       timer.collect();
       hist_timer.collect();
       if (hdr.error || !hdr.done) throw std::runtime_error("device trainer reported an internal error");
@@ -665,6 +687,15 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     }
     stats.rounds++;
     mark_round();
+    if (coll && test_stall_rank == coll->rank() && stats.rounds == test_stall_after) {
+      // Test hook (off unless MOJOTREES_DP_TEST_STALL_RANK names this rank):
+      // after a completed round, with nothing of this rank in flight, it
+      // stops participating for MOJOTREES_DP_TEST_STALL_S seconds (its
+      // communicator and memory stay valid meanwhile), then fails.
+      std::this_thread::sleep_for(std::chrono::duration<double>(test_stall_s));
+      throw std::runtime_error("injected failure: rank " + std::to_string(coll->rank()) +
+                               " stopped participating after round " + std::to_string(stats.rounds));
+    }
     stats.round_hist_ms.push_back(stats.hist_ms);  // cumulative; differenced below
     stats.round_hist_launches.push_back((double)stats.hist_launches);
     stats.round_launches.push_back((double)launches);
@@ -675,7 +706,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       break;
     }
   }
-  MTB_CUDA(cudaStreamSynchronize(st));
+  host_sync();
   for (size_t i = 0; i + 1 < round_ev.size(); ++i) {
     float ms = 0.f;
     MTB_CUDA(cudaEventElapsedTime(&ms, round_ev[i], round_ev[i + 1]));

@@ -81,7 +81,7 @@ def v4_text(m, K, lr, objective, n_features, n_bins, mbin, ncat):
 @pytest.mark.parametrize("name", ["l2", "bag", "ffrac", "misscat", "large", "logit", "multi"])
 def test_golden_fit_through_model_file(name, oracle, mtlib, tmp_path):
     fx = fixture(name)
-    bins, nb, mbin, ncat = _bins(fx, mtlib)
+    bins, nb, mbin, ncat = _bins(fx, oracle)
     K = fx.get("n_classes", 1)
     kw = dict(objective=fx["objective"], n_classes=K, num_rounds=fx["rounds"], learning_rate=fx["lr"],
               num_leaves=fx["leaves"], min_data_in_leaf=fx["min_data"], base_override=REFERENCE_BASE.get(name))
