@@ -205,7 +205,12 @@ TrainConfig parse_config(const char* params, bool need_training) {
       if (!(d == "gpu" || d == "cuda" || d == "auto"))
         throw InvalidArgument("device must be cpu, gpu or auto, got '" + v + "'");
     } else if (k == "gpu_device_id") c.gpu_device_id = (int)to_int(k, v);
-    else if (k == "dp_timeout_seconds") {
+    else if (k == "gpu_histogram_precision") {
+      const std::string d = lower(v);
+      if (d == "int32" || d == "32") c.hist_int64 = false;
+      else if (d == "int64" || d == "64") c.hist_int64 = true;
+      else throw InvalidArgument("gpu_histogram_precision must be int32 or int64, got '" + v + "'");
+    } else if (k == "dp_timeout_seconds") {
       c.dp_timeout_seconds = to_double(k, v);
       if (!(c.dp_timeout_seconds > 0.0)) throw InvalidArgument("dp_timeout_seconds must be positive");
     }

@@ -21,7 +21,7 @@ typedef struct {
   char internal[128];
 } nccl_unique_id_t;
 typedef void* nccl_comm_t;
-enum { kNcclSuccess = 0, kNcclInProgress = 7, kNcclInt8 = 0, kNcclInt32 = 2, kNcclUint64 = 5, kNcclFloat64 = 8 };
+enum { kNcclSuccess = 0, kNcclInProgress = 7, kNcclInt8 = 0, kNcclInt32 = 2, kNcclInt64 = 4, kNcclUint64 = 5, kNcclFloat64 = 8 };
 // The leading fields of ncclConfig_t as NCCL 2.14 laid them out; newer
 // libraries read `size` and treat the fields past it as unset.
 struct nccl_config_t {
@@ -221,6 +221,10 @@ void Collective::allreduce_sum_i32(int* buf, size_t n, cudaStream_t st) {
   MTB_NCCL_CALL(g_api.all_reduce(buf, buf, n, kNcclInt32, kNcclSum, (nccl_comm_t)comm_, st), "ncclAllReduce");
 }
 
+void Collective::allreduce_sum_i64(long long* buf, size_t n, cudaStream_t st) {
+  MTB_NCCL_CALL(g_api.all_reduce(buf, buf, n, kNcclInt64, kNcclSum, (nccl_comm_t)comm_, st), "ncclAllReduce");
+}
+
 void Collective::allreduce_max_u64(unsigned long long* buf, size_t n, cudaStream_t st) {
   MTB_NCCL_CALL(g_api.all_reduce(buf, buf, n, kNcclUint64, kNcclMax, (nccl_comm_t)comm_, st), "ncclAllReduce");
 }
@@ -249,14 +253,25 @@ void Collective::allgather_bytes(const void* send, void* recv, size_t bytes_per_
 }
 
 void Collective::reduce_scatter_slots_i32(int* base, size_t n_slots, size_t slot_len, size_t chunk, cudaStream_t st) {
+  reduce_scatter_slots(base, sizeof(int), kNcclInt32, n_slots, slot_len, chunk, st);
+}
+
+void Collective::reduce_scatter_slots_i64(long long* base, size_t n_slots, size_t slot_len, size_t chunk,
+                                          cudaStream_t st) {
+  reduce_scatter_slots(base, sizeof(long long), kNcclInt64, n_slots, slot_len, chunk, st);
+}
+
+void Collective::reduce_scatter_slots(void* base, size_t elem, int dtype, size_t n_slots, size_t slot_len,
+                                      size_t chunk, cudaStream_t st) {
   if (chunk * (size_t)world_ != slot_len) throw std::runtime_error("reduce-scatter: slot length is not world x chunk");
   if (!comm_) throw std::runtime_error("NCCL communicator was aborted");
   ck(g_api.group_start(), "ncclGroupStart");
   nccl_result_t r = kNcclSuccess;
-  for (size_t i = 0; i < n_slots && r == kNcclSuccess; ++i) {
-    int* slot = base + i * slot_len;
+  for (size_t i = 0; i < n_slots && (r == kNcclSuccess || r == kNcclInProgress); ++i) {
+    char* slot = static_cast<char*>(base) + i * slot_len * elem;
     // in place: rank r's result lands on its own chunk of the slot
-    r = g_api.reduce_scatter(slot, slot + (size_t)rank_ * chunk, chunk, kNcclInt32, kNcclSum, (nccl_comm_t)comm_, st);
+    r = g_api.reduce_scatter(slot, slot + (size_t)rank_ * chunk * elem, chunk, dtype, kNcclSum,
+                             (nccl_comm_t)comm_, st);
   }
   const nccl_result_t e = g_api.group_end();
   if (r != kNcclInProgress) ck(r, "ncclReduceScatter");

@@ -36,6 +36,7 @@ class Collective {
   int world() const { return world_; }
 
   void allreduce_sum_i32(int* buf, size_t n, cudaStream_t st);
+  void allreduce_sum_i64(long long* buf, size_t n, cudaStream_t st);
   void allreduce_max_u64(unsigned long long* buf, size_t n, cudaStream_t st);
   void allreduce_sum_f64(double* buf, size_t n, cudaStream_t st);
   void allgather_f64(const double* send, double* recv, size_t n_per_rank, cudaStream_t st);
@@ -45,6 +46,8 @@ class Collective {
   // [rank * chunk, (rank + 1) * chunk) of every slot, slot_len = world * chunk.
   // One NCCL group.
   void reduce_scatter_slots_i32(int* base, size_t n_slots, size_t slot_len, size_t chunk, cudaStream_t st);
+  // The same for int64 elements (slot_len and chunk in int64 elements).
+  void reduce_scatter_slots_i64(long long* base, size_t n_slots, size_t slot_len, size_t chunk, cudaStream_t st);
   // Throws if the communicator reported an asynchronous error (and aborts it).
   void check();
   // Host waits bounded by the timeout (see the constructor): until the
@@ -61,6 +64,8 @@ class Collective {
   // Polls until NCCL's asynchronous state leaves "in progress" (non-blocking
   // communicator), within the timeout.
   void settle(const char* what);
+  void reduce_scatter_slots(void* base, size_t elem, int dtype, size_t n_slots, size_t slot_len, size_t chunk,
+                            cudaStream_t st);
   void* comm_ = nullptr;
   double timeout_s_ = 300.0;
   cudaEvent_t ev_ = nullptr;

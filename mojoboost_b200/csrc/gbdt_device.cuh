@@ -200,7 +200,8 @@ struct RoundScales {
   double g_units, h_units;  // QUANT: units per gradient / hessian
   double g_lim, h_lim;
   int hq_const;     // FIXED const-hessian per-row hessian units
-  int pad;
+  int wide;         // FIXED with the 2^52 bound and Int64 cells
+  long long hq_const64;  // wide FIXED const-hessian per-row hessian units
 };
 
 }  // namespace mtb

@@ -17,6 +17,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "gbdt_device.cuh"
 #include "mt_math.h"
 
@@ -215,16 +217,18 @@ __global__ void __launch_bounds__(1024) k_pairwise_level(const double* __restric
 // Scales of the round from the reduced totals (FIXED: quantized_gradient.mojo:908;
 // QUANT: :1343-1453).  `fixed_totals` is null in QUANT mode.
 __global__ void k_scales(RoundScales* sc, const double* fixed_g, const double* fixed_h, int mode, int const_hess,
-                         int quant_bins) {
+                         int quant_bins, int wide) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  sc->wide = wide;
   if (mode == MODE_FIXED) {
     sc->g_total = *fixed_g;
     sc->h_total = *fixed_h;
-    sc->gsf = mt_fixed_point_scale(sc->g_total);
-    sc->hsf = mt_fixed_point_scale(sc->h_total);
+    sc->gsf = wide ? mt_fixed_point_scale52(sc->g_total) : mt_fixed_point_scale(sc->g_total);
+    sc->hsf = wide ? mt_fixed_point_scale52(sc->h_total) : mt_fixed_point_scale(sc->h_total);
     sc->g_inv = 1.0 / (double)sc->gsf;
     sc->h_inv = 1.0 / (double)sc->hsf;
-    sc->hq_const = __float2int_rn(__fmul_rn(1.0f, sc->hsf));
+    sc->hq_const = wide ? 0 : __float2int_rn(__fmul_rn(1.0f, sc->hsf));
+    sc->hq_const64 = wide ? __double2ll_rn(1.0 * (double)sc->hsf) : 0;
   } else {
     double gmax = sc->g_total < 1e-12 ? 1e-12 : sc->g_total;
     double hmax = sc->h_total < 1e-12 ? 1e-12 : sc->h_total;
@@ -236,7 +240,9 @@ __global__ void k_scales(RoundScales* sc, const double* fixed_g, const double* f
 }
 
 // Tree start: identity row list and the quantized pair of every row.
-template <int MODE>
+// WIDE (fixed point with the 2^52 bound): Int64(rint(f64(g) * s)), exact
+// product, ties to even; pairs are longlong2.
+template <int MODE, bool WIDE = false>
 __global__ void k_quantize(const float* __restrict__ g32, const float* __restrict__ h32, long long n,
                            long long row_offset, const RoundScales* __restrict__ sc, int const_hess,
                            uint64_t g_stream, uint64_t h_stream, int* __restrict__ rows, void* __restrict__ pairs) {
@@ -244,7 +250,11 @@ __global__ void k_quantize(const float* __restrict__ g32, const float* __restric
   if (r >= n) return;
   rows[r] = (int)r;
   float g = g32[r], h = h32[r];
-  if (MODE == MODE_FIXED) {
+  if (MODE == MODE_FIXED && WIDE) {
+    const long long gq = __double2ll_rn(__dmul_rn((double)g, (double)sc->gsf));
+    const long long hq = const_hess ? sc->hq_const64 : __double2ll_rn(__dmul_rn((double)h, (double)sc->hsf));
+    reinterpret_cast<longlong2*>(pairs)[r] = make_longlong2(gq, hq);
+  } else if (MODE == MODE_FIXED) {
     int gq = __float2int_rn(__fmul_rn(g, sc->gsf));
     int hq = const_hess ? sc->hq_const : __float2int_rn(__fmul_rn(h, sc->hsf));
     reinterpret_cast<int2*>(pairs)[r] = make_int2(gq, hq);
@@ -499,10 +509,33 @@ constexpr int kQuantCountBits = 15;
 //   HL_QUANT16R  the cells of HL_QUANT16; a chunk's row id, g + g_lim and h
 //                travel as one shuffled word (row << 6 | h << 3 | g + g_lim),
 //                for fewer than 2^26 rows and 2 g_lim, h_lim <= 7
-enum HistLayout : int { HL_QUANT = 0, HL_QUANT16 = 1, HL_FIXED_CH = 2, HL_FIXED = 3, HL_QUANT16R = 4 };
+//   64-bit cells, one red.shared.add.u64 per (row, feature):
+//   HL_Q64       int8 gradients: g + g_lim in bits 0-21, count in bits 22-42,
+//                h in bits 43-63 (unsigned fields, exact while a flush covers
+//                at most min(2^22-1 / 2 g_lim, 2^21-1 / h_lim, 2^21-1) rows)
+//   HL_Q64R      the cells of HL_Q64; row id, g + g_lim and h travel as one
+//                shuffled word as in HL_QUANT16R
+//   HL_FCH64     fixed point, constant hessian: count * 2^40 + g as one
+//                64-bit integer sum (|sum g| <= 2^30 < 2^39 and count < 2^24
+//                per flush make both recoverable)
+//   HL_F64H      HL_FCH64's cell plus a 32-bit h plane (two atomics instead
+//                of three)
+//   HL_W52       fixed point with the 2^52 bound (Int64 global cells): 64-bit
+//                g and h planes and a 32-bit count plane
+//   HL_W52CH     HL_W52 with a constant hessian: g and count planes
+enum HistLayout : int {
+  HL_QUANT = 0, HL_QUANT16 = 1, HL_FIXED_CH = 2, HL_FIXED = 3, HL_QUANT16R = 4,
+  HL_Q64 = 5, HL_Q64R = 6, HL_FCH64 = 7, HL_F64H = 8, HL_W52 = 9, HL_W52CH = 10
+};
 
+__host__ __device__ constexpr bool hist_layout_is64(int layout) { return layout >= HL_Q64; }
+
+// 32-bit words of shared memory a CTA's cells take (cells = lane cells of one plane)
 __host__ __device__ constexpr int hist_layout_words(int layout, int cells) {
-  return (layout == HL_QUANT16 || layout == HL_QUANT16R) ? cells + cells / 2 : layout == HL_FIXED ? 3 * cells : 2 * cells;
+  return (layout == HL_QUANT16 || layout == HL_QUANT16R) ? cells + cells / 2
+         : layout == HL_W52                              ? 5 * cells
+         : (layout == HL_FIXED || layout == HL_F64H || layout == HL_W52CH) ? 3 * cells
+                                                                           : 2 * cells;
 }
 
 __device__ __forceinline__ void built_range(const BatchItem& P, long long& b, long long& cnt) {
@@ -813,6 +846,285 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
   }
 }
 
+__device__ __forceinline__ void shared_red_add64(uint32_t addr, unsigned long long v) {
+  asm volatile("red.shared.add.u64 [%0], %1;" ::"r"(addr), "l"(v));
+}
+
+// hist_segment with 64-bit cells (HL_Q64, HL_Q64R, HL_FCH64, HL_F64H): one
+// 64-bit shared atomic carries a row's gradient, hessian (quantized mode) and
+// count into a (feature, bin) cell.  Same bank-per-lane geometry as the
+// 32-bit layouts: lane l owns features f0 + l*NPL + j, and cell (j, bin) of
+// lane l is 64-bit word (j * 256 + bin) * 32 + l, so the 32 lanes of one
+// instruction touch 32 consecutive words (two wavefronts, no conflicts).
+template <int NPL, int LAYOUT>
+__device__ void hist_segment64(cooperative_groups::cluster_group& cluster, const BatchItem& P, long long seg_b,
+                               long long seg_n, const uint8_t* __restrict__ bins_rm, int Fp, int F, int B,
+                               const int* __restrict__ rows0, const int* __restrict__ rows1,
+                               const void* __restrict__ pairs0, const void* __restrict__ pairs1, int* hs,
+                               long long rows_per_flush, int g_lim, unsigned char* smem) {
+  constexpr bool PR = LAYOUT == HL_Q64R;
+  constexpr bool QUANT = LAYOUT == HL_Q64 || PR;
+  constexpr bool HPLANE = LAYOUT == HL_F64H;
+  constexpr int FG = 32 * NPL;
+  constexpr int U = kHistUnroll;
+  constexpr int CELLS = NPL * kHistBinsPad * 32;  // 64-bit cells of a CTA
+  constexpr int BYTES = CELLS * 8 + (HPLANE ? CELLS * 4 : 0);
+  const int cs = (int)cluster.num_blocks();
+  const int crank = (int)cluster.block_rank();
+  const long long sub = (seg_n + cs - 1) / cs;
+  const long long s = seg_b + crank * sub;
+  long long e = s + sub;
+  if (e > seg_b + seg_n) e = seg_b + seg_n;
+  const long long n_pass = (sub + rows_per_flush - 1) / rows_per_flush;
+  const int f0 = blockIdx.x * FG;
+  const int* rows = P.dst_buf ? rows1 : rows0;
+  const void* pairs = P.dst_buf ? pairs1 : pairs0;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int n_warps = blockDim.x >> 5;
+  // lanes past the padded row width read the row's first bytes and add them
+  // to cells of features >= Fp, which the merge never reads
+  const bool lane_ok = f0 + lane * NPL < Fp;
+  const uint8_t* bcol = bins_rm + (lane_ok ? f0 + lane * NPL : 0);
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem) + 8u * lane;
+  const uint32_t hbase = sbase + 8u * CELLS - 4u * lane;
+  auto add_row = [&](unsigned int bw, unsigned long long v, unsigned int h) {
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+      const uint32_t b = (bw >> (8 * j)) & 0xffu;
+      shared_red_add64(sbase + (b << 8) + j * (256u * 256u), v);
+      if (HPLANE) shared_red_add(hbase + (b << 7) + j * (128u * 256u), h);
+    }
+  };
+  // the 64-bit addend of a quantized pair / a fixed-point gradient
+  auto q_value = [&](unsigned int gq, unsigned int hq) {
+    return ((unsigned long long)(hq << 11) << 32) | (unsigned long long)(gq | (1u << 22));
+  };
+  auto f_value = [&](int g) { return (unsigned long long)((long long)g + (1ll << 40)); };
+  for (long long pass = 0; pass < n_pass; ++pass) {
+    const long long ps = s + pass * rows_per_flush;
+    const long long pe = ps + rows_per_flush < e ? ps + rows_per_flush : e;
+    for (int c = threadIdx.x; c < BYTES / 16; c += blockDim.x) reinterpret_cast<uint4*>(smem)[c] = make_uint4(0, 0, 0, 0);
+    __syncthreads();
+    const long long stride = (long long)n_warps * 32;
+    long long c0 = ps + (long long)warp * 32;
+    // per lane, for position c0 + lane: row id (or the packed row word) and
+    // the pair (quantized: g + g_lim | h << 8; fixed point: g, h)
+    int nr = 0;
+    unsigned int na = 0u, nb2 = 0u;
+    auto fetch = [&](long long base, int& r, unsigned int& a, unsigned int& b) {
+      const long long i = base + lane;
+      r = 0;
+      a = 0u;
+      b = 0u;
+      if (i < pe) {
+        r = __ldg(rows + i);
+        if (QUANT) {
+          const uint16_t pr = __ldg(reinterpret_cast<const uint16_t*>(pairs) + i);
+          const unsigned int gq = (unsigned int)((int)(int8_t)(pr & 0xff) + g_lim), hq = (unsigned int)(pr >> 8);
+          if (PR)
+            a = ((unsigned int)r << 6) | (hq << 3) | gq;
+          else
+            a = gq | (hq << 8);
+        } else {
+          const int2 pr = __ldg(reinterpret_cast<const int2*>(pairs) + i);
+          a = (unsigned int)pr.x;
+          b = (unsigned int)pr.y;
+        }
+      }
+    };
+    if (c0 < pe) fetch(c0, nr, na, nb2);
+    for (; c0 < pe; c0 += stride) {
+      const int cr = nr;
+      const unsigned int ca = na, cb = nb2;
+      if (c0 + stride < pe) fetch(c0 + stride, nr, na, nb2);
+      const int n_in = pe - c0 >= 32 ? 32 : (int)(pe - c0);
+      if (n_in == 32) {
+#pragma unroll
+        for (int u0 = 0; u0 < 32; u0 += U) {
+          unsigned int bw[U], pa[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            int r;
+            pa[u] = __shfl_sync(0xffffffffu, ca, u0 + u);
+            if (PR)
+              r = (int)(pa[u] >> 6);
+            else
+              r = __shfl_sync(0xffffffffu, cr, u0 + u);
+            bw[u] = BinWord<NPL>::load(bcol + (size_t)(unsigned int)r * (unsigned int)Fp);
+          }
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            if (PR) {
+              add_row(bw[u], q_value(pa[u] & 7u, (pa[u] >> 3) & 7u), 0u);
+            } else if (QUANT) {
+              add_row(bw[u], q_value(pa[u] & 0xffu, pa[u] >> 8), 0u);
+            } else {
+              const unsigned int h = HPLANE ? __shfl_sync(0xffffffffu, cb, u0 + u) : 0u;
+              add_row(bw[u], f_value((int)pa[u]), h);
+            }
+          }
+        }
+      } else {
+        for (int u = 0; u < n_in; ++u) {
+          const unsigned int a = __shfl_sync(0xffffffffu, ca, u);
+          const int r = PR ? (int)(a >> 6) : __shfl_sync(0xffffffffu, cr, u);
+          const unsigned int h = HPLANE ? __shfl_sync(0xffffffffu, cb, u) : 0u;
+          const unsigned int bw = BinWord<NPL>::load(bcol + (size_t)(unsigned int)r * (unsigned int)Fp);
+          if (PR)
+            add_row(bw, q_value(a & 7u, (a >> 3) & 7u), 0u);
+          else if (QUANT)
+            add_row(bw, q_value(a & 0xffu, a >> 8), 0u);
+          else
+            add_row(bw, f_value((int)a), h);
+        }
+      }
+    }
+    cluster.sync();
+    const int slice = (CELLS + cs - 1) / cs;
+    const int m0 = crank * slice;
+    const int m1 = m0 + slice < CELLS ? m0 + slice : CELLS;
+    unsigned long long* c64 = reinterpret_cast<unsigned long long*>(smem);
+    unsigned int* c32 = reinterpret_cast<unsigned int*>(smem + 8 * CELLS);
+    for (int c = m0 + threadIdx.x; c < m1; c += blockDim.x) {
+      const int l = c & 31;
+      const int jb = c >> 5;
+      const int j = jb / kHistBinsPad;
+      const int bin = jb % kHistBinsPad;
+      const int f = f0 + l * NPL + j;
+      if (f >= F || bin >= B) continue;
+      long long g = 0, h = 0, cnt = 0;
+      for (int rk = 0; rk < cs; ++rk) {
+        const unsigned long long x = cluster.map_shared_rank(c64, rk)[c];
+        if (QUANT) {
+          g += (long long)(x & ((1ull << 22) - 1));
+          cnt += (long long)((x >> 22) & ((1ull << 21) - 1));
+          h += (long long)(x >> 43);
+        } else {
+          const long long gg = ((long long)(x << 24)) >> 24;  // sign-extend the low 40 bits
+          g += gg;
+          cnt += (long long)((x - (unsigned long long)gg) >> 40);
+          if (HPLANE) h += (long long)cluster.map_shared_rank(c32, rk)[c];
+        }
+      }
+      if (cnt == 0) continue;
+      if (QUANT) g -= (long long)g_lim * cnt;
+      int* cellp = hs + (f * 3) * B + bin;
+      atomicAdd(cellp, (int)g);
+      if (LAYOUT != HL_FCH64) atomicAdd(cellp + B, (int)h);
+      atomicAdd(cellp + 2 * B, (int)cnt);
+    }
+    cluster.sync();
+  }
+}
+
+// hist_segment for the fixed-point mode with the 2^52 bound (HL_W52,
+// HL_W52CH): Int64 gradient and hessian values, 64-bit shared cells for g
+// (and h), a 32-bit count plane, Int64 global cells.  Same bank-per-lane
+// geometry as hist_segment64.  A precision mode: one row id and two 64-bit
+// values broadcast per row.
+template <int NPL, int LAYOUT>
+__device__ void hist_segment_w52(cooperative_groups::cluster_group& cluster, const BatchItem& P, long long seg_b,
+                                 long long seg_n, const uint8_t* __restrict__ bins_rm, int Fp, int F, int B,
+                                 const int* __restrict__ rows0, const int* __restrict__ rows1,
+                                 const void* __restrict__ pairs0, const void* __restrict__ pairs1, int* hs_words,
+                                 long long rows_per_flush, unsigned char* smem) {
+  constexpr bool CH = LAYOUT == HL_W52CH;
+  constexpr int FG = 32 * NPL;
+  constexpr int U = 4;
+  constexpr int CELLS = NPL * kHistBinsPad * 32;
+  constexpr int PLANES64 = CH ? 1 : 2;
+  constexpr int BYTES = CELLS * (8 * PLANES64 + 4);
+  long long* hs = reinterpret_cast<long long*>(hs_words);
+  const int cs = (int)cluster.num_blocks();
+  const int crank = (int)cluster.block_rank();
+  const long long sub = (seg_n + cs - 1) / cs;
+  const long long s = seg_b + crank * sub;
+  long long e = s + sub;
+  if (e > seg_b + seg_n) e = seg_b + seg_n;
+  const long long n_pass = (sub + rows_per_flush - 1) / rows_per_flush;
+  const int f0 = blockIdx.x * FG;
+  const int* rows = P.dst_buf ? rows1 : rows0;
+  const longlong2* pairs = reinterpret_cast<const longlong2*>(P.dst_buf ? pairs1 : pairs0);
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int n_warps = blockDim.x >> 5;
+  const bool lane_ok = f0 + lane * NPL < Fp;
+  const uint8_t* bcol = bins_rm + (lane_ok ? f0 + lane * NPL : 0);
+  const uint32_t gbase = (uint32_t)__cvta_generic_to_shared(smem) + 8u * lane;
+  const uint32_t cbase = (uint32_t)__cvta_generic_to_shared(smem) + 8u * PLANES64 * CELLS + 4u * lane;
+  auto add_row = [&](unsigned int bw, long long g, long long h) {
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+      const uint32_t b = (bw >> (8 * j)) & 0xffu;
+      shared_red_add64(gbase + (b << 8) + j * (256u * 256u), (unsigned long long)g);
+      if (!CH) shared_red_add64(gbase + 8u * CELLS + (b << 8) + j * (256u * 256u), (unsigned long long)h);
+      shared_red_add(cbase + (b << 7) + j * (128u * 256u), 1u);
+    }
+  };
+  for (long long pass = 0; pass < n_pass; ++pass) {
+    const long long ps = s + pass * rows_per_flush;
+    const long long pe = ps + rows_per_flush < e ? ps + rows_per_flush : e;
+    for (int c = threadIdx.x; c < BYTES / 16; c += blockDim.x) reinterpret_cast<uint4*>(smem)[c] = make_uint4(0, 0, 0, 0);
+    __syncthreads();
+    const long long stride = (long long)n_warps * 32;
+    for (long long c0 = ps + (long long)warp * 32; c0 < pe; c0 += stride) {
+      const long long i = c0 + lane;
+      int r = 0;
+      long long g = 0, h = 0;
+      if (i < pe) {
+        r = __ldg(rows + i);
+        const longlong2 pr = __ldg(pairs + i);
+        g = pr.x;
+        h = pr.y;
+      }
+      const int n_in = pe - c0 >= 32 ? 32 : (int)(pe - c0);
+      for (int u0 = 0; u0 < n_in; u0 += U) {
+        unsigned int bw[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int rr = __shfl_sync(0xffffffffu, r, (u0 + u) & 31);
+          bw[u] = u0 + u < n_in ? BinWord<NPL>::load(bcol + (size_t)(unsigned int)rr * (unsigned int)Fp) : 0u;
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const long long gg = __shfl_sync(0xffffffffu, g, (u0 + u) & 31);
+          const long long hh = CH ? 0ll : __shfl_sync(0xffffffffu, h, (u0 + u) & 31);
+          if (u0 + u < n_in) add_row(bw[u], gg, hh);
+        }
+      }
+    }
+    cluster.sync();
+    const int slice = (CELLS + cs - 1) / cs;
+    const int m0 = crank * slice;
+    const int m1 = m0 + slice < CELLS ? m0 + slice : CELLS;
+    const unsigned long long* g64 = reinterpret_cast<const unsigned long long*>(smem);
+    const unsigned int* c32 = reinterpret_cast<const unsigned int*>(smem + 8 * PLANES64 * CELLS);
+    for (int c = m0 + threadIdx.x; c < m1; c += blockDim.x) {
+      const int l = c & 31;
+      const int jb = c >> 5;
+      const int j = jb / kHistBinsPad;
+      const int bin = jb % kHistBinsPad;
+      const int f = f0 + l * NPL + j;
+      if (f >= F || bin >= B) continue;
+      unsigned long long g = 0, h = 0;
+      long long cnt = 0;
+      for (int rk = 0; rk < cs; ++rk) {
+        const unsigned long long* q = cluster.map_shared_rank(g64, rk);
+        g += q[c];
+        if (!CH) h += q[CELLS + c];
+        cnt += (long long)cluster.map_shared_rank(c32, rk)[c];
+      }
+      if (cnt == 0) continue;
+      unsigned long long* cellp = reinterpret_cast<unsigned long long*>(hs + (long long)(f * 3) * B + bin);
+      atomicAdd(cellp, g);
+      if (!CH) atomicAdd(cellp + B, h);
+      atomicAdd(cellp + 2 * B, (unsigned long long)cnt);
+    }
+    cluster.sync();
+  }
+}
+
 // CTAs of one feature group form clusters of CS along grid y.  The batch's
 // built rows, taken as one sequence (item after item), are split evenly among
 // ceil(rows / (min_rows_per_cta * CS)) clusters at most; a cluster whose share
@@ -852,10 +1164,20 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__
     built_range(P, b, c);
     const long long s0 = lo > acc ? lo : acc;
     const long long s1 = hi < acc + c ? hi : acc + c;
-    if (s1 > s0)
-      hist_segment<NPL, LAYOUT>(cluster, P, b + (s0 - acc), s1 - s0, bins_rm, Fp, F, B, rows0, rows1, pairs0,
-                                pairs1, hist + (long long)(work_base + P.work) * slot_cells, rows_per_flush, g_lim,
-                                p0);
+    if (s1 > s0) {
+      if constexpr (LAYOUT == HL_W52 || LAYOUT == HL_W52CH)
+        hist_segment_w52<NPL, LAYOUT>(cluster, P, b + (s0 - acc), s1 - s0, bins_rm, Fp, F, B, rows0, rows1, pairs0,
+                                      pairs1, hist + (long long)(work_base + P.work) * slot_cells, rows_per_flush,
+                                      smem_raw);
+      else if constexpr (hist_layout_is64(LAYOUT))
+        hist_segment64<NPL, LAYOUT>(cluster, P, b + (s0 - acc), s1 - s0, bins_rm, Fp, F, B, rows0, rows1, pairs0,
+                                    pairs1, hist + (long long)(work_base + P.work) * slot_cells, rows_per_flush,
+                                    g_lim, smem_raw);
+      else
+        hist_segment<NPL, LAYOUT>(cluster, P, b + (s0 - acc), s1 - s0, bins_rm, Fp, F, B, rows0, rows1, pairs0,
+                                  pairs1, hist + (long long)(work_base + P.work) * slot_cells, rows_per_flush, g_lim,
+                                  p0);
+    }
     acc += c;
   }
 }
@@ -1064,7 +1386,7 @@ __device__ __noinline__ double scan_candidate_gain(long long Dg, long long Dh, l
 constexpr int kScanWarps = 8;    // pairs per block
 constexpr int kBinsPerLane = 8;  // 32 x 8 = 256 bins at most
 
-template <bool COMPACT, bool EXCHANGE>
+template <bool COMPACT, bool EXCHANGE, bool WIDE = false>
 __global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan_t(TreeState* __restrict__ ts, int* __restrict__ hist,
                                                           long long slot_cells, const int* __restrict__ feats,
                                                           const int* __restrict__ missing_bin,
@@ -1072,7 +1394,8 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan_t(TreeState* __rest
                                                           const RoundScales* __restrict__ sc, ScanParams sp,
                                                           FeatBest* __restrict__ out, int work_base,
                                                           ChildRec* __restrict__ rec) {
-  __shared__ int s_cells[kScanWarps][3][256];  // categorical searches only
+  using CT = typename std::conditional<WIDE, long long, int>::type;  // histogram cell type
+  __shared__ CT s_cells[kScanWarps][3][256];  // categorical searches only
   const Batch& Bt = ts->batch;
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const long long pair = (long long)blockIdx.x * kScanWarps + wib;
@@ -1085,14 +1408,14 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan_t(TreeState* __rest
   const int B = sp.B;
   const int f = feats[j];
   const bool built = Bt.root || side == (P.built_is_left ? 0 : 1);
-  int* hs = hist + (long long)(built ? P.built_hist : P.sib_hist) * slot_cells + (long long)f * 3 * B;
-  const int* wk = hist + (long long)(work_base + P.work) * slot_cells + (long long)f * 3 * B;
+  CT* hs = reinterpret_cast<CT*>(hist + (long long)(built ? P.built_hist : P.sib_hist) * slot_cells) + (long long)f * 3 * B;
+  const CT* wk = reinterpret_cast<const CT*>(hist + (long long)(work_base + P.work) * slot_cells) + (long long)f * 3 * B;
   const int mode = sp.mode;
   const bool ch_fixed = sp.const_hess && mode == MODE_FIXED;
-  const int hq = ch_fixed ? sc->hq_const : 0;
+  const long long hq = ch_fixed ? (WIDE ? sc->hq_const64 : (long long)sc->hq_const) : 0;
   const int b0 = lane * kBinsPerLane;
   // built child: the (reduced) work slot; sibling: parent - built, in place
-  int vg[kBinsPerLane], vh[kBinsPerLane], vc[kBinsPerLane];
+  CT vg[kBinsPerLane], vh[kBinsPerLane], vc[kBinsPerLane];
   long long sg = 0, sh = 0, scn = 0;
 #pragma unroll
   for (int q = 0; q < kBinsPerLane; ++q) {
@@ -1101,7 +1424,7 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan_t(TreeState* __rest
     vh[q] = 0;
     vc[q] = 0;
     if (b < B) {
-      const int wg = wk[b], wh = wk[B + b], wc = wk[2 * B + b];
+      const CT wg = wk[b], wh = wk[B + b], wc = wk[2 * B + b];
       if (built) {
         vg[q] = wg;
         vh[q] = wh;
@@ -1114,7 +1437,7 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan_t(TreeState* __rest
       hs[b] = vg[q];
       hs[B + b] = vh[q];
       hs[2 * B + b] = vc[q];
-      if (ch_fixed) vh[q] = (int)((long long)hq * vc[q]);
+      if (ch_fixed) vh[q] = (CT)(hq * (long long)vc[q]);
     }
     sg += vg[q];
     sh += vh[q];
@@ -1151,7 +1474,7 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan_t(TreeState* __rest
   fb.flags = 0;
   fb.n_left = 0;
   fb.bits[0] = fb.bits[1] = fb.bits[2] = fb.bits[3] = 0;
-  int(*cw)[256] = s_cells[wib];
+  CT(*cw)[256] = s_cells[wib];
   if (n_cats[f] >= 0) {
 #pragma unroll
     for (int q = 0; q < kBinsPerLane; ++q) {
@@ -1255,7 +1578,7 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan_t(TreeState* __rest
   const int n_scan = mb >= 0 ? mb : B;
   long long mg = 0, mh = 0, mc = 0;
   if (mb >= 0) {
-    int xg = 0, xh = 0, xc = 0;
+    CT xg = 0, xh = 0, xc = 0;
 #pragma unroll
     for (int q = 0; q < kBinsPerLane; ++q)
       if (b0 + q == mb) {

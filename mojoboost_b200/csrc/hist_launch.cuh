@@ -94,6 +94,16 @@ void launch_hist_t(const HistLaunch& hl, cudaStream_t st, const Batch* batch, co
     case HL_FIXED * 8 + 1: { constexpr int V = 1, L = HL_FIXED; EXPR; } break;                        \
     case HL_FIXED * 8 + 2: { constexpr int V = 2, L = HL_FIXED; EXPR; } break;                        \
     case HL_FIXED * 8 + 4: { constexpr int V = 4, L = HL_FIXED; EXPR; } break;                        \
+    case HL_Q64 * 8 + 1: { constexpr int V = 1, L = HL_Q64; EXPR; } break;                            \
+    case HL_Q64 * 8 + 2: { constexpr int V = 2, L = HL_Q64; EXPR; } break;                            \
+    case HL_Q64R * 8 + 1: { constexpr int V = 1, L = HL_Q64R; EXPR; } break;                          \
+    case HL_Q64R * 8 + 2: { constexpr int V = 2, L = HL_Q64R; EXPR; } break;                          \
+    case HL_FCH64 * 8 + 1: { constexpr int V = 1, L = HL_FCH64; EXPR; } break;                        \
+    case HL_FCH64 * 8 + 2: { constexpr int V = 2, L = HL_FCH64; EXPR; } break;                        \
+    case HL_F64H * 8 + 1: { constexpr int V = 1, L = HL_F64H; EXPR; } break;                          \
+    case HL_F64H * 8 + 2: { constexpr int V = 2, L = HL_F64H; EXPR; } break;                          \
+    case HL_W52 * 8 + 1: { constexpr int V = 1, L = HL_W52; EXPR; } break;                            \
+    case HL_W52CH * 8 + 1: { constexpr int V = 1, L = HL_W52CH; EXPR; } break;                        \
     default: throw std::runtime_error("bad histogram layout");                                         \
   }
 
@@ -111,7 +121,27 @@ inline void launch_hist(const HistLaunch& hl, cudaStream_t st, const Batch* batc
 
 // Cell layout and flush span for a fit.  quant_bins: the int8 gradient range
 // (|g| <= quant_bins / 2, h <= quant_bins); 0 for the fixed-point modes.
-inline void choose_hist_layout(HistLaunch& hl, int mode, bool const_h, int quant_bins) {
+inline void choose_hist_layout(HistLaunch& hl, int mode, bool const_h, int quant_bins, bool wide = false) {
+  if (wide) {
+    hl.layout = const_h ? HL_W52CH : HL_W52;
+    hl.rows_per_flush = 1ll << 40;  // Int64 cells: sums stay below 2^53, counts below 2^31 per CTA
+    return;
+  }
+  // 64-bit cells (one shared atomic per row and feature) unless
+  // MOJOTREES_HIST_CELLS=32 asks for the 32-bit layouts
+  const char* cells_env = getenv("MOJOTREES_HIST_CELLS");
+  if (!(cells_env && atoi(cells_env) == 32)) {
+    if (mode == MODE_QUANT) {
+      const long long gl = quant_bins / 2, hlim = quant_bins;
+      hl.layout = HL_Q64;
+      hl.rows_per_flush = std::min(std::min(((1ll << 22) - 1) / (2 * gl), ((1ll << 21) - 1) / hlim), (1ll << 21) - 1);
+      hl.g_lim = (int)gl;
+    } else {
+      hl.layout = const_h ? HL_FCH64 : HL_F64H;
+      hl.rows_per_flush = (1ll << 24) - 1;
+    }
+    return;
+  }
   if (mode == MODE_QUANT) {
     const long long gl = quant_bins / 2, hlim = quant_bins;
     const long long rpf16 = std::min<long long>(65535 / (2 * gl), 65535 / hlim);
@@ -137,12 +167,12 @@ inline void choose_hist_layout(HistLaunch& hl, int mode, bool const_h, int quant
 // n_rows > 0 (row ids below it) lets 16-bit packed cells with narrow
 // quantizers use HL_QUANT16R; MOJOTREES_HIST_NO_ROWPACK turns that off.
 inline HistLaunch choose_hist_launch(int mode, bool const_h, int quant_bins, int B, int Fp, int n_sm,
-                                     long long n_rows = 0) {
+                                     long long n_rows = 0, bool wide = false) {
   HistLaunch hl;
-  choose_hist_layout(hl, mode, const_h, quant_bins);
-  if (hl.layout == HL_QUANT16 && n_rows > 0 && n_rows <= (1ll << 26) && quant_bins <= 7
+  choose_hist_layout(hl, mode, const_h, quant_bins, wide);
+  if ((hl.layout == HL_QUANT16 || hl.layout == HL_Q64) && n_rows > 0 && n_rows <= (1ll << 26) && quant_bins <= 7
       && !getenv("MOJOTREES_HIST_NO_ROWPACK"))
-    hl.layout = HL_QUANT16R;
+    hl.layout = hl.layout == HL_Q64 ? HL_Q64R : HL_QUANT16R;
   // MOJOTREES_HIST_SMEM_KB / MOJOTREES_HIST_CLUSTER override the shared-memory
   // budget per CTA and the largest cluster size (tuning knobs)
   size_t budget = 220 * 1024;
@@ -154,6 +184,8 @@ inline HistLaunch choose_hist_launch(int mode, bool const_h, int quant_bins, int
   hl.groups = 1 << 30;
   for (int npl : {1, 2, 4}) {
     if ((hl.layout == HL_QUANT16 || hl.layout == HL_QUANT16R) && npl == 1) continue;
+    if (hist_layout_is64(hl.layout) && npl == 4) continue;
+    if ((hl.layout == HL_W52 || hl.layout == HL_W52CH) && npl != 1) continue;
     int groups = (Fp + 32 * npl - 1) / (32 * npl);
     if ((smem_of(npl) <= budget || hl.npl == 0) && groups < hl.groups) {
       hl.npl = npl;

@@ -51,7 +51,8 @@ struct TrainConfig {
   int num_grad_quant_bins = 4;
   int quant_seed = 11;
   int gpu_device_id = -1;      // -1: current device
-  double dp_timeout_seconds = 300.0;  // data-parallel fits: bound of every wait on the other ranks
+  double dp_timeout_seconds = 300.0;
+  bool hist_int64 = false;     // fixed-point histograms with the 2^52 bound and Int64 cells  // data-parallel fits: bound of every wait on the other ranks
   bool keep_training_scores = false;
   bool profile_phases = false;    // CUDA events around every kernel phase
   bool profile_histogram = false; // CUDA events around the histogram launches only

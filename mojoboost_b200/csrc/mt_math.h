@@ -148,3 +148,10 @@ MT_HD float mt_fixed_point_scale(double total) {
   double t = total < 1e-12 ? 1e-12 : total;
   return (float)mt_pow2_floor(1073741824.0 / t);
 }
+
+// The same rule with the bound 2^52 (Int64 cells; every sum of quantized
+// values stays below 2^53, so its Float64 dequantization is exact).
+MT_HD float mt_fixed_point_scale52(double total) {
+  double t = total < 1e-12 ? 1e-12 : total;
+  return (float)mt_pow2_floor(4503599627370496.0 / t);
+}

@@ -129,6 +129,8 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   if (cfg.objective == OBJECTIVE_MULTICLASS && (K < 2 || K > 64))
     throw Unsupported("num_class must be in [2, 64] on the device path");
   const int mode = cfg.use_quantized_grad ? MODE_QUANT : MODE_FIXED;
+  // fixed point with the 2^52 bound and Int64 cells (gpu_histogram_precision=int64)
+  const bool wide = mode == MODE_FIXED && cfg.hist_int64;
   if (mode == MODE_QUANT && (cfg.num_grad_quant_bins < 2 || cfg.num_grad_quant_bins > 254 ||
                              cfg.num_grad_quant_bins % 2 != 0))
     throw Unsupported("num_grad_quant_bins must be even and in [2, 254] on the device path");
@@ -295,7 +297,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   MTB_CUDA(cudaMemcpyAsync(d_missing.p, in.missing_bin, sizeof(int) * F, cudaMemcpyHostToDevice, st));
   MTB_CUDA(cudaMemcpyAsync(d_ncats.p, in.n_cats, sizeof(int) * F, cudaMemcpyHostToDevice, st));
 
-  const size_t pair_bytes = mode == MODE_QUANT ? 2 : 8;
+  const size_t pair_bytes = mode == MODE_QUANT ? 2 : wide ? 16 : 8;
   DevBuf<int> d_rows0, d_rows1;
   DevBuf<unsigned char> d_pairs0, d_pairs1;
   d_rows0.alloc(N);
@@ -350,7 +352,9 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   const char* dpx = getenv("MOJOTREES_DP_EXCHANGE");
   const bool dp_feature = coll && world > 1 && dpx && std::string(dpx) == "feature";
   const int Fb = dp_feature ? (F + world - 1) / world : F;  // feature ids a rank owns
-  const long long slot_cells = (long long)(dp_feature ? Fb * world : F) * 3 * B;
+  // cells of one histogram slot, in int32 words (an Int64 cell takes two)
+  const long long cell_words = wide ? 2 : 1;
+  const long long slot_cells = (long long)(dp_feature ? Fb * world : F) * 3 * B * cell_words;
   // Leaves expanded per iteration (speculative leaf batching); 1 grows one
   // split per iteration as the reference does.  MOJOTREES_BATCH overrides.
   int batch_cap = 32;
@@ -382,7 +386,8 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   // Histogram launch geometry: as many features per CTA as one SM's shared
   // memory holds, row chunks sized to fill every SM, CTAs of a feature group
   // in clusters of up to 8 that merge through DSMEM.
-  HistLaunch hl = choose_hist_launch(mode, const_h, mode == MODE_QUANT ? cfg.num_grad_quant_bins : 0, B, Fp, n_sm, N);
+  HistLaunch hl = choose_hist_launch(mode, const_h, mode == MODE_QUANT ? cfg.num_grad_quant_bins : 0, B, Fp, n_sm, N,
+                                     wide);
   // partition geometry (MOJOTREES_PART_ITEMS / MOJOTREES_PART_BLOCKS_PER_SM
   // override the rows per thread of a tile and the resident blocks per SM)
   int part_bps = 4;
@@ -398,6 +403,10 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     k_partition<uint16_t, IT><<<part_grid, part_threads, 0, st>>>(                                        \
         d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<uint16_t*>(d_pairs0.p),            \
         reinterpret_cast<uint16_t*>(d_pairs1.p), d_hist.p, slot_cells, work_base);                        \
+  else if (wide)                                                                                          \
+    k_partition<longlong2, IT><<<part_grid, part_threads, 0, st>>>(                                       \
+        d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<longlong2*>(d_pairs0.p),           \
+        reinterpret_cast<longlong2*>(d_pairs1.p), d_hist.p, slot_cells, work_base);                       \
   else                                                                                                    \
     k_partition<int2, IT><<<part_grid, part_threads, 0, st>>>(                                            \
         d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<int2*>(d_pairs0.p),                \
@@ -479,9 +488,15 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   };
   // the built children's cells summed over every device's rows (exact int32)
   auto reduce_work = [&]() {
-    if (dp_feature)
+    if (dp_feature && wide)
+      coll->reduce_scatter_slots_i64(reinterpret_cast<long long*>(d_hist.p + (size_t)work_base * slot_cells),
+                                     (size_t)batch_cap, (size_t)slot_cells / 2, (size_t)Fb * 3 * B, st);
+    else if (dp_feature)
       coll->reduce_scatter_slots_i32(d_hist.p + (size_t)work_base * slot_cells, (size_t)batch_cap,
                                      (size_t)slot_cells, (size_t)Fb * 3 * B, st);
+    else if (coll && wide)
+      coll->allreduce_sum_i64(reinterpret_cast<long long*>(d_hist.p + (size_t)work_base * slot_cells),
+                              (size_t)slot_cells / 2 * batch_cap, st);
     else if (coll)
       coll->allreduce_sum_i32(d_hist.p + (size_t)work_base * slot_cells, (size_t)slot_cells * batch_cap, st);
   };
@@ -564,12 +579,15 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       // trees is detected here (the bounded wait aborts the communicator),
       // with none of this rank's work queued behind the aborted collective.
       if (coll) coll->sync(st);
-      k_scales<<<1, 32, 0, st>>>(d_sc.p, tot_g, tot_h, mode, const_h ? 1 : 0, cfg.num_grad_quant_bins);
+      k_scales<<<1, 32, 0, st>>>(d_sc.p, tot_g, tot_h, mode, const_h ? 1 : 0, cfg.num_grad_quant_bins, wide ? 1 : 0);
       uint64_t gs = mt_quant_stream(cfg.quant_seed, it, k, 0);
       uint64_t hs = mt_quant_stream(cfg.quant_seed, it, k, 1);
       if (mode == MODE_QUANT)
         k_quantize<MODE_QUANT><<<grid256, 256, 0, st>>>(d_g.p, d_h.p, N, in.row_offset, d_sc.p, const_h, gs, hs,
                                                          d_rows0.p, d_pairs0.p);
+      else if (wide)
+        k_quantize<MODE_FIXED, true><<<grid256, 256, 0, st>>>(d_g.p, d_h.p, N, in.row_offset, d_sc.p, const_h, gs, hs,
+                                                               d_rows0.p, d_pairs0.p);
       else
         k_quantize<MODE_FIXED><<<grid256, 256, 0, st>>>(d_g.p, d_h.p, N, in.row_offset, d_sc.p, const_h, gs, hs,
                                                          d_rows0.p, d_pairs0.p);
@@ -641,14 +659,16 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
         reduce_work();
         timer.begin(&stats.scan_ms);
         if (!dp_feature) {
-          (scan_compact ? k_scan_t<true, false> : k_scan_t<false, false>)<<<scan_grid, kScanWarps * 32, 0, st>>>(
+          (wide ? (scan_compact ? k_scan_t<true, false, true> : k_scan_t<false, false, true>)
+                : (scan_compact ? k_scan_t<true, false> : k_scan_t<false, false>))<<<scan_grid, kScanWarps * 32, 0, st>>>(
               d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p, d_ncats.p, d_sc.p, sp, d_fb.p, work_base,
               nullptr);
         } else {
           // this rank's per-child bests -> every rank's -> the merged leaves
           MTB_CUDA(cudaMemsetAsync(d_rec.p, 0, sizeof(ChildRec) * 2 * (size_t)batch_cap, st));
           if (n_active > 0)
-            (scan_compact ? k_scan_t<true, true> : k_scan_t<false, true>)<<<scan_grid, kScanWarps * 32, 0, st>>>(
+            (wide ? (scan_compact ? k_scan_t<true, true, true> : k_scan_t<false, true, true>)
+                  : (scan_compact ? k_scan_t<true, true> : k_scan_t<false, true>))<<<scan_grid, kScanWarps * 32, 0, st>>>(
                 d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p, d_ncats.p, d_sc.p, sp, d_fb.p, work_base,
                 d_rec.p);
           coll->allgather_bytes(d_rec.p, d_rec_all.p, sizeof(ChildRec) * 2 * (size_t)batch_cap, st);

@@ -100,7 +100,11 @@ typedef struct {
 
 namespace {
 
-enum { MODE_CPU = 0, MODE_FIXED = 1, MODE_QUANT = 2 };
+enum { MODE_CPU = 0, MODE_FIXED = 1, MODE_QUANT = 2, MODE_FIXED52 = 3 };
+// MODE_FIXED52: the fixed-point mode with the scale bound raised from 2^30 to
+// 2^52 (Int64 cells): every dequantized sum is still exact in Float64, and the
+// per-row rounding error drops to 2^-53 of the |g| total.
+inline bool fixed_point(int mode) { return mode == MODE_FIXED || mode == MODE_FIXED52; }
 enum { OBJ_L2 = 0, OBJ_LOGISTIC = 1, OBJ_SOFTMAX = 2 };
 
 struct Data {
@@ -252,7 +256,15 @@ void prepare_integer_round(const Ctx& c, RoundState& st, int round_index, int cl
   int64_t n = c.d.n;
   st.qg.assign((size_t)n, 0);
   st.qh.assign((size_t)n, 0);
-  if (c.p.mode == MODE_FIXED) {
+  if (c.p.mode == MODE_FIXED52) {
+    st.gsf = mt_fixed_point_scale52(pow2_abs_total(st.grad));
+    st.hsf = mt_fixed_point_scale52(pow2_abs_total(st.hess));
+    const int64_t hq_const = (int64_t)nearbyint(1.0 * (double)st.hsf);
+    for (int64_t r = 0; r < n; ++r) {
+      st.qg[r] = (int64_t)nearbyint(st.grad[r] * (double)st.gsf);
+      st.qh[r] = st.const_h ? hq_const : (int64_t)nearbyint(st.hess[r] * (double)st.hsf);
+    }
+  } else if (c.p.mode == MODE_FIXED) {
     // histogram_gpu.mojo:1199 scale refresh; quantized_gradient.mojo:908 rule;
     // histogram.mojo:3624-3637 per-row Int32(round(x_f32 * s_f32)), ties to even.
     st.gsf = mt_fixed_point_scale(pow2_abs_total(st.grad));
@@ -293,7 +305,7 @@ void prepare_integer_round(const Ctx& c, RoundState& st, int round_index, int cl
 void dequantize(const Ctx& c, const RoundState& st, Hist& h, const std::vector<int>& feats) {
   int B = c.d.B;
   double g_inv, h_inv;
-  if (c.p.mode == MODE_FIXED) {
+  if (fixed_point(c.p.mode)) {
     g_inv = 1.0 / (double)st.gsf;
     h_inv = 1.0 / (double)st.hsf;
   } else {

@@ -11,7 +11,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 ORACLE_SO = os.path.join(ROOT, "oracle", "liboracle.so")
 
-MODE_CPU, MODE_FIXED, MODE_QUANT = 0, 1, 2
+MODE_CPU, MODE_FIXED, MODE_QUANT, MODE_FIXED52 = 0, 1, 2, 3
 OBJ_L2, OBJ_LOGISTIC, OBJ_SOFTMAX = 0, 1, 2
 
 

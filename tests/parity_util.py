@@ -47,7 +47,9 @@ def oracle_kwargs(p):
     kw = dict(objective=OBJ[p["objective"]], n_classes=p.get("num_class", 1), num_rounds=p["num_iterations"],
               learning_rate=p["learning_rate"], num_leaves=p["num_leaves"],
               min_data_in_leaf=p["min_data_in_leaf"],
-              mode=oa.MODE_QUANT if p.get("use_quantized_grad") else oa.MODE_FIXED, exp_kind=1)
+              mode=(oa.MODE_QUANT if p.get("use_quantized_grad")
+                    else oa.MODE_FIXED52 if str(p.get("gpu_histogram_precision", "int32")) == "int64"
+                    else oa.MODE_FIXED), exp_kind=1)
     for k in ("feature_fraction", "max_cat_to_onehot", "max_cat_threshold", "cat_smooth", "cat_l2",
               "min_data_per_group", "lambda_l2", "lambda_l1"):
         if k in p:
@@ -78,3 +80,40 @@ def assert_models_identical(gm, om, n_rows, check_raw=True):
         raw = gm.training_scores(n_rows)
         np.testing.assert_array_equal(raw.view(np.uint64), np.ravel(om.raw).view(np.uint64),
                                       err_msg="training raw scores (bits)")
+
+
+def fp_tolerance_report(gm, om, n_rows, gain_rtol=1e-5, pred_rms=1e-5):
+    """Compare a device fit with the oracle's Float64 CPU path (the reference's
+    own device=cpu arithmetic) within floating-point tolerances: identical tree
+    structure, split gains within gain_rtol relative, training raw scores
+    within pred_rms RMS.  Returns a list of failure messages (empty = pass);
+    a structural difference names the first divergent node and both gains, so
+    a flipped near-tie is told apart from an error."""
+    fails = []
+    if gm.num_trees != om.n_trees:
+        return [f"tree count {gm.num_trees} vs {om.n_trees}"]
+    worst = 0.0
+    for t in range(om.n_trees):
+        g = gm.tree(t)
+        nn = int(om.n_nodes[t])
+        if len(g["feature"]) != nn:
+            fails.append(f"tree {t}: {len(g['feature'])} nodes vs {nn}")
+            continue
+        for i in range(nn):
+            same = (g["feature"][i] == om.feature[t, i] and g["threshold_bin"][i] == om.threshold_bin[t, i]
+                    and g["left"][i] == om.left[t, i] and g["right"][i] == om.right[t, i])
+            if not same:
+                fails.append(f"tree {t} node {i}: split (feature {g['feature'][i]}, bin {g['threshold_bin'][i]}, "
+                             f"gain {g['gain'][i]!r}) vs CPU (feature {om.feature[t, i]}, bin "
+                             f"{om.threshold_bin[t, i]}, gain {om.gain[t, i]!r})")
+                break
+            if om.feature[t, i] >= 0:
+                rel = abs(g["gain"][i] - om.gain[t, i]) / abs(om.gain[t, i])
+                worst = max(worst, rel)
+                if rel > gain_rtol:
+                    fails.append(f"tree {t} node {i}: gain {g['gain'][i]!r} vs CPU {om.gain[t, i]!r} (rel {rel:.3g})")
+    raw = gm.training_scores(n_rows)
+    rms = float(np.sqrt(np.mean((raw - np.ravel(om.raw)) ** 2)))
+    if rms > pred_rms:
+        fails.append(f"training raw scores: RMS difference {rms:.3g} > {pred_rms}")
+    return fails

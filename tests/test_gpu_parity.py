@@ -55,6 +55,18 @@ CASES = {
     "regularised_fixed": (dict(seed=17, n=30_000, f=16), dict(objective="regression", rounds=4, leaves=31, min_data=2,
                                                              extra={"lambda_l1": 0.5, "lambda_l2": 0.0,
                                                                     "min_sum_hessian_in_leaf": 40.0}), 255),
+    # fixed point with the 2^52 bound and Int64 cells (gpu_histogram_precision=int64)
+    "l2_fixed52": (dict(seed=19, n=50_000, f=28), dict(objective="regression", rounds=4, leaves=63,
+                                                      extra={"gpu_histogram_precision": "int64"}), 255),
+    "binary_fixed52": (dict(seed=20, n=30_000, f=20, kind="binary", nan_frac=0.05),
+                       dict(objective="binary", rounds=4, leaves=31, extra={"gpu_histogram_precision": "int64"}), 255),
+    "multiclass_fixed52": (dict(seed=21, n=20_000, f=12, kind="multiclass", n_classes=4),
+                           dict(objective="multiclass", rounds=3, leaves=15, n_classes=4,
+                                extra={"gpu_histogram_precision": "int64"}), 255),
+    "missing_cat_fixed52": (dict(seed=22, n=20_000, f=8, nan_frac=0.1, cat_cols=(2, 5), n_cat=12),
+                            dict(objective="regression", rounds=3, leaves=31,
+                                 extra={"categorical_feature": "2,5", "min_data_per_group": 20, "cat_smooth": 5.0,
+                                        "gpu_histogram_precision": "int64"}), 63),
     "regularised_quant": (dict(seed=18, n=30_000, f=16, kind="binary"),
                           dict(objective="binary", rounds=4, leaves=31, quant=True, min_data=2,
                                extra={"lambda_l1": 0.2, "lambda_l2": 0.0, "min_sum_hessian_in_leaf": 3.0}), 255),
