@@ -64,6 +64,11 @@ CONFIGS = {
     "c2": dict(index=1, rows=10_000_000, feats=100, objective="binary", K=1, max_bin=255, leaves=255, quant=True,
                scaling="weak", desc="configs[1]: binary logistic, quantized int8 gradients, 10M x 100 per GPU, "
                                     "max_bin 255, num_leaves 255"),
+    "c3": dict(index=2, rows=5_000_000, feats=408, objective="regression", K=1, max_bin=63, leaves=127,
+               quant=False, scaling="weak",
+               desc="configs[2]: regression, 5M x (400 numeric at 90% zeros + 8 categorical of cardinality 1000), "
+                    "max_bin 63, num_leaves 127, fixed-point gradients; run dense and unbundled (408 binned "
+                    "columns: no sparse histogram path, no exclusive feature bundling)"),
     "c4": dict(index=3, rows=4_000_000, feats=64, objective="multiclass", K=10, max_bin=255, leaves=63, quant=False,
                scaling="weak", desc="configs[3]: softmax K=10, 4M x 64, max_bin 255, num_leaves 63, fixed-point "
                                     "gradients (ten trees per round)"),
@@ -117,6 +122,26 @@ def make_c4(n_rows, seed=3, row_offset=0):
     return X, y
 
 
+def make_c3(n_rows, seed=2, row_offset=0):
+    """400 numeric features at 90% zeros (nonzeros ~ LogNormal(0, 1))
+    then 8 categorical features of cardinality 1000 drawn Zipf(1.1) (codes
+    above 1000 folded back); y = sum of per-category random effects ~ N(0, 1)
+    + 0.2 x the sum of the first 10 numeric features.  X is feature-major
+    float64."""
+    effects = np.random.default_rng(seed).standard_normal((8, 1000))
+    rng = np.random.default_rng([seed, row_offset])
+    X = np.zeros((408, n_rows))
+    for f in range(400):
+        nz = np.flatnonzero(rng.random(n_rows) < 0.1)
+        X[f, nz] = rng.lognormal(0.0, 1.0, size=nz.size)
+    y = 0.2 * X[:10].sum(axis=0)
+    for c in range(8):
+        codes = (rng.zipf(1.1, size=n_rows) - 1) % 1000
+        X[400 + c] = codes
+        y += effects[c][codes]
+    return X, y
+
+
 C5_BLOCK = 1_000_000
 
 
@@ -143,10 +168,17 @@ def make_c5(row_begin, row_end, seed=4):
     return bins, y
 
 
+def binning_params(cfg):
+    p = {"max_bin": CONFIGS[cfg]["max_bin"]}
+    if cfg == "c3":
+        p["categorical_feature"] = ",".join(str(f) for f in range(400, 408))
+    return p
+
+
 def params(rounds, quant=True, extra=None, cfg="c2"):
     c = CONFIGS[cfg]
-    p = {"objective": c["objective"], "num_iterations": rounds, "num_leaves": c["leaves"], "max_bin": c["max_bin"],
-         "min_data_in_leaf": 20, "learning_rate": 0.1, "use_quantized_grad": c["quant"] and quant}
+    p = {"objective": c["objective"], "num_iterations": rounds, "num_leaves": c["leaves"], "min_data_in_leaf": 20,
+         "learning_rate": 0.1, "use_quantized_grad": c["quant"] and quant, **binning_params(cfg)}
     if c["K"] > 1:
         p["num_class"] = c["K"]
     if extra:
@@ -249,17 +281,19 @@ def config_data(cfg, rank=0, world=1, rows=None):
         X, y = make_c1(n, row_offset=off)
     elif cfg == "c4":
         X, y = make_c4(n, row_offset=off)
+    elif cfg == "c3":
+        X, y = make_c3(n, row_offset=off)
     else:
         X, y = make_data(n, seed=1, row_offset=off)
     return None, X, y, off, n * world
 
 
-def oracle_bins(X, max_bin):
-    """Bins through the oracle's restatement of the reference binner (the CPU
-    arms never load this library)."""
+def oracle_bins(X, max_bin, categorical=()):
+    """Bins of the feature-major matrix X through the oracle's restatement of
+    the reference binner (the CPU arms never load this library)."""
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import oracle_api
-    return oracle_api.bin_dense(np.asarray(X, dtype=np.float64).T, max_bin=max_bin)
+    return oracle_api.bin_dense(np.asarray(X, dtype=np.float64).T, max_bin=max_bin, categorical=categorical)
 
 
 def cpu_fit_timed(cfg, bins, nb, y, mbin, ncat, warmup, steps):
@@ -300,7 +334,7 @@ def run_reference(args):
     c = CONFIGS[cfg]
     bins, X, y, _, n = config_data(cfg, rows=args.rows)
     if bins is None:
-        bins, mbin, ncat, nb = oracle_bins(X.T, c["max_bin"])
+        bins, mbin, ncat, nb = oracle_bins(X, c["max_bin"], list(range(400, 408)) if cfg == "c3" else ())
         del X
     else:
         mbin, ncat, nb = None, None, c["max_bin"]
@@ -340,7 +374,7 @@ def run_gpu(args):
         del X
         # one bin mapper for all shards: each rank fits it on its own rows
         # (weak scaling: the shards are statistically identical)
-        bins, mbin, ncat, nb = mb.bin_dense(X64, {"max_bin": c["max_bin"]})
+        bins, mbin, ncat, nb = mb.bin_dense(X64, binning_params(cfg))
     else:
         mbin, ncat, nb = None, None, c["max_bin"]
     n_local = bins.shape[1]

@@ -67,6 +67,8 @@ def _rank_main(rank, world, port, quant, n_shard, out_q, exchange="allreduce", e
     (True, N_SHARD, "allreduce", None), (False, N_SHARD, "allreduce", None), (True, N_SHARD_RAGGED, "allreduce", None),
     (True, N_SHARD, "feature", None), (False, N_SHARD, "feature", None), (True, N_SHARD_RAGGED, "feature", None),
     (True, N_SHARD, "feature", {"feature_fraction": 0.25}),
+    (False, N_SHARD, "allreduce", {"gpu_histogram_precision": "int64"}),
+    (False, N_SHARD, "feature", {"gpu_histogram_precision": "int64"}),
 ])
 def test_two_gpu_fit_equals_single_gpu(mtlib, quant, n_shard, exchange, extra):
     import torch.multiprocessing as mp
