@@ -91,6 +91,8 @@ const std::vector<std::pair<std::string, std::vector<std::string>>>& param_table
       {"categorical_feature", {"cat_feature", "categorical_column", "cat_column", "categorical_features"}},
       {"device_type", {"device"}},
       {"gpu_device_id", {"device_id"}},
+      {"gpu_histogram_precision", {}},
+      {"dp_timeout_seconds", {}},
       {"use_quantized_grad", {}},
       {"num_grad_quant_bins", {}},
       {"stochastic_rounding", {}},

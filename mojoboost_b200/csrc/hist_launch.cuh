@@ -41,6 +41,7 @@ struct HistLaunch {
   size_t smem = 0;
   long long rows_per_flush = 1ll << 40;
   int g_lim = 0;               // HL_QUANT16: offset making g non-negative
+  HistPack pk;                 // HL_QP / HL_QPR field geometry and error flag
 };
 
 cudaLaunchConfig_t hist_config(const HistLaunch& hl, int cs, int row_ctas, cudaStream_t st, cudaLaunchAttribute* attr) {
@@ -75,7 +76,7 @@ void launch_hist_t(const HistLaunch& hl, cudaStream_t st, const Batch* batch, co
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t lc = hist_config(hl, hl.cluster, hl.row_ctas, st, attr);
   MTB_CUDA(cudaLaunchKernelEx(&lc, k_hist<NPL, L>, batch, bins_rm, Fp, F, B, r0, r1, p0, p1, hist, slot_cells,
-                              hl.rows_per_flush, hl.g_lim, ws, hl.min_rows_per_cta));
+                              hl.rows_per_flush, hl.g_lim, ws, hl.min_rows_per_cta, hl.pk));
 }
 
 // Every (layout, features per lane) instance the launch geometry can pick.
@@ -94,14 +95,10 @@ void launch_hist_t(const HistLaunch& hl, cudaStream_t st, const Batch* batch, co
     case HL_FIXED * 8 + 1: { constexpr int V = 1, L = HL_FIXED; EXPR; } break;                        \
     case HL_FIXED * 8 + 2: { constexpr int V = 2, L = HL_FIXED; EXPR; } break;                        \
     case HL_FIXED * 8 + 4: { constexpr int V = 4, L = HL_FIXED; EXPR; } break;                        \
-    case HL_Q64 * 8 + 1: { constexpr int V = 1, L = HL_Q64; EXPR; } break;                            \
-    case HL_Q64 * 8 + 2: { constexpr int V = 2, L = HL_Q64; EXPR; } break;                            \
-    case HL_Q64R * 8 + 1: { constexpr int V = 1, L = HL_Q64R; EXPR; } break;                          \
-    case HL_Q64R * 8 + 2: { constexpr int V = 2, L = HL_Q64R; EXPR; } break;                          \
-    case HL_FCH64 * 8 + 1: { constexpr int V = 1, L = HL_FCH64; EXPR; } break;                        \
-    case HL_FCH64 * 8 + 2: { constexpr int V = 2, L = HL_FCH64; EXPR; } break;                        \
-    case HL_F64H * 8 + 1: { constexpr int V = 1, L = HL_F64H; EXPR; } break;                          \
-    case HL_F64H * 8 + 2: { constexpr int V = 2, L = HL_F64H; EXPR; } break;                          \
+    case HL_QP * 8 + 2: { constexpr int V = 2, L = HL_QP; EXPR; } break;                              \
+    case HL_QP * 8 + 4: { constexpr int V = 4, L = HL_QP; EXPR; } break;                              \
+    case HL_QPR * 8 + 2: { constexpr int V = 2, L = HL_QPR; EXPR; } break;                            \
+    case HL_QPR * 8 + 4: { constexpr int V = 4, L = HL_QPR; EXPR; } break;                            \
     case HL_W52 * 8 + 1: { constexpr int V = 1, L = HL_W52; EXPR; } break;                            \
     case HL_W52CH * 8 + 1: { constexpr int V = 1, L = HL_W52CH; EXPR; } break;                        \
     default: throw std::runtime_error("bad histogram layout");                                         \
@@ -121,25 +118,38 @@ inline void launch_hist(const HistLaunch& hl, cudaStream_t st, const Batch* batc
 
 // Cell layout and flush span for a fit.  quant_bins: the int8 gradient range
 // (|g| <= quant_bins / 2, h <= quant_bins); 0 for the fixed-point modes.
-inline void choose_hist_layout(HistLaunch& hl, int mode, bool const_h, int quant_bins, bool wide = false) {
+// HL_QP field geometry for a quantizer of quant_bins (|g| <= q/2, h <= q):
+// the widest count field whose g and h sums still fit the word; false when
+// the count field would be narrower than 7 bits (spills every 32 rows or less).
+inline bool pack_geometry(int quant_bins, HistPack& pk) {
+  const long long m = std::max<long long>(quant_bins, 1);  // per-row maximum of g + g_lim and of h
+  for (int c = 10; c >= 7; --c) {
+    const long long top = m * ((1ll << c) - 1);
+    int w = 0;
+    while ((1ll << w) <= top) ++w;
+    if (c + 2 * w <= 32) {
+      pk.cbits = c;
+      pk.wbits = w;
+      pk.spill = 1u << (c - 2);
+      pk.guard = (1u << c) - (1u << (c - 3));
+      return true;
+    }
+  }
+  return false;
+}
+
+inline void choose_hist_layout(HistLaunch& hl, int mode, bool const_h, int quant_bins, bool wide = false,
+                               int* pack_err = nullptr) {
+  if (mode == MODE_QUANT && pack_err && !getenv("MOJOTREES_HIST_NO_PACKED") && pack_geometry(quant_bins, hl.pk)) {
+    hl.layout = HL_QP;
+    hl.pk.err = pack_err;
+    hl.g_lim = quant_bins / 2;
+    hl.rows_per_flush = 1ll << 40;  // the spills keep every field in range
+    return;
+  }
   if (wide) {
     hl.layout = const_h ? HL_W52CH : HL_W52;
     hl.rows_per_flush = 1ll << 40;  // Int64 cells: sums stay below 2^53, counts below 2^31 per CTA
-    return;
-  }
-  // 64-bit cells (one shared atomic per row and feature) unless
-  // MOJOTREES_HIST_CELLS=32 asks for the 32-bit layouts
-  const char* cells_env = getenv("MOJOTREES_HIST_CELLS");
-  if (!(cells_env && atoi(cells_env) == 32)) {
-    if (mode == MODE_QUANT) {
-      const long long gl = quant_bins / 2, hlim = quant_bins;
-      hl.layout = HL_Q64;
-      hl.rows_per_flush = std::min(std::min(((1ll << 22) - 1) / (2 * gl), ((1ll << 21) - 1) / hlim), (1ll << 21) - 1);
-      hl.g_lim = (int)gl;
-    } else {
-      hl.layout = const_h ? HL_FCH64 : HL_F64H;
-      hl.rows_per_flush = (1ll << 24) - 1;
-    }
     return;
   }
   if (mode == MODE_QUANT) {
@@ -166,13 +176,15 @@ inline void choose_hist_layout(HistLaunch& hl, int mode, bool const_h, int quant
 // clusters of up to 8 that merge through DSMEM.
 // n_rows > 0 (row ids below it) lets 16-bit packed cells with narrow
 // quantizers use HL_QUANT16R; MOJOTREES_HIST_NO_ROWPACK turns that off.
+// pack_err: device int the packed-cell kernels set on a guard hit; without
+// it the packed layouts are not used.
 inline HistLaunch choose_hist_launch(int mode, bool const_h, int quant_bins, int B, int Fp, int n_sm,
-                                     long long n_rows = 0, bool wide = false) {
+                                     long long n_rows = 0, bool wide = false, int* pack_err = nullptr) {
   HistLaunch hl;
-  choose_hist_layout(hl, mode, const_h, quant_bins, wide);
-  if ((hl.layout == HL_QUANT16 || hl.layout == HL_Q64) && n_rows > 0 && n_rows <= (1ll << 26) && quant_bins <= 7
+  choose_hist_layout(hl, mode, const_h, quant_bins, wide, pack_err);
+  if ((hl.layout == HL_QUANT16 || hl.layout == HL_QP) && n_rows > 0 && n_rows <= (1ll << 26) && quant_bins <= 7
       && !getenv("MOJOTREES_HIST_NO_ROWPACK"))
-    hl.layout = hl.layout == HL_Q64 ? HL_Q64R : HL_QUANT16R;
+    hl.layout = hl.layout == HL_QP ? HL_QPR : HL_QUANT16R;
   // MOJOTREES_HIST_SMEM_KB / MOJOTREES_HIST_CLUSTER override the shared-memory
   // budget per CTA and the largest cluster size (tuning knobs)
   size_t budget = 220 * 1024;
@@ -183,8 +195,9 @@ inline HistLaunch choose_hist_launch(int mode, bool const_h, int quant_bins, int
   hl.npl = 0;
   hl.groups = 1 << 30;
   for (int npl : {1, 2, 4}) {
-    if ((hl.layout == HL_QUANT16 || hl.layout == HL_QUANT16R) && npl == 1) continue;
-    if (hist_layout_is64(hl.layout) && npl == 4) continue;
+    if ((hl.layout == HL_QUANT16 || hl.layout == HL_QUANT16R || hl.layout == HL_QP || hl.layout == HL_QPR) &&
+        npl == 1)
+      continue;
     if ((hl.layout == HL_W52 || hl.layout == HL_W52CH) && npl != 1) continue;
     int groups = (Fp + 32 * npl - 1) / (32 * npl);
     if ((smem_of(npl) <= budget || hl.npl == 0) && groups < hl.groups) {

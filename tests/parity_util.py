@@ -6,9 +6,11 @@ import oracle_api as oa
 OBJ = {"regression": oa.OBJ_L2, "binary": oa.OBJ_LOGISTIC, "multiclass": oa.OBJ_SOFTMAX}
 
 
-def make_data(seed, n, f, kind="regression", n_classes=3, nan_frac=0.0, cat_cols=(), n_cat=12):
+def make_data(seed, n, f, kind="regression", n_classes=3, nan_frac=0.0, cat_cols=(), n_cat=12, zero_frac=0.0):
     rng = np.random.default_rng(seed)
     X = rng.normal(size=(n, f))
+    if zero_frac > 0:  # features 1.. are mostly one value (a dominant bin)
+        X[:, 1:][rng.random((n, f - 1)) < zero_frac] = 0.0
     for c in cat_cols:
         X[:, c] = rng.integers(0, n_cat, size=n).astype(np.float64)
     if nan_frac > 0:

@@ -55,6 +55,15 @@ CASES = {
     "regularised_fixed": (dict(seed=17, n=30_000, f=16), dict(objective="regression", rounds=4, leaves=31, min_data=2,
                                                              extra={"lambda_l1": 0.5, "lambda_l2": 0.0,
                                                                     "min_sum_hessian_in_leaf": 40.0}), 255),
+    # packed 32-bit cells with spills: quantizer widths 2 and 6 (other field
+    # geometries), and features with a dominant bin (a cell takes most rows,
+    # so its count field spills to the global cells many times per launch)
+    "binary_quant2": (dict(seed=23, n=60_000, f=24, kind="binary"),
+                      dict(objective="binary", rounds=3, leaves=63, quant=True, extra={"num_grad_quant_bins": 2}), 255),
+    "binary_quant6": (dict(seed=24, n=60_000, f=24, kind="binary"),
+                      dict(objective="binary", rounds=3, leaves=63, quant=True, extra={"num_grad_quant_bins": 6}), 255),
+    "binary_quant_skewed": (dict(seed=25, n=400_000, f=40, kind="binary", zero_frac=0.97),
+                            dict(objective="binary", rounds=3, leaves=127, quant=True), 63),
     # fixed point with the 2^52 bound and Int64 cells (gpu_histogram_precision=int64)
     "l2_fixed52": (dict(seed=19, n=50_000, f=28), dict(objective="regression", rounds=4, leaves=63,
                                                       extra={"gpu_histogram_precision": "int64"}), 255),
