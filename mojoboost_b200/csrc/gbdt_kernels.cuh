@@ -514,34 +514,14 @@ constexpr int kQuantCountBits = 15;
 //                has no native shared-memory unit on sm_100: it costs about six
 //                32-bit atomics, acceptable for a precision mode)
 //   HL_W52CH     HL_W52 with a constant hessian: g and count planes
-//   HL_QP        int8 gradients, one 32-bit cell per (feature, bin) holding
-//                count | g + g_lim | h as three unsigned fields (HistPack), so
-//                one shared atomic per (row, feature).  The atomic returns the
-//                old cell: the add that brings the count field to pk.spill
-//                moves the cell's contents (pk.spill rows' worth) to the global
-//                cells and subtracts them from the shared cell, so no field
-//                can carry (an add that sees the count at pk.guard or above
-//                flags an error instead of a silent carry)
-//   HL_QPR       HL_QP with the row id, g + g_lim and h in one shuffled word
-//                (as HL_QUANT16R)
 enum HistLayout : int {
-  HL_QUANT = 0, HL_QUANT16 = 1, HL_FIXED_CH = 2, HL_FIXED = 3, HL_QUANT16R = 4, HL_QP = 5, HL_QPR = 6,
-  HL_W52 = 9, HL_W52CH = 10
+  HL_QUANT = 0, HL_QUANT16 = 1, HL_FIXED_CH = 2, HL_FIXED = 3, HL_QUANT16R = 4, HL_W52 = 9, HL_W52CH = 10
 };
 
-// Field geometry of the HL_QP cells: count in bits [0, cbits), g + g_lim in
-// [cbits, cbits + wbits), h above; spill = 2^(cbits-2) rows, guard =
-// 2^cbits - 2^(cbits-3).  err: set to 1 when a guard is reached.
-struct HistPack {
-  int cbits = 0, wbits = 0;
-  unsigned int spill = 0, guard = 0;
-  int* err = nullptr;
-};
 
 // 32-bit words of shared memory a CTA's cells take (cells = lane cells of one plane)
 __host__ __device__ constexpr int hist_layout_words(int layout, int cells) {
-  return (layout == HL_QP || layout == HL_QPR)             ? cells
-         : (layout == HL_QUANT16 || layout == HL_QUANT16R) ? cells + cells / 2
+  return (layout == HL_QUANT16 || layout == HL_QUANT16R) ? cells + cells / 2
          : layout == HL_W52                              ? 5 * cells
          : (layout == HL_FIXED || layout == HL_W52CH) ? 3 * cells
                                                                            : 2 * cells;
@@ -859,146 +839,6 @@ __device__ __forceinline__ void shared_red_add64(uint32_t addr, unsigned long lo
   asm volatile("red.shared.add.u64 [%0], %1;" ::"r"(addr), "l"(v));
 }
 
-__device__ __forceinline__ unsigned int shared_atom_add(uint32_t addr, unsigned int v) {
-  unsigned int old;
-  asm volatile("atom.shared.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(addr), "r"(v));
-  return old;
-}
-
-// hist_segment for HL_QP / HL_QPR: one 32-bit packed cell per (feature, bin)
-// and one returning shared atomic per (row, feature); see HistPack.
-template <int NPL, bool PR>
-__device__ void hist_segment_packed(cooperative_groups::cluster_group& cluster, const BatchItem& P, long long seg_b,
-                                    long long seg_n, const uint8_t* __restrict__ bins_rm, int Fp, int F, int B,
-                                    const int* __restrict__ rows0, const int* __restrict__ rows1,
-                                    const void* __restrict__ pairs0, const void* __restrict__ pairs1, int* hs,
-                                    int g_lim, const HistPack& pk, unsigned int* p0) {
-  constexpr int FG = 32 * NPL;
-  constexpr int U = kHistUnroll;
-  constexpr int CELLS = NPL * kHistBinsPad * 32;
-  const int cs = (int)cluster.num_blocks();
-  const int crank = (int)cluster.block_rank();
-  const long long sub = (seg_n + cs - 1) / cs;
-  const long long s = seg_b + crank * sub;
-  long long e = s + sub;
-  if (e > seg_b + seg_n) e = seg_b + seg_n;
-  const int f0 = blockIdx.x * FG;
-  const int* rows = P.dst_buf ? rows1 : rows0;
-  const uint16_t* pairs = reinterpret_cast<const uint16_t*>(P.dst_buf ? pairs1 : pairs0);
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int n_warps = blockDim.x >> 5;
-  const bool lane_ok = f0 + lane * NPL < Fp;
-  const uint8_t* bcol = bins_rm + (lane_ok ? f0 + lane * NPL : 0);
-  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(p0) + 4u * lane;
-  constexpr uint32_t kFeat = 128u * kHistBinsPad;
-  const int cb = pk.cbits, gb = pk.cbits + pk.wbits;
-  const unsigned int cmask = (1u << pk.cbits) - 1u, wmask = (1u << pk.wbits) - 1u;
-  const unsigned int spill_at = pk.spill - 1u;
-  // the rare path: move pk.spill rows' worth of cell (j, bin) to the global cells
-  auto spill = [&](int j, unsigned int bin, uint32_t a, unsigned int cell) {
-    if (cell & cmask) {
-      shared_red_add(a, 0u - cell);
-      const int f = f0 + lane * NPL + j;
-      if (f < F && (int)bin < B) {
-        const int cnt = (int)(cell & cmask);
-        int* cellp = hs + (f * 3) * B + bin;
-        atomicAdd(cellp, (int)((cell >> cb) & wmask) - g_lim * cnt);
-        atomicAdd(cellp + B, (int)(cell >> gb));
-        atomicAdd(cellp + 2 * B, cnt);
-      }
-    }
-  };
-  auto add_row = [&](unsigned int bw, unsigned int v) {
-#pragma unroll
-    for (int j = 0; j < NPL; ++j) {
-      const unsigned int bin = (bw >> (8 * j)) & 0xffu;
-      const uint32_t a = sbase + (bin << 7) + j * kFeat;
-      const unsigned int old = shared_atom_add(a, v);
-      const unsigned int c = old & cmask;
-      if (c >= spill_at) {
-        if (c == spill_at)
-          spill(j, bin, a, old + v);
-        else if (c >= pk.guard)
-          *pk.err = 1;
-      }
-    }
-  };
-  auto value_of = [&](unsigned int gq, unsigned int hq) { return 1u | (gq << cb) | (hq << gb); };
-  for (int c = threadIdx.x; c < CELLS; c += blockDim.x) p0[c] = 0u;
-  __syncthreads();
-  const long long stride = (long long)n_warps * 32;
-  long long c0 = s + (long long)warp * 32;
-  // per lane, position c0 + lane: PR: row << 6 | h << 3 | g + g_lim;
-  // otherwise the row id and the packed addend
-  int nr = 0;
-  unsigned int na = 0u;
-  auto fetch = [&](long long base, int& r, unsigned int& a) {
-    const long long i = base + lane;
-    r = 0;
-    a = 0u;
-    if (i < e) {
-      r = __ldg(rows + i);
-      const uint16_t pr = __ldg(pairs + i);
-      const unsigned int gq = (unsigned int)((int)(int8_t)(pr & 0xff) + g_lim), hq = (unsigned int)(pr >> 8);
-      a = PR ? (((unsigned int)r << 6) | (hq << 3) | gq) : value_of(gq, hq);
-    }
-  };
-  if (c0 < e) fetch(c0, nr, na);
-  for (; c0 < e; c0 += stride) {
-    const int cr = nr;
-    const unsigned int ca = na;
-    if (c0 + stride < e) fetch(c0 + stride, nr, na);
-    if (e - c0 >= 32) {
-#pragma unroll
-      for (int u0 = 0; u0 < 32; u0 += U) {
-        unsigned int bw[U], pw[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          pw[u] = __shfl_sync(0xffffffffu, ca, u0 + u);
-          const int r = PR ? (int)(pw[u] >> 6) : __shfl_sync(0xffffffffu, cr, u0 + u);
-          bw[u] = BinWord<NPL>::load(bcol + (size_t)(unsigned int)r * (unsigned int)Fp);
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) add_row(bw[u], PR ? value_of(pw[u] & 7u, (pw[u] >> 3) & 7u) : pw[u]);
-      }
-    } else {
-      const int n_in = (int)(e - c0);
-      for (int u = 0; u < n_in; ++u) {
-        const unsigned int w = __shfl_sync(0xffffffffu, ca, u);
-        const int r = PR ? (int)(w >> 6) : __shfl_sync(0xffffffffu, cr, u);
-        add_row(BinWord<NPL>::load(bcol + (size_t)(unsigned int)r * (unsigned int)Fp),
-                PR ? value_of(w & 7u, (w >> 3) & 7u) : w);
-      }
-    }
-  }
-  cluster.sync();
-  const int slice = (CELLS + cs - 1) / cs;
-  const int m0 = crank * slice;
-  const int m1 = m0 + slice < CELLS ? m0 + slice : CELLS;
-  for (int c = m0 + threadIdx.x; c < m1; c += blockDim.x) {
-    const int l = c & 31;
-    const int jb = c >> 5;
-    const int j = jb / kHistBinsPad;
-    const int bin = jb % kHistBinsPad;
-    const int f = f0 + l * NPL + j;
-    if (f >= F || bin >= B) continue;
-    int g = 0, h = 0, cnt = 0;
-    for (int rk = 0; rk < cs; ++rk) {
-      const unsigned int x = cluster.map_shared_rank(p0, rk)[c];
-      cnt += (int)(x & cmask);
-      g += (int)((x >> cb) & wmask);
-      h += (int)(x >> gb);
-    }
-    if (cnt == 0) continue;
-    int* cellp = hs + (f * 3) * B + bin;
-    atomicAdd(cellp, g - g_lim * cnt);
-    atomicAdd(cellp + B, h);
-    atomicAdd(cellp + 2 * B, cnt);
-  }
-  cluster.sync();  // peers finished reading before anyone re-zeroes
-}
-
 // hist_segment for the fixed-point mode with the 2^52 bound (HL_W52,
 // HL_W52CH): Int64 gradient and hessian values, 64-bit shared cells for g
 // (and h), a 32-bit count plane, Int64 global cells.  Same bank-per-lane
@@ -1116,7 +956,7 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__
                                                const int* __restrict__ rows1, const void* __restrict__ pairs0,
                                                const void* __restrict__ pairs1, int* __restrict__ hist,
                                                long long slot_cells, long long rows_per_flush, int g_lim,
-                                               int work_base, int min_rows_per_cta, HistPack pk) {
+                                               int work_base, int min_rows_per_cta) {
   namespace cg = cooperative_groups;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   unsigned int* p0 = reinterpret_cast<unsigned int*>(smem_raw);
@@ -1146,12 +986,7 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__
     const long long s0 = lo > acc ? lo : acc;
     const long long s1 = hi < acc + c ? hi : acc + c;
     if (s1 > s0) {
-      if constexpr (LAYOUT == HL_QP || LAYOUT == HL_QPR)
-        hist_segment_packed<NPL, LAYOUT == HL_QPR>(cluster, P, b + (s0 - acc), s1 - s0, bins_rm, Fp, F, B, rows0,
-                                                    rows1, pairs0, pairs1,
-                                                    hist + (long long)(work_base + P.work) * slot_cells, g_lim, pk,
-                                                    p0);
-      else if constexpr (LAYOUT == HL_W52 || LAYOUT == HL_W52CH)
+      if constexpr (LAYOUT == HL_W52 || LAYOUT == HL_W52CH)
         hist_segment_w52<NPL, LAYOUT>(cluster, P, b + (s0 - acc), s1 - s0, bins_rm, Fp, F, B, rows0, rows1, pairs0,
                                       pairs1, hist + (long long)(work_base + P.work) * slot_cells, rows_per_flush,
                                       smem_raw);

@@ -41,7 +41,6 @@ struct HistLaunch {
   size_t smem = 0;
   long long rows_per_flush = 1ll << 40;
   int g_lim = 0;               // HL_QUANT16: offset making g non-negative
-  HistPack pk;                 // HL_QP / HL_QPR field geometry and error flag
 };
 
 cudaLaunchConfig_t hist_config(const HistLaunch& hl, int cs, int row_ctas, cudaStream_t st, cudaLaunchAttribute* attr) {
@@ -76,7 +75,7 @@ void launch_hist_t(const HistLaunch& hl, cudaStream_t st, const Batch* batch, co
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t lc = hist_config(hl, hl.cluster, hl.row_ctas, st, attr);
   MTB_CUDA(cudaLaunchKernelEx(&lc, k_hist<NPL, L>, batch, bins_rm, Fp, F, B, r0, r1, p0, p1, hist, slot_cells,
-                              hl.rows_per_flush, hl.g_lim, ws, hl.min_rows_per_cta, hl.pk));
+                              hl.rows_per_flush, hl.g_lim, ws, hl.min_rows_per_cta));
 }
 
 // Every (layout, features per lane) instance the launch geometry can pick.
@@ -95,10 +94,6 @@ void launch_hist_t(const HistLaunch& hl, cudaStream_t st, const Batch* batch, co
     case HL_FIXED * 8 + 1: { constexpr int V = 1, L = HL_FIXED; EXPR; } break;                        \
     case HL_FIXED * 8 + 2: { constexpr int V = 2, L = HL_FIXED; EXPR; } break;                        \
     case HL_FIXED * 8 + 4: { constexpr int V = 4, L = HL_FIXED; EXPR; } break;                        \
-    case HL_QP * 8 + 2: { constexpr int V = 2, L = HL_QP; EXPR; } break;                              \
-    case HL_QP * 8 + 4: { constexpr int V = 4, L = HL_QP; EXPR; } break;                              \
-    case HL_QPR * 8 + 2: { constexpr int V = 2, L = HL_QPR; EXPR; } break;                            \
-    case HL_QPR * 8 + 4: { constexpr int V = 4, L = HL_QPR; EXPR; } break;                            \
     case HL_W52 * 8 + 1: { constexpr int V = 1, L = HL_W52; EXPR; } break;                            \
     case HL_W52CH * 8 + 1: { constexpr int V = 1, L = HL_W52CH; EXPR; } break;                        \
     default: throw std::runtime_error("bad histogram layout");                                         \
@@ -118,35 +113,7 @@ inline void launch_hist(const HistLaunch& hl, cudaStream_t st, const Batch* batc
 
 // Cell layout and flush span for a fit.  quant_bins: the int8 gradient range
 // (|g| <= quant_bins / 2, h <= quant_bins); 0 for the fixed-point modes.
-// HL_QP field geometry for a quantizer of quant_bins (|g| <= q/2, h <= q):
-// the widest count field whose g and h sums still fit the word; false when
-// the count field would be narrower than 7 bits (spills every 32 rows or less).
-inline bool pack_geometry(int quant_bins, HistPack& pk) {
-  const long long m = std::max<long long>(quant_bins, 1);  // per-row maximum of g + g_lim and of h
-  for (int c = 10; c >= 7; --c) {
-    const long long top = m * ((1ll << c) - 1);
-    int w = 0;
-    while ((1ll << w) <= top) ++w;
-    if (c + 2 * w <= 32) {
-      pk.cbits = c;
-      pk.wbits = w;
-      pk.spill = 1u << (c - 2);
-      pk.guard = (1u << c) - (1u << (c - 3));
-      return true;
-    }
-  }
-  return false;
-}
-
-inline void choose_hist_layout(HistLaunch& hl, int mode, bool const_h, int quant_bins, bool wide = false,
-                               int* pack_err = nullptr) {
-  if (mode == MODE_QUANT && pack_err && !getenv("MOJOTREES_HIST_NO_PACKED") && pack_geometry(quant_bins, hl.pk)) {
-    hl.layout = HL_QP;
-    hl.pk.err = pack_err;
-    hl.g_lim = quant_bins / 2;
-    hl.rows_per_flush = 1ll << 40;  // the spills keep every field in range
-    return;
-  }
+inline void choose_hist_layout(HistLaunch& hl, int mode, bool const_h, int quant_bins, bool wide = false) {
   if (wide) {
     hl.layout = const_h ? HL_W52CH : HL_W52;
     hl.rows_per_flush = 1ll << 40;  // Int64 cells: sums stay below 2^53, counts below 2^31 per CTA
@@ -176,15 +143,13 @@ inline void choose_hist_layout(HistLaunch& hl, int mode, bool const_h, int quant
 // clusters of up to 8 that merge through DSMEM.
 // n_rows > 0 (row ids below it) lets 16-bit packed cells with narrow
 // quantizers use HL_QUANT16R; MOJOTREES_HIST_NO_ROWPACK turns that off.
-// pack_err: device int the packed-cell kernels set on a guard hit; without
-// it the packed layouts are not used.
 inline HistLaunch choose_hist_launch(int mode, bool const_h, int quant_bins, int B, int Fp, int n_sm,
-                                     long long n_rows = 0, bool wide = false, int* pack_err = nullptr) {
+                                     long long n_rows = 0, bool wide = false) {
   HistLaunch hl;
-  choose_hist_layout(hl, mode, const_h, quant_bins, wide, pack_err);
-  if ((hl.layout == HL_QUANT16 || hl.layout == HL_QP) && n_rows > 0 && n_rows <= (1ll << 26) && quant_bins <= 7
+  choose_hist_layout(hl, mode, const_h, quant_bins, wide);
+  if (hl.layout == HL_QUANT16 && n_rows > 0 && n_rows <= (1ll << 26) && quant_bins <= 7
       && !getenv("MOJOTREES_HIST_NO_ROWPACK"))
-    hl.layout = hl.layout == HL_QP ? HL_QPR : HL_QUANT16R;
+    hl.layout = HL_QUANT16R;
   // MOJOTREES_HIST_SMEM_KB / MOJOTREES_HIST_CLUSTER override the shared-memory
   // budget per CTA and the largest cluster size (tuning knobs)
   size_t budget = 220 * 1024;
@@ -195,9 +160,7 @@ inline HistLaunch choose_hist_launch(int mode, bool const_h, int quant_bins, int
   hl.npl = 0;
   hl.groups = 1 << 30;
   for (int npl : {1, 2, 4}) {
-    if ((hl.layout == HL_QUANT16 || hl.layout == HL_QUANT16R || hl.layout == HL_QP || hl.layout == HL_QPR) &&
-        npl == 1)
-      continue;
+    if ((hl.layout == HL_QUANT16 || hl.layout == HL_QUANT16R) && npl == 1) continue;
     if ((hl.layout == HL_W52 || hl.layout == HL_W52CH) && npl != 1) continue;
     int groups = (Fp + 32 * npl - 1) / (32 * npl);
     if ((smem_of(npl) <= budget || hl.npl == 0) && groups < hl.groups) {

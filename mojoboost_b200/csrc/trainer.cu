@@ -387,7 +387,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   // memory holds, row chunks sized to fill every SM, CTAs of a feature group
   // in clusters of up to 8 that merge through DSMEM.
   HistLaunch hl = choose_hist_launch(mode, const_h, mode == MODE_QUANT ? cfg.num_grad_quant_bins : 0, B, Fp, n_sm, N,
-                                     wide, &d_ts.p->hdr.error);
+                                     wide);
   // partition geometry (MOJOTREES_PART_ITEMS / MOJOTREES_PART_BLOCKS_PER_SM
   // override the rows per thread of a tile and the resident blocks per SM)
   int part_bps = 4;
