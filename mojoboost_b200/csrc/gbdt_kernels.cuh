@@ -398,6 +398,17 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
     for (long long i = tid; i < total; i += stride) hs[i] = 0;
   }
   if (Bt.root) return;  // the root's rows are already in place
+  // the batch's items, staged with one coalesced copy: every tile looks up
+  // its item and reads its split (from global memory each lookup would be a
+  // chain of dependent L2 round trips)
+  __shared__ BatchItem s_items[kMaxBatch];
+  {
+    const int* src = reinterpret_cast<const int*>(Bt.items);
+    int* dst = reinterpret_cast<int*>(s_items);
+    const int words = n_items * (int)(sizeof(BatchItem) / sizeof(int));
+    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+  }
+  __syncthreads();
   constexpr int TILE = 256 * ITEMS;
   // Per-warp left/right counts of each item row of a tile, and the tile's
   // cursor bases; double-buffered by tile parity, so a tile needs two block
@@ -411,8 +422,9 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
   int par = 0;
   for (long long tile = blockIdx.x; tile < Bt.n_tiles; tile += gridDim.x, par ^= 1) {
     int it = 0;
-    while (it + 1 < n_items && Bt.items[it + 1].tile0 <= tile) ++it;
-    BatchItem& P = Bt.items[it];
+    while (it + 1 < n_items && s_items[it + 1].tile0 <= tile) ++it;
+    const BatchItem& P = s_items[it];
+    BatchItem& PG = Bt.items[it];  // the item's cursors live in global memory
     const int* src_rows = P.src_buf ? rows1 : rows0;
     int* dst_rows = P.src_buf ? rows0 : rows1;
     const PairT* src_pairs = P.src_buf ? pairs1 : pairs0;
@@ -452,8 +464,8 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
           tl += s_cl[par][j][k];
           tr += s_cr[par][j][k];
         }
-      s_base_l[par] = atomicAdd(&P.cursor_left, (unsigned long long)tl);
-      const unsigned long long o = atomicAdd(&P.cursor_right, (unsigned long long)tr);
+      s_base_l[par] = atomicAdd(&PG.cursor_left, (unsigned long long)tl);
+      const unsigned long long o = atomicAdd(&PG.cursor_right, (unsigned long long)tr);
       s_base_r[par] = (unsigned long long)end - o - (unsigned long long)tr;  // rights fill from the back
     }
     __syncthreads();
@@ -585,6 +597,8 @@ constexpr int kHistUnroll = MTB_HIST_UNROLL;  // bin loads in flight per warp (d
 #endif
 constexpr int kHistThreads = MTB_HIST_THREADS;
 constexpr int kHistBinsPad = 256;  // bins per feature in the shared-memory layout
+// shared memory after the cells: the staged batch items and their built-row prefix sums
+constexpr int kHistBatchSmem = (int)((sizeof(BatchItem) * kMaxBatch + sizeof(long long) * (kMaxBatch + 1) + 15) / 16 * 16);
 
 // Atomic add to a shared-memory word whose result is not needed.  No memory
 // clobber: the cells are read only after a block or cluster barrier (which
@@ -794,42 +808,55 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
       }
     }
     cluster.sync();
-    for (int c = m0 + threadIdx.x; c < m1; c += blockDim.x) {
-      const int l = c & 31;
-      const int jb = c >> 5;
-      const int j = jb / kHistBinsPad;
-      const int bin = jb % kHistBinsPad;
-      const int f = f0 + l * NPL + j;
-      if (f >= F || bin >= B) continue;
-      int g = 0, h = 0, cnt = 0;
-      for (int rk = 0; rk < cs; ++rk) {
-        const unsigned int* q0 = cluster.map_shared_rank(p0, rk);
-        const unsigned int* q1 = q0 + cells;
-        if (Q16) {
-          const unsigned int x = q0[c];
-          cnt += (int)(x >> 16);
-          g += (int)(x & 0xffffu);
-          h += (int)((q1[(((j >> 1) * kHistBinsPad + bin) << 5) + l] >> (16 * (j & 1))) & 0xffffu);
-        } else if (LAYOUT == HL_QUANT) {
-          unsigned int x = q0[c];
-          cnt += (int)(x & ((1u << kQuantCountBits) - 1u));
-          g += (int)x >> kQuantCountBits;
-          h += (int)q1[c];
-        } else if (CONST_H) {
-          g += (int)q0[c];
-          cnt += (int)q1[c];
-        } else {
-          g += (int)q0[c];
-          h += (int)q1[c];
-          cnt += (int)q1[c + cells];
-        }
+    // Merge: cell c of every CTA of the cluster (DSMEM), two cells per thread
+    // at a time with every rank's words loaded before any is used, then one
+    // int32 global atomic per plane into the item's work slot.
+    auto add_cell = [&](const unsigned int* q0, int c, int& g, int& h, int& cnt) {
+      const unsigned int* q1 = q0 + cells;
+      if (Q16) {
+        const int l = c & 31, jb = c >> 5, j = jb / kHistBinsPad, bin = jb % kHistBinsPad;
+        const unsigned int x = q0[c];
+        cnt += (int)(x >> 16);
+        g += (int)(x & 0xffffu);
+        h += (int)((q1[(((j >> 1) * kHistBinsPad + bin) << 5) + l] >> (16 * (j & 1))) & 0xffffu);
+      } else if (LAYOUT == HL_QUANT) {
+        const unsigned int x = q0[c];
+        cnt += (int)(x & ((1u << kQuantCountBits) - 1u));
+        g += (int)x >> kQuantCountBits;
+        h += (int)q1[c];
+      } else if (CONST_H) {
+        g += (int)q0[c];
+        cnt += (int)q1[c];
+      } else {
+        g += (int)q0[c];
+        h += (int)q1[c];
+        cnt += (int)q1[c + cells];
       }
-      if (cnt == 0) continue;
+    };
+    auto emit_cell = [&](int c, int g, int h, int cnt) {
+      const int l = c & 31, jb = c >> 5, j = jb / kHistBinsPad, bin = jb % kHistBinsPad;
+      const int f = f0 + l * NPL + j;
+      if (f >= F || bin >= B || cnt == 0) return;
       if (Q16) g -= g_lim * cnt;  // sum of (g + g_lim) -> sum of g
       int* cellp = hs + (f * 3) * B + bin;
       atomicAdd(cellp, g);
       if (!(MODE == MODE_FIXED && CONST_H)) atomicAdd(cellp + B, h);
       atomicAdd(cellp + 2 * B, cnt);
+    };
+    for (int c = m0 + threadIdx.x; c < m1; c += 2 * blockDim.x) {
+      const int c2 = c + blockDim.x;
+      const bool two = c2 < m1;
+      int g0 = 0, h0 = 0, n0 = 0, g1 = 0, h1 = 0, n1 = 0;
+#pragma unroll
+      for (int rk = 0; rk < 8; ++rk) {
+        if (rk < cs) {
+          const unsigned int* q0 = cluster.map_shared_rank(p0, rk);
+          add_cell(q0, c, g0, h0, n0);
+          if (two) add_cell(q0, c2, g1, h1, n1);
+        }
+      }
+      emit_cell(c, g0, h0, n0);
+      if (two) emit_cell(c2, g1, h1, n1);
     }
     cluster.sync();  // peers finished reading before anyone re-zeroes
   }
@@ -960,27 +987,48 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__
   namespace cg = cooperative_groups;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   unsigned int* p0 = reinterpret_cast<unsigned int*>(smem_raw);
+  // After the cells: the batch's items and the prefix sums of their built
+  // rows, staged with one coalesced copy (the item records are read many
+  // times below; from global memory each read is a dependent L2 round trip).
+  constexpr int kCellBytes = 4 * hist_layout_words(LAYOUT, NPL * kHistBinsPad * 32);
+  BatchItem* s_items = reinterpret_cast<BatchItem*>(smem_raw + kCellBytes);
+  long long* s_pre = reinterpret_cast<long long*>(s_items + kMaxBatch);
   const int n_items = batch->n_items;  // uniform across the grid
   if (n_items == 0) return;
+  {
+    const int* src = reinterpret_cast<const int*>(batch->items);
+    int* dst = reinterpret_cast<int*>(s_items);
+    const int words = n_items * (int)(sizeof(BatchItem) / sizeof(int));
+    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    long long b, c = 0;
+    if (lane < n_items) built_range(s_items[lane], b, c);
+#pragma unroll
+    for (int k = 1; k < 32; k <<= 1) {
+      const long long o = __shfl_up_sync(0xffffffffu, c, k);
+      if (lane >= k) c += o;
+    }
+    s_pre[lane + 1] = c;
+    if (lane == 0) s_pre[0] = 0;
+  }
+  __syncthreads();
   cg::cluster_group cluster = cg::this_cluster();
   const int cs = (int)cluster.num_blocks();
   const long long n_clusters = gridDim.y / cs;
   const long long cid = blockIdx.y / cs;
-  long long S = 0;
-  for (int i = 0; i < n_items; ++i) {
-    long long b, c;
-    built_range(batch->items[i], b, c);
-    S += c;
-  }
+  const long long S = s_pre[n_items];
   if (S == 0) return;
   const long long per_cluster = (long long)min_rows_per_cta * cs;
   long long cap = (S + per_cluster - 1) / per_cluster;
   if (cap > n_clusters) cap = n_clusters;
   if (cid >= cap) return;  // the whole cluster leaves together
   const long long lo = S * cid / cap, hi = S * (cid + 1) / cap;
-  long long acc = 0;
-  for (int i = 0; i < n_items && acc < hi; ++i) {
-    const BatchItem& P = batch->items[i];
+  for (int i = 0; i < n_items && s_pre[i] < hi; ++i) {
+    const BatchItem& P = s_items[i];
+    const long long acc = s_pre[i];
     long long b, c;
     built_range(P, b, c);
     const long long s0 = lo > acc ? lo : acc;
@@ -995,7 +1043,6 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__
                                   pairs1, hist + (long long)(work_base + P.work) * slot_cells, rows_per_flush, g_lim,
                                   p0);
     }
-    acc += c;
   }
 }
 

@@ -156,7 +156,9 @@ inline HistLaunch choose_hist_launch(int mode, bool const_h, int quant_bins, int
   if (const char* e = getenv("MOJOTREES_HIST_SMEM_KB")) budget = (size_t)atoi(e) * 1024;
   int max_cs = 8;
   if (const char* e = getenv("MOJOTREES_HIST_CLUSTER")) max_cs = atoi(e);
-  auto smem_of = [&](int npl) { return (size_t)4 * hist_layout_words(hl.layout, 32 * npl * kHistBinsPad); };
+  auto smem_of = [&](int npl) {
+    return (size_t)4 * hist_layout_words(hl.layout, 32 * npl * kHistBinsPad) + (size_t)kHistBatchSmem;
+  };
   hl.npl = 0;
   hl.groups = 1 << 30;
   for (int npl : {1, 2, 4}) {
