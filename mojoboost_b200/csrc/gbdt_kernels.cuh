@@ -1004,14 +1004,18 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__
   __syncthreads();
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
-    long long b, c = 0;
-    if (lane < n_items) built_range(s_items[lane], b, c);
+    long long carry = 0;
+    for (int base = 0; base < n_items; base += 32) {
+      long long b, c = 0;
+      if (base + lane < n_items) built_range(s_items[base + lane], b, c);
 #pragma unroll
-    for (int k = 1; k < 32; k <<= 1) {
-      const long long o = __shfl_up_sync(0xffffffffu, c, k);
-      if (lane >= k) c += o;
+      for (int k = 1; k < 32; k <<= 1) {
+        const long long o = __shfl_up_sync(0xffffffffu, c, k);
+        if (lane >= k) c += o;
+      }
+      if (base + lane < n_items) s_pre[base + lane + 1] = carry + c;
+      carry += __shfl_sync(0xffffffffu, c, 31);
     }
-    s_pre[lane + 1] = c;
     if (lane == 0) s_pre[0] = 0;
   }
   __syncthreads();
@@ -1892,10 +1896,9 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
       if (n_new > free_slots) n_new = free_slots;
       if (n_new > (kMaxPool - pool0) / 2) n_new = (kMaxPool - pool0) / 2;
       if (n_new < 0) n_new = 0;
-      const bool take = lane < n_new;
-      long long tiles = 0;
-      if (take) {
-        const int idx = lane;
+      // item set-up, lane per item, 32 items per pass; the items' partition
+      // tiles get an exclusive prefix (tile0) over all passes
+      auto setup = [&](int idx) -> long long {
         const int leaf = s_sel[idx];
         LeafRec& L = ts->pool[leaf];
         const SplitRec& s = L.split;
@@ -1943,16 +1946,21 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
           CI.expanded = 0;
           CI.pad = 0;
         }
-        tiles = (L.count + cp.tile_rows - 1) / cp.tile_rows;
+        return (L.count + cp.tile_rows - 1) / cp.tile_rows;
+      };
+      long long total = 0;
+      for (int base = 0; base < n_new; base += 32) {
+        const int idx = base + lane;
+        const bool take = idx < n_new;
+        const long long tiles = take ? setup(idx) : 0;
+        long long incl = tiles;
+        for (int k = 1; k < 32; k <<= 1) {
+          const long long o = __shfl_up_sync(0xffffffffu, incl, k);
+          if (lane >= k) incl += o;
+        }
+        if (take) Bt.items[idx].tile0 = total + incl - tiles;
+        total += __shfl_sync(0xffffffffu, incl, 31);
       }
-      // exclusive prefix of tiles over the items (lane = item)
-      long long incl = tiles;
-      for (int k = 1; k < 32; k <<= 1) {
-        long long o = __shfl_up_sync(0xffffffffu, incl, k);
-        if (lane >= k) incl += o;
-      }
-      if (take) Bt.items[lane].tile0 = incl - tiles;
-      const long long total = __shfl_sync(0xffffffffu, incl, 31);
       if (lane == 0) {
         if (n_new == 0) {
           H.error = 1;  // reserved space exhausted (cannot happen within the bounds above)

@@ -357,7 +357,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   const long long slot_cells = (long long)(dp_feature ? Fb * world : F) * 3 * B * cell_words;
   // Leaves expanded per iteration (speculative leaf batching); 1 grows one
   // split per iteration as the reference does.  MOJOTREES_BATCH overrides.
-  int batch_cap = 32;
+  int batch_cap = kMaxBatch;
   // MOJOTREES_SCAN=compact selects the split scan whose candidate evaluation
   // is one out-of-line routine (same arithmetic, smaller code)
   const char* scan_env = getenv("MOJOTREES_SCAN");
