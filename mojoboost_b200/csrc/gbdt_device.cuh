@@ -48,7 +48,7 @@ struct SplitRec {
   unsigned long long bits[4];
 };
 
-constexpr int kMaxBatch = 64;                              // leaves expanded per iteration
+constexpr int kMaxBatch = 32;                              // leaves expanded per iteration
 // leaf records of one tree: 1 + 2 per expansion, expansions bounded by the
 // histogram slots (2 * num_leaves + batch)
 constexpr int kMaxPool = 4 * kMaxLeaves + 2 * kMaxBatch + 2;
