@@ -302,6 +302,12 @@ int32_t mojotrees_b200_histogram_u8_noalloc(const uint8_t *bins_rm, int64_t n_ro
                                             const uint16_t *pairs, int32_t num_grad_quant_bins, int32_t *out_hist,
                                             void *stream, MojoTreesError *error);
 
+/* Diagnostic: n random (integer sum, quantizer units) pairs dequantized on
+ * the device by the trainer's divide-free quotient and by the divide; the
+ * number of results whose bits differ goes to out_mismatches (0 expected).
+ * No counterpart in the reference. */
+int32_t mojotrees_b200_check_quotients(int64_t n, uint64_t seed, int64_t *out_mismatches, MojoTreesError *error);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

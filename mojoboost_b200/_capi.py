@@ -53,6 +53,7 @@ SIGNATURES = {
     "mojotrees_b200_bin_dense": (_I32, [_P, _I64, _I64, ctypes.c_char_p, _P, _P, _P, _P, _P]),
     "mojotrees_b200_bin_dense_gpu": (_I32, [_P, _I64, _I64, ctypes.c_char_p, _P, _P, _P, _P, _P]),
     "mojotrees_b200_shared_atomic_peak": (_I32, [_P, _P]),
+    "mojotrees_b200_check_quotients": (_I32, [_I64, ctypes.c_uint64, _P, _P]),
     "mojotrees_b200_predict_binned_u8": (_I32, [_P, _P, _I64, _I64, _P, _I64, _P]),
     "mojotrees_b200_tree_nodes": (_I32, [_P, _I64, _P, _P, _P, _P, _I64, _P, _P]),
     "mojotrees_b200_base_scores": (_I32, [_P, _P, _I64, _P]),
@@ -410,6 +411,15 @@ def shared_atomic_peak():
     e = _Err()
     e.check(lib().mojotrees_b200_shared_atomic_peak(ctypes.byref(v), e.h))
     return v.value
+
+
+def check_quotients(n, seed=1):
+    """Bits that differ between the trainer's divide-free dequantization and
+    the divide, over n random (sum, units) pairs on the device (0 expected)."""
+    out = ctypes.c_int64(-1)
+    e = _Err()
+    e.check(lib().mojotrees_b200_check_quotients(n, seed, ctypes.byref(out), e.h))
+    return out.value
 
 
 def gpu_available():

@@ -196,7 +196,7 @@ struct RoundScales {
   double g_total;   // FIXED: pairwise sum |g|;   QUANT: max |g|
   double h_total;
   float gsf, hsf;   // FIXED: pow2 scales as Float32
-  double g_inv, h_inv;  // FIXED: 1 / scale (exact)
+  double g_inv, h_inv;  // FIXED: 1 / scale (exact); QUANT: RN(1 / units)
   double g_units, h_units;  // QUANT: units per gradient / hessian
   double g_lim, h_lim;
   int hq_const;     // FIXED const-hessian per-row hessian units

@@ -236,6 +236,9 @@ __global__ void k_scales(RoundScales* sc, const double* fixed_g, const double* f
     sc->h_lim = const_hess ? 1.0 : (double)quant_bins;
     sc->g_units = sc->g_lim / gmax;
     sc->h_units = const_hess ? 1.0 / hmax : sc->h_lim / hmax;
+    // reciprocals for the divide-free dequantization (deq)
+    sc->g_inv = 1.0 / sc->g_units;
+    sc->h_inv = 1.0 / sc->h_units;
   }
 }
 
@@ -1078,9 +1081,26 @@ __device__ __forceinline__ double leaf_score(double g, double h, double l1, doub
   return t * t / (h + l2);
 }
 
-// Dequantize an exact integer sum.
+// The correctly rounded quotient a / b from y = RN(1 / b), without a divide:
+// two residual corrections q' = RN(q + RN(a - b q) y), the residual exact by
+// FMA (P. Markstein, "IA-64 and Elementary Functions", Prentice Hall 2000,
+// ch. 8: one correction of a faithful q yields RN(a / b); the first
+// correction makes RN(a y) faithful).  Valid while a / b and the residuals
+// stay normal, as they do for histogram sums over quantizer units
+// (mojotrees_b200_check_quotients verifies it against the divide).
+__device__ __forceinline__ double quot_exact(double a, double b, double y) {
+  double q = __dmul_rn(a, y);
+  double r = __fma_rn(-q, b, a);
+  q = __fma_rn(r, y, q);
+  r = __fma_rn(-q, b, a);
+  return __fma_rn(r, y, q);
+}
+
+// Dequantize an exact integer sum: FIXED multiplies by the power-of-two
+// inverse scale (exact); QUANT divides by the units (quantized_gradient.mojo:
+// 1324), with inv = RN(1 / units).
 __device__ __forceinline__ double deq(long long q, int mode, double inv, double units) {
-  return mode == MODE_FIXED ? (double)q * inv : (double)q / units;
+  return mode == MODE_FIXED ? (double)q * inv : quot_exact((double)q, units, inv);
 }
 
 // Called by every (child, feature) warp once its FeatBest is written; the
@@ -1751,6 +1771,56 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
     return __reduce_min_sync(0xffffffffu, best == top ? best_i : 0x7fffffff);
   };
 
+  // Up to 256 frontier slots the pick loops keep in warp 0's registers
+  // instead: slot s is key[s >> 5] of lane s & 31, its gain's bit pattern (0
+  // when the gain is not > 0), so a pick is three warp reductions with no
+  // shared-memory traffic and an update is two predicated moves.
+  const bool reg_frontier = L_max <= 256;
+  unsigned long long k0 = 0, k1 = 0, k2 = 0, k3 = 0, k4 = 0, k5 = 0, k6 = 0, k7 = 0;
+  auto key_of = [](double g) -> unsigned long long {
+    return g > 0.0 ? (unsigned long long)__double_as_longlong(g) : 0ull;
+  };
+#define MTB_FRONTIER_SET(SLOT, G)                              \
+  do {                                                         \
+    const int s_ = (SLOT);                                     \
+    const unsigned long long k_ = key_of(G);                   \
+    if (lane == (s_ & 31)) {                                   \
+      const int q_ = s_ >> 5;                                  \
+      k0 = q_ == 0 ? k_ : k0;                                  \
+      k1 = q_ == 1 ? k_ : k1;                                  \
+      k2 = q_ == 2 ? k_ : k2;                                  \
+      k3 = q_ == 3 ? k_ : k3;                                  \
+      k4 = q_ == 4 ? k_ : k4;                                  \
+      k5 = q_ == 5 ? k_ : k5;                                  \
+      k6 = q_ == 6 ? k_ : k6;                                  \
+      k7 = q_ == 7 ? k_ : k7;                                  \
+    }                                                          \
+  } while (0)
+  auto reg_pick = [&]() -> int {
+    unsigned long long best = 0ull;
+    int best_i = 0x7fffffff;
+    // ascending slot within the lane, strict >: the lowest slot wins ties
+    const unsigned long long ks[8] = {k0, k1, k2, k3, k4, k5, k6, k7};
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (ks[q] > best) {
+        best = ks[q];
+        best_i = q * 32 + lane;
+      }
+    const unsigned int hi = __reduce_max_sync(0xffffffffu, (unsigned int)(best >> 32));
+    const unsigned int lo =
+        __reduce_max_sync(0xffffffffu, (unsigned int)(best >> 32) == hi ? (unsigned int)best : 0u);
+    const unsigned long long top = ((unsigned long long)hi << 32) | lo;
+    if (top == 0ull) return -1;
+    return (int)__reduce_min_sync(0xffffffffu, best == top ? (unsigned int)best_i : 0x7fffffffu);
+  };
+  if (w == 0 && reg_frontier) {
+    for (int q = 0; q < 8; ++q) {
+      const int slot = q * 32 + lane;
+      MTB_FRONTIER_SET(slot, slot < nl0 ? s_g[slot] : -1.0);
+    }
+  }
+
   // ---- 2. the pick loop (growth_policy.mojo:659-677), on one warp over
   // shared memory: commit every pick whose children are computed
   if (w == 0) {
@@ -1758,7 +1828,7 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
     int n_commit = 0;
     int stop = H.done;
     while (!stop && nl < L_max) {
-      const int bs = warp_pick(s_g, nl);
+      const int bs = reg_frontier ? reg_pick() : warp_pick(s_g, nl);
       if (bs < 0) {
         stop = 1;
         break;
@@ -1766,6 +1836,10 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
       const int leaf = s_slot_leaf[bs];
       const LeafInfo I = info(leaf);
       if (!I.expanded) break;  // the pick still needs its expansion
+      if (reg_frontier) {
+        MTB_FRONTIER_SET(bs, info(I.child[0]).gain);
+        MTB_FRONTIER_SET(nl, info(I.child[1]).gain);
+      }
       if (lane == 0) {
         // node ids are assigned here, in commit order: a child committed in
         // the same launch as its parent finds its id in s_slot_node
@@ -1859,10 +1933,18 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
     if (w == 0) {
       int vn = nl, vleaves = nl, n_sel = 0;
       while (n_sel < cp.batch_cap && vleaves < L_max) {
-        const int bs = warp_pick(s_vg, vn);
+        const int bs = reg_frontier ? reg_pick() : warp_pick(s_vg, vn);
         if (bs < 0) break;
         const int leaf = s_vleaf[bs];
         const LeafInfo I = info(leaf);
+        if (reg_frontier) {
+          if (I.expanded) {
+            MTB_FRONTIER_SET(bs, info(I.child[0]).gain);
+            MTB_FRONTIER_SET(vn, info(I.child[1]).gain);
+          } else {
+            MTB_FRONTIER_SET(bs, -1.0);
+          }
+        }
         if (lane == 0) {
           if (I.expanded) {
             s_vleaf[bs] = I.child[0];
@@ -1985,6 +2067,7 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
     }
   }
 }
+#undef MTB_FRONTIER_SET
 
 // After the last iteration: the row -> leaf-value map.  The unexpanded leaf
 // records (committed leaves and speculative children) tile this device's rows:

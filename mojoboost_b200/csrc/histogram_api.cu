@@ -316,3 +316,61 @@ extern "C" int32_t mojotrees_b200_shared_atomic_peak(double* out_lane_atomics_pe
     return MOJOTREES_ERROR_TRAINING;
   }
 }
+
+// ---------------------------------------------------------------------------
+// Self-check of the divide-free dequantization (quot_exact): the correctly
+// rounded quotient of integer histogram sums by quantizer units, compared on
+// the device with the divide it replaces.
+// ---------------------------------------------------------------------------
+namespace mtb {
+namespace {
+
+__global__ void k_check_quotients(long long n, unsigned long long seed, unsigned long long* mismatches) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  unsigned long long bad = 0;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const uint64_t r0 = mt_splitmix64(seed + 2 * (uint64_t)i), r1 = mt_splitmix64(seed + 2 * (uint64_t)i + 1);
+    // sums: integers up to 2^40 in magnitude (a few small ones exactly);
+    // units: lim / max with lim in {1..127} and max a float32 in [1e-12, 1e38]
+    long long q = (long long)(r0 >> 24) - (1ll << 39);
+    if ((r0 & 15) == 0) q = (long long)(r0 >> 60) - 8;
+    const int lim = 1 + (int)((r1 >> 57) & 127) % 127;
+    const float mx = __uint_as_float((unsigned int)(0x2B8CBCCCu + (unsigned int)((r1 & 0xffffffffu) % 0x53000000u)));
+    const double units = (double)lim / (double)mx;
+    const double a = (double)q;
+    const double want = a / units;
+    const double got = quot_exact(a, units, 1.0 / units);
+    if (__double_as_longlong(want) != __double_as_longlong(got)) ++bad;
+  }
+  if (bad) atomicAdd(mismatches, bad);
+}
+
+}  // namespace
+}  // namespace mtb
+
+extern "C" int32_t mojotrees_b200_check_quotients(int64_t n, uint64_t seed, int64_t* out_mismatches,
+                                                  MojoTreesError* error) {
+  using namespace mtb;
+  capi_clear_error(error);
+  try {
+    if (!out_mismatches || n < 0) throw std::invalid_argument("invalid argument");
+    if (cuda_device_count() < 1) throw Unsupported("no CUDA device is available");
+    DevMem d(sizeof(unsigned long long));
+    MTB_CUDA(cudaMemset(d.p, 0, sizeof(unsigned long long)));
+    k_check_quotients<<<148 * 8, 256>>>(n, seed, (unsigned long long*)d.p);
+    MTB_CUDA(cudaGetLastError());
+    unsigned long long bad = 0;
+    MTB_CUDA(cudaMemcpy(&bad, d.p, sizeof bad, cudaMemcpyDeviceToHost));
+    *out_mismatches = (int64_t)bad;
+    return MOJOTREES_OK;
+  } catch (const std::invalid_argument& e) {
+    capi_set_error(error, e.what());
+    return MOJOTREES_ERROR_INVALID_ARGUMENT;
+  } catch (const Unsupported& e) {
+    capi_set_error(error, e.what());
+    return MOJOTREES_ERROR_UNSUPPORTED;
+  } catch (const std::exception& e) {
+    capi_set_error(error, e.what());
+    return MOJOTREES_ERROR_TRAINING;
+  }
+}
