@@ -413,6 +413,7 @@ def run_gpu(args):
     per_round = 1.0 / max(1, st["rounds"])
     phases = {"hist_ms": st["hist_ms"] * per_round}
     phases.update({"iterations_per_tree": st["iterations"] * per_round / c["K"],
+                   "pick_steps_per_tree": st.get("pick_steps", 0.0) * per_round / c["K"],
                    "expansions_per_tree": st["expansions"] * per_round / c["K"],
                    "hist_launches_timed": hist_launches, "hist_rows_timed": hist_rows})
     smem_peak = mb.shared_atomic_peak() if hist_ms > 0 else None

@@ -1096,7 +1096,8 @@ int32_t mojotrees_b200_train_stats(const MojoTreesModel* model, double* out_valu
         const double v[] = {s.fit_seconds, s.upload_seconds, s.hist_ms,   s.partition_ms,
                             s.scan_ms,     s.grad_ms,        s.hist_rows, s.hist_bytes,
                             (double)s.hist_launches, (double)s.kernel_launches, (double)s.rounds,
-                            s.commit_ms,   (double)s.iterations, (double)s.expansions, s.binning_seconds};
+                            s.commit_ms,   (double)s.iterations, (double)s.expansions, s.binning_seconds,
+                            (double)s.pick_steps};
         int64_t n = std::min<int64_t>(out_len, (int64_t)(sizeof v / sizeof v[0]));
         for (int64_t i = 0; i < n; ++i) out_values[i] = v[i];
         if (out_n) *out_n = n;

@@ -146,7 +146,7 @@ struct TreeHeader {
   int n_hist;                // histogram slots used
   int iterations;            // expansion iterations run for this tree
   int n_table;               // entries of the final row -> leaf table
-  int pad;
+  int pick_steps;            // steps of the commit kernel's pick loops (real and simulated), summed
 };
 
 // Compact per-leaf view the commit kernel loads in one pass: the leaf's gain

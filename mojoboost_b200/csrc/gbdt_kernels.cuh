@@ -330,6 +330,7 @@ __global__ void k_tree_init(TreeState* ts, long long n_local) {
   H.n_pool = 1;
   H.n_hist = 1;
   H.iterations = 0;
+  H.pick_steps = 0;
   LeafRec& L = ts->pool[0];
   L.node = 0;
   L.parent = -1;
@@ -601,7 +602,10 @@ constexpr int kHistUnroll = MTB_HIST_UNROLL;  // bin loads in flight per warp (d
 constexpr int kHistThreads = MTB_HIST_THREADS;
 constexpr int kHistBinsPad = 256;  // bins per feature in the shared-memory layout
 // shared memory after the cells: the staged batch items and their built-row prefix sums
-constexpr int kHistBatchSmem = (int)((sizeof(BatchItem) * kMaxBatch + sizeof(long long) * (kMaxBatch + 1) + 15) / 16 * 16);
+// (and 64 words of reduction scratch)
+constexpr int kHistBatchSmem =
+    (int)((sizeof(BatchItem) * kMaxBatch + sizeof(long long) * (kMaxBatch + 1) + 64 * sizeof(unsigned int) + 15) /
+          16 * 16);
 
 // Atomic add to a shared-memory word whose result is not needed.  No memory
 // clobber: the cells are read only after a block or cluster barrier (which
@@ -622,7 +626,7 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
                              long long seg_n, const uint8_t* __restrict__ bins_rm, int Fp, int F, int B,
                              const int* __restrict__ rows0, const int* __restrict__ rows1,
                              const void* __restrict__ pairs0, const void* __restrict__ pairs1, int* hs,
-                             long long rows_per_flush, int g_lim, unsigned int* p0) {
+                             long long rows_per_flush, int g_lim, unsigned int* p0, unsigned int* s_red) {
   constexpr bool PR = LAYOUT == HL_QUANT16R;          // row id packed with the gradient pair
   constexpr bool Q16 = LAYOUT == HL_QUANT16 || PR;     // 16-bit packed cells
   static_assert(!Q16 || NPL % 2 == 0, "packed cells pair features");
@@ -637,7 +641,10 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
   const long long s = seg_b + crank * sub;
   long long e = s + sub;
   if (e > seg_b + seg_n) e = seg_b + seg_n;
-  const long long n_pass = (sub + rows_per_flush - 1) / rows_per_flush;
+  // 16-bit packed cells take the segment in one pass: the rows go in windows
+  // the cells' headroom allows (below), so the cluster merges once
+  const long long pass_rows = Q16 ? (1ll << 40) : rows_per_flush;
+  const long long n_pass = (sub + pass_rows - 1) / pass_rows;
   const int f0 = blockIdx.x * FG;
   // cells are laid out for 256 bins whatever B is, so every plane and
   // feature offset below is a compile-time constant
@@ -676,11 +683,68 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
       }
     }
   };
+  // Q16: after a window of rows, the largest field of this CTA's cells
+  // bounds how many more rows the cells take without a carry (every row adds
+  // at most 2 g_lim to a g + g_lim or h field and 1 to a count); when that is
+  // under a chunk per warp, the CTA adds its cells to the work slot and
+  // starts again from zero (rare: a cell must have taken about 16k rows).
+  auto headroom = [&]() -> long long {
+    __syncthreads();
+    unsigned int mgh = 0u, mc = 0u;
+    for (int c = threadIdx.x; c < cells; c += blockDim.x) {
+      const unsigned int x = p0[c];
+      mgh = max(mgh, x & 0xffffu);
+      mc = max(mc, x >> 16);
+    }
+    for (int c = threadIdx.x; c < cells / 2; c += blockDim.x) {
+      const unsigned int x = p0[cells + c];
+      mgh = max(mgh, max(x & 0xffffu, x >> 16));
+    }
+    mgh = __reduce_max_sync(0xffffffffu, mgh);
+    mc = __reduce_max_sync(0xffffffffu, mc);
+    if (lane == 0) {
+      s_red[warp] = mgh;
+      s_red[32 + warp] = mc;
+    }
+    __syncthreads();
+    mgh = 0u;
+    mc = 0u;
+    for (int w = 0; w < n_warps; ++w) {
+      mgh = max(mgh, s_red[w]);
+      mc = max(mc, s_red[32 + w]);
+    }
+    const long long step = 2ll * (g_lim > 0 ? g_lim : 1);
+    long long ok = (65535ll - (long long)mgh) / step;
+    if (65535ll - (long long)mc < ok) ok = 65535ll - (long long)mc;
+    if (ok < 32ll * n_warps) {
+      for (int c = threadIdx.x; c < cells; c += blockDim.x) {
+        const unsigned int x = p0[c];
+        const int l = c & 31, jb = c >> 5, j = jb / kHistBinsPad, bin = jb % kHistBinsPad;
+        const int f = f0 + l * NPL + j;
+        const int cnt = (int)(x >> 16);
+        if (f < F && bin < B && cnt > 0) {
+          const int h = (int)((p0[cells + ((((j >> 1) * kHistBinsPad + bin) << 5) + l)] >> (16 * (j & 1))) & 0xffffu);
+          int* cellp = hs + (f * 3) * B + bin;
+          atomicAdd(cellp, (int)(x & 0xffffu) - g_lim * cnt);
+          atomicAdd(cellp + B, h);
+          atomicAdd(cellp + 2 * B, cnt);
+        }
+      }
+      __syncthreads();
+      for (int c = threadIdx.x; c < words; c += blockDim.x) p0[c] = 0u;
+      ok = rows_per_flush;
+    }
+    __syncthreads();
+    return ok;
+  };
   for (long long pass = 0; pass < n_pass; ++pass) {
-    const long long ps = s + pass * rows_per_flush;
-    const long long pe = ps + rows_per_flush < e ? ps + rows_per_flush : e;
+    const long long ps0 = s + pass * pass_rows;
+    const long long pe0 = ps0 + pass_rows < e ? ps0 + pass_rows : e;
     for (int c = threadIdx.x; c < words; c += blockDim.x) p0[c] = 0u;
     __syncthreads();
+    long long window = rows_per_flush;  // rows the cells take before the next headroom check
+    for (long long ps = ps0; ps < pe0;) {
+    const long long pe = Q16 && ps + window < pe0 ? ps + window : pe0;
     // Each warp takes chunks of 32 consecutive positions: lane k loads the
     // row id and gradient pair of position k (coalesced; the next chunk's are
     // fetched while this one is processed), then the warp walks the chunk with
@@ -809,6 +873,9 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
           add_row(BinWord<NPL>::load(bcol + (size_t)(unsigned int)r * (unsigned int)Fp), x0, x1);
         }
       }
+    }
+    ps = pe;
+    if (ps < pe0) window = headroom();
     }
     cluster.sync();
     // Merge: cell c of every CTA of the cluster (DSMEM), two cells per thread
@@ -996,6 +1063,7 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__
   constexpr int kCellBytes = 4 * hist_layout_words(LAYOUT, NPL * kHistBinsPad * 32);
   BatchItem* s_items = reinterpret_cast<BatchItem*>(smem_raw + kCellBytes);
   long long* s_pre = reinterpret_cast<long long*>(s_items + kMaxBatch);
+  unsigned int* s_red = reinterpret_cast<unsigned int*>(s_pre + kMaxBatch + 1);  // 64 words
   const int n_items = batch->n_items;  // uniform across the grid
   if (n_items == 0) return;
   {
@@ -1048,7 +1116,7 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__
       else
         hist_segment<NPL, LAYOUT>(cluster, P, b + (s0 - acc), s1 - s0, bins_rm, Fp, F, B, rows0, rows1, pairs0,
                                   pairs1, hist + (long long)(work_base + P.work) * slot_cells, rows_per_flush, g_lim,
-                                  p0);
+                                  p0, s_red);
     }
   }
 }
@@ -1859,6 +1927,7 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
     }
     if (nl >= L_max) stop = 1;
     if (lane == 0) {
+      H.pick_steps += n_commit + 1;
       s_ncommit = n_commit;
       s_nl = nl;
       s_stop = stop;
@@ -1961,7 +2030,10 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
         else ++n_sel;
         ++vleaves;
       }
-      if (lane == 0) s_nsel = n_sel;
+      if (lane == 0) {
+        s_nsel = n_sel;
+        H.pick_steps += vleaves - nl;
+      }
     }
     __syncthreads();
     if (w == 0) {
@@ -2062,8 +2134,7 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
     if (host_done) {
       // mapped host memory: the host learns without a copy in the stream
       volatile int* hd = host_done;
-      hd[host_done_index] = H.done ? 1 : 0;
-      __threadfence_system();
+      hd[host_done_index] = H.done ? 1 : 0;  // read after the host synchronises on this iteration's event
     }
   }
 }
@@ -2079,23 +2150,38 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
 // ancestor (the first record up the chain with a node id).  The table holds
 // the non-empty records sorted by range start (their starts are distinct).
 __global__ void __launch_bounds__(1024) k_leaf_table(TreeState* __restrict__ ts, long long* __restrict__ begins,
-                                                     int* __restrict__ order, double* __restrict__ values) {
+                                                     int* __restrict__ bufs, double* __restrict__ values,
+                                                     int stage_cap) {
+  // the leaf records' range starts, staged once when they fit (the rank of a
+  // record is the number of non-empty unexpanded records that start before it)
+  extern __shared__ long long s_begin[];  // n_pool entries, or none
   __shared__ int s_n;
   const int n_pool = ts->hdr.n_pool;
+  const bool staged = n_pool <= stage_cap;
+  auto begin_of = [&](int k) -> long long {
+    if (staged) return s_begin[k];
+    const LeafRec& Lk = ts->pool[k];
+    return (Lk.state == 0 && Lk.count > 0) ? Lk.begin : -1;
+  };
   if (threadIdx.x == 0) s_n = 0;
+  if (staged)
+    for (int k = threadIdx.x; k < n_pool; k += blockDim.x) {
+      const LeafRec& Lk = ts->pool[k];
+      s_begin[k] = (Lk.state == 0 && Lk.count > 0) ? Lk.begin : -1;
+    }
   __syncthreads();
   for (int i = threadIdx.x; i < n_pool; i += blockDim.x) {
-    const LeafRec& Li = ts->pool[i];
-    if (Li.state != 0 || Li.count <= 0) continue;
+    const long long bi = begin_of(i);
+    if (bi < 0) continue;
     int rank = 0;
     for (int k = 0; k < n_pool; ++k) {
-      const LeafRec& Lk = ts->pool[k];
-      if (Lk.state == 0 && Lk.count > 0 && Lk.begin < Li.begin) ++rank;
+      const long long bk = begin_of(k);
+      if (bk >= 0 && bk < bi) ++rank;
     }
     int a = i;
     while (ts->pool[a].node < 0) a = ts->pool[a].parent;
-    begins[rank] = Li.begin;
-    order[rank] = i;
+    begins[rank] = bi;
+    bufs[rank] = ts->pool[i].buf;
     values[rank] = ts->pool[a].value;
     atomicAdd(&s_n, 1);
   }
@@ -2104,25 +2190,46 @@ __global__ void __launch_bounds__(1024) k_leaf_table(TreeState* __restrict__ ts,
 }
 
 // raw[row * K + k] = fma(lr, value(leaf of row), raw[row * K + k])
-// (boosting.mojo:1991-2111, explicit fused multiply-add).
-__global__ void k_update_raw(const TreeState* __restrict__ ts, const long long* __restrict__ begins,
-                             const int* __restrict__ order, const double* __restrict__ values,
-                             const int* __restrict__ rows0, const int* __restrict__ rows1, double* __restrict__ raw,
-                             long long n, int K, int k, double lr) {
-  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
+// (boosting.mojo:1991-2111, explicit fused multiply-add).  The leaf table
+// (range starts, row buffers, values; at most kMaxPool entries) is staged in
+// shared memory by every block, and each position finds its entry there.
+__global__ void __launch_bounds__(256) k_update_raw(const TreeState* __restrict__ ts,
+                                                    const long long* __restrict__ begins,
+                                                    const int* __restrict__ bufs, const double* __restrict__ values,
+                                                    const int* __restrict__ rows0, const int* __restrict__ rows1,
+                                                    double* __restrict__ raw, long long n, int K, int k, double lr,
+                                                    int stage_cap) {
+  extern __shared__ long long s_tab[];  // stage_cap entries: begin, value (as bits), buffer
+  long long* s_begin = s_tab;
+  double* s_val = reinterpret_cast<double*>(s_tab + stage_cap);
+  int* s_buf = reinterpret_cast<int*>(s_val + stage_cap);
   const int nt = ts->hdr.n_table;
-  int lo = 0, hi = nt - 1;
-  while (lo < hi) {
-    int mid = (lo + hi + 1) >> 1;
-    if (begins[mid] <= i) lo = mid;
-    else hi = mid - 1;
+  const bool staged = nt <= stage_cap;
+  if (staged)
+    for (int t = threadIdx.x; t < nt; t += blockDim.x) {
+      s_begin[t] = begins[t];
+      s_buf[t] = bufs[t];
+      s_val[t] = values[t];
+    }
+  __syncthreads();
+  if (!staged) {
+    s_begin = const_cast<long long*>(begins);
+    s_buf = const_cast<int*>(bufs);
+    s_val = const_cast<double*>(values);
   }
-  const LeafRec* L = &ts->pool[order[lo]];
-  const int* rows = L->buf ? rows1 : rows0;
-  int r = rows[i];
-  double* p = raw + (long long)r * K + k;
-  *p = fma(lr, values[lo], *p);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    int lo = 0, hi = nt - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_begin[mid] <= i) lo = mid;
+      else hi = mid - 1;
+    }
+    const int* rows = s_buf[lo] ? rows1 : rows0;
+    const int r = rows[i];
+    double* p = raw + (long long)r * K + k;
+    *p = fma(lr, s_val[lo], *p);
+  }
 }
 
 }  // namespace

@@ -374,10 +374,15 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   DevBuf<FeatBest> d_fb;
   d_fb.alloc((size_t)2 * batch_cap * F);
   DevBuf<long long> d_begins;
-  DevBuf<int> d_order;
+  DevBuf<int> d_bufs;
   DevBuf<double> d_values;
   d_begins.alloc(kMaxPool);
-  d_order.alloc(kMaxPool);
+  d_bufs.alloc(kMaxPool);
+  // leaf-table entries the raw update stages in shared memory (20 B each;
+  // larger tables are searched in global memory), and its grid: a few
+  // resident blocks per SM, each staging the table once
+  const int table_stage = std::min(4 * cfg.num_leaves + 2 * kMaxBatch + 2, 2400);
+  const unsigned update_grid = (unsigned)std::max(1ll, std::min<long long>((N + 255) / 256, (long long)n_sm * 8));
   d_values.alloc(kMaxPool);
   host_sync();
   mark("work buffers");
@@ -685,10 +690,11 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
         launched++;
       }
       stats.hist_launches += launched;
-      k_leaf_table<<<1, 1024, 0, st>>>(d_ts.p, d_begins.p, d_order.p, d_values.p);
-      k_update_raw<<<grid256, 256, 0, st>>>(d_ts.p, d_begins.p, d_order.p, d_values.p, d_rows0.p, d_rows1.p,
-                                            d_raw.p, N, K, k,
-                                            cfg.learning_rate);
+      k_leaf_table<<<1, 1024, sizeof(long long) * table_stage, st>>>(d_ts.p, d_begins.p, d_bufs.p, d_values.p,
+                                                                      table_stage);
+      k_update_raw<<<update_grid, 256, 20 * (size_t)table_stage, st>>>(d_ts.p, d_begins.p, d_bufs.p, d_values.p,
+                                                                      d_rows0.p, d_rows1.p, d_raw.p, N, K, k,
+                                                                      cfg.learning_rate, table_stage);
       launches += 2;
       MTB_CUDA(cudaGetLastError());
       MTB_CUDA(cudaMemcpyAsync(&hdr, &d_ts.p->hdr, sizeof(TreeHeader), cudaMemcpyDeviceToHost, st));
@@ -699,6 +705,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       if (hdr.error || !hdr.done) throw std::runtime_error("device trainer reported an internal error");
       stats.iterations += hdr.iterations;
       stats.expansions += (hdr.n_pool - 1) / 2;
+      stats.pick_steps += hdr.pick_steps;
       if (coll) coll->check();
       std::vector<HostNode> tree(nodes_host.begin(), nodes_host.begin() + hdr.n_nodes);
       bool trivial = hdr.n_leaves == 1 && std::fabs(tree[0].value) < 1e-12;
