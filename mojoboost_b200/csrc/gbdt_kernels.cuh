@@ -683,59 +683,62 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
       }
     }
   };
-  // Q16: after a window of rows, the largest field of this CTA's cells
-  // bounds how many more rows the cells take without a carry (every row adds
-  // at most 2 g_lim to a g + g_lim or h field and 1 to a count); when that is
-  // under a chunk per warp, the CTA adds its cells to the work slot and
-  // starts again from zero (rare: a cell must have taken about 16k rows).
+  // Q16: after a window of rows, every cell word of a real feature whose
+  // largest field passed half its range goes to the work slot (its fields
+  // added with int32 atomics, the word zeroed); the largest field left then
+  // bounds the rows the next window may take without a carry (a row adds at
+  // most 2 g_lim to a g + g_lim or h field and 1 to a count).  Cells of
+  // padding features (>= F) are never read and are left to wrap.
   auto headroom = [&]() -> long long {
+    constexpr unsigned int kHot = 32767u;
     __syncthreads();
-    unsigned int mgh = 0u, mc = 0u;
-    for (int c = threadIdx.x; c < cells; c += blockDim.x) {
-      const unsigned int x = p0[c];
-      mgh = max(mgh, x & 0xffffu);
-      mc = max(mc, x >> 16);
-    }
-    for (int c = threadIdx.x; c < cells / 2; c += blockDim.x) {
-      const unsigned int x = p0[cells + c];
-      mgh = max(mgh, max(x & 0xffffu, x >> 16));
-    }
-    mgh = __reduce_max_sync(0xffffffffu, mgh);
-    mc = __reduce_max_sync(0xffffffffu, mc);
-    if (lane == 0) {
-      s_red[warp] = mgh;
-      s_red[32 + warp] = mc;
-    }
-    __syncthreads();
-    mgh = 0u;
-    mc = 0u;
-    for (int w = 0; w < n_warps; ++w) {
-      mgh = max(mgh, s_red[w]);
-      mc = max(mc, s_red[32 + w]);
-    }
+    unsigned int mx = 0u;
     const long long step = 2ll * (g_lim > 0 ? g_lim : 1);
-    long long ok = (65535ll - (long long)mgh) / step;
-    if (65535ll - (long long)mc < ok) ok = 65535ll - (long long)mc;
-    if (ok < 32ll * n_warps) {
-      for (int c = threadIdx.x; c < cells; c += blockDim.x) {
-        const unsigned int x = p0[c];
-        const int l = c & 31, jb = c >> 5, j = jb / kHistBinsPad, bin = jb % kHistBinsPad;
-        const int f = f0 + l * NPL + j;
-        const int cnt = (int)(x >> 16);
-        if (f < F && bin < B && cnt > 0) {
-          const int h = (int)((p0[cells + ((((j >> 1) * kHistBinsPad + bin) << 5) + l)] >> (16 * (j & 1))) & 0xffffu);
+    for (int c = threadIdx.x; c < cells; c += blockDim.x) {  // plane A: g + g_lim | count << 16
+      const int l = c & 31, jb = c >> 5, j = jb / kHistBinsPad, bin = jb % kHistBinsPad;
+      const int f = f0 + l * NPL + j;
+      if (f >= F) continue;
+      const unsigned int x = p0[c];
+      const unsigned int g = x & 0xffffu, cnt = x >> 16;
+      // the count field's load in units of the g field's per-row step
+      const long long cl_ = (long long)cnt * step;
+      const unsigned int load = max(g, (unsigned int)(cl_ < 65535ll ? cl_ : 65535ll));
+      if (load > kHot) {
+        if (bin < B) {
           int* cellp = hs + (f * 3) * B + bin;
-          atomicAdd(cellp, (int)(x & 0xffffu) - g_lim * cnt);
-          atomicAdd(cellp + B, h);
-          atomicAdd(cellp + 2 * B, cnt);
+          atomicAdd(cellp, (int)g - g_lim * (int)cnt);
+          atomicAdd(cellp + 2 * B, (int)cnt);
         }
+        p0[c] = 0u;
+      } else {
+        mx = max(mx, load);
       }
-      __syncthreads();
-      for (int c = threadIdx.x; c < words; c += blockDim.x) p0[c] = 0u;
-      ok = rows_per_flush;
     }
+    for (int c = threadIdx.x; c < cells / 2; c += blockDim.x) {  // plane B: h of features 2k, 2k+1
+      const int l = c & 31, jb = c >> 5, j2 = jb / kHistBinsPad, bin = jb % kHistBinsPad;
+      const int fa = f0 + l * NPL + 2 * j2;
+      if (fa >= F) continue;
+      const unsigned int x = p0[cells + c];
+      const unsigned int ha = x & 0xffffu, hb = x >> 16;
+      if (ha > kHot || hb > kHot) {
+        if (bin < B) {
+          atomicAdd(hs + (fa * 3 + 1) * B + bin, (int)ha);
+          if (fa + 1 < F) atomicAdd(hs + ((fa + 1) * 3 + 1) * B + bin, (int)hb);
+        }
+        p0[cells + c] = 0u;
+      } else {
+        mx = max(mx, max(ha, hb));
+      }
+    }
+    mx = __reduce_max_sync(0xffffffffu, mx);
+    if (lane == 0) s_red[warp] = mx;
     __syncthreads();
-    return ok;
+    mx = 0u;
+    for (int w = 0; w < n_warps; ++w) mx = max(mx, s_red[w]);
+    __syncthreads();  // zeroed words and s_red reads complete before the next window
+    // mx <= kHot, so every window takes at least (65535 - kHot) / step >= 1024 rows
+    const long long ok = (65535ll - (long long)mx) / step;
+    return ok > 1 ? ok : 1;
   };
   for (long long pass = 0; pass < n_pass; ++pass) {
     const long long ps0 = s + pass * pass_rows;

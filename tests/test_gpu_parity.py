@@ -64,6 +64,10 @@ CASES = {
                       dict(objective="binary", rounds=3, leaves=63, quant=True, extra={"num_grad_quant_bins": 6}), 255),
     "binary_quant_skewed": (dict(seed=25, n=400_000, f=40, kind="binary", zero_frac=0.97),
                             dict(objective="binary", rounds=3, leaves=127, quant=True), 63),
+    # more than 16k rows per CTA at the root: the 16-bit cells take several
+    # windows, and the dominant bins' cells go to the work slot between them
+    "binary_quant_skewed_large": (dict(seed=26, n=3_000_000, f=8, kind="binary", zero_frac=0.97),
+                                  dict(objective="binary", rounds=2, leaves=31, quant=True), 63),
     # fixed point with the 2^52 bound and Int64 cells (gpu_histogram_precision=int64)
     "l2_fixed52": (dict(seed=19, n=50_000, f=28), dict(objective="regression", rounds=4, leaves=63,
                                                       extra={"gpu_histogram_precision": "int64"}), 255),
