@@ -424,18 +424,33 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const unsigned below = (1u << lane) - 1u;
   int par = 0;
+  // exclusive prefixes of the (item row, warp) counts in element order,
+  // written over the counts by warp 0 between the two barriers
+  constexpr int E = ITEMS * 8;
+  constexpr int PER = (E + 31) / 32;
   for (long long tile = blockIdx.x; tile < Bt.n_tiles; tile += gridDim.x, par ^= 1) {
     int it = 0;
-    while (it + 1 < n_items && s_items[it + 1].tile0 <= tile) ++it;
+    {
+      int hi = n_items - 1;  // the last item whose first tile is <= tile
+      while (it < hi) {
+        const int mid = (it + hi + 1) >> 1;
+        if (s_items[mid].tile0 <= tile) it = mid;
+        else hi = mid - 1;
+      }
+    }
     const BatchItem& P = s_items[it];
     BatchItem& PG = Bt.items[it];  // the item's cursors live in global memory
-    const int* src_rows = P.src_buf ? rows1 : rows0;
-    int* dst_rows = P.src_buf ? rows0 : rows1;
-    const PairT* src_pairs = P.src_buf ? pairs1 : pairs0;
-    PairT* dst_pairs = P.src_buf ? pairs0 : pairs1;
+    const int src_buf = P.src_buf;
+    const int* src_rows = src_buf ? rows1 : rows0;
+    int* dst_rows = src_buf ? rows0 : rows1;
+    const PairT* src_pairs = src_buf ? pairs1 : pairs0;
+    PairT* dst_pairs = src_buf ? pairs0 : pairs1;
     const uint8_t* col = bins_cm + (long long)P.feature * n;
     const long long begin = P.begin, end = P.begin + P.count;
     const long long t0 = begin + (tile - P.tile0) * TILE;
+    const bool is_cat = P.is_cat != 0;
+    const int thr = P.threshold, mbin = P.missing_bin;
+    const bool dleft = P.default_left != 0;
     int rr[ITEMS];
     PairT pp[ITEMS];
     unsigned bl[ITEMS], br[ITEMS];
@@ -444,11 +459,17 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
     for (int j = 0; j < ITEMS; ++j) {  // every gather in flight before the first ballot
       const long long i = t0 + (long long)j * 256 + threadIdx.x;
       valid[j] = i < end;
-      left[j] = false;
       if (valid[j]) {
         rr[j] = src_rows[i];
         pp[j] = src_pairs[i];
-        left[j] = goes_left(P, col[rr[j]]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+      left[j] = false;
+      if (valid[j]) {
+        const int bin = col[rr[j]];
+        left[j] = is_cat ? goes_left(P, bin) : (bin == mbin ? dleft : bin <= thr);
       }
     }
 #pragma unroll
@@ -461,42 +482,58 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
       }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int tl = 0, tr = 0;
-      for (int j = 0; j < ITEMS; ++j)
-        for (int k = 0; k < 8; ++k) {
-          tl += s_cl[par][j][k];
-          tr += s_cr[par][j][k];
+    if (w == 0) {
+      int* fl = &s_cl[par][0][0];
+      int* fr = &s_cr[par][0][0];
+      int vl[PER], vr[PER];
+      int sl = 0, sr = 0;
+#pragma unroll
+      for (int q = 0; q < PER; ++q) {
+        const int e = lane * PER + q;
+        vl[q] = e < E ? fl[e] : 0;
+        vr[q] = e < E ? fr[e] : 0;
+        sl += vl[q];
+        sr += vr[q];
+      }
+      int il = sl, ir = sr;
+#pragma unroll
+      for (int k = 1; k < 32; k <<= 1) {
+        const int ol = __shfl_up_sync(0xffffffffu, il, k), orr = __shfl_up_sync(0xffffffffu, ir, k);
+        if (lane >= k) {
+          il += ol;
+          ir += orr;
         }
-      s_base_l[par] = atomicAdd(&PG.cursor_left, (unsigned long long)tl);
-      const unsigned long long o = atomicAdd(&PG.cursor_right, (unsigned long long)tr);
-      s_base_r[par] = (unsigned long long)end - o - (unsigned long long)tr;  // rights fill from the back
+      }
+      int rl = il - sl, rrr = ir - sr;
+#pragma unroll
+      for (int q = 0; q < PER; ++q) {
+        const int e = lane * PER + q;
+        if (e < E) {
+          fl[e] = rl;
+          fr[e] = rrr;
+        }
+        rl += vl[q];
+        rrr += vr[q];
+      }
+      const int tl = __shfl_sync(0xffffffffu, il, 31), tr = __shfl_sync(0xffffffffu, ir, 31);
+      if (lane == 0) {
+        s_base_l[par] = atomicAdd(&PG.cursor_left, (unsigned long long)tl);
+        const unsigned long long o = atomicAdd(&PG.cursor_right, (unsigned long long)tr);
+        s_base_r[par] = (unsigned long long)end - o - (unsigned long long)tr;  // rights fill from the back
+      }
     }
     __syncthreads();
     // ranks in element order (item row j major, then warp, then lane)
-    long long run_l = begin + (long long)s_base_l[par], run_r = (long long)s_base_r[par];
+    const long long base_l = begin + (long long)s_base_l[par], base_r = (long long)s_base_r[par];
 #pragma unroll
     for (int j = 0; j < ITEMS; ++j) {
-      int pre_l = 0, pre_r = 0, tot_l = 0, tot_r = 0;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int cl = s_cl[par][j][k], cr = s_cr[par][j][k];
-        if (k < w) {
-          pre_l += cl;
-          pre_r += cr;
-        }
-        tot_l += cl;
-        tot_r += cr;
-      }
       const unsigned m = 1u << lane;
       if ((bl[j] | br[j]) & m) {
-        const long long dst = (bl[j] & m) ? run_l + pre_l + __popc(bl[j] & below)
-                                          : run_r + pre_r + __popc(br[j] & below);
+        const long long dst = (bl[j] & m) ? base_l + s_cl[par][j][w] + __popc(bl[j] & below)
+                                          : base_r + s_cr[par][j][w] + __popc(br[j] & below);
         dst_rows[dst] = rr[j];
         dst_pairs[dst] = pp[j];
       }
-      run_l += tot_l;
-      run_r += tot_r;
     }
   }
 }
