@@ -408,7 +408,10 @@ def run_gpu(args):
     hist_ms = float(np.sum(rs[:, 1]))
     hist_launches = float(np.sum(rs[:, 2]))
     hist_rows = float(np.sum(rs[:, 3]))
-    hist_bytes = hist_rows * (F + pair_bytes)
+    # the tree's counts are global: with several ranks this rank's histogram
+    # launches read about its share of them (the shards are equal in size)
+    hist_rows_local = hist_rows * n_local / n_global if world > 1 else hist_rows
+    hist_bytes = hist_rows_local * (F + pair_bytes)
     hist_gbs = hist_bytes / (hist_ms / 1000.0) / 1e9 if hist_ms > 0 else None
     per_round = 1.0 / max(1, st["rounds"])
     phases = {"hist_ms": st["hist_ms"] * per_round}
@@ -418,7 +421,7 @@ def run_gpu(args):
                    "hist_launches_timed": hist_launches, "hist_rows_timed": hist_rows})
     smem_peak = mb.shared_atomic_peak() if hist_ms > 0 else None
     # useful shared atomics of the histogram: (g+count word, h word) per row and feature
-    smem_achieved = hist_rows * F * 2 / (hist_ms / 1000.0) if hist_ms > 0 else None
+    smem_achieved = hist_rows_local * F * 2 / (hist_ms / 1000.0) if hist_ms > 0 else None
     peak, peak_kind = measured_peak()
     e2e = None
     if world == 1 and not args.no_e2e:
@@ -460,10 +463,12 @@ def run_gpu(args):
                    **({"dp_exchange": os.environ.get("MOJOTREES_DP_EXCHANGE", "allreduce")} if world > 1 else {})},
         "roofline": {"bound": "hbm", "achieved": hist_gbs, "peak": peak, "unit": "GB/s",
                      "frac": (hist_gbs / peak) if hist_gbs else None,
-                     "traffic": (HIST_DRAM_BYTES_PER_ROW * hist_rows / hist_launches)
+                     "traffic": (HIST_DRAM_BYTES_PER_ROW * hist_rows_local / hist_launches)
                      if hist_launches and cfg == "c2" else None,
                      "peak_source": peak_kind, "kernel": "k_hist",
-                     "algorithmic_bytes": f"per launch: rows of the built children x ({F} bin bytes + "
+                     "algorithmic_bytes": ("with several ranks: this rank's share of the built rows (global / "
+                                           "ranks); " if world > 1 else "") +
+                                          f"per launch: rows of the built children x ({F} bin bytes + "
                                           f"{pair_bytes} gradient bytes); achieved = their sum over the timed "
                                           "rounds / the summed CUDA-event time of the histogram launches",
                      "traffic_source": "ncu dram read+write bytes per row of the k_hist capture "
