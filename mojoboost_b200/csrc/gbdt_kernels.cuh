@@ -918,55 +918,78 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
     if (ps < pe0) window = headroom();
     }
     cluster.sync();
-    // Merge: cell c of every CTA of the cluster (DSMEM), two cells per thread
-    // at a time with every rank's words loaded before any is used, then one
-    // int32 global atomic per plane into the item's work slot.
-    auto add_cell = [&](const unsigned int* q0, int c, int& g, int& h, int& cnt) {
-      const unsigned int* q1 = q0 + cells;
-      if (Q16) {
-        const int l = c & 31, jb = c >> 5, j = jb / kHistBinsPad, bin = jb % kHistBinsPad;
-        const unsigned int x = q0[c];
-        cnt += (int)(x >> 16);
-        g += (int)(x & 0xffffu);
-        h += (int)((q1[(((j >> 1) * kHistBinsPad + bin) << 5) + l] >> (16 * (j & 1))) & 0xffffu);
-      } else if (LAYOUT == HL_QUANT) {
-        const unsigned int x = q0[c];
-        cnt += (int)(x & ((1u << kQuantCountBits) - 1u));
-        g += (int)x >> kQuantCountBits;
-        h += (int)q1[c];
-      } else if (CONST_H) {
-        g += (int)q0[c];
-        cnt += (int)q1[c];
-      } else {
-        g += (int)q0[c];
-        h += (int)q1[c];
-        cnt += (int)q1[c + cells];
-      }
-    };
-    auto emit_cell = [&](int c, int g, int h, int cnt) {
-      const int l = c & 31, jb = c >> 5, j = jb / kHistBinsPad, bin = jb % kHistBinsPad;
-      const int f = f0 + l * NPL + j;
-      if (f >= F || bin >= B || cnt == 0) return;
-      if (Q16) g -= g_lim * cnt;  // sum of (g + g_lim) -> sum of g
-      int* cellp = hs + (f * 3) * B + bin;
-      atomicAdd(cellp, g);
-      if (!(MODE == MODE_FIXED && CONST_H)) atomicAdd(cellp + B, h);
-      atomicAdd(cellp + 2 * B, cnt);
-    };
-    for (int c = m0 + threadIdx.x; c < m1; c += 2 * blockDim.x) {
-      const int c2 = c + blockDim.x;
-      const bool two = c2 < m1;
-      int g0 = 0, h0 = 0, n0 = 0, g1 = 0, h1 = 0, n1 = 0;
+    // Merge, one tile of cells per warp at a time: 16 consecutive bins of
+    // one feature slot j for all 32 lanes (512 consecutive words).  Each
+    // plane's values are summed over the cluster's CTAs (DSMEM) with lane =
+    // feature, transposed in registers within each half-warp to lane = bin,
+    // and added to the work slot with int32 atomics whose lanes hit two runs
+    // of 16 consecutive cells (4 sectors a warp instruction instead of 32;
+    // about 5x faster through L2 than the lane = feature order).
+    {
+      constexpr int kPlanes = (MODE == MODE_FIXED && CONST_H) ? 2 : 3;  // g, [h,] count
+      const int tiles = (m1 - m0) >> 9;
+      const int half = lane >> 4, hl = lane & 15;
+      for (int t = warp; t < tiles; t += n_warps) {
+        const int c0 = m0 + (t << 9);
+        const int j = (c0 >> 5) / kHistBinsPad, bin0 = (c0 >> 5) % kHistBinsPad;
+#pragma unroll 1
+        for (int plane = 0; plane < kPlanes; ++plane) {
+          const int out_plane = (kPlanes == 2 && plane == 1) ? 2 : plane;  // constant hessian: g, count
+          int v[16];
 #pragma unroll
-      for (int rk = 0; rk < 8; ++rk) {
-        if (rk < cs) {
-          const unsigned int* q0 = cluster.map_shared_rank(p0, rk);
-          add_cell(q0, c, g0, h0, n0);
-          if (two) add_cell(q0, c2, g1, h1, n1);
+          for (int i = 0; i < 16; ++i) v[i] = 0;
+          for (int rk = 0; rk < cs; ++rk) {
+            const unsigned int* q0 = cluster.map_shared_rank(p0, rk);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int c = c0 + (i << 5) + lane;
+              if (Q16) {
+                if (plane == 1) {
+                  const unsigned int x = q0[cells + ((((j >> 1) * kHistBinsPad + bin0 + i) << 5) + lane)];
+                  v[i] += (int)((x >> (16 * (j & 1))) & 0xffffu);
+                } else {
+                  const unsigned int x = q0[c];
+                  v[i] += plane == 0 ? (int)(x & 0xffffu) - g_lim * (int)(x >> 16) : (int)(x >> 16);
+                }
+              } else if (LAYOUT == HL_QUANT) {
+                if (plane == 1) {
+                  v[i] += (int)q0[cells + c];
+                } else {
+                  const unsigned int x = q0[c];
+                  v[i] += plane == 0 ? ((int)x >> kQuantCountBits) : (int)(x & ((1u << kQuantCountBits) - 1u));
+                }
+              } else {
+                // fixed point: planes g, h, count (constant hessian: g, count)
+                v[i] += (int)q0[plane * cells + c];
+              }
+            }
+          }
+          // 16 x 16 transposes within each half-warp: lane 16 h + m, v[i] =
+          // cell (lane 16 h + m, bin i) becomes lane 16 h + i, v[m] = cell
+          // (lane 16 h + m, bin i)
+#pragma unroll
+          for (int sft = 8; sft >= 1; sft >>= 1) {
+            const bool upper = (lane & sft) != 0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              if ((i & sft) == 0) {
+                const int send = upper ? v[i] : v[i + sft];
+                const int recv = __shfl_xor_sync(0xffffffffu, send, sft);
+                if (upper)
+                  v[i] = recv;
+                else
+                  v[i + sft] = recv;
+              }
+            }
+          }
+          const int bin = bin0 + hl;
+#pragma unroll
+          for (int m = 0; m < 16; ++m) {
+            const int f = f0 + (16 * half + m) * NPL + j;
+            if (f < F && bin < B && v[m] != 0) atomicAdd(hs + (f * 3 + out_plane) * B + bin, v[m]);
+          }
         }
       }
-      emit_cell(c, g0, h0, n0);
-      if (two) emit_cell(c2, g1, h1, n1);
     }
     cluster.sync();  // peers finished reading before anyone re-zeroes
   }
