@@ -1928,16 +1928,23 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
     }                                                          \
   } while (0)
   auto reg_pick = [&]() -> int {
-    unsigned long long best = 0ull;
-    int best_i = 0x7fffffff;
-    // ascending slot within the lane, strict >: the lowest slot wins ties
-    const unsigned long long ks[8] = {k0, k1, k2, k3, k4, k5, k6, k7};
-#pragma unroll
-    for (int q = 0; q < 8; ++q)
-      if (ks[q] > best) {
-        best = ks[q];
-        best_i = q * 32 + lane;
-      }
+    // the lane's best slot by a depth-3 tournament; on equal keys the lower
+    // slot (lower q) wins, so the lane's lowest slot holding its maximum
+    auto better = [](unsigned long long ka, int qa, unsigned long long kb, int qb, unsigned long long& k, int& q) {
+      const bool a = ka >= kb;
+      k = a ? ka : kb;
+      q = a ? qa : qb;
+    };
+    unsigned long long k01, k23, k45, k67, k03, k47, best;
+    int q01, q23, q45, q67, q03, q47, qb;
+    better(k0, 0, k1, 1, k01, q01);
+    better(k2, 2, k3, 3, k23, q23);
+    better(k4, 4, k5, 5, k45, q45);
+    better(k6, 6, k7, 7, k67, q67);
+    better(k01, q01, k23, q23, k03, q03);
+    better(k45, q45, k67, q67, k47, q47);
+    better(k03, q03, k47, q47, best, qb);
+    const int best_i = best > 0ull ? qb * 32 + lane : 0x7fffffff;
     const unsigned int hi = __reduce_max_sync(0xffffffffu, (unsigned int)(best >> 32));
     const unsigned int lo =
         __reduce_max_sync(0xffffffffu, (unsigned int)(best >> 32) == hi ? (unsigned int)best : 0u);
