@@ -302,6 +302,24 @@ int32_t mojotrees_b200_histogram_u8_noalloc(const uint8_t *bins_rm, int64_t n_ro
                                             const uint16_t *pairs, int32_t num_grad_quant_bins, int32_t *out_hist,
                                             void *stream, MojoTreesError *error);
 
+/* Training on a compressed-sparse-column matrix: indptr[n_features + 1]
+ * offsets, row indices strictly increasing within each column, values; an
+ * absent entry is the value 0.0 and a stored NaN is missing.  The bins are
+ * those of the densified matrix (the reference's sparse fit bins them
+ * identically, sparse.mojo:535-570), computed from the compressed columns:
+ * the host holds n_rows x n_features bytes of bins, never the dense float64
+ * matrix.  Replaces the sparse fit of bindings/_mojotrees.mojo:3335-3420
+ * (fit_csc); the model predicts raw feature values like a dense fit's.
+ * mojotrees_b200_bin_csc returns those bins (feature-major), missing bins,
+ * category counts (-1 for numeric features) and the bin count. */
+int32_t mojotrees_b200_train_csc(const int64_t *indptr, const int64_t *indices, const double *values,
+                                 int64_t n_rows, int64_t n_features, const double *labels, const double *weights,
+                                 const char *parameters, MojoTreesModel **out_model, MojoTreesError *error);
+int32_t mojotrees_b200_bin_csc(const int64_t *indptr, const int64_t *indices, const double *values, int64_t n_rows,
+                               int64_t n_features, const char *parameters, uint8_t *out_bins,
+                               int32_t *out_missing_bin, int32_t *out_n_categories, int32_t *out_n_bins,
+                               MojoTreesError *error);
+
 /* Diagnostic: n random (integer sum, quantizer units) pairs dequantized on
  * the device by the trainer's divide-free quotient and by the divide; the
  * number of results whose bits differ goes to out_mismatches (0 expected).

@@ -54,6 +54,8 @@ SIGNATURES = {
     "mojotrees_b200_bin_dense_gpu": (_I32, [_P, _I64, _I64, ctypes.c_char_p, _P, _P, _P, _P, _P]),
     "mojotrees_b200_shared_atomic_peak": (_I32, [_P, _P]),
     "mojotrees_b200_check_quotients": (_I32, [_I64, ctypes.c_uint64, _P, _P]),
+    "mojotrees_b200_train_csc": (_I32, [_P, _P, _P, _I64, _I64, _P, _P, ctypes.c_char_p, _P, _P]),
+    "mojotrees_b200_bin_csc": (_I32, [_P, _P, _P, _I64, _I64, ctypes.c_char_p, _P, _P, _P, _P, _P]),
     "mojotrees_b200_predict_binned_u8": (_I32, [_P, _P, _I64, _I64, _P, _I64, _P]),
     "mojotrees_b200_tree_nodes": (_I32, [_P, _I64, _P, _P, _P, _P, _I64, _P, _P]),
     "mojotrees_b200_base_scores": (_I32, [_P, _P, _I64, _P]),
@@ -411,6 +413,36 @@ def shared_atomic_peak():
     e = _Err()
     e.check(lib().mojotrees_b200_shared_atomic_peak(ctypes.byref(v), e.h))
     return v.value
+
+
+def _csc_arrays(indptr, indices, values):
+    return (np.ascontiguousarray(indptr, dtype=np.int64), np.ascontiguousarray(indices, dtype=np.int64),
+            np.ascontiguousarray(values, dtype=np.float64))
+
+
+def train_csc(indptr, indices, values, n_rows, y, params=None):
+    """Train on a CSC matrix (n_rows x len(indptr) - 1) through mojotrees_b200_train_csc."""
+    ip, ix, vv = _csc_arrays(indptr, indices, values)
+    y = np.ascontiguousarray(y, dtype=np.float64)
+    e = _Err()
+    h = ctypes.c_void_p()
+    e.check(lib().mojotrees_b200_train_csc(_ptr(ip), _ptr(ix), _ptr(vv), n_rows, ip.size - 1, _ptr(y), None,
+                                           params_string(params), ctypes.byref(h), e.h))
+    return Model(h.value)
+
+
+def bin_csc(indptr, indices, values, n_rows, params=None):
+    """The bins train_csc trains on: (bins [F, N] uint8, missing_bin, n_categories, n_bins)."""
+    ip, ix, vv = _csc_arrays(indptr, indices, values)
+    f = ip.size - 1
+    bins = np.zeros((f, n_rows), np.uint8)
+    mb = np.zeros(f, np.int32)
+    nc = np.zeros(f, np.int32)
+    nb = ctypes.c_int32(0)
+    e = _Err()
+    e.check(lib().mojotrees_b200_bin_csc(_ptr(ip), _ptr(ix), _ptr(vv), n_rows, f, params_string(params), _ptr(bins),
+                                         _ptr(mb), _ptr(nc), ctypes.byref(nb), e.h))
+    return bins, mb, nc, nb.value
 
 
 def check_quotients(n, seed=1):

@@ -269,18 +269,38 @@ def _dense_params(params):
     return {k: v for k, v in params.items() if k not in _SPARSE_KEYS}
 
 
+def _csc_buffers(params):
+    """The CSC matrix's (indptr, indices, data) at the given addresses."""
+    f, nnz = int(params["n_features"]), int(params["sparse_nnz"])
+    if f < 0 or nnz < 0:
+        raise ValueError("sparse matrix: negative shape or nnz")
+    indptr = _i64(params["sparse_indptr_addr"], f + 1)
+    indices = _i64(params["sparse_indices_addr"], nnz)
+    data = _f64(int(params["sparse_data_addr"]), nnz) if nnz else np.zeros(0)
+    return indptr, indices, data
+
+
 def fit_csc(y_addr, objective, params):
-    """A fit on a CSC matrix: the densified matrix through the dense device
-    path (the same bins and trees as the reference's sparse fit of it)."""
-    X = _densify(params, True)
-    n, f = X.shape
-    return fit(X.ctypes.data, n, f, y_addr, int(objective), _dense_params(params))
+    """A fit on a CSC matrix (bindings/_mojotrees.mojo:3335): the compressed
+    columns are binned as the densified matrix would be
+    (mojotrees_b200_train_csc), so the host holds bins, not the dense
+    float64 matrix, and the trees equal the dense fit's."""
+    n = int(params["n_rows"])
+    indptr, indices, data = _csc_buffers(params)
+    y = _f64(int(y_addr), n)
+    e = _capi._Err()
+    h = ctypes.c_void_p()
+    e.check(_capi.lib().mojotrees_b200_train_csc(
+        indptr.ctypes.data_as(ctypes.c_void_p), indices.ctypes.data_as(ctypes.c_void_p),
+        data.ctypes.data_as(ctypes.c_void_p), n, indptr.size - 1, y.ctypes.data_as(ctypes.c_void_p), None,
+        param_string(int(objective), _dense_params(params)), ctypes.byref(h), e.h))
+    return _capi.Model(h.value)
 
 
 def fit_multiclass_csc(y_addr, n_classes, params):
-    X = _densify(params, True)
-    n, f = X.shape
-    return fit_multiclass(X.ctypes.data, n, f, y_addr, n_classes, _dense_params(params))
+    p = dict(params)
+    p["num_class"] = int(n_classes)
+    return fit_csc(y_addr, MULTICLASS, p)
 
 
 def _predict_csr(model, params, out_addr, raw):

@@ -158,6 +158,75 @@ int BinMapper::bin_value(int f, double v) const {
   return (int)(left - lo);
 }
 
+// Edges of one numeric feature from its sampled non-NaN values `col`
+// (n_sample values were sampled, NaN included); sorts col.  The missing bin
+// is reserved when a sampled value was NaN (binning.mojo:3565-4047).
+static void numeric_edges(std::vector<double>& col, int64_t n_sample, const BinningParams& p,
+                          std::vector<double>& below, std::vector<double>& above, std::vector<double>& levels,
+                          std::vector<int64_t>& level_counts, std::vector<uint64_t>& key0,
+                          std::vector<uint64_t>& key1, std::vector<double>& out, int* missing) {
+  int64_t n_valid = (int64_t)col.size();
+  bool reserve = p.use_missing && n_valid < n_sample;
+  int n_ordinary = reserve ? p.max_bins - 1 : p.max_bins;
+  below.clear();
+  above.clear();
+  // Sort once; -0.0 and 0.0 compare equal and are one level.
+  sort_doubles(col, key0, key1);
+  levels.clear();
+  level_counts.clear();
+  bool distinct_fits = n_valid >= 1;
+  for (int64_t i = 0; i < n_valid && distinct_fits; ++i) {
+    double v = col[i] == 0.0 ? 0.0 : col[i];
+    if (!levels.empty() && levels.back() == v) {
+      level_counts.back() += 1;
+      continue;
+    }
+    if ((int)levels.size() >= n_ordinary) {
+      distinct_fits = false;
+      break;
+    }
+    levels.push_back(v);
+    level_counts.push_back(1);
+  }
+  if (distinct_fits) {
+    // binning.mojo:3850-3868
+    if (p.min_data_in_bin <= 1) {
+      for (size_t j = 0; j + 1 < levels.size(); ++j) {
+        below.push_back(levels[j]);
+        above.push_back(levels[j + 1]);
+      }
+    } else {
+      int64_t acc = 0;
+      for (size_t j = 0; j + 1 < levels.size(); ++j) {
+        acc += level_counts[j];
+        if (acc >= p.min_data_in_bin) {
+          below.push_back(levels[j]);
+          above.push_back(levels[j + 1]);
+          acc = 0;
+        }
+      }
+    }
+  } else {
+    // binning.mojo:3876-3957
+    int64_t n_ord = n_ordinary;
+    if (p.min_data_in_bin > 1) {
+      int64_t cap = n_valid / p.min_data_in_bin;
+      if (cap < 1) cap = 1;
+      if (cap < n_ord) n_ord = cap;
+    }
+    for (int64_t b = 1; b < n_ord; ++b) {
+      int64_t idx = b * n_valid / n_ord;
+      if (idx <= 0 || idx >= n_valid) continue;
+      double w = col[idx - 1];
+      below.push_back(w);
+      auto it = std::upper_bound(col.begin() + idx, col.end(), w);
+      above.push_back(it != col.end() ? *it : w);
+    }
+  }
+  emit_edges(below, above, out);
+  *missing = reserve ? (int)out.size() + 1 : -1;
+}
+
 BinMapper fit_bins(const double* x, int64_t n_rows, int n_features, const BinningParams& p) {
   if (p.max_bins < 2 || p.max_bins > 256) throw std::runtime_error("max_bins must be in [2, 256]");
   if (n_rows < 1) throw std::runtime_error("n_rows must be positive");
@@ -211,67 +280,8 @@ BinMapper fit_bins(const double* x, int64_t n_rows, int n_features, const Binnin
         for (int64_t r = 0; r < n_rows; ++r)
           if (!std::isnan(base[r])) col.push_back(base[r]);
       }
-      int64_t n_valid = (int64_t)col.size();
-      bool reserve = p.use_missing && n_valid < n_sample;
-      int n_ordinary = reserve ? p.max_bins - 1 : p.max_bins;
-      below.clear();
-      above.clear();
-      // Sort once; -0.0 and 0.0 compare equal and are one level.
-      sort_doubles(col, key0, key1);
-      levels.clear();
-      level_counts.clear();
-      bool distinct_fits = n_valid >= 1;
-      for (int64_t i = 0; i < n_valid && distinct_fits; ++i) {
-        double v = col[i] == 0.0 ? 0.0 : col[i];
-        if (!levels.empty() && levels.back() == v) {
-          level_counts.back() += 1;
-          continue;
-        }
-        if ((int)levels.size() >= n_ordinary) {
-          distinct_fits = false;
-          break;
-        }
-        levels.push_back(v);
-        level_counts.push_back(1);
-      }
-      if (distinct_fits) {
-        // binning.mojo:3850-3868
-        if (p.min_data_in_bin <= 1) {
-          for (size_t j = 0; j + 1 < levels.size(); ++j) {
-            below.push_back(levels[j]);
-            above.push_back(levels[j + 1]);
-          }
-        } else {
-          int64_t acc = 0;
-          for (size_t j = 0; j + 1 < levels.size(); ++j) {
-            acc += level_counts[j];
-            if (acc >= p.min_data_in_bin) {
-              below.push_back(levels[j]);
-              above.push_back(levels[j + 1]);
-              acc = 0;
-            }
-          }
-        }
-      } else {
-        // binning.mojo:3876-3957
-        int64_t n_ord = n_ordinary;
-        if (p.min_data_in_bin > 1) {
-          int64_t cap = n_valid / p.min_data_in_bin;
-          if (cap < 1) cap = 1;
-          if (cap < n_ord) n_ord = cap;
-        }
-        for (int64_t b = 1; b < n_ord; ++b) {
-          int64_t idx = b * n_valid / n_ord;
-          if (idx <= 0 || idx >= n_valid) continue;
-          double w = col[idx - 1];
-          below.push_back(w);
-          auto it = std::upper_bound(col.begin() + idx, col.end(), w);
-          above.push_back(it != col.end() ? *it : w);
-        }
-      }
-      emit_edges(below, above, out);
+      numeric_edges(col, n_sample, p, below, above, levels, level_counts, key0, key1, out, &missing_f[f]);
       edges_f[f] = out;
-      missing_f[f] = reserve ? (int)out.size() + 1 : -1;
     }
   }
   if (failure) std::rethrow_exception(failure);
@@ -285,6 +295,138 @@ BinMapper fit_bins(const double* x, int64_t n_rows, int n_features, const Binnin
     m.missing_bin[f] = missing_f[f];
   }
   return m;
+}
+
+// Kept categorical codes of a compressed column: the stored values plus
+// n_zeros implicit 0.0 entries (code 0); the rule of kept_codes.
+static std::vector<int64_t> kept_codes_sparse(const double* vals, int64_t nnz_f, int64_t n_zeros, int max_bins) {
+  std::vector<int64_t> present;
+  present.reserve((size_t)nnz_f);
+  for (int64_t i = 0; i < nnz_f; ++i) {
+    double v = vals[i];
+    if (!(v >= 0.0)) continue;
+    if (v >= 2147483648.0) throw std::runtime_error("categorical code out of range (>= 2^31)");
+    present.push_back((int64_t)v);
+  }
+  std::sort(present.begin(), present.end());
+  std::vector<int64_t> codes, counts;
+  for (size_t i = 0; i < present.size();) {
+    size_t j = i;
+    while (j + 1 < present.size() && present[j + 1] == present[i]) ++j;
+    codes.push_back(present[i]);
+    counts.push_back((int64_t)(j - i + 1));
+    i = j + 1;
+  }
+  if (n_zeros > 0) {  // the implicit entries are code 0, the smallest code
+    if (!codes.empty() && codes[0] == 0) {
+      counts[0] += n_zeros;
+    } else {
+      codes.insert(codes.begin(), 0);
+      counts.insert(counts.begin(), n_zeros);
+    }
+  }
+  size_t keep = (size_t)(max_bins - 1);
+  if (codes.size() <= keep) return codes;
+  std::vector<size_t> order(codes.size());
+  for (size_t i = 0; i < order.size(); ++i) order[i] = i;
+  std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) { return counts[a] > counts[b]; });
+  std::vector<int64_t> kept;
+  for (size_t i = 0; i < keep; ++i) kept.push_back(codes[order[i]]);
+  std::sort(kept.begin(), kept.end());
+  return kept;
+}
+
+void check_csc(const int64_t* indptr, const int64_t* indices, int64_t n_rows, int n_features) {
+  if (indptr[0] != 0) throw std::invalid_argument("sparse matrix: indptr[0] must be 0");
+  for (int f = 0; f < n_features; ++f) {
+    if (indptr[f + 1] < indptr[f]) throw std::invalid_argument("sparse matrix: indptr is not non-decreasing");
+    for (int64_t i = indptr[f]; i < indptr[f + 1]; ++i) {
+      if (indices[i] < 0 || indices[i] >= n_rows) throw std::invalid_argument("sparse matrix: a row index is out of range");
+      if (i > indptr[f] && indices[i] <= indices[i - 1])
+        throw std::invalid_argument("sparse matrix: row indices must be strictly increasing within each column");
+    }
+  }
+}
+
+BinMapper fit_bins_csc(const int64_t* indptr, const int64_t* indices, const double* values, int64_t n_rows,
+                       int n_features, const BinningParams& p) {
+  if (p.max_bins < 2 || p.max_bins > 256) throw std::runtime_error("max_bins must be in [2, 256]");
+  if (n_rows < 1) throw std::runtime_error("n_rows must be positive");
+  if (p.min_data_in_bin < 1) throw std::runtime_error("min_data_in_bin must be positive");
+  BinMapper m;
+  m.n_features = n_features;
+  m.n_bins = p.max_bins;
+  m.missing_bin.assign((size_t)n_features, -1);
+  m.is_cat.assign((size_t)n_features, 0);
+  for (int f : p.categorical_features) {
+    if (f < 0 || f >= n_features) throw std::runtime_error("categorical feature index out of range");
+    if (m.is_cat[f]) throw std::runtime_error("categorical feature listed twice");
+    m.is_cat[f] = 1;
+  }
+  std::vector<std::vector<int64_t>> codes_f((size_t)n_features);
+  std::vector<std::vector<double>> edges_f((size_t)n_features);
+  std::vector<int> missing_f((size_t)n_features, -1);
+  std::vector<int64_t> sample = sample_rows(n_rows, p.bin_construct_sample_cnt, p.data_random_seed);
+  const bool sampled = !sample.empty();
+  const int64_t n_sample = sampled ? (int64_t)sample.size() : n_rows;
+  std::exception_ptr failure;
+#pragma omp parallel
+  {
+    std::vector<double> col, below, above, out, levels;
+    std::vector<int64_t> level_counts;
+    std::vector<uint64_t> key0, key1;
+#pragma omp for schedule(dynamic, 1)
+    for (int f = 0; f < n_features; ++f) {
+      const int64_t b = indptr[f], e = indptr[f + 1];
+      if (m.is_cat[f]) {
+        try {
+          codes_f[f] = kept_codes_sparse(values + b, e - b, n_rows - (e - b), p.max_bins);
+        } catch (...) {
+#pragma omp critical(mtb_fit_bins_csc_failure)
+          if (!failure) failure = std::current_exception();
+        }
+        continue;
+      }
+      // the sampled column of the densified matrix: a stored value, or 0.0
+      col.clear();
+      if (sampled) {
+        int64_t k = b;
+        for (int64_t i = 0; i < n_sample; ++i) {
+          const int64_t r = sample[i];
+          while (k < e && indices[k] < r) ++k;
+          const double v = (k < e && indices[k] == r) ? values[k] : 0.0;
+          if (!std::isnan(v)) col.push_back(v);
+        }
+      } else {
+        for (int64_t k = b; k < e; ++k)
+          if (!std::isnan(values[k])) col.push_back(values[k]);
+        col.insert(col.end(), (size_t)(n_rows - (e - b)), 0.0);
+      }
+      numeric_edges(col, n_sample, p, below, above, levels, level_counts, key0, key1, out, &missing_f[f]);
+      edges_f[f] = out;
+    }
+  }
+  if (failure) std::rethrow_exception(failure);
+  m.cat_offsets.push_back(0);
+  m.edge_offsets.push_back(0);
+  for (int f = 0; f < n_features; ++f) {
+    m.cat_codes.insert(m.cat_codes.end(), codes_f[f].begin(), codes_f[f].end());
+    m.cat_offsets.push_back((int64_t)m.cat_codes.size());
+    m.edges.insert(m.edges.end(), edges_f[f].begin(), edges_f[f].end());
+    m.edge_offsets.push_back((int64_t)m.edges.size());
+    m.missing_bin[f] = missing_f[f];
+  }
+  return m;
+}
+
+void transform_csc(const BinMapper& m, const int64_t* indptr, const int64_t* indices, const double* values,
+                   int64_t n_rows, uint8_t* out) {
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int f = 0; f < m.n_features; ++f) {
+    uint8_t* dst = out + (int64_t)f * n_rows;
+    memset(dst, m.bin_value(f, 0.0), (size_t)n_rows);
+    for (int64_t k = indptr[f]; k < indptr[f + 1]; ++k) dst[indices[k]] = (uint8_t)m.bin_value(f, values[k]);
+  }
 }
 
 void transform(const BinMapper& m, const double* x, int64_t n_rows, uint8_t* out) {

@@ -49,6 +49,17 @@ BinMapper fit_bins(const double* x, int64_t n_rows, int n_features, const Binnin
 // Writes feature-major bins: out[f * n_rows + r].
 void transform(const BinMapper& m, const double* x, int64_t n_rows, uint8_t* out);
 
+// The same for a compressed-sparse-column matrix (indptr[n_features + 1],
+// row indices strictly increasing within a column, values; an absent entry
+// is the value 0.0, a stored NaN is missing): the bins of the densified
+// matrix, without densifying it (sparse.mojo:535-570).  check_csc throws
+// std::invalid_argument on a malformed matrix.
+void check_csc(const int64_t* indptr, const int64_t* indices, int64_t n_rows, int n_features);
+BinMapper fit_bins_csc(const int64_t* indptr, const int64_t* indices, const double* values, int64_t n_rows,
+                       int n_features, const BinningParams& p);
+void transform_csc(const BinMapper& m, const int64_t* indptr, const int64_t* indices, const double* values,
+                   int64_t n_rows, uint8_t* out);
+
 // Equal-width binning of the reference's test fixtures (binning.mojo:4109-4168).
 void bin_equal_width(const double* x, int64_t n_rows, int n_features, int n_bins, uint8_t* out);
 

@@ -789,6 +789,65 @@ int32_t mojotrees_b200_bin_dense(const double* data, int64_t n_rows, int64_t n_f
 }
 
 
+int32_t mojotrees_b200_bin_csc(const int64_t* indptr, const int64_t* indices, const double* values, int64_t n_rows,
+                               int64_t n_features, const char* parameters, uint8_t* out_bins,
+                               int32_t* out_missing_bin, int32_t* out_n_categories, int32_t* out_n_bins,
+                               MojoTreesError* error) {
+  return guarded(
+      error,
+      [&]() -> int32_t {
+        if (!indptr || !out_bins) throw InvalidArgument("null pointer argument");
+        if (indptr[n_features] > 0 && (!indices || !values)) throw InvalidArgument("null pointer argument");
+        if (n_rows < 1 || n_features < 1) throw InvalidArgument("n_rows and n_features must be positive");
+        TrainConfig cfg = parse_config(parameters, false);
+        try {
+          mtb::check_csc(indptr, indices, n_rows, (int)n_features);
+        } catch (const std::invalid_argument& e) {
+          throw InvalidArgument(e.what());
+        }
+        mtb::BinMapper m = mtb::fit_bins_csc(indptr, indices, values, n_rows, (int)n_features, cfg.binning);
+        mtb::transform_csc(m, indptr, indices, values, n_rows, out_bins);
+        for (int64_t f = 0; f < n_features; ++f) {
+          if (out_missing_bin) out_missing_bin[f] = m.missing_bin[f];
+          if (out_n_categories) out_n_categories[f] = m.is_cat[f] ? m.n_categories((int)f) : -1;
+        }
+        if (out_n_bins) *out_n_bins = m.n_bins;
+        return MOJOTREES_OK;
+      },
+      MOJOTREES_ERROR_INVALID_ARGUMENT);
+}
+
+int32_t mojotrees_b200_train_csc(const int64_t* indptr, const int64_t* indices, const double* values, int64_t n_rows,
+                                 int64_t n_features, const double* labels, const double* weights,
+                                 const char* parameters, MojoTreesModel** out_model, MojoTreesError* error) {
+  return guarded(error, [&]() -> int32_t {
+    if (!indptr || !labels || !out_model) throw InvalidArgument("null pointer argument");
+    if (n_rows < 1 || n_features < 1) throw InvalidArgument("n_rows and n_features must be positive");
+    if (indptr[n_features] > 0 && (!indices || !values)) throw InvalidArgument("null pointer argument");
+    TrainConfig cfg = parse_config(parameters, true);
+    if (weights) throw mtb::Unsupported("sample weights are not covered by the device path");
+    try {
+      mtb::check_csc(indptr, indices, n_rows, (int)n_features);
+    } catch (const std::invalid_argument& e) {
+      throw InvalidArgument(e.what());
+    }
+    // bins of the densified matrix from the compressed columns: the host
+    // holds n_rows x n_features bytes of bins, never the float64 matrix
+    auto t0 = std::chrono::steady_clock::now();
+    mtb::BinMapper mapper = mtb::fit_bins_csc(indptr, indices, values, n_rows, (int)n_features, cfg.binning);
+    std::vector<uint8_t> bins((size_t)n_rows * (size_t)n_features);
+    mtb::transform_csc(mapper, indptr, indices, values, n_rows, bins.data());
+    const double bin_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    std::vector<int> ncats(n_features, -1);
+    for (int f = 0; f < n_features; ++f)
+      if (mapper.is_cat[f]) ncats[f] = mapper.n_categories(f);
+    int32_t rc = train_binned(bins.data(), n_rows, n_features, mapper.n_bins, mapper.missing_bin, ncats, labels, cfg,
+                              out_model, &mapper);
+    if (rc == MOJOTREES_OK && *out_model) (*out_model)->m.stats.binning_seconds = bin_s;
+    return rc;
+  });
+}
+
 int32_t mojotrees_b200_bin_dense_gpu(const double* data, int64_t n_rows, int64_t n_features, const char* parameters,
                                      uint8_t* out_bins, int32_t* out_missing_bin, int32_t* out_n_categories,
                                      int32_t* out_n_bins, MojoTreesError* error) {

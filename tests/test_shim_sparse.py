@@ -1,5 +1,7 @@
-"""Sparse input through the shim: CSC fits and CSR predictions take the dense
-path on the densified matrix (absent entries 0.0, stored NaN missing)."""
+"""Sparse input through the shim.  CSC fits bin the compressed columns as the
+densified matrix would be binned (absent entries 0.0, stored NaN missing)
+and train on those bins, without a dense float64 matrix on the host; CSR
+predictions take the host predictor on the densified rows."""
 import numpy as np
 import pytest
 import scipy.sparse as sp
@@ -64,19 +66,67 @@ def test_predict_csr_equals_dense(shim, tmp_path):
         shim.predict_csr(m, dict(p, device="gpu"), out.ctypes.data)
 
 
-def test_fit_csc_reaches_the_device_path(shim, mtlib, monkeypatch):
-    """The densified matrix and the estimator's parameters reach `fit`."""
-    seen = {}
-
-    def fake_fit(x_addr, n, f, y_addr, objective, params):
-        seen["X"] = shim._f64(x_addr, n * f).reshape(f, n).T.copy()
-        seen["params"] = params
-        return "model"
-
-    monkeypatch.setattr(shim, "fit", fake_fit)
+def test_fit_csc_reaches_the_device_path(shim, mtlib):
+    """The compressed columns go to mojotrees_b200_train_csc as they are (no
+    dense float64 matrix on the host); without a CUDA device the C ABI
+    refuses instead of falling back."""
     M = sp.random(40, 5, density=0.3, random_state=1, format="csc")
     p, keep = _params(M)
     y = np.zeros(40)
-    assert shim.fit_csc(y.ctypes.data, 0, dict(p, n_estimators=3)) == "model"
-    np.testing.assert_array_equal(seen["X"], M.toarray())
-    assert seen["params"] == {"n_estimators": 3}
+    if mtlib.gpu_available():
+        pytest.skip("host-only check (a GPU box trains)")
+    with pytest.raises(mtlib.UnsupportedError, match="CUDA device"):
+        shim.fit_csc(y.ctypes.data, 0, dict(p, n_estimators=3))
+
+
+def _messy_csc(seed, n, f):
+    rng = np.random.default_rng(seed)
+    X = rng.normal(size=(n, f))
+    X[rng.random((n, f)) < 0.85] = 0.0
+    X[:, 1] = np.round(X[:, 1] * 3)
+    X[::37, 2] = np.nan
+    X[:, 3] = np.where(rng.random(n) < 0.6, 0.0, rng.integers(0, 400, n).astype(np.float64))
+    X[rng.random(n) < 0.01, 3] = np.nan
+    C = sp.csc_matrix(np.where(np.isnan(X), 1.5e300, X))
+    C.data[C.data == 1.5e300] = np.nan
+    # an explicitly stored zero is the same value as an absent entry
+    C = C.tolil()
+    C[5, 0] = 0.0
+    C = C.tocsc()
+    C.data[C.indptr[0]] = C.data[C.indptr[0]]
+    return X, C
+
+
+@pytest.mark.parametrize("n,params", [(260_000, {"max_bin": 255}),
+                                      (20_000, {"max_bin": 63, "categorical_feature": "3"}),
+                                      (1_000, {"max_bin": 16})])
+def test_bins_of_csc_equal_bins_of_the_densified_matrix(mtlib, n, params):
+    X, C = _messy_csc(7, n, 5)
+    dense = mtlib.bin_dense(X, params)
+    sparse = mtlib.bin_csc(C.indptr, C.indices, C.data, n, params)
+    assert dense[3] == sparse[3]
+    for a, b in zip(dense[:3], sparse[:3]):
+        np.testing.assert_array_equal(a, b)
+
+
+def test_malformed_csc_is_refused(mtlib):
+    with pytest.raises(mtlib.MojoTreesError, match="strictly increasing"):
+        mtlib.bin_csc(np.array([0, 2]), np.array([3, 1]), np.array([1.0, 2.0]), 5)
+    with pytest.raises(mtlib.MojoTreesError, match="out of range"):
+        mtlib.bin_csc(np.array([0, 1]), np.array([9]), np.array([1.0]), 5)
+
+
+@pytest.mark.gpu
+def test_gpu_csc_fit_equals_the_dense_fit(mtlib):
+    X, C = _messy_csc(8, 50_000, 5)
+    y = np.nan_to_num(X[:, 0]) * 2 + np.nan_to_num(X[:, 1]) + 0.1 * np.arange(50_000) % 3
+    p = {"objective": "regression", "num_iterations": 4, "num_leaves": 31, "max_bin": 63,
+         "categorical_feature": "3", "keep_training_scores": True}
+    dm = mtlib.train_dense(X, y, p)
+    sm = mtlib.train_csc(C.indptr, C.indices, C.data, 50_000, y, p)
+    assert dm.num_trees == sm.num_trees
+    for t in range(dm.num_trees):
+        a, b = dm.tree(t), sm.tree(t)
+        for k in a:
+            np.testing.assert_array_equal(np.asarray(a[k]), np.asarray(b[k]), err_msg=f"tree {t} {k}")
+    np.testing.assert_array_equal(dm.training_scores(50_000), sm.training_scores(50_000))
