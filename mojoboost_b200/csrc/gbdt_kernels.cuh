@@ -1800,6 +1800,7 @@ struct CommitParams {
   int batch_cap;       // leaves expanded per iteration at most (<= kMaxBatch)
   int hist_slots;      // histogram slots available for leaves
   int tile_rows;       // rows per partition tile
+  int ranked_select;   // choose the next batch by bottleneck keys (block-parallel) instead of a pick-loop replay
 };
 
 
@@ -1813,17 +1814,21 @@ __device__ __forceinline__ double frontier_gain(const LeafRec& L) {
 // (records beyond it are read from global memory).
 constexpr int kCommitSlotBytes = 8 + 4 + 4 + 4 + 4 + 8 + 4 + 4;
 
+// Per leaf record kept in shared memory: its table entry, its bottleneck key
+// and a candidate-list slot (ranked batch selection).
+constexpr int kCommitInfoBytes = (int)sizeof(LeafInfo) + 8 + 4;
+
 // Leaf records whose table entries k_commit keeps in shared memory: every
 // record a tree of num_leaves can allocate, within about 200 KB.
 inline int commit_info_cap(int num_leaves) {
   const long long slots = (long long)num_leaves * kCommitSlotBytes;
-  const long long fit = (200ll * 1024 - slots) / (long long)sizeof(LeafInfo);
+  const long long fit = (200ll * 1024 - slots) / (long long)kCommitInfoBytes;
   const long long want = 4ll * num_leaves + 2 * kMaxBatch + 2;
   return (int)std::max(0ll, std::min(want, fit));
 }
 
 inline size_t commit_smem_bytes(int num_leaves) {
-  return (size_t)num_leaves * kCommitSlotBytes + (size_t)commit_info_cap(num_leaves) * sizeof(LeafInfo);
+  return (size_t)num_leaves * kCommitSlotBytes + (size_t)commit_info_cap(num_leaves) * kCommitInfoBytes;
 }
 
 __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict__ ts,
@@ -1834,13 +1839,16 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
   const int L_max = cp.num_leaves;
   double* s_g = reinterpret_cast<double*>(commit_smem);   // slot -> gain (-1: cannot split)
   double* s_vg = s_g + L_max;                              // simulated frontier: gain
-  LeafInfo* s_info = reinterpret_cast<LeafInfo*>(s_vg + L_max);  // leaf records [0, info_cap)
+  double* s_key = s_vg + L_max;                            // leaf record -> bottleneck key (ranked selection)
+  LeafInfo* s_info = reinterpret_cast<LeafInfo*>(s_key + info_cap);  // leaf records [0, info_cap)
   int* s_slot_leaf = reinterpret_cast<int*>(s_info + info_cap);  // slot -> leaf
   int* s_cslot = s_slot_leaf + L_max;                      // commit k: slot ...
   int* s_cpar = s_cslot + L_max;                           // ... and the leaf split there
   int* s_vleaf = s_cpar + L_max;                           // simulated frontier: leaf
   int* s_slot_node = s_vleaf + L_max;                      // slot -> node id of its leaf
   int* s_cnode = s_slot_node + L_max;                      // commit k: node id of the split leaf
+  int* s_cand = s_cnode + L_max;                           // ranked selection: candidate leaves
+  __shared__ int s_block, s_ncand, s_nexp, s_changed;
   __shared__ int s_ncommit, s_stop, s_nl, s_nsel;
   __shared__ int s_sel[kMaxBatch];
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
@@ -1973,7 +1981,10 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
       }
       const int leaf = s_slot_leaf[bs];
       const LeafInfo I = info(leaf);
-      if (!I.expanded) break;  // the pick still needs its expansion
+      if (!I.expanded) {  // the pick still needs its expansion
+        if (lane == 0) s_block = leaf;
+        break;
+      }
       if (reg_frontier) {
         MTB_FRONTIER_SET(bs, info(I.child[0]).gain);
         MTB_FRONTIER_SET(nl, info(I.child[1]).gain);
@@ -2064,45 +2075,108 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
       Bt.n_tiles = 0;
     }
   } else {
-    for (int i = t; i < nl; i += kCommitThreads) {
-      s_vleaf[i] = s_slot_leaf[i];
-      s_vg[i] = s_g[i];
-    }
-    __syncthreads();
-    if (w == 0) {
-      int vn = nl, vleaves = nl, n_sel = 0;
-      while (n_sel < cp.batch_cap && vleaves < L_max) {
-        const int bs = reg_frontier ? reg_pick() : warp_pick(s_vg, vn);
-        if (bs < 0) break;
-        const int leaf = s_vleaf[bs];
-        const LeafInfo I = info(leaf);
-        if (reg_frontier) {
-          if (I.expanded) {
-            MTB_FRONTIER_SET(bs, info(I.child[0]).gain);
-            MTB_FRONTIER_SET(vn, info(I.child[1]).gain);
-          } else {
-            MTB_FRONTIER_SET(bs, -1.0);
+    if (cp.ranked_select && cap == n_pool) {
+      // Block-parallel selection.  A best-first replay takes the virtual tree's
+      // nodes in decreasing order of their bottleneck key, the smallest gain on
+      // the path from the frontier (a node is only available once its parent is
+      // taken), so the leaves it would expand next are the unexpanded nodes
+      // reachable through expanded ones with the largest keys (ties by leaf id
+      // here, which only decides speculation, never the tree).  The leaf the
+      // commit loop stopped at goes first, so every iteration commits a split.
+      for (int i = t; i < cap; i += kCommitThreads) s_key[i] = -2.0;
+      if (t == 0) {
+        s_ncand = 0;
+        s_nexp = 0;
+      }
+      __syncthreads();
+      for (int i = t; i < nl; i += kCommitThreads) s_key[s_slot_leaf[i]] = s_g[i];
+      for (;;) {
+        __syncthreads();
+        if (t == 0) s_changed = 0;
+        __syncthreads();
+        for (int i = t; i < cap; i += kCommitThreads) {
+          const double k = s_key[i];
+          if (k > 0.0 && s_info[i].expanded)
+            for (int side = 0; side < 2; ++side) {
+              const int c = s_info[i].child[side];
+              const double g = s_info[c].gain;
+              const double kc = g < k ? g : k;
+              if (s_key[c] != kc) {
+                s_key[c] = kc;
+                s_changed = 1;
+              }
+            }
+        }
+        __syncthreads();
+        if (!s_changed) break;
+      }
+      const int blk = s_block;
+      for (int i = t; i < cap; i += kCommitThreads) {
+        if (!(s_key[i] > 0.0)) continue;
+        if (s_info[i].expanded) atomicAdd(&s_nexp, 1);
+        else if (i != blk) s_cand[atomicAdd(&s_ncand, 1)] = i;
+      }
+      __syncthreads();
+      const int nc = s_ncand;
+      int budget = L_max - nl - s_nexp;
+      if (budget < 1) budget = 1;
+      const int n_sel = min(min(cp.batch_cap, budget), 1 + nc);
+      for (int a = t; a < nc; a += kCommitThreads) {
+        const int la = s_cand[a];
+        const double ka = s_key[la];
+        int r = 0;
+        for (int b = 0; b < nc; ++b) {
+          const int lb = s_cand[b];
+          const double kb = s_key[lb];
+          r += (kb > ka || (kb == ka && lb < la)) ? 1 : 0;
+        }
+        if (1 + r < n_sel) s_sel[1 + r] = la;
+      }
+      if (t == 0) {
+        s_sel[0] = blk;
+        s_nsel = n_sel;
+      }
+    } else {
+      for (int i = t; i < nl; i += kCommitThreads) {
+        s_vleaf[i] = s_slot_leaf[i];
+        s_vg[i] = s_g[i];
+      }
+      __syncthreads();
+      if (w == 0) {
+        int vn = nl, vleaves = nl, n_sel = 0;
+        while (n_sel < cp.batch_cap && vleaves < L_max) {
+          const int bs = reg_frontier ? reg_pick() : warp_pick(s_vg, vn);
+          if (bs < 0) break;
+          const int leaf = s_vleaf[bs];
+          const LeafInfo I = info(leaf);
+          if (reg_frontier) {
+            if (I.expanded) {
+              MTB_FRONTIER_SET(bs, info(I.child[0]).gain);
+              MTB_FRONTIER_SET(vn, info(I.child[1]).gain);
+            } else {
+              MTB_FRONTIER_SET(bs, -1.0);
+            }
           }
+          if (lane == 0) {
+            if (I.expanded) {
+              s_vleaf[bs] = I.child[0];
+              s_vg[bs] = info(I.child[0]).gain;
+              s_vleaf[vn] = I.child[1];
+              s_vg[vn] = info(I.child[1]).gain;
+            } else {
+              s_sel[n_sel] = leaf;
+              s_vg[bs] = -1.0;
+            }
+          }
+          __syncwarp();
+          if (I.expanded) ++vn;
+          else ++n_sel;
+          ++vleaves;
         }
         if (lane == 0) {
-          if (I.expanded) {
-            s_vleaf[bs] = I.child[0];
-            s_vg[bs] = info(I.child[0]).gain;
-            s_vleaf[vn] = I.child[1];
-            s_vg[vn] = info(I.child[1]).gain;
-          } else {
-            s_sel[n_sel] = leaf;
-            s_vg[bs] = -1.0;
-          }
+          s_nsel = n_sel;
+          H.pick_steps += vleaves - nl;
         }
-        __syncwarp();
-        if (I.expanded) ++vn;
-        else ++n_sel;
-        ++vleaves;
-      }
-      if (lane == 0) {
-        s_nsel = n_sel;
-        H.pick_steps += vleaves - nl;
       }
     }
     __syncthreads();

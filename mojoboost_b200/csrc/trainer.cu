@@ -430,6 +430,12 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   cp.batch_cap = batch_cap;
   cp.hist_slots = hist_slots;
   cp.tile_rows = 256 * part_items;
+  {
+    // MOJOTREES_COMMIT_SELECT=ranked picks each speculative batch from bottleneck
+    // keys in one block-parallel pass; the default replays the pick loop
+    const char* sel = getenv("MOJOTREES_COMMIT_SELECT");
+    cp.ranked_select = (sel && std::string(sel) == "ranked") ? 1 : 0;
+  }
   const size_t commit_smem = commit_smem_bytes(cfg.num_leaves);
   const int commit_cap = commit_info_cap(cfg.num_leaves);
   MTB_CUDA(cudaFuncSetAttribute(k_commit, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)commit_smem));
