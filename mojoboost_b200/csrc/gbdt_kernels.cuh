@@ -918,76 +918,77 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
     if (ps < pe0) window = headroom();
     }
     cluster.sync();
-    // Merge, one tile of cells per warp at a time: 16 consecutive bins of
-    // one feature slot j for all 32 lanes (512 consecutive words).  Each
-    // plane's values are summed over the cluster's CTAs (DSMEM) with lane =
-    // feature, transposed in registers within each half-warp to lane = bin,
-    // and added to the work slot with int32 atomics whose lanes hit two runs
-    // of 16 consecutive cells (4 sectors a warp instruction instead of 32;
-    // about 5x faster through L2 than the lane = feature order).
+    // Merge: the work units are (tile, plane), one per warp at a time.  A
+    // tile is 16 consecutive bins of one feature slot j for all 32 lanes
+    // (512 consecutive words).  A unit's values are summed over the
+    // cluster's CTAs (DSMEM) with lane = feature, transposed in registers
+    // within each half-warp to lane = bin, and added to the work slot with
+    // int32 atomics whose lanes hit two runs of 16 consecutive cells (4
+    // sectors a warp instruction instead of 32; about 5x faster through L2
+    // than the lane = feature order).  A CTA's slice has 8 tiles in clusters
+    // of 8, so one unit per (tile, plane) keeps 24 of the 32 warps reading
+    // DSMEM at once instead of 8.
     {
       constexpr int kPlanes = (MODE == MODE_FIXED && CONST_H) ? 2 : 3;  // g, [h,] count
       const int tiles = (m1 - m0) >> 9;
       const int half = lane >> 4, hl = lane & 15;
-      for (int t = warp; t < tiles; t += n_warps) {
+      for (int wu = warp; wu < tiles * kPlanes; wu += n_warps) {
+        const int t = wu / kPlanes, plane = wu - t * kPlanes;
         const int c0 = m0 + (t << 9);
         const int j = (c0 >> 5) / kHistBinsPad, bin0 = (c0 >> 5) % kHistBinsPad;
-#pragma unroll 1
-        for (int plane = 0; plane < kPlanes; ++plane) {
-          const int out_plane = (kPlanes == 2 && plane == 1) ? 2 : plane;  // constant hessian: g, count
-          int v[16];
+        const int out_plane = (kPlanes == 2 && plane == 1) ? 2 : plane;  // constant hessian: g, count
+        int v[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = 0;
-          for (int rk = 0; rk < cs; ++rk) {
-            const unsigned int* q0 = cluster.map_shared_rank(p0, rk);
+        for (int i = 0; i < 16; ++i) v[i] = 0;
+        for (int rk = 0; rk < cs; ++rk) {
+          const unsigned int* q0 = cluster.map_shared_rank(p0, rk);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int c = c0 + (i << 5) + lane;
-              if (Q16) {
-                if (plane == 1) {
-                  const unsigned int x = q0[cells + ((((j >> 1) * kHistBinsPad + bin0 + i) << 5) + lane)];
-                  v[i] += (int)((x >> (16 * (j & 1))) & 0xffffu);
-                } else {
-                  const unsigned int x = q0[c];
-                  v[i] += plane == 0 ? (int)(x & 0xffffu) - g_lim * (int)(x >> 16) : (int)(x >> 16);
-                }
-              } else if (LAYOUT == HL_QUANT) {
-                if (plane == 1) {
-                  v[i] += (int)q0[cells + c];
-                } else {
-                  const unsigned int x = q0[c];
-                  v[i] += plane == 0 ? ((int)x >> kQuantCountBits) : (int)(x & ((1u << kQuantCountBits) - 1u));
-                }
+          for (int i = 0; i < 16; ++i) {
+            const int c = c0 + (i << 5) + lane;
+            if (Q16) {
+              if (plane == 1) {
+                const unsigned int x = q0[cells + ((((j >> 1) * kHistBinsPad + bin0 + i) << 5) + lane)];
+                v[i] += (int)((x >> (16 * (j & 1))) & 0xffffu);
               } else {
-                // fixed point: planes g, h, count (constant hessian: g, count)
-                v[i] += (int)q0[plane * cells + c];
+                const unsigned int x = q0[c];
+                v[i] += plane == 0 ? (int)(x & 0xffffu) - g_lim * (int)(x >> 16) : (int)(x >> 16);
               }
+            } else if (LAYOUT == HL_QUANT) {
+              if (plane == 1) {
+                v[i] += (int)q0[cells + c];
+              } else {
+                const unsigned int x = q0[c];
+                v[i] += plane == 0 ? ((int)x >> kQuantCountBits) : (int)(x & ((1u << kQuantCountBits) - 1u));
+              }
+            } else {
+              // fixed point: planes g, h, count (constant hessian: g, count)
+              v[i] += (int)q0[plane * cells + c];
             }
           }
-          // 16 x 16 transposes within each half-warp: lane 16 h + m, v[i] =
-          // cell (lane 16 h + m, bin i) becomes lane 16 h + i, v[m] = cell
-          // (lane 16 h + m, bin i)
+        }
+        // 16 x 16 transposes within each half-warp: lane 16 h + m, v[i] =
+        // cell (lane 16 h + m, bin i) becomes lane 16 h + i, v[m] = cell
+        // (lane 16 h + m, bin i)
 #pragma unroll
-          for (int sft = 8; sft >= 1; sft >>= 1) {
-            const bool upper = (lane & sft) != 0;
+        for (int sft = 8; sft >= 1; sft >>= 1) {
+          const bool upper = (lane & sft) != 0;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              if ((i & sft) == 0) {
-                const int send = upper ? v[i] : v[i + sft];
-                const int recv = __shfl_xor_sync(0xffffffffu, send, sft);
-                if (upper)
-                  v[i] = recv;
-                else
-                  v[i + sft] = recv;
-              }
+          for (int i = 0; i < 16; ++i) {
+            if ((i & sft) == 0) {
+              const int send = upper ? v[i] : v[i + sft];
+              const int recv = __shfl_xor_sync(0xffffffffu, send, sft);
+              if (upper)
+                v[i] = recv;
+              else
+                v[i + sft] = recv;
             }
           }
-          const int bin = bin0 + hl;
+        }
+        const int bin = bin0 + hl;
 #pragma unroll
-          for (int m = 0; m < 16; ++m) {
-            const int f = f0 + (16 * half + m) * NPL + j;
-            if (f < F && bin < B && v[m] != 0) atomicAdd(hs + (f * 3 + out_plane) * B + bin, v[m]);
-          }
+        for (int m = 0; m < 16; ++m) {
+          const int f = f0 + (16 * half + m) * NPL + j;
+          if (f < F && bin < B && v[m] != 0) atomicAdd(hs + (f * 3 + out_plane) * B + bin, v[m]);
         }
       }
     }
@@ -1814,9 +1815,9 @@ __device__ __forceinline__ double frontier_gain(const LeafRec& L) {
 // (records beyond it are read from global memory).
 constexpr int kCommitSlotBytes = 8 + 4 + 4 + 4 + 4 + 8 + 4 + 4;
 
-// Per leaf record kept in shared memory: its table entry, its bottleneck key
-// and a candidate-list slot (ranked batch selection).
-constexpr int kCommitInfoBytes = (int)sizeof(LeafInfo) + 8 + 4;
+// Per leaf record kept in shared memory: its table entry and its bottleneck key
+// (ranked batch selection).
+constexpr int kCommitInfoBytes = (int)sizeof(LeafInfo) + 8;
 
 // Leaf records whose table entries k_commit keeps in shared memory: every
 // record a tree of num_leaves can allocate, within about 200 KB.
@@ -1847,8 +1848,7 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
   int* s_vleaf = s_cpar + L_max;                           // simulated frontier: leaf
   int* s_slot_node = s_vleaf + L_max;                      // slot -> node id of its leaf
   int* s_cnode = s_slot_node + L_max;                      // commit k: node id of the split leaf
-  int* s_cand = s_cnode + L_max;                           // ranked selection: candidate leaves
-  __shared__ int s_block, s_ncand, s_nexp, s_changed;
+  __shared__ int s_block, s_changed;
   __shared__ int s_ncommit, s_stop, s_nl, s_nsel;
   __shared__ int s_sel[kMaxBatch];
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
@@ -2062,7 +2062,8 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
   }
 
   // ---- 4. next batch: the leaves the pick loop will need next, in order.
-  // The loop is simulated past this point on a copy of the frontier: an
+  // By default they are ranked by bottleneck keys (below).  Otherwise the
+  // loop is simulated past this point on a copy of the frontier: an
   // expanded leaf is committed virtually (its children, with their known
   // gains, take its slot and the next one), an unexpanded one is taken into
   // the batch and leaves the simulated frontier.  The first leaf taken is the
@@ -2084,10 +2085,6 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
       // here, which only decides speculation, never the tree).  The leaf the
       // commit loop stopped at goes first, so every iteration commits a split.
       for (int i = t; i < cap; i += kCommitThreads) s_key[i] = -2.0;
-      if (t == 0) {
-        s_ncand = 0;
-        s_nexp = 0;
-      }
       __syncthreads();
       for (int i = t; i < nl; i += kCommitThreads) s_key[s_slot_leaf[i]] = s_g[i];
       for (;;) {
@@ -2111,31 +2108,29 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
         if (!s_changed) break;
       }
       const int blk = s_block;
-      for (int i = t; i < cap; i += kCommitThreads) {
-        if (!(s_key[i] > 0.0)) continue;
-        if (s_info[i].expanded) atomicAdd(&s_nexp, 1);
-        else if (i != blk) s_cand[atomicAdd(&s_ncand, 1)] = i;
-      }
+      if (t == 0) s_nsel = 1;
+      // A candidate's replay step is the nodes taken before it: the stopped
+      // leaf, the candidates ranked above it and the expanded nodes whose key
+      // is not below its own (each adds a leaf).  It is selected when the
+      // replay reaches it before the tree is full and within the batch.
       __syncthreads();
-      const int nc = s_ncand;
-      int budget = L_max - nl - s_nexp;
-      if (budget < 1) budget = 1;
-      const int n_sel = min(min(cp.batch_cap, budget), 1 + nc);
-      for (int a = t; a < nc; a += kCommitThreads) {
-        const int la = s_cand[a];
-        const double ka = s_key[la];
-        int r = 0;
-        for (int b = 0; b < nc; ++b) {
-          const int lb = s_cand[b];
-          const double kb = s_key[lb];
-          r += (kb > ka || (kb == ka && lb < la)) ? 1 : 0;
+      const int room = L_max - nl;
+      for (int i = t; i < cap; i += kCommitThreads) {
+        const double ka = s_key[i];
+        if (!(ka > 0.0) || s_info[i].expanded || i == blk) continue;
+        int r = 0, e = 0;
+        for (int b = 0; b < cap; ++b) {
+          const double kb = s_key[b];
+          if (!(kb >= ka)) continue;
+          if (s_info[b].expanded) ++e;
+          else if (b != blk && (kb > ka || b < i)) ++r;
         }
-        if (1 + r < n_sel) s_sel[1 + r] = la;
+        if (1 + r < cp.batch_cap && 1 + r + e < room) {
+          s_sel[1 + r] = i;
+          atomicAdd(&s_nsel, 1);
+        }
       }
-      if (t == 0) {
-        s_sel[0] = blk;
-        s_nsel = n_sel;
-      }
+      if (t == 0) s_sel[0] = blk;
     } else {
       for (int i = t; i < nl; i += kCommitThreads) {
         s_vleaf[i] = s_slot_leaf[i];

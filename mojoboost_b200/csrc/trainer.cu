@@ -431,10 +431,11 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   cp.hist_slots = hist_slots;
   cp.tile_rows = 256 * part_items;
   {
-    // MOJOTREES_COMMIT_SELECT=ranked picks each speculative batch from bottleneck
-    // keys in one block-parallel pass; the default replays the pick loop
+    // each speculative batch is picked from bottleneck keys in one
+    // block-parallel pass; MOJOTREES_COMMIT_SELECT=replay replays the pick
+    // loop serially instead (same batches up to ties, more pick steps)
     const char* sel = getenv("MOJOTREES_COMMIT_SELECT");
-    cp.ranked_select = (sel && std::string(sel) == "ranked") ? 1 : 0;
+    cp.ranked_select = (sel && std::string(sel) == "replay") ? 0 : 1;
   }
   const size_t commit_smem = commit_smem_bytes(cfg.num_leaves);
   const int commit_cap = commit_info_cap(cfg.num_leaves);
@@ -491,11 +492,42 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
 
   auto t_fit = std::chrono::steady_clock::now();
   int launches = 0;
+  // MOJOTREES_TRACE_HIST=1 prints every histogram launch (device time, items,
+  // built rows) to stderr; it synchronises after each launch (diagnostic only)
+  const bool trace_hist = getenv("MOJOTREES_TRACE_HIST") != nullptr;
+  cudaEvent_t th0 = nullptr, th1 = nullptr;
+  struct TraceEvents {
+    cudaEvent_t &a, &b;
+    ~TraceEvents() {
+      if (a) cudaEventDestroy(a);
+      if (b) cudaEventDestroy(b);
+    }
+  } trace_events{th0, th1};
+  if (trace_hist) {
+    MTB_CUDA(cudaEventCreate(&th0));
+    MTB_CUDA(cudaEventCreate(&th1));
+  }
   auto hist = [&]() {
     hist_timer.begin(&stats.hist_ms);
+    if (trace_hist) MTB_CUDA(cudaEventRecord(th0, st));
     launch_hist(hl, st, batch_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p, d_pairs1.p,
                 d_hist.p, slot_cells, work_base);
     hist_timer.end();
+    if (trace_hist) {
+      MTB_CUDA(cudaEventRecord(th1, st));
+      Batch hb;
+      MTB_CUDA(cudaMemcpyAsync(&hb, batch_of(d_ts.p), sizeof(Batch), cudaMemcpyDeviceToHost, st));
+      MTB_CUDA(cudaStreamSynchronize(st));
+      float ms = 0.f;
+      MTB_CUDA(cudaEventElapsedTime(&ms, th0, th1));
+      long long rows = 0;
+      for (int i = 0; i < hb.n_items; ++i) {
+        const BatchItem& P = hb.items[i];
+        const long long nl = (long long)P.cursor_left;
+        rows += P.built_is_left ? nl : P.count - nl;
+      }
+      fprintf(stderr, "mojotrees hist: us %.1f items %d rows %lld\n", ms * 1000.0, hb.n_items, rows);
+    }
   };
   // the built children's cells summed over every device's rows (exact int32)
   auto reduce_work = [&]() {

@@ -209,3 +209,12 @@ def test_gpu_compact_scan_matches_oracle(case, mtlib, oracle, monkeypatch):
     oracle's trees bit for bit, like the default scan."""
     monkeypatch.setenv("MOJOTREES_SCAN", "compact")
     test_gpu_matches_oracle(case, mtlib, oracle)
+
+
+@pytest.mark.parametrize("case", ["binary_quant", "missing_cat_fixed", "binary_quant_large"])
+def test_gpu_replay_batch_selection_matches_oracle(case, mtlib, oracle, monkeypatch):
+    """MOJOTREES_COMMIT_SELECT=replay (each speculative batch chosen by a
+    serial replay of the pick loop instead of by bottleneck keys) decides
+    only which leaves are built early; the trees stay the oracle's."""
+    monkeypatch.setenv("MOJOTREES_COMMIT_SELECT", "replay")
+    test_gpu_matches_oracle(case, mtlib, oracle)

@@ -87,6 +87,7 @@ def _messy_csc(seed, n, f):
     X[::37, 2] = np.nan
     X[:, 3] = np.where(rng.random(n) < 0.6, 0.0, rng.integers(0, 400, n).astype(np.float64))
     X[rng.random(n) < 0.01, 3] = np.nan
+    X[5, 0] = 0.0  # stored explicitly below
     C = sp.csc_matrix(np.where(np.isnan(X), 1.5e300, X))
     C.data[C.data == 1.5e300] = np.nan
     # an explicitly stored zero is the same value as an absent entry
