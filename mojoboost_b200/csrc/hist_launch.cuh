@@ -151,11 +151,11 @@ inline HistLaunch choose_hist_launch(int mode, bool const_h, int quant_bins, int
       && !getenv("MOJOTREES_HIST_NO_ROWPACK"))
     hl.layout = HL_QUANT16R;
   // MOJOTREES_HIST_SMEM_KB / MOJOTREES_HIST_CLUSTER override the shared-memory
-  // budget per CTA and the largest cluster size (tuning knobs)
+  // budget per CTA and the cluster size (tuning knobs)
   size_t budget = 220 * 1024;
   if (const char* e = getenv("MOJOTREES_HIST_SMEM_KB")) budget = (size_t)atoi(e) * 1024;
-  int max_cs = 8;
-  if (const char* e = getenv("MOJOTREES_HIST_CLUSTER")) max_cs = atoi(e);
+  int max_cs = 8, force_cs = 0;
+  if (const char* e = getenv("MOJOTREES_HIST_CLUSTER")) force_cs = max_cs = atoi(e);
   auto smem_of = [&](int npl) {
     return (size_t)4 * hist_layout_words(hl.layout, 32 * npl * kHistBinsPad) + (size_t)kHistBatchSmem;
   };
@@ -194,10 +194,11 @@ inline HistLaunch choose_hist_launch(int mode, bool const_h, int quant_bins, int
     }
     int per_group = n_clusters / hl.groups;
     if (per_group < 1) continue;
-    if (per_group * cs * hl.groups > best_ctas) {
+    if (per_group * cs * hl.groups > best_ctas || cs == force_cs) {
       best_ctas = per_group * cs * hl.groups;
       hl.cluster = cs;
       hl.row_ctas = per_group * cs;
+      if (cs == force_cs) break;
     }
   }
   if (const char* e = getenv("MOJOTREES_HIST_MIN_ROWS")) hl.min_rows_per_cta = std::max(1, atoi(e));

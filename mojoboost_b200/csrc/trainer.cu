@@ -521,12 +521,16 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       float ms = 0.f;
       MTB_CUDA(cudaEventElapsedTime(&ms, th0, th1));
       long long rows = 0;
+      std::string sizes;
       for (int i = 0; i < hb.n_items; ++i) {
         const BatchItem& P = hb.items[i];
         const long long nl = (long long)P.cursor_left;
-        rows += P.built_is_left ? nl : P.count - nl;
+        const long long c = P.built_is_left ? nl : P.count - nl;
+        rows += c;
+        sizes += " " + std::to_string(c);
       }
-      fprintf(stderr, "mojotrees hist: us %.1f items %d rows %lld\n", ms * 1000.0, hb.n_items, rows);
+      fprintf(stderr, "mojotrees hist: us %.1f items %d rows %lld sizes%s\n", ms * 1000.0, hb.n_items, rows,
+              sizes.c_str());
     }
   };
   // the built children's cells summed over every device's rows (exact int32)
