@@ -386,11 +386,24 @@ __device__ __forceinline__ bool goes_left(const BatchItem& P, int bin) {
 // the front, each tile's rows in order) and right rows (from the back), into
 // the other ping-pong buffer.  Tiles of all items are one flat index space.
 // Also zeroes the work slots the built children accumulate into.
+// Programmatic dependent launch.  The iteration kernels (partition ->
+// histogram -> scan -> commit -> next partition) are launched with the
+// programmatic-stream-serialization attribute, so a kernel's CTAs may be
+// scheduled while its predecessor still runs.  Each first waits here for the
+// predecessor grid to complete and its memory to be visible, before touching
+// any data, and then lets its own dependents be scheduled.  Without the
+// attribute both instructions return at once.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 template <typename PairT, int ITEMS>
 __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t* __restrict__ bins_cm, long long n,
                                                    int* __restrict__ rows0, int* __restrict__ rows1,
                                                    PairT* __restrict__ pairs0, PairT* __restrict__ pairs1,
                                                    int* __restrict__ hist, long long slot_cells, int work_base) {
+  pdl_enter();
   Batch& Bt = ts->batch;
   const int n_items = Bt.n_items;
   if (n_items == 0) return;
@@ -1118,6 +1131,7 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__
                                                const void* __restrict__ pairs1, int* __restrict__ hist,
                                                long long slot_cells, long long rows_per_flush, int g_lim,
                                                int work_base, int min_rows_per_cta) {
+  pdl_enter();
   namespace cg = cooperative_groups;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   unsigned int* p0 = reinterpret_cast<unsigned int*>(smem_raw);
@@ -1414,6 +1428,7 @@ __global__ void __launch_bounds__(kScanWarps * 32, 3) k_scan_t(TreeState* __rest
                                                           const RoundScales* __restrict__ sc, ScanParams sp,
                                                           FeatBest* __restrict__ out, int work_base,
                                                           ChildRec* __restrict__ rec) {
+  pdl_enter();
   using CT = typename std::conditional<WIDE, long long, int>::type;  // histogram cell type
   __shared__ CT s_cells[kScanWarps][3][256];  // categorical searches only
   const Batch& Bt = ts->batch;
@@ -1836,6 +1851,7 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
                                                            const int* __restrict__ missing_bin, CommitParams cp,
                                                            int info_cap, int* __restrict__ host_done,
                                                            int host_done_index) {
+  pdl_enter();
   extern __shared__ __align__(16) unsigned char commit_smem[];
   const int L_max = cp.num_leaves;
   double* s_g = reinterpret_cast<double*>(commit_smem);   // slot -> gain (-1: cannot split)

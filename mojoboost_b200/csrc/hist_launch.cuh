@@ -9,6 +9,7 @@
 #include <cstddef>
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 #include "gbdt_device.cuh"
 #include "gbdt_kernels.cuh"
@@ -26,6 +27,24 @@ namespace {
   } while (0)
 #endif
 
+// Launches k on st; with pdl, as a programmatic dependent of the kernel
+// before it on the stream (the kernel must begin with pdl_enter()).
+template <typename... KArgs, typename... Args>
+void launch_chained(bool pdl, void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                    Args&&... args) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = pdl ? 1 : 0;
+  MTB_CUDA(cudaLaunchKernelEx(&lc, k, std::forward<Args>(args)...));
+}
+
 inline const Batch* batch_of(const TreeState* ts) {
   return reinterpret_cast<const Batch*>(reinterpret_cast<const char*>(ts) + offsetof(TreeState, batch));
 }
@@ -40,6 +59,7 @@ struct HistLaunch {
   int row_ctas = 1;
   size_t smem = 0;
   long long rows_per_flush = 1ll << 40;
+  bool pdl = false;            // launch as a programmatic dependent (trainer iterations)
   int g_lim = 0;               // HL_QUANT16: offset making g non-negative
 };
 
@@ -53,8 +73,10 @@ cudaLaunchConfig_t hist_config(const HistLaunch& hl, int cs, int row_ctas, cudaS
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = cs;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
-  lc.numAttrs = 1;
+  lc.numAttrs = hl.pdl ? 2 : 1;
   return lc;
 }
 
@@ -63,7 +85,7 @@ cudaError_t prepare_hist_t(const HistLaunch& hl, int cs, int* n_clusters) {
   auto k = k_hist<NPL, L>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   if (e != cudaSuccess) return e;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t lc = hist_config(hl, cs, hl.row_ctas / cs * cs, 0, attr);
   return cudaOccupancyMaxActiveClusters(n_clusters, k, &lc);
 }
@@ -72,7 +94,7 @@ template <int NPL, int L>
 void launch_hist_t(const HistLaunch& hl, cudaStream_t st, const Batch* batch, const uint8_t* bins_rm, int Fp, int F,
                    int B, const int* r0, const int* r1, const void* p0, const void* p1, int* hist,
                    long long slot_cells, int ws) {
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t lc = hist_config(hl, hl.cluster, hl.row_ctas, st, attr);
   MTB_CUDA(cudaLaunchKernelEx(&lc, k_hist<NPL, L>, batch, bins_rm, Fp, F, B, r0, r1, p0, p1, hist, slot_cells,
                               hl.rows_per_flush, hl.g_lim, ws, hl.min_rows_per_cta));

@@ -393,6 +393,11 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   // in clusters of up to 8 that merge through DSMEM.
   HistLaunch hl = choose_hist_launch(mode, const_h, mode == MODE_QUANT ? cfg.num_grad_quant_bins : 0, B, Fp, n_sm, N,
                                      wide);
+  // the iteration kernels run as programmatic dependents of one another
+  // (each may be scheduled while its predecessor finishes);
+  // MOJOTREES_NO_PDL=1 launches them plainly
+  const bool pdl = getenv("MOJOTREES_NO_PDL") == nullptr;
+  hl.pdl = pdl;
   // partition geometry (MOJOTREES_PART_ITEMS / MOJOTREES_PART_BLOCKS_PER_SM
   // override the rows per thread of a tile and the resident blocks per SM)
   int part_bps = 4;
@@ -405,17 +410,20 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   auto launch_partition = [&]() {
 #define MTB_PART(IT)                                                                                      \
   if (mode == MODE_QUANT)                                                                                 \
-    k_partition<uint16_t, IT><<<part_grid, part_threads, 0, st>>>(                                        \
-        d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<uint16_t*>(d_pairs0.p),            \
-        reinterpret_cast<uint16_t*>(d_pairs1.p), d_hist.p, slot_cells, work_base);                        \
+    launch_chained(pdl, k_partition<uint16_t, IT>, part_grid, part_threads, 0, st, d_ts.p,                \
+                   (const uint8_t*)d_bins_cm.p, N, d_rows0.p, d_rows1.p,                                  \
+                   reinterpret_cast<uint16_t*>(d_pairs0.p), reinterpret_cast<uint16_t*>(d_pairs1.p),      \
+                   d_hist.p, slot_cells, work_base);                                                      \
   else if (wide)                                                                                          \
-    k_partition<longlong2, IT><<<part_grid, part_threads, 0, st>>>(                                       \
-        d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<longlong2*>(d_pairs0.p),           \
-        reinterpret_cast<longlong2*>(d_pairs1.p), d_hist.p, slot_cells, work_base);                       \
+    launch_chained(pdl, k_partition<longlong2, IT>, part_grid, part_threads, 0, st, d_ts.p,               \
+                   (const uint8_t*)d_bins_cm.p, N, d_rows0.p, d_rows1.p,                                  \
+                   reinterpret_cast<longlong2*>(d_pairs0.p), reinterpret_cast<longlong2*>(d_pairs1.p),    \
+                   d_hist.p, slot_cells, work_base);                                                      \
   else                                                                                                    \
-    k_partition<int2, IT><<<part_grid, part_threads, 0, st>>>(                                            \
-        d_ts.p, d_bins_cm.p, N, d_rows0.p, d_rows1.p, reinterpret_cast<int2*>(d_pairs0.p),                \
-        reinterpret_cast<int2*>(d_pairs1.p), d_hist.p, slot_cells, work_base);
+    launch_chained(pdl, k_partition<int2, IT>, part_grid, part_threads, 0, st, d_ts.p,                    \
+                   (const uint8_t*)d_bins_cm.p, N, d_rows0.p, d_rows1.p,                                  \
+                   reinterpret_cast<int2*>(d_pairs0.p), reinterpret_cast<int2*>(d_pairs1.p), d_hist.p,   \
+                   slot_cells, work_base);
     if (part_items == 1) { MTB_PART(1) }
     else if (part_items == 2) { MTB_PART(2) }
     else if (part_items == 4) { MTB_PART(4) }
@@ -702,14 +710,20 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
         timer.begin(&stats.partition_ms);
         launch_partition();
         timer.end();
+        // "iteration i - 1 committed": recorded after this partition rather
+        // than after that commit, so the commit -> partition launch stays a
+        // programmatic dependency (the partition starts only once the commit
+        // grid has completed)
+        if (i > 0) MTB_CUDA(cudaEventRecord(iter_ev[(i - 1) % kRing], st));
         hist();
         reduce_work();
         timer.begin(&stats.scan_ms);
         if (!dp_feature) {
-          (wide ? (scan_compact ? k_scan_t<true, false, true> : k_scan_t<false, false, true>)
-                : (scan_compact ? k_scan_t<true, false> : k_scan_t<false, false>))<<<scan_grid, kScanWarps * 32, 0, st>>>(
-              d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p, d_ncats.p, d_sc.p, sp, d_fb.p, work_base,
-              nullptr);
+          launch_chained(pdl,
+                         wide ? (scan_compact ? k_scan_t<true, false, true> : k_scan_t<false, false, true>)
+                              : (scan_compact ? k_scan_t<true, false> : k_scan_t<false, false>),
+                         scan_grid, kScanWarps * 32, 0, st, d_ts.p, d_hist.p, slot_cells, d_feats.p, d_missing.p,
+                         d_ncats.p, d_sc.p, sp, d_fb.p, work_base, (ChildRec*)nullptr);
         } else {
           // this rank's per-child bests -> every rank's -> the merged leaves
           MTB_CUDA(cudaMemsetAsync(d_rec.p, 0, sizeof(ChildRec) * 2 * (size_t)batch_cap, st));
@@ -724,10 +738,9 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
         }
         timer.end();
         timer.begin(&stats.commit_ms);
-        k_commit<<<1, kCommitThreads, commit_smem, st>>>(d_ts.p, d_missing.p, cp, commit_cap, d_done,
-                                                          i % kRing);
+        launch_chained(pdl, k_commit, 1, kCommitThreads, commit_smem, st, d_ts.p, d_missing.p, cp, commit_cap,
+                       d_done, i % kRing);
         timer.end();
-        MTB_CUDA(cudaEventRecord(iter_ev[i % kRing], st));
         launches += 4;
         launched++;
       }
