@@ -387,9 +387,9 @@ __device__ __forceinline__ bool goes_left(const BatchItem& P, int bin) {
 // the other ping-pong buffer.  Tiles of all items are one flat index space.
 // Also zeroes the work slots the built children accumulate into.
 // Programmatic dependent launch.  The iteration kernels (partition ->
-// histogram -> scan -> commit -> next partition) are launched with the
-// programmatic-stream-serialization attribute, so a kernel's CTAs may be
-// scheduled while its predecessor still runs.  Each first waits here for the
+// histogram -> scan -> commit -> next partition) can be launched with the
+// programmatic-stream-serialization attribute (MOJOTREES_PDL=1), so a
+// kernel's CTAs may be scheduled while its predecessor still runs.  Each first waits here for the
 // predecessor grid to complete and its memory to be visible, before touching
 // any data, and then lets its own dependents be scheduled.  Without the
 // attribute both instructions return at once.
@@ -653,6 +653,9 @@ constexpr int kHistThreads = MTB_HIST_THREADS;
 constexpr int kHistBinsPad = 256;  // bins per feature in the shared-memory layout
 // shared memory after the cells: the staged batch items and their built-row prefix sums
 // (and 64 words of reduction scratch)
+// rows per CTA that one merged segment costs about as much as (the split of
+// a launch's rows over clusters weighs merges against rows with it)
+constexpr long long kHistMergeRows = 4500;
 constexpr int kHistBatchSmem =
     (int)((sizeof(BatchItem) * kMaxBatch + sizeof(long long) * (kMaxBatch + 1) + 64 * sizeof(unsigned int) + 15) /
           16 * 16);
@@ -1130,7 +1133,7 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__
                                                const int* __restrict__ rows1, const void* __restrict__ pairs0,
                                                const void* __restrict__ pairs1, int* __restrict__ hist,
                                                long long slot_cells, long long rows_per_flush, int g_lim,
-                                               int work_base, int min_rows_per_cta) {
+                                               int work_base, int min_rows_per_cta, int allow_owned) {
   pdl_enter();
   namespace cg = cooperative_groups;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -1178,6 +1181,89 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__
   long long cap = (S + per_cluster - 1) / per_cluster;
   if (cap > n_clusters) cap = n_clusters;
   if (cid >= cap) return;  // the whole cluster leaves together
+  // Rows to clusters, two ways.  Contiguous: cluster c takes rows
+  // [S c / cap, S (c + 1) / cap) of the batch in item order and merges one
+  // segment for every item its range meets.  Owned: every item with rows gets
+  // k_i = ceil(rows_i / R) clusters of its own, R the smallest row count per
+  // cluster with sum k_i <= cap, and each cluster merges one segment.  The
+  // launch takes the way whose costliest cluster is cheaper, a merged segment
+  // counting as kHistMergeRows rows per CTA (per-launch traces of configs[1]
+  // fit 32 us a merged segment against 3.6 ns a row for a cluster of two).
+  // Every CTA computes the same choice from the same staged items.
+  int* s_asg = reinterpret_cast<int*>(s_red);  // [0] owned; [1 + i] first cluster of item i
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const long long mr = (long long)kHistMergeRows * cs;
+    // contiguous: the largest cluster cost, lanes over clusters
+    long long cost_a = 0;
+    for (long long c = lane; c < cap; c += 32) {
+      const long long lo = S * c / cap, hi = S * (c + 1) / cap;
+      if (hi <= lo) continue;
+      int first = 0, last = n_items - 1;  // items meeting [lo, hi): s_pre[i + 1] > lo and s_pre[i] < hi
+      while (first < n_items && s_pre[first + 1] <= lo) ++first;
+      while (last > first && s_pre[last] >= hi) --last;
+      const long long cost = (hi - lo) + (long long)(last - first + 1) * mr;
+      cost_a = cost > cost_a ? cost : cost_a;
+    }
+    for (int k = 16; k > 0; k >>= 1) {
+      const long long o = __shfl_xor_sync(0xffffffffu, cost_a, k);
+      cost_a = o > cost_a ? o : cost_a;
+    }
+    // owned: binary search of the row count R per cluster (lane = item)
+    const long long rows_i = lane < n_items ? s_pre[lane + 1] - s_pre[lane] : 0;
+    long long r_lo = (S + cap - 1) / cap, r_hi = rows_i;
+    for (int k = 16; k > 0; k >>= 1) {
+      const long long o = __shfl_xor_sync(0xffffffffu, r_hi, k);
+      r_hi = o > r_hi ? o : r_hi;
+    }
+    const int nonempty = __popc(__ballot_sync(0xffffffffu, rows_i > 0));
+    bool owned = false;
+    long long k_i = 0;
+    if (nonempty <= cap) {
+      if (r_lo > r_hi) r_lo = r_hi;
+      while (r_lo < r_hi) {
+        const long long mid = (r_lo + r_hi) / 2;
+        long long need = rows_i > 0 ? (rows_i + mid - 1) / mid : 0;
+        for (int k = 16; k > 0; k >>= 1) need += __shfl_xor_sync(0xffffffffu, need, k);
+        if (need <= cap) r_hi = mid;
+        else r_lo = mid + 1;
+      }
+      owned = allow_owned && r_lo + mr < cost_a;
+      k_i = rows_i > 0 ? (rows_i + r_lo - 1) / r_lo : 0;
+    }
+    // exclusive prefix of the clusters per item
+    long long inc = k_i;
+    for (int k = 1; k < 32; k <<= 1) {
+      const long long o = __shfl_up_sync(0xffffffffu, inc, k);
+      if (lane >= k) inc += o;
+    }
+    if (lane < n_items) s_asg[2 + lane] = (int)inc;
+    if (lane == 0) {
+      s_asg[0] = owned ? 1 : 0;
+      s_asg[1] = 0;
+    }
+  }
+  __syncthreads();
+  if (s_asg[0]) {
+    int i = 0;
+    while (i < n_items && s_asg[2 + i] <= cid) ++i;
+    if (i >= n_items) return;  // a cluster no item needs
+    const BatchItem& P = s_items[i];
+    const long long k = s_asg[2 + i] - s_asg[1 + i], r = cid - s_asg[1 + i];
+    long long b, c;
+    built_range(P, b, c);
+    const long long s0 = c * r / k, s1 = c * (r + 1) / k;
+    if (s1 > s0) {
+      if constexpr (LAYOUT == HL_W52 || LAYOUT == HL_W52CH)
+        hist_segment_w52<NPL, LAYOUT>(cluster, P, b + s0, s1 - s0, bins_rm, Fp, F, B, rows0, rows1, pairs0, pairs1,
+                                      hist + (long long)(work_base + P.work) * slot_cells, rows_per_flush, smem_raw);
+      else
+        hist_segment<NPL, LAYOUT>(cluster, P, b + s0, s1 - s0, bins_rm, Fp, F, B, rows0, rows1, pairs0, pairs1,
+                                  hist + (long long)(work_base + P.work) * slot_cells, rows_per_flush, g_lim, p0,
+                                  s_red);
+    }
+    return;
+  }
   const long long lo = S * cid / cap, hi = S * (cid + 1) / cap;
   for (int i = 0; i < n_items && s_pre[i] < hi; ++i) {
     const BatchItem& P = s_items[i];

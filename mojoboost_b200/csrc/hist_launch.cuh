@@ -60,6 +60,7 @@ struct HistLaunch {
   size_t smem = 0;
   long long rows_per_flush = 1ll << 40;
   bool pdl = false;            // launch as a programmatic dependent (trainer iterations)
+  bool owned = true;           // may give items clusters of their own (k_hist); MOJOTREES_HIST_CONTIGUOUS=1: never
   int g_lim = 0;               // HL_QUANT16: offset making g non-negative
 };
 
@@ -97,7 +98,7 @@ void launch_hist_t(const HistLaunch& hl, cudaStream_t st, const Batch* batch, co
   cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t lc = hist_config(hl, hl.cluster, hl.row_ctas, st, attr);
   MTB_CUDA(cudaLaunchKernelEx(&lc, k_hist<NPL, L>, batch, bins_rm, Fp, F, B, r0, r1, p0, p1, hist, slot_cells,
-                              hl.rows_per_flush, hl.g_lim, ws, hl.min_rows_per_cta));
+                              hl.rows_per_flush, hl.g_lim, ws, hl.min_rows_per_cta, hl.owned ? 1 : 0));
 }
 
 // Every (layout, features per lane) instance the launch geometry can pick.
@@ -224,6 +225,7 @@ inline HistLaunch choose_hist_launch(int mode, bool const_h, int quant_bins, int
     }
   }
   if (const char* e = getenv("MOJOTREES_HIST_MIN_ROWS")) hl.min_rows_per_cta = std::max(1, atoi(e));
+  if (getenv("MOJOTREES_HIST_CONTIGUOUS")) hl.owned = false;
   return hl;
 }
 
