@@ -441,22 +441,47 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
   // written over the counts by warp 0 between the two barriers
   constexpr int E = ITEMS * 8;
   constexpr int PER = (E + 31) / 32;
-  for (long long tile = blockIdx.x; tile < Bt.n_tiles; tile += gridDim.x, par ^= 1) {
-    int it = 0;
-    {
-      int hi = n_items - 1;  // the last item whose first tile is <= tile
-      while (it < hi) {
-        const int mid = (it + hi + 1) >> 1;
-        if (s_items[mid].tile0 <= tile) it = mid;
-        else hi = mid - 1;
+  // The tile loop is software-pipelined: the next tile's row ids and pairs
+  // are loaded while this tile's ballots, cursor atomics and scatter run.
+  auto item_of = [&](long long tile) {
+    int it = 0, hi = n_items - 1;  // the last item whose first tile is <= tile
+    while (it < hi) {
+      const int mid = (it + hi + 1) >> 1;
+      if (s_items[mid].tile0 <= tile) it = mid;
+      else hi = mid - 1;
+    }
+    return it;
+  };
+  int rr[ITEMS], nrr[ITEMS] = {};
+  PairT pp[ITEMS], npp[ITEMS] = {};
+  auto load_tile = [&](long long tile, int (&r)[ITEMS], PairT (&q)[ITEMS]) {
+    const BatchItem& P = s_items[item_of(tile)];
+    const int* src_rows = P.src_buf ? rows1 : rows0;
+    const PairT* src_pairs = P.src_buf ? pairs1 : pairs0;
+    const long long end = P.begin + P.count;
+    const long long t0 = P.begin + (tile - P.tile0) * TILE;
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {  // every gather in flight before the first ballot
+      const long long i = t0 + (long long)j * 256 + threadIdx.x;
+      if (i < end) {
+        r[j] = src_rows[i];
+        q[j] = src_pairs[i];
       }
     }
+  };
+  if ((long long)blockIdx.x < Bt.n_tiles) load_tile(blockIdx.x, nrr, npp);
+  for (long long tile = blockIdx.x; tile < Bt.n_tiles; tile += gridDim.x, par ^= 1) {
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+      rr[j] = nrr[j];
+      pp[j] = npp[j];
+    }
+    if (tile + gridDim.x < Bt.n_tiles) load_tile(tile + gridDim.x, nrr, npp);
+    const int it = item_of(tile);
     const BatchItem& P = s_items[it];
     BatchItem& PG = Bt.items[it];  // the item's cursors live in global memory
     const int src_buf = P.src_buf;
-    const int* src_rows = src_buf ? rows1 : rows0;
     int* dst_rows = src_buf ? rows0 : rows1;
-    const PairT* src_pairs = src_buf ? pairs1 : pairs0;
     PairT* dst_pairs = src_buf ? pairs0 : pairs1;
     const uint8_t* col = bins_cm + (long long)P.feature * n;
     const long long begin = P.begin, end = P.begin + P.count;
@@ -464,19 +489,10 @@ __global__ void __launch_bounds__(256) k_partition(TreeState* ts, const uint8_t*
     const bool is_cat = P.is_cat != 0;
     const int thr = P.threshold, mbin = P.missing_bin;
     const bool dleft = P.default_left != 0;
-    int rr[ITEMS];
-    PairT pp[ITEMS];
     unsigned bl[ITEMS], br[ITEMS];
     bool valid[ITEMS], left[ITEMS];
 #pragma unroll
-    for (int j = 0; j < ITEMS; ++j) {  // every gather in flight before the first ballot
-      const long long i = t0 + (long long)j * 256 + threadIdx.x;
-      valid[j] = i < end;
-      if (valid[j]) {
-        rr[j] = src_rows[i];
-        pp[j] = src_pairs[i];
-      }
-    }
+    for (int j = 0; j < ITEMS; ++j) valid[j] = t0 + (long long)j * 256 + threadIdx.x < end;
 #pragma unroll
     for (int j = 0; j < ITEMS; ++j) {
       left[j] = false;
