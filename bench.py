@@ -51,7 +51,7 @@ LEAVES = 255
 # DRAM bytes (read + write) per row built, from the ncu capture of the root
 # histogram launch of the 2M-row case (k_hist, 16-bit packed cells):
 # 236.4 MB read + 4.1 MB written for 2,000,000 rows
-HIST_DRAM_BYTES_PER_ROW = (236.426240e6 + 4.148480e6) / 2_000_000
+HIST_DRAM_BYTES_PER_ROW = (237.680384e6 + 9.167616e6) / 2_000_000
 UNIT = "rounds/s"
 
 # The benchmark configurations: rows (per GPU for the
