@@ -67,8 +67,8 @@ CONFIGS = {
     "c3": dict(index=2, rows=5_000_000, feats=408, objective="regression", K=1, max_bin=63, leaves=127,
                quant=False, scaling="weak",
                desc="configs[2]: regression, 5M x (400 numeric at 90% zeros + 8 categorical of cardinality 1000), "
-                    "max_bin 63, num_leaves 127, fixed-point gradients; run dense and unbundled (408 binned "
-                    "columns: no sparse histogram path, no exclusive feature bundling)"),
+                    "max_bin 63, num_leaves 127, fixed-point gradients; sparse histograms (per row the bins outside "
+                    "each feature's default bin), unbundled (no bundle forms under max_conflict_rate 0)"),
     "c4": dict(index=3, rows=4_000_000, feats=64, objective="multiclass", K=10, max_bin=255, leaves=63, quant=False,
                scaling="weak", desc="configs[3]: softmax K=10, 4M x 64, max_bin 255, num_leaves 63, fixed-point "
                                     "gradients (ten trees per round)"),
@@ -434,7 +434,11 @@ def run_gpu(args):
     # the tree's counts are global: with several ranks this rank's histogram
     # launches read about its share of them (the shards are equal in size)
     hist_rows_local = hist_rows * n_local / n_global if world > 1 else hist_rows
-    hist_bytes = hist_rows_local * (F + pair_bytes)
+    sparse_entries = st.get("hist_sparse_entries", 0.0)
+    # sparse histograms read, per built row, its listed entries (4 B each),
+    # its row id (4 B), its two row offsets (16 B) and its gradient pair
+    row_bytes = (4.0 * sparse_entries / n_local + 20 + pair_bytes) if sparse_entries else (F + pair_bytes)
+    hist_bytes = hist_rows_local * row_bytes
     hist_gbs = hist_bytes / (hist_ms / 1000.0) / 1e9 if hist_ms > 0 else None
     per_round = 1.0 / max(1, st["rounds"])
     phases = {"hist_ms": st["hist_ms"] * per_round}
@@ -444,7 +448,10 @@ def run_gpu(args):
                    "hist_launches_timed": hist_launches, "hist_rows_timed": hist_rows})
     smem_peak = mb.shared_atomic_peak() if hist_ms > 0 else None
     # useful shared atomics of the histogram: (g+count word, h word) per row and feature
-    smem_achieved = hist_rows_local * F * 2 / (hist_ms / 1000.0) if hist_ms > 0 else None
+    # (sparse histograms: two atomics per listed entry for a constant hessian, three otherwise)
+    atomics_per_row = (sparse_entries / n_local * (2 if c["objective"] == "regression" else 3)
+                       if sparse_entries else F * 2)
+    smem_achieved = hist_rows_local * atomics_per_row / (hist_ms / 1000.0) if hist_ms > 0 else None
     peak, peak_kind = measured_peak()
     e2e = None
     if world == 1 and not args.no_e2e:
@@ -491,8 +498,13 @@ def run_gpu(args):
                      "peak_source": peak_kind, "kernel": "k_hist",
                      "algorithmic_bytes": ("with several ranks: this rank's share of the built rows (global / "
                                            "ranks); " if world > 1 else "") +
-                                          f"per launch: rows of the built children x ({F} bin bytes + "
-                                          f"{pair_bytes} gradient bytes); achieved = their sum over the timed "
+                                          (f"per launch: rows of the built children x {row_bytes:.1f} B (sparse "
+                                           f"histograms: {sparse_entries / n_local:.1f} listed entries x 4 B + "
+                                           f"row id, row offsets and {pair_bytes} gradient bytes)"
+                                           if sparse_entries else
+                                           f"per launch: rows of the built children x ({F} bin bytes + "
+                                           f"{pair_bytes} gradient bytes)") +
+                                          "; achieved = their sum over the timed "
                                           "rounds / the summed CUDA-event time of the histogram launches "
                                           "(a second fit of the same workload with those events on)",
                      "traffic_source": "ncu dram read+write bytes per row of the k_hist capture "

@@ -23,7 +23,7 @@ IMPORTANCE_SPLIT, IMPORTANCE_GAIN = 0, 1
 
 STAT_NAMES = ("fit_seconds", "upload_seconds", "hist_ms", "partition_ms", "scan_ms", "grad_ms",
               "hist_rows", "hist_bytes", "hist_launches", "kernel_launches", "rounds",
-              "commit_ms", "iterations", "expansions", "binning_seconds", "pick_steps")
+              "commit_ms", "iterations", "expansions", "binning_seconds", "pick_steps", "hist_sparse_entries")
 
 # Every symbol include/mojotrees.h declares, with its ctypes signature.
 _P, _I32, _I64, _D = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_double

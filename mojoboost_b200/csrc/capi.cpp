@@ -1156,7 +1156,7 @@ int32_t mojotrees_b200_train_stats(const MojoTreesModel* model, double* out_valu
                             s.scan_ms,     s.grad_ms,        s.hist_rows, s.hist_bytes,
                             (double)s.hist_launches, (double)s.kernel_launches, (double)s.rounds,
                             s.commit_ms,   (double)s.iterations, (double)s.expansions, s.binning_seconds,
-                            (double)s.pick_steps};
+                            (double)s.pick_steps, s.hist_sparse_entries};
         int64_t n = std::min<int64_t>(out_len, (int64_t)(sizeof v / sizeof v[0]));
         for (int64_t i = 0; i < n; ++i) out_values[i] = v[i];
         if (out_n) *out_n = n;

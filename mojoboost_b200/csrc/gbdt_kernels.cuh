@@ -1139,58 +1139,14 @@ __device__ void hist_segment_w52(cooperative_groups::cluster_group& cluster, con
   }
 }
 
-// CTAs of one feature group form clusters of CS along grid y.  The batch's
-// built rows, taken as one sequence (item after item), are split evenly among
-// ceil(rows / (min_rows_per_cta * CS)) clusters at most; a cluster whose share
-// spans several items accumulates one segment per item.
-template <int NPL, int LAYOUT>
-__global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__ batch, const uint8_t* __restrict__ bins_rm,
-                                               int Fp, int F, int B, const int* __restrict__ rows0,
-                                               const int* __restrict__ rows1, const void* __restrict__ pairs0,
-                                               const void* __restrict__ pairs1, int* __restrict__ hist,
-                                               long long slot_cells, long long rows_per_flush, int g_lim,
-                                               int work_base, int min_rows_per_cta, int allow_owned) {
-  pdl_enter();
-  namespace cg = cooperative_groups;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  unsigned int* p0 = reinterpret_cast<unsigned int*>(smem_raw);
-  // After the cells: the batch's items and the prefix sums of their built
-  // rows, staged with one coalesced copy (the item records are read many
-  // times below; from global memory each read is a dependent L2 round trip).
-  constexpr int kCellBytes = 4 * hist_layout_words(LAYOUT, NPL * kHistBinsPad * 32);
-  BatchItem* s_items = reinterpret_cast<BatchItem*>(smem_raw + kCellBytes);
-  long long* s_pre = reinterpret_cast<long long*>(s_items + kMaxBatch);
-  unsigned int* s_red = reinterpret_cast<unsigned int*>(s_pre + kMaxBatch + 1);  // 64 words
-  const int n_items = batch->n_items;  // uniform across the grid
-  if (n_items == 0) return;
-  {
-    const int* src = reinterpret_cast<const int*>(batch->items);
-    int* dst = reinterpret_cast<int*>(s_items);
-    const int words = n_items * (int)(sizeof(BatchItem) / sizeof(int));
-    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
-  }
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    long long carry = 0;
-    for (int base = 0; base < n_items; base += 32) {
-      long long b, c = 0;
-      if (base + lane < n_items) built_range(s_items[base + lane], b, c);
-#pragma unroll
-      for (int k = 1; k < 32; k <<= 1) {
-        const long long o = __shfl_up_sync(0xffffffffu, c, k);
-        if (lane >= k) c += o;
-      }
-      if (base + lane < n_items) s_pre[base + lane + 1] = carry + c;
-      carry += __shfl_sync(0xffffffffu, c, 31);
-    }
-    if (lane == 0) s_pre[0] = 0;
-  }
-  __syncthreads();
-  cg::cluster_group cluster = cg::this_cluster();
-  const int cs = (int)cluster.num_blocks();
-  const long long n_clusters = gridDim.y / cs;
-  const long long cid = blockIdx.y / cs;
+// Calls seg(item, first position, positions) for every segment cluster cid
+// of n_clusters (of cs CTAs each) accumulates in a launch over the staged
+// batch (s_pre: prefix sums of the items' built rows).  Every thread of the
+// block calls it; s_asg is 34 ints of shared scratch.
+template <typename Seg>
+__device__ void for_each_segment(int n_items, const BatchItem* s_items, const long long* s_pre, long long cid,
+                                 long long n_clusters, int cs, int min_rows_per_cta, int allow_owned, int* s_asg,
+                                 Seg&& seg) {
   const long long S = s_pre[n_items];
   if (S == 0) return;
   const long long per_cluster = (long long)min_rows_per_cta * cs;
@@ -1206,7 +1162,6 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__
   // counting as kHistMergeRows rows per CTA (per-launch traces of configs[1]
   // fit 32 us a merged segment against 3.6 ns a row for a cluster of two).
   // Every CTA computes the same choice from the same staged items.
-  int* s_asg = reinterpret_cast<int*>(s_red);  // [0] owned; [1 + i] first cluster of item i
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     const long long mr = (long long)kHistMergeRows * cs;
@@ -1269,15 +1224,7 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__
     long long b, c;
     built_range(P, b, c);
     const long long s0 = c * r / k, s1 = c * (r + 1) / k;
-    if (s1 > s0) {
-      if constexpr (LAYOUT == HL_W52 || LAYOUT == HL_W52CH)
-        hist_segment_w52<NPL, LAYOUT>(cluster, P, b + s0, s1 - s0, bins_rm, Fp, F, B, rows0, rows1, pairs0, pairs1,
-                                      hist + (long long)(work_base + P.work) * slot_cells, rows_per_flush, smem_raw);
-      else
-        hist_segment<NPL, LAYOUT>(cluster, P, b + s0, s1 - s0, bins_rm, Fp, F, B, rows0, rows1, pairs0, pairs1,
-                                  hist + (long long)(work_base + P.work) * slot_cells, rows_per_flush, g_lim, p0,
-                                  s_red);
-    }
+    if (s1 > s0) seg(P, b + s0, s1 - s0);
     return;
   }
   const long long lo = S * cid / cap, hi = S * (cid + 1) / cap;
@@ -1288,17 +1235,76 @@ __global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__
     built_range(P, b, c);
     const long long s0 = lo > acc ? lo : acc;
     const long long s1 = hi < acc + c ? hi : acc + c;
-    if (s1 > s0) {
-      if constexpr (LAYOUT == HL_W52 || LAYOUT == HL_W52CH)
-        hist_segment_w52<NPL, LAYOUT>(cluster, P, b + (s0 - acc), s1 - s0, bins_rm, Fp, F, B, rows0, rows1, pairs0,
-                                      pairs1, hist + (long long)(work_base + P.work) * slot_cells, rows_per_flush,
-                                      smem_raw);
-      else
-        hist_segment<NPL, LAYOUT>(cluster, P, b + (s0 - acc), s1 - s0, bins_rm, Fp, F, B, rows0, rows1, pairs0,
-                                  pairs1, hist + (long long)(work_base + P.work) * slot_cells, rows_per_flush, g_lim,
-                                  p0, s_red);
-    }
+    if (s1 > s0) seg(P, b + (s0 - acc), s1 - s0);
   }
+}
+
+// CTAs of one feature group form clusters of CS along grid y.  The batch's
+// built rows, taken as one sequence (item after item), are split evenly among
+// ceil(rows / (min_rows_per_cta * CS)) clusters at most; a cluster whose share
+// spans several items accumulates one segment per item.
+template <int NPL, int LAYOUT>
+__global__ void __launch_bounds__(kHistThreads) k_hist(const Batch* __restrict__ batch, const uint8_t* __restrict__ bins_rm,
+                                               int Fp, int F, int B, const int* __restrict__ rows0,
+                                               const int* __restrict__ rows1, const void* __restrict__ pairs0,
+                                               const void* __restrict__ pairs1, int* __restrict__ hist,
+                                               long long slot_cells, long long rows_per_flush, int g_lim,
+                                               int work_base, int min_rows_per_cta, int allow_owned) {
+  pdl_enter();
+  namespace cg = cooperative_groups;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  unsigned int* p0 = reinterpret_cast<unsigned int*>(smem_raw);
+  // After the cells: the batch's items and the prefix sums of their built
+  // rows, staged with one coalesced copy (the item records are read many
+  // times below; from global memory each read is a dependent L2 round trip).
+  constexpr int kCellBytes = 4 * hist_layout_words(LAYOUT, NPL * kHistBinsPad * 32);
+  BatchItem* s_items = reinterpret_cast<BatchItem*>(smem_raw + kCellBytes);
+  long long* s_pre = reinterpret_cast<long long*>(s_items + kMaxBatch);
+  unsigned int* s_red = reinterpret_cast<unsigned int*>(s_pre + kMaxBatch + 1);  // 64 words
+  const int n_items = batch->n_items;  // uniform across the grid
+  if (n_items == 0) return;
+  {
+    const int* src = reinterpret_cast<const int*>(batch->items);
+    int* dst = reinterpret_cast<int*>(s_items);
+    const int words = n_items * (int)(sizeof(BatchItem) / sizeof(int));
+    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    long long carry = 0;
+    for (int base = 0; base < n_items; base += 32) {
+      long long b, c = 0;
+      if (base + lane < n_items) built_range(s_items[base + lane], b, c);
+#pragma unroll
+      for (int k = 1; k < 32; k <<= 1) {
+        const long long o = __shfl_up_sync(0xffffffffu, c, k);
+        if (lane >= k) c += o;
+      }
+      if (base + lane < n_items) s_pre[base + lane + 1] = carry + c;
+      carry += __shfl_sync(0xffffffffu, c, 31);
+    }
+    if (lane == 0) s_pre[0] = 0;
+  }
+  __syncthreads();
+  cg::cluster_group cluster = cg::this_cluster();
+  const int cs = (int)cluster.num_blocks();
+  const long long n_clusters = gridDim.y / cs;
+  const long long cid = blockIdx.y / cs;
+  const long long S = s_pre[n_items];
+  if (S == 0) return;
+  for_each_segment(n_items, s_items, s_pre, cid, n_clusters, cs, min_rows_per_cta, allow_owned,
+                   reinterpret_cast<int*>(s_red), [&](const BatchItem& P, long long seg_b, long long seg_n) {
+                     if constexpr (LAYOUT == HL_W52 || LAYOUT == HL_W52CH)
+                       hist_segment_w52<NPL, LAYOUT>(cluster, P, seg_b, seg_n, bins_rm, Fp, F, B, rows0, rows1,
+                                                     pairs0, pairs1,
+                                                     hist + (long long)(work_base + P.work) * slot_cells,
+                                                     rows_per_flush, smem_raw);
+                     else
+                       hist_segment<NPL, LAYOUT>(cluster, P, seg_b, seg_n, bins_rm, Fp, F, B, rows0, rows1, pairs0,
+                                                 pairs1, hist + (long long)(work_base + P.work) * slot_cells,
+                                                 rows_per_flush, g_lim, p0, s_red);
+                   });
 }
 
 // ---------------------------------------------------------------------------

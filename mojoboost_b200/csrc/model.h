@@ -74,6 +74,7 @@ struct TrainStats {
   int iterations = 0;               // batch iterations that did work, summed over trees
   int expansions = 0;               // leaves whose children were computed, summed over trees
   long long pick_steps = 0;         // commit-kernel pick-loop steps, summed over trees
+  double hist_sparse_entries = 0.0; // entries of the sparse histogram's row lists (0: dense histograms)
   int kernel_launches = 0;          // kernels this library launched
   int rounds = 0;
   std::vector<double> round_ms;     // device time of each round (CUDA events on the trainer's stream)

@@ -22,6 +22,7 @@
 #include "gbdt_device.cuh"
 #include "gbdt_kernels.cuh"
 #include "hist_launch.cuh"
+#include "sparse_hist.cuh"
 #include "collective.h"
 #include "device_binning.h"
 #include "trainer.h"
@@ -400,6 +401,54 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   // clusters need.
   const bool pdl = getenv("MOJOTREES_PDL") != nullptr;
   hl.pdl = pdl;
+
+  // Sparse histograms (fixed-point modes): used when every feature's cells
+  // fit one CTA and a row lists under 40% of its bins outside the features'
+  // default bins.  MOJOTREES_HIST_SPARSE=0 never uses them, =1 whenever
+  // the cells fit.
+  int sparse_planes = 0, sparse_bp = 1;
+  DevBuf<int> d_default_bin;
+  DevBuf<long long> d_row_ptr;
+  DevBuf<uint32_t> d_entries;
+  {
+    const char* sp_env = getenv("MOJOTREES_HIST_SPARSE");
+    const int want = sp_env ? atoi(sp_env) : -1;
+    while (sparse_bp < B) sparse_bp <<= 1;
+    const int planes = const_h ? 2 : 3;
+    if (want != 0 && mode == MODE_FIXED && !wide && B <= 256 &&
+        sparse_hist_smem(planes, F, sparse_bp) <= 227 * 1024) {
+      d_default_bin.alloc(F);
+      k_sparse_default_bins<<<F, 256, 0, st>>>(d_bins_cm.p, N, d_default_bin.p);
+      DevBuf<long long> d_counts, d_block_sums;
+      d_counts.alloc(N);
+      d_row_ptr.alloc(N + 1);
+      const long long nb = (N + kScanChunk - 1) / kScanChunk;
+      d_block_sums.alloc(nb);
+      const unsigned rgrid = (unsigned)std::min<long long>((N + 255) / 256, (long long)n_sm * 16);
+      k_sparse_rows<<<rgrid, 256, Fp, st>>>(d_bins_rm.p, N, F, Fp, d_default_bin.p, d_counts.p, nullptr, nullptr);
+      k_prefix_blocks<<<(unsigned)nb, kScanChunk, 0, st>>>(d_counts.p, N, d_row_ptr.p, d_block_sums.p);
+      k_prefix_sums<<<1, 1024, 0, st>>>(d_block_sums.p, nb);
+      k_prefix_add<<<(unsigned)nb, kScanChunk, 0, st>>>(N, d_row_ptr.p, d_block_sums.p);
+      stats.kernel_launches += 5;
+      long long nnz = 0;
+      MTB_CUDA(cudaMemcpyAsync(&nnz, d_row_ptr.p + N, sizeof(long long), cudaMemcpyDeviceToHost, st));
+      MTB_CUDA(cudaStreamSynchronize(st));
+      if (want == 1 || (double)nnz < 0.4 * (double)F * (double)N) {
+        d_entries.alloc((size_t)std::max(1ll, nnz));
+        k_sparse_rows<<<rgrid, 256, Fp, st>>>(d_bins_rm.p, N, F, Fp, d_default_bin.p, nullptr, d_row_ptr.p,
+                                              d_entries.p);
+        stats.kernel_launches++;
+        sparse_planes = planes;
+        stats.hist_sparse_entries = (double)nnz;
+        MTB_CUDA(cudaFuncSetAttribute(planes == 2 ? k_hist_sparse<2> : k_hist_sparse<3>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)sparse_hist_smem(planes, F, sparse_bp)));
+      } else {
+        d_row_ptr.free();
+        d_default_bin.free();
+      }
+    }
+  }
   // partition geometry (MOJOTREES_PART_ITEMS / MOJOTREES_PART_BLOCKS_PER_SM
   // override the rows per thread of a tile and the resident blocks per SM)
   int part_bps = 4;
@@ -520,8 +569,16 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   auto hist = [&]() {
     hist_timer.begin(&stats.hist_ms);
     if (trace_hist) MTB_CUDA(cudaEventRecord(th0, st));
-    launch_hist(hl, st, batch_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p, d_pairs1.p,
-                d_hist.p, slot_cells, work_base);
+    if (sparse_planes)
+      launch_chained(pdl, sparse_planes == 2 ? k_hist_sparse<2> : k_hist_sparse<3>, n_sm, kSparseThreads,
+                     sparse_hist_smem(sparse_planes, F, sparse_bp), st, batch_of(d_ts.p),
+                     (const uint32_t*)d_entries.p, (const long long*)d_row_ptr.p, (const int*)d_default_bin.p, F, B,
+                     sparse_bp, (const int*)d_rows0.p, (const int*)d_rows1.p,
+                     reinterpret_cast<const int2*>(d_pairs0.p), reinterpret_cast<const int2*>(d_pairs1.p), d_hist.p,
+                     slot_cells, work_base, hl.min_rows_per_cta, hl.owned ? 1 : 0);
+    else
+      launch_hist(hl, st, batch_of(d_ts.p), d_bins_rm.p, Fp, F, B, d_rows0.p, d_rows1.p, d_pairs0.p, d_pairs1.p,
+                  d_hist.p, slot_cells, work_base);
     hist_timer.end();
     if (trace_hist) {
       MTB_CUDA(cudaEventRecord(th1, st));

@@ -80,6 +80,19 @@ CASES = {
                             dict(objective="regression", rounds=3, leaves=31,
                                  extra={"categorical_feature": "2,5", "min_data_per_group": 20, "cat_smooth": 5.0,
                                         "gpu_histogram_precision": "int64"}), 63),
+    # sparse histograms (fixed point, a row listing few bins outside its
+    # features' default bins): constant hessian (g, count cells), binary with
+    # missing values and categoricals (g, h, count), multiclass, and a
+    # configs[2]-like width of 400 columns at 63 bins
+    "sparse_l2_fixed": (dict(seed=27, n=80_000, f=60, zero_frac=0.9),
+                        dict(objective="regression", rounds=4, leaves=63), 63),
+    "sparse_binary_fixed": (dict(seed=28, n=60_000, f=40, kind="binary", zero_frac=0.85, nan_frac=0.03,
+                                 cat_cols=(3, 7), n_cat=20),
+                            dict(objective="binary", rounds=4, leaves=31, extra={"categorical_feature": "3,7"}), 255),
+    "sparse_multiclass_fixed": (dict(seed=29, n=30_000, f=24, kind="multiclass", n_classes=3, zero_frac=0.9),
+                                dict(objective="multiclass", rounds=3, leaves=15, n_classes=3), 63),
+    "sparse_wide_fixed": (dict(seed=30, n=40_000, f=400, zero_frac=0.9),
+                          dict(objective="regression", rounds=2, leaves=127), 63),
     "regularised_quant": (dict(seed=18, n=30_000, f=16, kind="binary"),
                           dict(objective="binary", rounds=4, leaves=31, quant=True, min_data=2,
                                extra={"lambda_l1": 0.2, "lambda_l2": 0.0, "min_sum_hessian_in_leaf": 3.0}), 255),
@@ -218,3 +231,24 @@ def test_gpu_replay_batch_selection_matches_oracle(case, mtlib, oracle, monkeypa
     only which leaves are built early; the trees stay the oracle's."""
     monkeypatch.setenv("MOJOTREES_COMMIT_SELECT", "replay")
     test_gpu_matches_oracle(case, mtlib, oracle)
+
+
+@pytest.mark.parametrize("case", ["l2_fixed", "missing_cat_fixed", "sparse_l2_fixed"])
+def test_gpu_forced_histogram_kind_matches_oracle(case, mtlib, oracle, monkeypatch):
+    """MOJOTREES_HIST_SPARSE=1 (sparse histograms even where rows list
+    nearly every bin) and =0 (dense histograms for sparse data) grow the
+    oracle's trees as well."""
+    for v in ("1", "0"):
+        monkeypatch.setenv("MOJOTREES_HIST_SPARSE", v)
+        test_gpu_matches_oracle(case, mtlib, oracle)
+
+
+def test_gpu_sparse_histograms_are_chosen(mtlib):
+    """Sparse data in a fixed-point mode takes the sparse histogram path, and
+    its row lists hold only the entries outside the default bins."""
+    X, y = make_data(31, 20_000, 30, zero_frac=0.9)
+    bins, mbin, ncat, nb = mtlib.bin_dense(X, {"max_bin": 63})
+    m = mtlib.train_binned(bins, nb, y, params_for("regression", 2, 15), missing_bin=mbin, n_categories=ncat)
+    entries = m.stats()["hist_sparse_entries"]
+    default = np.array([np.bincount(bins[f], minlength=256).argmax() for f in range(bins.shape[0])])
+    assert entries == int((bins != default[:, None]).sum())
