@@ -115,40 +115,67 @@ __device__ __forceinline__ void block_max_to(double ag, double ah, double* sm, R
 }
 
 // Per-row derivatives for L2 / logistic, narrowed to Float32.  1024 threads,
-// one row each.  FIXED mode writes per-block pairwise |g|, |h| partials;
-// QUANT mode folds max |g|, max |h| into the round's scales.
+// one row of each 1024-row chunk each.  FIXED mode writes per-chunk pairwise
+// |g|, |h| partials; QUANT mode folds max |g|, max |h| into the round's
+// scales.
 __global__ void __launch_bounds__(1024) k_grad(const double* __restrict__ raw, const double* __restrict__ y,
                                                float* __restrict__ g32, float* __restrict__ h32,
                                                long long n, int objective, int mode,
                                                double* __restrict__ part_g, double* __restrict__ part_h,
                                                RoundScales* sc) {
+  // Each block walks 1024-row chunks c = blockIdx.x, + gridDim.x, ... with
+  // the next chunk's raw scores and labels loaded while this one is
+  // computed; the fixed-point partial sums stay one per 1024-row chunk (the
+  // pairwise order the scale depends on), the quantized maxima are folded
+  // over the block's chunks before one atomic per block.
   __shared__ double sm[32];
-  long long r = (long long)blockIdx.x * 1024 + threadIdx.x;
-  double g = 0.0, h = 0.0;
-  if (r < n) {
-    double rr = raw[r];
-    double yy = y[r];
-    if (objective == OBJ_LOGISTIC) {
-      double p = mt_sigmoid(rr);
-      g = narrow32(1.0 * (p - yy));
-      double hh = p * (1.0 - p);
-      if (hh < 1e-16) hh = 1e-16;
-      h = narrow32(1.0 * hh);
-    } else {
-      g = narrow32(1.0 * (rr - yy));
-      h = 1.0;
+  const long long n_chunks = (n + 1023) / 1024;
+  double mg = 0.0, mh = 0.0;
+  double nr = 0.0, ny = 0.0;
+  long long c = blockIdx.x;
+  if (c < n_chunks) {
+    const long long r = c * 1024 + threadIdx.x;
+    if (r < n) {
+      nr = raw[r];
+      ny = y[r];
     }
-    g32[r] = (float)g;
-    h32[r] = (float)h;
   }
-  if (mode == MODE_FIXED) {
-    double sg = block_pairwise_1024(fabs(g), sm);
-    if (threadIdx.x == 0) part_g[blockIdx.x] = sg;
-    double sh = block_pairwise_1024(fabs(h), sm);
-    if (threadIdx.x == 0) part_h[blockIdx.x] = sh;
-  } else {
-    block_max_to(fabs(g), fabs(h), sm, sc);
+  for (; c < n_chunks; c += gridDim.x) {
+    const double rr = nr, yy = ny;
+    const long long r = c * 1024 + threadIdx.x;
+    if (c + gridDim.x < n_chunks) {
+      const long long rn = r + (long long)gridDim.x * 1024;
+      if (rn < n) {
+        nr = raw[rn];
+        ny = y[rn];
+      }
+    }
+    double g = 0.0, h = 0.0;
+    if (r < n) {
+      if (objective == OBJ_LOGISTIC) {
+        double p = mt_sigmoid(rr);
+        g = narrow32(1.0 * (p - yy));
+        double hh = p * (1.0 - p);
+        if (hh < 1e-16) hh = 1e-16;
+        h = narrow32(1.0 * hh);
+      } else {
+        g = narrow32(1.0 * (rr - yy));
+        h = 1.0;
+      }
+      g32[r] = (float)g;
+      h32[r] = (float)h;
+    }
+    if (mode == MODE_FIXED) {
+      double sg = block_pairwise_1024(fabs(g), sm);
+      if (threadIdx.x == 0) part_g[c] = sg;
+      double sh = block_pairwise_1024(fabs(h), sm);
+      if (threadIdx.x == 0) part_h[c] = sh;
+    } else {
+      mg = fmax(mg, fabs(g));
+      mh = fmax(mh, fabs(h));
+    }
   }
+  if (mode != MODE_FIXED) block_max_to(mg, mh, sm, sc);
 }
 
 // Softmax probabilities of every row (boosting.mojo:3529-3572), K <= 64.

@@ -653,8 +653,8 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
         MTB_CUDA(cudaMemsetAsync(d_ph.p, 0, sizeof(double) * P_rank, st));
       }
       if (K == 1)
-        k_grad<<<(unsigned)grid1024, 1024, 0, st>>>(d_raw.p, d_y.p, d_g.p, d_h.p, N, cfg.objective, mode, d_pg.p,
-                                                    d_ph.p, d_sc.p);
+        k_grad<<<(unsigned)std::min<long long>(grid1024, 2ll * n_sm), 1024, 0, st>>>(
+            d_raw.p, d_y.p, d_g.p, d_h.p, N, cfg.objective, mode, d_pg.p, d_ph.p, d_sc.p);
       else
         k_grad_softmax<<<(unsigned)grid1024, 1024, 0, st>>>(d_prob.p, d_y.p, d_g.p, d_h.p, N, K, k, mode, d_pg.p,
                                                             d_ph.p, d_sc.p);
