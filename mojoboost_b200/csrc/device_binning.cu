@@ -223,4 +223,55 @@ void transform_on_device(const BinMapper& m, const double* x, int64_t n_rows, ui
             (long long)n_rows, F);
 }
 
+// Host data (pre-binned uint8 columns, labels) to the device through the
+// same page-registered staging buffers as the float64 columns: 32 MB pieces, each
+// copied into a staging buffer by all host threads while the previous
+// piece's DMA runs (a plain copy from pageable memory moved ~6 GB/s).
+void upload_host(const void* src, int64_t bytes, void* dst_dev, cudaStream_t st) {
+  const uint8_t* bins = static_cast<const uint8_t*>(src);
+  uint8_t* d_bins = static_cast<uint8_t*>(dst_dev);
+  constexpr int kStages = 3;
+  constexpr int64_t kPiece = 32ll << 20;
+  if (bytes <= kPiece) {
+    MTB_CUDA_BIN(cudaMemcpyAsync(d_bins, bins, (size_t)bytes, cudaMemcpyHostToDevice, st));
+    MTB_CUDA_BIN(cudaStreamSynchronize(st));
+    return;
+  }
+  struct Stages {
+    uint8_t* h[kStages] = {};
+    bool reg[kStages] = {};
+    cudaEvent_t e[kStages] = {};
+    ~Stages() {
+      for (int i = 0; i < kStages; ++i) {
+        if (e[i]) {
+          cudaEventSynchronize(e[i]);
+          cudaEventDestroy(e[i]);
+        }
+        if (reg[i]) cudaHostUnregister(h[i]);
+        free(h[i]);
+      }
+    }
+  } sg;
+  for (int i = 0; i < kStages; ++i) {
+    sg.h[i] = static_cast<uint8_t*>(aligned_alloc(4096, (size_t)kPiece));
+    if (!sg.h[i]) throw std::runtime_error("host staging allocation failed");
+    MTB_CUDA_BIN(cudaHostRegister(sg.h[i], (size_t)kPiece, cudaHostRegisterDefault));
+    sg.reg[i] = true;
+    MTB_CUDA_BIN(cudaEventCreateWithFlags(&sg.e[i], cudaEventDisableTiming));
+  }
+  int k = 0;
+  for (int64_t off = 0; off < bytes; off += kPiece) {
+    const int64_t len = std::min<int64_t>(kPiece, bytes - off);
+    MTB_CUDA_BIN(cudaEventSynchronize(sg.e[k]));  // the buffer's previous DMA is done
+    uint8_t* dst = sg.h[k];
+    const int64_t part = 1 << 20;
+#pragma omp parallel for schedule(static)
+    for (int64_t b = 0; b < len; b += part) memcpy(dst + b, bins + off + b, (size_t)std::min<int64_t>(part, len - b));
+    MTB_CUDA_BIN(cudaMemcpyAsync(d_bins + off, dst, (size_t)len, cudaMemcpyHostToDevice, st));
+    MTB_CUDA_BIN(cudaEventRecord(sg.e[k], st));
+    k = (k + 1) % kStages;
+  }
+  MTB_CUDA_BIN(cudaStreamSynchronize(st));
+}
+
 }  // namespace mtb

@@ -19,4 +19,9 @@ namespace mtb {
 void transform_on_device(const BinMapper& m, const double* x, int64_t n_rows, uint8_t* d_bins,
                          cudaStream_t stream);
 
+// Copies `bytes` bytes of host memory (pre-binned columns, labels) to device
+// memory on `stream` through page-registered staging buffers; returns when
+// the copy is complete.  Throws std::runtime_error on a CUDA error.
+void upload_host(const void* src, int64_t bytes, void* dst_dev, cudaStream_t stream);
+
 }  // namespace mtb

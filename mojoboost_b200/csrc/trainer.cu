@@ -172,7 +172,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     if (!in.mapper) throw std::runtime_error("dense input without a bin mapper");
     transform_on_device(*in.mapper, in.dense_fm, N, d_bins_cm.p, st);
   } else {
-    MTB_CUDA(cudaMemcpyAsync(d_bins_cm.p, in.bins_fm, (size_t)F * N, cudaMemcpyHostToDevice, st));
+    upload_host(in.bins_fm, (int64_t)F * N, d_bins_cm.p, st);
   }
   {
     dim3 grid((unsigned)((N + 255) / 256), Fp / 16);
@@ -182,7 +182,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   DevBuf<double> d_y, d_raw, d_prob;
   mark("bins uploaded, transposed");
   d_y.alloc(N);
-  MTB_CUDA(cudaMemcpyAsync(d_y.p, in.labels, sizeof(double) * N, cudaMemcpyHostToDevice, st));
+  upload_host(in.labels, (int64_t)sizeof(double) * N, d_y.p, st);
   d_raw.alloc((size_t)N * K);
   if (K > 1) d_prob.alloc((size_t)N * K);
 
