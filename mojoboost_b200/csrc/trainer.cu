@@ -601,18 +601,23 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
     }
   };
   // the built children's cells summed over every device's rows (exact int32)
-  auto reduce_work = [&]() {
+  // Only the first `slots` work slots can be in use: iteration i of a tree
+  // expands at most 2^i leaves (the virtual tree has one more unexpanded node
+  // than it has expanded ones, and every expanded node came from an earlier
+  // iteration), and items take work slots 0, 1, ... in batch order.
+  auto reduce_work = [&](int iteration) {
+    const size_t slots = (size_t)std::min(batch_cap, 1 << std::min(iteration, 5));
     if (dp_feature && wide)
-      coll->reduce_scatter_slots_i64(reinterpret_cast<long long*>(d_hist.p + (size_t)work_base * slot_cells),
-                                     (size_t)batch_cap, (size_t)slot_cells / 2, (size_t)Fb * 3 * B, st);
+      coll->reduce_scatter_slots_i64(reinterpret_cast<long long*>(d_hist.p + (size_t)work_base * slot_cells), slots,
+                                     (size_t)slot_cells / 2, (size_t)Fb * 3 * B, st);
     else if (dp_feature)
-      coll->reduce_scatter_slots_i32(d_hist.p + (size_t)work_base * slot_cells, (size_t)batch_cap,
-                                     (size_t)slot_cells, (size_t)Fb * 3 * B, st);
+      coll->reduce_scatter_slots_i32(d_hist.p + (size_t)work_base * slot_cells, slots, (size_t)slot_cells,
+                                     (size_t)Fb * 3 * B, st);
     else if (coll && wide)
       coll->allreduce_sum_i64(reinterpret_cast<long long*>(d_hist.p + (size_t)work_base * slot_cells),
-                              (size_t)slot_cells / 2 * batch_cap, st);
+                              (size_t)slot_cells / 2 * slots, st);
     else if (coll)
-      coll->allreduce_sum_i32(d_hist.p + (size_t)work_base * slot_cells, (size_t)slot_cells * batch_cap, st);
+      coll->allreduce_sum_i32(d_hist.p + (size_t)work_base * slot_cells, (size_t)slot_cells * slots, st);
   };
   DevBuf<ChildRec> d_rec, d_rec_all;
   if (dp_feature) {
@@ -775,7 +780,7 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
         // grid has completed)
         if (i > 0) MTB_CUDA(cudaEventRecord(iter_ev[(i - 1) % kRing], st));
         hist();
-        reduce_work();
+        reduce_work(i);
         timer.begin(&stats.scan_ms);
         if (!dp_feature) {
           launch_chained(pdl,
