@@ -6,6 +6,8 @@
 
 #include <algorithm>
 #include <chrono>
+#include <map>
+#include <mutex>
 #include <cstdio>
 #include <stdexcept>
 #include <string>
@@ -98,6 +100,92 @@ struct DeviceArray {
   ~DeviceArray() { cudaFree(p); }
 };
 
+// Three 32 MB page-registered host buffers, three device buffers and their
+// events: the staging of the column uploads.  Registering and allocating
+// them costs tens of milliseconds, so each device keeps one set from its
+// first upload until the process exits (96 MB pinned host memory and 96 MB
+// device memory); an upload that finds the set in use by another thread
+// makes a set of its own for the call.
+constexpr int kStages = 3;
+constexpr size_t kStageBytes = 32u << 20;
+struct StagingSet {
+  uint8_t* h[kStages] = {};
+  bool reg[kStages] = {};
+  void* d[kStages] = {};
+  cudaEvent_t e[kStages] = {};
+  void create() {
+    for (int i = 0; i < kStages; ++i) {
+      h[i] = static_cast<uint8_t*>(aligned_alloc(4096, kStageBytes));
+      if (!h[i]) throw std::runtime_error("host staging allocation failed");
+      MTB_CUDA_BIN(cudaHostRegister(h[i], kStageBytes, cudaHostRegisterDefault));
+      reg[i] = true;
+      MTB_CUDA_BIN(cudaMalloc(&d[i], kStageBytes));
+      MTB_CUDA_BIN(cudaEventCreateWithFlags(&e[i], cudaEventDisableTiming));
+    }
+  }
+  void destroy() {
+    for (int i = 0; i < kStages; ++i) {
+      if (e[i]) {
+        cudaEventSynchronize(e[i]);
+        cudaEventDestroy(e[i]);
+      }
+      if (reg[i]) cudaHostUnregister(h[i]);
+      free(h[i]);
+      if (d[i]) cudaFree(d[i]);
+      e[i] = nullptr;
+      reg[i] = false;
+      h[i] = nullptr;
+      d[i] = nullptr;
+    }
+  }
+};
+std::mutex g_staging_mutex;
+std::map<int, StagingSet> g_staging;
+std::map<int, bool> g_staging_busy;
+
+// The device's cached set (or a fresh one for this call when it is in use),
+// released at scope exit.
+struct Staging {
+  StagingSet own;
+  StagingSet* set = nullptr;
+  int dev = -1;
+  Staging() {
+    MTB_CUDA_BIN(cudaGetDevice(&dev));
+    {
+      std::lock_guard<std::mutex> lock(g_staging_mutex);
+      if (!g_staging_busy[dev]) {
+        g_staging_busy[dev] = true;
+        set = &g_staging[dev];
+      }
+    }
+    if (!set) {
+      set = &own;
+      own.create();
+      return;
+    }
+    if (!set->h[0]) {
+      try {
+        set->create();
+      } catch (...) {
+        set->destroy();
+        std::lock_guard<std::mutex> lock(g_staging_mutex);
+        g_staging_busy[dev] = false;
+        throw;
+      }
+    }
+  }
+  ~Staging() {
+    for (int i = 0; i < kStages; ++i)
+      if (set->e[i]) cudaEventSynchronize(set->e[i]);
+    if (set == &own) {
+      own.destroy();
+    } else {
+      std::lock_guard<std::mutex> lock(g_staging_mutex);
+      g_staging_busy[dev] = false;
+    }
+  }
+};
+
 }  // namespace
 
 void transform_on_device(const BinMapper& m, const double* x, int64_t n_rows, uint8_t* d_bins,
@@ -126,21 +214,19 @@ void transform_on_device(const BinMapper& m, const double* x, int64_t n_rows, ui
     MTB_CUDA_BIN(cudaMemcpyAsync(d_codes.p, m.cat_codes.data(), sizeof(int64_t) * m.cat_codes.size(),
                                  cudaMemcpyHostToDevice, st));
 
-  // The column-major matrix is streamed in chunks of kChunkBytes: several
+  // The column-major matrix is streamed in chunks of kStageBytes: several
   // whole features when a column is short, else a row range of one feature.
-  // Each chunk is copied by all host threads into one of kStages page-locked
-  // buffers, sent to the device and binned there; the memcpy of a chunk
-  // overlaps the DMA of the previous one.  The buffers are ordinary
-  // allocations registered with the driver, which pins pages several times
-  // faster than cudaHostAlloc.
+  // Each chunk is copied by all host threads into one of the kStages
+  // page-locked staging buffers, sent to the device and binned there; the
+  // memcpy of a chunk overlaps the DMA of the previous one.  The buffers are
+  // ordinary allocations registered with the driver, which pins pages several
+  // times faster than cudaHostAlloc, kept per device (StagingSet).
   // MOJOTREES_TRACE_UPLOAD=1 prints the phase times of this function to stderr
   const bool trace = getenv("MOJOTREES_TRACE_UPLOAD") != nullptr;
   auto clk = [] { return std::chrono::steady_clock::now(); };
   const auto tt0 = clk();
   double t_wait = 0.0, t_copy = 0.0;
-  constexpr int kStages = 3;
-  constexpr int64_t kChunkBytes = 32ll << 20;
-  const int64_t chunk_elems_max = kChunkBytes / (int64_t)sizeof(double);
+  const int64_t chunk_elems_max = (int64_t)kStageBytes / (int64_t)sizeof(double);
   int64_t chunk_rows, per_chunk;
   if (n_rows >= chunk_elems_max) {
     chunk_rows = chunk_elems_max;
@@ -149,33 +235,8 @@ void transform_on_device(const BinMapper& m, const double* x, int64_t n_rows, ui
     chunk_rows = std::max<int64_t>(1, n_rows);
     per_chunk = std::max<int64_t>(1, std::min<int64_t>({(int64_t)F, chunk_elems_max / chunk_rows, 65535}));
   }
-  const int64_t stage_elems = chunk_rows * per_chunk;
-  struct Stages {
-    double* h[kStages] = {};
-    bool reg[kStages] = {};
-    double* d[kStages] = {};
-    cudaEvent_t e[kStages] = {};
-    ~Stages() {
-      for (int i = 0; i < kStages; ++i) {
-        if (e[i]) {
-          cudaEventSynchronize(e[i]);
-          cudaEventDestroy(e[i]);
-        }
-        if (reg[i]) cudaHostUnregister(h[i]);
-        free(h[i]);
-        if (d[i]) cudaFree(d[i]);
-      }
-    }
-  } sg;
-  const size_t stage_bytes = ((size_t)stage_elems * sizeof(double) + 4095) & ~(size_t)4095;
-  for (int i = 0; i < kStages; ++i) {
-    sg.h[i] = static_cast<double*>(aligned_alloc(4096, stage_bytes));
-    if (!sg.h[i]) throw std::runtime_error("host staging allocation failed");
-    MTB_CUDA_BIN(cudaHostRegister(sg.h[i], stage_bytes, cudaHostRegisterDefault));
-    sg.reg[i] = true;
-    MTB_CUDA_BIN(cudaMalloc(&sg.d[i], stage_bytes));
-    MTB_CUDA_BIN(cudaEventCreateWithFlags(&sg.e[i], cudaEventDisableTiming));
-  }
+  Staging stg;
+  StagingSet& sg = *stg.set;
   const int64_t rows_per_block = 8192;
   const auto tt1 = clk();
   int k = 0;
@@ -187,7 +248,7 @@ void transform_on_device(const BinMapper& m, const double* x, int64_t n_rows, ui
       const auto ta = clk();
       MTB_CUDA_BIN(cudaEventSynchronize(sg.e[k]));
       const auto tb = clk();
-      double* dst = sg.h[k];
+      double* dst = reinterpret_cast<double*>(sg.h[k]);
       // nf columns of nr values each, packed back to back
       const int64_t elems = (int64_t)nf * nr;
       const int64_t piece = 1 << 17;
@@ -209,7 +270,8 @@ void transform_on_device(const BinMapper& m, const double* x, int64_t n_rows, ui
       MTB_CUDA_BIN(cudaMemcpyAsync(sg.d[k], dst, sizeof(double) * elems, cudaMemcpyHostToDevice, st));
       MTB_CUDA_BIN(cudaEventRecord(sg.e[k], st));
       const unsigned row_blocks = (unsigned)((nr + rows_per_block - 1) / rows_per_block);
-      k_bin_columns<<<dim3(row_blocks, nf), kBinThreads, 0, st>>>(sg.d[k], nr, r0, n_rows, f0, d_fb.p,
+      k_bin_columns<<<dim3(row_blocks, nf), kBinThreads, 0, st>>>(static_cast<const double*>(sg.d[k]), nr, r0,
+                                                                 n_rows, f0, d_fb.p,
                                                                  d_edges.p, d_codes.p, d_bins, rows_per_block);
       MTB_CUDA_BIN(cudaGetLastError());
       k = (k + 1) % kStages;
@@ -230,35 +292,16 @@ void transform_on_device(const BinMapper& m, const double* x, int64_t n_rows, ui
 void upload_host(const void* src, int64_t bytes, void* dst_dev, cudaStream_t st) {
   const uint8_t* bins = static_cast<const uint8_t*>(src);
   uint8_t* d_bins = static_cast<uint8_t*>(dst_dev);
-  constexpr int kStages = 3;
-  constexpr int64_t kPiece = 32ll << 20;
-  if (bytes <= kPiece) {
+  constexpr int64_t kPiece = (int64_t)kStageBytes;
+  // registering the staging buffers costs ~25 ms: below 1 GB a direct copy
+  // from pageable memory is cheaper
+  if (bytes < (1ll << 30)) {
     MTB_CUDA_BIN(cudaMemcpyAsync(d_bins, bins, (size_t)bytes, cudaMemcpyHostToDevice, st));
     MTB_CUDA_BIN(cudaStreamSynchronize(st));
     return;
   }
-  struct Stages {
-    uint8_t* h[kStages] = {};
-    bool reg[kStages] = {};
-    cudaEvent_t e[kStages] = {};
-    ~Stages() {
-      for (int i = 0; i < kStages; ++i) {
-        if (e[i]) {
-          cudaEventSynchronize(e[i]);
-          cudaEventDestroy(e[i]);
-        }
-        if (reg[i]) cudaHostUnregister(h[i]);
-        free(h[i]);
-      }
-    }
-  } sg;
-  for (int i = 0; i < kStages; ++i) {
-    sg.h[i] = static_cast<uint8_t*>(aligned_alloc(4096, (size_t)kPiece));
-    if (!sg.h[i]) throw std::runtime_error("host staging allocation failed");
-    MTB_CUDA_BIN(cudaHostRegister(sg.h[i], (size_t)kPiece, cudaHostRegisterDefault));
-    sg.reg[i] = true;
-    MTB_CUDA_BIN(cudaEventCreateWithFlags(&sg.e[i], cudaEventDisableTiming));
-  }
+  Staging stg;
+  StagingSet& sg = *stg.set;
   int k = 0;
   for (int64_t off = 0; off < bytes; off += kPiece) {
     const int64_t len = std::min<int64_t>(kPiece, bytes - off);

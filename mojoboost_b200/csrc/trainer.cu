@@ -12,6 +12,8 @@
 
 #include <algorithm>
 #include <chrono>
+#include <map>
+#include <mutex>
 #include <thread>
 #include <cmath>
 #include <cstring>
@@ -54,22 +56,102 @@ __global__ void k_fill_raw(double* __restrict__ raw, const double* __restrict__ 
     raw[i] = base[i % K];
 }
 
+// Device memory of the fits comes from a per-process cache: a fit's buffers
+// go back to it when the fit ends, and the next fit on the same device takes
+// blocks of the sizes it needs from it instead of calling cudaMalloc (whose
+// cost for the ~4 GB a configs[1] fit allocates varies between tens and
+// hundreds of milliseconds).  Sizes are rounded up to 2 MB, a cached block
+// is reused for a request at most 1/8 smaller, the cache holds at most a
+// quarter of the device's memory, and a failed cudaMalloc empties it and
+// retries (MOJOTREES_NO_MEMORY_CACHE=1: no cache).  Returning a block
+// synchronises the device, as cudaFree does.
+class DeviceCache {
+ public:
+  static DeviceCache& get() {
+    static DeviceCache c;
+    return c;
+  }
+  void* take(size_t bytes) {
+    int dev = 0;
+    MTB_CUDA(cudaGetDevice(&dev));
+    {
+      std::lock_guard<std::mutex> lock(mu_);
+      auto& m = free_[dev];
+      for (auto it = m.lower_bound(bytes); it != m.end() && it->first <= bytes + bytes / 8;) {
+        void* p = it->second;
+        const size_t sz = it->first;
+        it = m.erase(it);
+        held_[dev] -= sz;
+        cudaPointerAttributes a;
+        if (cudaPointerGetAttributes(&a, p) == cudaSuccess && a.type == cudaMemoryTypeDevice && a.device == dev)
+          return p;
+        cudaGetLastError();  // a block from a context that no longer exists: dropped
+      }
+    }
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e == cudaErrorMemoryAllocation) {
+      cudaGetLastError();
+      release(dev);
+      e = cudaMalloc(&p, bytes);
+    }
+    if (e != cudaSuccess) throw std::runtime_error(std::string("CUDA error: ") + cudaGetErrorString(e) + " (cudaMalloc)");
+    return p;
+  }
+  void give(void* p, size_t bytes) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+      cudaGetLastError();
+      cudaFree(p);
+      return;
+    }
+    std::lock_guard<std::mutex> lock(mu_);
+    if (!limit_.count(dev)) {
+      size_t fr = 0, total = 0;
+      cudaMemGetInfo(&fr, &total);
+      limit_[dev] = getenv("MOJOTREES_NO_MEMORY_CACHE") ? 0 : total / 4;
+    }
+    if (held_[dev] + bytes > limit_[dev]) {
+      cudaFree(p);
+      return;
+    }
+    free_[dev].emplace(bytes, p);
+    held_[dev] += bytes;
+  }
+  void release(int dev) {
+    std::lock_guard<std::mutex> lock(mu_);
+    for (auto& kv : free_[dev]) cudaFree(kv.second);
+    free_[dev].clear();
+    held_[dev] = 0;
+  }
+
+ private:
+  std::mutex mu_;
+  std::map<int, std::multimap<size_t, void*>> free_;
+  std::map<int, size_t> held_, limit_;
+};
+
 template <typename T>
 struct DevBuf {
   T* p = nullptr;
   size_t n = 0;
+  size_t bytes = 0;
   DevBuf() = default;
   DevBuf(const DevBuf&) = delete;
   DevBuf& operator=(const DevBuf&) = delete;
   void alloc(size_t count) {
     free();
     n = count;
-    if (count) MTB_CUDA(cudaMalloc(&p, sizeof(T) * count));
+    if (count) {
+      bytes = (sizeof(T) * count + (2u << 20) - 1) & ~(size_t)((2u << 20) - 1);
+      p = static_cast<T*>(DeviceCache::get().take(bytes));
+    }
   }
   void free() {
-    if (p) cudaFree(p);
+    if (p) DeviceCache::get().give(p, bytes);
     p = nullptr;
     n = 0;
+    bytes = 0;
   }
   ~DevBuf() { free(); }
 };
@@ -229,11 +311,22 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   std::vector<double> base(K);
   if (K == 1) {
     double mean = 0.0;
-    for (long long r = 0; r < N; ++r) mean += 1.0 * in.labels[r];
     std::string err;
-    if (cfg.objective == OBJECTIVE_BINARY)
-      for (long long r = 0; r < N && err.empty(); ++r)
-        if (!(in.labels[r] == 0.0 || in.labels[r] == 1.0)) err = "binary labels must be 0 or 1";
+    if (cfg.objective == OBJECTIVE_BINARY) {
+      // 0/1 labels: the sequential sum is the count of ones, exact in any
+      // order, so it is counted in parallel together with the label check
+      long long ones = 0, bad = 0;
+#pragma omp parallel for reduction(+ : ones, bad) schedule(static)
+      for (long long r = 0; r < N; ++r) {
+        const double v = in.labels[r];
+        ones += v == 1.0 ? 1 : 0;
+        bad += (v == 0.0 || v == 1.0) ? 0 : 1;
+      }
+      if (bad) err = "binary labels must be 0 or 1";
+      mean = (double)ones;
+    } else {
+      for (long long r = 0; r < N; ++r) mean += 1.0 * in.labels[r];
+    }
     agree(err);
     if (coll) {
       MTB_CUDA(cudaMemcpyAsync(d_red.p + world, &mean, 8, cudaMemcpyHostToDevice, st));
