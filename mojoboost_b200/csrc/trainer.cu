@@ -250,12 +250,14 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   DevBuf<uint8_t> d_bins_cm, d_bins_rm;
   d_bins_cm.alloc((size_t)F * N);
   d_bins_rm.alloc((size_t)Fp * N);
+  mark("bin buffers allocated");
   if (in.dense_fm) {
     if (!in.mapper) throw std::runtime_error("dense input without a bin mapper");
     transform_on_device(*in.mapper, in.dense_fm, N, d_bins_cm.p, st);
   } else {
     upload_host(in.bins_fm, (int64_t)F * N, d_bins_cm.p, st);
   }
+  mark("bins on the device");
   {
     dim3 grid((unsigned)((N + 255) / 256), Fp / 16);
     k_transpose_bins<<<grid, 256, 0, st>>>(d_bins_cm.p, d_bins_rm.p, N, F, Fp);
