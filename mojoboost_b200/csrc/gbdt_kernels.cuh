@@ -1987,6 +1987,13 @@ __global__ void __launch_bounds__(kCommitThreads) k_commit(TreeState* __restrict
                                                            int info_cap, int* __restrict__ host_done,
                                                            int host_done_index) {
   pdl_enter();
+  if (ts->hdr.done) {  // an iteration the host launched ahead after the tree was finished
+    if (threadIdx.x == 0 && host_done) {
+      volatile int* hd = host_done;
+      hd[host_done_index] = 1;
+    }
+    return;
+  }
   extern __shared__ __align__(16) unsigned char commit_smem[];
   const int L_max = cp.num_leaves;
   double* s_g = reinterpret_cast<double*>(commit_smem);   // slot -> gain (-1: cannot split)
