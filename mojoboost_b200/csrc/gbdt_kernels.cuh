@@ -984,50 +984,16 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
     // within each half-warp to lane = bin, and added to the work slot with
     // int32 atomics whose lanes hit two runs of 16 consecutive cells (4
     // sectors a warp instruction instead of 32; about 5x faster through L2
-    // than the lane = feature order).  A CTA's slice has 8 tiles in clusters
-    // of 8, so one unit per (tile, plane) keeps 24 of the 32 warps reading
-    // DSMEM at once instead of 8.
+    // than the lane = feature order).  With 16-bit packed cells one unit
+    // reads the (g + g_lim | count) words once for both of their planes.
     {
       constexpr int kPlanes = (MODE == MODE_FIXED && CONST_H) ? 2 : 3;  // g, [h,] count
+      constexpr int kUnits = Q16 ? 2 : kPlanes;
       const int tiles = (m1 - m0) >> 9;
       const int half = lane >> 4, hl = lane & 15;
-      for (int wu = warp; wu < tiles * kPlanes; wu += n_warps) {
-        const int t = wu / kPlanes, plane = wu - t * kPlanes;
-        const int c0 = m0 + (t << 9);
-        const int j = (c0 >> 5) / kHistBinsPad, bin0 = (c0 >> 5) % kHistBinsPad;
-        const int out_plane = (kPlanes == 2 && plane == 1) ? 2 : plane;  // constant hessian: g, count
-        int v[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = 0;
-        for (int rk = 0; rk < cs; ++rk) {
-          const unsigned int* q0 = cluster.map_shared_rank(p0, rk);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int c = c0 + (i << 5) + lane;
-            if (Q16) {
-              if (plane == 1) {
-                const unsigned int x = q0[cells + ((((j >> 1) * kHistBinsPad + bin0 + i) << 5) + lane)];
-                v[i] += (int)((x >> (16 * (j & 1))) & 0xffffu);
-              } else {
-                const unsigned int x = q0[c];
-                v[i] += plane == 0 ? (int)(x & 0xffffu) - g_lim * (int)(x >> 16) : (int)(x >> 16);
-              }
-            } else if (LAYOUT == HL_QUANT) {
-              if (plane == 1) {
-                v[i] += (int)q0[cells + c];
-              } else {
-                const unsigned int x = q0[c];
-                v[i] += plane == 0 ? ((int)x >> kQuantCountBits) : (int)(x & ((1u << kQuantCountBits) - 1u));
-              }
-            } else {
-              // fixed point: planes g, h, count (constant hessian: g, count)
-              v[i] += (int)q0[plane * cells + c];
-            }
-          }
-        }
-        // 16 x 16 transposes within each half-warp: lane 16 h + m, v[i] =
-        // cell (lane 16 h + m, bin i) becomes lane 16 h + i, v[m] = cell
-        // (lane 16 h + m, bin i)
+      auto transpose16 = [&](int (&v)[16]) {
+        // lane 16 h + m, v[i] = cell (lane 16 h + m, bin i) becomes
+        // lane 16 h + i, v[m] = cell (lane 16 h + m, bin i)
 #pragma unroll
         for (int sft = 8; sft >= 1; sft >>= 1) {
           const bool upper = (lane & sft) != 0;
@@ -1043,12 +1009,65 @@ __device__ void hist_segment(cooperative_groups::cluster_group& cluster, const B
             }
           }
         }
+      };
+      auto emit = [&](int (&v)[16], int j, int bin0, int out_plane) {
+        transpose16(v);
         const int bin = bin0 + hl;
 #pragma unroll
         for (int m = 0; m < 16; ++m) {
           const int f = f0 + (16 * half + m) * NPL + j;
           if (f < F && bin < B && v[m] != 0) atomicAdd(hs + (f * 3 + out_plane) * B + bin, v[m]);
         }
+      };
+      for (int wu = warp; wu < tiles * kUnits; wu += n_warps) {
+        const int t = wu / kUnits, plane = wu - t * kUnits;
+        const int c0 = m0 + (t << 9);
+        const int j = (c0 >> 5) / kHistBinsPad, bin0 = (c0 >> 5) % kHistBinsPad;
+        int v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = 0;
+        if (Q16 && plane == 0) {
+          int vc[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) vc[i] = 0;
+          for (int rk = 0; rk < cs; ++rk) {
+            const unsigned int* q0 = cluster.map_shared_rank(p0, rk);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const unsigned int x = q0[c0 + (i << 5) + lane];
+              v[i] += (int)(x & 0xffffu);
+              vc[i] += (int)(x >> 16);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] -= g_lim * vc[i];
+          emit(v, j, bin0, 0);
+          emit(vc, j, bin0, 2);
+          continue;
+        }
+        const int out_plane = Q16 ? 1 : (kPlanes == 2 && plane == 1) ? 2 : plane;  // constant hessian: g, count
+        for (int rk = 0; rk < cs; ++rk) {
+          const unsigned int* q0 = cluster.map_shared_rank(p0, rk);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int c = c0 + (i << 5) + lane;
+            if (Q16) {  // plane B: h of features 2k (low half) and 2k + 1
+              const unsigned int x = q0[cells + ((((j >> 1) * kHistBinsPad + bin0 + i) << 5) + lane)];
+              v[i] += (int)((x >> (16 * (j & 1))) & 0xffffu);
+            } else if (LAYOUT == HL_QUANT) {
+              if (plane == 1) {
+                v[i] += (int)q0[cells + c];
+              } else {
+                const unsigned int x = q0[c];
+                v[i] += plane == 0 ? ((int)x >> kQuantCountBits) : (int)(x & ((1u << kQuantCountBits) - 1u));
+              }
+            } else {
+              // fixed point: planes g, h, count (constant hessian: g, count)
+              v[i] += (int)q0[plane * cells + c];
+            }
+          }
+        }
+        emit(v, j, bin0, out_plane);
       }
     }
     cluster.sync();  // peers finished reading before anyone re-zeroes
