@@ -2506,32 +2506,36 @@ __global__ void __launch_bounds__(1024) k_leaf_table(TreeState* __restrict__ ts,
 }
 
 // raw[row * K + k] = fma(lr, value(leaf of row), raw[row * K + k])
-// (boosting.mojo:1991-2111, explicit fused multiply-add).  The leaf table
-// (range starts, row buffers, values; at most kMaxPool entries) is staged in
-// shared memory by every block, and each position finds its entry there.
-__global__ void __launch_bounds__(256) k_update_raw(const TreeState* __restrict__ ts,
-                                                    const long long* __restrict__ begins,
-                                                    const int* __restrict__ bufs, const double* __restrict__ values,
-                                                    const int* __restrict__ rows0, const int* __restrict__ rows1,
-                                                    double* __restrict__ raw, long long n, int K, int k, double lr,
-                                                    int stage_cap) {
-  extern __shared__ long long s_tab[];  // stage_cap entries: begin, value (as bits), buffer
+// (boosting.mojo:1991-2111, explicit fused multiply-add), in two passes.
+// The leaf table lists rows by buffer position, so updating raw in position
+// order is a scattered 8-byte read-modify-write of the score array (each
+// touching its own 32-byte sector).  Instead, k_row_slots walks the positions
+// and scatters each row's table entry as a 2-byte slot into an N-entry array
+// small enough to stay in L2, and k_update_raw then walks the rows in order:
+// the slot and score loads and the score store are coalesced.  Every row gets
+// the same fma of the same operands, so the scores are bit-identical to a
+// position-order update.  Every row sits in exactly one table range, so every
+// slot is rewritten each tree and the array needs no clearing.
+__global__ void __launch_bounds__(256) k_row_slots(const TreeState* __restrict__ ts,
+                                                   const long long* __restrict__ begins,
+                                                   const int* __restrict__ bufs, const int* __restrict__ rows0,
+                                                   const int* __restrict__ rows1,
+                                                   unsigned short* __restrict__ slot_of_row, long long n,
+                                                   int stage_cap) {
+  extern __shared__ long long s_tab[];  // stage_cap entries: begin, buffer
   long long* s_begin = s_tab;
-  double* s_val = reinterpret_cast<double*>(s_tab + stage_cap);
-  int* s_buf = reinterpret_cast<int*>(s_val + stage_cap);
+  int* s_buf = reinterpret_cast<int*>(s_tab + stage_cap);
   const int nt = ts->hdr.n_table;
   const bool staged = nt <= stage_cap;
   if (staged)
     for (int t = threadIdx.x; t < nt; t += blockDim.x) {
       s_begin[t] = begins[t];
       s_buf[t] = bufs[t];
-      s_val[t] = values[t];
     }
   __syncthreads();
   if (!staged) {
     s_begin = const_cast<long long*>(begins);
     s_buf = const_cast<int*>(bufs);
-    s_val = const_cast<double*>(values);
   }
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -2542,9 +2546,26 @@ __global__ void __launch_bounds__(256) k_update_raw(const TreeState* __restrict_
       else hi = mid - 1;
     }
     const int* rows = s_buf[lo] ? rows1 : rows0;
-    const int r = rows[i];
-    double* p = raw + (long long)r * K + k;
-    *p = fma(lr, s_val[lo], *p);
+    slot_of_row[rows[i]] = (unsigned short)lo;
+  }
+}
+
+__global__ void __launch_bounds__(256) k_update_raw(const TreeState* __restrict__ ts,
+                                                    const double* __restrict__ values,
+                                                    const unsigned short* __restrict__ slot_of_row,
+                                                    double* __restrict__ raw, long long n, int K, int k, double lr,
+                                                    int stage_cap) {
+  extern __shared__ double s_val[];  // stage_cap leaf values
+  const int nt = ts->hdr.n_table;
+  const bool staged = nt <= stage_cap;
+  if (staged)
+    for (int t = threadIdx.x; t < nt; t += blockDim.x) s_val[t] = values[t];
+  __syncthreads();
+  const double* vals = staged ? s_val : values;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += stride) {
+    double* p = raw + r * K + k;
+    *p = fma(lr, vals[slot_of_row[r]], *p);
   }
 }
 

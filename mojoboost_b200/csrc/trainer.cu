@@ -474,12 +474,16 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
   DevBuf<double> d_values;
   d_begins.alloc(kMaxPool);
   d_bufs.alloc(kMaxPool);
-  // leaf-table entries the raw update stages in shared memory (20 B each;
+  // leaf-table entries the raw update stages in shared memory (12 B each in
+  // the slot scatter, 8 B in the score pass;
   // larger tables are searched in global memory), and its grid: a few
   // resident blocks per SM, each staging the table once
   const int table_stage = std::min(4 * cfg.num_leaves + 2 * kMaxBatch + 2, 2400);
   const unsigned update_grid = (unsigned)std::max(1ll, std::min<long long>((N + 255) / 256, (long long)n_sm * 8));
   d_values.alloc(kMaxPool);
+  static_assert(kMaxPool <= 65536, "leaf-table slots are 16-bit");
+  DevBuf<unsigned short> d_slot;  // each row's leaf-table entry, rewritten every tree
+  d_slot.alloc(N);
   host_sync();
   mark("work buffers");
   stats.upload_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
@@ -906,10 +910,11 @@ void train_gpu(const BinnedInput& in, const TrainConfig& cfg, Model& model) {
       stats.hist_launches += launched;
       k_leaf_table<<<1, 1024, sizeof(long long) * table_stage, st>>>(d_ts.p, d_begins.p, d_bufs.p, d_values.p,
                                                                       table_stage);
-      k_update_raw<<<update_grid, 256, 20 * (size_t)table_stage, st>>>(d_ts.p, d_begins.p, d_bufs.p, d_values.p,
-                                                                      d_rows0.p, d_rows1.p, d_raw.p, N, K, k,
-                                                                      cfg.learning_rate, table_stage);
-      launches += 2;
+      k_row_slots<<<update_grid, 256, 12 * (size_t)table_stage, st>>>(d_ts.p, d_begins.p, d_bufs.p, d_rows0.p,
+                                                                     d_rows1.p, d_slot.p, N, table_stage);
+      k_update_raw<<<update_grid, 256, 8 * (size_t)table_stage, st>>>(d_ts.p, d_values.p, d_slot.p, d_raw.p, N, K,
+                                                                     k, cfg.learning_rate, table_stage);
+      launches += 3;
       MTB_CUDA(cudaGetLastError());
       MTB_CUDA(cudaMemcpyAsync(&hdr, &d_ts.p->hdr, sizeof(TreeHeader), cudaMemcpyDeviceToHost, st));
       MTB_CUDA(cudaMemcpyAsync(nodes_host.data(), d_ts.p->nodes, sizeof(HostNode) * M, cudaMemcpyDeviceToHost, st));
